@@ -1,0 +1,435 @@
+"""Decode throughput of the B200 backend (libq35b) on the reference's headline
+metric: decode tokens/s at batch 1 / 64 (0.8B Q8_0, 4B IQ4_NL), GEMV HBM GB/s
+against the measured peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (`value`): the 0.8B-shaped Q8_0 model,
+batch 1: every sequence is prefilled with a 128-token prompt of seeded random
+ids, then K greedy decode steps are timed.  Weights are seeded synthetic
+(N(0, 0.02), packed on the device); 0.8 GB of weights per step is larger than
+L2 (126 MB), so no flush is needed between steps.  Multi-GPU (torchrun): one
+process per GPU, each an independent replica with its own sequences (weak
+scaling, no collective on the data path); the timed region is bracketed by a
+barrier and device syncs and the max over ranks is reported.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+PUBLISHED_08B_Q8_0_B1 = 121.84  # reference CUDA backend, RTX 4090 D
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in open(self.path):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def make_prompts(rng, n, length, vocab):
+    return [[int(t) for t in rng.integers(0, vocab, length)] for _ in range(n)]
+
+
+class Run:
+    """one model + engine on this rank, prefilled and ready to decode"""
+
+    def __init__(self, cfg_name, batch, prompt_len, extra_steps, seed):
+        import numpy as np
+        import torch
+
+        from qwen35_b200 import model as q35
+        self.torch = torch
+        self.cfg = q35.CONFIGS[cfg_name]
+        self.synth = q35.SyntheticModel(self.cfg, seed=seed)
+        self.batch = batch
+        self.max_seq = prompt_len + extra_steps + 8
+        self.eng = q35.Engine(self.synth, n_slots=batch, max_seq=self.max_seq, max_batch=batch)
+        rng = np.random.default_rng(seed + 17)
+        self.prompts = make_prompts(rng, batch, prompt_len, self.cfg.vocab)
+        for s in range(batch):
+            self.eng.reset_slot(s)
+        nxt = None
+        for pos in range(prompt_len):
+            nxt = self.eng.step_host([p[pos] for p in self.prompts], list(range(batch)), [pos] * batch)
+        self.pos = prompt_len
+        self.last = nxt
+        # device-resident inputs for the timed decode loop
+        L = self.eng.L
+        h = self.eng.h
+        i32 = torch.int32
+        q35.device_view(self.eng.d_tokens, batch, i32).copy_(torch.tensor(nxt, dtype=i32))
+        q35.device_view(self.eng.d_slots, batch, i32).copy_(torch.arange(batch, dtype=i32))
+        q35.device_view(self.eng.d_pos, batch, i32).fill_(self.pos)
+        torch.cuda.synchronize()
+        self.L, self.h = L, h
+        self.stream = torch.cuda.current_stream()
+
+    def dev_steps(self, k):
+        s = ctypes.c_void_p(self.stream.cuda_stream)
+        for _ in range(k):
+            rc = self.L.q35b_engine_step_dev(self.h, self.batch, self.max_seq, 1, s)
+            assert rc == 0, rc
+            rc = self.L.q35b_engine_advance(self.h, self.batch, s)
+            assert rc == 0, rc
+            self.pos += 1
+
+    def host_steps(self, k, toks):
+        """end-to-end through the public host-buffer API"""
+        slots = list(range(self.batch))
+        for _ in range(k):
+            toks = self.eng.step_host(toks, slots, [self.pos] * self.batch)
+            self.pos += 1
+        return toks
+
+    def launches_per_step(self):
+        return int(self.L.q35b_engine_launches_per_step(self.h)) + 1  # + the feedback kernel
+
+    def close(self):
+        self.eng.close()
+
+
+def time_decode(run, steps, warmup, dist):
+    torch = run.torch
+    run.dev_steps(warmup)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(run.stream)
+    run.dev_steps(steps)
+    e1.record(run.stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    return e0.elapsed_time(e1)
+
+
+def time_e2e(run, steps, warmup, dist):
+    torch = run.torch
+    toks = [int(t) for t in run.last]
+    toks = run.host_steps(warmup, toks)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    run.host_steps(steps, toks)
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1e3
+    if dist:
+        dist.barrier()
+    return ms
+
+
+def max_over_ranks(v, dist):
+    if not dist:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gemv_roofline(run, reps=20):
+    """the dominant launch of the batch-1 step, timed alone with CUDA events:
+    the tied lm_head GEMV over token_embd (vocab x hidden Q8_0, 270 MB > L2)."""
+    torch = run.torch
+    import numpy as np
+    L = run.L
+    tt, rows, cols, w = run.synth.tensors["token_embd.weight"]
+    e, b = {8: (32, 34), 20: (32, 18), 12: (256, 144), 13: (256, 176), 14: (256, 210)}[tt]
+    fam = 32 if e == 32 else 256
+    x = torch.randn(cols, device="cuda")
+    xq = torch.zeros(cols // fam * (34 if fam == 32 else 292), dtype=torch.uint8, device="cuda")
+    s = ctypes.c_void_p(run.stream.cuda_stream)
+    if fam == 32:
+        L.q35_launch_quantize_q8_0(x.data_ptr(), xq.data_ptr(), cols // 32, s)
+    else:
+        L.q35_launch_quantize_q8_K(x.data_ptr(), xq.data_ptr(), cols // 256, s)
+    out = torch.zeros(rows, device="cuda")
+    for _ in range(3):
+        assert L.q35_launch_mul_mat_vec(w.data_ptr(), xq.data_ptr(), out.data_ptr(), rows, cols, 1, tt, s) == 0
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, c in ev:
+        a.record(run.stream)
+        L.q35_launch_mul_mat_vec(w.data_ptr(), xq.data_ptr(), out.data_ptr(), rows, cols, 1, tt, s)
+        c.record(run.stream)
+    torch.cuda.synchronize()
+    ms = float(np.mean([a.elapsed_time(c) for a, c in ev]))
+    algo = rows * (cols // e) * b + xq.numel() + rows * 4
+    return {"kernel": "k_gemv<1> (lm_head, %dx%d %s)" % (rows, cols, {8: "Q8_0", 20: "IQ4_NL", 12: "Q4_K",
+                                                                   13: "Q5_K", 14: "Q6_K"}[tt]),
+            "bytes": algo, "ms": ms, "gbs": algo / (ms * 1e-3) / 1e9}
+
+
+def cpu_baseline(run, seconds_target=15.0):
+    """the reference's x86 kernels (oracle/_ref, compiled from the reference
+    sources) under the restated engine loop, on this host's cores"""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import numpy as np
+
+    import oracle_lib as ol
+    ref = os.path.exists(ol.REF_SO)
+    lib = ol._declare(ctypes.CDLL(ol.REF_SO)) if ref else ol.load_oracle()
+    ol._LIB_SAVE = ol._LIB
+    ol._LIB = lib
+    cores = os.cpu_count() or 1
+    try:
+        lib_m = _cpu_model(lib, run.synth, cores, 64)
+        m, keep = lib_m
+        prompt = run.prompts[0][:4]
+        for i, t in enumerate(prompt):
+            lib.q35o_forward(m, t, i)
+        # calibrate: one step, then size the sample to ~seconds_target
+        out = (ctypes.c_int * 64)()
+        dt1 = lib.q35o_time_decode(m, prompt[-1], len(prompt), 1, out)
+        n = int(max(2, min(48, seconds_target / max(dt1, 1e-3))))
+        dt = lib.q35o_time_decode(m, int(out[0]), len(prompt) + 1, n, out)
+        lib.q35o_model_destroy(m)
+        del keep
+        return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "reference" if ref else "port",
+                "sample": f"{run.cfg.name}, batch 1, {len(prompt)}-token prompt, {n} timed decode tokens "
+                          f"({'reference x86 C kernels' if ref else 'C restatement'} + restated engine loop, "
+                          f"{cores} threads)"}
+    finally:
+        ol._LIB = ol._LIB_SAVE
+
+
+def _cpu_model(lib, synth, threads, max_seq):
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as ol
+    c = synth.cfg
+    cfg = ol.Config(c.n_layers, c.full_attention_interval, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.n_ff,
+                    c.vocab, c.rms_eps, c.rope_freq_base, c.gdn_n_heads, c.gdn_num_k_heads, c.gdn_head_dim,
+                    c.conv_kernel)
+    m = lib.q35o_model_create(ctypes.byref(cfg), max_seq, threads)
+    keep = []
+    for name in synth.tensors:
+        tt, rows, cols, arr = synth.host(name)
+        arr = np.ascontiguousarray(arr)
+        keep.append(arr)
+        assert lib.q35o_model_set_tensor(m, name.encode(), tt, arr.ctypes.data, rows, cols) == 0
+    assert lib.q35o_model_check(m) == 0
+    return m, keep
+
+
+def run_reference_arm(args, rank):
+    """`--impl reference`: the reference's CPU implementation of the path on
+    this box's host cores, same metric and config; rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as ol
+    from qwen35_b200 import model as q35
+    synth = q35.SyntheticModel(q35.CONFIGS["0.8b"], seed=args.seed)
+    ref = os.path.exists(ol.REF_SO)
+    lib = ol._declare(ctypes.CDLL(ol.REF_SO)) if ref else ol.load_oracle()
+    cores = os.cpu_count() or 1
+    m, keep = _cpu_model(lib, synth, cores, 4 + args.warmup + args.steps + 8)
+    import numpy as np
+    rng = np.random.default_rng(args.seed + 17)
+    prompt = [int(t) for t in rng.integers(0, synth.cfg.vocab, 4)]
+    for i, t in enumerate(prompt):
+        lib.q35o_forward(m, t, i)
+    out = (ctypes.c_int * (args.warmup + args.steps + 1))()
+    lib.q35o_time_decode(m, prompt[-1], len(prompt), args.warmup, out)
+    tok = int(out[args.warmup - 1]) if args.warmup > 0 else prompt[-1]
+    dt = lib.q35o_time_decode(m, tok, len(prompt) + args.warmup, args.steps, out)
+    v = args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32", "data": "synthetic",
+        "config": CONFIG_08B,
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference" if ref else "port",
+                         "sample": f"0.8B Q8_0 batch 1, 4-token prompt, {args.steps} timed decode tokens per run "
+                                   f"({'reference x86 C kernels compiled from the reference sources' if ref else 'C restatement'}"
+                                   f", restated engine loop, {cores} threads)"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    lib.q35o_model_destroy(m)
+    del keep, torch
+
+
+METRIC = "decode tokens/s at batch 1/64 (0.8B Q8_0, 4B IQ4_NL); GEMV HBM GB/s vs peak"
+CONFIG_08B = {"workload": "0.8B-Q8_0 greedy decode, batch 1, 128-token prompt (BASELINE config 1)",
+              "model": "qwen3.5-0.8b-q8_0 (24 layers LLLFx6, hidden 1024, ffn 3584, vocab 248320)",
+              "global_batch": 1, "seq_len": 128, "parallelism": "replicas (sequence-sharded, no collective)",
+              "l2": "weights 0.80 GB per step > 126 MB L2: no flush needed"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--no-variants", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
+    else:
+        torch.cuda.set_device(0)
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    from qwen35_b200.build import build
+    if rank == 0:
+        build()
+    if dist:
+        dist.barrier()
+    pk, pk_kind = peaks()
+    extra = 2 * (args.warmup + args.steps) + 8
+
+    # ---------------- headline: 0.8B Q8_0, batch 1 ----------------
+    run = Run("0.8b", 1, args.prompt, extra, seed=args.seed + rank)
+    gpu_id = torch.cuda.get_device_properties(local).pci_bus_id if hasattr(
+        torch.cuda.get_device_properties(local), "pci_bus_id") else str(local)
+    clocks = ClockSampler(gpu_id)
+    clocks.start()
+    ms = time_decode(run, args.steps, args.warmup, dist)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, dist)
+    e2e_ms = max_over_ranks(time_e2e(run, args.steps, args.warmup, dist), dist)
+    launches = run.launches_per_step() * args.steps
+    roof = gemv_roofline(run) if rank == 0 else None
+    value = world * run.batch * args.steps / (ms * 1e-3)
+    e2e_val = world * run.batch * args.steps / (e2e_ms * 1e-3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(run)
+    run.close()
+    del run
+    torch.cuda.empty_cache()
+
+    variants = []
+    if not args.no_variants:
+        for cfg_name, batch in (("0.8b", 64), ("4b", 1), ("4b", 64)):
+            ksteps = min(args.steps, 32)
+            r = Run(cfg_name, batch, args.prompt, 2 * (args.warmup + ksteps) + 8, seed=args.seed + rank)
+            vms = max_over_ranks(time_decode(r, ksteps, args.warmup, dist), dist)
+            variants.append({"model": r.cfg.name, "batch_per_gpu": batch, "steps": ksteps,
+                             "ms_per_step": vms / ksteps,
+                             "value": world * batch * ksteps / (vms * 1e-3), "unit": "tokens/s"})
+            r.close()
+            del r
+            torch.cuda.empty_cache()
+
+    if rank == 0:
+        hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / world / PUBLISHED_08B_Q8_0_B1,
+            "dtype": "int8 x int8 -> int32 block dots, f32 fold/state/KV", "data": "synthetic",
+            "config": dict(CONFIG_08B, global_batch=world),
+            "clocks": clk,
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": 12 * world,
+                    "d2h_bytes_per_step": 4 * world},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "achieved": roof["gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": roof["gbs"] / hbm, "traffic": None, "kernel": roof["kernel"],
+                         "algorithmic_bytes_per_launch": roof["bytes"], "avg_launch_ms": roof["ms"],
+                         "peak_source": f"{pk_kind} (MEASURED_PEAKS.json hbm_gbs)" if pk_kind == "measured"
+                         else "fallback 6.65 TB/s"},
+            "cpu_baseline": cpu,
+            "variants": variants,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

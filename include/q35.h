@@ -1,0 +1,273 @@
+/*
+ * q35.h -- C ABI of libq35b, the B200 (sm_100a) backend for the Qwen3.5
+ * engine.
+ *
+ * Part 1 re-exports the reference's kernel launcher interface with identical
+ * names, signatures, argument meaning and error convention
+ * (src/kernels/cuda/api.h of frybox/qwen35; each declaration below cites the
+ * line it replaces), so the reference's CUDA host (src/backend_cuda.zig,
+ * `Kernels` extern block :80-218 and `Launch` table :283-345) links against
+ * this library unchanged.
+ *
+ * Part 2 is additive (`q35b_*`): a batched decode engine over per-sequence
+ * KV / GDN slots, a continuous-batching server loop, device weight encoders
+ * and error reporting.  The reference has no counterpart for these (it is a
+ * single-sequence engine); they follow the same conventions.
+ *
+ * Conventions (api.h:1-13): every launcher returns the numeric cudaError_t
+ * (0 = success); device pointers and streams are opaque `void *` / typed
+ * pointers; the caller owns all memory; zero-size work returns 0 without a
+ * launch; nothing aborts.  Launchers are not re-entrant across host threads
+ * (per-process static caches), as in the reference.
+ */
+#ifndef Q35_B200_H
+#define Q35_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================================================================== */
+/* Part 1: the reference's launcher interface (api.h)                     */
+/* ===================================================================== */
+
+#define Q35_API_QK8_0 32            /* api.h:23 */
+#define Q35_API_Q8_0_BLOCK_BYTES 34 /* api.h:24 */
+#define Q35_API_QK_K 256            /* api.h:28 */
+#define Q35_API_Q8_K_BLOCK_BYTES 292/* api.h:29 */
+
+/* TensorType ids, equal to GGUF's (api.h:42-75). */
+#define Q35_TT_F32 0
+#define Q35_TT_F16 1
+#define Q35_TT_Q4_0 2
+#define Q35_TT_Q8_0 8
+#define Q35_TT_Q4_K 12
+#define Q35_TT_Q5_K 13
+#define Q35_TT_Q6_K 14
+#define Q35_TT_Q8_K 15
+#define Q35_TT_IQ4_NL 20
+
+/* device capability probe (api.h:35-37) */
+int q35_gpu_cc(void);
+int q35_gpu_sm_count(void);
+const char *q35_gpu_name(void);
+
+/* activation quantization (api.h:79-93; the _q8_K_mmq twin is exported by
+ * the reference's mmvq.cu:1042).  Bit-exact with the reference CPU
+ * quantizers.  The mmq layouts are not produced by this backend: the _mmq
+ * entry points return cudaErrorNotSupported and q35_mmq_dp4a_wants() is 0,
+ * so the caller never asks for them. */
+int q35_launch_quantize_q8_0(const float *d_x, void *d_out, int nblocks, void *stream);
+int q35_launch_quantize_q8_K(const float *d_x, void *d_out, int nblocks, void *stream);
+int q35_launch_quantize_q8_1_mmq(const float *d_x, void *d_y, int nblocks_k, int nrows, void *stream);
+int q35_launch_quantize_q8_K_mmq(const float *d_x, void *d_out, void *d_mmq, int nblocks, void *stream);
+
+/* dequantization (api.h:95-105) */
+int q35_launch_dequantize(int ttype, const void *d_src, float *d_dst, int nblocks, void *stream);
+int q35_launch_dequantize_row(int ttype, const void *d_src_row, float *d_dst, int cols, void *stream);
+
+/* matvec (api.h:110-124): out[t*rows + r] = W[r] . xq[t], bit-exact with the
+ * reference scalar CPU tier (per-block integer dot, f32 fold in block order).
+ * Types: Q8_0, IQ4_NL, Q4_K, Q5_K, Q6_K; others -> cudaErrorInvalidValue. */
+int q35_launch_mul_mat_vec(const void *d_w, const void *d_xq, float *d_out, int rows, int cols, int tokens,
+                           int ttype, void *stream);
+int q35_launch_mul_mat_vec_q8_0(const void *d_w, const void *d_xq, float *d_out, int rows, int cols,
+                                int tokens, void *stream);
+int q35_launch_mul_mat_vec_f32(const float *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens,
+                               void *stream);
+/* prefill tile path (mmq.cu:2232-2245 in the reference): returns -1
+ * ("decline, use q35_launch_mul_mat_vec") for every shape in this build. */
+int q35_launch_mul_mat_vec_tile(const void *d_w, const void *d_xq, float *d_out, int rows, int cols, int tokens,
+                                int ttype, void *stream);
+
+/* elementwise (api.h:135-154) */
+int q35_launch_l2norm_qk_scale(float *d_x, int nk, int kd, int k_offset, float eps, float qscale, void *stream);
+int q35_launch_scale_vec(float *d_x, float s, int n, void *stream);
+int q35_launch_scale_vec_strided(float *d_x, int offset, float s, int n, int tokens, int stride, void *stream);
+int q35_launch_add_resid(float *d_dst, const float *d_src, int n, void *stream);
+int q35_launch_copy_range(float *d_dst, const float *d_src, int n, void *stream);
+int q35_launch_deinterleave_qg(float *d_q, float *d_gate, const float *d_src, int heads, int hd, void *stream);
+int q35_launch_deinterleave_qg_strided(float *d_q, float *d_gate, const float *d_src, int heads, int hd,
+                                       int tokens, void *stream);
+int q35_launch_zero_buf(float *d_buf, int n, void *stream);
+int q35_launch_set_int1(int *d, int v, void *stream);
+
+/* norms (api.h:168-176) */
+int q35_launch_rmsnorm(float *d_out, const float *d_x, const float *d_w, int rows, int n, float eps, void *stream);
+int q35_launch_l2norm(float *d_x, int rows, int n, float eps, void *stream);
+int q35_launch_l2norm_strided(float *d_x, int row_offset, int rows, int n, float eps, int tokens, int row_stride,
+                              void *stream);
+
+/* activations / conv (api.h:185-202) */
+int q35_launch_silu(float *d_x, int n, void *stream);
+int q35_launch_mul_silu(float *d_out, const float *d_gate, int n, void *stream);
+int q35_launch_mul_sigmoid(float *d_out, const float *d_gate, int n, void *stream);
+int q35_launch_swiglu(float *d_gate, const float *d_up, int n, void *stream);
+int q35_launch_softmax(float *d_x, int n, void *stream);
+int q35_launch_conv_step(float *d_conv, float *d_y, const float *d_wconv, int n, void *stream);
+int q35_launch_conv_step_rows(float *d_conv, float *d_y, const float *d_wconv, int n, int tokens, int y_stride,
+                              void *stream);
+int q35_launch_argmax(const float *d_x, int n, int *d_out, void *stream);
+
+/* rotary embedding (api.h:217-239) */
+int q35_launch_rope64(float *d_x, int heads, int hd, int pos, float base, void *stream);
+int q35_launch_rope64_dpos(float *d_x, int heads, int hd, const void *d_dyn, void *stream);
+void *q35_func_rope64_dpos(void);
+int q35_launch_rope64_rows_dpos(float *d_x, int rows, int heads, int hd, const void *d_dyn, void *stream);
+void *q35_func_rope64_rows_dpos(void);
+int q35_launch_rope64_setenv(int *d_dyn, int pos, float base, void *stream);
+
+/* gated delta net (api.h:256-335): bit-exact with the CPU gdnFused.
+ * q35_launch_gdn_step_wy accepts the same arguments as the chunk form and
+ * computes the identical per-token recurrence. */
+int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
+                             int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,
+                             const float *d_gamma, const float *d_beta, int heads, int nk, int kd, int vd,
+                             void *stream);
+int q35_launch_gdn_step_rows_chunk(float *d_state, int state_stride, const float *d_k, int k_stride,
+                                   const float *d_v, int v_stride, const float *d_q, int q_stride, float *d_km,
+                                   int km_stride, float *d_delta, int delta_stride, float *d_out, int out_stride,
+                                   const float *d_gamma, int gamma_stride, const float *d_beta, int beta_stride,
+                                   int heads, int nk, int kd, int vd, int rows, void *stream);
+int q35_launch_gdn_step_wy(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
+                           int v_stride, const float *d_q, int q_stride, float *d_km, int km_stride, float *d_delta,
+                           int delta_stride, float *d_out, int out_stride, const float *d_gamma, int gamma_stride,
+                           const float *d_beta, int beta_stride, int heads, int nk, int kd, int vd, int rows,
+                           void *stream);
+int q35_launch_gdn_step(float *d_state, const float *d_k, const float *d_v, const float *d_q, float *d_km,
+                        float *d_delta, float *d_out, float gamma, float beta, int vd, void *stream);
+int q35_launch_gdn_gamma(const float *d_a_raw, float *d_b_raw, const float *d_ssm_a, const float *d_dt_bias,
+                         float *d_gamma, int nv, void *stream);
+int q35_launch_gdn_gamma_rows(const float *d_a_raw, float *d_b_raw, const float *d_ssm_a, const float *d_dt_bias,
+                              float *d_gamma, int nv, int tokens, int a_stride, int b_stride, int gamma_stride,
+                              void *stream);
+
+/* full-attention decode (api.h:337-415); hd must be 256 */
+int q35_launch_attn_decode(const float *d_q, const float *d_gate, const float *d_kcache, const float *d_vcache,
+                           float *d_att, float *d_gout, int slot, int heads, int gqa, int hd, int kv_dim,
+                           float scale, void *stream);
+int q35_launch_attn_chunk(const float *d_q, const float *d_gate, const float *d_kcache, const float *d_vcache,
+                          float *d_gout, int slot0, int rows, int heads, int gqa, int hd, int kv_dim, float scale,
+                          void *stream);
+int q35_attn_chunk_max_rows(int slot0);
+void *q35_func_attn_decode_dyn(void);
+void *q35_func_attn_decode_coal(void);
+void *q35_func_attn_score_split(void);
+int q35_launch_attn_decode_dyn(const float *d_q, const float *d_gate, const float *d_kcache, const float *d_vcache,
+                               float *d_att, float *d_gout, const int *d_slot, int heads, int gqa, int hd,
+                               int kv_dim, float scale, void *stream);
+int q35_launch_attn_decode_coal(const float *d_q, const float *d_gate, const float *d_kcache,
+                                const float *d_vcache, float *d_att, float *d_gout, int slot, int heads, int gqa,
+                                int hd, int kv_dim, float scale, void *stream);
+void *q35_func_attn_score_split_dyn(void);
+void *q35_func_attn_pv_split_dyn(void);
+void *q35_func_attn_softmax_dyn(void);
+void *q35_func_attn_reduce(void);
+int q35_launch_attn_decode_split_dyn(const float *d_q, const float *d_gate, const float *d_kcache,
+                                     const float *d_vcache, float *d_att, float *d_gout, float *d_part,
+                                     const int *d_slot, int heads, int gqa, int hd, int kv_dim, float scale,
+                                     int split, void *stream);
+int q35_launch_attn_decode_split2(const float *d_q, const float *d_gate, const float *d_kcache,
+                                  const float *d_vcache, float *d_att, float *d_gout, float *d_part, int slot,
+                                  int heads, int gqa, int hd, int kv_dim, float scale, int split, void *stream);
+
+/* codebook upload (api.h:433-442).  The IQ4_NL codebook is compiled into
+ * the kernels, so init is a no-op that reports success. */
+int q35_launch_init_tables(void *stream);
+unsigned long long q35_iq_tables_bytes(void);
+int q35_iq_tables_ready(void);
+void q35_launch_deinit_tables(void);
+
+/* geometry queries (api.h:446-464) */
+int q35_quant_act_block_elems(int ttype);
+int q35_quant_geom(int ttype, int *block_elems, int *block_bytes);
+int q35_mmq_dp4a_wants(int ttype);
+int q35_mmq_act_block_bytes(void);
+
+/* ===================================================================== */
+/* Part 2: additive B200 API (no counterpart in the reference)            */
+/* ===================================================================== */
+
+/* Last bounded-wait failure recorded by a kernel (0 = none); reading clears
+ * it.  A kernel that gives up on a wait records a site code and returns
+ * instead of hanging. */
+int q35b_get_error(int *code);
+
+/* Device weight encoder: `nblocks` native blocks of `ttype` from f32.
+ * Q8_0 is the reference's weight quantizer (src/quant_dequant.zig:1404);
+ * IQ4_NL / Q4_K / Q5_K / Q6_K are this library's deterministic encoders. */
+int q35b_quantize_weight(int ttype, const float *d_src, void *d_dst, long long nblocks, void *stream);
+
+/* Matvec over up to 4 matrices sharing one quantized activation, with an
+ * optional residual add (mode 1: out += W x).  out_ld = floats between
+ * tokens.  All matrices must share the activation family of `ttype[0]`. */
+int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
+                           float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq,
+                           int cols, int tokens, void *stream);
+
+/* ---- batched engine --------------------------------------------------- */
+typedef struct q35b_config {
+    int n_layers, full_attention_interval, hidden, n_heads, n_kv_heads;
+    int head_dim, n_ff, vocab;
+    float rms_eps, rope_freq_base;
+    int gdn_n_heads, gdn_num_k_heads, gdn_head_dim, conv_kernel;
+} q35b_config;
+
+typedef struct q35b_engine q35b_engine;
+
+/* Create an engine on the current device with `n_slots` sequence slots of
+ * `max_seq` positions each and room for `max_batch` tokens per step. */
+int q35b_engine_create(const q35b_config *cfg, int n_slots, int max_seq, int max_batch, q35b_engine **out);
+int q35b_engine_destroy(q35b_engine *e);
+/* Register a tensor by GGUF name (blk.N.attn_qkv.weight, token_embd.weight,
+ * output.weight, output_norm.weight, ...).  `d_data` is a DEVICE pointer the
+ * caller keeps alive.  1-D f32 tensors pass ttype 0 and cols = length. */
+int q35b_engine_set_tensor(q35b_engine *e, const char *name, int ttype, const void *d_data, long long rows,
+                           long long cols);
+/* Validate the tensor set and allocate slots / scratch.  0 or an error. */
+int q35b_engine_finalize(q35b_engine *e);
+/* Zero the GDN state / conv history of `slot` and forget its KV. */
+int q35b_engine_reset_slot(q35b_engine *e, int slot, void *stream);
+/* One decode step for `n` sequences, one token each (device arrays of n
+ * ints): token id, slot and position (= KV length before the step).  Writes
+ * the greedy next token per sequence to d_next; d_logits (n x vocab f32) is
+ * optional.  Captured into a CUDA graph per n when use_graph != 0. */
+int q35b_engine_step(q35b_engine *e, int n, const int *d_tokens, const int *d_slots, const int *d_pos,
+                     int *d_next, float *d_logits, int use_graph, void *stream);
+/* Same step with HOST arrays: copies in, runs, copies the next tokens out,
+ * synchronizes the stream. */
+int q35b_engine_step_host(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int *next,
+                          void *stream);
+/* The engine's own device input/output arrays (max_batch ints each).  A
+ * caller that keeps tokens/slots/positions there steps without copies:
+ * q35b_engine_step_dev runs the step on them (max_len = longest context in
+ * the batch, an upper bound is fine) and q35b_engine_advance feeds the
+ * sampled tokens back (tokens = next, positions += 1) on the device. */
+int q35b_engine_device_inputs(q35b_engine *e, int **d_tokens, int **d_slots, int **d_pos, int **d_next);
+int q35b_engine_step_dev(q35b_engine *e, int n, int max_len, int use_graph, void *stream);
+int q35b_engine_advance(q35b_engine *e, int n, void *stream);
+/* Device pointer of the residual stream after layer `li` for the last step
+ * (n x hidden f32), for per-layer parity probes; NULL when probing is off. */
+int q35b_engine_set_probe(q35b_engine *e, int on);
+const float *q35b_engine_layer_out(q35b_engine *e, int li);
+/* Kernel launches issued by the last step (graph replays count the nodes). */
+long long q35b_engine_launches_per_step(q35b_engine *e);
+
+/* ---- continuous batching --------------------------------------------- */
+/* Serve `nseq` independent requests to completion with at most
+ * `max_batch` in flight: each step packs one token of every active sequence
+ * (a prompt token while it is prefilling, its last sampled token after),
+ * admits waiting requests into freed slots, and stops a sequence after
+ * n_gen[i] generated tokens.  prompts are concatenated (prompt_off[i],
+ * prompt_len[i]); generated tokens go to out + out_off[i].  Returns 0 or an
+ * error; *steps receives the number of engine steps taken. */
+int q35b_serve(q35b_engine *e, int nseq, const int *prompts, const long long *prompt_off, const int *prompt_len,
+               const int *n_gen, int *out, const long long *out_off, int max_batch, long long *steps,
+               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,232 @@
+// common.cuh -- device helpers shared by every kernel of libq35b (sm_100a).
+//
+// Numerics contract: the library is built with -fmad=false, so no multiply
+// and add are ever fused behind the source's back.  Where an operation order
+// matters (block folds, norms, the GDN recurrence) the kernels spell it with
+// __fmul_rn / __fadd_rn so the rounding sequence is visible in the source.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define Q35_DEV __device__ __forceinline__
+
+namespace q35 {
+
+// GGUF TensorType ids (the values of api.h / src/gguf.zig:87-122).
+enum : int {
+    TT_F32 = 0, TT_F16 = 1, TT_Q4_0 = 2, TT_Q8_0 = 8, TT_Q4_K = 12, TT_Q5_K = 13,
+    TT_Q6_K = 14, TT_Q8_K = 15, TT_IQ4_NL = 20, TT_BF16 = 30,
+};
+
+// Native block geometry of the weight types this library serves.
+struct Geom { int elems, bytes, family; };  // family: 32 = Q8_0 act, 256 = Q8_K act
+__host__ __device__ inline Geom geom_of(int tt) {
+    switch (tt) {
+    case TT_Q8_0: return {32, 34, 32};
+    case TT_IQ4_NL: return {32, 18, 32};
+    case TT_Q4_K: return {256, 144, 256};
+    case TT_Q5_K: return {256, 176, 256};
+    case TT_Q6_K: return {256, 210, 256};
+    default: return {0, 0, 0};
+    }
+}
+
+// ---------------------------------------------------------------------------
+// error word: kernels that give up on a bounded wait record a site code here
+// ---------------------------------------------------------------------------
+// defined once: the library is a single translation unit (q35b.cu)
+__device__ int g_q35_error;
+
+Q35_DEV void set_error(int code) { atomicCAS(&g_q35_error, 0, code); }
+
+Q35_DEV uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// f16 <-> f32
+// ---------------------------------------------------------------------------
+Q35_DEV float f16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Round-to-nearest-even with inf/nan -> inf.  `sub_carry` is written when a
+// subnormal rounds up into the smallest normal: 0x0400 is IEEE; the reference
+// activation quantizer writes 0x0380 there (src/kernels/x86/kernels32.c:95)
+// and the activation path keeps that value so its bytes match exactly.
+__host__ __device__ inline uint16_t f32_to_f16_bits(float x, uint16_t sub_carry) {
+#ifdef __CUDA_ARCH__
+    const uint32_t u = __float_as_uint(x);
+#else
+    uint32_t u;
+    memcpy(&u, &x, 4);
+#endif
+    const uint32_t sign = (u & 0x80000000u) >> 16;
+    const uint32_t e = (u >> 23) & 0xFFu;
+    const uint32_t m = u & 0x7FFFFFu;
+    if (e >= 143u) return (uint16_t)(0x7C00u | sign);
+    if (e >= 113u) {
+        uint32_t keep = m >> 13;
+        const uint32_t drop = m & 0x1FFFu;
+        keep += (drop > 0x1000u) || (drop == 0x1000u && (keep & 1u));
+        uint32_t e16 = e - 112u;
+        if (keep >= 0x400u) { keep = 0; e16 += 1; }
+        if (e16 > 30u) return (uint16_t)(0x7C00u | sign);
+        return (uint16_t)(sign | (e16 << 10) | keep);
+    }
+    const uint32_t t = m | 0x800000u;
+    const int s = (int)(126u - e);
+    if (s >= 25) return (uint16_t)sign;
+    uint32_t keep = t >> s;
+    const uint32_t drop = t & ((1u << s) - 1u);
+    const uint32_t mid = 1u << (s - 1);
+    keep += (drop > mid) || (drop == mid && (keep & 1u));
+    if (keep >= 0x400u) return (uint16_t)(sub_carry | sign);
+    return (uint16_t)(sign | keep);
+}
+
+// ---------------------------------------------------------------------------
+// loads of 2-byte aligned data (GGUF blocks are only 2-byte aligned)
+// ---------------------------------------------------------------------------
+Q35_DEV uint16_t ld_u16(const uint8_t *p) { return *reinterpret_cast<const uint16_t *>(p); }
+
+// N little-endian words starting at a 2-aligned SHARED address.  Reads one
+// word past the end when p is 4-aligned, so staging buffers carry 16 bytes
+// of padding.
+template <int N>
+Q35_DEV void lds_words_a2(const uint8_t *p, uint32_t (&w)[N]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *b = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(a & 2u) * 8u;
+    uint32_t r[N + 1];
+#pragma unroll
+    for (int i = 0; i <= N; i++) r[i] = b[i];
+#pragma unroll
+    for (int i = 0; i < N; i++) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
+}
+
+// ---------------------------------------------------------------------------
+// IQ4_NL codebook (src/iq_tables.zig:429-432) as four packed words, and a
+// 16-entry byte lookup for four nibbles at once via two byte permutes.
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) |
+           ((uint32_t)(d & 0xFF) << 24);
+}
+constexpr uint32_t kIq4T0 = pack4(-127, -104, -83, -65);
+constexpr uint32_t kIq4T1 = pack4(-49, -35, -22, -10);
+constexpr uint32_t kIq4T2 = pack4(1, 13, 25, 38);
+constexpr uint32_t kIq4T3 = pack4(53, 69, 89, 113);
+
+// idx holds four 4-bit indices in the low nibble of each byte (0..15).
+Q35_DEV uint32_t iq4_lookup4(uint32_t idx) {
+    // selector nibbles: bit 0-2 of each index select one of 8 bytes of a table
+    // half; gather the 4 indices' low 3 bits into the byte_perm selector
+    const uint32_t s = (idx & 0x7u) | ((idx >> 4) & 0x70u) | ((idx >> 8) & 0x700u) | ((idx >> 12) & 0x7000u);
+    const uint32_t lo = __byte_perm(kIq4T0, kIq4T1, s);
+    const uint32_t hi = __byte_perm(kIq4T2, kIq4T3, s);
+    // bit 3 of each index picks hi: selector byte k = k + 4*bit3
+    const uint32_t b3 = (idx >> 3) & 0x01010101u;
+    const uint32_t sel = 0x3210u | ((b3 & 1u) << 2) | (((b3 >> 8) & 1u) << 6) |
+                         (((b3 >> 16) & 1u) << 10) | (((b3 >> 24) & 1u) << 14);
+    return __byte_perm(lo, hi, sel);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy PTX (shared::cta addresses)
+// ---------------------------------------------------------------------------
+Q35_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+Q35_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+Q35_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+Q35_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+Q35_DEV void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+Q35_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t tx) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(tx)
+                 : "memory");
+}
+Q35_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after ~2 s of wall time, records `site` in the error
+// word and returns false.  Nothing in this library waits without a bound.
+Q35_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; it++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && globaltimer() - t0 > 2000000000ull) {
+            set_error(site);
+            return false;
+        }
+    }
+}
+
+// global -> shared bulk copy completing on `bar` (16-byte aligned, size % 16 == 0)
+Q35_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+Q35_DEV void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// block-wide sum (order is fixed for a given blockDim, not the CPU's serial
+// order; used only where the reference's own device path also reduces)
+// ---------------------------------------------------------------------------
+Q35_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+Q35_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <int NWARPS>
+Q35_DEV float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.0f;
+    if (NWARPS == 1) return red[0];
+#pragma unroll
+    for (int i = 0; i < NWARPS; i++) s = __fadd_rn(s, red[i]);
+    return s;
+}
+
+// exp / log1p evaluated in double and rounded once to f32: within an ulp of
+// the C library's correctly-rounded-in-practice expf/log1pf on the host.
+Q35_DEV float exp_f(float x) { return (float)exp((double)x); }
+Q35_DEV float log1p_f(float x) { return (float)log1p((double)x); }
+Q35_DEV float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, exp_f(-x))); }
+Q35_DEV float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f(-x))); }
+Q35_DEV float softplus_f(float x) { return x > 20.0f ? x : log1p_f(exp_f(x)); }
+
+}  // namespace q35
+
+#define Q35_CHECK_LAUNCH() ((int)cudaGetLastError())

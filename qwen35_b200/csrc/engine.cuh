@@ -1,0 +1,437 @@
+// engine.cuh -- batched decode step of the Qwen3.5 hybrid model on B200.
+//
+// The op order per layer is src/engine.zig's forwardGdn (:1505-1672),
+// forwardFull (:1949-2023) and forwardMlp (:2027-2036); the model head is
+// forwardLogits (:1242-1312) with greedy argmax.  What is new here (the
+// reference is a single-sequence engine) is the batch: one step advances n
+// independent sequences by one token each, every sequence owning a slot in
+// the KV / GDN-state pools, with per-sequence positions read from device
+// memory so the whole step is one CUDA graph that replays for any positions.
+//
+// Kernels per layer (n tokens): fused rmsnorm+quantize -> one multi-matrix
+// GEMV launch -> layer core (conv/gamma/l2norm + GDN state step, or q/k norm
+// + RoPE + KV append + split-KV attention) -> fused norm/gate+quantize ->
+// GEMV with the residual add in its epilogue -> MLP (norm+quantize, gate|up
+// GEMV, swiglu+quantize, down GEMV + residual).
+#pragma once
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace q35 {
+
+// ---------------------------------------------------------------------------
+// fused producers of quantized activations (warp per quant block)
+// ---------------------------------------------------------------------------
+__host__ __device__ inline long long act_row_bytes(int cols, int fam) {
+    return fam == 32 ? (long long)(cols / 32) * 34 : (long long)(cols / 256) * 292;
+}
+
+// quantize a row whose element i is produced by `f(i)`; called by whole CTA
+template <class F>
+Q35_DEV void quantize_row_cta(F f, int cols, int fam, uint8_t *dst) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (fam == 32) {
+        for (int b = warp; b < cols / 32; b += nw) quant_q8_0_warp(f(b * 32 + lane), dst + (size_t)b * 34, lane);
+    } else {
+        for (int b = warp; b < cols / 256; b += nw) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = f(b * 256 + lane * 8 + i);
+            quant_q8_K_warp(v, dst + (size_t)b * 292, lane);
+        }
+    }
+}
+
+// rmsnorm(x_row, w) -> quantized activation (CTA per token)
+__global__ void __launch_bounds__(256) k_rmsnorm_quant(const float *x, const float *w, int cols, float eps, int fam,
+                                                       uint8_t *xq, long long xq_ld, const int *active) {
+    __shared__ float red[8];
+    const int t = blockIdx.x;
+    if (active && !active[t]) return;
+    const float *xr = x + (long long)t * cols;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < cols; i += 256) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    ss = block_sum<8>(ss, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+    quantize_row_cta([&](int i) { return __fmul_rn(__fmul_rn(xr[i], scale), w[i]); }, cols, fam,
+                     xq + (long long)t * xq_ld);
+}
+
+// silu(g)*u -> quantized activation; grid (blocks, tokens), warp per block
+__global__ void __launch_bounds__(256) k_swiglu_quant(const float *g, const float *u, int cols, int fam, uint8_t *xq,
+                                                      long long xq_ld) {
+    const int t = blockIdx.y;
+    const float *gr = g + (long long)t * cols, *ur = u + (long long)t * cols;
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
+    uint8_t *dst = xq + (long long)t * xq_ld;
+    if (fam == 32) {
+        if (b >= cols / 32) return;
+        const int i = b * 32 + lane;
+        quant_q8_0_warp(__fmul_rn(silu_f(gr[i]), ur[i]), dst + (size_t)b * 34, lane);
+    } else {
+        if (b >= cols / 256) return;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = b * 256 + lane * 8 + k;
+            v[k] = __fmul_rn(silu_f(gr[i]), ur[i]);
+        }
+        quant_q8_K_warp(v, dst + (size_t)b * 292, lane);
+    }
+}
+
+// plain f32 rows -> quantized activation; grid (blocks, tokens)
+__global__ void __launch_bounds__(256) k_quant_rows(const float *x, long long x_ld, int cols, int fam, uint8_t *xq,
+                                                    long long xq_ld) {
+    const int t = blockIdx.y;
+    const float *xr = x + (long long)t * x_ld;
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
+    uint8_t *dst = xq + (long long)t * xq_ld;
+    if (fam == 32) {
+        if (b >= cols / 32) return;
+        quant_q8_0_warp(xr[b * 32 + lane], dst + (size_t)b * 34, lane);
+    } else {
+        if (b >= cols / 256) return;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = xr[b * 256 + lane * 8 + k];
+        quant_q8_K_warp(v, dst + (size_t)b * 292, lane);
+    }
+}
+
+// gated RMSNorm over nv heads of vd, times silu(z), then quantize (CTA per
+// token).  engine.zig:1658-1667: rmsnormRows(gout, ssm_norm) then mulSilu(z).
+__global__ void __launch_bounds__(256) k_gated_norm_quant(const float *g, const float *z, const float *w, int nv,
+                                                          int vd, float eps, int fam, uint8_t *xq, long long xq_ld) {
+    __shared__ float sc[64];
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cols = nv * vd;
+    const float *gr = g + (long long)t * cols, *zr = z + (long long)t * cols;
+    for (int h = warp; h < nv; h += 8) {
+        float ss = 0.0f;
+        for (int i = lane; i < vd; i += 32) ss = __fadd_rn(ss, __fmul_rn(gr[h * vd + i], gr[h * vd + i]));
+        ss = warp_sum(ss);
+        if (lane == 0) sc[h] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)vd), eps)));
+    }
+    __syncthreads();
+    quantize_row_cta(
+        [&](int i) {
+            const int h = i / vd, j = i - h * vd;
+            const float y = __fmul_rn(__fmul_rn(gr[i], sc[h]), w[j]);
+            return __fmul_rn(y, silu_f(zr[i]));
+        },
+        cols, fam, xq + (long long)t * xq_ld);
+}
+
+// ---------------------------------------------------------------------------
+// GDN prelude: causal conv + silu (per-slot history), gamma/beta
+// ---------------------------------------------------------------------------
+__global__ void k_conv_batched(float *conv_pool, long long conv_slot, const int *slots, float *y, int n,
+                               const float *w) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    if (i >= n) return;
+    float *h = conv_pool + (long long)slots[t] * conv_slot + (long long)i * 3;
+    float *yp = y + (long long)t * n + i;
+    const float cur = *yp;
+    const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(h[0], w[i * 4]), __fmul_rn(h[1], w[i * 4 + 1])),
+                                        __fmul_rn(h[2], w[i * 4 + 2])),
+                              __fmul_rn(cur, w[i * 4 + 3]));
+    *yp = silu_f(s);
+    h[0] = h[1];
+    h[1] = h[2];
+    h[2] = cur;
+}
+
+// ---------------------------------------------------------------------------
+// attention prelude: q/gate split, q/k RMSNorm, RoPE at pos[t], KV append
+// CTA (head index, token): heads q heads then kv_heads kv heads; hd = 256
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const float *kb, const float *vb, float *q,
+                                                      float *gate, const float *qw, const float *kw, int heads,
+                                                      int kv_heads, float eps, float base, const int *pos,
+                                                      const int *slots, float *kpool, float *vpool, long long kv_slot) {
+    __shared__ float red[8];
+    __shared__ float y[256];
+    const int hi = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
+    const int hd = 256, q_dim = heads * hd, kv_dim = kv_heads * hd;
+    float x;
+    const float *wn;
+    if (hi < heads) {
+        const float *src = qg + (long long)t * 2 * q_dim + (long long)hi * 2 * hd;
+        x = src[j];
+        gate[(long long)t * q_dim + hi * hd + j] = src[hd + j];
+        wn = qw;
+    } else {
+        x = kb[(long long)t * kv_dim + (hi - heads) * hd + j];
+        wn = kw;
+    }
+    const float ss = block_sum<8>(__fmul_rn(x, x), red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    y[j] = __fmul_rn(__fmul_rn(x, scale), wn[j]);
+    __syncthreads();
+    const int p = pos[t];
+    if (j < 32) {
+        float c, s;
+        rope_cs(p, base, j, c, s);
+        const float a = y[j], b = y[j + 32];
+        y[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        y[j + 32] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+    __syncthreads();
+    if (hi < heads) {
+        q[(long long)t * q_dim + hi * hd + j] = y[j];
+    } else {
+        const int kh = hi - heads;
+        const long long base_off = (long long)slots[t] * kv_slot + (long long)p * kv_dim + kh * hd + j;
+        kpool[base_off] = y[j];
+        vpool[base_off] = vb[(long long)t * kv_dim + kh * hd + j];
+    }
+}
+
+__global__ void k_pos_to_len(const int *pos, int *len, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) len[i] = pos[i] + 1;
+}
+
+__global__ void k_copy_rows(float *dst, const float *src, long long n) {
+    Q35_GRID_STRIDE(i, n) dst[i] = src[i];
+}
+
+__global__ void k_zero_bytes(uint8_t *p, long long n) {
+    Q35_GRID_STRIDE(i, n) p[i] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// engine
+// ---------------------------------------------------------------------------
+struct Lin {
+    const uint8_t *w = nullptr;
+    int tt = -1;
+    long long rows = 0, cols = 0;
+};
+struct LayerW {
+    const float *attn_norm = nullptr, *post_norm = nullptr;
+    Lin qkv, gate, alpha, beta, ssm_out;
+    const float *conv1d = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
+    Lin q, k, v, o;
+    const float *q_norm = nullptr, *k_norm = nullptr;
+    Lin ffn_gate, ffn_up, ffn_down;
+};
+
+}  // namespace q35
+
+struct q35b_engine {
+    q35b_config c;
+    int n_slots = 0, max_seq = 0, max_batch = 0;
+    q35::Lin token_embd, output;
+    const float *output_norm = nullptr;
+    std::vector<q35::LayerW> L;
+    std::vector<int> gdn_idx, full_idx;  // per layer: index into its pool (-1 if other kind)
+    bool finalized = false, probe = false;
+    int device = 0;
+    // pools
+    float *conv_pool = nullptr, *state_pool = nullptr, *kpool = nullptr, *vpool = nullptr;
+    long long conv_slot = 0, state_slot = 0, kv_slot = 0;
+    // per-step buffers
+    int *d_in = nullptr;  // tokens | slots | pos (3 * max_batch)
+    int *d_len = nullptr, *d_next = nullptr;
+    float *x = nullptr, *qkv = nullptr, *z = nullptr, *ab = nullptr, *gam = nullptr, *gout = nullptr;
+    float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;
+    float *logits = nullptr, *part_acc = nullptr, *part_ml = nullptr, *probe_buf = nullptr;
+    uint8_t *xq = nullptr;
+    long long xq_ld = 0;
+    std::map<long long, cudaGraphExec_t> graphs;
+    std::vector<void *> allocs;
+    long long launches = 0;
+};
+
+namespace q35 {
+
+inline int eng_alloc(q35b_engine *e, void **p, size_t bytes) {
+    cudaError_t r = cudaMalloc(p, bytes ? bytes : 16);
+    if (r != cudaSuccess) return (int)r;
+    e->allocs.push_back(*p);
+    return 0;
+}
+
+inline bool is_full_layer(const q35b_config &c, int li) {
+    return c.full_attention_interval > 0 && li % c.full_attention_interval == c.full_attention_interval - 1;
+}
+
+#define Q35_TRY(x)                 \
+    do {                           \
+        int _rc = (x);             \
+        if (_rc) return _rc;       \
+    } while (0)
+
+// one GEMV launch over up to 4 matrices of the same family sharing `xq`
+inline int eng_gemv(q35b_engine *e, int n, std::initializer_list<GemvSegDesc> segs, const uint8_t *xq, int cols,
+                    cudaStream_t st) {
+    e->launches += (n + GV_MAX_NT - 1) / GV_MAX_NT;
+    return gemv_launch(segs.begin(), (int)segs.size(), xq, cols, n, st);
+}
+
+inline int family_of(const Lin &l) { return geom_of(l.tt).family; }
+inline long long weight_row_bytes(int tt, long long cols) {
+    const Geom g = geom_of(tt);
+    return g.elems ? cols / g.elems * g.bytes : 0;
+}
+
+inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cudaStream_t st) {
+    k_rmsnorm_quant<<<n, 256, 0, st>>>(e->x, w, e->c.hidden, e->c.rms_eps, fam, e->xq, e->xq_ld, nullptr);
+    e->launches++;
+    return (int)cudaGetLastError();
+}
+
+inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
+    const q35b_config &c = e->c;
+    const LayerW &W = e->L[li];
+    const int nv = c.gdn_n_heads, nk = c.gdn_num_k_heads, kd = c.gdn_head_dim;
+    const int kq = nk * kd, vdim = nv * kd, conv_dim = 2 * kq + vdim;
+    const int fam = family_of(W.qkv);
+    Q35_TRY(eng_rmsnorm_quant(e, n, W.attn_norm, fam, st));
+    Q35_TRY(eng_gemv(e, n,
+                     {{W.qkv.w, e->qkv, W.qkv.rows, W.qkv.tt, conv_dim, GV_STORE},
+                      {W.gate.w, e->z, W.gate.rows, W.gate.tt, vdim, GV_STORE},
+                      {W.alpha.w, e->ab, W.alpha.rows, W.alpha.tt, 2 * nv, GV_STORE},
+                      {W.beta.w, e->ab + nv, W.beta.rows, W.beta.tt, 2 * nv, GV_STORE}},
+                     e->xq, c.hidden, st));
+    const int gi = e->gdn_idx[li];
+    const int *slots = e->d_in + e->max_batch;
+    k_conv_batched<<<dim3((conv_dim + 127) / 128, n), 128, 0, st>>>(e->conv_pool + gi * (long long)e->n_slots * e->conv_slot,
+                                                                      e->conv_slot, slots, e->qkv, conv_dim, W.conv1d);
+    k_gdn_gamma<<<ew_grid((long long)nv * n, 128), 128, 0, st>>>(e->ab, e->ab + nv, W.ssm_a, W.dt_bias, e->gam, nv, n,
+                                                                 2 * nv, 2 * nv, nv);
+    const float qscale = 1.0f / sqrtf((float)kd);
+    k_l2norm<128><<<nk * n, 128, 0, st>>>(e->qkv, 0, nk, kd, 1e-6f, conv_dim, qscale, 1);
+    k_l2norm<128><<<nk * n, 128, 0, st>>>(e->qkv, kq, nk, kd, 1e-6f, conv_dim, 1.0f, 0);
+    e->launches += 4;
+    Q35_TRY((int)cudaGetLastError());
+    GdnArgs a{};
+    a.state = e->state_pool + gi * (long long)e->n_slots * e->state_slot;
+    a.state_head = (long long)kd * kd;
+    a.state_slot = e->state_slot;
+    a.slots = slots;
+    a.k = e->qkv + kq; a.k_tok = conv_dim; a.k_head = kd;
+    a.q = e->qkv; a.q_tok = conv_dim; a.q_head = kd;
+    a.v = e->qkv + 2 * kq; a.v_tok = conv_dim; a.v_head = kd;
+    a.out = e->gout; a.out_tok = vdim; a.out_head = kd;
+    a.gamma = e->gam; a.g_tok = nv;
+    a.beta = e->ab + nv; a.b_tok = 2 * nv;
+    a.heads = nv; a.nk = nk; a.rows = 1;
+    Q35_TRY(gdn_launch(a, n, st));
+    e->launches++;
+    const int fo = family_of(W.ssm_out);
+    k_gated_norm_quant<<<n, 256, 0, st>>>(e->gout, e->z, W.ssm_norm, nv, kd, c.rms_eps, fo, e->xq, e->xq_ld);
+    e->launches++;
+    Q35_TRY((int)cudaGetLastError());
+    return eng_gemv(e, n, {{W.ssm_out.w, e->x, W.ssm_out.rows, W.ssm_out.tt, c.hidden, GV_ADD}}, e->xq, vdim, st);
+}
+
+inline int eng_attn_nsplit(int max_len) {
+    int ns = (max_len + 255) / 256, p = 1;
+    while (p < ns) p <<= 1;
+    return p;
+}
+
+inline int eng_layer_full(q35b_engine *e, int li, int n, int nsplit, cudaStream_t st) {
+    const q35b_config &c = e->c;
+    const LayerW &W = e->L[li];
+    const int heads = c.n_heads, kvh = c.n_kv_heads, hd = c.head_dim;
+    const int q_dim = heads * hd, kv_dim = kvh * hd;
+    Q35_TRY(eng_rmsnorm_quant(e, n, W.attn_norm, family_of(W.q), st));
+    Q35_TRY(eng_gemv(e, n,
+                     {{W.q.w, e->qkv, W.q.rows, W.q.tt, 2 * q_dim, GV_STORE},
+                      {W.k.w, e->kb, W.k.rows, W.k.tt, kv_dim, GV_STORE},
+                      {W.v.w, e->vb, W.v.rows, W.v.tt, kv_dim, GV_STORE}},
+                     e->xq, c.hidden, st));
+    const int fi = e->full_idx[li];
+    float *kp = e->kpool + fi * (long long)e->n_slots * e->kv_slot;
+    float *vp = e->vpool + fi * (long long)e->n_slots * e->kv_slot;
+    const int *slots = e->d_in + e->max_batch, *pos = e->d_in + 2 * e->max_batch;
+    k_attn_prelude<<<dim3(heads + kvh, n), 256, 0, st>>>(e->qkv, e->kb, e->vb, e->q, e->gate, W.q_norm, W.k_norm, heads,
+                                                        kvh, c.rms_eps, c.rope_freq_base, pos, slots, kp, vp,
+                                                        e->kv_slot);
+    e->launches++;
+    Q35_TRY((int)cudaGetLastError());
+    AttnArgs a{};
+    a.q = e->q;
+    a.gate = e->gate;
+    a.q_tok = q_dim;
+    a.kc = kp;
+    a.vc = vp;
+    a.kv_slot = e->kv_slot;
+    a.kv_dim = kv_dim;
+    a.slots = slots;
+    a.lens = e->d_len;
+    a.out = e->gout;
+    a.out_tok = q_dim;
+    a.part_acc = e->part_acc;
+    a.part_ml = e->part_ml;
+    a.nsplit = nsplit;
+    a.split_len = 256;
+    a.heads = heads;
+    a.kv_heads = kvh;
+    a.scale = 1.0f / sqrtf((float)hd);
+    Q35_TRY(attn_launch(a, n, nsplit * 256, st));
+    e->launches += nsplit > 1 ? 2 : 1;
+    const int fo = family_of(W.o);
+    k_quant_rows<<<dim3((q_dim / (fo == 32 ? 32 : 256) + 7) / 8, n), 256, 0, st>>>(e->gout, q_dim, q_dim, fo, e->xq,
+                                                                                  e->xq_ld);
+    e->launches++;
+    Q35_TRY((int)cudaGetLastError());
+    return eng_gemv(e, n, {{W.o.w, e->x, W.o.rows, W.o.tt, c.hidden, GV_ADD}}, e->xq, q_dim, st);
+}
+
+inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
+    const q35b_config &c = e->c;
+    const LayerW &W = e->L[li];
+    Q35_TRY(eng_rmsnorm_quant(e, n, W.post_norm, family_of(W.ffn_gate), st));
+    Q35_TRY(eng_gemv(e, n,
+                     {{W.ffn_gate.w, e->mh, W.ffn_gate.rows, W.ffn_gate.tt, c.n_ff, GV_STORE},
+                      {W.ffn_up.w, e->mh1, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}},
+                     e->xq, c.hidden, st));
+    const int fd = family_of(W.ffn_down);
+    k_swiglu_quant<<<dim3((c.n_ff / (fd == 32 ? 32 : 256) + 7) / 8, n), 256, 0, st>>>(e->mh, e->mh1, c.n_ff, fd, e->xq,
+                                                                                     e->xq_ld);
+    e->launches++;
+    Q35_TRY((int)cudaGetLastError());
+    return eng_gemv(e, n, {{W.ffn_down.w, e->x, W.ffn_down.rows, W.ffn_down.tt, c.hidden, GV_ADD}}, e->xq, c.n_ff, st);
+}
+
+// the whole step body (graph-capturable: every per-step value is in device memory)
+inline int eng_step_body(q35b_engine *e, int n, int nsplit, cudaStream_t st) {
+    const q35b_config &c = e->c;
+    e->launches = 0;
+    const int *tok = e->d_in;
+    k_embed_rows<<<dim3((c.hidden + 255) / 256, n), 256, 0, st>>>(
+        e->token_embd.tt, e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x, c.hidden);
+    k_pos_to_len<<<(n + 127) / 128, 128, 0, st>>>(e->d_in + 2 * e->max_batch, e->d_len, n);
+    e->launches += 2;
+    Q35_TRY((int)cudaGetLastError());
+    for (int li = 0; li < c.n_layers; li++) {
+        if (is_full_layer(c, li))
+            Q35_TRY(eng_layer_full(e, li, n, nsplit, st));
+        else
+            Q35_TRY(eng_layer_gdn(e, li, n, st));
+        Q35_TRY(eng_mlp(e, li, n, st));
+        if (e->probe) {
+            k_copy_rows<<<ew_grid((long long)n * c.hidden), 256, 0, st>>>(
+                e->probe_buf + (long long)li * e->max_batch * c.hidden, e->x, (long long)n * c.hidden);
+            e->launches++;
+        }
+    }
+    const Lin &H = e->output.w ? e->output : e->token_embd;
+    Q35_TRY(eng_rmsnorm_quant(e, n, e->output_norm, family_of(H), st));
+    Q35_TRY(eng_gemv(e, n, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, e->xq, c.hidden, st));
+    k_argmax<<<n, 1024, 0, st>>>(e->logits, c.vocab, c.vocab, e->d_next);
+    e->launches++;
+    return (int)cudaGetLastError();
+}
+
+}  // namespace q35

@@ -1,0 +1,373 @@
+// engine_api.cuh -- q35b_engine_* / q35b_serve: the batched engine's C ABI.
+#pragma once
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <deque>
+
+#include "engine.cuh"
+
+using namespace q35;
+
+namespace {
+
+int set_lin(Lin &l, int tt, const void *d, long long rows, long long cols) {
+    if (!geom_of(tt).elems || !d || rows <= 0 || cols <= 0 || cols % geom_of(tt).elems) return (int)cudaErrorInvalidValue;
+    l.w = reinterpret_cast<const uint8_t *>(d);
+    l.tt = tt;
+    l.rows = rows;
+    l.cols = cols;
+    return 0;
+}
+
+bool lin_ok(const Lin &l, long long rows, long long cols) { return l.w && l.rows == rows && l.cols == cols; }
+
+long long graph_key(int n, int nsplit) { return (long long)n * 64 + nsplit; }
+
+}  // namespace
+
+extern "C" {
+
+int q35b_engine_create(const q35b_config *cfg, int n_slots, int max_seq, int max_batch, q35b_engine **out) {
+    if (!cfg || !out || n_slots <= 0 || max_seq <= 0 || max_batch <= 0) return (int)cudaErrorInvalidValue;
+    if (cfg->gdn_head_dim != GDN_KD || cfg->head_dim != ATT_HD || cfg->conv_kernel != 4)
+        return (int)cudaErrorInvalidValue;
+    if (cfg->n_heads % cfg->n_kv_heads || cfg->n_heads / cfg->n_kv_heads > ATT_MAXG) return (int)cudaErrorInvalidValue;
+    if (cfg->gdn_num_k_heads <= 0 || cfg->gdn_n_heads % cfg->gdn_num_k_heads || cfg->gdn_n_heads > 64)
+        return (int)cudaErrorInvalidValue;
+    q35b_engine *e = new q35b_engine();
+    e->c = *cfg;
+    e->n_slots = n_slots;
+    e->max_seq = max_seq;
+    e->max_batch = max_batch;
+    e->L.resize(cfg->n_layers);
+    cudaGetDevice(&e->device);
+    *out = e;
+    return 0;
+}
+
+int q35b_engine_destroy(q35b_engine *e) {
+    if (!e) return 0;
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (void *p : e->allocs) cudaFree(p);
+    delete e;
+    return 0;
+}
+
+int q35b_engine_set_tensor(q35b_engine *e, const char *name, int tt, const void *d, long long rows, long long cols) {
+    if (!e || !name || e->finalized) return (int)cudaErrorInvalidValue;
+    if (!strcmp(name, "token_embd.weight")) return set_lin(e->token_embd, tt, d, rows, cols);
+    if (!strcmp(name, "output.weight")) return set_lin(e->output, tt, d, rows, cols);
+    if (!strcmp(name, "output_norm.weight")) {
+        if (tt != TT_F32 || cols != e->c.hidden) return (int)cudaErrorInvalidValue;
+        e->output_norm = reinterpret_cast<const float *>(d);
+        return 0;
+    }
+    int li = -1, off = 0;
+    if (sscanf(name, "blk.%d.%n", &li, &off) != 1 || li < 0 || li >= e->c.n_layers) return (int)cudaErrorInvalidValue;
+    const char *t = name + off;
+    LayerW &W = e->L[li];
+    struct F { const char *n; const float **p; };
+    const F f32s[] = {{"attn_norm.weight", &W.attn_norm},   {"post_attention_norm.weight", &W.post_norm},
+                      {"ssm_conv1d.weight", &W.conv1d},     {"ssm_dt.bias", &W.dt_bias},
+                      {"ssm_a", &W.ssm_a},                  {"ssm_norm.weight", &W.ssm_norm},
+                      {"attn_q_norm.weight", &W.q_norm},    {"attn_k_norm.weight", &W.k_norm}};
+    for (const F &x : f32s)
+        if (!strcmp(t, x.n)) {
+            if (tt != TT_F32 || !d) return (int)cudaErrorInvalidValue;
+            *x.p = reinterpret_cast<const float *>(d);
+            return 0;
+        }
+    struct Q { const char *n; Lin *l; };
+    const Q lins[] = {{"attn_qkv.weight", &W.qkv},   {"attn_gate.weight", &W.gate}, {"ssm_alpha.weight", &W.alpha},
+                      {"ssm_beta.weight", &W.beta},  {"ssm_out.weight", &W.ssm_out}, {"attn_q.weight", &W.q},
+                      {"attn_k.weight", &W.k},       {"attn_v.weight", &W.v},        {"attn_output.weight", &W.o},
+                      {"ffn_gate.weight", &W.ffn_gate}, {"ffn_up.weight", &W.ffn_up}, {"ffn_down.weight", &W.ffn_down}};
+    for (const Q &x : lins)
+        if (!strcmp(t, x.n)) return set_lin(*x.l, tt, d, rows, cols);
+    return (int)cudaErrorInvalidValue;
+}
+
+int q35b_engine_finalize(q35b_engine *e) {
+    if (!e || e->finalized) return (int)cudaErrorInvalidValue;
+    const q35b_config &c = e->c;
+    const long long h = c.hidden, nv = c.gdn_n_heads, nk = c.gdn_num_k_heads, kd = c.gdn_head_dim;
+    const long long kq = nk * kd, vdim = nv * kd, conv_dim = 2 * kq + vdim;
+    const long long q_dim = (long long)c.n_heads * c.head_dim, kv_dim = (long long)c.n_kv_heads * c.head_dim;
+    if (!lin_ok(e->token_embd, c.vocab, h) || !e->output_norm) return (int)cudaErrorInvalidValue;
+    if (e->output.w && !lin_ok(e->output, c.vocab, h)) return (int)cudaErrorInvalidValue;
+    int ngdn = 0, nfull = 0;
+    for (int li = 0; li < c.n_layers; li++) {
+        const LayerW &W = e->L[li];
+        if (!W.attn_norm || !W.post_norm || !lin_ok(W.ffn_gate, c.n_ff, h) || !lin_ok(W.ffn_up, c.n_ff, h) ||
+            !lin_ok(W.ffn_down, h, c.n_ff))
+            return (int)cudaErrorInvalidValue;
+        if (family_of(W.ffn_gate) != family_of(W.ffn_up)) return (int)cudaErrorInvalidValue;
+        if (is_full_layer(c, li)) {
+            if (!lin_ok(W.q, 2 * q_dim, h) || !lin_ok(W.k, kv_dim, h) || !lin_ok(W.v, kv_dim, h) ||
+                !lin_ok(W.o, h, q_dim) || !W.q_norm || !W.k_norm)
+                return (int)cudaErrorInvalidValue;
+            if (family_of(W.q) != family_of(W.k) || family_of(W.q) != family_of(W.v)) return (int)cudaErrorInvalidValue;
+            e->full_idx.push_back(nfull++);
+            e->gdn_idx.push_back(-1);
+        } else {
+            if (!lin_ok(W.qkv, conv_dim, h) || !lin_ok(W.gate, vdim, h) || !lin_ok(W.alpha, nv, h) ||
+                !lin_ok(W.beta, nv, h) || !lin_ok(W.ssm_out, h, vdim) || !W.conv1d || !W.dt_bias || !W.ssm_a ||
+                !W.ssm_norm)
+                return (int)cudaErrorInvalidValue;
+            const int f = family_of(W.qkv);
+            if (family_of(W.gate) != f || family_of(W.alpha) != f || family_of(W.beta) != f)
+                return (int)cudaErrorInvalidValue;
+            e->gdn_idx.push_back(ngdn++);
+            e->full_idx.push_back(-1);
+        }
+    }
+    const long long B = e->max_batch, S = e->n_slots;
+    e->conv_slot = conv_dim * 3;
+    e->state_slot = nv * kd * kd;
+    e->kv_slot = (long long)e->max_seq * kv_dim;
+    void *p;
+#define ALLOC(field, bytes)                                  \
+    do {                                                     \
+        Q35_TRY(eng_alloc(e, &p, (size_t)(bytes)));          \
+        e->field = reinterpret_cast<decltype(e->field)>(p);  \
+    } while (0)
+    ALLOC(conv_pool, 4 * ngdn * S * e->conv_slot);
+    ALLOC(state_pool, 4 * ngdn * S * e->state_slot);
+    ALLOC(kpool, 4 * nfull * S * e->kv_slot);
+    ALLOC(vpool, 4 * nfull * S * e->kv_slot);
+    ALLOC(d_in, 4 * 3 * B);
+    ALLOC(d_len, 4 * B);
+    ALLOC(d_next, 4 * B);
+    ALLOC(x, 4 * B * h);
+    ALLOC(qkv, 4 * B * std::max(conv_dim, 2 * q_dim));
+    ALLOC(z, 4 * B * std::max(vdim, q_dim));
+    ALLOC(ab, 4 * B * 2 * nv);
+    ALLOC(gam, 4 * B * nv);
+    ALLOC(gout, 4 * B * std::max(vdim, q_dim));
+    ALLOC(q, 4 * B * q_dim);
+    ALLOC(gate, 4 * B * q_dim);
+    ALLOC(kb, 4 * B * kv_dim);
+    ALLOC(vb, 4 * B * kv_dim);
+    ALLOC(mh, 4 * B * c.n_ff);
+    ALLOC(mh1, 4 * B * c.n_ff);
+    ALLOC(logits, 4 * B * (long long)c.vocab);
+    const long long maxsplit = (e->max_seq + 255) / 256 + 1;
+    ALLOC(part_acc, 4 * B * c.n_heads * maxsplit * ATT_HD);
+    ALLOC(part_ml, 4 * B * c.n_heads * maxsplit * 2);
+    ALLOC(probe_buf, 4 * (long long)c.n_layers * B * h);
+    long long maxcols = std::max(std::max(h, (long long)c.n_ff), std::max(vdim, q_dim));
+    e->xq_ld = ((maxcols / 32 * 34 + maxcols / 256 * 292) + 15) & ~15LL;
+    ALLOC(xq, e->xq_ld * B + 64);
+#undef ALLOC
+    Q35_TRY((int)cudaMemset(e->conv_pool, 0, 4 * ngdn * S * e->conv_slot));
+    Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));
+    Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 3 * B));
+    Q35_TRY((int)cudaDeviceSynchronize());
+    e->finalized = true;
+    return 0;
+}
+
+__global__ void k_reset_slot(float *conv_pool, long long conv_total, long long conv_slot, float *state_pool,
+                             long long state_total, long long state_slot, int n_layers_pool, int slot) {
+    // conv: n_gdn layers x [slot] x conv_slot ; state likewise
+    const long long nc = (long long)n_layers_pool * conv_slot, ns = (long long)n_layers_pool * state_slot;
+    Q35_GRID_STRIDE(i, nc + ns) {
+        if (i < nc) {
+            const long long l = i / conv_slot, j = i - l * conv_slot;
+            conv_pool[l * conv_total + slot * conv_slot + j] = 0.0f;
+        } else {
+            const long long k = i - nc, l = k / state_slot, j = k - l * state_slot;
+            state_pool[l * state_total + slot * state_slot + j] = 0.0f;
+        }
+    }
+}
+
+int q35b_engine_reset_slot(q35b_engine *e, int slot, void *stream) {
+    if (!e || !e->finalized || slot < 0 || slot >= e->n_slots) return (int)cudaErrorInvalidValue;
+    int ngdn = 0;
+    for (int v : e->gdn_idx) ngdn += v >= 0;
+    if (ngdn == 0) return 0;
+    const long long tot = (long long)ngdn * (e->conv_slot + e->state_slot);
+    k_reset_slot<<<ew_grid(tot), 256, 0, S(stream)>>>(e->conv_pool, (long long)e->n_slots * e->conv_slot, e->conv_slot,
+                                                      e->state_pool, (long long)e->n_slots * e->state_slot,
+                                                      e->state_slot, ngdn, slot);
+    return (int)cudaGetLastError();
+}
+
+int q35b_engine_set_probe(q35b_engine *e, int on) {
+    if (!e) return (int)cudaErrorInvalidValue;
+    e->probe = on != 0;
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+    return 0;
+}
+
+const float *q35b_engine_layer_out(q35b_engine *e, int li) {
+    if (!e || !e->finalized || !e->probe || li < 0 || li >= e->c.n_layers) return nullptr;
+    return e->probe_buf + (long long)li * e->max_batch * e->c.hidden;
+}
+
+long long q35b_engine_launches_per_step(q35b_engine *e) { return e ? e->launches : 0; }
+
+// Launch the step for `n` sequences whose inputs are already in e->d_in.
+static int engine_run(q35b_engine *e, int n, int max_len, int use_graph, cudaStream_t st) {
+    const int nsplit = eng_attn_nsplit(max_len);
+    if (!use_graph) return eng_step_body(e, n, nsplit, st);
+    const long long key = graph_key(n, nsplit);
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaStream_t cs;
+        Q35_TRY((int)cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+        cudaGraph_t g = nullptr;
+        int rc = (int)cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+        if (!rc) {
+            const int brc = eng_step_body(e, n, nsplit, cs);
+            rc = (int)cudaStreamEndCapture(cs, &g);
+            if (brc) rc = brc;
+        }
+        cudaGraphExec_t ge = nullptr;
+        if (!rc) rc = (int)cudaGraphInstantiate(&ge, g, 0);
+        if (g) cudaGraphDestroy(g);
+        cudaStreamDestroy(cs);
+        if (rc) return rc;
+        it = e->graphs.emplace(key, ge).first;
+    }
+    return (int)cudaGraphLaunch(it->second, st);
+}
+
+__global__ void k_max_pos(const int *pos, int n, int *out) {
+    int m = 0;
+    for (int i = 0; i < n; i++) m = max(m, pos[i]);
+    *out = m;
+}
+
+int q35b_engine_step(q35b_engine *e, int n, const int *d_tokens, const int *d_slots, const int *d_pos, int *d_next,
+                     float *d_logits, int use_graph, void *stream) {
+    if (!e || !e->finalized || n <= 0 || n > e->max_batch) return (int)cudaErrorInvalidValue;
+    cudaStream_t st = S(stream);
+    const size_t b = (size_t)n * 4;
+    // inputs the graph reads live at fixed addresses inside the engine
+    if (d_tokens != e->d_in) Q35_TRY((int)cudaMemcpyAsync(e->d_in, d_tokens, b, cudaMemcpyDeviceToDevice, st));
+    if (d_slots != e->d_in + e->max_batch)
+        Q35_TRY((int)cudaMemcpyAsync(e->d_in + e->max_batch, d_slots, b, cudaMemcpyDeviceToDevice, st));
+    if (d_pos != e->d_in + 2 * e->max_batch)
+        Q35_TRY((int)cudaMemcpyAsync(e->d_in + 2 * e->max_batch, d_pos, b, cudaMemcpyDeviceToDevice, st));
+    // the split count must cover the longest context; without a host copy of
+    // the positions it covers the whole slot
+    Q35_TRY(engine_run(e, n, e->max_seq, use_graph, st));
+    if (d_next && d_next != e->d_next)
+        Q35_TRY((int)cudaMemcpyAsync(d_next, e->d_next, b, cudaMemcpyDeviceToDevice, st));
+    if (d_logits)
+        Q35_TRY((int)cudaMemcpyAsync(d_logits, e->logits, (size_t)n * e->c.vocab * 4, cudaMemcpyDeviceToDevice, st));
+    return 0;
+}
+
+int q35b_engine_step_host(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int *next,
+                          void *stream) {
+    if (!e || !e->finalized || n <= 0 || n > e->max_batch) return (int)cudaErrorInvalidValue;
+    cudaStream_t st = S(stream);
+    const size_t b = (size_t)n * 4;
+    int max_len = 1;
+    for (int i = 0; i < n; i++) {
+        if (pos[i] < 0 || pos[i] >= e->max_seq || slots[i] < 0 || slots[i] >= e->n_slots)
+            return (int)cudaErrorInvalidValue;
+        max_len = std::max(max_len, pos[i] + 1);
+    }
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in, tokens, b, cudaMemcpyHostToDevice, st));
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in + e->max_batch, slots, b, cudaMemcpyHostToDevice, st));
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in + 2 * e->max_batch, pos, b, cudaMemcpyHostToDevice, st));
+    Q35_TRY(engine_run(e, n, max_len, 1, st));
+    Q35_TRY((int)cudaMemcpyAsync(next, e->d_next, b, cudaMemcpyDeviceToHost, st));
+    return (int)cudaStreamSynchronize(st);
+}
+
+int q35b_engine_device_inputs(q35b_engine *e, int **d_tokens, int **d_slots, int **d_pos, int **d_next) {
+    if (!e || !e->finalized) return (int)cudaErrorInvalidValue;
+    if (d_tokens) *d_tokens = e->d_in;
+    if (d_slots) *d_slots = e->d_in + e->max_batch;
+    if (d_pos) *d_pos = e->d_in + 2 * e->max_batch;
+    if (d_next) *d_next = e->d_next;
+    return 0;
+}
+
+__global__ void k_advance(int *tok, int *pos, const int *next, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        tok[i] = next[i];
+        pos[i] += 1;
+    }
+}
+
+int q35b_engine_step_dev(q35b_engine *e, int n, int max_len, int use_graph, void *stream) {
+    if (!e || !e->finalized || n <= 0 || n > e->max_batch || max_len <= 0 || max_len > e->max_seq)
+        return (int)cudaErrorInvalidValue;
+    return engine_run(e, n, max_len, use_graph, S(stream));
+}
+
+int q35b_engine_advance(q35b_engine *e, int n, void *stream) {
+    if (!e || !e->finalized || n <= 0 || n > e->max_batch) return (int)cudaErrorInvalidValue;
+    k_advance<<<(n + 127) / 128, 128, 0, S(stream)>>>(e->d_in, e->d_in + 2 * e->max_batch, e->d_next, n);
+    return (int)cudaGetLastError();
+}
+
+int q35b_serve(q35b_engine *e, int nseq, const int *prompts, const long long *prompt_off, const int *prompt_len,
+               const int *n_gen, int *out, const long long *out_off, int max_batch, long long *steps, void *stream) {
+    if (!e || !e->finalized || nseq < 0 || max_batch <= 0) return (int)cudaErrorInvalidValue;
+    max_batch = std::min(max_batch, std::min(e->max_batch, e->n_slots));
+    struct Act { int seq, slot, pos, gen, last; };
+    std::deque<int> waiting;
+    for (int i = 0; i < nseq; i++) {
+        if (prompt_len[i] <= 0 || n_gen[i] <= 0) continue;
+        if (prompt_len[i] + n_gen[i] - 1 > e->max_seq) return (int)cudaErrorInvalidValue;
+        waiting.push_back(i);
+    }
+    std::vector<int> free_slots;
+    for (int s = e->n_slots - 1; s >= 0; s--) free_slots.push_back(s);
+    std::vector<Act> act;
+    std::vector<int> tok, slot, pos, next;
+    long long nstep = 0;
+    cudaStream_t st = S(stream);
+    while (!waiting.empty() || !act.empty()) {
+        while ((int)act.size() < max_batch && !waiting.empty() && !free_slots.empty()) {
+            const int s = free_slots.back();
+            free_slots.pop_back();
+            Q35_TRY(q35b_engine_reset_slot(e, s, st));
+            act.push_back({waiting.front(), s, 0, 0, -1});
+            waiting.pop_front();
+        }
+        const int n = (int)act.size();
+        tok.resize(n);
+        slot.resize(n);
+        pos.resize(n);
+        next.resize(n);
+        for (int i = 0; i < n; i++) {
+            const Act &a = act[i];
+            tok[i] = a.pos < prompt_len[a.seq] ? prompts[prompt_off[a.seq] + a.pos] : a.last;
+            slot[i] = a.slot;
+            pos[i] = a.pos;
+        }
+        Q35_TRY(q35b_engine_step_host(e, n, tok.data(), slot.data(), pos.data(), next.data(), st));
+        nstep++;
+        std::vector<Act> keep;
+        for (int i = 0; i < n; i++) {
+            Act a = act[i];
+            const bool emits = a.pos >= prompt_len[a.seq] - 1;
+            a.pos++;
+            if (emits) {
+                out[out_off[a.seq] + a.gen] = next[i];
+                a.gen++;
+                a.last = next[i];
+            }
+            if (a.gen >= n_gen[a.seq])
+                free_slots.push_back(a.slot);
+            else
+                keep.push_back(a);
+        }
+        act.swap(keep);
+    }
+    if (steps) *steps = nstep;
+    return 0;
+}
+
+}  // extern "C"

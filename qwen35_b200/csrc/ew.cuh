@@ -1,0 +1,229 @@
+// ew.cuh -- elementwise, normalisation, conv, gamma, RoPE and argmax kernels.
+//
+// Per-element arithmetic follows src/elementwise.zig operation for operation
+// (silu = x/(1+exp(-x)), rmsnorm = x*scale*w, conv = ((p0+p1)+p2)+p3, ...).
+// exp / log1p / pow / sin / cos are evaluated in double and rounded once, so
+// they agree with the host C library's f32 functions except in rare
+// double-rounding cases.  Row reductions (sum of squares, softmax sum) use a
+// fixed tree, not the CPU's serial order: those outputs differ from the CPU
+// by a few ulp, as the reference's own device kernels do.
+#pragma once
+#include "common.cuh"
+
+namespace q35 {
+
+#define Q35_GRID_STRIDE(i, n) \
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (long long)gridDim.x * blockDim.x)
+
+inline unsigned ew_grid(long long n, int threads = 256) {
+    long long g = (n + threads - 1) / threads;
+    if (g > 148 * 16) g = 148 * 16;
+    return (unsigned)(g < 1 ? 1 : g);
+}
+
+__global__ void k_scale_vec(float *x, float s, long long n) {
+    Q35_GRID_STRIDE(i, n) x[i] = __fmul_rn(x[i], s);
+}
+__global__ void k_scale_vec_strided(float *x, int offset, float s, int n, int tokens, int stride) {
+    Q35_GRID_STRIDE(i, (long long)n * tokens) {
+        const long long t = i / n, j = i - t * n;
+        float *p = x + offset + t * stride + j;
+        *p = __fmul_rn(*p, s);
+    }
+}
+__global__ void k_add_resid(float *d, const float *s, long long n) {
+    Q35_GRID_STRIDE(i, n) d[i] = __fadd_rn(d[i], s[i]);
+}
+__global__ void k_copy(float *d, const float *s, long long n) {
+    Q35_GRID_STRIDE(i, n) d[i] = s[i];
+}
+__global__ void k_zero(float *d, long long n) {
+    Q35_GRID_STRIDE(i, n) d[i] = 0.0f;
+}
+__global__ void k_set_int1(int *d, int v) { *d = v; }
+__global__ void k_deinterleave_qg(float *q, float *g, const float *src, int heads, int hd, int tokens) {
+    const long long per = (long long)heads * hd;
+    Q35_GRID_STRIDE(i, per * tokens) {
+        const long long t = i / per, r = i - t * per, h = r / hd, j = r - h * hd;
+        const float *s = src + t * 2 * per + h * 2 * hd;
+        q[i] = s[j];
+        g[i] = s[hd + j];
+    }
+}
+__global__ void k_silu(float *x, long long n) {
+    Q35_GRID_STRIDE(i, n) x[i] = silu_f(x[i]);
+}
+__global__ void k_mul_silu(float *o, const float *g, long long n) {
+    Q35_GRID_STRIDE(i, n) o[i] = __fmul_rn(o[i], silu_f(g[i]));
+}
+__global__ void k_mul_sigmoid(float *o, const float *g, long long n) {
+    Q35_GRID_STRIDE(i, n) o[i] = __fmul_rn(o[i], sigmoid_f(g[i]));
+}
+__global__ void k_swiglu(float *g, const float *u, long long n) {
+    Q35_GRID_STRIDE(i, n) g[i] = __fmul_rn(silu_f(g[i]), u[i]);
+}
+
+// ---- row norms: one block per row ----------------------------------------
+// rmsnorm: scale = 1/sqrt(ss/n + eps); out = x*scale*w  (elementwise.zig:43-57)
+template <int NT>
+__global__ void __launch_bounds__(NT) k_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
+    __shared__ float red[NT / 32];
+    const float *xr = x + (long long)blockIdx.x * n;
+    float *orow = out + (long long)blockIdx.x * n;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += NT) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    ss = block_sum<NT / 32>(ss, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (int i = threadIdx.x; i < n; i += NT) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
+// l2norm: inv = 1/sqrt(ss + eps); x *= inv  (elementwise.zig:104-110)
+// Row r of token t lives at x + offset + t*row_stride + r*n.
+template <int NT>
+__global__ void __launch_bounds__(NT) k_l2norm(float *x, int offset, int rows, int n, float eps, int row_stride,
+                                               float post_scale, int apply_scale) {
+    __shared__ float red[NT / 32];
+    const int r = blockIdx.x % rows, t = blockIdx.x / rows;
+    float *xr = x + offset + (long long)t * row_stride + (long long)r * n;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += NT) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    ss = block_sum<NT / 32>(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
+    for (int i = threadIdx.x; i < n; i += NT) {
+        float v = __fmul_rn(xr[i], inv);
+        if (apply_scale) v = __fmul_rn(v, post_scale);
+        xr[i] = v;
+    }
+}
+
+// softmax over one vector (elementwise.zig:93-102)
+__global__ void __launch_bounds__(1024) k_softmax(float *x, int n) {
+    __shared__ float red[32];
+    float m = -3.40282347e38f;
+    for (int i = threadIdx.x; i < n; i += 1024) m = fmaxf(m, x[i]);
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = red[0];
+    for (int i = 1; i < 32; i++) m = fmaxf(m, red[i]);
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const float e = exp_f(__fsub_rn(x[i], m));
+        x[i] = e;
+        s = __fadd_rn(s, e);
+    }
+    s = block_sum<32>(s, red);
+    for (int i = threadIdx.x; i < n; i += 1024) x[i] = __fdiv_rn(x[i], s);
+}
+
+// ---- causal conv k=4 + silu (elementwise.zig:322-342) --------------------
+// One thread per channel walks `tokens` rows in order (the history is the
+// cross-token dependency), writing the conv output; silu follows in place.
+__global__ void k_conv_rows(float *conv, float *y, const float *w, int n, int tokens, int y_stride) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float h0 = conv[i * 3], h1 = conv[i * 3 + 1], h2 = conv[i * 3 + 2];
+    const float w0 = w[i * 4], w1 = w[i * 4 + 1], w2 = w[i * 4 + 2], w3 = w[i * 4 + 3];
+    for (int t = 0; t < tokens; t++) {
+        float *yp = y + (long long)t * y_stride + i;
+        const float cur = *yp;
+        const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(h0, w0), __fmul_rn(h1, w1)), __fmul_rn(h2, w2)),
+                                  __fmul_rn(cur, w3));
+        *yp = silu_f(s);
+        h0 = h1;
+        h1 = h2;
+        h2 = cur;
+    }
+    conv[i * 3] = h0;
+    conv[i * 3 + 1] = h1;
+    conv[i * 3 + 2] = h2;
+}
+
+// ---- beta = sigmoid(b) in place; gamma = exp(ssm_a*softplus(a+dt)) -------
+// (elementwise.zig:378-384)
+__global__ void k_gdn_gamma(const float *a, float *b, const float *ssm_a, const float *dt, float *gamma, int nv,
+                            int tokens, int a_stride, int b_stride, int g_stride) {
+    Q35_GRID_STRIDE(i, (long long)nv * tokens) {
+        const int t = (int)(i / nv), h = (int)(i - (long long)t * nv);
+        float *bp = b + (long long)t * b_stride + h;
+        *bp = sigmoid_f(*bp);
+        const float g = __fmul_rn(ssm_a[h], softplus_f(__fadd_rn(a[(long long)t * a_stride + h], dt[h])));
+        gamma[(long long)t * g_stride + h] = exp_f(g);
+    }
+}
+
+// ---- RoPE on dims 0..63 of each head, pairs (j, j+32) --------------------
+// theta = (f32)pos * base^(-(2j)/64) (elementwise.zig:306-318)
+Q35_DEV void rope_cs(int pos, float base, int j, float &c, float &s) {
+    const float ex = __fdiv_rn(-(float)(2 * j), 64.0f);
+    const float p = (float)pow((double)base, (double)ex);
+    const float th = __fmul_rn((float)pos, p);
+    c = (float)cos((double)th);
+    s = (float)sin((double)th);
+}
+Q35_DEV void rope_apply(float *hp, int j, float c, float s) {
+    const float a = hp[j], b = hp[j + 32];
+    hp[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    hp[j + 32] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+}
+// rows x heads heads; row r at pos0 + r (pos0 from `dyn` when non-null)
+__global__ void k_rope64(float *x, int rows, int heads, int hd, int pos0, float base, const int *dyn) {
+    const int j = threadIdx.x & 31;
+    const long long rh = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (rh >= (long long)rows * heads) return;
+    int p0 = pos0;
+    float bs = base;
+    if (dyn) {
+        p0 = dyn[0];
+        bs = __int_as_float(dyn[1]);
+    }
+    const int r = (int)(rh / heads);
+    float c, s;
+    rope_cs(p0 + r, bs, j, c, s);
+    rope_apply(x + rh * hd, j, c, s);
+}
+__global__ void k_rope_setenv(int *d, int pos, float base) {
+    d[0] = pos;
+    d[1] = __float_as_int(base);
+}
+
+// ---- argmax: first index of the strict maximum (elementwise.zig:395-405) -
+// one block per row of `n` values
+__global__ void __launch_bounds__(1024) k_argmax(const float *x, long long row_stride, int n, int *out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float *xr = x + (long long)blockIdx.x * row_stride;
+    float bv = -INFINITY;
+    int bi = n;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const float v = xr[i];
+        if (v > bv) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 32; w++)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        out[blockIdx.x] = bi >= n ? 0 : bi;
+    }
+}
+
+// f32 weights x f32 activation: out[t*rows + r] = W[r] . x[t] (warp per row)
+__global__ void k_matvec_f32(const float *w, const float *x, float *out, int rows, int cols) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.y;
+    if (r >= rows) return;
+    const float *wr = w + (long long)r * cols, *xr = x + (long long)t * cols;
+    float s = 0.0f;
+    for (int c = lane; c < cols; c += 32) s = __fadd_rn(s, __fmul_rn(wr[c], xr[c]));
+    s = warp_sum(s);
+    if (lane == 0) out[(long long)t * rows + r] = s;
+}
+
+}  // namespace q35

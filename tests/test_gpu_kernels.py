@@ -1,0 +1,388 @@
+"""Kernel parity on the GPU, through the C ABI (include/q35.h), against the
+CPU oracle on the same seeded inputs.
+
+Bars: integer / byte work (activation quantizers, weight encoders,
+dequantizers) and the block-ordered GEMV fold and the GDN recurrence are
+bit-exact; reductions whose order the device changes (norm sums, softmax)
+are within 1e-5 relative.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle_lib import (TT, GEOM, ROOT, act_row_bytes, bp, dequant, fp, load_oracle, matvec_q, quantize_act,
+                        quantize_weight, row_bytes)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def L():
+    from qwen35_b200 import lib
+    return lib.load()
+
+
+@pytest.fixture(scope="module")
+def O():
+    return load_oracle()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+S = None  # legacy default stream
+
+
+def ok(rc):
+    assert rc == 0, f"cuda error {rc}"
+
+
+def assert_no_kernel_error(L):
+    code = ctypes.c_int(-1)
+    ok(L.q35b_get_error(ctypes.byref(code)))
+    assert code.value == 0
+
+
+TYPES = ["Q8_0", "IQ4_NL", "Q4_K", "Q5_K", "Q6_K"]
+
+
+def test_quantize_q8_0_bit_exact(L, O):
+    rng = np.random.default_rng(0)
+    for scale in (1e-6, 1e-3, 1.0, 300.0):
+        x = (rng.standard_normal(32 * 257) * scale).astype(np.float32)
+        x[:32] = 0.0
+        x[32:64] = 7.0
+        ref = quantize_act(O, TT["Q8_0"], x)[0]
+        xd = dev(x)
+        out = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+        ok(L.q35_launch_quantize_q8_0(xd.data_ptr(), out.data_ptr(), x.size // 32, S))
+        assert np.array_equal(host(out), ref)
+
+
+def test_quantize_q8_K_bit_exact(L, O):
+    rng = np.random.default_rng(1)
+    for scale in (1e-5, 1.0, 1e4):
+        x = (rng.standard_normal(256 * 37) * scale).astype(np.float32)
+        x[:256] = 0.0
+        ref = quantize_act(O, TT["Q4_K"], x)[0]
+        xd = dev(x)
+        out = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+        ok(L.q35_launch_quantize_q8_K(xd.data_ptr(), out.data_ptr(), x.size // 256, S))
+        assert np.array_equal(host(out), ref)
+
+
+@pytest.mark.parametrize("name", TYPES)
+def test_weight_encoder_bit_exact(L, O, name):
+    tt = TT[name]
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((64, 1024)) * 0.02).astype(np.float32)
+    w[0, :256] = 0.0
+    ref = quantize_weight(O, tt, w)
+    e, b = GEOM[tt]
+    out = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+    ok(L.q35b_quantize_weight(tt, dev(w).data_ptr(), out.data_ptr(), w.size // e, S))
+    assert np.array_equal(host(out).reshape(ref.shape), ref)
+
+
+@pytest.mark.parametrize("name", TYPES)
+def test_dequant_row_bit_exact(L, O, name):
+    tt = TT[name]
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((4, 1024)) * 0.05).astype(np.float32)
+    wq = quantize_weight(O, tt, w)
+    ref = dequant(O, tt, wq, 1024)
+    wd = dev(wq)
+    for r in range(4):
+        out = torch.zeros(1024, dtype=torch.float32, device="cuda")
+        ok(L.q35_launch_dequantize_row(tt, wd[r].data_ptr(), out.data_ptr(), 1024, S))
+        assert np.array_equal(host(out).view(np.uint32), ref[r].view(np.uint32))
+
+
+def _gemv_case(L, O, name, rows, cols, tokens, seed):
+    tt = TT[name]
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((tokens, cols)).astype(np.float32)
+    wq = quantize_weight(O, tt, w)
+    xq = quantize_act(O, tt, x)
+    ref = matvec_q(O, tt, wq, xq, rows, cols, tokens)
+    out = torch.full((tokens, rows), float("nan"), dtype=torch.float32, device="cuda")
+    ok(L.q35_launch_mul_mat_vec(dev(wq).data_ptr(), dev(xq).data_ptr(), out.data_ptr(), rows, cols, tokens, tt, S))
+    got = host(out)
+    return got, ref
+
+
+@pytest.mark.parametrize("name", TYPES)
+@pytest.mark.parametrize("tokens", [1, 3, 8, 13])
+def test_gemv_bit_exact(L, O, name, tokens):
+    """out[t*rows+r] == the reference scalar tier's strict block-order fold"""
+    for rows, cols in [(300, 1024), (64, 3584), (129, 2048)]:
+        got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + tokens)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
+    assert_no_kernel_error(L)
+
+
+def test_gemv_golden_rows(L, O):
+    """the reference's udtest rows (96 x 256) through the device GEMV"""
+    gold = os.path.join(ROOT, "tests", "golden", "udtest")
+    ax = np.fromfile(os.path.join(gold, "A_x.f32"), dtype=np.float32)
+    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144)]:
+        tt = TT[name]
+        rows = np.fromfile(os.path.join(gold, f"{name}.bin"), dtype=np.uint8).reshape(-1, rb)
+        exp = np.fromfile(os.path.join(gold, f"{name}_expected.f32"), dtype=np.float32)
+        xq = quantize_act(O, tt, ax)
+        ref = matvec_q(O, tt, rows, xq, 96, 256, 1)[0]
+        out = torch.zeros(96, dtype=torch.float32, device="cuda")
+        ok(L.q35_launch_mul_mat_vec(dev(rows).data_ptr(), dev(xq).data_ptr(), out.data_ptr(), 96, 256, 1, tt, S))
+        got = host(out)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), name
+        # and close to the f32 known answers (activation quantization error only)
+        rel = np.abs(got - exp) / np.maximum(np.abs(exp), 1)
+        assert rel.max() < 5e-2, (name, rel.max())
+
+
+def test_gemv_unaligned_weight_base(L, O):
+    """a matrix starting 2 bytes past a 16-byte boundary (GGUF blocks are only
+    2-byte aligned) is streamed correctly, head/tail bytes included"""
+    tt = TT["Q6_K"]
+    rng = np.random.default_rng(9)
+    rows, cols = 37, 768
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    wq = quantize_weight(O, tt, w)
+    xq = quantize_act(O, tt, rng.standard_normal(cols).astype(np.float32))
+    ref = matvec_q(O, tt, wq, xq, rows, cols, 1)[0]
+    buf = torch.zeros(wq.size + 64, dtype=torch.uint8, device="cuda")
+    buf[2:2 + wq.size] = dev(wq.reshape(-1))
+    out = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    ok(L.q35_launch_mul_mat_vec(buf.data_ptr() + 2, dev(xq).data_ptr(), out.data_ptr(), rows, cols, 1, tt, S))
+    assert np.array_equal(host(out).view(np.uint32), ref.view(np.uint32))
+
+
+def test_gemv_multi_and_residual(L, O):
+    """one launch over 3 matrices; mode 1 adds into the output (x += W y),
+    bit-exact with the separate matvec then addResid"""
+    rng = np.random.default_rng(4)
+    cols, tokens = 1024, 2
+    shapes = [(TT["IQ4_NL"], 512), (TT["Q8_0"], 16), (TT["Q8_0"], 48)]
+    x = rng.standard_normal((tokens, cols)).astype(np.float32)
+    xq = quantize_act(O, TT["Q8_0"], x)
+    ws, refs, outs = [], [], []
+    base = rng.standard_normal((tokens, 48)).astype(np.float32)
+    for i, (tt, rows) in enumerate(shapes):
+        wq = quantize_weight(O, tt, (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32))
+        ws.append(dev(wq))
+        r = matvec_q(O, tt, wq, xq, rows, cols, tokens)
+        if i == 2:
+            r = (base + r).astype(np.float32)
+            outs.append(dev(base))
+        else:
+            outs.append(torch.zeros((tokens, rows), dtype=torch.float32, device="cuda"))
+        refs.append(r)
+    n = 3
+    W = (ctypes.c_void_p * n)(*[w.data_ptr() for w in ws])
+    T = (ctypes.c_int * n)(*[s[0] for s in shapes])
+    R = (ctypes.c_longlong * n)(*[s[1] for s in shapes])
+    Op = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+    LD = (ctypes.c_longlong * n)(*[s[1] for s in shapes])
+    M = (ctypes.c_int * n)(0, 0, 1)
+    ok(L.q35b_mul_mat_vec_multi(n, W, T, R, Op, LD, M, dev(xq).data_ptr(), cols, tokens, S))
+    for o, r in zip(outs, refs):
+        assert np.array_equal(host(o).view(np.uint32), r.view(np.uint32))
+
+
+def test_gemv_rejects_mixed_families(L):
+    n = 2
+    W = (ctypes.c_void_p * n)(16, 16)
+    T = (ctypes.c_int * n)(TT["Q8_0"], TT["Q4_K"])
+    R = (ctypes.c_longlong * n)(4, 4)
+    Op = (ctypes.c_void_p * n)(16, 16)
+    LD = (ctypes.c_longlong * n)(4, 4)
+    assert L.q35b_mul_mat_vec_multi(n, W, T, R, Op, LD, None, 16, 256, 1, S) == 1
+
+
+def test_gdn_step_rows_bit_exact(L, O):
+    """q35_launch_gdn_step_rows == CPU gdnFused per head (h % nk k-head map)"""
+    rng = np.random.default_rng(5)
+    heads, nk, kd = 6, 3, 128
+    state = (rng.standard_normal((heads, kd, kd)) * 0.1).astype(np.float32)
+    k = rng.standard_normal(nk * kd).astype(np.float32)
+    q = rng.standard_normal(nk * kd).astype(np.float32)
+    v = rng.standard_normal(heads * kd).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.0, heads).astype(np.float32)
+    beta = rng.uniform(0.0, 1.0, heads).astype(np.float32)
+    rs, rkm, rdl, rout = state.copy(), np.zeros(heads * kd, np.float32), np.zeros(heads * kd, np.float32), \
+        np.zeros(heads * kd, np.float32)
+    O.q35o_gdn_step_rows(fp(rs), fp(k), fp(v), fp(q), fp(rkm), fp(rdl), fp(rout), fp(gamma), fp(beta), heads, nk,
+                         kd, kd)
+    ds, dkm, ddl, dout = dev(state), *[torch.zeros(heads * kd, device="cuda") for _ in range(3)]
+    ok(L.q35_launch_gdn_step_rows(ds.data_ptr(), kd * kd, dev(k).data_ptr(), kd, dev(v).data_ptr(), kd,
+                                  dev(q).data_ptr(), kd, dkm.data_ptr(), ddl.data_ptr(), dout.data_ptr(),
+                                  dev(gamma).data_ptr(), dev(beta).data_ptr(), heads, nk, kd, kd, S))
+    for a, b in [(ds, rs), (dkm, rkm), (ddl, rdl), (dout, rout)]:
+        assert np.array_equal(host(a).reshape(-1).view(np.uint32), b.reshape(-1).view(np.uint32))
+
+
+def test_gdn_chunk_equals_rows(L, O):
+    """gdnStepRowsChunk == rows x gdnStepRows, bit-identical
+    (src/chunk_slot_tests.zig:247), incl. recurrence dependence"""
+    rng = np.random.default_rng(6)
+    heads, nk, kd, rows = 4, 2, 128, 5
+    conv_dim = 2 * nk * kd + heads * kd
+    state = (rng.standard_normal((heads, kd, kd)) * 0.1).astype(np.float32)
+    qkv = rng.standard_normal((rows, conv_dim)).astype(np.float32)
+    gam = rng.uniform(0.5, 1.0, (rows, heads)).astype(np.float32)
+    bet = rng.uniform(0.0, 1.0, (rows, heads)).astype(np.float32)
+    rs = state.copy()
+    rout = np.zeros((rows, heads * kd), np.float32)
+    km = np.zeros(heads * kd, np.float32)
+    dl = np.zeros(heads * kd, np.float32)
+    for t in range(rows):
+        row = qkv[t]
+        O.q35o_gdn_step_rows(fp(rs), fp(row[nk * kd:]), fp(row[2 * nk * kd:]), fp(row), fp(km), fp(dl),
+                             fp(rout[t]), fp(gam[t]), fp(bet[t]), heads, nk, kd, kd)
+    ds, dq = dev(state), dev(qkv)
+    dkm = torch.zeros((rows, heads * kd), device="cuda")
+    ddl = torch.zeros_like(dkm)
+    dout = torch.zeros_like(dkm)
+    base = dq.data_ptr()
+    ok(L.q35_launch_gdn_step_rows_chunk(ds.data_ptr(), kd * kd, base + 4 * nk * kd, conv_dim,
+                                        base + 4 * 2 * nk * kd, conv_dim, base, conv_dim, dkm.data_ptr(),
+                                        heads * kd, ddl.data_ptr(), heads * kd, dout.data_ptr(), heads * kd,
+                                        dev(gam).data_ptr(), heads, dev(bet).data_ptr(), heads, heads, nk, kd, kd,
+                                        rows, S))
+    assert np.array_equal(host(ds).view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(host(dout).view(np.uint32), rout.view(np.uint32))
+
+
+def test_conv_gamma_exact_paths(L, O):
+    rng = np.random.default_rng(7)
+    n, tokens = 768, 3
+    conv = rng.standard_normal(n * 3).astype(np.float32)
+    y = rng.standard_normal((tokens, n)).astype(np.float32)
+    w = rng.standard_normal(n * 4).astype(np.float32)
+    rc, ry = conv.copy(), y.copy()
+    for t in range(tokens):
+        O.q35o_conv_step(fp(rc), fp(ry[t]), fp(w), n)
+    dc, dy = dev(conv), dev(y)
+    ok(L.q35_launch_conv_step_rows(dc.data_ptr(), dy.data_ptr(), dev(w).data_ptr(), n, tokens, n, S))
+    assert np.array_equal(host(dc), rc)
+    assert np.abs(host(dy) - ry).max() <= 1e-6 * np.abs(ry).max()
+    nv = 16
+    a = rng.standard_normal(nv).astype(np.float32) * 3
+    b = rng.standard_normal(nv).astype(np.float32)
+    sa = -np.exp(rng.uniform(-1, 1, nv)).astype(np.float32)
+    dt = rng.standard_normal(nv).astype(np.float32)
+    rb, rg = b.copy(), np.zeros(nv, np.float32)
+    O.q35o_gdn_gamma(fp(a), fp(rb), fp(sa), fp(dt), fp(rg), nv)
+    db, dg = dev(b), torch.zeros(nv, device="cuda")
+    ok(L.q35_launch_gdn_gamma(dev(a).data_ptr(), db.data_ptr(), dev(sa).data_ptr(), dev(dt).data_ptr(),
+                              dg.data_ptr(), nv, S))
+    assert np.abs(host(db) - rb).max() <= 1e-6
+    assert np.abs(host(dg) - rg).max() <= 1e-6
+
+
+def test_norms_and_activations(L, O):
+    rng = np.random.default_rng(8)
+    rows, n = 5, 1024
+    x = rng.standard_normal((rows, n)).astype(np.float32)
+    w = rng.standard_normal(n).astype(np.float32)
+    ref = np.zeros_like(x)
+    O.q35o_rmsnorm_rows(fp(ref), fp(x), fp(w), rows, n, 1e-6)
+    out = torch.zeros_like(dev(x))
+    ok(L.q35_launch_rmsnorm(out.data_ptr(), dev(x).data_ptr(), dev(w).data_ptr(), rows, n, 1e-6, S))
+    assert np.abs(host(out) - ref).max() <= 1e-5 * np.abs(ref).max()
+    nk, kd = 4, 128
+    v = rng.standard_normal(3 * nk * kd).astype(np.float32)
+    rv = v.copy()
+    O.q35o_l2norm_qk_scale(fp(rv), nk, kd, nk * kd, np.float32(1 / np.sqrt(128)))
+    dv = dev(v)
+    ok(L.q35_launch_l2norm_qk_scale(dv.data_ptr(), nk, kd, nk * kd, 1e-6, float(np.float32(1 / np.sqrt(128))), S))
+    assert np.abs(host(dv) - rv).max() <= 1e-6
+    g = rng.standard_normal(4096).astype(np.float32) * 4
+    u = rng.standard_normal(4096).astype(np.float32)
+    rg = g.copy()
+    O.q35o_swiglu(fp(rg), fp(u), 4096)
+    dg = dev(g)
+    ok(L.q35_launch_swiglu(dg.data_ptr(), dev(u).data_ptr(), 4096, S))
+    assert np.abs(host(dg) - rg).max() <= 1e-6 * np.abs(rg).max()
+    sm = rng.standard_normal(3000).astype(np.float32) * 5
+    rsm = sm.copy()
+    O.q35o_softmax(fp(rsm), 3000)
+    dsm = dev(sm)
+    ok(L.q35_launch_softmax(dsm.data_ptr(), 3000, S))
+    assert np.abs(host(dsm) - rsm).max() <= 1e-6
+
+
+def test_rope_and_argmax(L, O):
+    rng = np.random.default_rng(10)
+    heads, hd = 8, 256
+    for pos in (0, 1, 37, 4095):
+        x = rng.standard_normal(heads * hd).astype(np.float32)
+        rx = x.copy()
+        O.q35o_rope64_rows(fp(rx), 1, heads, hd, pos, 1e7)
+        dx = dev(x)
+        ok(L.q35_launch_rope64(dx.data_ptr(), heads, hd, pos, 1e7, S))
+        assert np.abs(host(dx) - rx).max() <= 1e-5, pos
+    x = rng.standard_normal(248320).astype(np.float32)
+    x[1000] = x[200000] = 9.0  # tie: first index wins
+    o = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ok(L.q35_launch_argmax(dev(x).data_ptr(), x.size, o.data_ptr(), S))
+    assert int(host(o)[0]) == 1000 == O.q35o_argmax(fp(x), x.size)
+
+
+@pytest.mark.parametrize("slot", [0, 5, 300, 1100])
+def test_attn_decode(L, O, slot):
+    rng = np.random.default_rng(slot)
+    heads, kvh, hd = 8, 2, 256
+    kv_dim = kvh * hd
+    q = rng.standard_normal(heads * hd).astype(np.float32)
+    g = rng.standard_normal(heads * hd).astype(np.float32)
+    K = rng.standard_normal((slot + 1, kv_dim)).astype(np.float32)
+    V = rng.standard_normal((slot + 1, kv_dim)).astype(np.float32)
+    att = np.zeros(slot + 1, np.float32)
+    ref = np.zeros(heads * hd, np.float32)
+    scale = np.float32(1 / 16)
+    O.q35o_attn_decode(fp(q), fp(g), fp(K), fp(V), fp(att), fp(ref), slot, heads, heads // kvh, hd, kv_dim, scale)
+    out = torch.zeros(heads * hd, device="cuda")
+    datt = torch.zeros(slot + 1, device="cuda")
+    ok(L.q35_launch_attn_decode(dev(q).data_ptr(), dev(g).data_ptr(), dev(K).data_ptr(), dev(V).data_ptr(),
+                                datt.data_ptr(), out.data_ptr(), slot, heads, heads // kvh, hd, kv_dim,
+                                float(scale), S))
+    assert np.abs(host(out) - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max())
+    # device-slot twin
+    ds = torch.tensor([slot], dtype=torch.int32, device="cuda")
+    out2 = torch.zeros_like(out)
+    ok(L.q35_launch_attn_decode_dyn(dev(q).data_ptr(), dev(g).data_ptr(), dev(K).data_ptr(), dev(V).data_ptr(),
+                                    datt.data_ptr(), out2.data_ptr(), ds.data_ptr(), heads, heads // kvh, hd,
+                                    kv_dim, float(scale), S))
+    assert torch.equal(out, out2)
+
+
+def test_attn_chunk_equals_decode_rows(L):
+    """attnChunk == k x attnDecode (src/chunk_slot_tests.zig:40)"""
+    rng = np.random.default_rng(11)
+    heads, kvh, hd, slot0, rows = 4, 1, 256, 20, 6
+    kv_dim = kvh * hd
+    q = dev(rng.standard_normal((rows, heads * hd)).astype(np.float32))
+    g = dev(rng.standard_normal((rows, heads * hd)).astype(np.float32))
+    K = dev(rng.standard_normal((slot0 + rows, kv_dim)).astype(np.float32))
+    V = dev(rng.standard_normal((slot0 + rows, kv_dim)).astype(np.float32))
+    out = torch.zeros((rows, heads * hd), device="cuda")
+    ok(L.q35_launch_attn_chunk(q.data_ptr(), g.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), slot0, rows,
+                               heads, heads // kvh, hd, kv_dim, 1 / 16, S))
+    for r in range(rows):
+        o = torch.zeros(heads * hd, device="cuda")
+        att = torch.zeros(slot0 + rows, device="cuda")
+        ok(L.q35_launch_attn_decode(q[r].data_ptr(), g[r].data_ptr(), K.data_ptr(), V.data_ptr(), att.data_ptr(),
+                                    o.data_ptr(), slot0 + r, heads, heads // kvh, hd, kv_dim, 1 / 16, S))
+        assert torch.equal(o, out[r])
+    assert_no_kernel_error(L)
