@@ -162,9 +162,11 @@ def time_decode(run, steps, warmup, dist):
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("q35_timed")
     e0.record(run.stream)
     run.dev_steps(steps)
     e1.record(run.stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()

@@ -77,6 +77,10 @@ int q35_launch_mul_mat_vec_q8_0(const void *d_w, const void *d_xq, float *d_out,
                                 int tokens, void *stream);
 int q35_launch_mul_mat_vec_f32(const float *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens,
                                void *stream);
+/* f16 / bf16 weights x f32 activation (reference mmvq.cu:1011): per-32 block
+ * serial sums folded in block order, as rowDotF16 / rowDotBF16. */
+int q35_launch_mul_mat_vec_w16(const void *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens,
+                               int ttype, void *stream);
 /* prefill tile path (mmq.cu:2232-2245 in the reference): returns -1
  * ("decline, use q35_launch_mul_mat_vec") for every shape in this build. */
 int q35_launch_mul_mat_vec_tile(const void *d_w, const void *d_xq, float *d_out, int rows, int cols, int tokens,
@@ -92,6 +96,7 @@ int q35_launch_deinterleave_qg(float *d_q, float *d_gate, const float *d_src, in
 int q35_launch_deinterleave_qg_strided(float *d_q, float *d_gate, const float *d_src, int heads, int hd,
                                        int tokens, void *stream);
 int q35_launch_zero_buf(float *d_buf, int n, void *stream);
+void *q35_func_copy_range(void); /* reference elementwise.cu:157 */
 int q35_launch_set_int1(int *d, int v, void *stream);
 
 /* norms (api.h:168-176) */
@@ -113,6 +118,8 @@ int q35_launch_argmax(const float *d_x, int n, int *d_out, void *stream);
 
 /* rotary embedding (api.h:217-239) */
 int q35_launch_rope64(float *d_x, int heads, int hd, int pos, float base, void *stream);
+int q35_launch_rope64_rows(float *d_x, int rows, int heads, int hd, int pos0, float base, void *stream);
+void *q35_func_rope64(void); /* reference rope.cu:243-277 */
 int q35_launch_rope64_dpos(float *d_x, int heads, int hd, const void *d_dyn, void *stream);
 void *q35_func_rope64_dpos(void);
 int q35_launch_rope64_rows_dpos(float *d_x, int rows, int heads, int hd, const void *d_dyn, void *stream);
@@ -152,6 +159,7 @@ int q35_launch_attn_chunk(const float *d_q, const float *d_gate, const float *d_
                           float *d_gout, int slot0, int rows, int heads, int gqa, int hd, int kv_dim, float scale,
                           void *stream);
 int q35_attn_chunk_max_rows(int slot0);
+void *q35_func_attn_decode(void); /* reference attn.cu:393 */
 void *q35_func_attn_decode_dyn(void);
 void *q35_func_attn_decode_coal(void);
 void *q35_func_attn_score_split(void);
@@ -172,6 +180,17 @@ int q35_launch_attn_decode_split_dyn(const float *d_q, const float *d_gate, cons
 int q35_launch_attn_decode_split2(const float *d_q, const float *d_gate, const float *d_kcache,
                                   const float *d_vcache, float *d_att, float *d_gout, float *d_part, int slot,
                                   int heads, int gqa, int hd, int kv_dim, float scale, int split, void *stream);
+
+/* device sampler (reference sample.cu:559-664, control block of 16 int32).
+ * Sampling is outside this backend's hot path: q35_launch_sample implements
+ * the greedy branch (ctl[6] = first index of the max logit).  A non-zero
+ * temperature in ctl[1] still writes the argmax and records error 201 for
+ * q35b_get_error.  _init allocates the two regions, as in the reference. */
+int q35_sample_scratch_ints(void);
+int q35_sample_ctl_ints(void);
+int q35_launch_sample_init(void **d_ctl, void **d_scratch);
+void q35_launch_sample_deinit(void **d_ctl, void **d_scratch);
+int q35_launch_sample(const float *d_logits, int n, int *d_ctl, void *d_scratch, void *stream);
 
 /* codebook upload (api.h:433-442).  The IQ4_NL codebook is compiled into
  * the kernels, so init is a no-op that reports success. */

@@ -100,6 +100,14 @@ int q35_launch_mul_mat_vec_f32(const float *d_w, const float *d_x, float *d_out,
     k_matvec_f32<<<dim3((unsigned)((rows + 7) / 8), (unsigned)tokens), 256, 0, S(stream)>>>(d_w, d_x, d_out, rows, cols);
     return (int)cudaGetLastError();
 }
+int q35_launch_mul_mat_vec_w16(const void *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens, int ttype,
+                               void *stream) {
+    if (rows <= 0 || cols <= 0 || tokens <= 0) return 0;
+    if ((ttype != TT_F16 && ttype != TT_BF16) || cols % 32) return (int)cudaErrorInvalidValue;
+    k_matvec_w16<<<dim3((unsigned)((rows + 7) / 8), (unsigned)tokens), 256, 0, S(stream)>>>(
+        (const uint16_t *)d_w, d_x, d_out, rows, cols, ttype == TT_BF16);
+    return (int)cudaGetLastError();
+}
 int q35_launch_mul_mat_vec_tile(const void *, const void *, float *, int, int, int, int, void *) { return -1; }
 
 // ---- elementwise (api.h:135-154) ----
@@ -133,6 +141,7 @@ int q35_launch_deinterleave_qg_strided(float *d_q, float *d_gate, const float *d
 int q35_launch_deinterleave_qg(float *d_q, float *d_gate, const float *d_src, int heads, int hd, void *stream) {
     return q35_launch_deinterleave_qg_strided(d_q, d_gate, d_src, heads, hd, 1, stream);
 }
+void *q35_func_copy_range(void) { return (void *)k_copy; }
 int q35_launch_zero_buf(float *d_buf, int n, void *stream) {
     if (n <= 0) return 0;
     k_zero<<<ew_grid(n), 256, 0, S(stream)>>>(d_buf, n);
@@ -224,6 +233,13 @@ int q35_launch_rope64_rows_dpos(float *d_x, int rows, int heads, int hd, const v
 int q35_launch_rope64_dpos(float *d_x, int heads, int hd, const void *d_dyn, void *stream) {
     return q35_launch_rope64_rows_dpos(d_x, 1, heads, hd, d_dyn, stream);
 }
+int q35_launch_rope64_rows(float *d_x, int rows, int heads, int hd, int pos0, float base, void *stream) {
+    if (heads <= 0 || rows <= 0) return 0;
+    if (hd < 64) return (int)cudaErrorInvalidValue;
+    k_rope64<<<(rows * heads + 7) / 8, 256, 0, S(stream)>>>(d_x, rows, heads, hd, pos0, base, nullptr);
+    return (int)cudaGetLastError();
+}
+void *q35_func_rope64(void) { return (void *)k_rope64; }
 void *q35_func_rope64_dpos(void) { return (void *)k_rope64; }
 void *q35_func_rope64_rows_dpos(void) { return (void *)k_rope64; }
 int q35_launch_rope64_setenv(int *d_dyn, int pos, float base, void *stream) {
@@ -383,6 +399,7 @@ int q35_launch_attn_chunk(const float *d_q, const float *d_gate, const float *d_
     return 0;
 }
 int q35_attn_chunk_max_rows(int) { return 1 << 20; }
+void *q35_func_attn_decode(void) { return (void *)k_attn_split<4>; }
 void *q35_func_attn_decode_dyn(void) { return (void *)k_attn_split<4>; }
 void *q35_func_attn_decode_coal(void) { return (void *)k_attn_split<4>; }
 void *q35_func_attn_score_split(void) { return (void *)k_attn_split<4>; }
@@ -390,6 +407,37 @@ void *q35_func_attn_score_split_dyn(void) { return (void *)k_attn_split<4>; }
 void *q35_func_attn_pv_split_dyn(void) { return (void *)k_attn_merge; }
 void *q35_func_attn_softmax_dyn(void) { return (void *)k_attn_merge; }
 void *q35_func_attn_reduce(void) { return (void *)k_attn_merge; }
+
+// ---- device sampler (src/kernels/cuda/sample.cu:559-664): greedy only ----
+int q35_sample_scratch_ints(void) { return 16; }
+int q35_sample_ctl_ints(void) { return 16; }
+int q35_launch_sample_init(void **d_ctl, void **d_scratch) {
+    if (!d_ctl || !d_scratch) return (int)cudaErrorInvalidValue;
+    if (!*d_ctl) {
+        if (cudaMalloc(d_ctl, 16 * sizeof(int)) != cudaSuccess) {
+            *d_ctl = nullptr;
+            return (int)cudaGetLastError();
+        }
+        cudaMemset(*d_ctl, 0, 16 * sizeof(int));
+    }
+    if (!*d_scratch) {
+        if (cudaMalloc(d_scratch, 16 * sizeof(int)) != cudaSuccess) {
+            cudaFree(*d_ctl);
+            *d_ctl = nullptr;
+            return (int)cudaGetLastError();
+        }
+    }
+    return 0;
+}
+void q35_launch_sample_deinit(void **d_ctl, void **d_scratch) {
+    if (d_ctl && *d_ctl) { cudaFree(*d_ctl); *d_ctl = nullptr; }
+    if (d_scratch && *d_scratch) { cudaFree(*d_scratch); *d_scratch = nullptr; }
+}
+int q35_launch_sample(const float *d_logits, int n, int *d_ctl, void *d_scratch, void *stream) {
+    if (!d_logits || !d_ctl || !d_scratch || n <= 0) return (int)cudaErrorInvalidValue;
+    k_sample_greedy<<<1, 1024, 0, S(stream)>>>(d_logits, n, d_ctl);
+    return (int)cudaGetLastError();
+}
 
 // ---- codebooks (api.h:433-442): compiled into the kernels ----
 int q35_launch_init_tables(void *) { return 0; }

@@ -273,7 +273,7 @@ inline bool is_full_layer(const q35b_config &c, int li) {
 inline int eng_gemv(q35b_engine *e, int n, std::initializer_list<GemvSegDesc> segs, const uint8_t *xq, int cols,
                     cudaStream_t st) {
     e->launches += (n + GV_MAX_NT - 1) / GV_MAX_NT;
-    return gemv_launch(segs.begin(), (int)segs.size(), xq, cols, n, st);
+    return gemv_launch(segs.begin(), (int)segs.size(), xq, cols, n, st, e->xq_ld);
 }
 
 inline int family_of(const Lin &l) { return geom_of(l.tt).family; }

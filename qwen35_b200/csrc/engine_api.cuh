@@ -152,7 +152,8 @@ int q35b_engine_finalize(q35b_engine *e) {
     ALLOC(mh, 4 * B * c.n_ff);
     ALLOC(mh1, 4 * B * c.n_ff);
     ALLOC(logits, 4 * B * (long long)c.vocab);
-    const long long maxsplit = (e->max_seq + 255) / 256 + 1;
+    long long maxsplit = 1;
+    while (maxsplit < (e->max_seq + 255) / 256) maxsplit <<= 1;
     ALLOC(part_acc, 4 * B * c.n_heads * maxsplit * ATT_HD);
     ALLOC(part_ml, 4 * B * c.n_heads * maxsplit * 2);
     ALLOC(probe_buf, 4 * (long long)c.n_layers * B * h);
@@ -163,6 +164,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY((int)cudaMemset(e->conv_pool, 0, 4 * ngdn * S * e->conv_slot));
     Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 3 * B));
+    Q35_TRY(gemv_prepare());
     Q35_TRY((int)cudaDeviceSynchronize());
     e->finalized = true;
     return 0;

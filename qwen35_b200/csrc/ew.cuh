@@ -226,4 +226,61 @@ __global__ void k_matvec_f32(const float *w, const float *x, float *out, int row
     if (lane == 0) out[(long long)t * rows + r] = s;
 }
 
+// f16 / bf16 weights (2 B per element, no block metadata) x f32 activation:
+// per 32-element block a serial f32 sum, blocks folded in order
+// (src/quant_dequant.zig:1352-1384 rowDotF16 / rowDotBF16).  Warp per row,
+// lane per block, lane 0 folds the block sums in block order.
+__global__ void k_matvec_w16(const uint16_t *w, const float *x, float *out, int rows, int cols, int bf16) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.y;
+    if (r >= rows) return;
+    const uint16_t *wr = w + (long long)r * cols;
+    const float *xr = x + (long long)t * cols;
+    const int nb = cols / 32;
+    float sum = 0.0f;
+    for (int b0 = 0; b0 < nb; b0 += 32) {
+        const int b = b0 + lane;
+        float acc = 0.0f;
+        if (b < nb)
+            for (int k = 0; k < 32; k++) {
+                const uint16_t h = wr[b * 32 + k];
+                const float wv = bf16 ? __uint_as_float((uint32_t)h << 16) : __half2float(__ushort_as_half(h));
+                acc = __fadd_rn(acc, __fmul_rn(wv, xr[b * 32 + k]));
+            }
+        const int n = min(32, nb - b0);
+        for (int j = 0; j < n; j++) {
+            const float v = __shfl_sync(0xffffffffu, acc, j);
+            sum = __fadd_rn(sum, v);
+        }
+    }
+    if (lane == 0) out[(long long)t * rows + r] = sum;
+}
+
+// greedy branch of the reference's device sampler contract: ctl[6] <- argmax
+__global__ void __launch_bounds__(1024) k_sample_greedy(const float *x, int n, int *ctl) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float bv = -INFINITY;
+    int bi = n;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const float v = x[i];
+        if (v > bv) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 32; w++)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        ctl[6] = bi >= n ? 0 : bi;
+        // a non-zero temperature asks for a stochastic draw, which this build
+        // does not implement: record it rather than pretend
+        if (ctl[1] != 0) set_error(201);
+    }
+}
+
 }  // namespace q35

@@ -21,13 +21,19 @@
 #pragma once
 #include "common.cuh"
 
+#define Q35_TRY_RC(x)          \
+    do {                       \
+        int _r = (x);          \
+        if (_r) return _r;     \
+    } while (0)
+
 namespace q35 {
 
 constexpr int GV_WARPS = 8;                      // consumer warps
 constexpr int GV_THREADS = (GV_WARPS + 1) * 32;  // + one producer warp
 constexpr int GV_MAX_SEG = 4;
 constexpr int GV_MAX_NT = 16;                    // tokens per pass
-constexpr int GV_FOLD_LD = 33;                   // padded fold row (bank-conflict free)
+constexpr int GV_FOLD_LD = 36;                   // fold row: 16-byte aligned for vector reads
 
 enum { GV_STORE = 0, GV_ADD = 1 };
 
@@ -193,11 +199,12 @@ Q35_DEV void part_q6_k(const uint8_t *wb, const ActView &A, int ntok, int b, int
 }
 
 // One row: lanes split blocks (LPB lanes per block), terms folded in order.
-template <int NT>
+// The fold reads a chunk's BPC terms with 128-bit shared loads (all issued
+// before the first add) and adds them in block order.
+template <int NT, int LPB>
 Q35_DEV void gemv_row(int tt, const uint8_t *rowp, const ActView &A, int ntok, int nb, float *fold,
                       float *out_t0, long long out_ld, int mode, int lane) {
-    const int LPB = (tt == TT_Q8_0 || tt == TT_IQ4_NL) ? 1 : 4;
-    const int BPC = 32 / LPB;
+    constexpr int BPC = 32 / LPB;
     const int bsz = geom_of(tt).bytes;
     const int p = lane % LPB;
     float acc = 0.0f;
@@ -209,13 +216,18 @@ Q35_DEV void gemv_row(int tt, const uint8_t *rowp, const ActView &A, int ntok, i
 #pragma unroll
         for (int t = 0; t < NT; t++) is[t] = 0, ms[t] = 0;
         if (act) {
-            switch (tt) {
-            case TT_Q8_0: part_q8_0<NT>(wb, A, ntok, b, is); break;
-            case TT_IQ4_NL: part_iq4_nl<NT>(wb, A, ntok, b, is); break;
-            case TT_Q4_K: part_q45_k<NT, false>(wb, A, ntok, b, p, is, ms); break;
-            case TT_Q5_K: part_q45_k<NT, true>(wb, A, ntok, b, p, is, ms); break;
-            case TT_Q6_K: part_q6_k<NT>(wb, A, ntok, b, p, is); break;
-            default: break;
+            if (LPB == 1) {
+                if (tt == TT_Q8_0)
+                    part_q8_0<NT>(wb, A, ntok, b, is);
+                else
+                    part_iq4_nl<NT>(wb, A, ntok, b, is);
+            } else {
+                if (tt == TT_Q4_K)
+                    part_q45_k<NT, false>(wb, A, ntok, b, p, is, ms);
+                else if (tt == TT_Q5_K)
+                    part_q45_k<NT, true>(wb, A, ntok, b, p, is, ms);
+                else
+                    part_q6_k<NT>(wb, A, ntok, b, p, is);
             }
         }
         if (LPB > 1) {
@@ -252,9 +264,22 @@ Q35_DEV void gemv_row(int tt, const uint8_t *rowp, const ActView &A, int ntok, i
         }
         __syncwarp();
         if (lane < ntok) {
-            const int n = min(BPC, nb - cb);
             const float *f = fold + lane * GV_FOLD_LD;
-            for (int j = 0; j < n; j++) acc = __fadd_rn(acc, f[j]);
+            if (nb - cb >= BPC) {
+                float4 v[BPC / 4];
+#pragma unroll
+                for (int i = 0; i < BPC / 4; i++) v[i] = reinterpret_cast<const float4 *>(f)[i];
+#pragma unroll
+                for (int i = 0; i < BPC / 4; i++) {
+                    acc = __fadd_rn(acc, v[i].x);
+                    acc = __fadd_rn(acc, v[i].y);
+                    acc = __fadd_rn(acc, v[i].z);
+                    acc = __fadd_rn(acc, v[i].w);
+                }
+            } else {
+                const int n = nb - cb;
+                for (int j = 0; j < n; j++) acc = __fadd_rn(acc, f[j]);
+            }
         }
         __syncwarp();
     }
@@ -385,9 +410,15 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
         const uintptr_t start = reinterpret_cast<uintptr_t>(sg.w) + (uintptr_t)r0 * sg.row_bytes;
         const uint8_t *buf = stages + (size_t)s * stage_ld + (start & 15);
         const int nb = a.cols / geom_of(sg.ttype).elems;
-        for (int rr = warp; rr < nr; rr += GV_WARPS)
-            gemv_row<NT>(sg.ttype, buf + (size_t)rr * sg.row_bytes, A, a.ntok, nb, fold, sg.out + r0 + rr,
-                         sg.out_ld, sg.mode, lane);
+        const bool lpb1 = sg.ttype == TT_Q8_0 || sg.ttype == TT_IQ4_NL;
+        for (int rr = warp; rr < nr; rr += GV_WARPS) {
+            if (lpb1)
+                gemv_row<NT, 1>(sg.ttype, buf + (size_t)rr * sg.row_bytes, A, a.ntok, nb, fold, sg.out + r0 + rr,
+                                sg.out_ld, sg.mode, lane);
+            else
+                gemv_row<NT, 4>(sg.ttype, buf + (size_t)rr * sg.row_bytes, A, a.ntok, nb, fold, sg.out + r0 + rr,
+                                sg.out_ld, sg.mode, lane);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -414,25 +445,33 @@ inline size_t gemv_smem_bytes(int ntok, int act_stride, int stage_bytes, int nst
     return s;
 }
 
+// Set the dynamic shared-memory ceiling of every instantiation once, outside
+// any stream capture (attribute calls are not stream work, but doing them
+// up front keeps a captured step free of host-side configuration).
+inline int gemv_prepare() {
+    static int done = 0;
+    if (done) return 0;
+    const int lim = 227 * 1024;
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e != cudaSuccess) return (int)e;
+    done = 1;
+    return 0;
+}
+
 template <int NT>
 inline int gemv_launch_nt(GemvArgs &a, cudaStream_t st) {
-    static size_t configured = 0;
-    static int occ_cache_smem = -1, occ_cache = 1;
     const size_t smem = gemv_smem_bytes(a.ntok, a.act_stride, a.stage_bytes, a.nstage);
     if (smem > 227 * 1024) return (int)cudaErrorInvalidValue;
-    if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return (int)e;
-        configured = smem;
-    }
-    if (occ_cache_smem != (int)smem) {
-        int occ = 1;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemv<NT>, GV_THREADS, smem) != cudaSuccess || occ < 1)
-            occ = 1;
-        occ_cache = occ;
-        occ_cache_smem = (int)smem;
-    }
-    long long grid = (long long)gemv_sm_count() * occ_cache;
+    Q35_TRY_RC(gemv_prepare());
+    // resident CTAs per SM from shared memory (228 KB per SM, 1 KB reserved
+    // per CTA) and registers (<= 96 x 288 threads): at most 2
+    int occ = (int)((228 * 1024) / (smem + 1024));
+    occ = occ < 1 ? 1 : (occ > 2 ? 2 : occ);
+    long long grid = (long long)gemv_sm_count() * occ;
     if (grid > a.total_tiles) grid = a.total_tiles;
     if (grid < 1) grid = 1;
     k_gemv<NT><<<(unsigned)grid, GV_THREADS, smem, st>>>(a);
@@ -441,7 +480,8 @@ inline int gemv_launch_nt(GemvArgs &a, cudaStream_t st) {
 
 // Launch y = W x for up to GV_MAX_SEG matrices sharing one activation.
 // `xq` is the API-layout quantized activation (tokens rows of act_row_bytes).
-inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st) {
+inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                       long long xq_ld = 0) {
     if (nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || ntok <= 0) return (int)cudaErrorInvalidValue;
     const int fam = geom_of(segs[0].ttype).family;
     if (!fam) return (int)cudaErrorInvalidValue;
@@ -451,7 +491,9 @@ inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int co
         if ((reinterpret_cast<uintptr_t>(segs[i].w) & 1u) != 0) return (int)cudaErrorMisalignedAddress;
     }
     if (fam == 256 && (reinterpret_cast<uintptr_t>(xq) & 3u) != 0) return (int)cudaErrorMisalignedAddress;
-    const long long act_row_bytes = fam == 32 ? (long long)(cols / 32) * 34 : (long long)(cols / 256) * 292;
+    const long long act_row_bytes =
+        xq_ld > 0 ? xq_ld : (fam == 32 ? (long long)(cols / 32) * 34 : (long long)(cols / 256) * 292);
+    if (fam == 256 && (act_row_bytes & 3)) return (int)cudaErrorMisalignedAddress;
     const int nsm = gemv_sm_count();
     int max_rb = 0;
     long long total_rows = 0;
@@ -463,7 +505,10 @@ inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int co
     }
     int stage = 16384;
     if (max_rb + 16 > stage) stage = (max_rb + 16 + 15) & ~15;
-    const int group = (long long)GV_MAX_NT * gemv_act_stride(cols, fam) <= 96 * 1024 ? GV_MAX_NT : 8;
+    // tokens per pass: the largest group whose shared activation copy plus a
+    // 3-stage weight ring fits the CTA's shared memory
+    int group = GV_MAX_NT;
+    while (group > 1 && gemv_smem_bytes(group, gemv_act_stride(cols, fam), stage, 3) > 220 * 1024) group >>= 1;
     for (int t0 = 0; t0 < ntok; t0 += group) {
         const int nt = ntok - t0 < group ? ntok - t0 : group;
         GemvArgs a{};

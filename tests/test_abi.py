@@ -12,7 +12,8 @@ from qwen35_b200.build import LIB, build
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
-# every reference launcher the CUDA host binds (src/kernels/cuda/api.h)
+# every launcher the reference's CUDA host binds: api.h plus the extern block
+# of src/backend_cuda.zig:80-218 (sampler, w16 matvec, rope rows, func getters)
 REFERENCE_API = """
 q35_gpu_cc q35_gpu_sm_count q35_gpu_name q35_launch_quantize_q8_0 q35_launch_quantize_q8_K
 q35_launch_quantize_q8_1_mmq q35_launch_dequantize q35_launch_dequantize_row q35_launch_mul_mat_vec
@@ -30,6 +31,7 @@ q35_func_attn_score_split_dyn q35_func_attn_pv_split_dyn q35_func_attn_softmax_d
 q35_launch_attn_decode_split_dyn q35_launch_attn_decode_split2 q35_launch_init_tables q35_iq_tables_bytes
 q35_iq_tables_ready q35_launch_deinit_tables q35_quant_act_block_elems q35_quant_geom q35_mmq_dp4a_wants
 q35_mmq_act_block_bytes q35_launch_mul_mat_vec_tile q35_launch_quantize_q8_K_mmq
+ q35_launch_mul_mat_vec_w16 q35_launch_rope64_rows q35_func_rope64 q35_func_attn_decode q35_func_copy_range q35_launch_sample q35_launch_sample_init q35_launch_sample_deinit q35_sample_ctl_ints q35_sample_scratch_ints
 """.split()
 
 

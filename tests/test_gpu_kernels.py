@@ -30,8 +30,22 @@ def O():
     return load_oracle()
 
 
+_KEEP = []
+
+
+@pytest.fixture(autouse=True)
+def _keepalive():
+    """device copies made inline (dev(x).data_ptr() as a call argument) must
+    outlive the asynchronous kernel that reads them; free them after the test"""
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
+
+
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t):
