@@ -18,6 +18,7 @@ namespace q35 {
 constexpr int ATT_HD = 256;
 constexpr int ATT_WARPS = 4;
 constexpr int ATT_MAXG = 8;
+constexpr int ATT_SPLIT = 32 * ATT_WARPS;  // positions per split CTA in the engine
 
 struct AttnArgs {
     const float *q, *gate;
@@ -38,10 +39,17 @@ struct AttnArgs {
     const int *active;
 };
 
+// CTA (kv head, sequence, split): up to 32 * ATT_WARPS positions.  Warp w
+// takes positions p0 + 32 w + lane: each lane computes its position's scores
+// for the gqa heads with a serial dot over the 256 dims (the CPU's order, so a
+// score is bit-exact given q and k), then the warp forms max / exp / sum, and
+// P.V runs lane-per-dim over the warp's positions (V rows read coalesced).
+// The ATT_WARPS partials are merged in shared memory.
 template <int G>
 __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(const __grid_constant__ AttnArgs a) {
+    __shared__ __align__(16) float s_q[G][ATT_HD];
     __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
-    __shared__ float s_acc[ATT_WARPS][G][ATT_HD];
+    __shared__ __align__(16) float s_acc[ATT_WARPS][G][ATT_HD];
     const int kvh = blockIdx.x, seq = blockIdx.y, sp = blockIdx.z;
     if (a.active && !a.active[seq]) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -49,41 +57,66 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(const __grid_cons
     const int len = a.lens ? a.lens[seq] : (a.last_pos ? a.last_pos[0] + 1 : a.len_imm);
     const int p0 = sp * a.split_len;
     const int p1 = min(len, p0 + a.split_len);
-    const float *K = a.kc + slot * a.kv_slot + kvh * ATT_HD + lane * 8;
-    const float *V = a.vc + slot * a.kv_slot + kvh * ATT_HD + lane * 8;
-
-    float qv[G][8], acc[G][8], m[G], l[G];
+    for (int i = threadIdx.x; i < G * ATT_HD; i += ATT_WARPS * 32) {
+        const int g = i / ATT_HD, j = i - g * ATT_HD;
+        s_q[g][j] = a.q[(long long)seq * a.q_tok + (long long)(kvh * G + g) * ATT_HD + j];
+    }
+    __syncthreads();
+    const float *Kb = a.kc + slot * a.kv_slot + kvh * ATT_HD;
+    const float *Vb = a.vc + slot * a.kv_slot + kvh * ATT_HD;
+    float m[G], l[G], acc[G][8];
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        const float *qp = a.q + (long long)seq * a.q_tok + (long long)(kvh * G + g) * ATT_HD + lane * 8;
-        const float4 x0 = reinterpret_cast<const float4 *>(qp)[0], x1 = reinterpret_cast<const float4 *>(qp)[1];
-        qv[g][0] = x0.x; qv[g][1] = x0.y; qv[g][2] = x0.z; qv[g][3] = x0.w;
-        qv[g][4] = x1.x; qv[g][5] = x1.y; qv[g][6] = x1.z; qv[g][7] = x1.w;
         m[g] = -INFINITY;
         l[g] = 0.0f;
 #pragma unroll
         for (int i = 0; i < 8; i++) acc[g][i] = 0.0f;
     }
-    for (int t = p0 + warp; t < p1; t += ATT_WARPS) {
-        const float4 *kp = reinterpret_cast<const float4 *>(K + (long long)t * a.kv_dim);
-        const float4 k0 = kp[0], k1 = kp[1];
-        const float4 *vp = reinterpret_cast<const float4 *>(V + (long long)t * a.kv_dim);
-        const float4 v0 = vp[0], v1 = vp[1];
-        const float kk[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    for (int base = p0 + 32 * warp; base < p1; base += 32 * ATT_WARPS) {
+        const int t = base + lane;
+        const bool live = t < p1;
+        float s[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) s[g] = 0.0f;
+        if (live) {
+            const float4 *kr = reinterpret_cast<const float4 *>(Kb + (long long)t * a.kv_dim);
+#pragma unroll 4
+            for (int c = 0; c < ATT_HD / 4; c++) {
+                const float4 kv = kr[c];
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const float4 qv = reinterpret_cast<const float4 *>(s_q[g])[c];
+                    s[g] = __fadd_rn(s[g], __fmul_rn(qv.x, kv.x));
+                    s[g] = __fadd_rn(s[g], __fmul_rn(qv.y, kv.y));
+                    s[g] = __fadd_rn(s[g], __fmul_rn(qv.z, kv.z));
+                    s[g] = __fadd_rn(s[g], __fmul_rn(qv.w, kv.w));
+                }
+            }
+        }
+        const int nlive = min(32, p1 - base);
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float s = 0.0f;
+            const float sc = live ? __fmul_rn(s[g], a.scale) : -INFINITY;
+            const float mw = fmaxf(warp_max(sc), m[g]);
+            const float p = live ? expf(__fsub_rn(sc, mw)) : 0.0f;
+            const float c = expf(__fsub_rn(m[g], mw));  // 0 on the first chunk (m = -inf)
+            l[g] = __fadd_rn(__fmul_rn(l[g], c), warp_sum(p));
 #pragma unroll
-            for (int i = 0; i < 8; i++) s = __fadd_rn(s, __fmul_rn(qv[g][i], kk[i]));
-            s = __fmul_rn(warp_sum(s), a.scale);
-            const float mn = fmaxf(m[g], s);
-            const float c = exp_f(__fsub_rn(m[g], mn));
-            const float e = exp_f(__fsub_rn(s, mn));
-            l[g] = __fadd_rn(__fmul_rn(l[g], c), e);
-#pragma unroll
-            for (int i = 0; i < 8; i++) acc[g][i] = __fadd_rn(__fmul_rn(acc[g][i], c), __fmul_rn(e, vv[i]));
-            m[g] = mn;
+            for (int i = 0; i < 8; i++) acc[g][i] = __fmul_rn(acc[g][i], c);
+            m[g] = mw;
+            for (int u = 0; u < nlive; u++) {
+                const float pu = __shfl_sync(0xffffffffu, p, u);
+                const float4 *vr = reinterpret_cast<const float4 *>(Vb + (long long)(base + u) * a.kv_dim + lane * 8);
+                const float4 v0 = vr[0], v1 = vr[1];
+                acc[g][0] = __fadd_rn(acc[g][0], __fmul_rn(pu, v0.x));
+                acc[g][1] = __fadd_rn(acc[g][1], __fmul_rn(pu, v0.y));
+                acc[g][2] = __fadd_rn(acc[g][2], __fmul_rn(pu, v0.z));
+                acc[g][3] = __fadd_rn(acc[g][3], __fmul_rn(pu, v0.w));
+                acc[g][4] = __fadd_rn(acc[g][4], __fmul_rn(pu, v1.x));
+                acc[g][5] = __fadd_rn(acc[g][5], __fmul_rn(pu, v1.y));
+                acc[g][6] = __fadd_rn(acc[g][6], __fmul_rn(pu, v1.z));
+                acc[g][7] = __fadd_rn(acc[g][7], __fmul_rn(pu, v1.w));
+            }
         }
     }
 #pragma unroll
@@ -96,7 +129,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(const __grid_cons
         for (int i = 0; i < 8; i++) s_acc[warp][g][lane * 8 + i] = acc[g][i];
     }
     __syncthreads();
-    // merge the warps: thread handles dims j and j+128 for every head
     for (int idx = threadIdx.x; idx < G * ATT_HD; idx += ATT_WARPS * 32) {
         const int g = idx / ATT_HD, j = idx - g * ATT_HD;
         float M = -INFINITY;
@@ -107,7 +139,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attn_split(const __grid_cons
 #pragma unroll
             for (int w = 0; w < ATT_WARPS; w++) {
                 if (s_m[w][g] == -INFINITY) continue;
-                const float c = exp_f(__fsub_rn(s_m[w][g], M));
+                const float c = expf(__fsub_rn(s_m[w][g], M));
                 L = __fadd_rn(L, __fmul_rn(s_l[w][g], c));
                 A = __fadd_rn(A, __fmul_rn(s_acc[w][g][j], c));
             }
@@ -140,7 +172,7 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_merge(const __grid_constant__ A
     for (int s = 0; s < ns; s++) {
         const float ms = a.part_ml[(pb + s) * 2];
         if (ms == -INFINITY) continue;
-        const float c = exp_f(__fsub_rn(ms, M));
+        const float c = expf(__fsub_rn(ms, M));
         L = __fadd_rn(L, __fmul_rn(a.part_ml[(pb + s) * 2 + 1], c));
         A = __fadd_rn(A, __fmul_rn(a.part_acc[(pb + s) * ATT_HD + j], c));
     }

@@ -219,6 +219,14 @@ Q35_DEV float block_sum(float v, float *red) {
     return s;
 }
 
+// Sum of squares in the CPU's serial order: ((x0*x0 + x1*x1) + x2*x2) + ...
+// (src/elementwise.zig:45-46).  One thread, one dependent add per element.
+Q35_DEV float serial_sumsq(const float *x, int n) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+    return s;
+}
+
 // exp / log1p evaluated in double and rounded once to f32: within an ulp of
 // the C library's correctly-rounded-in-practice expf/log1pf on the host.
 Q35_DEV float exp_f(float x) { return (float)exp((double)x); }

@@ -48,13 +48,13 @@ Q35_DEV void quantize_row_cta(F f, int cols, int fam, uint8_t *dst) {
 // rmsnorm(x_row, w) -> quantized activation (CTA per token)
 __global__ void __launch_bounds__(256) k_rmsnorm_quant(const float *x, const float *w, int cols, float eps, int fam,
                                                        uint8_t *xq, long long xq_ld, const int *active) {
-    __shared__ float red[8];
     const int t = blockIdx.x;
     if (active && !active[t]) return;
     const float *xr = x + (long long)t * cols;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < cols; i += 256) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-    ss = block_sum<8>(ss, red);
+    __shared__ float sss;
+    if (threadIdx.x == 0) sss = serial_sumsq(xr, cols);
+    __syncthreads();
+    const float ss = sss;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     quantize_row_cta([&](int i) { return __fmul_rn(__fmul_rn(xr[i], scale), w[i]); }, cols, fam,
                      xq + (long long)t * xq_ld);
@@ -113,9 +113,7 @@ __global__ void __launch_bounds__(256) k_gated_norm_quant(const float *g, const 
     const int cols = nv * vd;
     const float *gr = g + (long long)t * cols, *zr = z + (long long)t * cols;
     for (int h = warp; h < nv; h += 8) {
-        float ss = 0.0f;
-        for (int i = lane; i < vd; i += 32) ss = __fadd_rn(ss, __fmul_rn(gr[h * vd + i], gr[h * vd + i]));
-        ss = warp_sum(ss);
+        const float ss = serial_sumsq(gr + h * vd, vd);
         if (lane == 0) sc[h] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)vd), eps)));
     }
     __syncthreads();
@@ -155,7 +153,6 @@ __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const flo
                                                       float *gate, const float *qw, const float *kw, int heads,
                                                       int kv_heads, float eps, float base, const int *pos,
                                                       const int *slots, float *kpool, float *vpool, long long kv_slot) {
-    __shared__ float red[8];
     __shared__ float y[256];
     const int hi = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
     const int hd = 256, q_dim = heads * hd, kv_dim = kv_heads * hd;
@@ -170,7 +167,13 @@ __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const flo
         x = kb[(long long)t * kv_dim + (hi - heads) * hd + j];
         wn = kw;
     }
-    const float ss = block_sum<8>(__fmul_rn(x, x), red);
+    y[j] = x;
+    __syncthreads();
+    __shared__ float sss;
+    if (j == 0) sss = serial_sumsq(y, hd);
+    __syncthreads();
+    const float ss = sss;
+    __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
     y[j] = __fmul_rn(__fmul_rn(x, scale), wn[j]);
     __syncthreads();
@@ -334,7 +337,7 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
 }
 
 inline int eng_attn_nsplit(int max_len) {
-    int ns = (max_len + 255) / 256, p = 1;
+    int ns = (max_len + ATT_SPLIT - 1) / ATT_SPLIT, p = 1;
     while (p < ns) p <<= 1;
     return p;
 }
@@ -374,11 +377,11 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int nsplit, cudaStream_
     a.part_acc = e->part_acc;
     a.part_ml = e->part_ml;
     a.nsplit = nsplit;
-    a.split_len = 256;
+    a.split_len = ATT_SPLIT;
     a.heads = heads;
     a.kv_heads = kvh;
     a.scale = 1.0f / sqrtf((float)hd);
-    Q35_TRY(attn_launch(a, n, nsplit * 256, st));
+    Q35_TRY(attn_launch(a, n, nsplit * ATT_SPLIT, st));
     e->launches += nsplit > 1 ? 2 : 1;
     const int fo = family_of(W.o);
     k_quant_rows<<<dim3((q_dim / (fo == 32 ? 32 : 256) + 7) / 8, n), 256, 0, st>>>(e->gout, q_dim, q_dim, fo, e->xq,

@@ -153,7 +153,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     ALLOC(mh1, 4 * B * c.n_ff);
     ALLOC(logits, 4 * B * (long long)c.vocab);
     long long maxsplit = 1;
-    while (maxsplit < (e->max_seq + 255) / 256) maxsplit <<= 1;
+    while (maxsplit < (e->max_seq + ATT_SPLIT - 1) / ATT_SPLIT) maxsplit <<= 1;
     ALLOC(part_acc, 4 * B * c.n_heads * maxsplit * ATT_HD);
     ALLOC(part_ml, 4 * B * c.n_heads * maxsplit * 2);
     ALLOC(probe_buf, 4 * (long long)c.n_layers * B * h);

@@ -67,12 +67,12 @@ __global__ void k_swiglu(float *g, const float *u, long long n) {
 // rmsnorm: scale = 1/sqrt(ss/n + eps); out = x*scale*w  (elementwise.zig:43-57)
 template <int NT>
 __global__ void __launch_bounds__(NT) k_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
-    __shared__ float red[NT / 32];
     const float *xr = x + (long long)blockIdx.x * n;
     float *orow = out + (long long)blockIdx.x * n;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += NT) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-    ss = block_sum<NT / 32>(ss, red);
+    __shared__ float sss;
+    if (threadIdx.x == 0) sss = serial_sumsq(xr, n);
+    __syncthreads();
+    const float ss = sss;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
     for (int i = threadIdx.x; i < n; i += NT) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
@@ -82,12 +82,12 @@ __global__ void __launch_bounds__(NT) k_rmsnorm(float *out, const float *x, cons
 template <int NT>
 __global__ void __launch_bounds__(NT) k_l2norm(float *x, int offset, int rows, int n, float eps, int row_stride,
                                                float post_scale, int apply_scale) {
-    __shared__ float red[NT / 32];
     const int r = blockIdx.x % rows, t = blockIdx.x / rows;
     float *xr = x + offset + (long long)t * row_stride + (long long)r * n;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += NT) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-    ss = block_sum<NT / 32>(ss, red);
+    __shared__ float sss;
+    if (threadIdx.x == 0) sss = serial_sumsq(xr, n);
+    __syncthreads();
+    const float ss = sss;
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
     for (int i = threadIdx.x; i < n; i += NT) {
         float v = __fmul_rn(xr[i], inv);

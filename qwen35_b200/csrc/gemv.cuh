@@ -29,11 +29,11 @@
 
 namespace q35 {
 
-constexpr int GV_WARPS = 8;                      // consumer warps
+constexpr int GV_WARPS = 4;                      // consumer warps
 constexpr int GV_THREADS = (GV_WARPS + 1) * 32;  // + one producer warp
 constexpr int GV_MAX_SEG = 4;
 constexpr int GV_MAX_NT = 16;                    // tokens per pass
-constexpr int GV_FOLD_LD = 36;                   // fold row: 16-byte aligned for vector reads
+constexpr int GV_FOLD_FLOATS = 640;              // per-warp fold scratch (R * NT * (BPP + 4) <= 640)
 
 enum { GV_STORE = 0, GV_ADD = 1 };
 
@@ -198,19 +198,29 @@ Q35_DEV void part_q6_k(const uint8_t *wb, const ActView &A, int ntok, int b, int
     }
 }
 
-// One row: lanes split blocks (LPB lanes per block), terms folded in order.
-// The fold reads a chunk's BPC terms with 128-bit shared loads (all issued
-// before the first add) and adds them in block order.
-template <int NT, int LPB>
-Q35_DEV void gemv_row(int tt, const uint8_t *rowp, const ActView &A, int ntok, int nb, float *fold,
-                      float *out_t0, long long out_ld, int mode, int lane) {
-    constexpr int BPC = 32 / LPB;
+// R rows per warp, LR = 32/R lanes per row.  Lane (g, q) = (lane / LR,
+// lane % LR) works on row g: with LPB lanes per block it takes block part
+// q % LPB of block cb + q / LPB, for BPP = LR / LPB blocks per pass.  Lane
+// (g, t) with t < ntok then folds token t's terms of that pass in block
+// order into its running sum -- the reference scalar tier's rounding
+// sequence -- so R rows (and NT tokens) fold concurrently on different lanes.
+template <int NT, int LPB, int R>
+Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, const ActView &A, int ntok, int nb,
+                       float *fold, float *out_r0, long long out_ld, int mode, int lane) {
+    constexpr int LR = 32 / R;
+    constexpr int BPP = LR / LPB;
+    constexpr int FL = BPP + 4;
+    static_assert(NT <= LR, "one folding lane per (row, token)");
     const int bsz = geom_of(tt).bytes;
-    const int p = lane % LPB;
+    const int g = lane / LR, q = lane % LR;
+    const int j = q / LPB, p = q % LPB;
+    const bool row_ok = g < nvalid;
+    const uint8_t *rowp = rowp0 + (size_t)(row_ok ? g : 0) * row_bytes;
+    float *fg = fold + g * NT * FL;
     float acc = 0.0f;
-    for (int cb = 0; cb < nb; cb += BPC) {
-        const int b = cb + lane / LPB;
-        const bool act = b < nb;
+    for (int cb = 0; cb < nb; cb += BPP) {
+        const int b = cb + j;
+        const bool act = row_ok && b < nb;
         const uint8_t *wb = rowp + (size_t)(act ? b : 0) * bsz;
         int is[NT], ms[NT];
 #pragma unroll
@@ -240,7 +250,6 @@ Q35_DEV void gemv_row(int tt, const uint8_t *rowp, const ActView &A, int ntok, i
             }
         }
         if (act && p == 0) {
-            const int j = lane / LPB;
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t < ntok) {
@@ -258,33 +267,33 @@ Q35_DEV void gemv_row(int tt, const uint8_t *rowp, const ActView &A, int ntok, i
                         const float dm = __fmul_rn(dy, f16_to_f32(ld_u16(wb + 2)));
                         term = __fsub_rn(__fmul_rn(d, __int2float_rn(is[t])), __fmul_rn(dm, __int2float_rn(ms[t])));
                     }
-                    fold[t * GV_FOLD_LD + j] = term;
+                    fg[t * FL + j] = term;
                 }
             }
         }
         __syncwarp();
-        if (lane < ntok) {
-            const float *f = fold + lane * GV_FOLD_LD;
-            if (nb - cb >= BPC) {
-                float4 v[BPC / 4];
+        if (row_ok && q < ntok) {
+            const float *f = fg + q * FL;
+            if (BPP >= 4 && nb - cb >= BPP) {
+                float4 v[BPP / 4 > 0 ? BPP / 4 : 1];
 #pragma unroll
-                for (int i = 0; i < BPC / 4; i++) v[i] = reinterpret_cast<const float4 *>(f)[i];
+                for (int i = 0; i < BPP / 4; i++) v[i] = reinterpret_cast<const float4 *>(f)[i];
 #pragma unroll
-                for (int i = 0; i < BPC / 4; i++) {
+                for (int i = 0; i < BPP / 4; i++) {
                     acc = __fadd_rn(acc, v[i].x);
                     acc = __fadd_rn(acc, v[i].y);
                     acc = __fadd_rn(acc, v[i].z);
                     acc = __fadd_rn(acc, v[i].w);
                 }
             } else {
-                const int n = nb - cb;
-                for (int j = 0; j < n; j++) acc = __fadd_rn(acc, f[j]);
+                const int n = min(BPP, nb - cb);
+                for (int i = 0; i < n; i++) acc = __fadd_rn(acc, f[i]);
             }
         }
         __syncwarp();
     }
-    if (lane < ntok) {
-        float *o = out_t0 + (long long)lane * out_ld;
+    if (row_ok && q < ntok) {
+        float *o = out_r0 + g + (long long)q * out_ld;
         *o = mode == GV_ADD ? __fadd_rn(*o, acc) : acc;
     }
 }
@@ -297,13 +306,13 @@ Q35_DEV int gemv_find_seg(const GemvArgs &a, long long tile) {
     return s;
 }
 
-template <int NT>
+template <int NT, int R>
 __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + a.nstage;
     float *foldbase = reinterpret_cast<float *>(smem + 256);
-    uint8_t *act = smem + 256 + GV_WARPS * GV_MAX_NT * GV_FOLD_LD * 4;
+    uint8_t *act = smem + 256 + GV_WARPS * GV_FOLD_FLOATS * 4;
     act = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(act) + 127) & ~uintptr_t(127));
     uint8_t *stages = act + (size_t)a.ntok * a.act_stride;
     stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
@@ -398,7 +407,7 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
     named_bar_sync(1, cthreads);
 
     ActView A{act, a.act_stride, a.cols};
-    float *fold = foldbase + warp * GV_MAX_NT * GV_FOLD_LD;
+    float *fold = foldbase + warp * GV_FOLD_FLOATS;
     long long it = 0;
     for (long long tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x, it++) {
         const int s = (int)(it % a.nstage);
@@ -411,13 +420,14 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
         const uint8_t *buf = stages + (size_t)s * stage_ld + (start & 15);
         const int nb = a.cols / geom_of(sg.ttype).elems;
         const bool lpb1 = sg.ttype == TT_Q8_0 || sg.ttype == TT_IQ4_NL;
-        for (int rr = warp; rr < nr; rr += GV_WARPS) {
+        for (int rg = warp * R; rg < nr; rg += GV_WARPS * R) {
+            const int nv = min(R, nr - rg);
             if (lpb1)
-                gemv_row<NT, 1>(sg.ttype, buf + (size_t)rr * sg.row_bytes, A, a.ntok, nb, fold, sg.out + r0 + rr,
-                                sg.out_ld, sg.mode, lane);
+                gemv_rows<NT, 1, R>(sg.ttype, buf + (size_t)rg * sg.row_bytes, sg.row_bytes, nv, A, a.ntok, nb, fold,
+                                    sg.out + r0 + rg, sg.out_ld, sg.mode, lane);
             else
-                gemv_row<NT, 4>(sg.ttype, buf + (size_t)rr * sg.row_bytes, A, a.ntok, nb, fold, sg.out + r0 + rr,
-                                sg.out_ld, sg.mode, lane);
+                gemv_rows<NT, 4, R>(sg.ttype, buf + (size_t)rg * sg.row_bytes, sg.row_bytes, nv, A, a.ntok, nb, fold,
+                                    sg.out + r0 + rg, sg.out_ld, sg.mode, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -439,7 +449,7 @@ struct GemvSegDesc {
 int gemv_sm_count();
 
 inline size_t gemv_smem_bytes(int ntok, int act_stride, int stage_bytes, int nstage) {
-    size_t s = 256 + (size_t)GV_WARPS * GV_MAX_NT * GV_FOLD_LD * 4 + 128;
+    size_t s = 256 + (size_t)GV_WARPS * GV_FOLD_FLOATS * 4 + 128;
     s += (size_t)ntok * act_stride + 128;
     s += (size_t)nstage * (stage_bytes + 32);
     return s;
@@ -448,34 +458,45 @@ inline size_t gemv_smem_bytes(int ntok, int act_stride, int stage_bytes, int nst
 // Set the dynamic shared-memory ceiling of every instantiation once, outside
 // any stream capture (attribute calls are not stream work, but doing them
 // up front keeps a captured step free of host-side configuration).
+template <int NT, int R>
+inline cudaError_t gemv_set_smem() {
+    return cudaFuncSetAttribute(k_gemv<NT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
 inline int gemv_prepare() {
     static int done = 0;
     if (done) return 0;
-    const int lim = 227 * 1024;
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e != cudaSuccess) return (int)e;
+    const cudaError_t es[] = {gemv_set_smem<1, 1>(), gemv_set_smem<1, 2>(), gemv_set_smem<1, 4>(),
+                              gemv_set_smem<2, 1>(), gemv_set_smem<2, 2>(), gemv_set_smem<2, 4>(),
+                              gemv_set_smem<4, 1>(), gemv_set_smem<4, 2>(), gemv_set_smem<4, 4>(),
+                              gemv_set_smem<8, 1>(), gemv_set_smem<8, 2>(), gemv_set_smem<8, 4>(),
+                              gemv_set_smem<16, 1>(), gemv_set_smem<16, 2>()};
+    for (cudaError_t e : es)
+        if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;
 }
 
-template <int NT>
+template <int NT, int R>
 inline int gemv_launch_nt(GemvArgs &a, cudaStream_t st) {
     const size_t smem = gemv_smem_bytes(a.ntok, a.act_stride, a.stage_bytes, a.nstage);
     if (smem > 227 * 1024) return (int)cudaErrorInvalidValue;
     Q35_TRY_RC(gemv_prepare());
     // resident CTAs per SM from shared memory (228 KB per SM, 1 KB reserved
-    // per CTA) and registers (<= 96 x 288 threads): at most 2
+    // per CTA) and registers (<= 96 x 160 threads): at most 3
     int occ = (int)((228 * 1024) / (smem + 1024));
-    occ = occ < 1 ? 1 : (occ > 2 ? 2 : occ);
+    occ = occ < 1 ? 1 : (occ > 3 ? 3 : occ);
     long long grid = (long long)gemv_sm_count() * occ;
     if (grid > a.total_tiles) grid = a.total_tiles;
     if (grid < 1) grid = 1;
-    k_gemv<NT><<<(unsigned)grid, GV_THREADS, smem, st>>>(a);
+    k_gemv<NT, R><<<(unsigned)grid, GV_THREADS, smem, st>>>(a);
     return (int)cudaGetLastError();
+}
+
+template <int NT>
+inline int gemv_launch_r(GemvArgs &a, int R, cudaStream_t st) {
+    if (NT <= 8 && R >= 4) return gemv_launch_nt<NT, (NT <= 8 ? 4 : 2)>(a, st);
+    if (R >= 2) return gemv_launch_nt<NT, 2>(a, st);
+    return gemv_launch_nt<NT, 1>(a, st);
 }
 
 // Launch y = W x for up to GV_MAX_SEG matrices sharing one activation.
@@ -503,8 +524,12 @@ inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int co
         max_rb = rb > max_rb ? rb : max_rb;
         total_rows += segs[i].rows;
     }
-    int stage = 16384;
-    if (max_rb + 16 > stage) stage = (max_rb + 16 + 15) & ~15;
+    // rows per warp: several short rows per warp amortise the ordered fold
+    const int R = max_rb <= 1152 ? 4 : (max_rb <= 2304 ? 2 : 1);
+    // a stage holds at least one round (every consumer warp busy on R rows)
+    int stage = GV_WARPS * R * max_rb + 32;
+    if (stage < 16384) stage = 16384;
+    stage = (stage + 15) & ~15;
     // tokens per pass: the largest group whose shared activation copy plus a
     // 3-stage weight ring fits the CTA's shared memory
     int group = GV_MAX_NT;
@@ -536,7 +561,7 @@ inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int co
             int rpt = (stage - 16) / s.row_bytes;
             // at least ~2 tiles per SM when the matrix is small
             const long long want = (total_rows + 2LL * nsm - 1) / (2LL * nsm);
-            if (want < rpt) rpt = (int)(want > 0 ? want : 1);
+            if (want < rpt) rpt = (int)(((want > 0 ? want : 1) + R - 1) / R * R) < rpt ? (int)(((want > 0 ? want : 1) + R - 1) / R * R) : rpt;
             if (rpt < 1) rpt = 1;
             s.rows_per_tile = rpt;
             s.tile_begin = tiles;
@@ -546,15 +571,15 @@ inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int co
         if (tiles == 0) continue;
         int rc;
         if (nt == 1)
-            rc = gemv_launch_nt<1>(a, st);
+            rc = gemv_launch_r<1>(a, R, st);
         else if (nt == 2)
-            rc = gemv_launch_nt<2>(a, st);
+            rc = gemv_launch_r<2>(a, R, st);
         else if (nt <= 4)
-            rc = gemv_launch_nt<4>(a, st);
+            rc = gemv_launch_r<4>(a, R, st);
         else if (nt <= 8)
-            rc = gemv_launch_nt<8>(a, st);
+            rc = gemv_launch_r<8>(a, R, st);
         else
-            rc = gemv_launch_nt<16>(a, st);
+            rc = gemv_launch_r<16>(a, R, st);
         if (rc) return rc;
     }
     return 0;

@@ -2,8 +2,10 @@
 the CPU oracle engine over the same packed weight bytes.
 
 Bars: per-layer f32 outputs within 1e-3 relative L2,
-greedy tokens identical; here the measured gap is ~1e-6 (only reduction
-order differs), so the tests also assert a 1e-4 bound.
+greedy tokens identical.  Every op except attention's softmax / P.V sums is
+bit-exact with the CPU (norm sums included), and the int8 activation
+quantization launders attention's last-ulp differences, so the measured gap
+is 0 or a few 1e-7.
 """
 import os
 
@@ -77,8 +79,8 @@ def _run_parity(q35, cfg_name, prompt_len, n_gen, seed=1, threads=None):
 @pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed"])
 def test_engine_matches_oracle(q35, cfg_name):
     tg, tc, wl, wlay = _run_parity(q35, cfg_name, prompt_len=7, n_gen=12)
-    assert wl < 1e-3 and wlay < 1e-3
-    assert wl < 1e-4 and wlay < 1e-4, (wl, wlay)
+    assert wl < 1e-3 and wlay < 1e-3, (wl, wlay)
+    assert wl < 1e-5 and wlay < 1e-5, (wl, wlay)
     assert tg == tc
 
 

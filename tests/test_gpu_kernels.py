@@ -2,9 +2,9 @@
 CPU oracle on the same seeded inputs.
 
 Bars: integer / byte work (activation quantizers, weight encoders,
-dequantizers) and the block-ordered GEMV fold and the GDN recurrence are
-bit-exact; reductions whose order the device changes (norm sums, softmax)
-are within 1e-5 relative.
+dequantizers), the block-ordered GEMV fold, the norms (serial sum order) and
+the GDN recurrence are bit-exact; attention's softmax / P.V reductions and
+the double-evaluated transcendentals are within 1e-5 relative.
 """
 import ctypes
 import os
@@ -313,14 +313,15 @@ def test_norms_and_activations(L, O):
     O.q35o_rmsnorm_rows(fp(ref), fp(x), fp(w), rows, n, 1e-6)
     out = torch.zeros_like(dev(x))
     ok(L.q35_launch_rmsnorm(out.data_ptr(), dev(x).data_ptr(), dev(w).data_ptr(), rows, n, 1e-6, S))
-    assert np.abs(host(out) - ref).max() <= 1e-5 * np.abs(ref).max()
+    # sums of squares are taken in the CPU's serial order: bit-exact
+    assert np.array_equal(host(out).view(np.uint32), ref.view(np.uint32))
     nk, kd = 4, 128
     v = rng.standard_normal(3 * nk * kd).astype(np.float32)
     rv = v.copy()
     O.q35o_l2norm_qk_scale(fp(rv), nk, kd, nk * kd, np.float32(1 / np.sqrt(128)))
     dv = dev(v)
     ok(L.q35_launch_l2norm_qk_scale(dv.data_ptr(), nk, kd, nk * kd, 1e-6, float(np.float32(1 / np.sqrt(128))), S))
-    assert np.abs(host(dv) - rv).max() <= 1e-6
+    assert np.array_equal(host(dv).view(np.uint32), rv.view(np.uint32))
     g = rng.standard_normal(4096).astype(np.float32) * 4
     u = rng.standard_normal(4096).astype(np.float32)
     rg = g.copy()
