@@ -89,6 +89,17 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def nvsmi_id(local):
+    """nvidia-smi --id for this rank's device: its PCI bus id, matched through
+    torch's device properties (CUDA_VISIBLE_DEVICES may renumber devices)."""
+    import torch
+    p = torch.cuda.get_device_properties(local)
+    try:
+        return "%08X:%02X:%02X.0" % (int(p.pci_domain_id), int(p.pci_bus_id), int(p.pci_device_id))
+    except Exception:
+        return str(local)
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -374,9 +385,7 @@ def main():
 
     # ---------------- headline: 0.8B Q8_0, batch 1 ----------------
     run = Run("0.8b", 1, args.prompt, extra, seed=args.seed + rank)
-    gpu_id = torch.cuda.get_device_properties(local).pci_bus_id if hasattr(
-        torch.cuda.get_device_properties(local), "pci_bus_id") else str(local)
-    clocks = ClockSampler(gpu_id)
+    clocks = ClockSampler(nvsmi_id(local))
     clocks.start()
     ms = time_decode(run, args.steps, args.warmup, dist)
     clk = clocks.stop()

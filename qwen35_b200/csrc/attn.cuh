@@ -207,3 +207,161 @@ inline int attn_launch(AttnArgs a, int nseq, int max_len, cudaStream_t st) {
 }
 
 }  // namespace q35
+
+namespace q35 {
+
+// ---------------------------------------------------------------------------
+// Decode attention in the CPU's exact operation order (src/elementwise.zig:
+// 349-372): score_t = (sum_j q_j k_tj) * scale with j ascending; softmax as
+// max, e_t = exp(score_t - max), serial sum over t, e_t / sum; out_j =
+// sum_t p_t v_tj with t ascending; out_j *= sigmoid(gate_j).
+// Kernel 1 (scores): CTA (kv head, sequence, 128-position chunk), a lane per
+// position computing the gqa heads' serial dots.
+// Kernel 2 (softmax + P.V): CTA (q head, sequence, 64-dim chunk); every CTA
+// of a head recomputes the (cheap) softmax, then thread j walks t in order
+// for its dim.  Parallelism comes from dims, not positions, so no split
+// re-associates a sum.
+// ---------------------------------------------------------------------------
+constexpr int ATTX_CHUNK = 128;
+constexpr int ATTX_DIMS = 64;
+
+struct AttnXArgs {
+    const float *q, *gate;
+    long long q_tok;
+    const float *kc, *vc;
+    long long kv_slot;
+    int kv_dim;
+    const int *slots, *lens;
+    const int *last_pos;
+    int len_imm;
+    float *scores;       // [n][heads][max_len]
+    int max_len;
+    float *out;          // gated attention output
+    long long out_tok;
+    int heads, kv_heads;
+    float scale;
+    int fam;             // 32: also quantize the output (Q8_0 blocks) into xq
+    uint8_t *xq;
+    long long xq_ld;
+};
+
+Q35_DEV int attx_len(const AttnXArgs &a, int seq) {
+    return a.lens ? a.lens[seq] : (a.last_pos ? a.last_pos[0] + 1 : a.len_imm);
+}
+
+template <int G>
+__global__ void __launch_bounds__(ATTX_CHUNK) k_attx_scores(const __grid_constant__ AttnXArgs a) {
+    __shared__ __align__(16) float s_q[G][ATT_HD];
+    const int kvh = blockIdx.x, seq = blockIdx.y, t = blockIdx.z * ATTX_CHUNK + threadIdx.x;
+    const int len = attx_len(a, seq);
+    if (blockIdx.z * ATTX_CHUNK >= len) return;
+    for (int i = threadIdx.x; i < G * ATT_HD; i += ATTX_CHUNK) {
+        const int g = i / ATT_HD, j = i - g * ATT_HD;
+        s_q[g][j] = a.q[(long long)seq * a.q_tok + (long long)(kvh * G + g) * ATT_HD + j];
+    }
+    __syncthreads();
+    if (t >= len) return;
+    const long long slot = a.slots ? a.slots[seq] : seq;
+    const float4 *kr = reinterpret_cast<const float4 *>(a.kc + slot * a.kv_slot + (long long)t * a.kv_dim + kvh * ATT_HD);
+    float s[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) s[g] = 0.0f;
+#pragma unroll 4
+    for (int c = 0; c < ATT_HD / 4; c++) {
+        const float4 kv = kr[c];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float4 qv = reinterpret_cast<const float4 *>(s_q[g])[c];
+            s[g] = __fadd_rn(s[g], __fmul_rn(qv.x, kv.x));
+            s[g] = __fadd_rn(s[g], __fmul_rn(qv.y, kv.y));
+            s[g] = __fadd_rn(s[g], __fmul_rn(qv.z, kv.z));
+            s[g] = __fadd_rn(s[g], __fmul_rn(qv.w, kv.w));
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        a.scores[((long long)seq * a.heads + kvh * G + g) * a.max_len + t] = __fmul_rn(s[g], a.scale);
+}
+
+__global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ AttnXArgs a) {
+    extern __shared__ float s_p[];  // len probabilities
+    __shared__ float s_red[2];
+    const int h = blockIdx.x, seq = blockIdx.y, dc = blockIdx.z, j = threadIdx.x;
+    const int len = attx_len(a, seq);
+    const int gqa = a.heads / a.kv_heads, kvh = h / gqa;
+    const float *sc = a.scores + ((long long)seq * a.heads + h) * a.max_len;
+    float m = -3.40282347e38f;
+    for (int t = j; t < len; t += ATTX_DIMS) {
+        const float v = sc[t];
+        s_p[t] = v;
+        m = fmaxf(m, v);
+    }
+    m = warp_max(m);
+    if ((j & 31) == 0) s_red[j >> 5] = m;
+    __syncthreads();
+    m = fmaxf(s_red[0], s_red[1]);
+    for (int t = j; t < len; t += ATTX_DIMS) s_p[t] = exp_f(__fsub_rn(s_p[t], m));
+    __syncthreads();
+    if (j == 0) {
+        float sum = 0.0f;
+        for (int t = 0; t < len; t++) sum = __fadd_rn(sum, s_p[t]);
+        s_red[0] = sum;
+    }
+    __syncthreads();
+    const float sum = s_red[0];
+    for (int t = j; t < len; t += ATTX_DIMS) s_p[t] = __fdiv_rn(s_p[t], sum);
+    __syncthreads();
+    const long long slot = a.slots ? a.slots[seq] : seq;
+    const float *vb = a.vc + slot * a.kv_slot + kvh * ATT_HD + dc * ATTX_DIMS + j;
+    float acc = 0.0f;
+    int t = 0;
+    for (; t + 4 <= len; t += 4) {
+        const float v0 = vb[(long long)t * a.kv_dim], v1 = vb[(long long)(t + 1) * a.kv_dim];
+        const float v2 = vb[(long long)(t + 2) * a.kv_dim], v3 = vb[(long long)(t + 3) * a.kv_dim];
+        acc = __fadd_rn(acc, __fmul_rn(s_p[t], v0));
+        acc = __fadd_rn(acc, __fmul_rn(s_p[t + 1], v1));
+        acc = __fadd_rn(acc, __fmul_rn(s_p[t + 2], v2));
+        acc = __fadd_rn(acc, __fmul_rn(s_p[t + 3], v3));
+    }
+    for (; t < len; t++) acc = __fadd_rn(acc, __fmul_rn(s_p[t], vb[(long long)t * a.kv_dim]));
+    const int dim = dc * ATTX_DIMS + j;
+    const float gt = a.gate[(long long)seq * a.q_tok + (long long)h * ATT_HD + dim];
+    const float o = __fmul_rn(acc, sigmoid_f(gt));
+    a.out[(long long)seq * a.out_tok + (long long)h * ATT_HD + dim] = o;
+    if (a.fam == 32) {
+        const int blk = (h * ATT_HD + dc * ATTX_DIMS) / 32 + (j >> 5);
+        quant_q8_0_warp(o, a.xq + (long long)seq * a.xq_ld + (long long)blk * 34, j & 31);
+    }
+}
+
+inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t st) {
+    if (nseq <= 0) return 0;
+    if (a.kv_heads <= 0 || a.heads % a.kv_heads) return (int)cudaErrorInvalidValue;
+    const int G = a.heads / a.kv_heads;
+    if (max_len <= 0 || max_len > a.max_len) return (int)cudaErrorInvalidValue;
+    const dim3 g1((unsigned)a.kv_heads, (unsigned)nseq, (unsigned)((max_len + ATTX_CHUNK - 1) / ATTX_CHUNK));
+    switch (G) {
+    case 1: k_attx_scores<1><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    case 2: k_attx_scores<2><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    case 3: k_attx_scores<3><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    case 4: k_attx_scores<4><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    case 6: k_attx_scores<6><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    case 8: k_attx_scores<8><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    default: return (int)cudaErrorInvalidValue;
+    }
+    int rc = (int)cudaGetLastError();
+    if (rc) return rc;
+    const size_t smem = (size_t)max_len * 4;
+    if (smem > 48 * 1024) {
+        static size_t configured = 0;
+        if (smem > configured) {
+            rc = (int)cudaFuncSetAttribute(k_attx_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (rc) return rc;
+            configured = smem;
+        }
+    }
+    k_attx_pv<<<dim3((unsigned)a.heads, (unsigned)nseq, ATT_HD / ATTX_DIMS), ATTX_DIMS, smem, st>>>(a);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace q35

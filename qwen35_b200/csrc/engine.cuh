@@ -245,7 +245,7 @@ struct q35b_engine {
     int *d_len = nullptr, *d_next = nullptr;
     float *x = nullptr, *qkv = nullptr, *z = nullptr, *ab = nullptr, *gam = nullptr, *gout = nullptr;
     float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;
-    float *logits = nullptr, *part_acc = nullptr, *part_ml = nullptr, *probe_buf = nullptr;
+    float *logits = nullptr, *scores = nullptr, *probe_buf = nullptr;
     uint8_t *xq = nullptr;
     long long xq_ld = 0;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -305,44 +305,53 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
                       {W.beta.w, e->ab + nv, W.beta.rows, W.beta.tt, 2 * nv, GV_STORE}},
                      e->xq, c.hidden, st));
     const int gi = e->gdn_idx[li];
-    const int *slots = e->d_in + e->max_batch;
-    k_conv_batched<<<dim3((conv_dim + 127) / 128, n), 128, 0, st>>>(e->conv_pool + gi * (long long)e->n_slots * e->conv_slot,
-                                                                      e->conv_slot, slots, e->qkv, conv_dim, W.conv1d);
-    k_gdn_gamma<<<ew_grid((long long)nv * n, 128), 128, 0, st>>>(e->ab, e->ab + nv, W.ssm_a, W.dt_bias, e->gam, nv, n,
-                                                                 2 * nv, 2 * nv, nv);
-    const float qscale = 1.0f / sqrtf((float)kd);
-    k_l2norm<128><<<nk * n, 128, 0, st>>>(e->qkv, 0, nk, kd, 1e-6f, conv_dim, qscale, 1);
-    k_l2norm<128><<<nk * n, 128, 0, st>>>(e->qkv, kq, nk, kd, 1e-6f, conv_dim, 1.0f, 0);
-    e->launches += 4;
-    Q35_TRY((int)cudaGetLastError());
-    GdnArgs a{};
-    a.state = e->state_pool + gi * (long long)e->n_slots * e->state_slot;
-    a.state_head = (long long)kd * kd;
-    a.state_slot = e->state_slot;
-    a.slots = slots;
-    a.k = e->qkv + kq; a.k_tok = conv_dim; a.k_head = kd;
-    a.q = e->qkv; a.q_tok = conv_dim; a.q_head = kd;
-    a.v = e->qkv + 2 * kq; a.v_tok = conv_dim; a.v_head = kd;
-    a.out = e->gout; a.out_tok = vdim; a.out_head = kd;
-    a.gamma = e->gam; a.g_tok = nv;
-    a.beta = e->ab + nv; a.b_tok = 2 * nv;
-    a.heads = nv; a.nk = nk; a.rows = 1;
-    Q35_TRY(gdn_launch(a, n, st));
-    e->launches++;
     const int fo = family_of(W.ssm_out);
-    k_gated_norm_quant<<<n, 256, 0, st>>>(e->gout, e->z, W.ssm_norm, nv, kd, c.rms_eps, fo, e->xq, e->xq_ld);
+    GdnCoreArgs g{};
+    g.qkv = e->qkv;
+    g.qkv_ld = conv_dim;
+    g.z = e->z;
+    g.z_ld = vdim;
+    g.ab = e->ab;
+    g.ab_ld = 2 * nv;
+    g.conv_w = W.conv1d;
+    g.hist = e->conv_pool + gi * (long long)e->n_slots * e->conv_slot;
+    g.hist_slot = e->conv_slot;
+    g.ssm_a = W.ssm_a;
+    g.dt_bias = W.dt_bias;
+    g.ssm_norm = W.ssm_norm;
+    g.state = e->state_pool + gi * (long long)e->n_slots * e->state_slot;
+    g.state_slot = e->state_slot;
+    g.slots = e->d_in + e->max_batch;
+    g.pos = e->d_in + 2 * e->max_batch;
+    g.nv = nv;
+    g.nk = nk;
+    g.eps = c.rms_eps;
+    g.qscale = 1.0f / sqrtf((float)kd);
+    g.fam = fo;
+    g.xq = e->xq;
+    g.xq_ld = e->xq_ld;
+    g.gout = e->gout;
+    g.gout_ld = vdim;
+    k_gdn_core<<<dim3(nv, n), GDN_KD, 0, st>>>(g);
     e->launches++;
     Q35_TRY((int)cudaGetLastError());
+    if (fo != 32) {
+        k_quant_rows<<<dim3((vdim / 256 + 7) / 8, n), 256, 0, st>>>(e->gout, vdim, vdim, fo, e->xq, e->xq_ld);
+        e->launches++;
+        Q35_TRY((int)cudaGetLastError());
+    }
     return eng_gemv(e, n, {{W.ssm_out.w, e->x, W.ssm_out.rows, W.ssm_out.tt, c.hidden, GV_ADD}}, e->xq, vdim, st);
 }
 
-inline int eng_attn_nsplit(int max_len) {
-    int ns = (max_len + ATT_SPLIT - 1) / ATT_SPLIT, p = 1;
-    while (p < ns) p <<= 1;
-    return p;
+// context bucket a captured step is built for: the score / P.V grids cover
+// max_len positions (power of two multiple of 128, capped at the slot size)
+inline int eng_len_bucket(int max_len, int max_seq) {
+    int b = 128;
+    while (b < max_len) b <<= 1;
+    return b < max_seq ? b : max_seq;
 }
 
-inline int eng_layer_full(q35b_engine *e, int li, int n, int nsplit, cudaStream_t st) {
+inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream_t st) {
     const q35b_config &c = e->c;
     const LayerW &W = e->L[li];
     const int heads = c.n_heads, kvh = c.n_kv_heads, hd = c.head_dim;
@@ -362,7 +371,8 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int nsplit, cudaStream_
                                                         e->kv_slot);
     e->launches++;
     Q35_TRY((int)cudaGetLastError());
-    AttnArgs a{};
+    const int fo = family_of(W.o);
+    AttnXArgs a{};
     a.q = e->q;
     a.gate = e->gate;
     a.q_tok = q_dim;
@@ -372,22 +382,23 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int nsplit, cudaStream_
     a.kv_dim = kv_dim;
     a.slots = slots;
     a.lens = e->d_len;
+    a.scores = e->scores;
+    a.max_len = e->max_seq;
     a.out = e->gout;
     a.out_tok = q_dim;
-    a.part_acc = e->part_acc;
-    a.part_ml = e->part_ml;
-    a.nsplit = nsplit;
-    a.split_len = ATT_SPLIT;
     a.heads = heads;
     a.kv_heads = kvh;
     a.scale = 1.0f / sqrtf((float)hd);
-    Q35_TRY(attn_launch(a, n, nsplit * ATT_SPLIT, st));
-    e->launches += nsplit > 1 ? 2 : 1;
-    const int fo = family_of(W.o);
-    k_quant_rows<<<dim3((q_dim / (fo == 32 ? 32 : 256) + 7) / 8, n), 256, 0, st>>>(e->gout, q_dim, q_dim, fo, e->xq,
-                                                                                  e->xq_ld);
-    e->launches++;
-    Q35_TRY((int)cudaGetLastError());
+    a.fam = fo;
+    a.xq = e->xq;
+    a.xq_ld = e->xq_ld;
+    Q35_TRY(attx_launch(a, n, max_len, st));
+    e->launches += 2;
+    if (fo != 32) {
+        k_quant_rows<<<dim3((q_dim / 256 + 7) / 8, n), 256, 0, st>>>(e->gout, q_dim, q_dim, fo, e->xq, e->xq_ld);
+        e->launches++;
+        Q35_TRY((int)cudaGetLastError());
+    }
     return eng_gemv(e, n, {{W.o.w, e->x, W.o.rows, W.o.tt, c.hidden, GV_ADD}}, e->xq, q_dim, st);
 }
 
@@ -408,7 +419,7 @@ inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
 }
 
 // the whole step body (graph-capturable: every per-step value is in device memory)
-inline int eng_step_body(q35b_engine *e, int n, int nsplit, cudaStream_t st) {
+inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
     const q35b_config &c = e->c;
     e->launches = 0;
     const int *tok = e->d_in;
@@ -419,7 +430,7 @@ inline int eng_step_body(q35b_engine *e, int n, int nsplit, cudaStream_t st) {
     Q35_TRY((int)cudaGetLastError());
     for (int li = 0; li < c.n_layers; li++) {
         if (is_full_layer(c, li))
-            Q35_TRY(eng_layer_full(e, li, n, nsplit, st));
+            Q35_TRY(eng_layer_full(e, li, n, max_len, st));
         else
             Q35_TRY(eng_layer_gdn(e, li, n, st));
         Q35_TRY(eng_mlp(e, li, n, st));

@@ -22,7 +22,7 @@ int set_lin(Lin &l, int tt, const void *d, long long rows, long long cols) {
 
 bool lin_ok(const Lin &l, long long rows, long long cols) { return l.w && l.rows == rows && l.cols == cols; }
 
-long long graph_key(int n, int nsplit) { return (long long)n * 64 + nsplit; }
+long long graph_key(int n, int len_bucket) { return (long long)n * (1LL << 32) + len_bucket; }
 
 }  // namespace
 
@@ -123,7 +123,7 @@ int q35b_engine_finalize(q35b_engine *e) {
         }
     }
     const long long B = e->max_batch, S = e->n_slots;
-    e->conv_slot = conv_dim * 3;
+    e->conv_slot = conv_dim * 3 * 2;  // history double-buffered by position parity
     e->state_slot = nv * kd * kd;
     e->kv_slot = (long long)e->max_seq * kv_dim;
     void *p;
@@ -152,10 +152,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     ALLOC(mh, 4 * B * c.n_ff);
     ALLOC(mh1, 4 * B * c.n_ff);
     ALLOC(logits, 4 * B * (long long)c.vocab);
-    long long maxsplit = 1;
-    while (maxsplit < (e->max_seq + ATT_SPLIT - 1) / ATT_SPLIT) maxsplit <<= 1;
-    ALLOC(part_acc, 4 * B * c.n_heads * maxsplit * ATT_HD);
-    ALLOC(part_ml, 4 * B * c.n_heads * maxsplit * 2);
+    ALLOC(scores, 4 * B * c.n_heads * (long long)e->max_seq);
     ALLOC(probe_buf, 4 * (long long)c.n_layers * B * h);
     long long maxcols = std::max(std::max(h, (long long)c.n_ff), std::max(vdim, q_dim));
     e->xq_ld = ((maxcols / 32 * 34 + maxcols / 256 * 292) + 15) & ~15LL;
@@ -214,9 +211,9 @@ long long q35b_engine_launches_per_step(q35b_engine *e) { return e ? e->launches
 
 // Launch the step for `n` sequences whose inputs are already in e->d_in.
 static int engine_run(q35b_engine *e, int n, int max_len, int use_graph, cudaStream_t st) {
-    const int nsplit = eng_attn_nsplit(max_len);
-    if (!use_graph) return eng_step_body(e, n, nsplit, st);
-    const long long key = graph_key(n, nsplit);
+    const int bucket = eng_len_bucket(max_len, e->max_seq);
+    if (!use_graph) return eng_step_body(e, n, bucket, st);
+    const long long key = graph_key(n, bucket);
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
         cudaStream_t cs;
@@ -224,7 +221,7 @@ static int engine_run(q35b_engine *e, int n, int max_len, int use_graph, cudaStr
         cudaGraph_t g = nullptr;
         int rc = (int)cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
         if (!rc) {
-            const int brc = eng_step_body(e, n, nsplit, cs);
+            const int brc = eng_step_body(e, n, bucket, cs);
             rc = (int)cudaStreamEndCapture(cs, &g);
             if (brc) rc = brc;
         }

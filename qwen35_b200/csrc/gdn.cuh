@@ -87,3 +87,125 @@ inline int gdn_launch(const GdnArgs &a, int nseq, cudaStream_t st) {
 }
 
 }  // namespace q35
+
+namespace q35 {
+
+// ---------------------------------------------------------------------------
+// Fused GDN layer core for the batched decode step: one CTA per (value head,
+// sequence), 128 threads, everything between the input projections and the
+// output projection of a GDN layer (src/engine.zig:1505-1667):
+//   causal conv k=4 + silu on this head's q / k / v channels
+//   l2norm(q) * 1/sqrt(kd), l2norm(k)            (norm sums in serial order)
+//   beta = sigmoid(b), gamma = exp(ssm_a * softplus(a + dt_bias))
+//   delta-rule state update (column j per thread, state in registers)
+//   gated RMSNorm(out, ssm_norm) * silu(z), quantized for ssm_out
+// The conv history is double-buffered by position parity: every CTA reads the
+// history of position p and the owner of a channel writes position p+1's, so
+// value heads that share a k head (nv > nk) never race on it.
+// ---------------------------------------------------------------------------
+struct GdnCoreArgs {
+    const float *qkv;   // raw projections, [n][conv_dim]
+    long long qkv_ld;
+    const float *z;     // gate projection, [n][nv*vd]
+    long long z_ld;
+    const float *ab;    // [n][2 nv]: alpha (a) then beta (b)
+    long long ab_ld;
+    const float *conv_w;  // [conv_dim][4]
+    float *hist;          // per slot: 2 x [conv_dim][3]
+    long long hist_slot;
+    const float *ssm_a, *dt_bias, *ssm_norm;
+    float *state;
+    long long state_slot;
+    const int *slots, *pos;
+    int nv, nk;
+    float eps, qscale;
+    int fam;              // activation family of ssm_out (32: quantize here)
+    uint8_t *xq;
+    long long xq_ld;
+    float *gout;          // f32 gated output when fam != 32
+    long long gout_ld;
+};
+
+__global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ GdnCoreArgs a) {
+    __shared__ float sq[GDN_KD], sk[GDN_KD], so[GDN_KD];
+    __shared__ float s_scal[4];
+    const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
+    const int kd = GDN_KD, kq = a.nk * kd, conv_dim = 2 * kq + a.nv * kd;
+    const int kh = h % a.nk;
+    const long long slot = a.slots[b];
+    const int p = a.pos[b];
+    const float *hin = a.hist + slot * a.hist_slot + (long long)(p & 1) * conv_dim * 3;
+    float *hout = a.hist + slot * a.hist_slot + (long long)((p + 1) & 1) * conv_dim * 3;
+    const float *raw = a.qkv + (long long)b * a.qkv_ld;
+
+    auto conv = [&](int ch, bool owner) {
+        const float *hh = hin + (long long)ch * 3;
+        const float *w = a.conv_w + (long long)ch * 4;
+        const float cur = raw[ch];
+        const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(hh[0], w[0]), __fmul_rn(hh[1], w[1])),
+                                            __fmul_rn(hh[2], w[2])),
+                                  __fmul_rn(cur, w[3]));
+        if (owner) {
+            float *ho = hout + (long long)ch * 3;
+            ho[0] = hh[1];
+            ho[1] = hh[2];
+            ho[2] = cur;
+        }
+        return silu_f(s);
+    };
+    const bool qk_owner = h < a.nk;
+    sq[j] = conv(kh * kd + j, qk_owner);
+    sk[j] = conv(kq + kh * kd + j, qk_owner);
+    const float vj = conv(2 * kq + h * kd + j, true);
+    __syncthreads();
+    if (j == 0) s_scal[0] = serial_sumsq(sq, kd);
+    if (j == 32) s_scal[1] = serial_sumsq(sk, kd);
+    if (j == 64) {
+        const float *ar = a.ab + (long long)b * a.ab_ld;
+        s_scal[2] = sigmoid_f(ar[a.nv + h]);
+        s_scal[3] = exp_f(__fmul_rn(a.ssm_a[h], softplus_f(__fadd_rn(ar[h], a.dt_bias[h]))));
+    }
+    __syncthreads();
+    const float iq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[0], 1e-6f)));
+    const float ik = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[1], 1e-6f)));
+    const float qj = __fmul_rn(__fmul_rn(sq[j], iq), a.qscale);
+    const float kj = __fmul_rn(sk[j], ik);
+    const float be = s_scal[2], g = s_scal[3];
+    __syncthreads();
+    sq[j] = qj;
+    sk[j] = kj;
+    float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
+    float col[GDN_KD];
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) col[i] = S[(long long)i * GDN_KD + j];
+    __syncthreads();
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) acc = __fadd_rn(acc, __fmul_rn(col[i], sk[i]));
+    const float km = __fmul_rn(acc, g);
+    const float d = __fmul_rn(__fsub_rn(vj, km), be);
+    float o = 0.0f;
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) {
+        const float nvv = __fadd_rn(__fmul_rn(col[i], g), __fmul_rn(sk[i], d));
+        col[i] = nvv;
+        o = __fadd_rn(o, __fmul_rn(nvv, sq[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
+    so[j] = o;
+    __syncthreads();
+    if (j == 0) s_scal[0] = serial_sumsq(so, kd);
+    __syncthreads();
+    const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s_scal[0], (float)kd), a.eps)));
+    float y = __fmul_rn(__fmul_rn(o, sc), a.ssm_norm[j]);
+    y = __fmul_rn(y, silu_f(a.z[(long long)b * a.z_ld + (long long)h * kd + j]));
+    if (a.fam == 32) {
+        const int w = j >> 5;
+        quant_q8_0_warp(y, a.xq + (long long)b * a.xq_ld + (long long)(h * (kd / 32) + w) * 34, j & 31);
+    } else {
+        a.gout[(long long)b * a.gout_ld + (long long)h * kd + j] = y;
+    }
+}
+
+}  // namespace q35
