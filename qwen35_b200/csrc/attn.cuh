@@ -251,6 +251,8 @@ Q35_DEV int attx_len(const AttnXArgs &a, int seq) {
 
 template <int G>
 __global__ void __launch_bounds__(ATTX_CHUNK) k_attx_scores(const __grid_constant__ AttnXArgs a) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ __align__(16) float s_q[G][ATT_HD];
     const int kvh = blockIdx.x, seq = blockIdx.y, t = blockIdx.z * ATTX_CHUNK + threadIdx.x;
     const int len = attx_len(a, seq);
@@ -284,6 +286,8 @@ __global__ void __launch_bounds__(ATTX_CHUNK) k_attx_scores(const __grid_constan
 }
 
 __global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ AttnXArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float s_p[];  // len probabilities
     __shared__ float s_red[2];
     const int h = blockIdx.x, seq = blockIdx.y, dc = blockIdx.z, j = threadIdx.x;
@@ -340,16 +344,16 @@ inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t s
     const int G = a.heads / a.kv_heads;
     if (max_len <= 0 || max_len > a.max_len) return (int)cudaErrorInvalidValue;
     const dim3 g1((unsigned)a.kv_heads, (unsigned)nseq, (unsigned)((max_len + ATTX_CHUNK - 1) / ATTX_CHUNK));
+    int rc = 0;
     switch (G) {
-    case 1: k_attx_scores<1><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
-    case 2: k_attx_scores<2><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
-    case 3: k_attx_scores<3><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
-    case 4: k_attx_scores<4><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
-    case 6: k_attx_scores<6><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
-    case 8: k_attx_scores<8><<<g1, ATTX_CHUNK, 0, st>>>(a); break;
+    case 1: rc = launch_k(k_attx_scores<1>, g1, dim3(ATTX_CHUNK), 0, st, a); break;
+    case 2: rc = launch_k(k_attx_scores<2>, g1, dim3(ATTX_CHUNK), 0, st, a); break;
+    case 3: rc = launch_k(k_attx_scores<3>, g1, dim3(ATTX_CHUNK), 0, st, a); break;
+    case 4: rc = launch_k(k_attx_scores<4>, g1, dim3(ATTX_CHUNK), 0, st, a); break;
+    case 6: rc = launch_k(k_attx_scores<6>, g1, dim3(ATTX_CHUNK), 0, st, a); break;
+    case 8: rc = launch_k(k_attx_scores<8>, g1, dim3(ATTX_CHUNK), 0, st, a); break;
     default: return (int)cudaErrorInvalidValue;
     }
-    int rc = (int)cudaGetLastError();
     if (rc) return rc;
     const size_t smem = (size_t)max_len * 4;
     if (smem > 48 * 1024) {
@@ -360,8 +364,8 @@ inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t s
             configured = smem;
         }
     }
-    k_attx_pv<<<dim3((unsigned)a.heads, (unsigned)nseq, ATT_HD / ATTX_DIMS), ATTX_DIMS, smem, st>>>(a);
-    return (int)cudaGetLastError();
+    return launch_k(k_attx_pv, dim3((unsigned)a.heads, (unsigned)nseq, ATT_HD / ATTX_DIMS), dim3(ATTX_DIMS), smem, st,
+                    a);
 }
 
 }  // namespace q35

@@ -10,6 +10,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define Q35_DEV __device__ __forceinline__
 
 namespace q35 {
@@ -188,6 +190,37 @@ Q35_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
 
 Q35_DEV void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch.  A kernel of the decode step calls
+// pdl_trigger() first (its successor may then be scheduled while it runs) and
+// pdl_wait() before its first access to memory an earlier kernel writes or
+// reads; both are no-ops when the launch did not opt in.
+// ---------------------------------------------------------------------------
+Q35_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+Q35_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launches issued while this is set (the engine's step body) opt in to
+// programmatic stream serialization; other launches are plain.
+inline bool &pdl_enabled() {
+    static thread_local bool on = false;
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

@@ -48,6 +48,8 @@ Q35_DEV void quantize_row_cta(F f, int cols, int fam, uint8_t *dst) {
 // rmsnorm(x_row, w) -> quantized activation (CTA per token)
 __global__ void __launch_bounds__(256) k_rmsnorm_quant(const float *x, const float *w, int cols, float eps, int fam,
                                                        uint8_t *xq, long long xq_ld, const int *active) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x;
     if (active && !active[t]) return;
     const float *xr = x + (long long)t * cols;
@@ -63,6 +65,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm_quant(const float *x, const flo
 // silu(g)*u -> quantized activation; grid (blocks, tokens), warp per block
 __global__ void __launch_bounds__(256) k_swiglu_quant(const float *g, const float *u, int cols, int fam, uint8_t *xq,
                                                       long long xq_ld) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const float *gr = g + (long long)t * cols, *ur = u + (long long)t * cols;
     const int lane = threadIdx.x & 31;
@@ -87,6 +91,8 @@ __global__ void __launch_bounds__(256) k_swiglu_quant(const float *g, const floa
 // plain f32 rows -> quantized activation; grid (blocks, tokens)
 __global__ void __launch_bounds__(256) k_quant_rows(const float *x, long long x_ld, int cols, int fam, uint8_t *xq,
                                                     long long xq_ld) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const float *xr = x + (long long)t * x_ld;
     const int lane = threadIdx.x & 31;
@@ -108,6 +114,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float *x, long long x_
 // token).  engine.zig:1658-1667: rmsnormRows(gout, ssm_norm) then mulSilu(z).
 __global__ void __launch_bounds__(256) k_gated_norm_quant(const float *g, const float *z, const float *w, int nv,
                                                           int vd, float eps, int fam, uint8_t *xq, long long xq_ld) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sc[64];
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cols = nv * vd;
@@ -153,6 +161,8 @@ __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const flo
                                                       float *gate, const float *qw, const float *kw, int heads,
                                                       int kv_heads, float eps, float base, const int *pos,
                                                       const int *slots, float *kpool, float *vpool, long long kv_slot) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float y[256];
     const int hi = blockIdx.x, t = blockIdx.y, j = threadIdx.x;
     const int hd = 256, q_dim = heads * hd, kv_dim = kv_heads * hd;
@@ -197,11 +207,15 @@ __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const flo
 }
 
 __global__ void k_pos_to_len(const int *pos, int *len, int n) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) len[i] = pos[i] + 1;
 }
 
 __global__ void k_copy_rows(float *dst, const float *src, long long n) {
+    pdl_trigger();
+    pdl_wait();
     Q35_GRID_STRIDE(i, n) dst[i] = src[i];
 }
 
@@ -286,9 +300,9 @@ inline long long weight_row_bytes(int tt, long long cols) {
 }
 
 inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cudaStream_t st) {
-    k_rmsnorm_quant<<<n, 256, 0, st>>>(e->x, w, e->c.hidden, e->c.rms_eps, fam, e->xq, e->xq_ld, nullptr);
     e->launches++;
-    return (int)cudaGetLastError();
+    return launch_k(k_rmsnorm_quant, dim3(n), dim3(256), 0, st, (const float *)e->x, w, e->c.hidden, e->c.rms_eps, fam,
+                    e->xq, e->xq_ld, (const int *)nullptr);
 }
 
 inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
@@ -332,13 +346,12 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
     g.xq_ld = e->xq_ld;
     g.gout = e->gout;
     g.gout_ld = vdim;
-    k_gdn_core<<<dim3(nv, n), GDN_KD, 0, st>>>(g);
     e->launches++;
-    Q35_TRY((int)cudaGetLastError());
+    Q35_TRY(launch_k(k_gdn_core, dim3(nv, n), dim3(GDN_KD), 0, st, g));
     if (fo != 32) {
-        k_quant_rows<<<dim3((vdim / 256 + 7) / 8, n), 256, 0, st>>>(e->gout, vdim, vdim, fo, e->xq, e->xq_ld);
         e->launches++;
-        Q35_TRY((int)cudaGetLastError());
+        Q35_TRY(launch_k(k_quant_rows, dim3((vdim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
+                         (long long)vdim, vdim, fo, e->xq, e->xq_ld));
     }
     return eng_gemv(e, n, {{W.ssm_out.w, e->x, W.ssm_out.rows, W.ssm_out.tt, c.hidden, GV_ADD}}, e->xq, vdim, st);
 }
@@ -366,11 +379,10 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
     float *kp = e->kpool + fi * (long long)e->n_slots * e->kv_slot;
     float *vp = e->vpool + fi * (long long)e->n_slots * e->kv_slot;
     const int *slots = e->d_in + e->max_batch, *pos = e->d_in + 2 * e->max_batch;
-    k_attn_prelude<<<dim3(heads + kvh, n), 256, 0, st>>>(e->qkv, e->kb, e->vb, e->q, e->gate, W.q_norm, W.k_norm, heads,
-                                                        kvh, c.rms_eps, c.rope_freq_base, pos, slots, kp, vp,
-                                                        e->kv_slot);
+    Q35_TRY(launch_k(k_attn_prelude, dim3(heads + kvh, n), dim3(256), 0, st, (const float *)e->qkv,
+                     (const float *)e->kb, (const float *)e->vb, e->q, e->gate, W.q_norm, W.k_norm, heads, kvh,
+                     c.rms_eps, c.rope_freq_base, pos, slots, kp, vp, e->kv_slot));
     e->launches++;
-    Q35_TRY((int)cudaGetLastError());
     const int fo = family_of(W.o);
     AttnXArgs a{};
     a.q = e->q;
@@ -395,9 +407,9 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
     Q35_TRY(attx_launch(a, n, max_len, st));
     e->launches += 2;
     if (fo != 32) {
-        k_quant_rows<<<dim3((q_dim / 256 + 7) / 8, n), 256, 0, st>>>(e->gout, q_dim, q_dim, fo, e->xq, e->xq_ld);
         e->launches++;
-        Q35_TRY((int)cudaGetLastError());
+        Q35_TRY(launch_k(k_quant_rows, dim3((q_dim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
+                         (long long)q_dim, q_dim, fo, e->xq, e->xq_ld));
     }
     return eng_gemv(e, n, {{W.o.w, e->x, W.o.rows, W.o.tt, c.hidden, GV_ADD}}, e->xq, q_dim, st);
 }
@@ -411,23 +423,29 @@ inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
                       {W.ffn_up.w, e->mh1, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}},
                      e->xq, c.hidden, st));
     const int fd = family_of(W.ffn_down);
-    k_swiglu_quant<<<dim3((c.n_ff / (fd == 32 ? 32 : 256) + 7) / 8, n), 256, 0, st>>>(e->mh, e->mh1, c.n_ff, fd, e->xq,
-                                                                                     e->xq_ld);
     e->launches++;
-    Q35_TRY((int)cudaGetLastError());
+    Q35_TRY(launch_k(k_swiglu_quant, dim3((c.n_ff / (fd == 32 ? 32 : 256) + 7) / 8, n), dim3(256), 0, st,
+                     (const float *)e->mh, (const float *)e->mh1, c.n_ff, fd, e->xq, e->xq_ld));
     return eng_gemv(e, n, {{W.ffn_down.w, e->x, W.ffn_down.rows, W.ffn_down.tt, c.hidden, GV_ADD}}, e->xq, c.n_ff, st);
 }
 
 // the whole step body (graph-capturable: every per-step value is in device memory)
+struct PdlScope {
+    bool prev;
+    PdlScope() : prev(pdl_enabled()) { pdl_enabled() = true; }
+    ~PdlScope() { pdl_enabled() = prev; }
+};
+
 inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
+    const PdlScope pdl_scope;
     const q35b_config &c = e->c;
     e->launches = 0;
     const int *tok = e->d_in;
-    k_embed_rows<<<dim3((c.hidden + 255) / 256, n), 256, 0, st>>>(
-        e->token_embd.tt, e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x, c.hidden);
-    k_pos_to_len<<<(n + 127) / 128, 128, 0, st>>>(e->d_in + 2 * e->max_batch, e->d_len, n);
+    Q35_TRY(launch_k(k_embed_rows, dim3((c.hidden + 255) / 256, n), dim3(256), 0, st, e->token_embd.tt,
+                     e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x, c.hidden));
+    Q35_TRY(launch_k(k_pos_to_len, dim3((n + 127) / 128), dim3(128), 0, st, (const int *)(e->d_in + 2 * e->max_batch),
+                     e->d_len, n));
     e->launches += 2;
-    Q35_TRY((int)cudaGetLastError());
     for (int li = 0; li < c.n_layers; li++) {
         if (is_full_layer(c, li))
             Q35_TRY(eng_layer_full(e, li, n, max_len, st));
@@ -435,17 +453,18 @@ inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
             Q35_TRY(eng_layer_gdn(e, li, n, st));
         Q35_TRY(eng_mlp(e, li, n, st));
         if (e->probe) {
-            k_copy_rows<<<ew_grid((long long)n * c.hidden), 256, 0, st>>>(
-                e->probe_buf + (long long)li * e->max_batch * c.hidden, e->x, (long long)n * c.hidden);
+            Q35_TRY(launch_k(k_copy_rows, dim3(ew_grid((long long)n * c.hidden)), dim3(256), 0, st,
+                             e->probe_buf + (long long)li * e->max_batch * c.hidden, (const float *)e->x,
+                             (long long)n * c.hidden));
             e->launches++;
         }
     }
     const Lin &H = e->output.w ? e->output : e->token_embd;
     Q35_TRY(eng_rmsnorm_quant(e, n, e->output_norm, family_of(H), st));
     Q35_TRY(eng_gemv(e, n, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, e->xq, c.hidden, st));
-    k_argmax<<<n, 1024, 0, st>>>(e->logits, c.vocab, c.vocab, e->d_next);
     e->launches++;
-    return (int)cudaGetLastError();
+    return launch_k(k_argmax, dim3(n), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab, c.vocab,
+                    e->d_next);
 }
 
 }  // namespace q35

@@ -191,6 +191,8 @@ __global__ void k_rope_setenv(int *d, int pos, float base) {
 // ---- argmax: first index of the strict maximum (elementwise.zig:395-405) -
 // one block per row of `n` values
 __global__ void __launch_bounds__(1024) k_argmax(const float *x, long long row_stride, int n, int *out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float *xr = x + (long long)blockIdx.x * row_stride;

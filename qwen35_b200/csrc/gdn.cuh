@@ -127,6 +127,8 @@ struct GdnCoreArgs {
 };
 
 __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ GdnCoreArgs a) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sq[GDN_KD], sk[GDN_KD], so[GDN_KD];
     __shared__ float s_scal[4];
     const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;

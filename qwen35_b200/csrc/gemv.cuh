@@ -319,6 +319,7 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
     const int stage_ld = a.stage_bytes + 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nstage; s++) {
             mbar_init(&full[s], 1);
@@ -369,6 +370,9 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
     }
 
     // ---------------- consumers ----------------
+    // The producer streams weights (never written during a step) without
+    // waiting; the activation and the outputs belong to earlier kernels.
+    pdl_wait();
     // 1. activation -> shared aligned layout
     const int ctid = threadIdx.x;
     const int cthreads = GV_WARPS * 32;
@@ -488,8 +492,7 @@ inline int gemv_launch_nt(GemvArgs &a, cudaStream_t st) {
     long long grid = (long long)gemv_sm_count() * occ;
     if (grid > a.total_tiles) grid = a.total_tiles;
     if (grid < 1) grid = 1;
-    k_gemv<NT, R><<<(unsigned)grid, GV_THREADS, smem, st>>>(a);
-    return (int)cudaGetLastError();
+    return launch_k(k_gemv<NT, R>, dim3((unsigned)grid), dim3(GV_THREADS), smem, st, a);
 }
 
 template <int NT>

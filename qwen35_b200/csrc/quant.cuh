@@ -149,6 +149,8 @@ __global__ void k_dequant_row(int tt, const uint8_t *__restrict__ row, float *__
 // rows gathered by token id: out[t*cols + i] = dequant(W[tokens[t]])[i]
 __global__ void k_embed_rows(int tt, const uint8_t *__restrict__ w, size_t row_bytes,
                              const int *__restrict__ tokens, float *__restrict__ out, int cols) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const uint8_t *row = w + (size_t)tokens[t] * row_bytes;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x)
