@@ -253,11 +253,34 @@ Q35_DEV float block_sum(float v, float *red) {
 }
 
 // Sum of squares in the CPU's serial order: ((x0*x0 + x1*x1) + x2*x2) + ...
-// (src/elementwise.zig:45-46).  One thread, one dependent add per element.
+// (src/elementwise.zig:45-46).  One thread, one dependent add per element;
+// `x` should be in shared memory (4-float reads keep the chain fed).
 Q35_DEV float serial_sumsq(const float *x, int n) {
     float s = 0.0f;
-    for (int i = 0; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+    int i = 0;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        for (; i + 4 <= n; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + i);
+            s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+            s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+            s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+            s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+        }
+    }
+    for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
     return s;
+}
+
+// The same serial sum for a row in global memory, by a whole CTA: the row is
+// copied into shared memory (`sm`, n floats, 16-byte aligned) in parallel,
+// then thread 0 runs the chain.  Every thread returns the sum.
+Q35_DEV float cta_serial_sumsq(const float *xg, int n, float *sm) {
+    __shared__ float res;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sm[i] = xg[i];
+    __syncthreads();
+    if (threadIdx.x == 0) res = serial_sumsq(sm, n);
+    __syncthreads();
+    return res;
 }
 
 // exp / log1p evaluated in double and rounded once to f32: within an ulp of

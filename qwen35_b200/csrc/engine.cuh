@@ -53,12 +53,10 @@ __global__ void __launch_bounds__(256) k_rmsnorm_quant(const float *x, const flo
     const int t = blockIdx.x;
     if (active && !active[t]) return;
     const float *xr = x + (long long)t * cols;
-    __shared__ float sss;
-    if (threadIdx.x == 0) sss = serial_sumsq(xr, cols);
-    __syncthreads();
-    const float ss = sss;
+    extern __shared__ __align__(16) float xs[];  // cols floats
+    const float ss = cta_serial_sumsq(xr, cols, xs);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
-    quantize_row_cta([&](int i) { return __fmul_rn(__fmul_rn(xr[i], scale), w[i]); }, cols, fam,
+    quantize_row_cta([&](int i) { return __fmul_rn(__fmul_rn(xs[i], scale), w[i]); }, cols, fam,
                      xq + (long long)t * xq_ld);
 }
 
@@ -108,49 +106,6 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float *x, long long x_
         for (int k = 0; k < 8; k++) v[k] = xr[b * 256 + lane * 8 + k];
         quant_q8_K_warp(v, dst + (size_t)b * 292, lane);
     }
-}
-
-// gated RMSNorm over nv heads of vd, times silu(z), then quantize (CTA per
-// token).  engine.zig:1658-1667: rmsnormRows(gout, ssm_norm) then mulSilu(z).
-__global__ void __launch_bounds__(256) k_gated_norm_quant(const float *g, const float *z, const float *w, int nv,
-                                                          int vd, float eps, int fam, uint8_t *xq, long long xq_ld) {
-    pdl_trigger();
-    pdl_wait();
-    __shared__ float sc[64];
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int cols = nv * vd;
-    const float *gr = g + (long long)t * cols, *zr = z + (long long)t * cols;
-    for (int h = warp; h < nv; h += 8) {
-        const float ss = serial_sumsq(gr + h * vd, vd);
-        if (lane == 0) sc[h] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)vd), eps)));
-    }
-    __syncthreads();
-    quantize_row_cta(
-        [&](int i) {
-            const int h = i / vd, j = i - h * vd;
-            const float y = __fmul_rn(__fmul_rn(gr[i], sc[h]), w[j]);
-            return __fmul_rn(y, silu_f(zr[i]));
-        },
-        cols, fam, xq + (long long)t * xq_ld);
-}
-
-// ---------------------------------------------------------------------------
-// GDN prelude: causal conv + silu (per-slot history), gamma/beta
-// ---------------------------------------------------------------------------
-__global__ void k_conv_batched(float *conv_pool, long long conv_slot, const int *slots, float *y, int n,
-                               const float *w) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
-    if (i >= n) return;
-    float *h = conv_pool + (long long)slots[t] * conv_slot + (long long)i * 3;
-    float *yp = y + (long long)t * n + i;
-    const float cur = *yp;
-    const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(h[0], w[i * 4]), __fmul_rn(h[1], w[i * 4 + 1])),
-                                        __fmul_rn(h[2], w[i * 4 + 2])),
-                              __fmul_rn(cur, w[i * 4 + 3]));
-    *yp = silu_f(s);
-    h[0] = h[1];
-    h[1] = h[2];
-    h[2] = cur;
 }
 
 // ---------------------------------------------------------------------------
@@ -301,7 +256,8 @@ inline long long weight_row_bytes(int tt, long long cols) {
 
 inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cudaStream_t st) {
     e->launches++;
-    return launch_k(k_rmsnorm_quant, dim3(n), dim3(256), 0, st, (const float *)e->x, w, e->c.hidden, e->c.rms_eps, fam,
+    return launch_k(k_rmsnorm_quant, dim3(n), dim3(256), (size_t)e->c.hidden * 4, st, (const float *)e->x, w,
+                    e->c.hidden, e->c.rms_eps, fam,
                     e->xq, e->xq_ld, (const int *)nullptr);
 }
 

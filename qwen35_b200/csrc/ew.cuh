@@ -69,12 +69,10 @@ template <int NT>
 __global__ void __launch_bounds__(NT) k_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
     const float *xr = x + (long long)blockIdx.x * n;
     float *orow = out + (long long)blockIdx.x * n;
-    __shared__ float sss;
-    if (threadIdx.x == 0) sss = serial_sumsq(xr, n);
-    __syncthreads();
-    const float ss = sss;
+    extern __shared__ __align__(16) float xs[];  // n floats
+    const float ss = cta_serial_sumsq(xr, n, xs);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-    for (int i = threadIdx.x; i < n; i += NT) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+    for (int i = threadIdx.x; i < n; i += NT) orow[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
 }
 
 // l2norm: inv = 1/sqrt(ss + eps); x *= inv  (elementwise.zig:104-110)
@@ -84,13 +82,11 @@ __global__ void __launch_bounds__(NT) k_l2norm(float *x, int offset, int rows, i
                                                float post_scale, int apply_scale) {
     const int r = blockIdx.x % rows, t = blockIdx.x / rows;
     float *xr = x + offset + (long long)t * row_stride + (long long)r * n;
-    __shared__ float sss;
-    if (threadIdx.x == 0) sss = serial_sumsq(xr, n);
-    __syncthreads();
-    const float ss = sss;
+    extern __shared__ __align__(16) float xs[];  // n floats
+    const float ss = cta_serial_sumsq(xr, n, xs);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
     for (int i = threadIdx.x; i < n; i += NT) {
-        float v = __fmul_rn(xr[i], inv);
+        float v = __fmul_rn(xs[i], inv);
         if (apply_scale) v = __fmul_rn(v, post_scale);
         xr[i] = v;
     }
