@@ -226,6 +226,17 @@ int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, c
                            float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq,
                            int cols, int tokens, void *stream);
 
+/* Decode attention that allocates nothing (no counterpart in the reference):
+ * q35_launch_attn_decode's arguments and result, computed split-KV with the
+ * partials in one fixed 4.2 MB device array per device instead of a
+ * caller buffer.  heads <= 64 (larger: cudaErrorInvalidValue, nothing
+ * launched).  The first call on a device looks the array up (make it before
+ * any stream capture).  Calls on one device share the array: calls that may
+ * overlap in time race on it, so order them on one stream or with events. */
+int q35b_attn_decode_noalloc(const float *d_q, const float *d_gate, const float *d_kcache, const float *d_vcache,
+                             float *d_gout, int slot, int heads, int gqa, int hd, int kv_dim, float scale,
+                             void *stream);
+
 /* ---- batched engine --------------------------------------------------- */
 typedef struct q35b_config {
     int n_layers, full_attention_interval, hidden, n_heads, n_kv_heads;

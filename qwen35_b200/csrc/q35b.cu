@@ -14,3 +14,4 @@
 #include "attn.cuh"
 #include "api.cuh"
 #include "engine_api.cuh"
+#include "noalloc.cuh"
