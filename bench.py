@@ -201,12 +201,9 @@ def time_e2e(run, steps, warmup, dist):
 
 
 def max_over_ranks(v, dist):
-    if not dist:
-        return v
-    import torch
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    """largest value over ranks (NCCL all-reduce on this rank's device)"""
+    from qwen35_b200.shard import max_over_ranks as mor
+    return mor(v, dist, "cuda")
 
 
 def gemv_roofline(run, reps=20):
@@ -237,8 +234,12 @@ def gemv_roofline(run, reps=20):
     torch.cuda.synchronize()
     ms = float(np.mean([a.elapsed_time(c) for a, c in ev]))
     algo = rows * (cols // e) * b + xq.numel() + rows * 4
-    return {"kernel": "k_gemv<1> (lm_head, %dx%d %s)" % (rows, cols, {8: "Q8_0", 20: "IQ4_NL", 12: "Q4_K",
-                                                                   13: "Q5_K", 14: "Q6_K"}[tt]),
+    # the library takes the lane-per-row kernel for 16-byte-aligned rows of
+    # these types, the block-splitting one otherwise
+    lpr = tt in (8, 20, 12, 13) and cols % 256 == 0 and w.data_ptr() % 16 == 0
+    kname = "k_gemv_lpr<1>" if lpr else "k_gemv<1>"
+    return {"kernel": "%s (lm_head, %dx%d %s)" % (kname, rows, cols, {8: "Q8_0", 20: "IQ4_NL", 12: "Q4_K",
+                                                                     13: "Q5_K", 14: "Q6_K"}[tt]),
             "bytes": algo, "ms": ms, "gbs": algo / (ms * 1e-3) / 1e9}
 
 

@@ -155,14 +155,14 @@ int q35_launch_set_int1(int *d, int v, void *stream) {
 // ---- norms (api.h:135, 168-176) ----
 int q35_launch_rmsnorm(float *d_out, const float *d_x, const float *d_w, int rows, int n, float eps, void *stream) {
     if (rows <= 0 || n <= 0) return 0;
-    if (n > 12288) return (int)cudaErrorInvalidValue;
+    if (n > 8192) return (int)cudaErrorInvalidValue;
     k_rmsnorm<256><<<rows, 256, (size_t)n * 4, S(stream)>>>(d_out, d_x, d_w, n, eps);
     return (int)cudaGetLastError();
 }
 int q35_launch_l2norm_strided(float *d_x, int row_offset, int rows, int n, float eps, int tokens, int row_stride,
                               void *stream) {
     if (rows <= 0 || n <= 0 || tokens <= 0) return 0;
-    if (n > 12288) return (int)cudaErrorInvalidValue;
+    if (n > 8192) return (int)cudaErrorInvalidValue;
     k_l2norm<128><<<rows * tokens, 128, (size_t)n * 4, S(stream)>>>(d_x, row_offset, rows, n, eps, row_stride, 1.0f, 0);
     return (int)cudaGetLastError();
 }
@@ -173,7 +173,7 @@ int q35_launch_l2norm(float *d_x, int rows, int n, float eps, void *stream) {
 int q35_launch_l2norm_qk_scale(float *d_x, int nk, int kd, int k_offset, float eps, float qscale, void *stream) {
     if (nk <= 0 || kd <= 0) return 0;
     if (k_offset < nk * kd) return (int)cudaErrorInvalidValue;
-    if (kd > 12288) return (int)cudaErrorInvalidValue;
+    if (kd > 8192) return (int)cudaErrorInvalidValue;
     k_l2norm<128><<<nk, 128, (size_t)kd * 4, S(stream)>>>(d_x, 0, nk, kd, eps, nk * kd, qscale, 1);
     k_l2norm<128><<<nk, 128, (size_t)kd * 4, S(stream)>>>(d_x, k_offset, nk, kd, eps, nk * kd, 1.0f, 0);
     return (int)cudaGetLastError();

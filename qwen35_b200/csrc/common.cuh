@@ -208,8 +208,16 @@ inline bool &pdl_enabled() {
     return on;
 }
 
+// kernels launched through launch_k by this host thread (the engine reports
+// the count of one step body)
+inline long long &launch_count() {
+    static thread_local long long n = 0;
+    return n;
+}
+
 template <typename... KArgs, typename... Args>
 inline int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+    launch_count()++;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;

@@ -244,7 +244,6 @@ inline bool is_full_layer(const q35b_config &c, int li) {
 // one GEMV launch over up to 4 matrices of the same family sharing `xq`
 inline int eng_gemv(q35b_engine *e, int n, std::initializer_list<GemvSegDesc> segs, const uint8_t *xq, int cols,
                     cudaStream_t st) {
-    e->launches += (n + GV_MAX_NT - 1) / GV_MAX_NT;
     return gemv_launch(segs.begin(), (int)segs.size(), xq, cols, n, st, e->xq_ld);
 }
 
@@ -255,10 +254,20 @@ inline long long weight_row_bytes(int tt, long long cols) {
 }
 
 inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cudaStream_t st) {
-    e->launches++;
     return launch_k(k_rmsnorm_quant, dim3(n), dim3(256), (size_t)e->c.hidden * 4, st, (const float *)e->x, w,
                     e->c.hidden, e->c.rms_eps, fam,
                     e->xq, e->xq_ld, (const int *)nullptr);
+}
+
+// rmsnorm(x) * w -> quantize -> GEMV: one launch where the lane-per-row GEMV
+// takes the matrices (it builds the activation itself), else two
+inline int eng_norm_gemv(q35b_engine *e, int n, const float *w, std::initializer_list<GemvSegDesc> segs,
+                         cudaStream_t st) {
+    const LprPrologue pro{LPR_PRO_NORM, e->x, nullptr, w, (long long)e->c.hidden, e->c.rms_eps};
+    const int rc = gemv_lpr_launch(segs.begin(), (int)segs.size(), nullptr, e->c.hidden, n, st, e->xq_ld, &pro);
+    if (rc != -1) return rc;
+    Q35_TRY(eng_rmsnorm_quant(e, n, w, geom_of(segs.begin()->ttype).family, st));
+    return eng_gemv(e, n, segs, e->xq, e->c.hidden, st);
 }
 
 inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
@@ -267,13 +276,12 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
     const int nv = c.gdn_n_heads, nk = c.gdn_num_k_heads, kd = c.gdn_head_dim;
     const int kq = nk * kd, vdim = nv * kd, conv_dim = 2 * kq + vdim;
     const int fam = family_of(W.qkv);
-    Q35_TRY(eng_rmsnorm_quant(e, n, W.attn_norm, fam, st));
-    Q35_TRY(eng_gemv(e, n,
-                     {{W.qkv.w, e->qkv, W.qkv.rows, W.qkv.tt, conv_dim, GV_STORE},
-                      {W.gate.w, e->z, W.gate.rows, W.gate.tt, vdim, GV_STORE},
-                      {W.alpha.w, e->ab, W.alpha.rows, W.alpha.tt, 2 * nv, GV_STORE},
-                      {W.beta.w, e->ab + nv, W.beta.rows, W.beta.tt, 2 * nv, GV_STORE}},
-                     e->xq, c.hidden, st));
+    Q35_TRY(eng_norm_gemv(e, n, W.attn_norm,
+                          {{W.qkv.w, e->qkv, W.qkv.rows, W.qkv.tt, conv_dim, GV_STORE},
+                           {W.gate.w, e->z, W.gate.rows, W.gate.tt, vdim, GV_STORE},
+                           {W.alpha.w, e->ab, W.alpha.rows, W.alpha.tt, 2 * nv, GV_STORE},
+                           {W.beta.w, e->ab + nv, W.beta.rows, W.beta.tt, 2 * nv, GV_STORE}},
+                          st));
     const int gi = e->gdn_idx[li];
     const int fo = family_of(W.ssm_out);
     GdnCoreArgs g{};
@@ -302,10 +310,8 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
     g.xq_ld = e->xq_ld;
     g.gout = e->gout;
     g.gout_ld = vdim;
-    e->launches++;
     Q35_TRY(launch_k(k_gdn_core, dim3(nv, n), dim3(GDN_KD), 0, st, g));
     if (fo != 32) {
-        e->launches++;
         Q35_TRY(launch_k(k_quant_rows, dim3((vdim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
                          (long long)vdim, vdim, fo, e->xq, e->xq_ld));
     }
@@ -325,12 +331,11 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
     const LayerW &W = e->L[li];
     const int heads = c.n_heads, kvh = c.n_kv_heads, hd = c.head_dim;
     const int q_dim = heads * hd, kv_dim = kvh * hd;
-    Q35_TRY(eng_rmsnorm_quant(e, n, W.attn_norm, family_of(W.q), st));
-    Q35_TRY(eng_gemv(e, n,
-                     {{W.q.w, e->qkv, W.q.rows, W.q.tt, 2 * q_dim, GV_STORE},
-                      {W.k.w, e->kb, W.k.rows, W.k.tt, kv_dim, GV_STORE},
-                      {W.v.w, e->vb, W.v.rows, W.v.tt, kv_dim, GV_STORE}},
-                     e->xq, c.hidden, st));
+    Q35_TRY(eng_norm_gemv(e, n, W.attn_norm,
+                          {{W.q.w, e->qkv, W.q.rows, W.q.tt, 2 * q_dim, GV_STORE},
+                           {W.k.w, e->kb, W.k.rows, W.k.tt, kv_dim, GV_STORE},
+                           {W.v.w, e->vb, W.v.rows, W.v.tt, kv_dim, GV_STORE}},
+                          st));
     const int fi = e->full_idx[li];
     float *kp = e->kpool + fi * (long long)e->n_slots * e->kv_slot;
     float *vp = e->vpool + fi * (long long)e->n_slots * e->kv_slot;
@@ -338,7 +343,6 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
     Q35_TRY(launch_k(k_attn_prelude, dim3(heads + kvh, n), dim3(256), 0, st, (const float *)e->qkv,
                      (const float *)e->kb, (const float *)e->vb, e->q, e->gate, W.q_norm, W.k_norm, heads, kvh,
                      c.rms_eps, c.rope_freq_base, pos, slots, kp, vp, e->kv_slot));
-    e->launches++;
     const int fo = family_of(W.o);
     AttnXArgs a{};
     a.q = e->q;
@@ -361,9 +365,7 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
     a.xq = e->xq;
     a.xq_ld = e->xq_ld;
     Q35_TRY(attx_launch(a, n, max_len, st));
-    e->launches += 2;
     if (fo != 32) {
-        e->launches++;
         Q35_TRY(launch_k(k_quant_rows, dim3((q_dim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
                          (long long)q_dim, q_dim, fo, e->xq, e->xq_ld));
     }
@@ -373,16 +375,18 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
 inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
     const q35b_config &c = e->c;
     const LayerW &W = e->L[li];
-    Q35_TRY(eng_rmsnorm_quant(e, n, W.post_norm, family_of(W.ffn_gate), st));
-    Q35_TRY(eng_gemv(e, n,
-                     {{W.ffn_gate.w, e->mh, W.ffn_gate.rows, W.ffn_gate.tt, c.n_ff, GV_STORE},
-                      {W.ffn_up.w, e->mh1, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}},
-                     e->xq, c.hidden, st));
+    Q35_TRY(eng_norm_gemv(e, n, W.post_norm,
+                          {{W.ffn_gate.w, e->mh, W.ffn_gate.rows, W.ffn_gate.tt, c.n_ff, GV_STORE},
+                           {W.ffn_up.w, e->mh1, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}},
+                          st));
     const int fd = family_of(W.ffn_down);
-    e->launches++;
+    const GemvSegDesc down{W.ffn_down.w, e->x, W.ffn_down.rows, W.ffn_down.tt, c.hidden, GV_ADD};
+    const LprPrologue pro{LPR_PRO_SWIGLU, e->mh, e->mh1, nullptr, (long long)c.n_ff, 0.0f};
+    const int rc = gemv_lpr_launch(&down, 1, nullptr, c.n_ff, n, st, e->xq_ld, &pro);
+    if (rc != -1) return rc;
     Q35_TRY(launch_k(k_swiglu_quant, dim3((c.n_ff / (fd == 32 ? 32 : 256) + 7) / 8, n), dim3(256), 0, st,
                      (const float *)e->mh, (const float *)e->mh1, c.n_ff, fd, e->xq, e->xq_ld));
-    return eng_gemv(e, n, {{W.ffn_down.w, e->x, W.ffn_down.rows, W.ffn_down.tt, c.hidden, GV_ADD}}, e->xq, c.n_ff, st);
+    return eng_gemv(e, n, {down}, e->xq, c.n_ff, st);
 }
 
 // the whole step body (graph-capturable: every per-step value is in device memory)
@@ -395,13 +399,12 @@ struct PdlScope {
 inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
     const PdlScope pdl_scope;
     const q35b_config &c = e->c;
-    e->launches = 0;
+    const long long l0 = launch_count();
     const int *tok = e->d_in;
     Q35_TRY(launch_k(k_embed_rows, dim3((c.hidden + 255) / 256, n), dim3(256), 0, st, e->token_embd.tt,
                      e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x, c.hidden));
     Q35_TRY(launch_k(k_pos_to_len, dim3((n + 127) / 128), dim3(128), 0, st, (const int *)(e->d_in + 2 * e->max_batch),
                      e->d_len, n));
-    e->launches += 2;
     for (int li = 0; li < c.n_layers; li++) {
         if (is_full_layer(c, li))
             Q35_TRY(eng_layer_full(e, li, n, max_len, st));
@@ -412,15 +415,14 @@ inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
             Q35_TRY(launch_k(k_copy_rows, dim3(ew_grid((long long)n * c.hidden)), dim3(256), 0, st,
                              e->probe_buf + (long long)li * e->max_batch * c.hidden, (const float *)e->x,
                              (long long)n * c.hidden));
-            e->launches++;
         }
     }
     const Lin &H = e->output.w ? e->output : e->token_embd;
-    Q35_TRY(eng_rmsnorm_quant(e, n, e->output_norm, family_of(H), st));
-    Q35_TRY(eng_gemv(e, n, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, e->xq, c.hidden, st));
-    e->launches++;
-    return launch_k(k_argmax, dim3(n), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab, c.vocab,
-                    e->d_next);
+    Q35_TRY(eng_norm_gemv(e, n, e->output_norm, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, st));
+    const int rc = launch_k(k_argmax, dim3(n), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab,
+                            c.vocab, e->d_next);
+    e->launches = launch_count() - l0;
+    return rc;
 }
 
 }  // namespace q35

@@ -502,10 +502,11 @@ inline int gemv_launch_r(GemvArgs &a, int R, cudaStream_t st) {
     return gemv_launch_nt<NT, 1>(a, st);
 }
 
-// Launch y = W x for up to GV_MAX_SEG matrices sharing one activation.
+// Launch y = W x for up to GV_MAX_SEG matrices sharing one activation with
+// the block-splitting kernel (any alignment, every type).
 // `xq` is the API-layout quantized activation (tokens rows of act_row_bytes).
-inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
-                       long long xq_ld = 0) {
+inline int gemv_launch_split(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                             long long xq_ld = 0) {
     if (nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || ntok <= 0) return (int)cudaErrorInvalidValue;
     const int fam = geom_of(segs[0].ttype).family;
     if (!fam) return (int)cudaErrorInvalidValue;

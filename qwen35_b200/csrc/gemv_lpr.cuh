@@ -1,0 +1,709 @@
+// gemv_lpr.cuh -- decode GEMV with one lane per weight row (sm_100a).
+//
+// A lane owns one row and walks its blocks in order, so the f32 fold
+// `sumf += term_b` runs in the reference scalar tier's order
+// (kernels32.c:462, kernels256.c:494,625) without any cross-lane exchange:
+// no fold scratch, no shuffles, no per-pass warp syncs.  Per 32-weight block a
+// lane spends ~20 instructions at one token.
+//
+// Data movement: a warp owns 32 consecutive rows (a "warp tile") and streams
+// them in column chunks of 256 / 512 columns.  Each lane issues the bulk copy
+// (cp.async.bulk, completing on the warp's mbarrier) of its own row's chunk
+// into a per-warp ring of NS stages; the destination row stride is an odd
+// multiple of 16 bytes, so the 128-bit shared loads of 32 lanes (32 rows at
+// the same column) hit distinct bank groups.  The warp refills a slot right
+// after it has consumed it; nothing else touches the ring, so only "full"
+// barriers exist.  Weight copies are issued before the programmatic-launch
+// wait, so they overlap the previous kernel's tail.
+//
+// Eligible: Q8_0 / IQ4_NL / Q4_K / Q5_K rows whose byte length and base are
+// multiples of 16 (cols % 256 == 0).  Anything else uses k_gemv.
+#pragma once
+#include "gemv.cuh"
+
+namespace q35 {
+
+constexpr int LPR_MAX_CW = 8;    // warps per CTA
+constexpr int LPR_MAX_NS = 16;   // ring stages per warp
+constexpr int LPR_MAX_NT = 8;    // tokens per pass
+// dynamic shared memory ceiling: the 227 KB opt-in limit less room for the
+// kernel's static shared variables
+constexpr size_t LPR_SMEM_MAX = 226 * 1024;
+
+struct LprSeg {
+    const uint8_t *w;
+    float *out;
+    long long rows;
+    long long out_ld;
+    long long tile_begin;   // first warp tile of this matrix
+    int ttype;
+    int row_bytes;
+    int chunk_bytes;        // bytes of one row's column chunk
+    int mode;
+};
+
+struct LprArgs {
+    LprSeg seg[GV_MAX_SEG];
+    int nseg;
+    long long total_tiles;  // warp tiles (32 rows) over all matrices
+    const uint8_t *xq;
+    long long act_row_bytes;
+    int ntok, cols, family, act_stride;
+    int chunk_cols, nchunk; // columns per chunk, chunks per row
+    int ns, rs;             // ring stages per warp, shared row stride (bytes)
+    int kw;                 // warps splitting one warp tile's columns (1: no split)
+    int tst;                // floats between lanes' term rows (odd), when kw > 1
+    int t_off;              // byte offset of the term buffers, when kw > 1
+    int act_off;            // byte offset of the activation in shared memory
+    int ring_off;           // byte offset of warp 0's ring
+    // prologue: build the quantized activation in shared memory from f32
+    // rows instead of reading `xq` (LPR_PRO_NORM: rmsnorm(px) * pw;
+    // LPR_PRO_SWIGLU: silu(px) * pu)
+    int prologue;
+    const float *px, *pu, *pw;
+    long long px_ld;
+    float eps;
+    int x_off;              // byte offset of the staged f32 rows (norm)
+};
+
+enum { LPR_PRO_NONE = 0, LPR_PRO_NORM = 1, LPR_PRO_SWIGLU = 2 };
+
+// The activation quantizers (quant_q8_0_warp / quant_q8_K_warp), writing the
+// GEMV's shared layout directly: int8 plane, f32 scale per block (for Q8_0
+// the f16-rounded scale the API layout would carry), int32 16-element sums.
+Q35_DEV void lpr_quant_q8_0(float v, uint8_t *at, int cols, int b, int lane) {
+    const float amax = warp_max(fabsf(v));
+    const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float inv = amax > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    if (lane == 0) reinterpret_cast<float *>(at + cols)[b] = f16_to_f32(f32_to_f16_bits(scale, 0x0380u));
+    const float x = __fmul_rn(v, inv);
+    int q = __float2int_rz(__fadd_rn(x, x >= 0.0f ? 0.5f : -0.5f));
+    q = q > 127 ? 127 : (q < -128 ? -128 : q);
+    reinterpret_cast<int8_t *>(at)[b * 32 + lane] = (int8_t)q;
+}
+Q35_DEV void lpr_quant_q8_K(const float (&v)[8], uint8_t *at, int cols, int b, int lane) {
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) a = fmaxf(a, fabsf(v[i]));
+    const float amax = warp_max(a);
+    const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float inv = amax > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    if (lane == 0) reinterpret_cast<float *>(at + cols)[b] = scale;
+    int s = 0;
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float r = roundf(__fmul_rn(v[i], inv));
+        if (r < -127.0f) r = -127.0f;
+        if (r > 127.0f) r = 127.0f;
+        if (!(r >= -127.0f)) r = 127.0f;
+        const int q = (int)r;
+        s += q;
+        if (i < 4)
+            w0 |= (uint32_t)(q & 0xFF) << (8 * i);
+        else
+            w1 |= (uint32_t)(q & 0xFF) << (8 * (i - 4));
+    }
+    uint32_t *qs = reinterpret_cast<uint32_t *>(at + b * 256 + lane * 8);
+    qs[0] = w0;
+    qs[1] = w1;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if ((lane & 1) == 0) reinterpret_cast<int *>(at + cols + (cols / 32) * 4)[b * 16 + (lane >> 1)] = s;
+}
+
+Q35_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+Q35_DEV float f16_lo(uint32_t w) { return f16_to_f32((uint16_t)(w & 0xFFFFu)); }
+Q35_DEV float f16_hi(uint32_t w) { return f16_to_f32((uint16_t)(w >> 16)); }
+
+// Eight IQ4_NL values from one word of packed nibbles: lo = codebook of the
+// four low nibbles (elements j..j+3), hi = of the four high nibbles
+// (elements j+16..j+19).  Byte permutes over the codebook split in halves;
+// bit 3 of each index then picks the half.
+Q35_DEV void iq4_word(uint32_t q, uint32_t &lo, uint32_t &hi) {
+    const uint32_t s = q & 0x77777777u;
+    const uint32_t l0 = __byte_perm(kIq4T0, kIq4T1, s), h0 = __byte_perm(kIq4T2, kIq4T3, s);
+    const uint32_t l1 = __byte_perm(kIq4T0, kIq4T1, s >> 16), h1 = __byte_perm(kIq4T2, kIq4T3, s >> 16);
+    // nibble n of q -> value n: choose the upper table half where bit 3 is set
+    const uint32_t v0 = __byte_perm(l0, h0, 0x3210u | ((q >> 1) & 0x4444u));
+    const uint32_t v1 = __byte_perm(l1, h1, 0x3210u | ((q >> 17) & 0x4444u));
+    // v0 = [lo b0, hi b0, lo b1, hi b1], v1 = [lo b2, hi b2, lo b3, hi b3]
+    lo = __byte_perm(v0, v1, 0x6420u);
+    hi = __byte_perm(v0, v1, 0x7531u);
+}
+
+// byte k of the 12 K-quant scale bytes held in words S[0..2]
+Q35_DEV int kq_byte(const uint32_t *S, int k) { return (int)((S[k >> 2] >> ((k & 3) * 8)) & 0xFFu); }
+Q35_DEV void kq_scale_min_w(int j, const uint32_t *S, int &sc, int &m) {
+    if (j < 4) {
+        sc = kq_byte(S, j) & 63;
+        m = kq_byte(S, j + 4) & 63;
+    } else {
+        sc = (kq_byte(S, j + 4) & 0xF) | ((kq_byte(S, j - 4) >> 6) << 4);
+        m = (kq_byte(S, j + 4) >> 4) | ((kq_byte(S, j) >> 6) << 4);
+    }
+}
+
+// ---- one lane, one row, one column chunk ---------------------------------
+// rp: the row's chunk in shared memory (16-byte aligned); gb0: global block
+// index of the chunk's first block.  Each block's f32 term goes to a sink:
+// FoldSink adds it to the lane's running sums (the whole row is this
+// lane's), TermSink stores it for the ordered fold after a K split.
+template <int NT>
+struct FoldSink {
+    float (&acc)[NT];
+    Q35_DEV void put(int t, int, float v) { acc[t] = __fadd_rn(acc[t], v); }
+};
+struct TermSink {
+    float *tl;     // this lane's term row (token 0)
+    int tok_ld;    // floats between tokens
+    Q35_DEV void put(int t, int b, float v) { tl[t * tok_ld + b] = v; }
+};
+
+template <int NT, class Sink>
+Q35_DEV void lpr_q8_0(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
+    for (int g = 0; g < nblk; g += 8) {  // 8 blocks = 272 bytes = 17 x 16
+        uint32_t W[68];
+        const uint4 *s = reinterpret_cast<const uint4 *>(rp + g * 34);
+#pragma unroll
+        for (int i = 0; i < 17; i++) {
+            const uint4 v = s[i];
+            W[4 * i] = v.x;
+            W[4 * i + 1] = v.y;
+            W[4 * i + 2] = v.z;
+            W[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int o = 34 * k, w0 = o >> 2;
+            uint32_t q[8];
+            float dx;
+            if ((o & 3) == 0) {  // d in the low half of W[w0], qs start 2 bytes in
+                dx = f16_lo(W[w0]);
+#pragma unroll
+                for (int i = 0; i < 8; i++) q[i] = __funnelshift_r(W[w0 + i], W[w0 + i + 1], 16);
+            } else {             // d in the high half, qs word-aligned
+                dx = f16_hi(W[w0]);
+#pragma unroll
+                for (int i = 0; i < 8; i++) q[i] = W[w0 + 1 + i];
+            }
+            const int b = gb0 + g + k;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < ntok) {
+                    int si = dot4x4(q[0], q[1], q[2], q[3], A.q16(t, b * 32), 0);
+                    si = dot4x4(q[4], q[5], q[6], q[7], A.q16(t, b * 32 + 16), si);
+                    // sumf += dx * dy * (float)sumi
+                    sk.put(t, b, __fmul_rn(__fmul_rn(dx, A.dsc(t, b)), __int2float_rn(si)));
+                }
+            }
+        }
+    }
+}
+
+template <int NT, class Sink>
+Q35_DEV void lpr_iq4_nl(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
+    for (int g = 0; g < nblk; g += 8) {  // 8 blocks = 144 bytes = 9 x 16
+        uint32_t W[36];
+        const uint4 *s = reinterpret_cast<const uint4 *>(rp + g * 18);
+#pragma unroll
+        for (int i = 0; i < 9; i++) {
+            const uint4 v = s[i];
+            W[4 * i] = v.x;
+            W[4 * i + 1] = v.y;
+            W[4 * i + 2] = v.z;
+            W[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int o = 18 * k, w0 = o >> 2;
+            uint32_t q[4];
+            float dx;
+            if ((o & 3) == 0) {
+                dx = f16_lo(W[w0]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(W[w0 + i], W[w0 + i + 1], 16);
+            } else {
+                dx = f16_hi(W[w0]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) q[i] = W[w0 + 1 + i];
+            }
+            uint32_t lo[4], hi[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) iq4_word(q[i], lo[i], hi[i]);
+            const int b = gb0 + g + k;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < ntok) {
+                    int si = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, b * 32), 0);
+                    si = dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, b * 32 + 16), si);
+                    sk.put(t, b, __fmul_rn(__fmul_rn(dx, A.dsc(t, b)), __int2float_rn(si)));
+                }
+            }
+        }
+    }
+}
+
+// Q4_K (144 B: d|dmin, 12 scale bytes, 128 qs) and Q5_K (176 B: d|dmin,
+// scales, 32 qh, 128 qs); both 16-byte multiples, so every block of the
+// chunk starts 16-byte aligned.
+template <int NT, bool Q5, class Sink>
+Q35_DEV void lpr_q45_k(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
+    constexpr int NW = Q5 ? 44 : 36;
+    for (int k = 0; k < nblk; k++) {
+        uint32_t W[NW];
+        const uint4 *s = reinterpret_cast<const uint4 *>(rp + k * NW * 4);
+#pragma unroll
+        for (int i = 0; i < NW / 4; i++) {
+            const uint4 v = s[i];
+            W[4 * i] = v.x;
+            W[4 * i + 1] = v.y;
+            W[4 * i + 2] = v.z;
+            W[4 * i + 3] = v.w;
+        }
+        const int b = gb0 + k;
+        int is[NT], ms[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) is[t] = 0, ms[t] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            int sc0, m0, sc1, m1;
+            kq_scale_min_w(2 * c, W + 1, sc0, m0);
+            kq_scale_min_w(2 * c + 1, W + 1, sc1, m1);
+            uint32_t lo[8], hi[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t ql = W[(Q5 ? 12 : 4) + 8 * c + i];
+                lo[i] = ql & 0x0F0F0F0Fu;
+                hi[i] = (ql >> 4) & 0x0F0F0F0Fu;
+                if (Q5) {
+                    const uint32_t qh = W[4 + i];
+                    lo[i] |= ((qh >> (2 * c)) & 0x01010101u) << 4;
+                    hi[i] |= ((qh >> (2 * c + 1)) & 0x01010101u) << 4;
+                }
+            }
+            const int e0 = b * 256 + 64 * c;
+            const int gq = b * 16 + 4 * c;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < ntok) {
+                    int dl = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, e0), 0);
+                    dl = dot4x4(lo[4], lo[5], lo[6], lo[7], A.q16(t, e0 + 16), dl);
+                    int dh = dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, e0 + 32), 0);
+                    dh = dot4x4(hi[4], hi[5], hi[6], hi[7], A.q16(t, e0 + 48), dh);
+                    is[t] += sc0 * dl + sc1 * dh;
+                    ms[t] += m0 * (A.bsum(t, gq) + A.bsum(t, gq + 1)) + m1 * (A.bsum(t, gq + 2) + A.bsum(t, gq + 3));
+                }
+            }
+        }
+        const float dw = f16_lo(W[0]), dmw = f16_hi(W[0]);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            if (t < ntok) {
+                // d = dy*d_w; dmin = dy*dmin_w; sumf += d*isum - dmin*sumi
+                const float dy = A.dsc(t, b);
+                const float d = __fmul_rn(dy, dw), dm = __fmul_rn(dy, dmw);
+                sk.put(t, b, __fsub_rn(__fmul_rn(d, __int2float_rn(is[t])), __fmul_rn(dm, __int2float_rn(ms[t]))));
+            }
+        }
+    }
+}
+
+Q35_DEV int lpr_find_seg(const LprArgs &a, long long tile) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < GV_MAX_SEG; i++)
+        if (i < a.nseg && tile >= a.seg[i].tile_begin) s = i;
+    return s;
+}
+
+template <int NT, class Sink>
+Q35_DEV void lpr_chunk(int tt, const uint8_t *rp, const ActView &A, int ntok, int c, int chunk_cols, Sink &sk) {
+    switch (tt) {
+    case TT_Q8_0: lpr_q8_0<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_IQ4_NL: lpr_iq4_nl<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_Q4_K: lpr_q45_k<NT, false>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
+    default: lpr_q45_k<NT, true>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
+    }
+}
+
+// CTA = rw row groups x kw column warps.  A row group owns a warp tile (32
+// rows) at a time; its kw warps take contiguous column-chunk ranges of it.
+// kw == 1: the lane folds its row in registers.  kw > 1: lanes store their
+// block terms, and after a named barrier warp 0 of the group folds each row's
+// terms in block order (the same rounding sequence).
+template <int NT>
+__global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_constant__ LprArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int cw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kw = a.kw, rg = warp / kw, kq = warp - rg * kw, rw = cw / kw;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem) + warp * LPR_MAX_NS;
+    uint8_t *act = smem + a.act_off;
+    uint8_t *ring = smem + a.ring_off + (size_t)warp * a.ns * 32 * a.rs;
+    float *terms = reinterpret_cast<float *>(smem + a.t_off) + (size_t)rg * NT * 32 * a.tst;
+    pdl_trigger();
+    if (lane == 0) {
+        for (int s = 0; s < a.ns; s++) mbar_init(&bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    const long long tstride = (long long)gridDim.x * rw;
+    const long long t0 = (long long)blockIdx.x * rw + rg;
+    const long long my_tiles = t0 < a.total_tiles ? (a.total_tiles - 1 - t0) / tstride + 1 : 0;
+    const int c_lo = kq * a.nchunk / kw, c_hi = (kq + 1) * a.nchunk / kw, nck = c_hi - c_lo;
+    const long long nst = my_tiles * nck;  // stages this warp consumes
+
+    // stage i of this warp -> (matrix, first row, chunk); lane `lane` copies its row
+    auto issue = [&](long long i) {
+        const long long tile = t0 + (i / nck) * tstride;
+        const int c = c_lo + (int)(i % nck);
+        const LprSeg &sg = a.seg[lpr_find_seg(a, tile)];
+        const long long r0 = (tile - sg.tile_begin) * 32;
+        const int nv = (int)min(32LL, sg.rows - r0);
+        const int slot = (int)(i % a.ns);
+        if (lane == 0) mbar_arrive_expect_tx(&bar[slot], (uint32_t)(nv * sg.chunk_bytes));
+        __syncwarp();
+        if (lane < nv)
+            bulk_g2s(ring + ((size_t)slot * 32 + lane) * a.rs,
+                     sg.w + (size_t)(r0 + lane) * sg.row_bytes + (size_t)c * sg.chunk_bytes, (uint32_t)sg.chunk_bytes,
+                     &bar[slot]);
+    };
+    long long issued = nst < a.ns ? nst : a.ns;
+    for (long long i = 0; i < issued; i++) issue(i);
+
+    // the activation belongs to the previous kernel
+    pdl_wait();
+    if (a.prologue != LPR_PRO_NONE) {
+        __shared__ float s_scale[LPR_MAX_NT];
+        const float *xs = reinterpret_cast<const float *>(smem + a.x_off);
+        if (a.prologue == LPR_PRO_NORM) {
+            // rmsnorm: x staged in shared memory, the sum of squares taken in
+            // the CPU's serial order, one thread per token (engine.zig:1507,
+            // elementwise.zig:43-57)
+            float4 *xd = reinterpret_cast<float4 *>(smem + a.x_off);
+            const int c4 = a.cols / 4;
+            for (int idx = threadIdx.x; idx < a.ntok * c4; idx += blockDim.x) {
+                const int t = idx / c4, j = idx - t * c4;
+                xd[idx] = reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j];
+            }
+            __syncthreads();
+            if ((int)threadIdx.x < a.ntok) {
+                const float ss = serial_sumsq(xs + (size_t)threadIdx.x * a.cols, a.cols);
+                s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
+            }
+            __syncthreads();
+        }
+        auto val = [&](int t, int i) -> float {
+            if (a.prologue == LPR_PRO_NORM)
+                return __fmul_rn(__fmul_rn(xs[(size_t)t * a.cols + i], s_scale[t]), a.pw[i]);
+            const long long o = (long long)t * a.px_ld + i;
+            return __fmul_rn(silu_f(a.px[o]), a.pu[o]);
+        };
+        if (a.family == 32) {
+            const int nb = a.cols / 32;
+            for (int bi = warp; bi < a.ntok * nb; bi += cw) {
+                const int t = bi / nb, b = bi - t * nb;
+                lpr_quant_q8_0(val(t, b * 32 + lane), act + (size_t)t * a.act_stride, a.cols, b, lane);
+            }
+        } else {
+            const int nb = a.cols / 256;
+            for (int bi = warp; bi < a.ntok * nb; bi += cw) {
+                const int t = bi / nb, b = bi - t * nb;
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[k] = val(t, b * 256 + lane * 8 + k);
+                lpr_quant_q8_K(v, act + (size_t)t * a.act_stride, a.cols, b, lane);
+            }
+        }
+    } else if (a.family == 32) {
+        const int nb = a.cols / 32;
+        for (int idx = threadIdx.x; idx < a.ntok * nb; idx += blockDim.x) {
+            const int t = idx / nb, b = idx - t * nb;
+            const uint8_t *src = a.xq + (size_t)t * a.act_row_bytes + (size_t)b * 34;
+            uint8_t *dst = act + (size_t)t * a.act_stride;
+            reinterpret_cast<float *>(dst + a.cols)[b] = f16_to_f32(ld_u16(src));
+            uint32_t *q = reinterpret_cast<uint32_t *>(dst + b * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                q[i] = (uint32_t)ld_u16(src + 2 + 4 * i) | ((uint32_t)ld_u16(src + 4 + 4 * i) << 16);
+        }
+    } else {
+        const int nb = a.cols / 256;
+        for (int idx = threadIdx.x; idx < a.ntok * nb * 17; idx += blockDim.x) {
+            const int part = idx % 17, tb = idx / 17, t = tb / nb, b = tb - t * nb;
+            const uint8_t *src = a.xq + (size_t)t * a.act_row_bytes + (size_t)b * 292;
+            uint8_t *dst = act + (size_t)t * a.act_stride;
+            if (part < 16) {
+                const uint32_t *s4 = reinterpret_cast<const uint32_t *>(src + 4 + part * 16);
+                uint32_t *d4 = reinterpret_cast<uint32_t *>(dst + b * 256 + part * 16);
+#pragma unroll
+                for (int i = 0; i < 4; i++) d4[i] = s4[i];
+            } else {
+                reinterpret_cast<float *>(dst + a.cols)[b] = *reinterpret_cast<const float *>(src);
+                int *bs = reinterpret_cast<int *>(dst + a.cols + (a.cols / 32) * 4) + b * 16;
+                const int16_t *sb = reinterpret_cast<const int16_t *>(src + 260);
+#pragma unroll
+                for (int g = 0; g < 16; g++) bs[g] = sb[g];
+            }
+        }
+    }
+    __syncthreads();
+
+    const ActView A{act, a.act_stride, a.cols};
+    const int nb = a.cols / geom_of(a.seg[0].ttype).elems;  // blocks per row
+    bool failed = false;
+    long long waited = 0;
+    long long i = 0;
+    for (long long ti = 0; ti < my_tiles; ti++) {
+        const long long tile = t0 + ti * tstride;
+        const LprSeg &sg = a.seg[lpr_find_seg(a, tile)];
+        const long long r0 = (tile - sg.tile_begin) * 32;
+        const int nv = (int)min(32LL, sg.rows - r0);
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+        for (int c = c_lo; c < c_hi; c++, i++) {
+            const int slot = (int)(i % a.ns);
+            if (!failed) {
+                if (mbar_wait(&bar[slot], (uint32_t)((i / a.ns) & 1), 111))
+                    waited = i + 1;
+                else
+                    failed = true;  // keep walking the loop: the named barriers below need every warp
+            }
+            if (!failed && lane < nv) {
+                const uint8_t *rp = ring + ((size_t)slot * 32 + lane) * a.rs;
+                if (kw == 1) {
+                    FoldSink<NT> sk{acc};
+                    lpr_chunk<NT>(sg.ttype, rp, A, a.ntok, c, a.chunk_cols, sk);
+                } else {
+                    TermSink sk{terms + (size_t)lane * a.tst, 32 * a.tst};
+                    lpr_chunk<NT>(sg.ttype, rp, A, a.ntok, c, a.chunk_cols, sk);
+                }
+            }
+            // every lane is done reading this slot before the bulk engine refills it
+            __syncwarp();
+            fence_proxy_async_smem();
+            if (!failed && issued < nst && issued == i + a.ns) issue(issued++);
+        }
+        if (kw > 1) {
+            named_bar_sync(1, kw * 32);  // the group's terms for this tile are stored (kw > 1: one group)
+            if (kq == 0 && !failed && lane < nv) {
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    if (t < a.ntok) {
+                        const float *tl = terms + ((size_t)t * 32 + lane) * a.tst;
+                        float s = 0.0f;
+#pragma unroll 8
+                        for (int b = 0; b < nb; b++) s = __fadd_rn(s, tl[b]);
+                        acc[t] = s;
+                    }
+                }
+            }
+            named_bar_sync(1, kw * 32);  // folded before the next tile's terms land
+        }
+        if (kq == 0 && !failed && lane < nv) {
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < a.ntok) {
+                    float *o = sg.out + r0 + lane + (long long)t * sg.out_ld;
+                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
+                }
+            }
+        }
+    }
+    if (failed) {
+        // give the copies still in flight into this warp's ring a bounded chance to land
+        for (long long k = waited + 1; k < issued; k++)
+            if (!mbar_wait(&bar[k % a.ns], (uint32_t)((k / a.ns) & 1), 112)) break;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <int NT>
+inline cudaError_t gemv_lpr_set_smem() {
+    return cudaFuncSetAttribute(k_gemv_lpr<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LPR_SMEM_MAX);
+}
+inline int gemv_lpr_prepare() {
+    static int done = 0;
+    if (done) return 0;
+    const cudaError_t es[] = {gemv_lpr_set_smem<1>(), gemv_lpr_set_smem<2>(), gemv_lpr_set_smem<4>(),
+                              gemv_lpr_set_smem<8>()};
+    for (cudaError_t e : es)
+        if (e != cudaSuccess) return (int)e;
+    done = 1;
+    return 0;
+}
+
+inline bool lpr_type_ok(int tt) { return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K; }
+
+// f32 rows the launch quantizes itself (see LprArgs::prologue)
+struct LprPrologue {
+    int kind;              // LPR_PRO_NORM or LPR_PRO_SWIGLU
+    const float *x, *u, *w;
+    long long ld;          // floats between tokens of x (and u)
+    float eps;
+};
+constexpr size_t LPR_NORM_STAGE_MAX = 48 * 1024;  // f32 rows staged for the serial norm sum
+
+// Try the lane-per-row kernel.  Returns -1 (nothing launched) when the
+// matrices or the shape are not eligible, else the launch status.
+#ifndef LPR_CHUNK_COLS
+#define LPR_CHUNK_COLS 256      // columns per streamed chunk
+#endif
+#ifndef LPR_TALL_OCC
+#define LPR_TALL_OCC 2          // CTAs per SM for tall matrices (4 row groups each)
+#endif
+#ifndef LPR_WARPS_PER_SM
+#define LPR_WARPS_PER_SM 8      // warps per SM aimed at for short matrices (columns split)
+#endif
+
+inline int lpr_tmpl_nt(int nt) { return nt == 1 ? 1 : (nt == 2 ? 2 : (nt <= 4 ? 4 : 8)); }
+
+inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                           long long xq_ld, const LprPrologue *pro = nullptr) {
+    if (nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || ntok <= 0 || cols % 256 != 0) return -1;
+    if (pro) {
+        if (pro->kind != LPR_PRO_NORM && pro->kind != LPR_PRO_SWIGLU) return -1;
+        if ((reinterpret_cast<uintptr_t>(pro->x) & 15u) || (pro->ld & 3)) return -1;
+    }
+    const int fam = geom_of(segs[0].ttype).family;
+    const int chunk_cols = cols % LPR_CHUNK_COLS == 0 ? LPR_CHUNK_COLS : 256;
+    int rs = 0;
+    long long T = 0;
+    for (int i = 0; i < nseg; i++) {
+        const Geom g = geom_of(segs[i].ttype);
+        if (!lpr_type_ok(segs[i].ttype) || g.family != fam) return -1;
+        const int rb = cols / g.elems * g.bytes;
+        if (rb % 16 != 0 || (reinterpret_cast<uintptr_t>(segs[i].w) & 15u) != 0) return -1;
+        int cb = chunk_cols / g.elems * g.bytes;
+        if ((cb / 16) % 2 == 0) cb += 16;  // odd multiple of 16: conflict-free 128-bit loads
+        rs = cb > rs ? cb : rs;
+        T += (segs[i].rows + 31) / 32;
+    }
+    if (!pro && fam == 256 && (reinterpret_cast<uintptr_t>(xq) & 3u) != 0) return -1;
+    const long long act_row_bytes =
+        xq_ld > 0 ? xq_ld : (fam == 32 ? (long long)(cols / 32) * 34 : (long long)(cols / 256) * 292);
+    if (!pro && fam == 256 && (act_row_bytes & 3)) return -1;
+    if (T == 0) return 0;
+    Q35_TRY_RC(gemv_lpr_prepare());
+    const int nsm = gemv_sm_count();
+    const int nchunk = cols / chunk_cols;
+    const int nb = cols / (fam == 32 ? 32 : 256);
+    const int tst = nb % 2 == 0 ? nb + 1 : nb;
+    const int act_stride = gemv_act_stride(cols, fam);
+
+    // launch geometry: tall matrices keep a whole row per lane (kw = 1, four
+    // row groups per CTA); short ones split each warp tile's columns over kw
+    // warps so that ~LPR_WARPS_PER_SM warps per SM stream the matrix
+    int kw = 1, rw = 4, occ = LPR_TALL_OCC;
+    long long ctas;
+    if (T >= (long long)nsm * LPR_TALL_OCC * 4) {
+        ctas = (T + 3) / 4;
+    } else {
+        rw = 1;
+        const long long want = (long long)nsm * LPR_WARPS_PER_SM / T;
+        while (kw * 2 <= want && kw * 2 <= LPR_MAX_CW && kw * 2 <= nchunk) kw *= 2;
+        ctas = T;
+        occ = (int)((ctas + nsm - 1) / nsm);
+    }
+    occ = occ < 1 ? 1 : (occ > 8 ? 8 : occ);
+    const int cw = rw * kw;
+    size_t budget = occ == 1 ? LPR_SMEM_MAX : (228 * 1024) / occ - 2048;
+    const bool stage_x = pro && pro->kind == LPR_PRO_NORM;
+    auto xbytes = [&](int nt) { return stage_x ? (((size_t)nt * cols * 4 + 127) & ~size_t(127)) : 0; };
+    auto tbytes = [&](int nt) { return kw > 1 ? (size_t)rw * lpr_tmpl_nt(nt) * 32 * tst * 4 : 0; };
+    auto base_of = [&](int nt) {  // barriers | activation | staged rows | terms
+        return (size_t)(LPR_MAX_CW * LPR_MAX_NS * 8) + (((size_t)nt * act_stride + 127) & ~size_t(127)) + xbytes(nt) +
+               ((tbytes(nt) + 127) & ~size_t(127));
+    };
+    // tokens per pass: at most LPR_MAX_NT, with room for a 2-stage ring
+    int group = LPR_MAX_NT;
+    if (stage_x)
+        while (group > 1 && (size_t)group * cols * 4 > LPR_NORM_STAGE_MAX) group >>= 1;
+    if (stage_x && (size_t)group * cols * 4 > LPR_NORM_STAGE_MAX) return -1;
+    while (group > 1 && base_of(group) + (size_t)cw * 2 * 32 * rs > budget) group >>= 1;
+    if (base_of(group) + (size_t)cw * 32 * rs > budget) budget = LPR_SMEM_MAX;  // fewer CTAs per SM
+    if (base_of(group) + (size_t)cw * 32 * rs > budget) return -1;
+    const long long grid = ctas < (long long)nsm * occ ? ctas : (long long)nsm * occ;
+    for (int t0 = 0; t0 < ntok; t0 += group) {
+        const int nt = ntok - t0 < group ? ntok - t0 : group;
+        LprArgs a{};
+        a.nseg = nseg;
+        a.xq = reinterpret_cast<const uint8_t *>(xq) + (size_t)t0 * act_row_bytes;
+        a.act_row_bytes = act_row_bytes;
+        a.ntok = nt;
+        a.cols = cols;
+        a.family = fam;
+        a.act_stride = act_stride;
+        a.chunk_cols = chunk_cols;
+        a.nchunk = nchunk;
+        a.rs = rs;
+        a.kw = kw;
+        a.tst = tst;
+        a.act_off = LPR_MAX_CW * LPR_MAX_NS * 8;
+        a.x_off = (int)(a.act_off + (((size_t)nt * act_stride + 127) & ~size_t(127)));
+        a.t_off = (int)(a.x_off + xbytes(nt));
+        a.ring_off = (int)base_of(nt);
+        if (pro) {
+            a.prologue = pro->kind;
+            a.px = pro->x + (size_t)t0 * pro->ld;
+            a.pu = pro->u ? pro->u + (size_t)t0 * pro->ld : nullptr;
+            a.pw = pro->w;
+            a.px_ld = pro->ld;
+            a.eps = pro->eps;
+        }
+        long long tiles = 0;
+        for (int i = 0; i < nseg; i++) {
+            const Geom g = geom_of(segs[i].ttype);
+            LprSeg &s = a.seg[i];
+            s.w = reinterpret_cast<const uint8_t *>(segs[i].w);
+            s.rows = segs[i].rows;
+            s.ttype = segs[i].ttype;
+            s.row_bytes = cols / g.elems * g.bytes;
+            s.chunk_bytes = chunk_cols / g.elems * g.bytes;
+            s.out = segs[i].out + (size_t)t0 * segs[i].out_ld;
+            s.out_ld = segs[i].out_ld;
+            s.mode = segs[i].mode;
+            s.tile_begin = tiles;
+            tiles += (s.rows + 31) / 32;
+        }
+        a.total_tiles = tiles;
+        const size_t base = base_of(nt);
+        long long ns = base < budget ? (long long)((budget - base) / ((size_t)cw * 32 * rs)) : 0;
+        // no more stages than the busiest warp consumes
+        const long long per_warp = ((tiles + grid * rw - 1) / (grid * rw)) * ((nchunk + kw - 1) / kw);
+        if (ns > per_warp) ns = per_warp;
+        if (ns > LPR_MAX_NS) ns = LPR_MAX_NS;
+        if (ns < 1) ns = 1;
+        a.ns = (int)ns;
+        const size_t smem = base + (size_t)cw * ns * 32 * rs;
+        if (smem > LPR_SMEM_MAX) return (int)cudaErrorInvalidValue;
+        int rc;
+        const dim3 gd((unsigned)grid), bd((unsigned)(cw * 32));
+        if (nt == 1)
+            rc = launch_k(k_gemv_lpr<1>, gd, bd, smem, st, a);
+        else if (nt == 2)
+            rc = launch_k(k_gemv_lpr<2>, gd, bd, smem, st, a);
+        else if (nt <= 4)
+            rc = launch_k(k_gemv_lpr<4>, gd, bd, smem, st, a);
+        else
+            rc = launch_k(k_gemv_lpr<8>, gd, bd, smem, st, a);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+// y = W x for up to GV_MAX_SEG matrices sharing one activation: the
+// lane-per-row kernel where the matrices allow it, else the block-splitting
+// kernel.  Validation (types, families, alignment) is the latter's.
+inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                       long long xq_ld = 0) {
+    const int rc = gemv_lpr_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
+    if (rc != -1) return rc;
+    return gemv_launch_split(segs, nseg, xq, cols, ntok, st, xq_ld);
+}
+
+}  // namespace q35

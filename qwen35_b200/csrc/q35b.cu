@@ -9,6 +9,7 @@
 #include "common.cuh"
 #include "quant.cuh"
 #include "gemv.cuh"
+#include "gemv_lpr.cuh"
 #include "ew.cuh"
 #include "gdn.cuh"
 #include "attn.cuh"

@@ -139,7 +139,13 @@ def _gemv_case(L, O, name, rows, cols, tokens, seed):
 @pytest.mark.parametrize("tokens", [1, 3, 8, 13])
 def test_gemv_bit_exact(L, O, name, tokens):
     """out[t*rows+r] == the reference scalar tier's strict block-order fold"""
-    for rows, cols in [(300, 1024), (64, 3584), (129, 2048)]:
+    # lane-per-row kernel: columns split over 8, 4, 2 and 1 warps, and tall
+    # matrices (4 row groups per CTA);
+    # cols % 256 != 0 takes the block-splitting kernel
+    shapes = [(300, 1024), (64, 3584), (129, 2048), (10000, 512), (19000, 256), (40000, 256)]
+    if GEOM[TT[name]][0] == 32:
+        shapes.append((77, 2080))
+    for rows, cols in shapes:
         got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + tokens)
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
     assert_no_kernel_error(L)
@@ -164,10 +170,11 @@ def test_gemv_golden_rows(L, O):
         assert rel.max() < 5e-2, (name, rel.max())
 
 
-def test_gemv_unaligned_weight_base(L, O):
+@pytest.mark.parametrize("name", TYPES)
+def test_gemv_unaligned_weight_base(L, O, name):
     """a matrix starting 2 bytes past a 16-byte boundary (GGUF blocks are only
     2-byte aligned) is streamed correctly, head/tail bytes included"""
-    tt = TT["Q6_K"]
+    tt = TT[name]
     rng = np.random.default_rng(9)
     rows, cols = 37, 768
     w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
