@@ -215,15 +215,27 @@ namespace q35 {
 // 349-372): score_t = (sum_j q_j k_tj) * scale with j ascending; softmax as
 // max, e_t = exp(score_t - max), serial sum over t, e_t / sum; out_j =
 // sum_t p_t v_tj with t ascending; out_j *= sigmoid(gate_j).
-// Kernel 1 (scores): CTA (kv head, sequence, 128-position chunk), a lane per
-// position computing the gqa heads' serial dots.
+// Kernel 1 (scores): CTA (kv head, sequence, 32-position chunk), one warp;
+// the chunk's K rows are copied to shared memory with cp.async (every copy
+// in flight at once), then a lane per position computes the gqa heads'
+// serial dots from there.
 // Kernel 2 (softmax + P.V): CTA (q head, sequence, 64-dim chunk); every CTA
 // of a head recomputes the (cheap) softmax, then thread j walks t in order
-// for its dim.  Parallelism comes from dims, not positions, so no split
-// re-associates a sum.
+// for its dim over V tiles double-buffered in shared memory by cp.async.
+// Parallelism comes from dims, not positions, so no split re-associates a
+// sum.
 // ---------------------------------------------------------------------------
-constexpr int ATTX_CHUNK = 128;
+constexpr int ATTX_CHUNK = 32;             // positions per score CTA
+constexpr int ATTX_KLD = ATT_HD + 4;       // shared K row stride (floats): 1040 B, an odd multiple of 16
 constexpr int ATTX_DIMS = 64;
+constexpr int ATTX_VT = 128;               // positions per V tile
+
+Q35_DEV void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+Q35_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+Q35_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 struct AttnXArgs {
     const float *q, *gate;
@@ -254,20 +266,29 @@ __global__ void __launch_bounds__(ATTX_CHUNK) k_attx_scores(const __grid_constan
     pdl_trigger();
     pdl_wait();
     __shared__ __align__(16) float s_q[G][ATT_HD];
-    const int kvh = blockIdx.x, seq = blockIdx.y, t = blockIdx.z * ATTX_CHUNK + threadIdx.x;
+    __shared__ __align__(16) float s_k[ATTX_CHUNK][ATTX_KLD];
+    const int kvh = blockIdx.x, seq = blockIdx.y, p0 = blockIdx.z * ATTX_CHUNK, lane = threadIdx.x;
     const int len = attx_len(a, seq);
-    if (blockIdx.z * ATTX_CHUNK >= len) return;
-    for (int i = threadIdx.x; i < G * ATT_HD; i += ATTX_CHUNK) {
+    if (p0 >= len) return;
+    const int np = min(ATTX_CHUNK, len - p0);
+    const long long slot = a.slots ? a.slots[seq] : seq;
+    const float *kb = a.kc + slot * a.kv_slot + (long long)p0 * a.kv_dim + kvh * ATT_HD;
+    for (int idx = lane; idx < np * (ATT_HD / 4); idx += ATTX_CHUNK) {
+        const int r = idx / (ATT_HD / 4), c = idx - r * (ATT_HD / 4);
+        cp_async16(&s_k[r][c * 4], kb + (long long)r * a.kv_dim + c * 4);
+    }
+    cp_async_commit();
+    for (int i = lane; i < G * ATT_HD; i += ATTX_CHUNK) {
         const int g = i / ATT_HD, j = i - g * ATT_HD;
         s_q[g][j] = a.q[(long long)seq * a.q_tok + (long long)(kvh * G + g) * ATT_HD + j];
     }
+    cp_async_wait<0>();
     __syncthreads();
-    if (t >= len) return;
-    const long long slot = a.slots ? a.slots[seq] : seq;
-    const float4 *kr = reinterpret_cast<const float4 *>(a.kc + slot * a.kv_slot + (long long)t * a.kv_dim + kvh * ATT_HD);
+    if (lane >= np) return;
     float s[G];
 #pragma unroll
     for (int g = 0; g < G; g++) s[g] = 0.0f;
+    const float4 *kr = reinterpret_cast<const float4 *>(s_k[lane]);
 #pragma unroll 4
     for (int c = 0; c < ATT_HD / 4; c++) {
         const float4 kv = kr[c];
@@ -282,17 +303,35 @@ __global__ void __launch_bounds__(ATTX_CHUNK) k_attx_scores(const __grid_constan
     }
 #pragma unroll
     for (int g = 0; g < G; g++)
-        a.scores[((long long)seq * a.heads + kvh * G + g) * a.max_len + t] = __fmul_rn(s[g], a.scale);
+        a.scores[((long long)seq * a.heads + kvh * G + g) * a.max_len + p0 + lane] = __fmul_rn(s[g], a.scale);
 }
 
+// dynamic shared memory: 2 V tiles [ATTX_VT][ATTX_DIMS] then the len probabilities
 __global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ AttnXArgs a) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float s_p[];  // len probabilities
+    extern __shared__ __align__(16) float s_dyn[];
+    float *s_v = s_dyn;                                  // [2][ATTX_VT][ATTX_DIMS]
+    float *s_p = s_dyn + 2 * ATTX_VT * ATTX_DIMS;        // [len]
     __shared__ float s_red[2];
     const int h = blockIdx.x, seq = blockIdx.y, dc = blockIdx.z, j = threadIdx.x;
     const int len = attx_len(a, seq);
     const int gqa = a.heads / a.kv_heads, kvh = h / gqa;
+    const long long slot = a.slots ? a.slots[seq] : seq;
+    const float *vb = a.vc + slot * a.kv_slot + kvh * ATT_HD + dc * ATTX_DIMS;
+    const int ntile = (len + ATTX_VT - 1) / ATTX_VT;
+    // V tile k -> buffer k & 1: rows of 64 floats (16 x 16 B pieces)
+    auto load_tile = [&](int k) {
+        const int t0 = k * ATTX_VT, nt = min(ATTX_VT, len - t0);
+        float *dst = s_v + (size_t)(k & 1) * ATTX_VT * ATTX_DIMS;
+        for (int idx = j; idx < nt * (ATTX_DIMS / 4); idx += ATTX_DIMS) {
+            const int r = idx / (ATTX_DIMS / 4), c = idx - r * (ATTX_DIMS / 4);
+            cp_async16(dst + r * ATTX_DIMS + c * 4, vb + (long long)(t0 + r) * a.kv_dim + c * 4);
+        }
+        cp_async_commit();
+    };
+    if (ntile > 0) load_tile(0);  // in flight during the softmax
+
     const float *sc = a.scores + ((long long)seq * a.heads + h) * a.max_len;
     float m = -3.40282347e38f;
     for (int t = j; t < len; t += ATTX_DIMS) {
@@ -314,20 +353,22 @@ __global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ A
     __syncthreads();
     const float sum = s_red[0];
     for (int t = j; t < len; t += ATTX_DIMS) s_p[t] = __fdiv_rn(s_p[t], sum);
-    __syncthreads();
-    const long long slot = a.slots ? a.slots[seq] : seq;
-    const float *vb = a.vc + slot * a.kv_slot + kvh * ATT_HD + dc * ATTX_DIMS + j;
+
     float acc = 0.0f;
-    int t = 0;
-    for (; t + 4 <= len; t += 4) {
-        const float v0 = vb[(long long)t * a.kv_dim], v1 = vb[(long long)(t + 1) * a.kv_dim];
-        const float v2 = vb[(long long)(t + 2) * a.kv_dim], v3 = vb[(long long)(t + 3) * a.kv_dim];
-        acc = __fadd_rn(acc, __fmul_rn(s_p[t], v0));
-        acc = __fadd_rn(acc, __fmul_rn(s_p[t + 1], v1));
-        acc = __fadd_rn(acc, __fmul_rn(s_p[t + 2], v2));
-        acc = __fadd_rn(acc, __fmul_rn(s_p[t + 3], v3));
+    for (int k = 0; k < ntile; k++) {
+        if (k + 1 < ntile) {
+            load_tile(k + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();  // tile k (and, first time round, every s_p) visible to all
+        const float *v = s_v + (size_t)(k & 1) * ATTX_VT * ATTX_DIMS + j;
+        const int t0 = k * ATTX_VT, nt = min(ATTX_VT, len - t0);
+#pragma unroll 8
+        for (int r = 0; r < nt; r++) acc = __fadd_rn(acc, __fmul_rn(s_p[t0 + r], v[r * ATTX_DIMS]));
+        __syncthreads();  // done with buffer k & 1 before tile k + 2 lands in it
     }
-    for (; t < len; t++) acc = __fadd_rn(acc, __fmul_rn(s_p[t], vb[(long long)t * a.kv_dim]));
     const int dim = dc * ATTX_DIMS + j;
     const float gt = a.gate[(long long)seq * a.q_tok + (long long)h * ATT_HD + dim];
     const float o = __fmul_rn(acc, sigmoid_f(gt));
@@ -336,6 +377,21 @@ __global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ A
         const int blk = (h * ATT_HD + dc * ATTX_DIMS) / 32 + (j >> 5);
         quant_q8_0_warp(o, a.xq + (long long)seq * a.xq_ld + (long long)blk * 34, j & 31);
     }
+}
+
+inline size_t attx_pv_smem(int max_len) { return (size_t)(2 * ATTX_VT * ATTX_DIMS + max_len) * 4; }
+
+// raise k_attx_pv's dynamic shared-memory ceiling to cover contexts up to
+// max_len (a high-water mark; the engine calls this before any capture)
+inline int attx_prepare(int max_len) {
+    static size_t configured = 48 * 1024;
+    const size_t smem = attx_pv_smem(max_len);
+    if (smem <= configured) return 0;
+    if (smem > 227 * 1024 - 256) return (int)cudaErrorInvalidValue;
+    const int rc = (int)cudaFuncSetAttribute(k_attx_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (rc) return rc;
+    configured = smem;
+    return 0;
 }
 
 inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t st) {
@@ -355,15 +411,9 @@ inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t s
     default: return (int)cudaErrorInvalidValue;
     }
     if (rc) return rc;
-    const size_t smem = (size_t)max_len * 4;
-    if (smem > 48 * 1024) {
-        static size_t configured = 0;
-        if (smem > configured) {
-            rc = (int)cudaFuncSetAttribute(k_attx_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (rc) return rc;
-            configured = smem;
-        }
-    }
+    const size_t smem = attx_pv_smem(max_len);
+    if (smem > 227 * 1024 - 256) return (int)cudaErrorInvalidValue;
+    Q35_TRY_RC(attx_prepare(max_len));
     return launch_k(k_attx_pv, dim3((unsigned)a.heads, (unsigned)nseq, ATT_HD / ATTX_DIMS), dim3(ATTX_DIMS), smem, st,
                     a);
 }

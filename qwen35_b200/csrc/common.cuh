@@ -266,13 +266,27 @@ Q35_DEV float block_sum(float v, float *red) {
 Q35_DEV float serial_sumsq(const float *x, int n) {
     float s = 0.0f;
     int i = 0;
-    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
-        for (; i + 4 <= n; i += 4) {
-            const float4 v = *reinterpret_cast<const float4 *>(x + i);
-            s = __fadd_rn(s, __fmul_rn(v.x, v.x));
-            s = __fadd_rn(s, __fmul_rn(v.y, v.y));
-            s = __fadd_rn(s, __fmul_rn(v.z, v.z));
-            s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && n >= 32) {
+        // 32-element chunks: the next chunk's loads are in flight while the
+        // dependent adds of this one run, so the chain costs ~1 add latency
+        // per element
+        const float4 *v = reinterpret_cast<const float4 *>(x);
+        float4 cur[8], nxt[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) cur[k] = v[k];
+        for (; i + 32 <= n; i += 32) {
+            const bool more = i + 64 <= n;
+#pragma unroll
+            for (int k = 0; k < 8; k++) nxt[k] = more ? v[(i + 32) / 4 + k] : cur[k];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                s = __fadd_rn(s, __fmul_rn(cur[k].x, cur[k].x));
+                s = __fadd_rn(s, __fmul_rn(cur[k].y, cur[k].y));
+                s = __fadd_rn(s, __fmul_rn(cur[k].z, cur[k].z));
+                s = __fadd_rn(s, __fmul_rn(cur[k].w, cur[k].w));
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++) cur[k] = nxt[k];
         }
     }
     for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));

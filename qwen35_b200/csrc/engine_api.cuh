@@ -162,6 +162,8 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 3 * B));
     Q35_TRY(gemv_prepare());
+    Q35_TRY(gemv_lpr_prepare());
+    Q35_TRY(attx_prepare(e->max_seq));
     Q35_TRY((int)cudaDeviceSynchronize());
     e->finalized = true;
     return 0;

@@ -140,32 +140,60 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     float *hout = a.hist + slot * a.hist_slot + (long long)((p + 1) & 1) * conv_dim * 3;
     const float *raw = a.qkv + (long long)b * a.qkv_ld;
 
-    auto conv = [&](int ch, bool owner) {
-        const float *hh = hin + (long long)ch * 3;
-        const float *w = a.conv_w + (long long)ch * 4;
-        const float cur = raw[ch];
+    // every global load this CTA needs, issued up front so their latencies
+    // overlap: the state column, the conv taps / history / inputs, the gate
+    // and norm operands
+    float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
+    float col[GDN_KD];
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) col[i] = S[(long long)i * GDN_KD + j];
+    const int chq = kh * kd + j, chk = kq + kh * kd + j, chv = 2 * kq + h * kd + j;
+    float hq[3], hk[3], hv[3], wq[4], wk[4], wv[4];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        hq[i] = hin[(long long)chq * 3 + i];
+        hk[i] = hin[(long long)chk * 3 + i];
+        hv[i] = hin[(long long)chv * 3 + i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        wq[i] = a.conv_w[(long long)chq * 4 + i];
+        wk[i] = a.conv_w[(long long)chk * 4 + i];
+        wv[i] = a.conv_w[(long long)chv * 4 + i];
+    }
+    const float cq = raw[chq], ck = raw[chk], cv = raw[chv];
+    const float zj = a.z[(long long)b * a.z_ld + (long long)h * kd + j];
+    const float nwj = a.ssm_norm[j];
+    const float *ar = a.ab + (long long)b * a.ab_ld;
+    const float a_raw = ar[h], b_raw = ar[a.nv + h], ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
+
+    // causal conv k=4 + silu: y = w0*h0 + w1*h1 + w2*h2 + w3*x, left to right
+    auto conv = [&](const float (&hh)[3], const float (&w)[4], float cur) {
         const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(hh[0], w[0]), __fmul_rn(hh[1], w[1])),
                                             __fmul_rn(hh[2], w[2])),
                                   __fmul_rn(cur, w[3]));
-        if (owner) {
-            float *ho = hout + (long long)ch * 3;
-            ho[0] = hh[1];
-            ho[1] = hh[2];
-            ho[2] = cur;
-        }
         return silu_f(s);
     };
-    const bool qk_owner = h < a.nk;
-    sq[j] = conv(kh * kd + j, qk_owner);
-    sk[j] = conv(kq + kh * kd + j, qk_owner);
-    const float vj = conv(2 * kq + h * kd + j, true);
+    auto shift = [&](int ch, const float (&hh)[3], float cur) {
+        float *ho = hout + (long long)ch * 3;
+        ho[0] = hh[1];
+        ho[1] = hh[2];
+        ho[2] = cur;
+    };
+    if (h < a.nk) {  // the owner of a k head's q / k channels advances their history
+        shift(chq, hq, cq);
+        shift(chk, hk, ck);
+    }
+    shift(chv, hv, cv);
+    sq[j] = conv(hq, wq, cq);
+    sk[j] = conv(hk, wk, ck);
+    const float vj = conv(hv, wv, cv);
     __syncthreads();
     if (j == 0) s_scal[0] = serial_sumsq(sq, kd);
     if (j == 32) s_scal[1] = serial_sumsq(sk, kd);
     if (j == 64) {
-        const float *ar = a.ab + (long long)b * a.ab_ld;
-        s_scal[2] = sigmoid_f(ar[a.nv + h]);
-        s_scal[3] = exp_f(__fmul_rn(a.ssm_a[h], softplus_f(__fadd_rn(ar[h], a.dt_bias[h]))));
+        s_scal[2] = sigmoid_f(b_raw);
+        s_scal[3] = exp_f(__fmul_rn(ssm_a, softplus_f(__fadd_rn(a_raw, dtb))));
     }
     __syncthreads();
     const float iq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[0], 1e-6f)));
@@ -176,10 +204,6 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     __syncthreads();
     sq[j] = qj;
     sk[j] = kj;
-    float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
-    float col[GDN_KD];
-#pragma unroll
-    for (int i = 0; i < GDN_KD; i++) col[i] = S[(long long)i * GDN_KD + j];
     __syncthreads();
     float acc = 0.0f;
 #pragma unroll
@@ -200,8 +224,8 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     if (j == 0) s_scal[0] = serial_sumsq(so, kd);
     __syncthreads();
     const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s_scal[0], (float)kd), a.eps)));
-    float y = __fmul_rn(__fmul_rn(o, sc), a.ssm_norm[j]);
-    y = __fmul_rn(y, silu_f(a.z[(long long)b * a.z_ld + (long long)h * kd + j]));
+    float y = __fmul_rn(__fmul_rn(o, sc), nwj);
+    y = __fmul_rn(y, silu_f(zj));
     if (a.fam == 32) {
         const int w = j >> 5;
         quant_q8_0_warp(y, a.xq + (long long)b * a.xq_ld + (long long)(h * (kd / 32) + w) * 34, j & 31);

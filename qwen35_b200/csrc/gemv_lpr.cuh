@@ -7,18 +7,23 @@
 // lane spends ~20 instructions at one token.
 //
 // Data movement: a warp owns 32 consecutive rows (a "warp tile") and streams
-// them in column chunks of 256 / 512 columns.  Each lane issues the bulk copy
-// (cp.async.bulk, completing on the warp's mbarrier) of its own row's chunk
-// into a per-warp ring of NS stages; the destination row stride is an odd
-// multiple of 16 bytes, so the 128-bit shared loads of 32 lanes (32 rows at
-// the same column) hit distinct bank groups.  The warp refills a slot right
-// after it has consumed it; nothing else touches the ring, so only "full"
-// barriers exist.  Weight copies are issued before the programmatic-launch
-// wait, so they overlap the previous kernel's tail.
+// them in 256-column chunks: one 2D TMA load (cp.async.bulk.tensor, a box of
+// 32 rows x one chunk, completing on the warp's mbarrier) per stage of a
+// per-warp ring.  At 256 columns a row's chunk is 272 (Q8_0), 144 (IQ4_NL,
+// Q4_K) or 176 (Q5_K) bytes -- an odd multiple of 16 -- so the 128-bit shared
+// loads of 32 lanes (32 rows at the same column) hit distinct bank groups.
+// The warp refills a slot right after it has consumed it; nothing else
+// touches the ring, so only "full" barriers exist.  Weight loads are issued
+// before the programmatic-launch wait, so they overlap the previous kernel's
+// tail.  (Per-row copies of a few hundred bytes were issue-bound in the TMA
+// unit at ~3.3 TB/s; one box per stage removes that.)
 //
 // Eligible: Q8_0 / IQ4_NL / Q4_K / Q5_K rows whose byte length and base are
 // multiples of 16 (cols % 256 == 0).  Anything else uses k_gemv.
 #pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "gemv.cuh"
 
 namespace q35 {
@@ -43,6 +48,7 @@ struct LprSeg {
 };
 
 struct LprArgs {
+    CUtensorMap tmap[GV_MAX_SEG];  // per matrix: u64 elements, box = 32 rows x one chunk
     LprSeg seg[GV_MAX_SEG];
     int nseg;
     long long total_tiles;  // warp tiles (32 rows) over all matrices
@@ -71,16 +77,42 @@ enum { LPR_PRO_NONE = 0, LPR_PRO_NORM = 1, LPR_PRO_SWIGLU = 2 };
 // The activation quantizers (quant_q8_0_warp / quant_q8_K_warp), writing the
 // GEMV's shared layout directly: int8 plane, f32 scale per block (for Q8_0
 // the f16-rounded scale the API layout would carry), int32 16-element sums.
-Q35_DEV void lpr_quant_q8_0(float v, uint8_t *at, int cols, int b, int lane) {
-    const float amax = warp_max(fabsf(v));
+// The same Q8_0 quantizer with one thread per 32-element block (x: the
+// block's f32 values in shared memory): no shuffles, so a CTA quantizes a
+// whole row in one pass.  max() is exact in any order, and every element
+// takes the warp version's operations.
+Q35_DEV void lpr_quant_q8_0_thread(const float *x, uint8_t *at, int cols, int b) {
+    float v[32];
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float4 t = x4[k];
+        v[4 * k] = t.x;
+        v[4 * k + 1] = t.y;
+        v[4 * k + 2] = t.z;
+        v[4 * k + 3] = t.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
     const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     const float inv = amax > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    if (lane == 0) reinterpret_cast<float *>(at + cols)[b] = f16_to_f32(f32_to_f16_bits(scale, 0x0380u));
-    const float x = __fmul_rn(v, inv);
-    int q = __float2int_rz(__fadd_rn(x, x >= 0.0f ? 0.5f : -0.5f));
-    q = q > 127 ? 127 : (q < -128 ? -128 : q);
-    reinterpret_cast<int8_t *>(at)[b * 32 + lane] = (int8_t)q;
+    reinterpret_cast<float *>(at + cols)[b] = f16_to_f32(f32_to_f16_bits(scale, 0x0380u));
+    uint32_t *dst = reinterpret_cast<uint32_t *>(at + b * 32);
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float xx = __fmul_rn(v[4 * w + k], inv);
+            int q = __float2int_rz(__fadd_rn(xx, xx >= 0.0f ? 0.5f : -0.5f));
+            q = q > 127 ? 127 : (q < -128 ? -128 : q);
+            word |= (uint32_t)(q & 0xFF) << (8 * k);
+        }
+        dst[w] = word;
+    }
 }
+
 Q35_DEV void lpr_quant_q8_K(const float (&v)[8], uint8_t *at, int cols, int b, int lane) {
     float a = 0.0f;
 #pragma unroll
@@ -112,6 +144,15 @@ Q35_DEV void lpr_quant_q8_K(const float (&v)[8], uint8_t *at, int cols, int b, i
 }
 
 Q35_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 2D tiled TMA load of one box into shared memory, completing on `bar`
+Q35_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 
 Q35_DEV float f16_lo(uint32_t w) { return f16_to_f32((uint16_t)(w & 0xFFFFu)); }
 Q35_DEV float f16_hi(uint32_t w) { return f16_to_f32((uint16_t)(w >> 16)); }
@@ -191,8 +232,8 @@ Q35_DEV void lpr_q8_0(const uint8_t *rp, const ActView &A, int ntok, int gb0, in
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t < ntok) {
-                    int si = dot4x4(q[0], q[1], q[2], q[3], A.q16(t, b * 32), 0);
-                    si = dot4x4(q[4], q[5], q[6], q[7], A.q16(t, b * 32 + 16), si);
+                    const int s0 = dot4x4(q[0], q[1], q[2], q[3], A.q16(t, b * 32), 0);
+                    const int si = s0 + dot4x4(q[4], q[5], q[6], q[7], A.q16(t, b * 32 + 16), 0);
                     // sumf += dx * dy * (float)sumi
                     sk.put(t, b, __fmul_rn(__fmul_rn(dx, A.dsc(t, b)), __int2float_rn(si)));
                 }
@@ -235,8 +276,8 @@ Q35_DEV void lpr_iq4_nl(const uint8_t *rp, const ActView &A, int ntok, int gb0, 
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t < ntok) {
-                    int si = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, b * 32), 0);
-                    si = dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, b * 32 + 16), si);
+                    const int s0 = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, b * 32), 0);
+                    const int si = s0 + dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, b * 32 + 16), 0);
                     sk.put(t, b, __fmul_rn(__fmul_rn(dx, A.dsc(t, b)), __int2float_rn(si)));
                 }
             }
@@ -287,10 +328,10 @@ Q35_DEV void lpr_q45_k(const uint8_t *rp, const ActView &A, int ntok, int gb0, i
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t < ntok) {
-                    int dl = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, e0), 0);
-                    dl = dot4x4(lo[4], lo[5], lo[6], lo[7], A.q16(t, e0 + 16), dl);
-                    int dh = dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, e0 + 32), 0);
-                    dh = dot4x4(hi[4], hi[5], hi[6], hi[7], A.q16(t, e0 + 48), dh);
+                    const int dl = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, e0), 0) +
+                                   dot4x4(lo[4], lo[5], lo[6], lo[7], A.q16(t, e0 + 16), 0);
+                    const int dh = dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, e0 + 32), 0) +
+                                   dot4x4(hi[4], hi[5], hi[6], hi[7], A.q16(t, e0 + 48), 0);
                     is[t] += sc0 * dl + sc1 * dh;
                     ms[t] += m0 * (A.bsum(t, gq) + A.bsum(t, gq + 1)) + m1 * (A.bsum(t, gq + 2) + A.bsum(t, gq + 3));
                 }
@@ -358,16 +399,15 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     auto issue = [&](long long i) {
         const long long tile = t0 + (i / nck) * tstride;
         const int c = c_lo + (int)(i % nck);
-        const LprSeg &sg = a.seg[lpr_find_seg(a, tile)];
+        const int si = lpr_find_seg(a, tile);
+        const LprSeg &sg = a.seg[si];
         const long long r0 = (tile - sg.tile_begin) * 32;
-        const int nv = (int)min(32LL, sg.rows - r0);
         const int slot = (int)(i % a.ns);
-        if (lane == 0) mbar_arrive_expect_tx(&bar[slot], (uint32_t)(nv * sg.chunk_bytes));
-        __syncwarp();
-        if (lane < nv)
-            bulk_g2s(ring + ((size_t)slot * 32 + lane) * a.rs,
-                     sg.w + (size_t)(r0 + lane) * sg.row_bytes + (size_t)c * sg.chunk_bytes, (uint32_t)sg.chunk_bytes,
-                     &bar[slot]);
+        if (lane == 0) {
+            // the box is always 32 full rows (rows past the end are zero-filled)
+            mbar_arrive_expect_tx(&bar[slot], (uint32_t)(32 * sg.chunk_bytes));
+            tma_load_2d(ring + (size_t)slot * 32 * a.rs, &a.tmap[si], c * (sg.chunk_bytes / 8), (int)r0, &bar[slot]);
+        }
     };
     long long issued = nst < a.ns ? nst : a.ns;
     for (long long i = 0; i < issued; i++) issue(i);
@@ -375,17 +415,22 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     // the activation belongs to the previous kernel
     pdl_wait();
     if (a.prologue != LPR_PRO_NONE) {
+        // Build the f32 input rows in shared memory first, every global load
+        // independent of the others (coalesced float4), then quantize from
+        // shared memory; the per-block quantize steps are warp-synchronous
+        // and would otherwise wait out one memory round trip each.
         __shared__ float s_scale[LPR_MAX_NT];
-        const float *xs = reinterpret_cast<const float *>(smem + a.x_off);
+        float *xs = reinterpret_cast<float *>(smem + a.x_off);  // [ntok][cols]
+        float *ws = xs + (size_t)a.ntok * a.cols;                 // norm weight [cols]
+        const int c4 = a.cols / 4;
+        float4 *xd = reinterpret_cast<float4 *>(xs);
         if (a.prologue == LPR_PRO_NORM) {
-            // rmsnorm: x staged in shared memory, the sum of squares taken in
-            // the CPU's serial order, one thread per token (engine.zig:1507,
-            // elementwise.zig:43-57)
-            float4 *xd = reinterpret_cast<float4 *>(smem + a.x_off);
-            const int c4 = a.cols / 4;
-            for (int idx = threadIdx.x; idx < a.ntok * c4; idx += blockDim.x) {
+            // rmsnorm (engine.zig:1507, elementwise.zig:43-57): the sum of
+            // squares in the CPU's serial order, one thread per token
+            for (int idx = threadIdx.x; idx < (a.ntok + 1) * c4; idx += blockDim.x) {
                 const int t = idx / c4, j = idx - t * c4;
-                xd[idx] = reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j];
+                xd[idx] = t < a.ntok ? reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j]
+                                     : reinterpret_cast<const float4 *>(a.pw)[j];
             }
             __syncthreads();
             if ((int)threadIdx.x < a.ntok) {
@@ -393,26 +438,36 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
                 s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
             }
             __syncthreads();
+            for (int idx = threadIdx.x; idx < a.ntok * a.cols; idx += blockDim.x) {
+                const int t = idx / a.cols, i = idx - t * a.cols;
+                xs[idx] = __fmul_rn(__fmul_rn(xs[idx], s_scale[t]), ws[i]);
+            }
+        } else {
+            // silu(gate) * up (engine.zig:2027-2036)
+            for (int idx = threadIdx.x; idx < a.ntok * c4; idx += blockDim.x) {
+                const int t = idx / c4, j = idx - t * c4;
+                const float4 g = reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j];
+                const float4 u = reinterpret_cast<const float4 *>(a.pu + (long long)t * a.px_ld)[j];
+                xd[idx] = make_float4(__fmul_rn(silu_f(g.x), u.x), __fmul_rn(silu_f(g.y), u.y),
+                                      __fmul_rn(silu_f(g.z), u.z), __fmul_rn(silu_f(g.w), u.w));
+            }
         }
-        auto val = [&](int t, int i) -> float {
-            if (a.prologue == LPR_PRO_NORM)
-                return __fmul_rn(__fmul_rn(xs[(size_t)t * a.cols + i], s_scale[t]), a.pw[i]);
-            const long long o = (long long)t * a.px_ld + i;
-            return __fmul_rn(silu_f(a.px[o]), a.pu[o]);
-        };
+        __syncthreads();
         if (a.family == 32) {
             const int nb = a.cols / 32;
-            for (int bi = warp; bi < a.ntok * nb; bi += cw) {
+            for (int bi = threadIdx.x; bi < a.ntok * nb; bi += blockDim.x) {
                 const int t = bi / nb, b = bi - t * nb;
-                lpr_quant_q8_0(val(t, b * 32 + lane), act + (size_t)t * a.act_stride, a.cols, b, lane);
+                lpr_quant_q8_0_thread(xs + (size_t)t * a.cols + b * 32, act + (size_t)t * a.act_stride, a.cols, b);
             }
         } else {
             const int nb = a.cols / 256;
             for (int bi = warp; bi < a.ntok * nb; bi += cw) {
                 const int t = bi / nb, b = bi - t * nb;
                 float v[8];
-#pragma unroll
-                for (int k = 0; k < 8; k++) v[k] = val(t, b * 256 + lane * 8 + k);
+                const float4 *src = reinterpret_cast<const float4 *>(xs + (size_t)t * a.cols + b * 256 + lane * 8);
+                const float4 v0 = src[0], v1 = src[1];
+                v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+                v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
                 lpr_quant_q8_K(v, act + (size_t)t * a.act_stride, a.cols, b, lane);
             }
         }
@@ -472,7 +527,7 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
                     failed = true;  // keep walking the loop: the named barriers below need every warp
             }
             if (!failed && lane < nv) {
-                const uint8_t *rp = ring + ((size_t)slot * 32 + lane) * a.rs;
+                const uint8_t *rp = ring + (size_t)slot * 32 * a.rs + (size_t)lane * sg.chunk_bytes;
                 if (kw == 1) {
                     FoldSink<NT> sk{acc};
                     lpr_chunk<NT>(sg.ttype, rp, A, a.ntok, c, a.chunk_cols, sk);
@@ -546,16 +601,42 @@ struct LprPrologue {
     long long ld;          // floats between tokens of x (and u)
     float eps;
 };
-constexpr size_t LPR_NORM_STAGE_MAX = 48 * 1024;  // f32 rows staged for the serial norm sum
+constexpr size_t LPR_PRO_STAGE_MAX = 64 * 1024;  // f32 rows a fused prologue stages in shared memory
 
 // Try the lane-per-row kernel.  Returns -1 (nothing launched) when the
 // matrices or the shape are not eligible, else the launch status.
-#ifndef LPR_CHUNK_COLS
-#define LPR_CHUNK_COLS 256      // columns per streamed chunk
-#endif
 #ifndef LPR_TALL_OCC
-#define LPR_TALL_OCC 2          // CTAs per SM for tall matrices (4 row groups each)
+#define LPR_TALL_OCC 3          // CTAs per SM for tall matrices (4 row groups each)
 #endif
+constexpr int LPR_CHUNK_COLS = 256;  // columns per streamed chunk (row chunks are odd multiples of 16 B)
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+inline PFN_cuTensorMapEncodeTiled_v12000 lpr_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// the weight matrix as [rows][row_bytes / 8] u64 elements; box = 32 rows x
+// one chunk.  Base and row length are multiples of 16 bytes (checked by the
+// caller), as the tensor-map rules require.
+inline bool lpr_encode(CUtensorMap *m, const void *w, int row_bytes, long long rows, int chunk_bytes) {
+    const auto fn = lpr_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(chunk_bytes / 8), 32u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 #ifndef LPR_WARPS_PER_SM
 #define LPR_WARPS_PER_SM 8      // warps per SM aimed at for short matrices (columns split)
 #endif
@@ -570,7 +651,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         if ((reinterpret_cast<uintptr_t>(pro->x) & 15u) || (pro->ld & 3)) return -1;
     }
     const int fam = geom_of(segs[0].ttype).family;
-    const int chunk_cols = cols % LPR_CHUNK_COLS == 0 ? LPR_CHUNK_COLS : 256;
+    const int chunk_cols = LPR_CHUNK_COLS;
     int rs = 0;
     long long T = 0;
     for (int i = 0; i < nseg; i++) {
@@ -578,8 +659,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         if (!lpr_type_ok(segs[i].ttype) || g.family != fam) return -1;
         const int rb = cols / g.elems * g.bytes;
         if (rb % 16 != 0 || (reinterpret_cast<uintptr_t>(segs[i].w) & 15u) != 0) return -1;
-        int cb = chunk_cols / g.elems * g.bytes;
-        if ((cb / 16) % 2 == 0) cb += 16;  // odd multiple of 16: conflict-free 128-bit loads
+        const int cb = chunk_cols / g.elems * g.bytes;  // 272 / 144 / 144 / 176
         rs = cb > rs ? cb : rs;
         T += (segs[i].rows + 31) / 32;
     }
@@ -612,21 +692,29 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     occ = occ < 1 ? 1 : (occ > 8 ? 8 : occ);
     const int cw = rw * kw;
     size_t budget = occ == 1 ? LPR_SMEM_MAX : (228 * 1024) / occ - 2048;
-    const bool stage_x = pro && pro->kind == LPR_PRO_NORM;
-    auto xbytes = [&](int nt) { return stage_x ? (((size_t)nt * cols * 4 + 127) & ~size_t(127)) : 0; };
+    // prologue staging: the f32 rows (+ the norm weight) of one pass
+    auto xbytes = [&](int nt) -> size_t {
+        if (!pro) return 0;
+        const size_t b = (size_t)(nt + (pro->kind == LPR_PRO_NORM ? 1 : 0)) * cols * 4;
+        return (b + 127) & ~size_t(127);
+    };
     auto tbytes = [&](int nt) { return kw > 1 ? (size_t)rw * lpr_tmpl_nt(nt) * 32 * tst * 4 : 0; };
     auto base_of = [&](int nt) {  // barriers | activation | staged rows | terms
         return (size_t)(LPR_MAX_CW * LPR_MAX_NS * 8) + (((size_t)nt * act_stride + 127) & ~size_t(127)) + xbytes(nt) +
                ((tbytes(nt) + 127) & ~size_t(127));
     };
     // tokens per pass: at most LPR_MAX_NT, with room for a 2-stage ring
-    int group = LPR_MAX_NT;
-    if (stage_x)
-        while (group > 1 && (size_t)group * cols * 4 > LPR_NORM_STAGE_MAX) group >>= 1;
-    if (stage_x && (size_t)group * cols * 4 > LPR_NORM_STAGE_MAX) return -1;
-    while (group > 1 && base_of(group) + (size_t)cw * 2 * 32 * rs > budget) group >>= 1;
-    if (base_of(group) + (size_t)cw * 32 * rs > budget) budget = LPR_SMEM_MAX;  // fewer CTAs per SM
-    if (base_of(group) + (size_t)cw * 32 * rs > budget) return -1;
+    // tokens per pass: as many as the kernel takes (each pass streams the
+    // weights again), giving up CTAs per SM, then ring depth, before tokens
+    int group = ntok < LPR_MAX_NT ? lpr_tmpl_nt(ntok) : LPR_MAX_NT;
+    if (pro && xbytes(group) > LPR_PRO_STAGE_MAX) return -1;  // a fused prologue stages a whole pass
+    auto need = [&](int g, int nsmin) { return base_of(g) + (size_t)cw * nsmin * 32 * rs; };
+    if (need(group, 2) > budget) {
+        budget = LPR_SMEM_MAX;
+        occ = 1;
+    }
+    while (group > 1 && need(group, 1) > budget) group >>= 1;
+    if (need(group, 1) > budget) return -1;
     const long long grid = ctas < (long long)nsm * occ ? ctas : (long long)nsm * occ;
     for (int t0 = 0; t0 < ntok; t0 += group) {
         const int nt = ntok - t0 < group ? ntok - t0 : group;
@@ -669,6 +757,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
             s.mode = segs[i].mode;
             s.tile_begin = tiles;
             tiles += (s.rows + 31) / 32;
+            if (!lpr_encode(&a.tmap[i], s.w, s.row_bytes, s.rows, s.chunk_bytes)) return t0 == 0 ? -1 : 1;
         }
         a.total_tiles = tiles;
         const size_t base = base_of(nt);
