@@ -227,10 +227,13 @@ def gemv_roofline(run, reps=20):
         assert L.q35_launch_mul_mat_vec(w.data_ptr(), xq.data_ptr(), out.data_ptr(), rows, cols, 1, tt, s) == 0
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    # NVTX range for the ncu capture of this kernel (profiles/gemv_lpr_lmhead_0p8b_q8_0.md)
+    torch.cuda.nvtx.range_push("q35_roofline")
     for a, c in ev:
         a.record(run.stream)
         L.q35_launch_mul_mat_vec(w.data_ptr(), xq.data_ptr(), out.data_ptr(), rows, cols, 1, tt, s)
         c.record(run.stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ms = float(np.mean([a.elapsed_time(c) for a, c in ev]))
     algo = rows * (cols // e) * b + xq.numel() + rows * 4
@@ -241,6 +244,19 @@ def gemv_roofline(run, reps=20):
     return {"kernel": "%s (lm_head, %dx%d %s)" % (kname, rows, cols, {8: "Q8_0", 20: "IQ4_NL", 12: "Q4_K",
                                                                      13: "Q5_K", 14: "Q6_K"}[tt]),
             "bytes": algo, "ms": ms, "gbs": algo / (ms * 1e-3) / 1e9}
+
+
+def measured_traffic(kernel):
+    """DRAM bytes per launch of the roofline kernel from the committed ncu
+    summary (profiles/*.json), when the summary covers this kernel"""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+    except (OSError, ValueError):
+        return None
+    e = d.get(kernel)
+    return float(e["dram_bytes_per_launch"]) if e else None
 
 
 def cpu_baseline(run, seconds_target=15.0):
@@ -430,7 +446,8 @@ def main():
                     "d2h_bytes_per_step": 4 * world},
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved": roof["gbs"], "peak": hbm, "unit": "GB/s",
-                         "frac": roof["gbs"] / hbm, "traffic": None, "kernel": roof["kernel"],
+                         "frac": roof["gbs"] / hbm, "traffic": measured_traffic(roof["kernel"]),
+                         "kernel": roof["kernel"],
                          "algorithmic_bytes_per_launch": roof["bytes"], "avg_launch_ms": roof["ms"],
                          "peak_source": f"{pk_kind} (MEASURED_PEAKS.json hbm_gbs)" if pk_kind == "measured"
                          else "fallback 6.65 TB/s"},

@@ -691,7 +691,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     }
     occ = occ < 1 ? 1 : (occ > 8 ? 8 : occ);
     const int cw = rw * kw;
-    size_t budget = occ == 1 ? LPR_SMEM_MAX : (228 * 1024) / occ - 2048;
+    size_t budget = occ == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / occ - 2048;
     // prologue staging: the f32 rows (+ the norm weight) of one pass
     auto xbytes = [&](int nt) -> size_t {
         if (!pro) return 0;
@@ -709,10 +709,8 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     int group = ntok < LPR_MAX_NT ? lpr_tmpl_nt(ntok) : LPR_MAX_NT;
     if (pro && xbytes(group) > LPR_PRO_STAGE_MAX) return -1;  // a fused prologue stages a whole pass
     auto need = [&](int g, int nsmin) { return base_of(g) + (size_t)cw * nsmin * 32 * rs; };
-    if (need(group, 2) > budget) {
-        budget = LPR_SMEM_MAX;
-        occ = 1;
-    }
+    auto budget_of = [](int o) { return o == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / o - 2048; };
+    while (occ > 1 && need(group, 2) > budget) budget = budget_of(--occ);
     while (group > 1 && need(group, 1) > budget) group >>= 1;
     if (need(group, 1) > budget) return -1;
     const long long grid = ctas < (long long)nsm * occ ? ctas : (long long)nsm * occ;
