@@ -648,6 +648,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     if (nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || ntok <= 0 || cols % 256 != 0) return -1;
     if (pro) {
         if (pro->kind != LPR_PRO_NORM && pro->kind != LPR_PRO_SWIGLU) return -1;
+        if (ntok >= 16) return -1;  // many tokens: the tensor-core path, after a separate prologue kernel
         if ((reinterpret_cast<uintptr_t>(pro->x) & 15u) || (pro->ld & 3)) return -1;
     }
     const int fam = geom_of(segs[0].ttype).family;
@@ -783,12 +784,18 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     return 0;
 }
 
-// y = W x for up to GV_MAX_SEG matrices sharing one activation: the
-// lane-per-row kernel where the matrices allow it, else the block-splitting
-// kernel.  Validation (types, families, alignment) is the latter's.
+// y = W x for up to GV_MAX_SEG matrices sharing one activation: the tensor-
+// core MMQ for >= 16 tokens of Q8_0 / IQ4_NL, the lane-per-row kernel where
+// the matrices allow it, else the block-splitting kernel.  Validation
+// (types, families, alignment) is the latter's.
+inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                      long long xq_ld);
+
 inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
                        long long xq_ld = 0) {
-    const int rc = gemv_lpr_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
+    int rc = mmq_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
+    if (rc != -1) return rc;
+    rc = gemv_lpr_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
     if (rc != -1) return rc;
     return gemv_launch_split(segs, nseg, xq, cols, ntok, st, xq_ld);
 }

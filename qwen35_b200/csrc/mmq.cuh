@@ -1,0 +1,431 @@
+// mmq.cuh -- quantized matrix x many-token product on the 5th-generation
+// tensor cores (tcgen05, sm_100a): batched decode and prefill.
+//
+//   y[t][r] = sum over blocks b, in block order, of  (dw[r][b] * dx[t][b]) * isum[r][t][b]
+//
+// isum is the exact int32 dot of the 32 int8 weights and activations of
+// block b: one `tcgen05.mma.kind::i8` (M = 128 rows, N = 64 tokens, K = 32)
+// per block computes it for a 128 x 64 tile, each block into its own TMEM
+// accumulator region.  The f32 fold then runs on the CUDA cores in the
+// reference scalar tier's order (kernels32.c:462), so the result is bit-exact
+// with the CPU and with the decode GEMV -- the tensor core does the integer
+// part only, where reordering is exact.
+//
+// CTA = 6 warps, tile = 128 weight rows x 64 tokens, K in 256-column chunks:
+//   warp 0 (one lane): TMA producer -- per chunk one 2D box of the raw GGUF
+//     weight rows (128 x 272 B Q8_0 / 144 B IQ4_NL) and one of the raw Q8_0
+//     activation rows (64 x 272 B) into a 2-stage ring;
+//   warp 1: allocates / frees 256 TMEM columns, one lane issues the MMAs;
+//   warps 2-5 (thread = weight row = TMEM lane): convert the raw chunk into
+//     the canonical K-major operand layout (no swizzle: 8-row x 16-byte core
+//     matrices, K-adjacent cores 128 B apart, 8-row groups 256 B apart) with
+//     the per-block scales split off, then read the accumulators back
+//     (tcgen05.ld 32x32b) and fold.
+// Per chunk: convert 8 blocks -> MMA blocks 0-3 -> fold -> MMA blocks 4-7 ->
+// fold.  Named barrier 1 (warps 1-5) hands the operands / TMEM back and forth;
+// mbarriers (bounded waits) carry TMA and MMA completion.
+#pragma once
+#include "gemv_lpr.cuh"
+
+namespace q35 {
+
+constexpr int MMQ_M = 128;          // weight rows per tile (TMEM lanes)
+constexpr int MMQ_N = 64;           // tokens per tile (MMA N)
+constexpr int MMQ_KB = 8;           // 32-element blocks per chunk (256 columns)
+constexpr int MMQ_RB = 4;           // blocks per MMA round (TMEM: 4 x 64 columns)
+constexpr int MMQ_NS = 2;           // raw-chunk ring stages
+constexpr int MMQ_THREADS = 192;
+constexpr int MMQ_TMEM_COLS = MMQ_RB * MMQ_N;  // 256
+constexpr int MMQ_MIN_TOK = 16;     // below this the decode GEMV is used
+
+struct MmqSeg {
+    float *out;
+    long long rows, out_ld;
+    long long tile_begin;   // first row tile of this matrix
+    int ttype, row_bytes, chunk_bytes, mode;
+};
+
+struct MmqArgs {
+    CUtensorMap wmap[GV_MAX_SEG];   // weights: [rows][row_bytes/8] u64, box 128 rows x one chunk
+    CUtensorMap xmap;               // activations: [ntok][act_row_bytes/8] u64, box 64 rows x 272 B
+    MmqSeg seg[GV_MAX_SEG];
+    int nseg;
+    long long total_tiles;          // row tiles over all matrices
+    int ntok, nchunk;
+};
+
+// shared memory plan (bytes from the 1024-aligned base)
+constexpr int MMQ_W_STAGE = MMQ_M * 272;                    // raw weight chunk (Q8_0 size; IQ4_NL uses less)
+constexpr int MMQ_X_STAGE = MMQ_N * 272;                    // raw activation chunk
+constexpr int MMQ_OFF_A = 0;                                // A operands: KB x (128 x 32 B)
+constexpr int MMQ_OFF_B = MMQ_OFF_A + MMQ_KB * MMQ_M * 32;  // B operands: KB x (64 x 32 B)
+constexpr int MMQ_OFF_DW = MMQ_OFF_B + MMQ_KB * MMQ_N * 32; // f32 [KB][128]
+constexpr int MMQ_OFF_DX = MMQ_OFF_DW + MMQ_KB * MMQ_M * 4; // f32 [KB][64]
+constexpr int MMQ_OFF_RAW = MMQ_OFF_DX + MMQ_KB * MMQ_N * 4;
+constexpr int MMQ_OFF_BAR = MMQ_OFF_RAW + MMQ_NS * (MMQ_W_STAGE + MMQ_X_STAGE);
+constexpr int MMQ_SMEM = MMQ_OFF_BAR + 128 + 1024;          // + barriers, + alignment slack
+
+// ---- tcgen05 / descriptor helpers -----------------------------------------
+// shared-memory matrix descriptor, K-major, no swizzle (version 1 = sm_100)
+Q35_DEV uint64_t umma_desc(const void *smem_ptr, uint32_t lbo, uint32_t sbo) {
+    const uint32_t a = smem_u32(smem_ptr);
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = MMQ_N
+constexpr uint32_t MMQ_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MMQ_N >> 3) << 17) |
+                               ((uint32_t)(MMQ_M >> 4) << 24);
+
+Q35_DEV void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+Q35_DEV void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+Q35_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+Q35_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive columns of 32-bit TMEM: register i = column c0 + i
+Q35_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+Q35_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// (float)d for |d| < 2^22, exactly: the integer placed in the mantissa of
+// 1.5 * 2^23, which is then subtracted (both steps exact)
+Q35_DEV float exact_i2f(int d) { return __fsub_rn(__int_as_float(0x4B400000 + d), 12582912.0f); }
+
+// canonical K-major no-swizzle offset of row m, 16-byte half h of a 32-byte K slice
+Q35_DEV int umma_off(int m, int h) { return (m >> 3) * 256 + h * 128 + (m & 7) * 16; }
+
+// raw Q8_0 chunk row (8 blocks, 272 B at a 16-byte-aligned address) ->
+// 8 operand rows + scales; `put(b, d, q)` receives block b's f16 scale and
+// its 8 packed int8 words
+template <class Put>
+Q35_DEV void unpack_q8_0_chunk(const uint8_t *rp, Put put) {
+    uint32_t W[68];
+    const uint4 *s = reinterpret_cast<const uint4 *>(rp);
+#pragma unroll
+    for (int i = 0; i < 17; i++) {
+        const uint4 v = s[i];
+        W[4 * i] = v.x;
+        W[4 * i + 1] = v.y;
+        W[4 * i + 2] = v.z;
+        W[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int o = 34 * k, w0 = o >> 2;
+        uint32_t q[8];
+        uint16_t d;
+        if ((o & 3) == 0) {
+            d = (uint16_t)(W[w0] & 0xFFFFu);
+#pragma unroll
+            for (int i = 0; i < 8; i++) q[i] = __funnelshift_r(W[w0 + i], W[w0 + i + 1], 16);
+        } else {
+            d = (uint16_t)(W[w0] >> 16);
+#pragma unroll
+            for (int i = 0; i < 8; i++) q[i] = W[w0 + 1 + i];
+        }
+        put(k, d, q);
+    }
+}
+
+// raw IQ4_NL chunk row (8 blocks, 144 B) -> int8 codebook values: low
+// nibbles are elements 0..15 of a block, high nibbles 16..31
+template <class Put>
+Q35_DEV void unpack_iq4_nl_chunk(const uint8_t *rp, Put put) {
+    uint32_t W[36];
+    const uint4 *s = reinterpret_cast<const uint4 *>(rp);
+#pragma unroll
+    for (int i = 0; i < 9; i++) {
+        const uint4 v = s[i];
+        W[4 * i] = v.x;
+        W[4 * i + 1] = v.y;
+        W[4 * i + 2] = v.z;
+        W[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int o = 18 * k, w0 = o >> 2;
+        uint32_t qs[4];
+        uint16_t d;
+        if ((o & 3) == 0) {
+            d = (uint16_t)(W[w0] & 0xFFFFu);
+#pragma unroll
+            for (int i = 0; i < 4; i++) qs[i] = __funnelshift_r(W[w0 + i], W[w0 + i + 1], 16);
+        } else {
+            d = (uint16_t)(W[w0] >> 16);
+#pragma unroll
+            for (int i = 0; i < 4; i++) qs[i] = W[w0 + 1 + i];
+        }
+        uint32_t q[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) iq4_word(qs[i], q[i], q[4 + i]);
+        put(k, d, q);
+    }
+}
+
+Q35_DEV int mmq_find_seg(const MmqArgs &a, long long tile) {
+    int s = 0;
+#pragma unroll
+    for (int i = 1; i < GV_MAX_SEG; i++)
+        if (i < a.nseg && tile >= a.seg[i].tile_begin) s = i;
+    return s;
+}
+
+__global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ MmqArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = sm + MMQ_OFF_A, *sB = sm + MMQ_OFF_B;
+    float *sDW = reinterpret_cast<float *>(sm + MMQ_OFF_DW), *sDX = reinterpret_cast<float *>(sm + MMQ_OFF_DX);
+    uint8_t *raw = sm + MMQ_OFF_RAW;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + MMQ_OFF_BAR);  // [MMQ_NS]
+    uint64_t *empty = full + MMQ_NS;                                  // [MMQ_NS]
+    uint64_t *mma_bar = empty + MMQ_NS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 1);
+    __shared__ int s_fail;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int issued = 0, ncommit = 0;  // producer's TMA chunks, MMA thread's commits
+    const long long tile = blockIdx.x;
+    const int t0 = blockIdx.y * MMQ_N;
+    const int si = mmq_find_seg(a, tile);
+    const MmqSeg &sg = a.seg[si];
+    const long long r0 = (tile - sg.tile_begin) * MMQ_M;
+
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < MMQ_NS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 4);
+        }
+        mbar_init(mma_bar, 1);
+        s_fail = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(MMQ_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // the activations (and a residual) belong to the previous kernel
+    pdl_wait();
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes), xbytes = (uint32_t)(MMQ_N * 272);
+            for (int c = 0; c < a.nchunk; c++, issued++) {
+                const int s = c % MMQ_NS;
+                if (c >= MMQ_NS && !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 121)) {
+                    s_fail = 1;
+                    break;
+                }
+                uint8_t *wst = raw + s * (MMQ_W_STAGE + MMQ_X_STAGE);
+                mbar_arrive_expect_tx(&full[s], wbytes + xbytes);
+                tma_load_2d(wst, &a.wmap[si], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
+                tma_load_2d(wst + MMQ_W_STAGE, &a.xmap, c * 34, t0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        for (int c = 0; c < a.nchunk; c++) {
+            for (int round = 0; round < MMQ_KB / MMQ_RB; round++) {
+                named_bar_sync(1, 160);  // operands converted / previous round's TMEM read
+                tc_fence_after();
+                if (lane == 0 && !s_fail) {
+                    for (int kb = 0; kb < MMQ_RB; kb++) {
+                        const int b = round * MMQ_RB + kb;
+                        const uint64_t ad = umma_desc(sA + b * MMQ_M * 32, 128, 256);
+                        const uint64_t bd = umma_desc(sB + b * MMQ_N * 32, 128, 256);
+                        umma_i8(tmem + (uint32_t)(kb * MMQ_N), ad, bd, MMQ_IDESC, 0u);
+                    }
+                    umma_commit(mma_bar);
+                    ncommit++;
+                }
+                __syncwarp();
+            }
+        }
+    } else {
+        // ---------------- converters + fold (thread = row = TMEM lane) ----------------
+        const int q = warp & 3;                       // TMEM lane quarter this warp may access
+        const int row = q * 32 + lane;
+        const int ct = threadIdx.x - 64;              // 0..127
+        float acc[MMQ_N];
+#pragma unroll
+        for (int t = 0; t < MMQ_N; t++) acc[t] = 0.0f;
+        int mma_phase = 0;
+        for (int c = 0; c < a.nchunk; c++) {
+            const int s = c % MMQ_NS;
+            const uint8_t *wst = raw + s * (MMQ_W_STAGE + MMQ_X_STAGE);
+            if (!s_fail && !mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 122)) s_fail = 1;
+            if (!s_fail) {
+                // weights: thread `ct` converts row `ct`
+                auto putw = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
+                    uint8_t *dst = sA + b * MMQ_M * 32;
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                    sDW[b * MMQ_M + ct] = f16_to_f32(d);
+                };
+                if (sg.ttype == TT_Q8_0)
+                    unpack_q8_0_chunk(wst + ct * sg.chunk_bytes, putw);
+                else
+                    unpack_iq4_nl_chunk(wst + ct * sg.chunk_bytes, putw);
+                // activations: threads 0..63 convert token rows
+                if (ct < MMQ_N) {
+                    auto putx = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
+                        uint8_t *dst = sB + b * MMQ_N * 32;
+                        *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                        *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                        sDX[b * MMQ_N + ct] = f16_to_f32(d);
+                    };
+                    unpack_q8_0_chunk(wst + MMQ_W_STAGE + ct * 272, putx);
+                }
+            }
+            // the raw stage is consumed: hand it back to the producer
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            // operands visible to the tensor core's (async) proxy
+            fence_proxy_async_smem();
+            for (int round = 0; round < MMQ_KB / MMQ_RB; round++) {
+                tc_fence_before();
+                named_bar_sync(1, 160);
+                if (!s_fail && !mbar_wait(mma_bar, (uint32_t)(mma_phase & 1), 123)) s_fail = 1;
+                mma_phase++;
+                tc_fence_after();
+                if (!s_fail) {
+                    for (int kb = 0; kb < MMQ_RB; kb++) {
+                        const int b = round * MMQ_RB + kb;
+                        const float dw = sDW[b * MMQ_M + row];
+                        const float *dx = sDX + b * MMQ_N;
+#pragma unroll
+                        for (int half = 0; half < MMQ_N / 32; half++) {
+                            uint32_t d[32];
+                            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(kb * MMQ_N + half * 32), d);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int i = 0; i < 32; i++) {
+                                const int t = half * 32 + i;
+                                // sumf += dw * dx * (float)sumi
+                                acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, dx[t]), exact_i2f((int)d[i])));
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        // outputs: row `row` of this tile, tokens t0 .. t0 + 63
+        const long long r = r0 + row;
+        if (!s_fail && r < sg.rows) {
+            const int nt = min(MMQ_N, a.ntok - t0);
+#pragma unroll
+            for (int t = 0; t < MMQ_N; t++) {
+                if (t < nt) {
+                    float *o = sg.out + (long long)(t0 + t) * sg.out_ld + r;
+                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (s_fail) {
+        // a wait gave up: let this CTA's own copies and MMAs land (bounded)
+        // before its shared memory and TMEM are released
+        if (warp == 0 && lane == 0)
+            for (int c = issued > MMQ_NS ? issued - MMQ_NS : 0; c < issued; c++)
+                if (!mbar_wait(&full[c % MMQ_NS], (uint32_t)((c / MMQ_NS) & 1), 124)) break;
+        if (warp == 1 && lane == 0 && ncommit > 0) mbar_wait(mma_bar, (uint32_t)((ncommit - 1) & 1), 125);
+        if (threadIdx.x == 0) set_error(120);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(MMQ_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+inline bool mmq_encode(CUtensorMap *m, const void *base, long long rows, long long row_stride, int row_bytes,
+                       int box_bytes, int box_rows) {
+    const auto fn = lpr_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_stride};
+    const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 8), (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1u, 1u};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline int mmq_prepare() {
+    static int done = 0;
+    if (done) return 0;
+    const cudaError_t e = cudaFuncSetAttribute(k_mmq, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM);
+    if (e != cudaSuccess) return (int)e;
+    done = 1;
+    return 0;
+}
+
+// Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL weights with
+// 16-byte-aligned rows and an API-layout Q8_0 activation at a 16-byte
+// multiple stride.  Returns -1 (nothing launched) when not eligible.
+inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                      long long xq_ld) {
+    if (ntok < MMQ_MIN_TOK || nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || cols % 256 != 0) return -1;
+    const long long act_row = (long long)(cols / 32) * 34;
+    const long long ld = xq_ld > 0 ? xq_ld : act_row;
+    if ((reinterpret_cast<uintptr_t>(xq) & 15u) || (ld & 15)) return -1;
+    MmqArgs a{};
+    long long tiles = 0;
+    for (int i = 0; i < nseg; i++) {
+        const int tt = segs[i].ttype;
+        if (tt != TT_Q8_0 && tt != TT_IQ4_NL) return -1;
+        const Geom g = geom_of(tt);
+        const int rb = cols / g.elems * g.bytes;
+        if (rb % 16 || (reinterpret_cast<uintptr_t>(segs[i].w) & 15u)) return -1;
+        MmqSeg &s = a.seg[i];
+        s.out = segs[i].out;
+        s.rows = segs[i].rows;
+        s.out_ld = segs[i].out_ld;
+        s.ttype = tt;
+        s.row_bytes = rb;
+        s.chunk_bytes = 256 / g.elems * g.bytes;  // 272 / 144
+        s.mode = segs[i].mode;
+        s.tile_begin = tiles;
+        tiles += (s.rows + MMQ_M - 1) / MMQ_M;
+        if (!mmq_encode(&a.wmap[i], segs[i].w, s.rows, rb, rb, s.chunk_bytes, MMQ_M)) return -1;
+    }
+    if (!mmq_encode(&a.xmap, xq, ntok, ld, (int)act_row, 272, MMQ_N)) return -1;
+    if (tiles == 0) return 0;
+    a.nseg = nseg;
+    a.total_tiles = tiles;
+    a.ntok = ntok;
+    a.nchunk = cols / 256;
+    Q35_TRY_RC(mmq_prepare());
+    const dim3 grid((unsigned)tiles, (unsigned)((ntok + MMQ_N - 1) / MMQ_N));
+    return launch_k(k_mmq, grid, dim3(MMQ_THREADS), (size_t)MMQ_SMEM, st, a);
+}
+
+}  // namespace q35

@@ -10,6 +10,7 @@
 #include "quant.cuh"
 #include "gemv.cuh"
 #include "gemv_lpr.cuh"
+#include "mmq.cuh"
 #include "ew.cuh"
 #include "gdn.cuh"
 #include "attn.cuh"

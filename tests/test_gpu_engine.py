@@ -125,6 +125,34 @@ def test_batched_equals_single(q35):
     eng.close()
 
 
+@pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed"])
+def test_batch_20_equals_single(q35, cfg_name):
+    """a 20-sequence step (tensor-core MMQ projections) gives every sequence
+    the same next tokens as stepping it alone (decode GEMV projections)"""
+    cfg = q35.CONFIGS[cfg_name]
+    synth = q35.SyntheticModel(cfg, seed=8)
+    nseq = 20
+    eng = q35.Engine(synth, n_slots=nseq + 1, max_seq=32, max_batch=nseq)
+    rng = np.random.default_rng(8)
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab, 6)] for _ in range(nseq)]
+    for s in range(nseq):
+        eng.reset_slot(s)
+    batched = []
+    last = None
+    for pos in range(8):
+        toks = [p[pos] if pos < len(p) else last[i] for i, p in enumerate(prompts)]
+        last = eng.step_host(toks, list(range(nseq)), [pos] * nseq)
+        batched.append(list(last))
+    for i in (0, 7, 19):
+        eng.reset_slot(nseq)
+        lt = None
+        for pos in range(8):
+            t = prompts[i][pos] if pos < len(prompts[i]) else lt
+            lt = eng.step_host([t], [nseq], [pos])[0]
+            assert lt == batched[pos][i], (cfg_name, i, pos)
+    eng.close()
+
+
 def test_graph_equals_direct(q35):
     cfg = q35.CONFIGS["tiny"]
     synth = q35.SyntheticModel(cfg, seed=2)

@@ -151,6 +151,50 @@ def test_gemv_bit_exact(L, O, name, tokens):
     assert_no_kernel_error(L)
 
 
+@pytest.mark.parametrize("name", ["Q8_0", "IQ4_NL"])
+@pytest.mark.parametrize("tokens", [16, 37, 64, 100])
+def test_mmq_tensor_core_bit_exact(L, O, name, tokens):
+    """>= 16 tokens of Q8_0 / IQ4_NL go to the tcgen05 MMQ: the int8 block dots
+    on the tensor core, the f32 fold in block order on the CUDA cores --
+    bit-exact with the reference scalar tier like the decode GEMV"""
+    for rows, cols in [(300, 1024), (129, 2048), (1000, 768), (128, 256)]:
+        got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + 7 * tokens)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
+    assert_no_kernel_error(L)
+
+
+def test_mmq_multi_and_residual(L, O):
+    """the MMQ over mixed IQ4_NL / Q8_0 matrices in one launch, residual mode"""
+    rng = np.random.default_rng(14)
+    cols, tokens = 512, 40
+    shapes = [(TT["IQ4_NL"], 300), (TT["Q8_0"], 16), (TT["Q8_0"], 130)]
+    x = rng.standard_normal((tokens, cols)).astype(np.float32)
+    xq = quantize_act(O, TT["Q8_0"], x)
+    ws, refs, outs = [], [], []
+    base = rng.standard_normal((tokens, 130)).astype(np.float32)
+    for i, (tt, rows) in enumerate(shapes):
+        wq = quantize_weight(O, tt, (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32))
+        ws.append(dev(wq))
+        r = matvec_q(O, tt, wq, xq, rows, cols, tokens)
+        if i == 2:
+            r = (base + r).astype(np.float32)
+            outs.append(dev(base))
+        else:
+            outs.append(torch.zeros((tokens, rows), dtype=torch.float32, device="cuda"))
+        refs.append(r)
+    n = 3
+    W = (ctypes.c_void_p * n)(*[w.data_ptr() for w in ws])
+    T = (ctypes.c_int * n)(*[s[0] for s in shapes])
+    R = (ctypes.c_longlong * n)(*[s[1] for s in shapes])
+    Op = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+    LD = (ctypes.c_longlong * n)(*[s[1] for s in shapes])
+    M = (ctypes.c_int * n)(0, 0, 1)
+    ok(L.q35b_mul_mat_vec_multi(n, W, T, R, Op, LD, M, dev(xq).data_ptr(), cols, tokens, S))
+    for o, r in zip(outs, refs):
+        assert np.array_equal(host(o).view(np.uint32), r.view(np.uint32))
+    assert_no_kernel_error(L)
+
+
 def test_gemv_golden_rows(L, O):
     """the reference's udtest rows (96 x 256) through the device GEMV"""
     gold = os.path.join(ROOT, "tests", "golden", "udtest")
