@@ -200,6 +200,36 @@ def time_e2e(run, steps, warmup, dist):
     return ms
 
 
+def time_prefill(cfg_name, ntok, chunk, seed, dist):
+    """one prompt of ntok seeded tokens through q35b_engine_prefill (runs of
+    `chunk` tokens: tensor-core projections, chunked GDN recurrence, causal
+    attention), CUDA events on the stream the engine runs on"""
+    import numpy as np
+    import torch
+
+    from qwen35_b200 import model as q35
+    synth = q35.SyntheticModel(q35.CONFIGS[cfg_name], seed=seed)
+    eng = q35.Engine(synth, n_slots=1, max_seq=ntok + 8, max_batch=chunk)
+    prompt = [int(t) for t in np.random.default_rng(seed + 5).integers(0, synth.cfg.vocab, ntok)]
+    eng.reset_slot(0)
+    eng.prefill(0, prompt)  # warm-up
+    eng.reset_slot(0)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    eng.prefill(0, prompt, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist)
+    eng.close()
+    del synth
+    torch.cuda.empty_cache()
+    return ms
+
+
 def max_over_ranks(v, dist):
     """largest value over ranks (NCCL all-reduce on this rank's device)"""
     from qwen35_b200.shard import max_over_ranks as mor
@@ -432,6 +462,10 @@ def main():
             r.close()
             del r
             torch.cuda.empty_cache()
+        for cfg_name, ntok, chunk in (("0.8b", 512, 256), ("4b", 512, 256)):
+            pms = time_prefill(cfg_name, ntok, chunk, args.seed + rank, dist)
+            variants.append({"model": cfg_name, "prefill_tokens": ntok, "chunk": chunk, "ms": pms,
+                             "value": world * ntok / (pms * 1e-3), "unit": "prefill tokens/s"})
 
     if rank == 0:
         hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))

@@ -286,11 +286,26 @@ const float *q35b_engine_layer_out(q35b_engine *e, int li);
 long long q35b_engine_launches_per_step(q35b_engine *e);
 
 /* ---- continuous batching --------------------------------------------- */
+/* One forward over n tokens packed as nrun runs: run r is tokens
+ * [run_end[r-1], run_end[r]) (run_end[-1] = 0), all of one slot at
+ * consecutive positions; a decode token is a run of one, a prompt chunk a
+ * longer run, and one call may mix them (continuous batching; no slot in two
+ * runs).  The GDN recurrence steps each run in order; attention is causal per
+ * token.  next[r] = greedy token after the last token of run r.  Host
+ * arrays; n <= max_batch.  Runs of one token use the step's CUDA graph. */
+int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int nrun,
+                        const int *run_end, int *next, void *stream);
+
+/* Prompt prefill of one slot: ntok tokens from position pos0 as runs of up
+ * to max_batch tokens (src/engine.zig:2078-2177, forwardChunk); *next = greedy token after
+ * the last one. */
+int q35b_engine_prefill(q35b_engine *e, int slot, const int *tokens, int ntok, int pos0, int *next, void *stream);
+
 /* Serve `nseq` independent requests to completion with at most
- * `max_batch` in flight: each step packs one token of every active sequence
- * (a prompt token while it is prefilling, its last sampled token after),
- * admits waiting requests into freed slots, and stops a sequence after
- * n_gen[i] generated tokens.  prompts are concatenated (prompt_off[i],
+ * `max_batch` in flight: each forward packs one token of every decoding
+ * sequence, then chunks of waiting prompts up to the engine's max_batch
+ * tokens (runs, see q35b_engine_forward), admits waiting requests into freed
+ * slots, and stops a sequence after n_gen[i] generated tokens.  prompts are concatenated (prompt_off[i],
  * prompt_len[i]); generated tokens go to out + out_off[i].  Returns 0 or an
  * error; *steps receives the number of engine steps taken. */
 int q35b_serve(q35b_engine *e, int nseq, const int *prompts, const long long *prompt_off, const int *prompt_len,

@@ -210,11 +210,12 @@ struct q35b_engine {
     float *conv_pool = nullptr, *state_pool = nullptr, *kpool = nullptr, *vpool = nullptr;
     long long conv_slot = 0, state_slot = 0, kv_slot = 0;
     // per-step buffers
-    int *d_in = nullptr;  // tokens | slots | pos (3 * max_batch)
+    int *d_in = nullptr;  // tokens | slots | pos | run_end (4 * max_batch)
     int *d_len = nullptr, *d_next = nullptr;
     float *x = nullptr, *qkv = nullptr, *z = nullptr, *ab = nullptr, *gam = nullptr, *gout = nullptr;
     float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;
     float *logits = nullptr, *scores = nullptr, *probe_buf = nullptr;
+    float *xh = nullptr;  // last row of each run, gathered for the model head
     uint8_t *xq = nullptr;
     long long xq_ld = 0;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -253,8 +254,9 @@ inline long long weight_row_bytes(int tt, long long cols) {
     return g.elems ? cols / g.elems * g.bytes : 0;
 }
 
-inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cudaStream_t st) {
-    return launch_k(k_rmsnorm_quant, dim3(n), dim3(256), (size_t)e->c.hidden * 4, st, (const float *)e->x, w,
+inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cudaStream_t st,
+                             const float *src = nullptr) {
+    return launch_k(k_rmsnorm_quant, dim3(n), dim3(256), (size_t)e->c.hidden * 4, st, src ? src : (const float *)e->x, w,
                     e->c.hidden, e->c.rms_eps, fam,
                     e->xq, e->xq_ld, (const int *)nullptr);
 }
@@ -262,15 +264,16 @@ inline int eng_rmsnorm_quant(q35b_engine *e, int n, const float *w, int fam, cud
 // rmsnorm(x) * w -> quantize -> GEMV: one launch where the lane-per-row GEMV
 // takes the matrices (it builds the activation itself), else two
 inline int eng_norm_gemv(q35b_engine *e, int n, const float *w, std::initializer_list<GemvSegDesc> segs,
-                         cudaStream_t st) {
-    const LprPrologue pro{LPR_PRO_NORM, e->x, nullptr, w, (long long)e->c.hidden, e->c.rms_eps};
+                         cudaStream_t st, const float *src = nullptr) {
+    const float *x = src ? src : e->x;
+    const LprPrologue pro{LPR_PRO_NORM, x, nullptr, w, (long long)e->c.hidden, e->c.rms_eps};
     const int rc = gemv_lpr_launch(segs.begin(), (int)segs.size(), nullptr, e->c.hidden, n, st, e->xq_ld, &pro);
     if (rc != -1) return rc;
-    Q35_TRY(eng_rmsnorm_quant(e, n, w, geom_of(segs.begin()->ttype).family, st));
+    Q35_TRY(eng_rmsnorm_quant(e, n, w, geom_of(segs.begin()->ttype).family, st, x));
     return eng_gemv(e, n, segs, e->xq, e->c.hidden, st);
 }
 
-inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
+inline int eng_layer_gdn(q35b_engine *e, int li, int n, int nrun, cudaStream_t st) {
     const q35b_config &c = e->c;
     const LayerW &W = e->L[li];
     const int nv = c.gdn_n_heads, nk = c.gdn_num_k_heads, kd = c.gdn_head_dim;
@@ -301,6 +304,7 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
     g.state_slot = e->state_slot;
     g.slots = e->d_in + e->max_batch;
     g.pos = e->d_in + 2 * e->max_batch;
+    g.run_end = nrun < n ? e->d_in + 3 * e->max_batch : nullptr;
     g.nv = nv;
     g.nk = nk;
     g.eps = c.rms_eps;
@@ -310,7 +314,10 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, cudaStream_t st) {
     g.xq_ld = e->xq_ld;
     g.gout = e->gout;
     g.gout_ld = vdim;
-    Q35_TRY(launch_k(k_gdn_core, dim3(nv, n), dim3(GDN_KD), 0, st, g));
+    Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), 0, st, g));
+    if (g.run_end)
+        Q35_TRY(launch_k(k_gdn_hist_settle, dim3((unsigned)((conv_dim * 3 + 255) / 256), (unsigned)nrun), dim3(256), 0,
+                         st, g.hist, g.hist_slot, conv_dim, g.slots, g.pos, g.run_end));
     if (fo != 32) {
         Q35_TRY(launch_k(k_quant_rows, dim3((vdim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
                          (long long)vdim, vdim, fo, e->xq, e->xq_ld));
@@ -396,7 +403,21 @@ struct PdlScope {
     ~PdlScope() { pdl_enabled() = prev; }
 };
 
-inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
+// gather the last row of each run (x[run_end[r] - 1]) into xh[r]
+__global__ void k_gather_run_rows(const float *x, const int *run_end, float *xh, int cols) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.y;
+    const float *src = x + (long long)(run_end[r] - 1) * cols;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x)
+        xh[(long long)r * cols + i] = src[i];
+}
+
+// n tokens in nrun runs (nrun == n: every token its own run, the decode
+// step; nrun < n: runs of consecutive positions of one sequence each, the
+// boundaries in d_in[3 max_batch ..]); logits / next token for the last
+// token of each run
+inline int eng_step_body(q35b_engine *e, int n, int nrun, int max_len, cudaStream_t st) {
     const PdlScope pdl_scope;
     const q35b_config &c = e->c;
     const long long l0 = launch_count();
@@ -409,7 +430,7 @@ inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
         if (is_full_layer(c, li))
             Q35_TRY(eng_layer_full(e, li, n, max_len, st));
         else
-            Q35_TRY(eng_layer_gdn(e, li, n, st));
+            Q35_TRY(eng_layer_gdn(e, li, n, nrun, st));
         Q35_TRY(eng_mlp(e, li, n, st));
         if (e->probe) {
             Q35_TRY(launch_k(k_copy_rows, dim3(ew_grid((long long)n * c.hidden)), dim3(256), 0, st,
@@ -418,8 +439,15 @@ inline int eng_step_body(q35b_engine *e, int n, int max_len, cudaStream_t st) {
         }
     }
     const Lin &H = e->output.w ? e->output : e->token_embd;
-    Q35_TRY(eng_norm_gemv(e, n, e->output_norm, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, st));
-    const int rc = launch_k(k_argmax, dim3(n), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab,
+    if (nrun < n) {
+        Q35_TRY(launch_k(k_gather_run_rows, dim3((unsigned)((c.hidden + 255) / 256), (unsigned)nrun), dim3(256), 0,
+                         st, (const float *)e->x, (const int *)(e->d_in + 3 * e->max_batch), e->xh, c.hidden));
+        Q35_TRY(eng_norm_gemv(e, nrun, e->output_norm, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, st,
+                              e->xh));
+    } else {
+        Q35_TRY(eng_norm_gemv(e, n, e->output_norm, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, st));
+    }
+    const int rc = launch_k(k_argmax, dim3(nrun), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab,
                             c.vocab, e->d_next);
     e->launches = launch_count() - l0;
     return rc;

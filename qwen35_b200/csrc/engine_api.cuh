@@ -136,7 +136,8 @@ int q35b_engine_finalize(q35b_engine *e) {
     ALLOC(state_pool, 4 * ngdn * S * e->state_slot);
     ALLOC(kpool, 4 * nfull * S * e->kv_slot);
     ALLOC(vpool, 4 * nfull * S * e->kv_slot);
-    ALLOC(d_in, 4 * 3 * B);
+    ALLOC(d_in, 4 * 4 * B);
+    ALLOC(xh, 4 * B * h);
     ALLOC(d_len, 4 * B);
     ALLOC(d_next, 4 * B);
     ALLOC(x, 4 * B * h);
@@ -160,7 +161,7 @@ int q35b_engine_finalize(q35b_engine *e) {
 #undef ALLOC
     Q35_TRY((int)cudaMemset(e->conv_pool, 0, 4 * ngdn * S * e->conv_slot));
     Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));
-    Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 3 * B));
+    Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 4 * B));
     Q35_TRY(gemv_prepare());
     Q35_TRY(gemv_lpr_prepare());
     Q35_TRY(attx_prepare(e->max_seq));
@@ -214,7 +215,7 @@ long long q35b_engine_launches_per_step(q35b_engine *e) { return e ? e->launches
 // Launch the step for `n` sequences whose inputs are already in e->d_in.
 static int engine_run(q35b_engine *e, int n, int max_len, int use_graph, cudaStream_t st) {
     const int bucket = eng_len_bucket(max_len, e->max_seq);
-    if (!use_graph) return eng_step_body(e, n, bucket, st);
+    if (!use_graph) return eng_step_body(e, n, n, bucket, st);
     const long long key = graph_key(n, bucket);
     auto it = e->graphs.find(key);
     if (it == e->graphs.end()) {
@@ -223,7 +224,7 @@ static int engine_run(q35b_engine *e, int n, int max_len, int use_graph, cudaStr
         cudaGraph_t g = nullptr;
         int rc = (int)cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
         if (!rc) {
-            const int brc = eng_step_body(e, n, bucket, cs);
+            const int brc = eng_step_body(e, n, n, bucket, cs);
             rc = (int)cudaStreamEndCapture(cs, &g);
             if (brc) rc = brc;
         }
@@ -312,10 +313,62 @@ int q35b_engine_advance(q35b_engine *e, int n, void *stream) {
     return (int)cudaGetLastError();
 }
 
+// One forward over n tokens in nrun runs (host arrays); see include/q35.h.
+int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int nrun,
+                        const int *run_end, int *next, void *stream) {
+    if (!e || !e->finalized || n <= 0 || n > e->max_batch || nrun <= 0 || nrun > n || !run_end)
+        return (int)cudaErrorInvalidValue;
+    if (run_end[nrun - 1] != n) return (int)cudaErrorInvalidValue;
+    int max_len = 1, b0 = 0;
+    std::vector<char> seen(e->n_slots, 0);
+    for (int r = 0; r < nrun; r++) {
+        const int b1 = run_end[r];
+        if (b1 <= b0) return (int)cudaErrorInvalidValue;
+        const int sl = slots[b0];
+        if (sl < 0 || sl >= e->n_slots || seen[sl]) return (int)cudaErrorInvalidValue;  // one run per slot
+        seen[sl] = 1;
+        for (int i = b0; i < b1; i++) {
+            if (slots[i] != sl || pos[i] < 0 || pos[i] >= e->max_seq) return (int)cudaErrorInvalidValue;
+            if (i > b0 && pos[i] != pos[i - 1] + 1) return (int)cudaErrorInvalidValue;
+            max_len = std::max(max_len, pos[i] + 1);
+        }
+        b0 = b1;
+    }
+    cudaStream_t st = S(stream);
+    const size_t b = (size_t)n * 4;
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in, tokens, b, cudaMemcpyHostToDevice, st));
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in + e->max_batch, slots, b, cudaMemcpyHostToDevice, st));
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in + 2 * e->max_batch, pos, b, cudaMemcpyHostToDevice, st));
+    if (nrun == n) {
+        Q35_TRY(engine_run(e, n, max_len, 1, st));
+    } else {
+        // runs longer than one token (prefill): launched directly, the
+        // launch cost spread over the run's tokens
+        Q35_TRY((int)cudaMemcpyAsync(e->d_in + 3 * e->max_batch, run_end, (size_t)nrun * 4, cudaMemcpyHostToDevice,
+                                     st));
+        Q35_TRY(eng_step_body(e, n, nrun, eng_len_bucket(max_len, e->max_seq), st));
+    }
+    Q35_TRY((int)cudaMemcpyAsync(next, e->d_next, (size_t)nrun * 4, cudaMemcpyDeviceToHost, st));
+    return (int)cudaStreamSynchronize(st);
+}
+
+int q35b_engine_prefill(q35b_engine *e, int slot, const int *tokens, int ntok, int pos0, int *next, void *stream) {
+    if (!e || !e->finalized || ntok <= 0 || pos0 < 0 || pos0 + ntok > e->max_seq) return (int)cudaErrorInvalidValue;
+    std::vector<int> sl(e->max_batch, slot), ps(e->max_batch);
+    for (int t0 = 0; t0 < ntok; t0 += e->max_batch) {
+        const int k = std::min(e->max_batch, ntok - t0);
+        for (int i = 0; i < k; i++) ps[i] = pos0 + t0 + i;
+        const int run_end = k;
+        Q35_TRY(q35b_engine_forward(e, k, tokens + t0, sl.data(), ps.data(), 1, &run_end, next, stream));
+    }
+    return 0;
+}
+
 int q35b_serve(q35b_engine *e, int nseq, const int *prompts, const long long *prompt_off, const int *prompt_len,
                const int *n_gen, int *out, const long long *out_off, int max_batch, long long *steps, void *stream) {
     if (!e || !e->finalized || nseq < 0 || max_batch <= 0) return (int)cudaErrorInvalidValue;
-    max_batch = std::min(max_batch, std::min(e->max_batch, e->n_slots));
+    const int max_seqs = std::min(max_batch, std::min(e->max_batch, e->n_slots));
+    const int budget = e->max_batch;  // tokens per forward
     struct Act { int seq, slot, pos, gen, last; };
     std::deque<int> waiting;
     for (int i = 0; i < nseq; i++) {
@@ -326,40 +379,59 @@ int q35b_serve(q35b_engine *e, int nseq, const int *prompts, const long long *pr
     std::vector<int> free_slots;
     for (int s = e->n_slots - 1; s >= 0; s--) free_slots.push_back(s);
     std::vector<Act> act;
-    std::vector<int> tok, slot, pos, next;
+    std::vector<int> tok, slot, pos, run_end, run_act, next;
     long long nstep = 0;
     cudaStream_t st = S(stream);
     while (!waiting.empty() || !act.empty()) {
-        while ((int)act.size() < max_batch && !waiting.empty() && !free_slots.empty()) {
+        while ((int)act.size() < max_seqs && !waiting.empty() && !free_slots.empty()) {
             const int s = free_slots.back();
             free_slots.pop_back();
             Q35_TRY(q35b_engine_reset_slot(e, s, st));
             act.push_back({waiting.front(), s, 0, 0, -1});
             waiting.pop_front();
         }
-        const int n = (int)act.size();
-        tok.resize(n);
-        slot.resize(n);
-        pos.resize(n);
-        next.resize(n);
-        for (int i = 0; i < n; i++) {
-            const Act &a = act[i];
-            tok[i] = a.pos < prompt_len[a.seq] ? prompts[prompt_off[a.seq] + a.pos] : a.last;
-            slot[i] = a.slot;
-            pos[i] = a.pos;
-        }
-        Q35_TRY(q35b_engine_step_host(e, n, tok.data(), slot.data(), pos.data(), next.data(), st));
-        nstep++;
-        std::vector<Act> keep;
-        for (int i = 0; i < n; i++) {
-            Act a = act[i];
-            const bool emits = a.pos >= prompt_len[a.seq] - 1;
-            a.pos++;
-            if (emits) {
-                out[out_off[a.seq] + a.gen] = next[i];
-                a.gen++;
-                a.last = next[i];
+        // decoding sequences first (one token each), then prompt chunks in
+        // the remaining token budget
+        tok.clear();
+        slot.clear();
+        pos.clear();
+        run_end.clear();
+        run_act.clear();
+        for (int pass = 0; pass < 2; pass++) {
+            for (int i = 0; i < (int)act.size(); i++) {
+                const Act &a = act[i];
+                const int plen = prompt_len[a.seq];
+                const bool decoding = a.pos >= plen;
+                if (decoding != (pass == 0)) continue;
+                const int room = budget - (int)tok.size();
+                if (room <= 0) break;
+                const int k = decoding ? 1 : std::min(plen - a.pos, room);
+                for (int q = 0; q < k; q++) {
+                    tok.push_back(decoding ? a.last : prompts[prompt_off[a.seq] + a.pos + q]);
+                    slot.push_back(a.slot);
+                    pos.push_back(a.pos + q);
+                }
+                run_end.push_back((int)tok.size());
+                run_act.push_back(i);
             }
+        }
+        const int nrun = (int)run_end.size();
+        next.resize(nrun);
+        Q35_TRY(q35b_engine_forward(e, (int)tok.size(), tok.data(), slot.data(), pos.data(), nrun, run_end.data(),
+                                    next.data(), st));
+        nstep++;
+        for (int r = 0; r < nrun; r++) {
+            Act &a = act[run_act[r]];
+            const int k = run_end[r] - (r ? run_end[r - 1] : 0);
+            a.pos += k;
+            if (a.pos >= prompt_len[a.seq]) {  // the run reached the last prompt token or decoded
+                out[out_off[a.seq] + a.gen] = next[r];
+                a.gen++;
+                a.last = next[r];
+            }
+        }
+        std::vector<Act> keep;
+        for (const Act &a : act) {
             if (a.gen >= n_gen[a.seq])
                 free_slots.push_back(a.slot);
             else

@@ -117,6 +117,7 @@ struct GdnCoreArgs {
     float *state;
     long long state_slot;
     const int *slots, *pos;
+    const int *run_end;   // null: token b is its own run; else run r = tokens [run_end[r-1], run_end[r])
     int nv, nk;
     float eps, qscale;
     int fam;              // activation family of ssm_out (32: quantize here)
@@ -131,107 +132,140 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     pdl_wait();
     __shared__ float sq[GDN_KD], sk[GDN_KD], so[GDN_KD];
     __shared__ float s_scal[4];
-    const int h = blockIdx.x, b = blockIdx.y, j = threadIdx.x;
+    const int h = blockIdx.x, r = blockIdx.y, j = threadIdx.x;
     const int kd = GDN_KD, kq = a.nk * kd, conv_dim = 2 * kq + a.nv * kd;
     const int kh = h % a.nk;
-    const long long slot = a.slots[b];
-    const int p = a.pos[b];
-    const float *hin = a.hist + slot * a.hist_slot + (long long)(p & 1) * conv_dim * 3;
-    float *hout = a.hist + slot * a.hist_slot + (long long)((p + 1) & 1) * conv_dim * 3;
-    const float *raw = a.qkv + (long long)b * a.qkv_ld;
+    // the run: consecutive positions of one sequence, stepped in order
+    const int i0 = a.run_end ? (r == 0 ? 0 : a.run_end[r - 1]) : r;
+    const int i1 = a.run_end ? a.run_end[r] : r + 1;
+    const long long slot = a.slots[i0];
+    const int p0 = a.pos[i0];
+    // history: read the buffer of the run's first position's parity, write
+    // the other one -- CTAs of value heads sharing a k head read the q / k
+    // history at their start, so nothing may write that buffer during the
+    // kernel.  A run of even length ends on its first parity: k_gdn_hist_settle
+    // moves the result there afterwards.
+    const float *hin = a.hist + slot * a.hist_slot + (long long)(p0 & 1) * conv_dim * 3;
+    float *hout = a.hist + slot * a.hist_slot + (long long)((p0 & 1) ^ 1) * conv_dim * 3;
 
-    // every global load this CTA needs, issued up front so their latencies
-    // overlap: the state column, the conv taps / history / inputs, the gate
-    // and norm operands
+    // loads that do not depend on the token, issued up front so their
+    // latencies overlap: the state column, conv taps and history, the norm
     float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
     float col[GDN_KD];
 #pragma unroll
     for (int i = 0; i < GDN_KD; i++) col[i] = S[(long long)i * GDN_KD + j];
     const int chq = kh * kd + j, chk = kq + kh * kd + j, chv = 2 * kq + h * kd + j;
-    float hq[3], hk[3], hv[3], wq[4], wk[4], wv[4];
+    // conv history and taps of this thread's q / k / v channels, kept in
+    // shared memory (the state column already takes the registers)
+    __shared__ float s_h[3][3][GDN_KD], s_w[3][4][GDN_KD];
+    const int chs[3] = {chq, chk, chv};
 #pragma unroll
-    for (int i = 0; i < 3; i++) {
-        hq[i] = hin[(long long)chq * 3 + i];
-        hk[i] = hin[(long long)chk * 3 + i];
-        hv[i] = hin[(long long)chv * 3 + i];
-    }
+    for (int c = 0; c < 3; c++) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        wq[i] = a.conv_w[(long long)chq * 4 + i];
-        wk[i] = a.conv_w[(long long)chk * 4 + i];
-        wv[i] = a.conv_w[(long long)chv * 4 + i];
+        for (int i = 0; i < 3; i++) s_h[c][i][j] = hin[(long long)chs[c] * 3 + i];
+#pragma unroll
+        for (int i = 0; i < 4; i++) s_w[c][i][j] = a.conv_w[(long long)chs[c] * 4 + i];
     }
-    const float cq = raw[chq], ck = raw[chk], cv = raw[chv];
-    const float zj = a.z[(long long)b * a.z_ld + (long long)h * kd + j];
     const float nwj = a.ssm_norm[j];
-    const float *ar = a.ab + (long long)b * a.ab_ld;
-    const float a_raw = ar[h], b_raw = ar[a.nv + h], ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
+    const float ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
 
-    // causal conv k=4 + silu: y = w0*h0 + w1*h1 + w2*h2 + w3*x, left to right
-    auto conv = [&](const float (&hh)[3], const float (&w)[4], float cur) {
-        const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(hh[0], w[0]), __fmul_rn(hh[1], w[1])),
-                                            __fmul_rn(hh[2], w[2])),
-                                  __fmul_rn(cur, w[3]));
+    // causal conv k=4 + silu: y = w0*h0 + w1*h1 + w2*h2 + w3*x, left to right;
+    // then the history shifts in x
+    auto conv = [&](int c, float cur) {
+        const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(s_h[c][0][j], s_w[c][0][j]),
+                                                      __fmul_rn(s_h[c][1][j], s_w[c][1][j])),
+                                            __fmul_rn(s_h[c][2][j], s_w[c][2][j])),
+                                  __fmul_rn(cur, s_w[c][3][j]));
+        s_h[c][0][j] = s_h[c][1][j];
+        s_h[c][1][j] = s_h[c][2][j];
+        s_h[c][2][j] = cur;
         return silu_f(s);
     };
-    auto shift = [&](int ch, const float (&hh)[3], float cur) {
-        float *ho = hout + (long long)ch * 3;
-        ho[0] = hh[1];
-        ho[1] = hh[2];
-        ho[2] = cur;
-    };
-    if (h < a.nk) {  // the owner of a k head's q / k channels advances their history
-        shift(chq, hq, cq);
-        shift(chk, hk, ck);
-    }
-    shift(chv, hv, cv);
-    sq[j] = conv(hq, wq, cq);
-    sk[j] = conv(hk, wk, ck);
-    const float vj = conv(hv, wv, cv);
-    __syncthreads();
-    if (j == 0) s_scal[0] = serial_sumsq(sq, kd);
-    if (j == 32) s_scal[1] = serial_sumsq(sk, kd);
-    if (j == 64) {
-        s_scal[2] = sigmoid_f(b_raw);
-        s_scal[3] = exp_f(__fmul_rn(ssm_a, softplus_f(__fadd_rn(a_raw, dtb))));
-    }
-    __syncthreads();
-    const float iq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[0], 1e-6f)));
-    const float ik = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[1], 1e-6f)));
-    const float qj = __fmul_rn(__fmul_rn(sq[j], iq), a.qscale);
-    const float kj = __fmul_rn(sk[j], ik);
-    const float be = s_scal[2], g = s_scal[3];
-    __syncthreads();
-    sq[j] = qj;
-    sk[j] = kj;
-    __syncthreads();
-    float acc = 0.0f;
+    for (int b = i0; b < i1; b++) {
+        const float *raw = a.qkv + (long long)b * a.qkv_ld;
+        const float cq = raw[chq], ck = raw[chk], cv = raw[chv];
+        const float zj = a.z[(long long)b * a.z_ld + (long long)h * kd + j];
+        const float *ar = a.ab + (long long)b * a.ab_ld;
+        const float a_raw = ar[h], b_raw = ar[a.nv + h];
+        sq[j] = conv(0, cq);
+        sk[j] = conv(1, ck);
+        const float vj = conv(2, cv);
+        __syncthreads();
+        if (j == 0) s_scal[0] = serial_sumsq(sq, kd);
+        if (j == 32) s_scal[1] = serial_sumsq(sk, kd);
+        if (j == 64) {
+            s_scal[2] = sigmoid_f(b_raw);
+            s_scal[3] = exp_f(__fmul_rn(ssm_a, softplus_f(__fadd_rn(a_raw, dtb))));
+        }
+        __syncthreads();
+        const float iq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[0], 1e-6f)));
+        const float ik = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_scal[1], 1e-6f)));
+        const float qj = __fmul_rn(__fmul_rn(sq[j], iq), a.qscale);
+        const float kj = __fmul_rn(sk[j], ik);
+        const float be = s_scal[2], g = s_scal[3];
+        __syncthreads();
+        sq[j] = qj;
+        sk[j] = kj;
+        __syncthreads();
+        float acc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < GDN_KD; i++) acc = __fadd_rn(acc, __fmul_rn(col[i], sk[i]));
-    const float km = __fmul_rn(acc, g);
-    const float d = __fmul_rn(__fsub_rn(vj, km), be);
-    float o = 0.0f;
+        for (int i = 0; i < GDN_KD; i++) acc = __fadd_rn(acc, __fmul_rn(col[i], sk[i]));
+        const float km = __fmul_rn(acc, g);
+        const float d = __fmul_rn(__fsub_rn(vj, km), be);
+        float o = 0.0f;
 #pragma unroll
-    for (int i = 0; i < GDN_KD; i++) {
-        const float nvv = __fadd_rn(__fmul_rn(col[i], g), __fmul_rn(sk[i], d));
-        col[i] = nvv;
-        o = __fadd_rn(o, __fmul_rn(nvv, sq[i]));
+        for (int i = 0; i < GDN_KD; i++) {
+            const float nvv = __fadd_rn(__fmul_rn(col[i], g), __fmul_rn(sk[i], d));
+            col[i] = nvv;
+            o = __fadd_rn(o, __fmul_rn(nvv, sq[i]));
+        }
+        so[j] = o;
+        __syncthreads();
+        if (j == 0) s_scal[0] = serial_sumsq(so, kd);
+        __syncthreads();
+        const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s_scal[0], (float)kd), a.eps)));
+        float y = __fmul_rn(__fmul_rn(o, sc), nwj);
+        y = __fmul_rn(y, silu_f(zj));
+        if (a.fam == 32) {
+            const int w = j >> 5;
+            quant_q8_0_warp(y, a.xq + (long long)b * a.xq_ld + (long long)(h * (kd / 32) + w) * 34, j & 31);
+        } else {
+            a.gout[(long long)b * a.gout_ld + (long long)h * kd + j] = y;
+        }
+        __syncthreads();  // s_scal / sq / sk / so reused by the next token
     }
 #pragma unroll
     for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
-    so[j] = o;
-    __syncthreads();
-    if (j == 0) s_scal[0] = serial_sumsq(so, kd);
-    __syncthreads();
-    const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s_scal[0], (float)kd), a.eps)));
-    float y = __fmul_rn(__fmul_rn(o, sc), nwj);
-    y = __fmul_rn(y, silu_f(zj));
-    if (a.fam == 32) {
-        const int w = j >> 5;
-        quant_q8_0_warp(y, a.xq + (long long)b * a.xq_ld + (long long)(h * (kd / 32) + w) * 34, j & 31);
-    } else {
-        a.gout[(long long)b * a.gout_ld + (long long)h * kd + j] = y;
+    // the history after the run, for the position after it; the owner of a
+    // k head's q / k channels writes those
+    auto store = [&](int c) {
+        float *ho = hout + (long long)chs[c] * 3;
+        ho[0] = s_h[c][0][j];
+        ho[1] = s_h[c][1][j];
+        ho[2] = s_h[c][2][j];
+    };
+    if (h < a.nk) {
+        store(0);
+        store(1);
     }
+    store(2);
+}
+
+// after k_gdn_core over runs: a run of even length wrote its final conv
+// history to the buffer of the other parity; move it to the parity of the
+// position after the run (its first position's), where the next step reads it
+__global__ void k_gdn_hist_settle(float *hist, long long hist_slot, int conv_dim, const int *slots, const int *pos,
+                                  const int *run_end) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.y;
+    const int i0 = r == 0 ? 0 : run_end[r - 1], i1 = run_end[r];
+    if ((i1 - i0) & 1) return;
+    const int p0 = pos[i0];
+    float *base = hist + (long long)slots[i0] * hist_slot;
+    const float *src = base + (long long)((p0 & 1) ^ 1) * conv_dim * 3;
+    float *dst = base + (long long)(p0 & 1) * conv_dim * 3;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < conv_dim * 3; i += gridDim.x * blockDim.x) dst[i] = src[i];
 }
 
 }  // namespace q35

@@ -60,8 +60,8 @@ constexpr int MMQ_X_STAGE = MMQ_N * 272;                    // raw activation ch
 constexpr int MMQ_OFF_A = 0;                                // A operands: KB x (128 x 32 B)
 constexpr int MMQ_OFF_B = MMQ_OFF_A + MMQ_KB * MMQ_M * 32;  // B operands: KB x (64 x 32 B)
 constexpr int MMQ_OFF_DW = MMQ_OFF_B + MMQ_KB * MMQ_N * 32; // f32 [KB][128]
-constexpr int MMQ_OFF_DX = MMQ_OFF_DW + MMQ_KB * MMQ_M * 4; // f32 [KB][64]
-constexpr int MMQ_OFF_RAW = MMQ_OFF_DX + MMQ_KB * MMQ_N * 4;
+constexpr int MMQ_OFF_DX = MMQ_OFF_DW + MMQ_KB * MMQ_M * 4; // f32 [2][KB][64] (by chunk parity)
+constexpr int MMQ_OFF_RAW = MMQ_OFF_DX + 2 * MMQ_KB * MMQ_N * 4;
 constexpr int MMQ_OFF_BAR = MMQ_OFF_RAW + MMQ_NS * (MMQ_W_STAGE + MMQ_X_STAGE);
 constexpr int MMQ_SMEM = MMQ_OFF_BAR + 128 + 1024;          // + barriers, + alignment slack
 
@@ -276,25 +276,30 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
             const int s = c % MMQ_NS;
             const uint8_t *wst = raw + s * (MMQ_W_STAGE + MMQ_X_STAGE);
             if (!s_fail && !mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 122)) s_fail = 1;
+            float *dxc = sDX + (c & 1) * MMQ_KB * MMQ_N;  // chunk c's activation scales
             if (!s_fail) {
-                // weights: thread `ct` converts row `ct`
+                // weights: each thread converts the row it folds later (its
+                // block scales are then read by the thread that wrote them)
                 auto putw = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
                     uint8_t *dst = sA + b * MMQ_M * 32;
-                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                    sDW[b * MMQ_M + ct] = f16_to_f32(d);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                    sDW[b * MMQ_M + row] = f16_to_f32(d);
                 };
                 if (sg.ttype == TT_Q8_0)
-                    unpack_q8_0_chunk(wst + ct * sg.chunk_bytes, putw);
+                    unpack_q8_0_chunk(wst + row * sg.chunk_bytes, putw);
                 else
-                    unpack_iq4_nl_chunk(wst + ct * sg.chunk_bytes, putw);
-                // activations: threads 0..63 convert token rows
+                    unpack_iq4_nl_chunk(wst + row * sg.chunk_bytes, putw);
+                // activations: threads 0..63 convert token rows; their scales
+                // are read by every thread, so they alternate between two
+                // buffers (a writer of chunk c+2 has passed chunk c+1's
+                // barrier, which every reader of chunk c reached after its fold)
                 if (ct < MMQ_N) {
                     auto putx = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
                         uint8_t *dst = sB + b * MMQ_N * 32;
                         *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
                         *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                        sDX[b * MMQ_N + ct] = f16_to_f32(d);
+                        dxc[b * MMQ_N + ct] = f16_to_f32(d);
                     };
                     unpack_q8_0_chunk(wst + MMQ_W_STAGE + ct * 272, putx);
                 }
@@ -314,7 +319,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
                     for (int kb = 0; kb < MMQ_RB; kb++) {
                         const int b = round * MMQ_RB + kb;
                         const float dw = sDW[b * MMQ_M + row];
-                        const float *dx = sDX + b * MMQ_N;
+                        const float *dx = dxc + b * MMQ_N;
 #pragma unroll
                         for (int half = 0; half < MMQ_N / 32; half++) {
                             uint32_t d[32];
@@ -364,6 +369,269 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------
+// K-quant weights (Q4_K, Q5_K) x Q8_K activations.  A 256-element block has
+// 8 sub-blocks with 6-bit scales sc_j and mins m_j (kernels256.c:474-498,
+// 605-629):  isum = sum_j sc_j * dot_j,  summs = sum_j m_j * bsum_j,
+// sumf += (dy*d)*isum - (dy*dmin)*summs.  One MMA per sub-block (K = 32) into
+// its own 64-column TMEM region (8 regions = 512 columns); the epilogue forms
+// isum / summs in exact integer arithmetic, then the f32 fold.  Chunk = one
+// block (256 columns); the Q8_K activation rows (292 B, only 4-byte aligned)
+// are read by the converter threads directly.
+// ---------------------------------------------------------------------------
+constexpr int MMQK_TMEM_COLS = 8 * MMQ_N;                    // 512
+constexpr int MMQK_W_STAGE = MMQ_M * 176;                    // raw weight block rows (Q5_K size)
+constexpr int MMQK_OFF_A = 0;                                // 8 sub-blocks x (128 x 32 B)
+constexpr int MMQK_OFF_B = MMQK_OFF_A + 8 * MMQ_M * 32;      // 8 sub-blocks x (64 x 32 B)
+constexpr int MMQK_OFF_SC = MMQK_OFF_B + 8 * MMQ_N * 32;     // int [8][128] scales
+constexpr int MMQK_OFF_MN = MMQK_OFF_SC + 8 * MMQ_M * 4;     // int [8][128] mins
+constexpr int MMQK_OFF_D = MMQK_OFF_MN + 8 * MMQ_M * 4;      // f32 [128] d, [128] dmin
+constexpr int MMQK_OFF_DY = MMQK_OFF_D + 2 * MMQ_M * 4;      // f32 [2][64] activation scales (by block parity)
+constexpr int MMQK_OFF_BS = MMQK_OFF_DY + 2 * MMQ_N * 4;     // int [2][8][64] sub-block sums
+constexpr int MMQK_OFF_RAW = MMQK_OFF_BS + 2 * 8 * MMQ_N * 4;
+constexpr int MMQK_OFF_BAR = MMQK_OFF_RAW + MMQ_NS * MMQK_W_STAGE;
+constexpr int MMQK_SMEM = MMQK_OFF_BAR + 128 + 1024;
+
+struct MmqkArgs {
+    CUtensorMap wmap[GV_MAX_SEG];   // weights: [rows][row_bytes/8] u64, box 128 rows x one block
+    MmqSeg seg[GV_MAX_SEG];
+    int nseg;
+    long long total_tiles;
+    const uint8_t *xq;              // Q8_K activation rows
+    long long xq_ld;
+    int ntok, nblk;                 // tokens, 256-element blocks per row
+};
+
+__global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = sm + MMQK_OFF_A, *sB = sm + MMQK_OFF_B;
+    int *sSC = reinterpret_cast<int *>(sm + MMQK_OFF_SC), *sMN = reinterpret_cast<int *>(sm + MMQK_OFF_MN);
+    float *sD = reinterpret_cast<float *>(sm + MMQK_OFF_D), *sDY = reinterpret_cast<float *>(sm + MMQK_OFF_DY);
+    int *sBS = reinterpret_cast<int *>(sm + MMQK_OFF_BS);
+    uint8_t *raw = sm + MMQK_OFF_RAW;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + MMQK_OFF_BAR);
+    uint64_t *empty = full + MMQ_NS;
+    uint64_t *mma_bar = empty + MMQ_NS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 1);
+    __shared__ int s_fail;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int issued = 0, ncommit = 0;
+    const long long tile = blockIdx.x;
+    const int t0 = blockIdx.y * MMQ_N;
+    int sgi = 0;
+#pragma unroll
+    for (int i = 1; i < GV_MAX_SEG; i++)
+        if (i < a.nseg && tile >= a.seg[i].tile_begin) sgi = i;
+    const MmqSeg &sg = a.seg[sgi];
+    const long long r0 = (tile - sg.tile_begin) * MMQ_M;
+    const bool q5 = sg.ttype == TT_Q5_K;
+    const uint32_t idesc = MMQ_IDESC;
+
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < MMQ_NS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 4);
+        }
+        mbar_init(mma_bar, 1);
+        s_fail = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(MMQK_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes);
+            for (int c = 0; c < a.nblk; c++, issued++) {
+                const int s = c % MMQ_NS;
+                if (c >= MMQ_NS && !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 131)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], wbytes);
+                tma_load_2d(raw + s * MMQK_W_STAGE, &a.wmap[sgi], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        for (int c = 0; c < a.nblk; c++) {
+            named_bar_sync(1, 160);  // operands of block c converted, TMEM of block c-1 read
+            tc_fence_after();
+            if (lane == 0 && !s_fail) {
+                for (int j = 0; j < 8; j++) {
+                    const uint64_t ad = umma_desc(sA + j * MMQ_M * 32, 128, 256);
+                    const uint64_t bd = umma_desc(sB + j * MMQ_N * 32, 128, 256);
+                    umma_i8(tmem + (uint32_t)(j * MMQ_N), ad, bd, idesc, 0u);
+                }
+                umma_commit(mma_bar);
+                ncommit++;
+            }
+            __syncwarp();
+        }
+    } else {
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const int ct = threadIdx.x - 64;
+        float acc[MMQ_N];
+#pragma unroll
+        for (int t = 0; t < MMQ_N; t++) acc[t] = 0.0f;
+        for (int c = 0; c < a.nblk; c++) {
+            const int s = c % MMQ_NS;
+            // activations of block c (global -> operand layout), independent of the weight TMA
+            {
+                const int tk = ct & (MMQ_N - 1), h = ct >> 6;  // token, half (sub-blocks 4h .. 4h+3)
+                const bool live = t0 + tk < a.ntok;
+                const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)c * 292;
+                uint32_t w[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    w[i] = live ? reinterpret_cast<const uint32_t *>(src + 4 + 128 * h)[i] : 0u;
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    uint8_t *dst = sB + (4 * h + jj) * MMQ_N * 32;
+                    *reinterpret_cast<uint4 *>(dst + umma_off(tk, 0)) =
+                        make_uint4(w[8 * jj], w[8 * jj + 1], w[8 * jj + 2], w[8 * jj + 3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(tk, 1)) =
+                        make_uint4(w[8 * jj + 4], w[8 * jj + 5], w[8 * jj + 6], w[8 * jj + 7]);
+                }
+                // per-token values alternate between two buffers (see k_mmq)
+                if (h == 0) {
+                    sDY[(c & 1) * MMQ_N + tk] = live ? *reinterpret_cast<const float *>(src) : 0.0f;
+                    const int16_t *bs = reinterpret_cast<const int16_t *>(src + 260);
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        sBS[((c & 1) * 8 + j) * MMQ_N + tk] = live ? (int)bs[2 * j] + (int)bs[2 * j + 1] : 0;
+                }
+            }
+            if (!s_fail && !mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 132)) s_fail = 1;
+            if (!s_fail) {
+                // weights: each thread converts the row it folds later
+                const uint8_t *rp = raw + s * MMQK_W_STAGE + row * sg.chunk_bytes;
+                uint32_t W[44];
+                const uint4 *v4 = reinterpret_cast<const uint4 *>(rp);
+#pragma unroll
+                for (int i = 0; i < 9; i++) {
+                    const uint4 v = v4[i];
+                    W[4 * i] = v.x;
+                    W[4 * i + 1] = v.y;
+                    W[4 * i + 2] = v.z;
+                    W[4 * i + 3] = v.w;
+                }
+                if (q5) {
+#pragma unroll
+                    for (int i = 9; i < 11; i++) {
+                        const uint4 v = v4[i];
+                        W[4 * i] = v.x;
+                        W[4 * i + 1] = v.y;
+                        W[4 * i + 2] = v.z;
+                        W[4 * i + 3] = v.w;
+                    }
+                }
+                sD[row] = f16_lo(W[0]);
+                sD[MMQ_M + row] = f16_hi(W[0]);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    int sc, mn;
+                    kq_scale_min_w(j, W + 1, sc, mn);
+                    sSC[j * MMQ_M + row] = sc;
+                    sMN[j * MMQ_M + row] = mn;
+                    const int cq = j >> 1;
+                    uint32_t o[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const uint32_t ql = q5 ? W[12 + 8 * cq + i] : W[4 + 8 * cq + i];
+                        uint32_t v = (j & 1) ? (ql >> 4) & 0x0F0F0F0Fu : ql & 0x0F0F0F0Fu;
+                        if (q5) v |= ((W[4 + i] >> j) & 0x01010101u) << 4;
+                        o[i] = v;
+                    }
+                    uint8_t *dst = sA + j * MMQ_M * 32;
+                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 0)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            fence_proxy_async_smem();
+            tc_fence_before();
+            named_bar_sync(1, 160);
+            if (!s_fail && !mbar_wait(mma_bar, (uint32_t)(c & 1), 133)) s_fail = 1;
+            tc_fence_after();
+            if (!s_fail) {
+                const float dw = sD[row], dmw = sD[MMQ_M + row];
+                int sc[8], mn[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    sc[j] = sSC[j * MMQ_M + row];
+                    mn[j] = sMN[j * MMQ_M + row];
+                }
+#pragma unroll
+                for (int half = 0; half < MMQ_N / 32; half++) {
+                    int is[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) is[i] = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        uint32_t d[32];
+                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * MMQ_N + half * 32), d);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) is[i] += sc[j] * (int)d[i];
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const int t = half * 32 + i;
+                        int ms = 0;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) ms += mn[j] * sBS[((c & 1) * 8 + j) * MMQ_N + t];
+                        // d = dy*d_w; dmin = dy*dmin_w; sumf += d*isum - dmin*sumi
+                        const float dy = sDY[(c & 1) * MMQ_N + t];
+                        const float d = __fmul_rn(dy, dw), dm = __fmul_rn(dy, dmw);
+                        acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d, __int2float_rn(is[i])),
+                                                             __fmul_rn(dm, __int2float_rn(ms))));
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        const long long r = r0 + row;
+        if (!s_fail && r < sg.rows) {
+            const int nt = min(MMQ_N, a.ntok - t0);
+#pragma unroll
+            for (int t = 0; t < MMQ_N; t++) {
+                if (t < nt) {
+                    float *o = sg.out + (long long)(t0 + t) * sg.out_ld + r;
+                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (s_fail) {
+        if (warp == 0 && lane == 0)
+            for (int c = issued > MMQ_NS ? issued - MMQ_NS : 0; c < issued; c++)
+                if (!mbar_wait(&full[c % MMQ_NS], (uint32_t)((c / MMQ_NS) & 1), 134)) break;
+        if (warp == 1 && lane == 0 && ncommit > 0) mbar_wait(mma_bar, (uint32_t)((ncommit - 1) & 1), 135);
+        if (threadIdx.x == 0) set_error(130);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(MMQK_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 inline bool mmq_encode(CUtensorMap *m, const void *base, long long rows, long long row_stride, int row_bytes,
@@ -382,18 +650,60 @@ inline bool mmq_encode(CUtensorMap *m, const void *base, long long rows, long lo
 inline int mmq_prepare() {
     static int done = 0;
     if (done) return 0;
-    const cudaError_t e = cudaFuncSetAttribute(k_mmq, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_mmq, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_mmq_kq, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM);
     if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;
 }
 
-// Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL weights with
-// 16-byte-aligned rows and an API-layout Q8_0 activation at a 16-byte
-// multiple stride.  Returns -1 (nothing launched) when not eligible.
+// K-quant (Q4_K / Q5_K) weights x Q8_K activations; -1 when not eligible
+inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
+                         long long xq_ld) {
+    const long long act_row = (long long)(cols / 256) * 292;
+    const long long ld = xq_ld > 0 ? xq_ld : act_row;
+    if ((reinterpret_cast<uintptr_t>(xq) & 3u) || (ld & 3)) return -1;
+    MmqkArgs a{};
+    long long tiles = 0;
+    for (int i = 0; i < nseg; i++) {
+        const int tt = segs[i].ttype;
+        if (tt != TT_Q4_K && tt != TT_Q5_K) return -1;
+        const Geom g = geom_of(tt);
+        const int rb = cols / 256 * g.bytes;
+        if (rb % 16 || (reinterpret_cast<uintptr_t>(segs[i].w) & 15u)) return -1;
+        MmqSeg &s = a.seg[i];
+        s.out = segs[i].out;
+        s.rows = segs[i].rows;
+        s.out_ld = segs[i].out_ld;
+        s.ttype = tt;
+        s.row_bytes = rb;
+        s.chunk_bytes = g.bytes;  // 144 / 176
+        s.mode = segs[i].mode;
+        s.tile_begin = tiles;
+        tiles += (s.rows + MMQ_M - 1) / MMQ_M;
+        if (!mmq_encode(&a.wmap[i], segs[i].w, s.rows, rb, rb, s.chunk_bytes, MMQ_M)) return -1;
+    }
+    if (tiles == 0) return 0;
+    a.nseg = nseg;
+    a.total_tiles = tiles;
+    a.xq = reinterpret_cast<const uint8_t *>(xq);
+    a.xq_ld = ld;
+    a.ntok = ntok;
+    a.nblk = cols / 256;
+    Q35_TRY_RC(mmq_prepare());
+    const dim3 grid((unsigned)tiles, (unsigned)((ntok + MMQ_N - 1) / MMQ_N));
+    return launch_k(k_mmq_kq, grid, dim3(MMQ_THREADS), (size_t)MMQK_SMEM, st, a);
+}
+
+// Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL (Q8_0
+// activation at a 16-byte multiple stride) or Q4_K / Q5_K (Q8_K activation)
+// weights with 16-byte-aligned rows.  Returns -1 (nothing launched) when not
+// eligible.
 inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
                       long long xq_ld) {
     if (ntok < MMQ_MIN_TOK || nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || cols % 256 != 0) return -1;
+    if (geom_of(segs[0].ttype).family == 256) return mmq_kq_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
     const long long act_row = (long long)(cols / 32) * 34;
     const long long ld = xq_ld > 0 ? xq_ld : act_row;
     if ((reinterpret_cast<uintptr_t>(xq) & 15u) || (ld & 15)) return -1;

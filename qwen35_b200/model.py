@@ -210,6 +210,24 @@ class Engine:
         check(self.L.q35b_engine_step_host(self.h, n, t, s, p, nx, _stream(stream)), "step_host")
         return list(nx)
 
+    def forward(self, tokens, slots, pos, run_end, stream=None):
+        """one forward over runs (q35b_engine_forward); returns the next token
+        of every run"""
+        n, nrun = len(tokens), len(run_end)
+        arr = ctypes.c_int * n
+        nx = (ctypes.c_int * nrun)()
+        check(self.L.q35b_engine_forward(self.h, n, arr(*tokens), arr(*slots), arr(*pos), nrun,
+                                         (ctypes.c_int * nrun)(*run_end), nx, _stream(stream)), "forward")
+        return list(nx)
+
+    def prefill(self, slot, tokens, pos0=0, stream=None):
+        """prompt prefill of one slot (q35b_engine_prefill); returns the greedy
+        token after the last prompt token"""
+        nx = ctypes.c_int(0)
+        check(self.L.q35b_engine_prefill(self.h, slot, (ctypes.c_int * len(tokens))(*tokens), len(tokens), pos0,
+                                         ctypes.byref(nx), _stream(stream)), "prefill")
+        return nx.value
+
     def step(self, d_tokens, d_slots, d_pos, d_next, d_logits=None, use_graph=True, stream=None):
         """device int32 tensors (n,) -> writes d_next (and d_logits n x vocab)"""
         n = d_tokens.numel()

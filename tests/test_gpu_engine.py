@@ -153,6 +153,54 @@ def test_batch_20_equals_single(q35, cfg_name):
     eng.close()
 
 
+@pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed"])
+def test_prefill_chunks_equal_token_steps(q35, cfg_name):
+    """a 37-token prompt prefilled in runs of up to 16 tokens (chunked GDN
+    recurrence, causal attention over the run) leaves the slot exactly as 37
+    single-token steps: same next token, same 6 decoded tokens after it"""
+    cfg = q35.CONFIGS[cfg_name]
+    synth = q35.SyntheticModel(cfg, seed=12)
+    eng = q35.Engine(synth, n_slots=2, max_seq=64, max_batch=16)
+    rng = np.random.default_rng(12)
+    prompt = [int(t) for t in rng.integers(0, cfg.vocab, 37)]
+    eng.reset_slot(0)
+    nxt = eng.prefill(0, prompt)
+    got = [nxt]
+    for pos in range(len(prompt), len(prompt) + 6):
+        got.append(eng.step_host([got[-1]], [0], [pos])[0])
+    eng.reset_slot(1)
+    ref = []
+    for pos, t in enumerate(prompt):
+        r = eng.step_host([t], [1], [pos])[0]
+    ref.append(r)
+    for pos in range(len(prompt), len(prompt) + 6):
+        ref.append(eng.step_host([ref[-1]], [1], [pos])[0])
+    assert got == ref
+    eng.close()
+
+
+def test_forward_mixes_prefill_and_decode_runs(q35):
+    """one forward with a decode token of sequence A and a 9-token prompt run of
+    sequence B gives each the token it gets alone"""
+    cfg = q35.CONFIGS["tiny-mixed"]
+    synth = q35.SyntheticModel(cfg, seed=13)
+    eng = q35.Engine(synth, n_slots=4, max_seq=64, max_batch=16)
+    rng = np.random.default_rng(13)
+    pa = [int(t) for t in rng.integers(0, cfg.vocab, 5)]
+    pb = [int(t) for t in rng.integers(0, cfg.vocab, 9)]
+    for s in range(4):
+        eng.reset_slot(s)
+    # A: prompt in slot 0, then one decode token mixed with B's prompt in slot 1
+    na = eng.prefill(0, pa)
+    mixed = eng.forward([na] + pb, [0] + [1] * 9, [len(pa)] + list(range(9)), [1, 10])
+    # alone: A in slot 2, B in slot 3
+    eng.prefill(2, pa)
+    a_alone = eng.step_host([na], [2], [len(pa)])[0]
+    b_alone = eng.prefill(3, pb)
+    assert mixed == [a_alone, b_alone]
+    eng.close()
+
+
 def test_graph_equals_direct(q35):
     cfg = q35.CONFIGS["tiny"]
     synth = q35.SyntheticModel(cfg, seed=2)
@@ -192,6 +240,7 @@ def test_serve_continuous_batching(q35):
         res = (ctypes.c_int * g)()
         n = O.q35o_generate(m, arr, len(p), g, res)
         assert n == g and list(res) == out
-    assert steps >= max(len(p) + g - 1 for p, g in zip(prompts, n_gen))
+    # prompts are prefilled in chunks, so fewer forwards than tokens
+    assert 0 < steps <= sum(len(p) + g - 1 for p, g in zip(prompts, n_gen))
     O.q35o_model_destroy(m)
     eng.close()

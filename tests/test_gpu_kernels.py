@@ -151,12 +151,13 @@ def test_gemv_bit_exact(L, O, name, tokens):
     assert_no_kernel_error(L)
 
 
-@pytest.mark.parametrize("name", ["Q8_0", "IQ4_NL"])
+@pytest.mark.parametrize("name", ["Q8_0", "IQ4_NL", "Q4_K", "Q5_K"])
 @pytest.mark.parametrize("tokens", [16, 37, 64, 100])
 def test_mmq_tensor_core_bit_exact(L, O, name, tokens):
-    """>= 16 tokens of Q8_0 / IQ4_NL go to the tcgen05 MMQ: the int8 block dots
-    on the tensor core, the f32 fold in block order on the CUDA cores --
-    bit-exact with the reference scalar tier like the decode GEMV"""
+    """>= 16 tokens of Q8_0 / IQ4_NL / Q4_K / Q5_K go to the tcgen05 MMQ: the
+    int8 (sub-)block dots on the tensor core, scales, mins and the f32 fold in
+    block order on the CUDA cores -- bit-exact with the reference scalar tier
+    like the decode GEMV"""
     for rows, cols in [(300, 1024), (129, 2048), (1000, 768), (128, 256)]:
         got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + 7 * tokens)
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
