@@ -286,6 +286,20 @@ const float *q35b_engine_layer_out(q35b_engine *e, int li);
 long long q35b_engine_launches_per_step(q35b_engine *e);
 
 /* ---- continuous batching --------------------------------------------- */
+/* Tensor parallelism (no counterpart in the reference: it runs one GPU).  A
+ * rank's engine is created with the rank-local config (heads, kv heads, GDN
+ * value / k heads and n_ff divided by nranks; hidden and vocab whole) and fed
+ * its shard of every tensor (qwen35_b200/tp.py): row-parallel projections
+ * then produce partial sums that are all-reduced (NCCL, loaded at run time)
+ * before the residual add, and the lm_head covers rows [vocab_offset,
+ * vocab_offset + vocab_local) with a global greedy argmax.  q35b_tp_unique_id
+ * (one rank) makes the 128-byte NCCL id every rank passes to
+ * q35b_engine_set_tp, which is called by all ranks together, before
+ * finalize. */
+int q35b_tp_unique_id(void *out, int bytes);
+int q35b_engine_set_tp(q35b_engine *e, int nranks, int rank, long long vocab_local, long long vocab_offset,
+                       const void *unique_id);
+
 /* One forward over n tokens packed as nrun runs: run r is tokens
  * [run_end[r-1], run_end[r]) (run_end[-1] = 0), all of one slot at
  * consecutive positions; a decode token is a run of one, a prompt chunk a

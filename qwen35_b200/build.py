@@ -18,7 +18,7 @@ FLAGS = [
     # no multiply-add contraction: every product and sum rounds separately,
     # which is what the bit-exact paths (block folds, GDN recurrence) rely on
     "-fmad=false",
-    "-Xcompiler", "-fPIC", "-shared",
+    "-Xcompiler", "-fPIC", "-shared", "-ldl",
 ]
 
 

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace q35 {
 
@@ -216,6 +217,12 @@ struct q35b_engine {
     float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;
     float *logits = nullptr, *scores = nullptr, *probe_buf = nullptr;
     float *xh = nullptr;  // last row of each run, gathered for the model head
+    // tensor parallelism (1 rank: off)
+    int tp_n = 1, tp_rank = 0;
+    long long vocab_local = 0, vocab_off = 0;  // this rank's lm_head rows
+    ncclComm_t comm = nullptr;
+    float *part = nullptr;                     // row-parallel partial sums [n][hidden]
+    int *am_pair = nullptr, *am_all = nullptr; // (max, index) per run: local / every rank
     uint8_t *xq = nullptr;
     long long xq_ld = 0;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -273,6 +280,23 @@ inline int eng_norm_gemv(q35b_engine *e, int n, const float *w, std::initializer
     return eng_gemv(e, n, segs, e->xq, e->c.hidden, st);
 }
 
+// Row-parallel projections (attn_output, ssm_out, ffn_down) add into the
+// residual stream.  Under tensor parallelism they write partial sums, which
+// are all-reduced over the ranks and then added.
+inline GemvSegDesc eng_rowpar_seg(q35b_engine *e, const Lin &w) {
+    if (e->tp_n > 1) return {w.w, e->part, w.rows, w.tt, (long long)e->c.hidden, GV_STORE};
+    return {w.w, e->x, w.rows, w.tt, (long long)e->c.hidden, GV_ADD};
+}
+inline int eng_rowpar_finish(q35b_engine *e, int n, cudaStream_t st) {
+    if (e->tp_n <= 1) return 0;
+    const long long cnt = (long long)n * e->c.hidden;
+    const NcclApi &api = nccl_api();
+    if (api.all_reduce(e->part, e->part, (size_t)cnt, ncclFloat32, ncclSum, e->comm, st) != ncclSuccess)
+        return (int)cudaErrorUnknown;
+    return launch_k(k_add_rows, dim3((unsigned)std::min<long long>((cnt + 255) / 256, 1024)), dim3(256), 0, st, e->x,
+                    (const float *)e->part, cnt);
+}
+
 inline int eng_layer_gdn(q35b_engine *e, int li, int n, int nrun, cudaStream_t st) {
     const q35b_config &c = e->c;
     const LayerW &W = e->L[li];
@@ -322,7 +346,8 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, int nrun, cudaStream_t s
         Q35_TRY(launch_k(k_quant_rows, dim3((vdim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
                          (long long)vdim, vdim, fo, e->xq, e->xq_ld));
     }
-    return eng_gemv(e, n, {{W.ssm_out.w, e->x, W.ssm_out.rows, W.ssm_out.tt, c.hidden, GV_ADD}}, e->xq, vdim, st);
+    Q35_TRY(eng_gemv(e, n, {eng_rowpar_seg(e, W.ssm_out)}, e->xq, vdim, st));
+    return eng_rowpar_finish(e, n, st);
 }
 
 // context bucket a captured step is built for: the score / P.V grids cover
@@ -376,7 +401,8 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
         Q35_TRY(launch_k(k_quant_rows, dim3((q_dim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
                          (long long)q_dim, q_dim, fo, e->xq, e->xq_ld));
     }
-    return eng_gemv(e, n, {{W.o.w, e->x, W.o.rows, W.o.tt, c.hidden, GV_ADD}}, e->xq, q_dim, st);
+    Q35_TRY(eng_gemv(e, n, {eng_rowpar_seg(e, W.o)}, e->xq, q_dim, st));
+    return eng_rowpar_finish(e, n, st);
 }
 
 inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
@@ -387,13 +413,17 @@ inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
                            {W.ffn_up.w, e->mh1, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}},
                           st));
     const int fd = family_of(W.ffn_down);
-    const GemvSegDesc down{W.ffn_down.w, e->x, W.ffn_down.rows, W.ffn_down.tt, c.hidden, GV_ADD};
+    const GemvSegDesc down = eng_rowpar_seg(e, W.ffn_down);
     const LprPrologue pro{LPR_PRO_SWIGLU, e->mh, e->mh1, nullptr, (long long)c.n_ff, 0.0f};
     const int rc = gemv_lpr_launch(&down, 1, nullptr, c.n_ff, n, st, e->xq_ld, &pro);
-    if (rc != -1) return rc;
-    Q35_TRY(launch_k(k_swiglu_quant, dim3((c.n_ff / (fd == 32 ? 32 : 256) + 7) / 8, n), dim3(256), 0, st,
-                     (const float *)e->mh, (const float *)e->mh1, c.n_ff, fd, e->xq, e->xq_ld));
-    return eng_gemv(e, n, {down}, e->xq, c.n_ff, st);
+    if (rc == -1) {
+        Q35_TRY(launch_k(k_swiglu_quant, dim3((c.n_ff / (fd == 32 ? 32 : 256) + 7) / 8, n), dim3(256), 0, st,
+                         (const float *)e->mh, (const float *)e->mh1, c.n_ff, fd, e->xq, e->xq_ld));
+        Q35_TRY(eng_gemv(e, n, {down}, e->xq, c.n_ff, st));
+    } else if (rc) {
+        return rc;
+    }
+    return eng_rowpar_finish(e, n, st);
 }
 
 // the whole step body (graph-capturable: every per-step value is in device memory)
@@ -439,16 +469,26 @@ inline int eng_step_body(q35b_engine *e, int n, int nrun, int max_len, cudaStrea
         }
     }
     const Lin &H = e->output.w ? e->output : e->token_embd;
+    const long long vl = e->tp_n > 1 ? e->vocab_local : c.vocab;  // lm_head rows on this rank
     if (nrun < n) {
         Q35_TRY(launch_k(k_gather_run_rows, dim3((unsigned)((c.hidden + 255) / 256), (unsigned)nrun), dim3(256), 0,
                          st, (const float *)e->x, (const int *)(e->d_in + 3 * e->max_batch), e->xh, c.hidden));
-        Q35_TRY(eng_norm_gemv(e, nrun, e->output_norm, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, st,
-                              e->xh));
+        Q35_TRY(eng_norm_gemv(e, nrun, e->output_norm, {{H.w, e->logits, H.rows, H.tt, vl, GV_STORE}}, st, e->xh));
     } else {
-        Q35_TRY(eng_norm_gemv(e, n, e->output_norm, {{H.w, e->logits, H.rows, H.tt, c.vocab, GV_STORE}}, st));
+        Q35_TRY(eng_norm_gemv(e, n, e->output_norm, {{H.w, e->logits, H.rows, H.tt, vl, GV_STORE}}, st));
     }
-    const int rc = launch_k(k_argmax, dim3(nrun), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab,
-                            c.vocab, e->d_next);
+    int rc;
+    if (e->tp_n > 1) {
+        Q35_TRY(launch_k(k_argmax_pair, dim3(nrun), dim3(1024), 0, st, (const float *)e->logits, vl, (int)vl,
+                         (int)e->vocab_off, e->am_pair));
+        if (nccl_api().all_gather(e->am_pair, e->am_all, (size_t)2 * nrun, ncclInt32, e->comm, st) != ncclSuccess)
+            return (int)cudaErrorUnknown;
+        rc = launch_k(k_argmax_combine, dim3((unsigned)((nrun + 127) / 128)), dim3(128), 0, st,
+                      (const int *)e->am_all, nrun, e->tp_n, e->d_next);
+    } else {
+        rc = launch_k(k_argmax, dim3(nrun), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab,
+                      c.vocab, e->d_next);
+    }
     e->launches = launch_count() - l0;
     return rc;
 }

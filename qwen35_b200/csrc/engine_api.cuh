@@ -48,9 +48,41 @@ int q35b_engine_create(const q35b_config *cfg, int n_slots, int max_seq, int max
 
 int q35b_engine_destroy(q35b_engine *e) {
     if (!e) return 0;
+    // graphs holding collectives go before the communicator
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+    if (e->comm) nccl_api().comm_destroy(e->comm);
     for (void *p : e->allocs) cudaFree(p);
     delete e;
+    return 0;
+}
+
+int q35b_tp_unique_id(void *out, int bytes) {
+    const NcclApi &api = nccl_api();
+    if (!api.ok) return (int)cudaErrorSharedObjectInitFailed;
+    if (!out || bytes < (int)sizeof(ncclUniqueId)) return (int)cudaErrorInvalidValue;
+    ncclUniqueId id;
+    if (api.get_unique_id(&id) != ncclSuccess) return (int)cudaErrorUnknown;
+    memcpy(out, &id, sizeof(id));
+    return 0;
+}
+
+int q35b_engine_set_tp(q35b_engine *e, int nranks, int rank, long long vocab_local, long long vocab_offset,
+                       const void *unique_id) {
+    if (!e || e->finalized || nranks < 2 || rank < 0 || rank >= nranks || !unique_id || vocab_local <= 0 ||
+        vocab_offset < 0 || vocab_offset + vocab_local > e->c.vocab || e->comm)
+        return (int)cudaErrorInvalidValue;
+    const NcclApi &api = nccl_api();
+    if (!api.ok) return (int)cudaErrorSharedObjectInitFailed;
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof(id));
+    ncclComm_t comm = nullptr;
+    if (api.comm_init_rank(&comm, nranks, id, rank) != ncclSuccess) return (int)cudaErrorUnknown;
+    e->comm = comm;
+    e->tp_n = nranks;
+    e->tp_rank = rank;
+    e->vocab_local = vocab_local;
+    e->vocab_off = vocab_offset;
     return 0;
 }
 
@@ -95,7 +127,9 @@ int q35b_engine_finalize(q35b_engine *e) {
     const long long kq = nk * kd, vdim = nv * kd, conv_dim = 2 * kq + vdim;
     const long long q_dim = (long long)c.n_heads * c.head_dim, kv_dim = (long long)c.n_kv_heads * c.head_dim;
     if (!lin_ok(e->token_embd, c.vocab, h) || !e->output_norm) return (int)cudaErrorInvalidValue;
-    if (e->output.w && !lin_ok(e->output, c.vocab, h)) return (int)cudaErrorInvalidValue;
+    if (e->output.w && !lin_ok(e->output, e->tp_n > 1 ? e->vocab_local : (long long)c.vocab, h))
+        return (int)cudaErrorInvalidValue;
+    if (e->tp_n > 1 && !e->output.w) return (int)cudaErrorInvalidValue;  // a rank's lm_head is its own shard
     int ngdn = 0, nfull = 0;
     for (int li = 0; li < c.n_layers; li++) {
         const LayerW &W = e->L[li];
@@ -137,6 +171,11 @@ int q35b_engine_finalize(q35b_engine *e) {
     ALLOC(kpool, 4 * nfull * S * e->kv_slot);
     ALLOC(vpool, 4 * nfull * S * e->kv_slot);
     ALLOC(d_in, 4 * 4 * B);
+    if (e->tp_n > 1) {
+        ALLOC(part, 4 * B * h);
+        ALLOC(am_pair, 4 * 2 * B);
+        ALLOC(am_all, 4 * 2 * B * e->tp_n);
+    }
     ALLOC(xh, 4 * B * h);
     ALLOC(d_len, 4 * B);
     ALLOC(d_next, 4 * B);

@@ -70,6 +70,11 @@ CONFIGS = {
     "tiny-mixed": ModelConfig("tiny-mixed", 8, 512, 1024, 4096, 4, 1, 4, 2,
                               quant=(("bulk", "IQ4_NL"), ("ffn_down", "Q5_K"), ("ssm_alpha", "Q8_0"),
                                      ("ssm_beta", "Q8_0"), ("output", "Q6_K"), ("attn_output", "Q4_K"))),
+    # tensor-parallel parity cases: every head count splits two ways
+    "tiny-tp": ModelConfig("tiny-tp-q8_0", 4, 256, 1024, 2048, 4, 2, 4, 2, quant=(("bulk", "Q8_0"),)),
+    "tiny-tp-mixed": ModelConfig("tiny-tp-mixed", 4, 512, 1024, 4096, 4, 2, 8, 4,
+                                 quant=(("bulk", "IQ4_NL"), ("ffn_down", "Q5_K"), ("ssm_alpha", "Q8_0"),
+                                        ("ssm_beta", "Q8_0"), ("output", "Q6_K"), ("attn_output", "Q4_K"))),
 }
 
 
@@ -171,7 +176,10 @@ class SyntheticModel:
 class Engine:
     """Batched decode engine (q35b_engine) over a SyntheticModel."""
 
-    def __init__(self, model, n_slots, max_seq, max_batch):
+    def __init__(self, model, n_slots, max_seq, max_batch, tp_id=None):
+        """model: a SyntheticModel, or a tp.ShardModel (then `tp_id`, the
+        NCCL id of q35b_tp_unique_id shared by all ranks, is required and every
+        rank constructs its engine at the same time)"""
         self.L = _lib.load()
         self.model = model
         self.cfg = model.cfg
@@ -182,6 +190,12 @@ class Engine:
         h = ctypes.c_void_p()
         check(self.L.q35b_engine_create(ctypes.addressof(cc), n_slots, max_seq, max_batch, ctypes.byref(h)), "create")
         self.h = h
+        if getattr(model, "P", 1) > 1:
+            if tp_id is None:
+                raise ValueError("a tensor-parallel shard needs the NCCL id")
+            idbuf = ctypes.create_string_buffer(bytes(tp_id), len(tp_id))
+            check(self.L.q35b_engine_set_tp(h, model.P, model.p, model.vocab_local, model.vocab_offset,
+                                            ctypes.cast(idbuf, ctypes.c_void_p)), "set_tp")
         for name, (tt, rows, cols, t) in model.tensors.items():
             check(self.L.q35b_engine_set_tensor(h, name.encode(), tt, t.data_ptr(), rows, cols), name)
         check(self.L.q35b_engine_finalize(h), "finalize")

@@ -1,0 +1,99 @@
+"""Tensor-parallel decode on 2 GPUs (NCCL): two ranks, each running the
+engine on its shard, against one GPU running the whole model.
+
+Row-parallel partial sums are added in a different order than the single
+GPU's one serial fold, so the comparison is by tolerance: the residual
+stream after every layer within 1e-3 relative L2 (the BASELINE per-layer
+bar) and the same greedy tokens.  Skipped with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+N_STEPS = 14
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(eng, cfg, prompt, n_layers):
+    toks, probes = [], []
+    last = None
+    eng.reset_slot(0)
+    for pos in range(N_STEPS):
+        t = prompt[pos] if pos < len(prompt) else last
+        last = eng.step_host([t], [0], [pos])[0]
+        toks.append(last)
+        probes.append(np.stack([eng.layer_out(li, 1)[0].cpu().numpy() for li in range(n_layers)]))
+    return toks, np.stack(probes)
+
+
+def _worker(rank, world, port, out_dir, cfg_name):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    from qwen35_b200 import lib, tp
+    from qwen35_b200 import model as q35
+    L = lib.load()
+    cfg = q35.CONFIGS[cfg_name]
+    full = q35.SyntheticModel(cfg, seed=21)
+    shard = tp.ShardModel(full, world, rank)
+    buf = (torch.zeros(128, dtype=torch.uint8)).numpy()
+    if rank == 0:
+        import ctypes
+        raw = ctypes.create_string_buffer(128)
+        assert L.q35b_tp_unique_id(ctypes.cast(raw, ctypes.c_void_p), 128) == 0
+        buf = np.frombuffer(bytes(raw), dtype=np.uint8).copy()
+    t = torch.from_numpy(buf).cuda()
+    dist.broadcast(t, 0)
+    uid = t.cpu().numpy().tobytes()
+    eng = q35.Engine(shard, n_slots=2, max_seq=64, max_batch=4, tp_id=uid)
+    eng.set_probe(True)
+    prompt = [int(v) for v in np.random.default_rng(21).integers(0, cfg.vocab, 6)]
+    toks, probes = _run(eng, cfg, prompt, cfg.n_layers)
+    eng.close()  # its graphs hold NCCL work: released before the process group
+    np.save(os.path.join(out_dir, f"probe{rank}.npy"), probes)
+    np.save(os.path.join(out_dir, f"toks{rank}.npy"), np.array(toks))
+    if rank == 0:
+        ref = q35.Engine(full, n_slots=2, max_seq=64, max_batch=4)
+        ref.set_probe(True)
+        rt, rp = _run(ref, cfg, prompt, cfg.n_layers)
+        ref.close()
+        np.save(os.path.join(out_dir, "probe_ref.npy"), rp)
+        np.save(os.path.join(out_dir, "toks_ref.npy"), np.array(rt))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("cfg_name", ["tiny-tp", "tiny-tp-mixed"])
+def test_tp2_matches_single_gpu(cfg_name):
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(2, _free_port(), d, cfg_name), nprocs=2, start_method="spawn")
+        p0, p1, pr = (np.load(os.path.join(d, f)) for f in ("probe0.npy", "probe1.npy", "probe_ref.npy"))
+        t0, t1, tr = (np.load(os.path.join(d, f)) for f in ("toks0.npy", "toks1.npy", "toks_ref.npy"))
+        # the ranks hold one residual stream, bit for bit
+        assert np.array_equal(p0.view(np.uint32), p1.view(np.uint32))
+        assert np.array_equal(t0, t1)
+        # and it follows the single GPU within the per-layer bar
+        worst = 0.0
+        for s in range(p0.shape[0]):
+            for li in range(p0.shape[1]):
+                a, b = p0[s, li].astype(np.float64), pr[s, li].astype(np.float64)
+                worst = max(worst, np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+        assert worst < 1e-3, worst
+        assert np.array_equal(t0, tr)
