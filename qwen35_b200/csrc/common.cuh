@@ -20,6 +20,10 @@ namespace q35 {
 enum : int {
     TT_F32 = 0, TT_F16 = 1, TT_Q4_0 = 2, TT_Q8_0 = 8, TT_Q4_K = 12, TT_Q5_K = 13,
     TT_Q6_K = 14, TT_Q8_K = 15, TT_IQ4_NL = 20, TT_BF16 = 30,
+    // engine-internal: Q6_K blocks padded from 210 to 224 bytes (same field
+    // offsets, 14 zero bytes after d), so that rows are 16-byte multiples for
+    // TMA; not a GGUF type id
+    TT_Q6_K_P = 0x1000 + 14,
 };
 
 // Native block geometry of the weight types this library serves.
@@ -31,6 +35,7 @@ __host__ __device__ inline Geom geom_of(int tt) {
     case TT_Q4_K: return {256, 144, 256};
     case TT_Q5_K: return {256, 176, 256};
     case TT_Q6_K: return {256, 210, 256};
+    case TT_Q6_K_P: return {256, 224, 256};
     default: return {0, 0, 0};
     }
 }

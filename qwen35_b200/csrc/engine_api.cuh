@@ -120,6 +120,16 @@ int q35b_engine_set_tensor(q35b_engine *e, const char *name, int tt, const void 
     return (int)cudaErrorInvalidValue;
 }
 
+// Q6_K (210 B) -> padded Q6_K (224 B): 105 halfwords of a block, then zeros
+__global__ void k_repack_q6k(const uint8_t *src, uint8_t *dst, long long nblk) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= nblk * 112) return;
+    const long long b = i / 112;
+    const int hw = (int)(i - b * 112);
+    const uint16_t v = hw < 105 ? reinterpret_cast<const uint16_t *>(src + b * 210)[hw] : (uint16_t)0;
+    reinterpret_cast<uint16_t *>(dst + b * 224)[hw] = v;
+}
+
 int q35b_engine_finalize(q35b_engine *e) {
     if (!e || e->finalized) return (int)cudaErrorInvalidValue;
     const q35b_config &c = e->c;
@@ -201,6 +211,25 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY((int)cudaMemset(e->conv_pool, 0, 4 * ngdn * S * e->conv_slot));
     Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 4 * B));
+    // load-time repack: Q6_K projections to 224-byte blocks (16-byte rows for
+    // the TMA-streamed GEMV); the caller's buffers stay untouched
+    auto repack = [&](Lin &l) -> int {
+        if (l.tt != TT_Q6_K || !l.w) return 0;
+        const long long nblk = l.rows * (l.cols / 256);
+        void *dst;
+        Q35_TRY(eng_alloc(e, &dst, (size_t)nblk * 224));
+        const long long nthreads = nblk * 112;
+        k_repack_q6k<<<(unsigned)((nthreads + 255) / 256), 256>>>(l.w, static_cast<uint8_t *>(dst), nblk);
+        Q35_TRY((int)cudaGetLastError());
+        l.w = static_cast<const uint8_t *>(dst);
+        l.tt = TT_Q6_K_P;
+        return 0;
+    };
+    Q35_TRY(repack(e->output));
+    for (LayerW &W : e->L)
+        for (Lin *l : {&W.qkv, &W.gate, &W.alpha, &W.beta, &W.ssm_out, &W.q, &W.k, &W.v, &W.o, &W.ffn_gate, &W.ffn_up,
+                       &W.ffn_down})
+            Q35_TRY(repack(*l));
     Q35_TRY(gemv_prepare());
     Q35_TRY(gemv_lpr_prepare());
     Q35_TRY(attx_prepare(e->max_seq));

@@ -257,7 +257,7 @@ Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, 
                     if (tt == TT_Q8_0 || tt == TT_IQ4_NL) {
                         // sumf += dx * dy * (float)sumi
                         term = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb)), A.dsc(t, b)), __int2float_rn(is[t]));
-                    } else if (tt == TT_Q6_K) {
+                    } else if (tt == TT_Q6_K || tt == TT_Q6_K_P) {
                         // sumf += d_w * dy * (float)isum
                         term = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb + 208)), A.dsc(t, b)), __int2float_rn(is[t]));
                     } else {

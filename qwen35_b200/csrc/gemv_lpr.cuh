@@ -350,6 +350,66 @@ Q35_DEV void lpr_q45_k(const uint8_t *rp, const ActView &A, int ntok, int gb0, i
     }
 }
 
+// Q6_K in the padded 224-byte layout: ql[128] @0, qh[64] @128, int8
+// scales[16] @192, f16 d @208 (kernels256.c:720-738): 4 parts (2 halves x 2
+// sixteen-element ranges) of 4 x 16 elements, isum = sum of scale x
+// 16-element dot, sumf += (d_w*dy)*(float)isum
+template <int NT, class Sink>
+Q35_DEV void lpr_q6_k(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
+    for (int k = 0; k < nblk; k++) {
+        uint32_t W[56];
+        const uint4 *s = reinterpret_cast<const uint4 *>(rp + k * 224);
+#pragma unroll
+        for (int i = 0; i < 14; i++) {
+            const uint4 v = s[i];
+            W[4 * i] = v.x;
+            W[4 * i + 1] = v.y;
+            W[4 * i + 2] = v.z;
+            W[4 * i + 3] = v.w;
+        }
+        const int b = gb0 + k;
+        int is[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) is[t] = 0;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int h = p >> 1, hf = p & 1;
+            int sc[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int byte = h * 8 + hf + 2 * u;  // scales[h*8 + hf + 2u]
+                sc[u] = (int)(int8_t)((W[48 + (byte >> 2)] >> ((byte & 3) * 8)) & 0xFFu);
+            }
+            uint32_t v1[4], v2[4], v3[4], v4[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t qa = W[(h * 64 + 16 * hf) / 4 + i];
+                const uint32_t qb = W[(h * 64 + 32 + 16 * hf) / 4 + i];
+                const uint32_t qh = W[(128 + h * 32 + 16 * hf) / 4 + i];
+                v1[i] = __vsub4((qa & 0x0F0F0F0Fu) | ((qh & 0x03030303u) << 4), 0x20202020u);
+                v2[i] = __vsub4((qb & 0x0F0F0F0Fu) | (((qh >> 2) & 0x03030303u) << 4), 0x20202020u);
+                v3[i] = __vsub4(((qa >> 4) & 0x0F0F0F0Fu) | (((qh >> 4) & 0x03030303u) << 4), 0x20202020u);
+                v4[i] = __vsub4(((qb >> 4) & 0x0F0F0F0Fu) | (((qh >> 6) & 0x03030303u) << 4), 0x20202020u);
+            }
+            const int e0 = b * 256 + h * 128 + 16 * hf;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < ntok) {
+                    const int d1 = dot4x4(v1[0], v1[1], v1[2], v1[3], A.q16(t, e0), 0);
+                    const int d2 = dot4x4(v2[0], v2[1], v2[2], v2[3], A.q16(t, e0 + 32), 0);
+                    const int d3 = dot4x4(v3[0], v3[1], v3[2], v3[3], A.q16(t, e0 + 64), 0);
+                    const int d4 = dot4x4(v4[0], v4[1], v4[2], v4[3], A.q16(t, e0 + 96), 0);
+                    is[t] += sc[0] * d1 + sc[1] * d2 + sc[2] * d3 + sc[3] * d4;
+                }
+            }
+        }
+        const float dw = f16_lo(W[52]);
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+            if (t < ntok) sk.put(t, b, __fmul_rn(__fmul_rn(dw, A.dsc(t, b)), __int2float_rn(is[t])));
+    }
+}
+
 Q35_DEV int lpr_find_seg(const LprArgs &a, long long tile) {
     int s = 0;
 #pragma unroll
@@ -364,6 +424,7 @@ Q35_DEV void lpr_chunk(int tt, const uint8_t *rp, const ActView &A, int ntok, in
     case TT_Q8_0: lpr_q8_0<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_IQ4_NL: lpr_iq4_nl<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_Q4_K: lpr_q45_k<NT, false>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
+    case TT_Q6_K_P: lpr_q6_k<NT>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
     default: lpr_q45_k<NT, true>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
     }
 }
@@ -592,7 +653,9 @@ inline int gemv_lpr_prepare() {
     return 0;
 }
 
-inline bool lpr_type_ok(int tt) { return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K; }
+inline bool lpr_type_ok(int tt) {
+    return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K || tt == TT_Q6_K_P;
+}
 
 // f32 rows the launch quantizes itself (see LprArgs::prologue)
 struct LprPrologue {

@@ -73,8 +73,10 @@ Q35_DEV uint64_t umma_desc(const void *smem_ptr, uint32_t lbo, uint32_t sbo) {
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 // instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = MMQ_N
-constexpr uint32_t MMQ_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MMQ_N >> 3) << 17) |
-                               ((uint32_t)(MMQ_M >> 4) << 24);
+template <int TN>
+__host__ __device__ constexpr uint32_t mmq_idesc() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(MMQ_M >> 4) << 24);
+}
 
 Q35_DEV void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -185,6 +187,7 @@ Q35_DEV int mmq_find_seg(const MmqArgs &a, long long tile) {
     return s;
 }
 
+template <int TN>
 __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ MmqArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int issued = 0, ncommit = 0;  // producer's TMA chunks, MMA thread's commits
     const long long tile = blockIdx.x;
-    const int t0 = blockIdx.y * MMQ_N;
+    const int t0 = blockIdx.y * TN;
     const int si = mmq_find_seg(a, tile);
     const MmqSeg &sg = a.seg[si];
     const long long r0 = (tile - sg.tile_begin) * MMQ_M;
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes), xbytes = (uint32_t)(MMQ_N * 272);
+            const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes), xbytes = (uint32_t)(TN * 272);
             for (int c = 0; c < a.nchunk; c++, issued++) {
                 const int s = c % MMQ_NS;
                 if (c >= MMQ_NS && !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 121)) {
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
                         const int b = round * MMQ_RB + kb;
                         const uint64_t ad = umma_desc(sA + b * MMQ_M * 32, 128, 256);
                         const uint64_t bd = umma_desc(sB + b * MMQ_N * 32, 128, 256);
-                        umma_i8(tmem + (uint32_t)(kb * MMQ_N), ad, bd, MMQ_IDESC, 0u);
+                        umma_i8(tmem + (uint32_t)(kb * MMQ_N), ad, bd, mmq_idesc<TN>(), 0u);
                     }
                     umma_commit(mma_bar);
                     ncommit++;
@@ -268,9 +271,9 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
         const int q = warp & 3;                       // TMEM lane quarter this warp may access
         const int row = q * 32 + lane;
         const int ct = threadIdx.x - 64;              // 0..127
-        float acc[MMQ_N];
+        float acc[TN];
 #pragma unroll
-        for (int t = 0; t < MMQ_N; t++) acc[t] = 0.0f;
+        for (int t = 0; t < TN; t++) acc[t] = 0.0f;
         int mma_phase = 0;
         for (int c = 0; c < a.nchunk; c++) {
             const int s = c % MMQ_NS;
@@ -294,7 +297,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
                 // are read by every thread, so they alternate between two
                 // buffers (a writer of chunk c+2 has passed chunk c+1's
                 // barrier, which every reader of chunk c reached after its fold)
-                if (ct < MMQ_N) {
+                if (ct < TN) {
                     auto putx = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
                         uint8_t *dst = sB + b * MMQ_N * 32;
                         *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
                         const float dw = sDW[b * MMQ_M + row];
                         const float *dx = dxc + b * MMQ_N;
 #pragma unroll
-                        for (int half = 0; half < MMQ_N / 32; half++) {
+                        for (int half = 0; half < TN / 32; half++) {
                             uint32_t d[32];
                             tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(kb * MMQ_N + half * 32), d);
                             tmem_ld_wait();
@@ -340,9 +343,9 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
         // outputs: row `row` of this tile, tokens t0 .. t0 + 63
         const long long r = r0 + row;
         if (!s_fail && r < sg.rows) {
-            const int nt = min(MMQ_N, a.ntok - t0);
+            const int nt = min(TN, a.ntok - t0);
 #pragma unroll
-            for (int t = 0; t < MMQ_N; t++) {
+            for (int t = 0; t < TN; t++) {
                 if (t < nt) {
                     float *o = sg.out + (long long)(t0 + t) * sg.out_ld + r;
                     *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
@@ -401,6 +404,7 @@ struct MmqkArgs {
     int ntok, nblk;                 // tokens, 256-element blocks per row
 };
 
+template <int TN>
 __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -418,7 +422,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int issued = 0, ncommit = 0;
     const long long tile = blockIdx.x;
-    const int t0 = blockIdx.y * MMQ_N;
+    const int t0 = blockIdx.y * TN;
     int sgi = 0;
 #pragma unroll
     for (int i = 1; i < GV_MAX_SEG; i++)
@@ -426,7 +430,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
     const MmqSeg &sg = a.seg[sgi];
     const long long r0 = (tile - sg.tile_begin) * MMQ_M;
     const bool q5 = sg.ttype == TT_Q5_K;
-    const uint32_t idesc = MMQ_IDESC;
+    const uint32_t idesc = mmq_idesc<TN>();
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -482,23 +486,25 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const int ct = threadIdx.x - 64;
-        float acc[MMQ_N];
+        float acc[TN];
 #pragma unroll
-        for (int t = 0; t < MMQ_N; t++) acc[t] = 0.0f;
+        for (int t = 0; t < TN; t++) acc[t] = 0.0f;
         for (int c = 0; c < a.nblk; c++) {
             const int s = c % MMQ_NS;
             // activations of block c (global -> operand layout), independent of the weight TMA
             {
-                const int tk = ct & (MMQ_N - 1), h = ct >> 6;  // token, half (sub-blocks 4h .. 4h+3)
+                // thread: token tk, sub-blocks [SPT*h, SPT*h + SPT)
+                constexpr int SPT = TN / 16;
+                const int tk = ct % TN, h = ct / TN;
                 const bool live = t0 + tk < a.ntok;
                 const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)c * 292;
-                uint32_t w[32];
+                uint32_t w[SPT * 8];
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    w[i] = live ? reinterpret_cast<const uint32_t *>(src + 4 + 128 * h)[i] : 0u;
+                for (int i = 0; i < SPT * 8; i++)
+                    w[i] = live ? reinterpret_cast<const uint32_t *>(src + 4 + 32 * SPT * h)[i] : 0u;
 #pragma unroll
-                for (int jj = 0; jj < 4; jj++) {
-                    uint8_t *dst = sB + (4 * h + jj) * MMQ_N * 32;
+                for (int jj = 0; jj < SPT; jj++) {
+                    uint8_t *dst = sB + (SPT * h + jj) * MMQ_N * 32;
                     *reinterpret_cast<uint4 *>(dst + umma_off(tk, 0)) =
                         make_uint4(w[8 * jj], w[8 * jj + 1], w[8 * jj + 2], w[8 * jj + 3]);
                     *reinterpret_cast<uint4 *>(dst + umma_off(tk, 1)) =
@@ -575,7 +581,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
                     mn[j] = sMN[j * MMQ_M + row];
                 }
 #pragma unroll
-                for (int half = 0; half < MMQ_N / 32; half++) {
+                for (int half = 0; half < TN / 32; half++) {
                     int is[32];
 #pragma unroll
                     for (int i = 0; i < 32; i++) is[i] = 0;
@@ -605,9 +611,9 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         tc_fence_before();
         const long long r = r0 + row;
         if (!s_fail && r < sg.rows) {
-            const int nt = min(MMQ_N, a.ntok - t0);
+            const int nt = min(TN, a.ntok - t0);
 #pragma unroll
-            for (int t = 0; t < MMQ_N; t++) {
+            for (int t = 0; t < TN; t++) {
                 if (t < nt) {
                     float *o = sg.out + (long long)(t0 + t) * sg.out_ld + r;
                     *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
@@ -650,12 +656,22 @@ inline bool mmq_encode(CUtensorMap *m, const void *base, long long rows, long lo
 inline int mmq_prepare() {
     static int done = 0;
     if (done) return 0;
-    cudaError_t e = cudaFuncSetAttribute(k_mmq, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_mmq_kq, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM);
-    if (e != cudaSuccess) return (int)e;
+    const cudaError_t es[] = {
+        cudaFuncSetAttribute(k_mmq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM),
+        cudaFuncSetAttribute(k_mmq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM)};
+    for (cudaError_t e : es)
+        if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;
+}
+
+// token tile: 64, or 32 when 64-token tiles would leave SMs idle (short
+// matrices: fewer row tiles than SMs)
+inline int mmq_token_tile(long long row_tiles, int ntok) {
+    const long long ctas64 = row_tiles * ((ntok + 63) / 64);
+    return ctas64 < gemv_sm_count() && ntok > 16 ? 32 : 64;
 }
 
 // K-quant (Q4_K / Q5_K) weights x Q8_K activations; -1 when not eligible
@@ -692,8 +708,11 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
     a.ntok = ntok;
     a.nblk = cols / 256;
     Q35_TRY_RC(mmq_prepare());
-    const dim3 grid((unsigned)tiles, (unsigned)((ntok + MMQ_N - 1) / MMQ_N));
-    return launch_k(k_mmq_kq, grid, dim3(MMQ_THREADS), (size_t)MMQK_SMEM, st, a);
+    if (mmq_token_tile(tiles, ntok) == 32)
+        return launch_k(k_mmq_kq<32>, dim3((unsigned)tiles, (unsigned)((ntok + 31) / 32)), dim3(MMQ_THREADS),
+                        (size_t)MMQK_SMEM, st, a);
+    return launch_k(k_mmq_kq<64>, dim3((unsigned)tiles, (unsigned)((ntok + 63) / 64)), dim3(MMQ_THREADS),
+                    (size_t)MMQK_SMEM, st, a);
 }
 
 // Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL (Q8_0
@@ -727,15 +746,17 @@ inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int col
         tiles += (s.rows + MMQ_M - 1) / MMQ_M;
         if (!mmq_encode(&a.wmap[i], segs[i].w, s.rows, rb, rb, s.chunk_bytes, MMQ_M)) return -1;
     }
-    if (!mmq_encode(&a.xmap, xq, ntok, ld, (int)act_row, 272, MMQ_N)) return -1;
     if (tiles == 0) return 0;
+    const int tn = mmq_token_tile(tiles, ntok);
+    if (!mmq_encode(&a.xmap, xq, ntok, ld, (int)act_row, 272, tn)) return -1;
     a.nseg = nseg;
     a.total_tiles = tiles;
     a.ntok = ntok;
     a.nchunk = cols / 256;
     Q35_TRY_RC(mmq_prepare());
-    const dim3 grid((unsigned)tiles, (unsigned)((ntok + MMQ_N - 1) / MMQ_N));
-    return launch_k(k_mmq, grid, dim3(MMQ_THREADS), (size_t)MMQ_SMEM, st, a);
+    const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn));
+    if (tn == 32) return launch_k(k_mmq<32>, grid, dim3(MMQ_THREADS), (size_t)MMQ_SMEM, st, a);
+    return launch_k(k_mmq<64>, grid, dim3(MMQ_THREADS), (size_t)MMQ_SMEM, st, a);
 }
 
 }  // namespace q35

@@ -158,7 +158,9 @@ def test_mmq_tensor_core_bit_exact(L, O, name, tokens):
     int8 (sub-)block dots on the tensor core, scales, mins and the f32 fold in
     block order on the CUDA cores -- bit-exact with the reference scalar tier
     like the decode GEMV"""
-    for rows, cols in [(300, 1024), (129, 2048), (1000, 768), (128, 256)]:
+    # 32-token tiles when row tiles are fewer than SMs, 64-token tiles for
+    # the 19000-row matrix (and at 16 tokens)
+    for rows, cols in [(300, 1024), (129, 2048), (1000, 768), (128, 256), (19000, 256)]:
         got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + 7 * tokens)
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
     assert_no_kernel_error(L)
