@@ -214,6 +214,13 @@ int q35_mmq_act_block_bytes(void);
  * instead of hanging. */
 int q35b_get_error(int *code);
 
+/* Failure-detection self-test: one kernel waits on an mbarrier that nothing
+ * completes, with the same bounded wait every kernel of this library uses,
+ * here limited to limit_ms (1..2000); it gives up, records site 150 for
+ * q35b_get_error and returns.  The call returns 0 once the kernel has ended;
+ * the context stays usable. */
+int q35b_selftest_wait(int limit_ms, void *stream);
+
 /* Device weight encoder: `nblocks` native blocks of `ttype` from f32.
  * Q8_0 is the reference's weight quantizer (src/quant_dequant.zig:1404);
  * IQ4_NL / Q4_K / Q5_K / Q6_K are this library's deterministic encoders. */

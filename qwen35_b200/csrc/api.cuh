@@ -461,6 +461,23 @@ int q35_mmq_dp4a_wants(int) { return 0; }
 int q35_mmq_act_block_bytes(void) { return 288; }
 
 // ---- additive API ----
+// failure-detection self-test: a wait on an mbarrier nothing ever completes
+__global__ void k_wait_probe(unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0u, 150, limit_ns);  // never completes: gives up, records 150
+}
+
+int q35b_selftest_wait(int limit_ms, void *stream) {
+    if (limit_ms <= 0 || limit_ms > 2000) return (int)cudaErrorInvalidValue;
+    k_wait_probe<<<1, 32, 0, S(stream)>>>((unsigned long long)limit_ms * 1000000ull);
+    const int rc = (int)cudaGetLastError();
+    if (rc) return rc;
+    return (int)cudaStreamSynchronize(S(stream));
+}
+
 int q35b_get_error(int *code) {
     int v = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_q35_error, sizeof(int));

@@ -173,12 +173,12 @@ Q35_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 // Bounded wait: gives up after ~2 s of wall time, records `site` in the error
 // word and returns false.  Nothing in this library waits without a bound.
-Q35_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int site) {
+Q35_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int site, uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 0;; it++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 255u && globaltimer() - t0 > 2000000000ull) {
+        if ((it & 255u) == 255u && globaltimer() - t0 > limit_ns) {
             set_error(site);
             return false;
         }
@@ -272,26 +272,28 @@ Q35_DEV float serial_sumsq(const float *x, int n) {
     float s = 0.0f;
     int i = 0;
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && n >= 32) {
-        // 32-element chunks: the next chunk's loads are in flight while the
-        // dependent adds of this one run, so the chain costs ~1 add latency
-        // per element
+        // 32-element chunks: the next chunk's loads and all of this chunk's
+        // products are issued before the dependent adds, so the chain runs at
+        // one add latency per element
         const float4 *v = reinterpret_cast<const float4 *>(x);
-        float4 cur[8], nxt[8];
+        float4 cur[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) cur[k] = v[k];
         for (; i + 32 <= n; i += 32) {
-            const bool more = i + 64 <= n;
-#pragma unroll
-            for (int k = 0; k < 8; k++) nxt[k] = more ? v[(i + 32) / 4 + k] : cur[k];
+            float p[32];
 #pragma unroll
             for (int k = 0; k < 8; k++) {
-                s = __fadd_rn(s, __fmul_rn(cur[k].x, cur[k].x));
-                s = __fadd_rn(s, __fmul_rn(cur[k].y, cur[k].y));
-                s = __fadd_rn(s, __fmul_rn(cur[k].z, cur[k].z));
-                s = __fadd_rn(s, __fmul_rn(cur[k].w, cur[k].w));
+                p[4 * k] = __fmul_rn(cur[k].x, cur[k].x);
+                p[4 * k + 1] = __fmul_rn(cur[k].y, cur[k].y);
+                p[4 * k + 2] = __fmul_rn(cur[k].z, cur[k].z);
+                p[4 * k + 3] = __fmul_rn(cur[k].w, cur[k].w);
+            }
+            if (i + 64 <= n) {
+#pragma unroll
+                for (int k = 0; k < 8; k++) cur[k] = v[(i + 32) / 4 + k];
             }
 #pragma unroll
-            for (int k = 0; k < 8; k++) cur[k] = nxt[k];
+            for (int k = 0; k < 32; k++) s = __fadd_rn(s, p[k]);
         }
     }
     for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));

@@ -338,7 +338,7 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, int nrun, cudaStream_t s
     g.xq_ld = e->xq_ld;
     g.gout = e->gout;
     g.gout_ld = vdim;
-    Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), 0, st, g));
+    Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), (size_t)GDN_KD * GDN_KD * 4, st, g));
     if (g.run_end)
         Q35_TRY(launch_k(k_gdn_hist_settle, dim3((unsigned)((conv_dim * 3 + 255) / 256), (unsigned)nrun), dim3(256), 0,
                          st, g.hist, g.hist_slot, conv_dim, g.slots, g.pos, g.run_end));

@@ -232,6 +232,7 @@ int q35b_engine_finalize(q35b_engine *e) {
             Q35_TRY(repack(*l));
     Q35_TRY(gemv_prepare());
     Q35_TRY(gemv_lpr_prepare());
+    Q35_TRY(gdn_prepare());
     Q35_TRY(attx_prepare(e->max_seq));
     Q35_TRY((int)cudaDeviceSynchronize());
     e->finalized = true;

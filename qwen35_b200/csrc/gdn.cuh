@@ -130,7 +130,7 @@ struct GdnCoreArgs {
 __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ GdnCoreArgs a) {
     pdl_trigger();
     pdl_wait();
-    __shared__ float sq[GDN_KD], sk[GDN_KD], so[GDN_KD];
+    __shared__ __align__(16) float sq[GDN_KD], sk[GDN_KD], so[GDN_KD];
     __shared__ float s_scal[4];
     const int h = blockIdx.x, r = blockIdx.y, j = threadIdx.x;
     const int kd = GDN_KD, kq = a.nk * kd, conv_dim = 2 * kq + a.nv * kd;
@@ -149,11 +149,17 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     float *hout = a.hist + slot * a.hist_slot + (long long)((p0 & 1) ^ 1) * conv_dim * 3;
 
     // loads that do not depend on the token, issued up front so their
-    // latencies overlap: the state column, conv taps and history, the norm
+    // latencies overlap: the 64 KB state block (one bulk copy into shared
+    // memory), conv taps and history, the norm
     float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
-    float col[GDN_KD];
-#pragma unroll
-    for (int i = 0; i < GDN_KD; i++) col[i] = S[(long long)i * GDN_KD + j];
+    extern __shared__ __align__(128) float s_state[];  // [kd][kd]
+    __shared__ __align__(8) uint64_t s_bar;
+    if (j == 0) {
+        mbar_init(&s_bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&s_bar, (uint32_t)(kd * kd * 4));
+        bulk_g2s(s_state, S, (uint32_t)(kd * kd * 4), &s_bar);
+    }
     const int chq = kh * kd + j, chk = kq + kh * kd + j, chv = 2 * kq + h * kd + j;
     // conv history and taps of this thread's q / k / v channels, kept in
     // shared memory (the state column already takes the registers)
@@ -168,6 +174,18 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     }
     const float nwj = a.ssm_norm[j];
     const float ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
+    __shared__ int s_ok;
+    if (j == 0) s_ok = mbar_wait(&s_bar, 0u, 140) ? 1 : 0;
+    __syncthreads();  // thread 0 saw the copy land (or gave up); all threads learn which
+    if (!s_ok) {
+        // the copy did not land in time: let it finish (bounded) before the
+        // shared memory is released, write nothing
+        if (j == 0) mbar_wait(&s_bar, 0u, 141);
+        return;
+    }
+    float col[GDN_KD];
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) col[i] = s_state[i * GDN_KD + j];
 
     // causal conv k=4 + silu: y = w0*h0 + w1*h1 + w2*h2 + w3*x, left to right;
     // then the history shifts in x
@@ -207,17 +225,34 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
         sq[j] = qj;
         sk[j] = kj;
         __syncthreads();
+        // pass 1: acc = sum_i S[i][j] k[i] (i ascending), products ahead of the adds
         float acc = 0.0f;
+        const float4 *sk4 = reinterpret_cast<const float4 *>(sk), *sq4 = reinterpret_cast<const float4 *>(sq);
 #pragma unroll
-        for (int i = 0; i < GDN_KD; i++) acc = __fadd_rn(acc, __fmul_rn(col[i], sk[i]));
+        for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+            const float4 kv = sk4[i4];
+            const float p0 = __fmul_rn(col[4 * i4], kv.x), p1 = __fmul_rn(col[4 * i4 + 1], kv.y);
+            const float p2 = __fmul_rn(col[4 * i4 + 2], kv.z), p3 = __fmul_rn(col[4 * i4 + 3], kv.w);
+            acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, p0), p1), p2), p3);
+        }
         const float km = __fmul_rn(acc, g);
         const float d = __fmul_rn(__fsub_rn(vj, km), be);
+        // pass 2: S[i][j] = S[i][j]*g + k[i]*d; out += S[i][j]*q[i]
         float o = 0.0f;
 #pragma unroll
-        for (int i = 0; i < GDN_KD; i++) {
-            const float nvv = __fadd_rn(__fmul_rn(col[i], g), __fmul_rn(sk[i], d));
-            col[i] = nvv;
-            o = __fadd_rn(o, __fmul_rn(nvv, sq[i]));
+        for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+            const float4 kv = sk4[i4], qv = sq4[i4];
+            const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
+            float pr[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = 4 * i4 + u;
+                const float nvv = __fadd_rn(__fmul_rn(col[i], g), __fmul_rn(kk[u], d));
+                col[i] = nvv;
+                pr[u] = __fmul_rn(nvv, qq[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) o = __fadd_rn(o, pr[u]);
         }
         so[j] = o;
         __syncthreads();
@@ -249,6 +284,17 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
         store(1);
     }
     store(2);
+}
+
+// k_gdn_core stages the 64 KB state block in dynamic shared memory
+inline int gdn_prepare() {
+    static int done = 0;
+    if (done) return 0;
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_gdn_core, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_KD * GDN_KD * 4);
+    if (e != cudaSuccess) return (int)e;
+    done = 1;
+    return 0;
 }
 
 // after k_gdn_core over runs: a run of even length wrote its final conv

@@ -77,40 +77,41 @@ enum { LPR_PRO_NONE = 0, LPR_PRO_NORM = 1, LPR_PRO_SWIGLU = 2 };
 // The activation quantizers (quant_q8_0_warp / quant_q8_K_warp), writing the
 // GEMV's shared layout directly: int8 plane, f32 scale per block (for Q8_0
 // the f16-rounded scale the API layout would carry), int32 16-element sums.
-// The same Q8_0 quantizer with one thread per 32-element block (x: the
-// block's f32 values in shared memory): no shuffles, so a CTA quantizes a
-// whole row in one pass.  max() is exact in any order, and every element
-// takes the warp version's operations.
-Q35_DEV void lpr_quant_q8_0_thread(const float *x, uint8_t *at, int cols, int b) {
-    float v[32];
-    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+// The same Q8_0 quantizer with 4 threads per 32-element block (x: the
+// block's f32 values in shared memory; thread q of the quad takes elements
+// 8q .. 8q+7): the block max by two shuffles (max is exact in any order),
+// then every element takes the warp version's operations.
+Q35_DEV void lpr_quant_q8_0_quad(const float *x, uint8_t *at, int cols, int b, int q, bool store,
+                                 float scale_x = 0.0f, const float *w = nullptr) {
+    float v[8];
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + 8 * q);
+    const float4 t0 = x4[0], t1 = x4[1];
+    v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
+    v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+    if (w) {  // rmsnorm fused: v = (x * scale) * w (elementwise.zig:43-57)
+        const float4 *w4 = reinterpret_cast<const float4 *>(w + 8 * q);
+        const float4 u0 = w4[0], u1 = w4[1];
+        const float wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const float4 t = x4[k];
-        v[4 * k] = t.x;
-        v[4 * k + 1] = t.y;
-        v[4 * k + 2] = t.z;
-        v[4 * k + 3] = t.w;
+        for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], scale_x), wv[k]);
     }
     float amax = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
+    for (int k = 0; k < 8; k++) amax = fmaxf(amax, fabsf(v[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     const float inv = amax > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    reinterpret_cast<float *>(at + cols)[b] = f16_to_f32(f32_to_f16_bits(scale, 0x0380u));
-    uint32_t *dst = reinterpret_cast<uint32_t *>(at + b * 32);
+    if (store && q == 0) reinterpret_cast<float *>(at + cols)[b] = f16_to_f32(f32_to_f16_bits(scale, 0x0380u));
+    uint32_t word[2] = {0u, 0u};
 #pragma unroll
-    for (int w = 0; w < 8; w++) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const float xx = __fmul_rn(v[4 * w + k], inv);
-            int q = __float2int_rz(__fadd_rn(xx, xx >= 0.0f ? 0.5f : -0.5f));
-            q = q > 127 ? 127 : (q < -128 ? -128 : q);
-            word |= (uint32_t)(q & 0xFF) << (8 * k);
-        }
-        dst[w] = word;
+    for (int k = 0; k < 8; k++) {
+        const float xx = __fmul_rn(v[k], inv);
+        int qv = __float2int_rz(__fadd_rn(xx, xx >= 0.0f ? 0.5f : -0.5f));
+        qv = qv > 127 ? 127 : (qv < -128 ? -128 : qv);
+        word[k >> 2] |= (uint32_t)(qv & 0xFF) << (8 * (k & 3));
     }
+    if (store) *reinterpret_cast<uint2 *>(at + b * 32 + 8 * q) = make_uint2(word[0], word[1]);
 }
 
 Q35_DEV void lpr_quant_q8_K(const float (&v)[8], uint8_t *at, int cols, int b, int lane) {
@@ -472,6 +473,11 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     };
     long long issued = nst < a.ns ? nst : a.ns;
     for (long long i = 0; i < issued; i++) issue(i);
+    // the norm weight is constant: staged before the dependency wait
+    if (a.prologue == LPR_PRO_NORM) {
+        float4 *wd = reinterpret_cast<float4 *>(smem + a.x_off) + (size_t)a.ntok * (a.cols / 4);
+        for (int j = threadIdx.x; j < a.cols / 4; j += blockDim.x) wd[j] = reinterpret_cast<const float4 *>(a.pw)[j];
+    }
 
     // the activation belongs to the previous kernel
     pdl_wait();
@@ -488,20 +494,14 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
         if (a.prologue == LPR_PRO_NORM) {
             // rmsnorm (engine.zig:1507, elementwise.zig:43-57): the sum of
             // squares in the CPU's serial order, one thread per token
-            for (int idx = threadIdx.x; idx < (a.ntok + 1) * c4; idx += blockDim.x) {
+            for (int idx = threadIdx.x; idx < a.ntok * c4; idx += blockDim.x) {
                 const int t = idx / c4, j = idx - t * c4;
-                xd[idx] = t < a.ntok ? reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j]
-                                     : reinterpret_cast<const float4 *>(a.pw)[j];
+                xd[idx] = reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j];
             }
             __syncthreads();
             if ((int)threadIdx.x < a.ntok) {
                 const float ss = serial_sumsq(xs + (size_t)threadIdx.x * a.cols, a.cols);
                 s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
-            }
-            __syncthreads();
-            for (int idx = threadIdx.x; idx < a.ntok * a.cols; idx += blockDim.x) {
-                const int t = idx / a.cols, i = idx - t * a.cols;
-                xs[idx] = __fmul_rn(__fmul_rn(xs[idx], s_scale[t]), ws[i]);
             }
         } else {
             // silu(gate) * up (engine.zig:2027-2036)
@@ -516,9 +516,18 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
         __syncthreads();
         if (a.family == 32) {
             const int nb = a.cols / 32;
-            for (int bi = threadIdx.x; bi < a.ntok * nb; bi += blockDim.x) {
-                const int t = bi / nb, b = bi - t * nb;
-                lpr_quant_q8_0_thread(xs + (size_t)t * a.cols + b * 32, act + (size_t)t * a.act_stride, a.cols, b);
+            const bool nrm = a.prologue == LPR_PRO_NORM;
+            // quads of threads per block; every quad of a warp takes part in
+            // the shuffles, so the loop runs whole-warp rounds
+            const int nq = a.ntok * nb * 4;
+            for (int base = warp * 32; base < nq; base += blockDim.x) {
+                const int qi = base + lane;
+                const int bi = qi >> 2, q = qi & 3;
+                const bool live = bi < a.ntok * nb;
+                const int bs = live ? bi : 0;  // lanes past the end redo block 0 without storing
+                const int t = bs / nb, b = bs - t * nb;
+                lpr_quant_q8_0_quad(xs + (size_t)t * a.cols + b * 32, act + (size_t)t * a.act_stride, a.cols, b, q,
+                                    live, nrm ? s_scale[t] : 0.0f, nrm ? ws + b * 32 : nullptr);
             }
         } else {
             const int nb = a.cols / 256;
@@ -529,6 +538,10 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
                 const float4 v0 = src[0], v1 = src[1];
                 v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
                 v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+                if (a.prologue == LPR_PRO_NORM) {
+#pragma unroll
+                    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(__fmul_rn(v[k], s_scale[t]), ws[b * 256 + lane * 8 + k]);
+                }
                 lpr_quant_q8_K(v, act + (size_t)t * a.act_stride, a.cols, b, lane);
             }
         }

@@ -455,3 +455,21 @@ def test_attn_chunk_equals_decode_rows(L):
                                     o.data_ptr(), slot0 + r, heads, heads // kvh, hd, kv_dim, 1 / 16, S))
         assert torch.equal(o, out[r])
     assert_no_kernel_error(L)
+
+
+def test_bounded_wait_ends_with_an_error_not_a_hang(L):
+    """failure detection without a GPU fault: a kernel whose wait is never
+    satisfied gives up after its limit, records a site code, and the context
+    keeps working"""
+    import time
+    assert_no_kernel_error(L)
+    t0 = time.time()
+    ok(L.q35b_selftest_wait(100, S))
+    assert time.time() - t0 < 5.0
+    code = ctypes.c_int(0)
+    ok(L.q35b_get_error(ctypes.byref(code)))
+    assert code.value == 150
+    # the context is still usable: a GEMV runs and is exact
+    got, ref = _gemv_case(L, load_oracle(), "Q8_0", 64, 512, 1, seed=3)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    assert_no_kernel_error(L)
