@@ -200,7 +200,7 @@ def time_e2e(run, steps, warmup, dist):
     return ms
 
 
-def time_prefill(cfg_name, ntok, chunk, seed, dist):
+def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False):
     """one prompt of ntok seeded tokens through q35b_engine_prefill (runs of
     `chunk` tokens: tensor-core projections, chunked GDN recurrence, causal
     attention), CUDA events on the stream the engine runs on"""
@@ -210,6 +210,7 @@ def time_prefill(cfg_name, ntok, chunk, seed, dist):
     from qwen35_b200 import model as q35
     synth = q35.SyntheticModel(q35.CONFIGS[cfg_name], seed=seed)
     eng = q35.Engine(synth, n_slots=1, max_seq=ntok + 8, max_batch=chunk)
+    eng.set_prefill_wy(wy)
     prompt = [int(t) for t in np.random.default_rng(seed + 5).integers(0, synth.cfg.vocab, ntok)]
     eng.reset_slot(0)
     eng.prefill(0, prompt)  # warm-up
@@ -228,6 +229,62 @@ def time_prefill(cfg_name, ntok, chunk, seed, dist):
     del synth
     torch.cuda.empty_cache()
     return ms
+
+
+def time_tp_decode(cfg_name, batch, ctx, steps, warmup, seed, dist, world, rank):
+    """batch-`batch` greedy decode at `ctx` context, tensor-parallel over all
+    `world` ranks (one engine per rank on its shard, NCCL all-reduce of the
+    row-parallel partials; world 1 is the whole model on one GPU).  The
+    context is synthetic: every slot steps from position `ctx` over the
+    engine's zeroed KV pools and a zero GDN state, which reads and writes the
+    same bytes per step as after a real prefill (values do not change the
+    work) without prefilling batch x ctx prompt tokens.  Returns (ms for
+    `steps` steps, max over ranks; this rank's weight bytes)."""
+    import numpy as np
+    import torch
+
+    from qwen35_b200 import model as q35
+    from qwen35_b200 import tp
+    cfg = q35.CONFIGS[cfg_name]
+    m = q35.SyntheticModel(cfg, seed=seed)  # same seed on every rank: one model
+    uid = None
+    if world > 1:
+        m = tp.ShardModel(m, world, rank)
+        torch.cuda.empty_cache()
+        uid = tp.shared_nccl_id(dist, "cuda")
+    wbytes = sum(t.numel() * t.element_size() for (_, _, _, t) in m.tensors.values())
+    max_seq = ctx + warmup + steps + 8
+    eng = q35.Engine(m, n_slots=batch, max_seq=max_seq, max_batch=batch, tp_id=uid)
+    i32 = torch.int32
+    toks = np.random.default_rng(seed + 3).integers(0, cfg.vocab, batch)
+    q35.device_view(eng.d_tokens, batch, i32).copy_(torch.tensor(toks, dtype=i32))
+    q35.device_view(eng.d_slots, batch, i32).copy_(torch.arange(batch, dtype=i32))
+    q35.device_view(eng.d_pos, batch, i32).fill_(ctx)
+    st = torch.cuda.current_stream()
+    s = ctypes.c_void_p(st.cuda_stream)
+
+    def run(k):
+        for _ in range(k):
+            rc = eng.L.q35b_engine_step_dev(eng.h, batch, max_seq, 1, s)
+            assert rc == 0, rc
+            rc = eng.L.q35b_engine_advance(eng.h, batch, s)
+            assert rc == 0, rc
+
+    run(warmup)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    run(steps)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist)
+    eng.close()  # its graphs hold NCCL work: released before the process group
+    del m
+    torch.cuda.empty_cache()
+    return ms, wbytes
 
 
 def max_over_ranks(v, dist):
@@ -462,10 +519,20 @@ def main():
             r.close()
             del r
             torch.cuda.empty_cache()
+        # 27B tensor-parallel over every rank of this run (strong scaling: the
+        # batch of 32 sequences at 4096 context is fixed)
+        ksteps = min(args.steps, 16)
+        tms, wb = time_tp_decode("27b", 32, 4096, ksteps, args.warmup, args.seed, dist, world, rank)
+        variants.append({"model": "qwen3.5-27b-q4_k", "tp": world, "batch": 32, "context": 4096,
+                         "context_fill": "synthetic (zero KV / GDN state, positions at 4096)",
+                         "steps": ksteps, "ms_per_step": tms / ksteps, "value": 32 * ksteps / (tms * 1e-3),
+                         "unit": "tokens/s", "scaling": "strong", "weight_bytes_per_rank": wb})
         for cfg_name, ntok, chunk in (("0.8b", 512, 256), ("4b", 512, 256)):
-            pms = time_prefill(cfg_name, ntok, chunk, args.seed + rank, dist)
-            variants.append({"model": cfg_name, "prefill_tokens": ntok, "chunk": chunk, "ms": pms,
-                             "value": world * ntok / (pms * 1e-3), "unit": "prefill tokens/s"})
+            for wy in (False, True):
+                pms = time_prefill(cfg_name, ntok, chunk, args.seed + rank, dist, wy)
+                variants.append({"model": cfg_name, "prefill_tokens": ntok, "chunk": chunk,
+                                 "gdn": "chunked WY" if wy else "per-token (exact)", "ms": pms,
+                                 "value": world * ntok / (pms * 1e-3), "unit": "prefill tokens/s"})
 
     if rank == 0:
         hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))

@@ -127,8 +127,9 @@ void *q35_func_rope64_rows_dpos(void);
 int q35_launch_rope64_setenv(int *d_dyn, int pos, float base, void *stream);
 
 /* gated delta net (api.h:256-335): bit-exact with the CPU gdnFused.
- * q35_launch_gdn_step_wy accepts the same arguments as the chunk form and
- * computes the identical per-token recurrence. */
+ * q35_launch_gdn_step_wy (api.h:290-308) takes the chunk form's arguments and
+ * solves the same recurrence in the WY form, 32 tokens per block: equal to
+ * the per-token kernels to f32 rounding, not bitwise. */
 int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
                              int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,
                              const float *d_gamma, const float *d_beta, int heads, int nk, int kd, int vd,
@@ -316,6 +317,12 @@ int q35b_engine_set_tp(q35b_engine *e, int nranks, int rank, long long vocab_loc
  * arrays; n <= max_batch.  Runs of one token use the step's CUDA graph. */
 int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int nrun,
                         const int *run_end, int *next, void *stream);
+
+/* Prefill runs (longer than one token) through the chunked WY form of the
+ * GDN recurrence (on) or token by token (off, the default).  WY re-associates
+ * the recurrence's sums: it agrees with the per-token form to rounding, not
+ * bitwise. */
+int q35b_engine_set_prefill_wy(q35b_engine *e, int on);
 
 /* Prompt prefill of one slot: ntok tokens from position pos0 as runs of up
  * to max_batch tokens (src/engine.zig:2078-2177, forwardChunk); *next = greedy token after

@@ -278,9 +278,23 @@ int q35_launch_gdn_step_wy(float *d_state, int state_stride, const float *d_k, i
                            int delta_stride, float *d_out, int out_stride, const float *d_gamma, int gamma_stride,
                            const float *d_beta, int beta_stride, int heads, int nk, int kd, int vd, int rows,
                            void *stream) {
-    return q35_launch_gdn_step_rows_chunk(d_state, state_stride, d_k, k_stride, d_v, v_stride, d_q, q_stride, d_km,
-                                          km_stride, d_delta, delta_stride, d_out, out_stride, d_gamma, gamma_stride,
-                                          d_beta, beta_stride, heads, nk, kd, vd, rows, stream);
+    if (heads <= 0 || rows <= 0) return 0;
+    if (vd != GDN_KD || kd != GDN_KD || nk <= 0 || nk > heads) return (int)cudaErrorInvalidValue;
+    const int prc = gdn_prepare();
+    if (prc) return prc;
+    GdnArgs a{};
+    a.state = d_state;
+    a.state_head = state_stride;
+    a.k = d_k; a.k_tok = k_stride; a.k_head = kd;
+    a.q = d_q; a.q_tok = q_stride; a.q_head = kd;
+    a.v = d_v; a.v_tok = v_stride; a.v_head = vd;
+    a.km = d_km; a.km_tok = km_stride; a.km_head = vd;
+    a.delta = d_delta; a.delta_tok = delta_stride; a.delta_head = vd;
+    a.out = d_out; a.out_tok = out_stride; a.out_head = vd;
+    a.gamma = d_gamma; a.g_tok = gamma_stride;
+    a.beta = d_beta; a.b_tok = beta_stride;
+    a.heads = heads; a.nk = nk; a.rows = rows;
+    return gdn_wy_rows_launch(a, S(stream));
 }
 int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
                              int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,

@@ -230,12 +230,6 @@ constexpr int ATTX_KLD = ATT_HD + 4;       // shared K row stride (floats): 1040
 constexpr int ATTX_DIMS = 64;
 constexpr int ATTX_VT = 128;               // positions per V tile
 
-Q35_DEV void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-Q35_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-Q35_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 struct AttnXArgs {
     const float *q, *gate;

@@ -217,6 +217,7 @@ struct q35b_engine {
     float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;
     float *logits = nullptr, *scores = nullptr, *probe_buf = nullptr;
     float *xh = nullptr;  // last row of each run, gathered for the model head
+    bool gdn_wy = false;  // prefill runs through the chunked (WY) GDN form
     // tensor parallelism (1 rank: off)
     int tp_n = 1, tp_rank = 0;
     long long vocab_local = 0, vocab_off = 0;  // this rank's lm_head rows
@@ -338,7 +339,10 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, int nrun, cudaStream_t s
     g.xq_ld = e->xq_ld;
     g.gout = e->gout;
     g.gout_ld = vdim;
-    Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), (size_t)GDN_KD * GDN_KD * 4, st, g));
+    if (g.run_end && e->gdn_wy)
+        Q35_TRY(launch_k(k_gdn_wy, dim3(nv, nrun), dim3(GDN_KD), WY_SMEM, st, g));
+    else
+        Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), (size_t)GDN_KD * GDN_KD * 4, st, g));
     if (g.run_end)
         Q35_TRY(launch_k(k_gdn_hist_settle, dim3((unsigned)((conv_dim * 3 + 255) / 256), (unsigned)nrun), dim3(256), 0,
                          st, g.hist, g.hist_slot, conv_dim, g.slots, g.pos, g.run_end));

@@ -57,6 +57,12 @@ int q35b_engine_destroy(q35b_engine *e) {
     return 0;
 }
 
+int q35b_engine_set_prefill_wy(q35b_engine *e, int on) {
+    if (!e) return (int)cudaErrorInvalidValue;
+    e->gdn_wy = on != 0;
+    return 0;
+}
+
 int q35b_tp_unique_id(void *out, int bytes) {
     const NcclApi &api = nccl_api();
     if (!api.ok) return (int)cudaErrorSharedObjectInitFailed;
@@ -210,6 +216,10 @@ int q35b_engine_finalize(q35b_engine *e) {
 #undef ALLOC
     Q35_TRY((int)cudaMemset(e->conv_pool, 0, 4 * ngdn * S * e->conv_slot));
     Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));
+    // KV pools start as finite zeros (positions past a slot's length are never
+    // read; a caller that steps at a position it never filled reads zeros)
+    Q35_TRY((int)cudaMemset(e->kpool, 0, 4 * nfull * S * e->kv_slot));
+    Q35_TRY((int)cudaMemset(e->vpool, 0, 4 * nfull * S * e->kv_slot));
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 4 * B));
     // load-time repack: Q6_K projections to 224-byte blocks (16-byte rows for
     // the TMA-streamed GEMV); the caller's buffers stay untouched

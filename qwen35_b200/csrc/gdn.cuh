@@ -18,6 +18,18 @@
 
 namespace q35 {
 
+// asynchronous global -> shared copies (LDGSTS): 16 bytes through L2 only,
+// 4 bytes through L1; a thread's own copies are visible to it after the wait
+Q35_DEV void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+Q35_DEV void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+Q35_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+Q35_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 constexpr int GDN_KD = 128;
 
 struct GdnArgs {
@@ -199,12 +211,35 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
         s_h[c][2][j] = cur;
         return silu_f(s);
     };
-    for (int b = i0; b < i1; b++) {
+    // the next token's inputs are copied (cp.async, no registers held) while
+    // this one is stepped: a run's tokens would otherwise each wait a full L2
+    // round trip first.  Thread j copies and reads only its own slots.
+    __shared__ float s_in[2][4][GDN_KD], s_gab[2][2];
+    auto fetch = [&](int b) {
+        const int pb = b & 1;
         const float *raw = a.qkv + (long long)b * a.qkv_ld;
-        const float cq = raw[chq], ck = raw[chk], cv = raw[chv];
-        const float zj = a.z[(long long)b * a.z_ld + (long long)h * kd + j];
-        const float *ar = a.ab + (long long)b * a.ab_ld;
-        const float a_raw = ar[h], b_raw = ar[a.nv + h];
+        cp_async4(&s_in[pb][0][j], raw + chq);
+        cp_async4(&s_in[pb][1][j], raw + chk);
+        cp_async4(&s_in[pb][2][j], raw + chv);
+        cp_async4(&s_in[pb][3][j], a.z + (long long)b * a.z_ld + (long long)h * kd + j);
+        if (j == 64) {
+            const float *ar = a.ab + (long long)b * a.ab_ld;
+            cp_async4(&s_gab[pb][0], ar + h);
+            cp_async4(&s_gab[pb][1], ar + a.nv + h);
+        }
+        cp_async_commit();
+    };
+    fetch(i0);
+    for (int b = i0; b < i1; b++) {
+        if (b + 1 < i1) {
+            fetch(b + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        const int pb = b & 1;
+        const float cq = s_in[pb][0][j], ck = s_in[pb][1][j], cv = s_in[pb][2][j], zj = s_in[pb][3][j];
+        const float a_raw = j == 64 ? s_gab[pb][0] : 0.0f, b_raw = j == 64 ? s_gab[pb][1] : 0.0f;
         sq[j] = conv(0, cq);
         sk[j] = conv(1, ck);
         const float vj = conv(2, cv);
@@ -286,12 +321,364 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     store(2);
 }
 
+// ---------------------------------------------------------------------------
+// Chunked (WY) form of the same recurrence (the reference's q35_gdn_step_wy,
+// gdn.cu:452-631): per chunk of WY_C tokens, with cumulative log decay
+// L_t = sum_{s<=t} log g_s and decay(t, s) = exp(L_t - L_s),
+//   km_t    = exp(L_t) S0^T k_t + sum_{s<t} decay(t,s) (k_t.k_s) delta_s
+//   delta_t = beta_t (v_t - km_t)
+//   o_t     = exp(L_t) S0^T q_t + sum_{s<=t} decay(t,s) (q_t.k_s) delta_s
+//   S       = exp(L_C) S0 + sum_s decay(C,s) k_s delta_s^T
+// which unrolls  S_t = g_t S_{t-1} + k_t delta_t^T,
+// km_t = g_t S_{t-1}^T k_t, o_t = S_t^T q_t  exactly; the sums are
+// re-associated (f32, fused multiply-adds), so this form agrees with the
+// per-token kernels to f32 rounding, not bitwise.
+// CTA per (value head, run), thread j owns state column j (128 registers);
+// the chunk's q / k / v rows sit in shared memory with a 132-float pitch
+// (an odd multiple of 16 bytes: float4 row reads by 8 lanes of different
+// rows hit 8 distinct bank quads).
+// ---------------------------------------------------------------------------
+constexpr int WY_C = 32;
+constexpr int WY_LD = GDN_KD + 4;
+constexpr size_t WY_SMEM = (size_t)GDN_KD * GDN_KD * 4 + (size_t)5 * WY_C * WY_LD * 4 +
+                           (size_t)2 * WY_C * (WY_C + 1) * 4 + (size_t)8 * WY_C * 4;
+constexpr float WY_LOG_MIN = -88.0f;  // log decay floor: exp() of it is ~0, sums stay finite
+
+struct WyBufs {
+    float *Qs, *Ks, *Vs;  // [C][WY_LD] chunk rows (q scaled and normalised, k normalised)
+    float *Us, *Ws;       // [C][WY_LD] S0^T k_t, S0^T q_t; Us then holds o_t
+    float *Am, *Mm;       // [C][C+1] decay(t,s) k_t.k_s (s < t), decay(t,s) q_t.k_s (s <= t)
+    float *Lc;            // [C] cumulative log decay
+    float *eL, *eE;       // [C] exp(L_t), exp(L_end - L_t)
+    float *bet;           // [C]
+};
+
+__device__ __forceinline__ WyBufs wy_bufs(float *base) {
+    WyBufs m;
+    m.Qs = base;
+    m.Ks = m.Qs + WY_C * WY_LD;
+    m.Vs = m.Ks + WY_C * WY_LD;
+    m.Us = m.Vs + WY_C * WY_LD;
+    m.Ws = m.Us + WY_C * WY_LD;
+    m.Am = m.Ws + WY_C * WY_LD;
+    m.Mm = m.Am + WY_C * (WY_C + 1);
+    m.Lc = m.Mm + WY_C * (WY_C + 1);
+    m.eL = m.Lc + WY_C;
+    m.eE = m.eL + WY_C;
+    m.bet = m.eE + WY_C;
+    return m;
+}
+
+// cumulative log decay of the chunk from per-token log decays lg[0..nc)
+// (thread 127; the caller synchronises before and after)
+__device__ __forceinline__ void wy_cumulate(const WyBufs &m, const float *lg, int nc, int j) {
+    if (j == GDN_KD - 1) {
+        float L = 0.0f;
+        for (int t = 0; t < nc; t++) {
+            L = __fadd_rn(L, lg[t]);
+            m.Lc[t] = L;
+        }
+    }
+}
+
+// One chunk for state column j (col).  On entry Qs / Ks / Vs, Lc and bet
+// hold the chunk's nc tokens and every thread has passed a barrier since
+// they were written.  On exit Us[t][j] = o_t, col is the state after the
+// chunk, and sink(t, km_t, delta_t) has seen every token; the caller
+// synchronises before the buffers are reused.
+template <class Sink>
+__device__ __forceinline__ void wy_chunk(float (&col)[GDN_KD], const WyBufs &m, int nc, int j, Sink sink) {
+    const int warp = j >> 5, lane = j & 31;
+    if (j < nc) {
+        m.eL[j] = expf(m.Lc[j]);
+        m.eE[j] = expf(m.Lc[nc - 1] - m.Lc[j]);
+    }
+    // U = S0^T k_t, W = S0^T q_t (column j); four partial sums per dot
+    // (i mod 4) keep eight independent FMA chains in flight
+    for (int t = 0; t < nc; t++) {
+        const float4 *k4 = reinterpret_cast<const float4 *>(m.Ks + t * WY_LD);
+        const float4 *q4 = reinterpret_cast<const float4 *>(m.Qs + t * WY_LD);
+        float u0 = 0.0f, u1 = 0.0f, u2 = 0.0f, u3 = 0.0f, w0 = 0.0f, w1 = 0.0f, w2 = 0.0f, w3 = 0.0f;
+#pragma unroll
+        for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+            const float4 kv = k4[i4], qv = q4[i4];
+            u0 = __fmaf_rn(col[4 * i4], kv.x, u0);
+            u1 = __fmaf_rn(col[4 * i4 + 1], kv.y, u1);
+            u2 = __fmaf_rn(col[4 * i4 + 2], kv.z, u2);
+            u3 = __fmaf_rn(col[4 * i4 + 3], kv.w, u3);
+            w0 = __fmaf_rn(col[4 * i4], qv.x, w0);
+            w1 = __fmaf_rn(col[4 * i4 + 1], qv.y, w1);
+            w2 = __fmaf_rn(col[4 * i4 + 2], qv.z, w2);
+            w3 = __fmaf_rn(col[4 * i4 + 3], qv.w, w3);
+        }
+        m.Us[t * WY_LD + j] = (u0 + u1) + (u2 + u3);
+        m.Ws[t * WY_LD + j] = (w0 + w1) + (w2 + w3);
+    }
+    // A and M: lane = s, warp w takes t = w, w + 4, ...
+    {
+        const int s = lane;
+        const float4 *ks4 = reinterpret_cast<const float4 *>(m.Ks + s * WY_LD);
+        for (int t = warp; t < nc; t += 4) {
+            const float4 *kt4 = reinterpret_cast<const float4 *>(m.Ks + t * WY_LD);
+            const float4 *qt4 = reinterpret_cast<const float4 *>(m.Qs + t * WY_LD);
+            float kk = 0.0f, qk = 0.0f;
+            if (s <= t) {
+                float k0 = 0.0f, k1 = 0.0f, k2 = 0.0f, k3 = 0.0f, q0 = 0.0f, q1 = 0.0f, q2 = 0.0f, q3 = 0.0f;
+#pragma unroll 8
+                for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+                    const float4 x = ks4[i4], y = kt4[i4], z = qt4[i4];
+                    k0 = __fmaf_rn(y.x, x.x, k0);
+                    k1 = __fmaf_rn(y.y, x.y, k1);
+                    k2 = __fmaf_rn(y.z, x.z, k2);
+                    k3 = __fmaf_rn(y.w, x.w, k3);
+                    q0 = __fmaf_rn(z.x, x.x, q0);
+                    q1 = __fmaf_rn(z.y, x.y, q1);
+                    q2 = __fmaf_rn(z.z, x.z, q2);
+                    q3 = __fmaf_rn(z.w, x.w, q3);
+                }
+                kk = (k0 + k1) + (k2 + k3);
+                qk = (q0 + q1) + (q2 + q3);
+            }
+            const float dec = s <= t ? expf(m.Lc[t] - m.Lc[s]) : 0.0f;
+            m.Am[t * (WY_C + 1) + s] = s < t ? dec * kk : 0.0f;
+            m.Mm[t * (WY_C + 1) + s] = s <= t ? dec * qk : 0.0f;
+        }
+    }
+    __syncthreads();
+    // forward substitution for km / delta of column j, then the outputs
+    float dl[WY_C];
+#pragma unroll
+    for (int t = 0; t < WY_C; t++) {
+        dl[t] = 0.0f;
+        if (t < nc) {
+            float km = m.eL[t] * m.Us[t * WY_LD + j];
+#pragma unroll
+            for (int s = 0; s < t; s++) km = __fmaf_rn(m.Am[t * (WY_C + 1) + s], dl[s], km);
+            dl[t] = m.bet[t] * (m.Vs[t * WY_LD + j] - km);
+            sink(t, km, dl[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < WY_C; t++) {
+        if (t < nc) {
+            float o = m.eL[t] * m.Ws[t * WY_LD + j];
+#pragma unroll
+            for (int s = 0; s <= t; s++) o = __fmaf_rn(m.Mm[t * (WY_C + 1) + s], dl[s], o);
+            m.Us[t * WY_LD + j] = o;  // U no longer needed: o_t
+        }
+    }
+    // state: exp(L_end) S0 + sum_t decay(end, t) k_t delta_t^T, t ascending
+    const float gend = m.eL[nc - 1];
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) col[i] = gend * col[i];
+#pragma unroll
+    for (int t = 0; t < WY_C; t++) {
+        if (t < nc) {
+            const float e = m.eE[t] * dl[t];
+            const float4 *k4 = reinterpret_cast<const float4 *>(m.Ks + t * WY_LD);
+#pragma unroll
+            for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+                const float4 kv = k4[i4];
+                col[4 * i4] = __fmaf_rn(kv.x, e, col[4 * i4]);
+                col[4 * i4 + 1] = __fmaf_rn(kv.y, e, col[4 * i4 + 1]);
+                col[4 * i4 + 2] = __fmaf_rn(kv.z, e, col[4 * i4 + 2]);
+                col[4 * i4 + 3] = __fmaf_rn(kv.w, e, col[4 * i4 + 3]);
+            }
+        }
+    }
+}
+
+struct WyNoSink {
+    __device__ void operator()(int, float, float) const {}
+};
+
+// The engine's GDN layer core over prefill runs in the WY form: the same
+// conv / gates / l2 norms / gated RMSNorm as k_gdn_core around wy_chunk.
+__global__ void __launch_bounds__(GDN_KD) k_gdn_wy(const __grid_constant__ GdnCoreArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(128) float smw[];
+    float *s_state = smw;  // [kd][kd] (bulk copy)
+    const WyBufs m = wy_bufs(s_state + GDN_KD * GDN_KD);
+    float *lg = m.bet + WY_C;  // [C] log g_t
+    float *scq = lg + WY_C, *sck = scq + WY_C, *sco = sck + WY_C;
+    __shared__ __align__(8) uint64_t s_bar;
+    __shared__ int s_ok;
+    __shared__ float s_h[3][3][GDN_KD], s_w[3][4][GDN_KD];
+    const int h = blockIdx.x, r = blockIdx.y, j = threadIdx.x, warp = j >> 5, lane = j & 31;
+    const int kd = GDN_KD, kq = a.nk * kd, conv_dim = 2 * kq + a.nv * kd;
+    const int kh = h % a.nk;
+    const int i0 = a.run_end ? (r == 0 ? 0 : a.run_end[r - 1]) : r;
+    const int i1 = a.run_end ? a.run_end[r] : r + 1;
+    const long long slot = a.slots[i0];
+    const int p0 = a.pos[i0];
+    const float *hin = a.hist + slot * a.hist_slot + (long long)(p0 & 1) * conv_dim * 3;
+    float *hout = a.hist + slot * a.hist_slot + (long long)((p0 & 1) ^ 1) * conv_dim * 3;
+    float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
+    if (j == 0) {
+        mbar_init(&s_bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&s_bar, (uint32_t)(kd * kd * 4));
+        bulk_g2s(s_state, S, (uint32_t)(kd * kd * 4), &s_bar);
+    }
+    const int chq = kh * kd + j, chk = kq + kh * kd + j, chv = 2 * kq + h * kd + j;
+    const int chs[3] = {chq, chk, chv};
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+#pragma unroll
+        for (int i = 0; i < 3; i++) s_h[c][i][j] = hin[(long long)chs[c] * 3 + i];
+#pragma unroll
+        for (int i = 0; i < 4; i++) s_w[c][i][j] = a.conv_w[(long long)chs[c] * 4 + i];
+    }
+    const float nwj = a.ssm_norm[j];
+    const float ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
+    if (j == 0) s_ok = mbar_wait(&s_bar, 0u, 142) ? 1 : 0;
+    __syncthreads();
+    if (!s_ok) {
+        if (j == 0) mbar_wait(&s_bar, 0u, 143);
+        return;
+    }
+    float col[GDN_KD];
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) col[i] = s_state[i * GDN_KD + j];
+    auto conv = [&](int c, float cur) {
+        const float sm = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(s_h[c][0][j], s_w[c][0][j]),
+                                                       __fmul_rn(s_h[c][1][j], s_w[c][1][j])),
+                                             __fmul_rn(s_h[c][2][j], s_w[c][2][j])),
+                                   __fmul_rn(cur, s_w[c][3][j]));
+        s_h[c][0][j] = s_h[c][1][j];
+        s_h[c][1][j] = s_h[c][2][j];
+        s_h[c][2][j] = cur;
+        return silu_f(sm);
+    };
+    for (int t0 = i0; t0 < i1; t0 += WY_C) {
+        const int nc = min(WY_C, i1 - t0);
+        // 1. q, k, v of every token: the raw inputs first (independent loads),
+        //    then the conv in token order (history advanced in order), gates
+#pragma unroll 4
+        for (int t = 0; t < nc; t++) {
+            const float *raw = a.qkv + (long long)(t0 + t) * a.qkv_ld;
+            m.Qs[t * WY_LD + j] = raw[chq];
+            m.Ks[t * WY_LD + j] = raw[chk];
+            m.Vs[t * WY_LD + j] = raw[chv];
+        }
+        for (int t = 0; t < nc; t++) {
+            m.Qs[t * WY_LD + j] = conv(0, m.Qs[t * WY_LD + j]);
+            m.Ks[t * WY_LD + j] = conv(1, m.Ks[t * WY_LD + j]);
+            m.Vs[t * WY_LD + j] = conv(2, m.Vs[t * WY_LD + j]);
+        }
+        if (j < nc) {
+            const float *ar = a.ab + (long long)(t0 + j) * a.ab_ld;
+            // log of k_gdn_core's gamma, floored
+            lg[j] = fmaxf(__fmul_rn(ssm_a, softplus_f(__fadd_rn(ar[h], dtb))), WY_LOG_MIN);
+            m.bet[j] = sigmoid_f(ar[a.nv + h]);
+        }
+        __syncthreads();
+        // 2. l2norm scales (serial sums, as k_gdn_core), cumulative log decay
+        if (j < nc) scq[j] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(serial_sumsq(m.Qs + j * WY_LD, kd), 1e-6f)));
+        if (j >= 64 && j < 64 + nc)
+            sck[j - 64] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(serial_sumsq(m.Ks + (j - 64) * WY_LD, kd), 1e-6f)));
+        wy_cumulate(m, lg, nc, j);
+        __syncthreads();
+        for (int t = 0; t < nc; t++) {
+            m.Qs[t * WY_LD + j] = __fmul_rn(__fmul_rn(m.Qs[t * WY_LD + j], scq[t]), a.qscale);
+            m.Ks[t * WY_LD + j] = __fmul_rn(m.Ks[t * WY_LD + j], sck[t]);
+        }
+        __syncthreads();
+        // 3. the recurrence over the chunk
+        wy_chunk(col, m, nc, j, WyNoSink{});
+        __syncthreads();
+        // 4. gated RMSNorm (serial sums, as k_gdn_core) x silu(z), quantized per token
+        if (j < nc)
+            sco[j] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(serial_sumsq(m.Us + j * WY_LD, kd), (float)kd), a.eps)));
+        __syncthreads();
+        for (int t = 0; t < nc; t++) {
+            const long long b = t0 + t;
+            float y = __fmul_rn(__fmul_rn(m.Us[t * WY_LD + j], sco[t]), nwj);
+            y = __fmul_rn(y, silu_f(a.z[b * a.z_ld + (long long)h * kd + j]));
+            if (a.fam == 32)
+                quant_q8_0_warp(y, a.xq + b * a.xq_ld + (long long)(h * (kd / 32) + warp) * 34, lane);
+            else
+                a.gout[b * a.gout_ld + (long long)h * kd + j] = y;
+        }
+        __syncthreads();  // chunk buffers reused
+    }
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
+    auto store = [&](int c) {
+        float *ho = hout + (long long)chs[c] * 3;
+        ho[0] = s_h[c][0][j];
+        ho[1] = s_h[c][1][j];
+        ho[2] = s_h[c][2][j];
+    };
+    if (h < a.nk) {
+        store(0);
+        store(1);
+    }
+    store(2);
+}
+
+// The operator form (q35_launch_gdn_step_wy, api.h:290-308): q / k already
+// normalised, gamma / beta given per token; writes out, km, delta and the
+// state like the per-token k_gdn_step over `rows` tokens of one sequence.
+// CTA per value head; the state column streams from HBM straight into
+// registers (no shared copy: the chunk buffers need the room).
+__global__ void __launch_bounds__(GDN_KD) k_gdn_wy_rows(const __grid_constant__ GdnArgs a) {
+    extern __shared__ __align__(128) float smr[];
+    const WyBufs m = wy_bufs(smr);
+    float *lg = m.bet + WY_C;
+    const int h = blockIdx.x, j = threadIdx.x;
+    const int kh = h % a.nk;
+    float *S = a.state + h * a.state_head;
+    float col[GDN_KD];
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) col[i] = S[(long long)i * GDN_KD + j];
+    for (int t0 = 0; t0 < a.rows; t0 += WY_C) {
+        const int nc = min(WY_C, a.rows - t0);
+        for (int t = 0; t < nc; t++) {
+            const long long tok = t0 + t;
+            m.Qs[t * WY_LD + j] = a.q[tok * a.q_tok + kh * a.q_head + j];
+            m.Ks[t * WY_LD + j] = a.k[tok * a.k_tok + kh * a.k_head + j];
+            m.Vs[t * WY_LD + j] = a.v[tok * a.v_tok + h * a.v_head + j];
+        }
+        if (j < nc) {
+            const long long tok = t0 + j;
+            lg[j] = fmaxf(logf(a.gamma ? a.gamma[tok * a.g_tok + h] : a.gamma_imm), WY_LOG_MIN);
+            m.bet[j] = a.beta ? a.beta[tok * a.b_tok + h] : a.beta_imm;
+        }
+        __syncthreads();
+        wy_cumulate(m, lg, nc, j);
+        __syncthreads();
+        auto sink = [&](int t, float km, float d) {
+            const long long tok = t0 + t;
+            if (a.km) a.km[tok * a.km_tok + h * a.km_head + j] = km;
+            if (a.delta) a.delta[tok * a.delta_tok + h * a.delta_head + j] = d;
+        };
+        wy_chunk(col, m, nc, j, sink);
+        for (int t = 0; t < nc; t++) a.out[(t0 + t) * a.out_tok + h * a.out_head + j] = m.Us[t * WY_LD + j];
+        __syncthreads();  // chunk buffers reused
+    }
+#pragma unroll
+    for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
+}
+
+constexpr size_t WY_ROWS_SMEM = WY_SMEM - (size_t)GDN_KD * GDN_KD * 4;
+
+inline int gdn_wy_rows_launch(const GdnArgs &a, cudaStream_t st) {
+    if (a.heads <= 0 || a.rows <= 0) return 0;
+    if (a.nk <= 0) return (int)cudaErrorInvalidValue;
+    k_gdn_wy_rows<<<(unsigned)a.heads, GDN_KD, WY_ROWS_SMEM, st>>>(a);
+    return (int)cudaGetLastError();
+}
+
 // k_gdn_core stages the 64 KB state block in dynamic shared memory
 inline int gdn_prepare() {
     static int done = 0;
     if (done) return 0;
-    const cudaError_t e =
-        cudaFuncSetAttribute(k_gdn_core, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_KD * GDN_KD * 4);
+    cudaError_t e = cudaFuncSetAttribute(k_gdn_core, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_KD * GDN_KD * 4);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gdn_wy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gdn_wy_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_ROWS_SMEM);
     if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;

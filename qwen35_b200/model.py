@@ -75,6 +75,11 @@ CONFIGS = {
     "tiny-tp-mixed": ModelConfig("tiny-tp-mixed", 4, 512, 1024, 4096, 4, 2, 8, 4,
                                  quant=(("bulk", "IQ4_NL"), ("ffn_down", "Q5_K"), ("ssm_alpha", "Q8_0"),
                                         ("ssm_beta", "Q8_0"), ("output", "Q6_K"), ("attn_output", "Q4_K"))),
+    # the 27B TP-8 shapes in small: one kv head replicated on both ranks, an
+    # odd count of ffn blocks (3 -> 2 + 1), Q4_K bulk with a Q6_K lm_head
+    # (GDN value heads in pairs: ssm_out columns in whole 256-blocks)
+    "tiny-tp-rep": ModelConfig("tiny-tp-rep", 4, 512, 768, 4096, 4, 1, 8, 4,
+                               quant=(("bulk", "Q4_K"), ("output", "Q6_K"))),
 }
 
 
@@ -233,6 +238,9 @@ class Engine:
         check(self.L.q35b_engine_forward(self.h, n, arr(*tokens), arr(*slots), arr(*pos), nrun,
                                          (ctypes.c_int * nrun)(*run_end), nx, _stream(stream)), "forward")
         return list(nx)
+
+    def set_prefill_wy(self, on):
+        check(self.L.q35b_engine_set_prefill_wy(self.h, 1 if on else 0), "set_prefill_wy")
 
     def prefill(self, slot, tokens, pos0=0, stream=None):
         """prompt prefill of one slot (q35b_engine_prefill); returns the greedy

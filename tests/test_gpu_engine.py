@@ -179,6 +179,40 @@ def test_prefill_chunks_equal_token_steps(q35, cfg_name):
     eng.close()
 
 
+@pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed"])
+def test_wy_prefill_matches_per_token(q35, cfg_name):
+    """the engine's chunked WY GDN form over a 70-token prompt run (3 chunks
+    of <= 32) against the exact per-token recurrence: the same greedy tokens.
+    Layer outputs are compared loosely: the GDN output is quantized (Q8_0 /
+    Q8_K) before ssm_out, so the WY form's f32-rounding differences (bounded
+    at 1e-4 per op by test_gdn_wy_matches_per_token) either vanish or flip a
+    whole quantum now and then, and a flip propagates through later layers
+    and tokens of a random-weight network: the first layer stays within
+    2e-3, every layer within 0.1"""
+    cfg = q35.CONFIGS[cfg_name]
+    synth = q35.SyntheticModel(cfg, seed=31)
+    rng = np.random.default_rng(31)
+    prompt = [int(t) for t in rng.integers(0, cfg.vocab, 70)]
+    res = []
+    for wy in (False, True):
+        eng = q35.Engine(synth, n_slots=1, max_seq=96, max_batch=80)
+        eng.set_prefill_wy(wy)
+        eng.set_probe(True)
+        eng.reset_slot(0)
+        nxt = eng.prefill(0, prompt)
+        layers = [eng.layer_out(li, len(prompt)).cpu().numpy() for li in range(cfg.n_layers)]
+        toks = [nxt]
+        for pos in range(len(prompt), len(prompt) + 5):
+            toks.append(eng.step_host([toks[-1]], [0], [pos])[0])
+        res.append((layers, toks))
+        eng.close()
+    (le, te), (lw, tw) = res
+    rels = [np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b) for a, b in zip(lw, le)]
+    assert rels[0] < 2e-3, rels
+    assert max(rels) < 0.1, rels
+    assert tw == te
+
+
 def test_forward_mixes_prefill_and_decode_runs(q35):
     """one forward with a decode token of sequence A and a 9-token prompt run of
     sequence B gives each the token it gets alone"""

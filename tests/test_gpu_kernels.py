@@ -331,6 +331,46 @@ def test_gdn_chunk_equals_rows(L, O):
     assert np.array_equal(host(dout).view(np.uint32), rout.view(np.uint32))
 
 
+def _wy_inputs(rng, heads, nk, kd, rows, decay_scale=1.0):
+    """config-3 statistics: q / k l2-normalised (q also x 1/sqrt(kd)),
+    v ~ N(0,1), beta = sigmoid(N(0,1)), gamma = exp(-softplus(N(0,1)))"""
+    def l2n(x):
+        return x / np.sqrt((x.astype(np.float64) ** 2).sum(-1, keepdims=True) + 1e-6)
+    k = l2n(rng.standard_normal((rows, nk, kd))).astype(np.float32)
+    q = (l2n(rng.standard_normal((rows, nk, kd))) / np.sqrt(kd)).astype(np.float32)
+    v = rng.standard_normal((rows, heads, kd)).astype(np.float32)
+    bet = (1 / (1 + np.exp(-rng.standard_normal((rows, heads))))).astype(np.float32)
+    gam = np.exp(-decay_scale * np.log1p(np.exp(rng.standard_normal((rows, heads))))).astype(np.float32)
+    state = (rng.standard_normal((heads, kd, kd)) * 0.1).astype(np.float32)
+    return k, q, v, bet, gam, state
+
+
+@pytest.mark.parametrize("rows,decay_scale", [(525, 1.0), (33, 1.0), (7, 1.0), (96, 0.02), (64, 60.0)])
+def test_gdn_wy_matches_per_token(L, rows, decay_scale):
+    """q35_launch_gdn_step_wy (WY form, 32-token blocks) against the per-token
+    chunk kernel on the same inputs: out, km, delta and the final state
+    within 1e-4 relative L2 (the reference records 1.6e-7..1.8e-6 for its WY
+    kernel at rows = 525, api.h:290-296).  Covers a ragged last block, fewer
+    rows than one block, slow decay (gamma ~ 0.99) and decay strong enough
+    that gamma underflows toward 0."""
+    rng = np.random.default_rng(rows)
+    heads, nk, kd = 4, 2, 128
+    k, q, v, bet, gam, state = _wy_inputs(rng, heads, nk, kd, rows, decay_scale)
+    dk, dq, dv, db, dg = dev(k), dev(q), dev(v), dev(bet), dev(gam)
+    outs = []
+    for fn in (L.q35_launch_gdn_step_rows_chunk, L.q35_launch_gdn_step_wy):
+        ds = dev(state)
+        dkm, ddl, dout = (torch.zeros((rows, heads * kd), device="cuda") for _ in range(3))
+        ok(fn(ds.data_ptr(), kd * kd, dk.data_ptr(), nk * kd, dv.data_ptr(), heads * kd, dq.data_ptr(), nk * kd,
+              dkm.data_ptr(), heads * kd, ddl.data_ptr(), heads * kd, dout.data_ptr(), heads * kd,
+              dg.data_ptr(), heads, db.data_ptr(), heads, heads, nk, kd, kd, rows, S))
+        outs.append([host(t).astype(np.float64) for t in (dout, dkm, ddl, ds)])
+    for name, a, b in zip(("out", "km", "delta", "state"), outs[1], outs[0]):
+        assert np.isfinite(a).all(), name
+        rel = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+        assert rel < 1e-4, (name, rel)
+
+
 def test_conv_gamma_exact_paths(L, O):
     rng = np.random.default_rng(7)
     n, tokens = 768, 3

@@ -46,21 +46,12 @@ def _worker(rank, world, port, out_dir, cfg_name):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
-    from qwen35_b200 import lib, tp
+    from qwen35_b200 import tp
     from qwen35_b200 import model as q35
-    L = lib.load()
     cfg = q35.CONFIGS[cfg_name]
     full = q35.SyntheticModel(cfg, seed=21)
     shard = tp.ShardModel(full, world, rank)
-    buf = (torch.zeros(128, dtype=torch.uint8)).numpy()
-    if rank == 0:
-        import ctypes
-        raw = ctypes.create_string_buffer(128)
-        assert L.q35b_tp_unique_id(ctypes.cast(raw, ctypes.c_void_p), 128) == 0
-        buf = np.frombuffer(bytes(raw), dtype=np.uint8).copy()
-    t = torch.from_numpy(buf).cuda()
-    dist.broadcast(t, 0)
-    uid = t.cpu().numpy().tobytes()
+    uid = tp.shared_nccl_id(dist, torch.device("cuda", rank))
     eng = q35.Engine(shard, n_slots=2, max_seq=64, max_batch=4, tp_id=uid)
     eng.set_probe(True)
     prompt = [int(v) for v in np.random.default_rng(21).integers(0, cfg.vocab, 6)]
@@ -80,7 +71,7 @@ def _worker(rank, world, port, out_dir, cfg_name):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("cfg_name", ["tiny-tp", "tiny-tp-mixed"])
+@pytest.mark.parametrize("cfg_name", ["tiny-tp", "tiny-tp-mixed", "tiny-tp-rep"])
 def test_tp2_matches_single_gpu(cfg_name):
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_worker, args=(2, _free_port(), d, cfg_name), nprocs=2, start_method="spawn")

@@ -22,11 +22,12 @@ def fake_tensors(cfg, seed=0):
     return out
 
 
-@pytest.mark.parametrize("cfg_name,P", [("tiny-tp", 2), ("tiny-tp-mixed", 2), ("tiny-tp-mixed", 4)])
+@pytest.mark.parametrize("cfg_name,P", [("tiny-tp", 2), ("tiny-tp-mixed", 2), ("tiny-tp-mixed", 4),
+                                         ("tiny-tp-rep", 2)])
 def test_shards_reassemble(cfg_name, P):
+    """replicated kv heads write the same rows from several ranks; uneven ffn
+    shards still cover every block once"""
     cfg = CONFIGS[cfg_name]
-    if cfg.n_kv_heads % P or cfg.gdn_num_k_heads % P or cfg.n_heads % P:
-        pytest.skip("does not split")
     full = fake_tensors(cfg)
     shards = [tp.shard_tensors(cfg, full, P, p) for p in range(P)]
     plan = [tp.shard_plan(cfg, P, p) for p in range(P)]
@@ -63,14 +64,24 @@ def test_shards_reassemble(cfg_name, P):
 
 
 def test_gdn_head_map_stays_local():
-    """value head h = p + P*i uses k head h % nk = p + P*(i % (nk/P)): the
-    local index i % (nk/P) of a k head this rank holds"""
-    for nv, nk, P in [(48, 16, 2), (48, 16, 4), (32, 16, 8), (16, 16, 2), (4, 2, 2)]:
+    """the local value head l (global h) reads local k head l % (nk/P), which
+    is global k head h % nk, for head groups of 1 (32-element blocks) and 2
+    (256-element blocks)"""
+    import dataclasses
+    for nv, nk, P, ssm_out in [(48, 16, 2, "Q4_K"), (48, 16, 4, "Q4_K"), (48, 16, 8, "Q4_K"), (32, 16, 8, "IQ4_NL"),
+                               (16, 16, 2, "Q8_0"), (4, 2, 2, "Q8_0"), (8, 4, 2, "Q4_K"), (32, 16, 4, "Q5_K")]:
+        cfg = dataclasses.replace(CONFIGS["27b"], gdn_n_heads=nv, gdn_num_k_heads=nk,
+                                  quant=(("bulk", "Q4_K"), ("ssm_out", ssm_out)))
+        seen = []
         for p in range(P):
-            vh = list(range(p, nv, P))
-            kh = list(range(p, nk, P))
-            for i, h in enumerate(vh):
-                assert kh[i % (nk // P)] == h % nk
+            vh, kh = tp.gdn_heads(cfg, P, p)
+            assert len(vh) == nv // P and len(kh) == nk // P
+            for l, h in enumerate(vh):
+                assert kh[l % (nk // P)] == h % nk
+            if GEOM[TT[ssm_out]][0] == 256:  # whole ssm_out blocks: heads in aligned pairs
+                assert all(vh[2 * i] % 2 == 0 and vh[2 * i + 1] == vh[2 * i] + 1 for i in range(len(vh) // 2))
+            seen += vh
+        assert sorted(seen) == list(range(nv))
 
 
 def test_local_config_and_rejects():
@@ -78,5 +89,17 @@ def test_local_config_and_rejects():
     loc = tp.local_config(cfg, 4)
     assert (loc.n_heads, loc.n_kv_heads, loc.gdn_n_heads, loc.gdn_num_k_heads, loc.n_ff) == (6, 1, 12, 4, 4352)
     assert loc.vocab == cfg.vocab and loc.hidden == cfg.hidden
+    # TP 8: 4 kv heads replicated on rank pairs, 68 ffn blocks as 9,9,9,9,8,8,8,8
+    locs = [tp.local_config(cfg, 8, p) for p in range(8)]
+    assert [c.n_ff for c in locs] == [2304] * 4 + [2048] * 4
+    assert all((c.n_heads, c.n_kv_heads, c.gdn_n_heads, c.gdn_num_k_heads) == (3, 1, 6, 2) for c in locs)
+    assert [tp.kv_heads(cfg, 8, p) for p in range(8)] == [[0], [0], [1], [1], [2], [2], [3], [3]]
+    # every rank's q heads read only the kv head it holds (GQA group = H / KV)
+    for p in range(8):
+        grp = cfg.n_heads // cfg.n_kv_heads
+        assert {h // grp for h in range(p * 3, p * 3 + 3)} == set(tp.kv_heads(cfg, 8, p))
+    assert sum(tp.ffn_range(cfg, 8, p)[1] - tp.ffn_range(cfg, 8, p)[0] for p in range(8)) == cfg.n_ff
     with pytest.raises(ValueError):
-        tp.local_config(cfg, 8)  # 4 kv heads do not split 8 ways
+        tp.local_config(cfg, 16)  # 24 q heads do not split 16 ways
+    with pytest.raises(ValueError):
+        tp.local_config(CONFIGS["tiny-tp-mixed"], 3)
