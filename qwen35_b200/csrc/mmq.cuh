@@ -4,39 +4,25 @@
 //   y[t][r] = sum over blocks b, in block order, of  (dw[r][b] * dx[t][b]) * isum[r][t][b]
 //
 // isum is the exact int32 dot of the 32 int8 weights and activations of
-// block b: one `tcgen05.mma.kind::i8` (M = 128 rows, N = 64 tokens, K = 32)
-// per block computes it for a 128 x 64 tile, each block into its own TMEM
+// block b: one `tcgen05.mma.kind::i8` (M = 128 rows, N = TN tokens, K = 32)
+// per block computes it for a 128 x TN tile, each block into its own TMEM
 // accumulator region.  The f32 fold then runs on the CUDA cores in the
 // reference scalar tier's order (kernels32.c:462), so the result is bit-exact
 // with the CPU and with the decode GEMV -- the tensor core does the integer
-// part only, where reordering is exact.
-//
-// CTA = 6 warps, tile = 128 weight rows x 64 tokens, K in 256-column chunks:
-//   warp 0 (one lane): TMA producer -- per chunk one 2D box of the raw GGUF
-//     weight rows (128 x 272 B Q8_0 / 144 B IQ4_NL) and one of the raw Q8_0
-//     activation rows (64 x 272 B) into a 2-stage ring;
-//   warp 1: allocates / frees 256 TMEM columns, one lane issues the MMAs;
-//   warps 2-5 (thread = weight row = TMEM lane): convert the raw chunk into
-//     the canonical K-major operand layout (no swizzle: 8-row x 16-byte core
-//     matrices, K-adjacent cores 128 B apart, 8-row groups 256 B apart) with
-//     the per-block scales split off, then read the accumulators back
-//     (tcgen05.ld 32x32b) and fold.
-// Per chunk: convert 8 blocks -> MMA blocks 0-3 -> fold -> MMA blocks 4-7 ->
-// fold.  Named barrier 1 (warps 1-5) hands the operands / TMEM back and forth;
-// mbarriers (bounded waits) carry TMA and MMA completion.
+// part only, where reordering is exact.  The fold is the arithmetic bound of
+// this kernel (three rounded f32 operations per weight block and token), so
+// it runs on packed f32x2 instructions and overlaps conversion, TMA and MMA
+// (see k_mmq below).
 #pragma once
 #include "gemv_lpr.cuh"
 
 namespace q35 {
 
 constexpr int MMQ_M = 128;          // weight rows per tile (TMEM lanes)
-constexpr int MMQ_N = 64;           // tokens per tile (MMA N)
-constexpr int MMQ_KB = 8;           // 32-element blocks per chunk (256 columns)
-constexpr int MMQ_RB = 4;           // blocks per MMA round (TMEM: 4 x 64 columns)
-constexpr int MMQ_NS = 2;           // raw-chunk ring stages
-constexpr int MMQ_THREADS = 192;
-constexpr int MMQ_TMEM_COLS = MMQ_RB * MMQ_N;  // 256
+constexpr int MMQ_N = 64;           // tokens per tile of the K-quant kernel (MMA N)
 constexpr int MMQ_MIN_TOK = 16;     // below this the decode GEMV is used
+constexpr int MMQ_KB = 8;           // 32-element blocks per chunk (256 columns)
+constexpr int MMQ_NS = 2;           // raw-chunk ring stages
 
 struct MmqSeg {
     float *out;
@@ -53,17 +39,6 @@ struct MmqArgs {
     long long total_tiles;          // row tiles over all matrices
     int ntok, nchunk;
 };
-
-// shared memory plan (bytes from the 1024-aligned base)
-constexpr int MMQ_W_STAGE = MMQ_M * 272;                    // raw weight chunk (Q8_0 size; IQ4_NL uses less)
-constexpr int MMQ_X_STAGE = MMQ_N * 272;                    // raw activation chunk
-constexpr int MMQ_OFF_A = 0;                                // A operands: KB x (128 x 32 B)
-constexpr int MMQ_OFF_B = MMQ_OFF_A + MMQ_KB * MMQ_M * 32;  // B operands: KB x (64 x 32 B)
-constexpr int MMQ_OFF_DW = MMQ_OFF_B + MMQ_KB * MMQ_N * 32; // f32 [KB][128]
-constexpr int MMQ_OFF_DX = MMQ_OFF_DW + MMQ_KB * MMQ_M * 4; // f32 [2][KB][64] (by chunk parity)
-constexpr int MMQ_OFF_RAW = MMQ_OFF_DX + 2 * MMQ_KB * MMQ_N * 4;
-constexpr int MMQ_OFF_BAR = MMQ_OFF_RAW + MMQ_NS * (MMQ_W_STAGE + MMQ_X_STAGE);
-constexpr int MMQ_SMEM = MMQ_OFF_BAR + 128 + 1024;          // + barriers, + alignment slack
 
 // ---- tcgen05 / descriptor helpers -----------------------------------------
 // shared-memory matrix descriptor, K-major, no swizzle (version 1 = sm_100)
@@ -101,6 +76,26 @@ Q35_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
+}
+// 32 lanes x 16 / 8 consecutive columns
+Q35_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+Q35_DEV void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+template <int N>
+Q35_DEV void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) tmem_ld32(taddr, r);
+    else if constexpr (N == 16) tmem_ld16(taddr, r);
+    else tmem_ld8(taddr, r);
 }
 Q35_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -187,21 +182,97 @@ Q35_DEV int mmq_find_seg(const MmqArgs &a, long long tile) {
     return s;
 }
 
+// packed f32 pairs (sub / mul .rn.f32x2, sm_100a): two IEEE
+// round-to-nearest operations per instruction, lane for lane the scalar
+// result.  A packed multiply whose result feeds a packed add can be
+// contracted into a fused multiply-add (one rounding) by the code generator,
+// so exact sums of products take their final add in scalar form.
+Q35_DEV uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+Q35_DEV void f2_unpack(uint64_t v, float &lo, float &hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+Q35_DEV uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+Q35_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// (float)d0, (float)d1 for |d| < 2^22, exactly (exact_i2f on a pair)
+Q35_DEV uint64_t f2_exact_i2f(uint32_t d0, uint32_t d1) {
+    const uint64_t m = f2_pack(__int_as_float(0x4B400000 + (int)d0), __int_as_float(0x4B400000 + (int)d1));
+    return f2_sub(m, f2_pack(12582912.0f, 12582912.0f));
+}
+
+// ---------------------------------------------------------------------------
+// k_mmq: warp-specialised pipeline, one 128-row x TN-token tile per CTA
+//   warp 0      TMA producer: raw weight + activation chunks, 2-stage ring
+//   warp 1      TMEM owner; one lane issues the MMAs of a round (RB blocks)
+//               into one of two TMEM halves and commits
+//   warps 2-5   converters: raw chunk -> K-major operands + scales, into
+//               operand buffer c % NB
+//   warps 6-13  fold: thread = weight row = TMEM lane (quarter = warp % 4),
+//               warps 6-9 the first half of the tokens, 10-13 the second;
+//               reads a round's accumulators and folds them in block order
+// so conversion of chunk c+1, the MMAs of round g+1 and the fold of round g
+// run at once.  Hand-offs are mbarriers with bounded waits:
+//   full / empty [stage]    TMA -> converters -> TMA
+//   ready [buffer]          converters -> MMA issuer and fold (operands, scales)
+//   opfree [buffer]         MMA completion (commit) -> converters (operands read)
+//   tfull / tfree [half]    commit -> fold -> MMA issuer (TMEM half)
+//   sfree [buffer]          fold -> converters (scales read)
+// ---------------------------------------------------------------------------
+constexpr int MMQ_THREADS = 448;  // 14 warps
+
+template <int TN>
+struct MmqPlan {
+    static constexpr int RB = 256 / TN < MMQ_KB ? 256 / TN : MMQ_KB;  // blocks per round
+    static constexpr int ROUNDS = MMQ_KB / RB;
+    static constexpr int HALF = RB * TN;                             // TMEM columns per half
+    static constexpr int TMEM_COLS = 2 * HALF < 32 ? 32 : 2 * HALF;
+    static constexpr int W_STAGE = MMQ_M * 272;
+    static constexpr int X_STAGE = TN * 272;
+    static constexpr int A_BUF = MMQ_KB * MMQ_M * 32;
+    static constexpr int B_BUF = MMQ_KB * TN * 32;
+    // operand / scale buffers: chunks in flight between the converters and
+    // the fold (3 where shared memory allows, so conversion runs two chunks ahead)
+    static constexpr int NB = TN <= 32 ? 3 : 2;
+    static constexpr int OFF_A = 0;                                   // [NB] A operands
+    static constexpr int OFF_B = OFF_A + NB * A_BUF;                  // [NB] B operands
+    static constexpr int OFF_DW = OFF_B + NB * B_BUF;                 // [NB][KB][128] f32
+    static constexpr int OFF_DX = OFF_DW + NB * MMQ_KB * MMQ_M * 4;   // [NB][KB][TN] f32
+    static constexpr int OFF_RAW = (OFF_DX + NB * MMQ_KB * TN * 4 + 1023) / 1024 * 1024;
+    static constexpr int OFF_BAR = OFF_RAW + MMQ_NS * (W_STAGE + X_STAGE);
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;  // barriers (2 NS + 3 NB + 4) + TMEM slot, alignment slack
+    static_assert(8 * (2 * MMQ_NS + 3 * NB + 4) + 4 <= 256, "barrier area");
+    static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
 template <int TN>
 __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ MmqArgs a) {
+    using P = MmqPlan<TN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = sm + MMQ_OFF_A, *sB = sm + MMQ_OFF_B;
-    float *sDW = reinterpret_cast<float *>(sm + MMQ_OFF_DW), *sDX = reinterpret_cast<float *>(sm + MMQ_OFF_DX);
-    uint8_t *raw = sm + MMQ_OFF_RAW;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + MMQ_OFF_BAR);  // [MMQ_NS]
-    uint64_t *empty = full + MMQ_NS;                                  // [MMQ_NS]
-    uint64_t *mma_bar = empty + MMQ_NS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 1);
-    __shared__ int s_fail;
+    uint8_t *raw = sm + P::OFF_RAW;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + P::OFF_BAR);  // [NS]
+    uint64_t *empty = full + MMQ_NS;                                 // [NS]
+    uint64_t *ready = empty + MMQ_NS;                                // [NB]
+    uint64_t *opfree = ready + P::NB;                                // [NB]
+    uint64_t *sfree = opfree + P::NB;                                // [NB]
+    uint64_t *tfull = sfree + P::NB;                                 // [2]
+    uint64_t *tfree = tfull + 2;                                     // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + 2);
+    __shared__ volatile int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int issued = 0, ncommit = 0;  // producer's TMA chunks, MMA thread's commits
+    int issued = 0, ncommit = 0;
+    uint64_t *last_commit = nullptr;
+    uint32_t last_parity = 0;
     const long long tile = blockIdx.x;
     const int t0 = blockIdx.y * TN;
     const int si = mmq_find_seg(a, tile);
@@ -214,13 +285,21 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 4);
         }
-        mbar_init(mma_bar, 1);
+        for (int p = 0; p < P::NB; p++) {
+            mbar_init(&ready[p], 4);
+            mbar_init(&opfree[p], 1);
+            mbar_init(&sfree[p], 8);
+        }
+        for (int h = 0; h < 2; h++) {
+            mbar_init(&tfull[h], 1);
+            mbar_init(&tfree[h], 8);
+        }
         s_fail = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(MMQ_TMEM_COLS)
+                     "r"(P::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -235,120 +314,191 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
         // ---------------- producer ----------------
         if (lane == 0) {
             const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes), xbytes = (uint32_t)(TN * 272);
-            for (int c = 0; c < a.nchunk; c++, issued++) {
+            for (int c = 0; c < a.nchunk; c++) {
                 const int s = c % MMQ_NS;
-                if (c >= MMQ_NS && !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 121)) {
+                if (c >= MMQ_NS && (s_fail || !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 121))) {
                     s_fail = 1;
                     break;
                 }
-                uint8_t *wst = raw + s * (MMQ_W_STAGE + MMQ_X_STAGE);
+                uint8_t *wst = raw + s * (P::W_STAGE + P::X_STAGE);
                 mbar_arrive_expect_tx(&full[s], wbytes + xbytes);
                 tma_load_2d(wst, &a.wmap[si], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
-                tma_load_2d(wst + MMQ_W_STAGE, &a.xmap, c * 34, t0, &full[s]);
+                tma_load_2d(wst + P::W_STAGE, &a.xmap, c * 34, t0, &full[s]);
+                issued++;
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        for (int c = 0; c < a.nchunk; c++) {
-            for (int round = 0; round < MMQ_KB / MMQ_RB; round++) {
-                named_bar_sync(1, 160);  // operands converted / previous round's TMEM read
+        // lane 0 waits and issues; its verdict is shuffled to the warp so
+        // the warp stays converged
+        int g = 0;
+        bool ok = true;
+        for (int c = 0; c < a.nchunk && ok; c++) {
+            const int p = c % P::NB;
+            const uint32_t use = (uint32_t)(c / P::NB);  // this buffer's use count
+            if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 126);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint8_t *sA = sm + P::OFF_A + p * P::A_BUF, *sB = sm + P::OFF_B + p * P::B_BUF;
+            for (int r = 0; r < P::ROUNDS; r++, g++) {
+                const int h = g & 1;
+                if (lane == 0 && g >= 2) ok = !s_fail && mbar_wait(&tfree[h], (uint32_t)(((g >> 1) - 1) & 1), 127);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
                 tc_fence_after();
-                if (lane == 0 && !s_fail) {
-                    for (int kb = 0; kb < MMQ_RB; kb++) {
-                        const int b = round * MMQ_RB + kb;
+                if (lane == 0) {
+                    for (int kb = 0; kb < P::RB; kb++) {
+                        const int b = r * P::RB + kb;
                         const uint64_t ad = umma_desc(sA + b * MMQ_M * 32, 128, 256);
-                        const uint64_t bd = umma_desc(sB + b * MMQ_N * 32, 128, 256);
-                        umma_i8(tmem + (uint32_t)(kb * MMQ_N), ad, bd, mmq_idesc<TN>(), 0u);
+                        const uint64_t bd = umma_desc(sB + b * TN * 32, 128, 256);
+                        umma_i8(tmem + (uint32_t)(h * P::HALF + kb * TN), ad, bd, mmq_idesc<TN>(), 0u);
                     }
-                    umma_commit(mma_bar);
+                    umma_commit(&tfull[h]);
+                    last_commit = &tfull[h];
+                    last_parity = (uint32_t)((g >> 1) & 1);
                     ncommit++;
                 }
                 __syncwarp();
             }
-        }
-    } else {
-        // ---------------- converters + fold (thread = row = TMEM lane) ----------------
-        const int q = warp & 3;                       // TMEM lane quarter this warp may access
-        const int row = q * 32 + lane;
-        const int ct = threadIdx.x - 64;              // 0..127
-        float acc[TN];
-#pragma unroll
-        for (int t = 0; t < TN; t++) acc[t] = 0.0f;
-        int mma_phase = 0;
-        for (int c = 0; c < a.nchunk; c++) {
-            const int s = c % MMQ_NS;
-            const uint8_t *wst = raw + s * (MMQ_W_STAGE + MMQ_X_STAGE);
-            if (!s_fail && !mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 122)) s_fail = 1;
-            float *dxc = sDX + (c & 1) * MMQ_KB * MMQ_N;  // chunk c's activation scales
-            if (!s_fail) {
-                // weights: each thread converts the row it folds later (its
-                // block scales are then read by the thread that wrote them)
-                auto putw = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
-                    uint8_t *dst = sA + b * MMQ_M * 32;
-                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                    sDW[b * MMQ_M + row] = f16_to_f32(d);
-                };
-                if (sg.ttype == TT_Q8_0)
-                    unpack_q8_0_chunk(wst + row * sg.chunk_bytes, putw);
-                else
-                    unpack_iq4_nl_chunk(wst + row * sg.chunk_bytes, putw);
-                // activations: threads 0..63 convert token rows; their scales
-                // are read by every thread, so they alternate between two
-                // buffers (a writer of chunk c+2 has passed chunk c+1's
-                // barrier, which every reader of chunk c reached after its fold)
-                if (ct < TN) {
-                    auto putx = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
-                        uint8_t *dst = sB + b * MMQ_N * 32;
-                        *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-                        *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                        dxc[b * MMQ_N + ct] = f16_to_f32(d);
-                    };
-                    unpack_q8_0_chunk(wst + MMQ_W_STAGE + ct * 272, putx);
-                }
+            if (!ok) break;
+            if (lane == 0) {
+                umma_commit(&opfree[p]);
+                last_commit = &opfree[p];
+                last_parity = use & 1u;
+                ncommit++;
             }
-            // the raw stage is consumed: hand it back to the producer
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!ok) s_fail = 1;
+        // the last commit covers every MMA of the tile: wait for its arrival
+        // before the barriers' memory can go away
+        if (ok && lane == 0 && ncommit > 0 && !mbar_wait(last_commit, last_parity, 130)) s_fail = 1;
+        __syncwarp();
+    } else if (warp < 6) {
+        // ---------------- converters (thread = weight row; < TN: also a token row) ----------------
+        const int ct = threadIdx.x - 64;
+        for (int c = 0; c < a.nchunk; c++) {
+            const int s = c % MMQ_NS, p = c % P::NB;
+            const uint32_t use = (uint32_t)(c / P::NB);
+            // every lane waits (acquire); the warp votes so it breaks as one
+            bool ok = !s_fail && mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 122);
+            if (ok && use > 0)
+                ok = mbar_wait(&opfree[p], (use - 1) & 1u, 128) && mbar_wait(&sfree[p], (use - 1) & 1u, 129);
+            if (!__all_sync(0xffffffffu, ok)) {
+                s_fail = 1;
+                break;
+            }
+            const uint8_t *wst = raw + s * (P::W_STAGE + P::X_STAGE);
+            uint8_t *sA = sm + P::OFF_A + p * P::A_BUF, *sB = sm + P::OFF_B + p * P::B_BUF;
+            float *sDW = reinterpret_cast<float *>(sm + P::OFF_DW) + p * MMQ_KB * MMQ_M;
+            float *sDX = reinterpret_cast<float *>(sm + P::OFF_DX) + p * MMQ_KB * TN;
+            auto putw = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
+                uint8_t *dst = sA + b * MMQ_M * 32;
+                *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                sDW[b * MMQ_M + ct] = f16_to_f32(d);
+            };
+            if (sg.ttype == TT_Q8_0)
+                unpack_q8_0_chunk(wst + ct * sg.chunk_bytes, putw);
+            else
+                unpack_iq4_nl_chunk(wst + ct * sg.chunk_bytes, putw);
+            if (ct < TN) {
+                auto putx = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
+                    uint8_t *dst = sB + b * TN * 32;
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+                    sDX[b * TN + ct] = f16_to_f32(d);
+                };
+                unpack_q8_0_chunk(wst + P::W_STAGE + ct * 272, putx);
+            }
             // operands visible to the tensor core's (async) proxy
             fence_proxy_async_smem();
-            for (int round = 0; round < MMQ_KB / MMQ_RB; round++) {
-                tc_fence_before();
-                named_bar_sync(1, 160);
-                if (!s_fail && !mbar_wait(mma_bar, (uint32_t)(mma_phase & 1), 123)) s_fail = 1;
-                mma_phase++;
-                tc_fence_after();
-                if (!s_fail) {
-                    for (int kb = 0; kb < MMQ_RB; kb++) {
-                        const int b = round * MMQ_RB + kb;
-                        const float dw = sDW[b * MMQ_M + row];
-                        const float *dx = dxc + b * MMQ_N;
-#pragma unroll
-                        for (int half = 0; half < TN / 32; half++) {
-                            uint32_t d[32];
-                            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(kb * MMQ_N + half * 32), d);
-                            tmem_ld_wait();
-#pragma unroll
-                            for (int i = 0; i < 32; i++) {
-                                const int t = half * 32 + i;
-                                // sumf += dw * dx * (float)sumi
-                                acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, dx[t]), exact_i2f((int)d[i])));
-                            }
-                        }
-                    }
-                }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[s]);
+                mbar_arrive(&ready[p]);
             }
         }
-        tc_fence_before();
-        // outputs: row `row` of this tile, tokens t0 .. t0 + 63
-        const long long r = r0 + row;
-        if (!s_fail && r < sg.rows) {
-            const int nt = min(TN, a.ntok - t0);
+    } else {
+        // ---------------- fold (thread = row = TMEM lane, half the tokens) ----------------
+        constexpr int TH = TN / 2;            // tokens per fold warp
+        const int q = warp & 3;               // TMEM lane quarter this warp may access
+        const int fh = (warp - 6) >> 2;       // its token half
+        const int row = q * 32 + lane;
+        uint64_t acc[TH / 2];
 #pragma unroll
-            for (int t = 0; t < TN; t++) {
-                if (t < nt) {
-                    float *o = sg.out + (long long)(t0 + t) * sg.out_ld + r;
-                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
+        for (int t = 0; t < TH / 2; t++) acc[t] = 0ull;
+        const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+        int g = 0;
+        for (int c = 0; c < a.nchunk; c++) {
+            const int p = c % P::NB;
+            if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(c / P::NB) & 1u, 123))) {
+                s_fail = 1;
+                break;
+            }
+            const float *sDW = reinterpret_cast<const float *>(sm + P::OFF_DW) + p * MMQ_KB * MMQ_M;
+            const float *sDX = reinterpret_cast<const float *>(sm + P::OFF_DX) + p * MMQ_KB * TN + fh * TH;
+            for (int r = 0; r < P::ROUNDS; r++, g++) {
+                const int h = g & 1;
+                if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&tfull[h], (uint32_t)((g >> 1) & 1), 124))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                // one block's TH columns per load, the next block's load in
+                // flight while the current one is folded
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * P::HALF + fh * TH);
+                uint32_t dA[TH], dB[TH];
+                tmem_ldn<TH>(tbase, dA);
+                tmem_ld_wait();
+#pragma unroll
+                for (int kb = 0; kb < P::RB; kb++) {
+                    uint32_t(&d)[TH] = (kb & 1) ? dB : dA;
+                    if (kb + 1 < P::RB) tmem_ldn<TH>(tbase + (uint32_t)((kb + 1) * TN), (kb & 1) ? dA : dB);
+                    const int b = r * P::RB + kb;
+                    const float dw = sDW[b * MMQ_M + row];
+                    const uint64_t dw2 = f2_pack(dw, dw);
+                    const uint64_t *dx2 = reinterpret_cast<const uint64_t *>(sDX + b * TN);
+#pragma unroll
+                    for (int i = 0; i < TH; i += 2) {
+                        // sumf += dw * dx * (float)sumi for a pair of tokens: the
+                        // products on packed f32x2, the sum in scalar adds (a
+                        // packed multiply feeding a packed add may be contracted
+                        // into one fused multiply-add, which rounds once)
+                        const uint64_t f = f2_sub(f2_pack(__int_as_float(0x4B400000 + (int)d[i]),
+                                                          __int_as_float(0x4B400000 + (int)d[i + 1])),
+                                                  magic);
+                        float a0, a1, p0, p1;
+                        f2_unpack(acc[i / 2], a0, a1);
+                        f2_unpack(f2_mul(f2_mul(dw2, dx2[i / 2]), f), p0, p1);
+                        acc[i / 2] = f2_pack(__fadd_rn(a0, p0), __fadd_rn(a1, p1));
+                    }
+                    tmem_ld_wait();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tfree[h]);
+            }
+            if (__any_sync(0xffffffffu, s_fail != 0)) break;
+            if (lane == 0) mbar_arrive(&sfree[p]);
+        }
+        // outputs: row `row` of this tile, tokens t0 + fh*TH .. + TH - 1
+        const long long rr = r0 + row;
+        if (!s_fail && rr < sg.rows) {
+            const int nt = min(TN, a.ntok - t0) - fh * TH;
+#pragma unroll
+            for (int i = 0; i < TH; i += 2) {
+                float v0, v1;
+                f2_unpack(acc[i / 2], v0, v1);
+                const long long tk = t0 + fh * TH + i;
+                if (i < nt) {
+                    float *o = sg.out + tk * sg.out_ld + rr;
+                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, v0) : v0;
+                }
+                if (i + 1 < nt) {
+                    float *o = sg.out + (tk + 1) * sg.out_ld + rr;
+                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, v1) : v1;
                 }
             }
         }
@@ -359,14 +509,14 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
         // before its shared memory and TMEM are released
         if (warp == 0 && lane == 0)
             for (int c = issued > MMQ_NS ? issued - MMQ_NS : 0; c < issued; c++)
-                if (!mbar_wait(&full[c % MMQ_NS], (uint32_t)((c / MMQ_NS) & 1), 124)) break;
-        if (warp == 1 && lane == 0 && ncommit > 0) mbar_wait(mma_bar, (uint32_t)((ncommit - 1) & 1), 125);
+                if (!mbar_wait(&full[c % MMQ_NS], (uint32_t)((c / MMQ_NS) & 1), 125)) break;
+        if (warp == 1 && lane == 0 && ncommit > 0) mbar_wait(last_commit, last_parity, 125);
         if (threadIdx.x == 0) set_error(120);
     }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(MMQ_TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TMEM_COLS)
                      : "memory");
     }
 }
@@ -381,6 +531,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
 // block (256 columns); the Q8_K activation rows (292 B, only 4-byte aligned)
 // are read by the converter threads directly.
 // ---------------------------------------------------------------------------
+constexpr int MMQK_THREADS = 192;
 constexpr int MMQK_TMEM_COLS = 8 * MMQ_N;                    // 512
 constexpr int MMQK_W_STAGE = MMQ_M * 176;                    // raw weight block rows (Q5_K size)
 constexpr int MMQK_OFF_A = 0;                                // 8 sub-blocks x (128 x 32 B)
@@ -405,7 +556,7 @@ struct MmqkArgs {
 };
 
 template <int TN>
-__global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
+__global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = sm + MMQK_OFF_A, *sB = sm + MMQK_OFF_B;
@@ -657,8 +808,9 @@ inline int mmq_prepare() {
     static int done = 0;
     if (done) return 0;
     const cudaError_t es[] = {
-        cudaFuncSetAttribute(k_mmq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM),
-        cudaFuncSetAttribute(k_mmq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQ_SMEM),
+        cudaFuncSetAttribute(k_mmq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<64>::SMEM),
+        cudaFuncSetAttribute(k_mmq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<32>::SMEM),
+        cudaFuncSetAttribute(k_mmq<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<16>::SMEM),
         cudaFuncSetAttribute(k_mmq_kq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM),
         cudaFuncSetAttribute(k_mmq_kq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM)};
     for (cudaError_t e : es)
@@ -667,11 +819,21 @@ inline int mmq_prepare() {
     return 0;
 }
 
-// token tile: 64, or 32 when 64-token tiles would leave SMs idle (short
-// matrices: fewer row tiles than SMs)
+// token tile of the K-quant kernel: 64, or 32 when 64-token tiles would
+// leave SMs idle (short matrices: fewer row tiles than SMs)
 inline int mmq_token_tile(long long row_tiles, int ntok) {
     const long long ctas64 = row_tiles * ((ntok + 63) / 64);
     return ctas64 < gemv_sm_count() && ntok > 16 ? 32 : 64;
+}
+
+// token tile of k_mmq: the widest of 64 / 32 / 16 that still gives every SM
+// a tile (the fold work per tile scales with the tile's tokens, so narrower
+// tiles spread a short matrix over more SMs); 16 when none does
+inline int mmq_q32_token_tile(long long row_tiles, int ntok) {
+    const long long sms = gemv_sm_count();
+    for (int tn : {64, 32})
+        if (row_tiles * ((ntok + tn - 1) / tn) >= sms) return tn;
+    return 16;
 }
 
 // K-quant (Q4_K / Q5_K) weights x Q8_K activations; -1 when not eligible
@@ -709,9 +871,9 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
     a.nblk = cols / 256;
     Q35_TRY_RC(mmq_prepare());
     if (mmq_token_tile(tiles, ntok) == 32)
-        return launch_k(k_mmq_kq<32>, dim3((unsigned)tiles, (unsigned)((ntok + 31) / 32)), dim3(MMQ_THREADS),
+        return launch_k(k_mmq_kq<32>, dim3((unsigned)tiles, (unsigned)((ntok + 31) / 32)), dim3(MMQK_THREADS),
                         (size_t)MMQK_SMEM, st, a);
-    return launch_k(k_mmq_kq<64>, dim3((unsigned)tiles, (unsigned)((ntok + 63) / 64)), dim3(MMQ_THREADS),
+    return launch_k(k_mmq_kq<64>, dim3((unsigned)tiles, (unsigned)((ntok + 63) / 64)), dim3(MMQK_THREADS),
                     (size_t)MMQK_SMEM, st, a);
 }
 
@@ -747,7 +909,7 @@ inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int col
         if (!mmq_encode(&a.wmap[i], segs[i].w, s.rows, rb, rb, s.chunk_bytes, MMQ_M)) return -1;
     }
     if (tiles == 0) return 0;
-    const int tn = mmq_token_tile(tiles, ntok);
+    const int tn = mmq_q32_token_tile(tiles, ntok);
     if (!mmq_encode(&a.xmap, xq, ntok, ld, (int)act_row, 272, tn)) return -1;
     a.nseg = nseg;
     a.total_tiles = tiles;
@@ -755,8 +917,9 @@ inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int col
     a.nchunk = cols / 256;
     Q35_TRY_RC(mmq_prepare());
     const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn));
-    if (tn == 32) return launch_k(k_mmq<32>, grid, dim3(MMQ_THREADS), (size_t)MMQ_SMEM, st, a);
-    return launch_k(k_mmq<64>, grid, dim3(MMQ_THREADS), (size_t)MMQ_SMEM, st, a);
+    if (tn == 16) return launch_k(k_mmq<16>, grid, dim3(MMQ_THREADS), (size_t)MmqPlan<16>::SMEM, st, a);
+    if (tn == 32) return launch_k(k_mmq<32>, grid, dim3(MMQ_THREADS), (size_t)MmqPlan<32>::SMEM, st, a);
+    return launch_k(k_mmq<64>, grid, dim3(MMQ_THREADS), (size_t)MmqPlan<64>::SMEM, st, a);
 }
 
 }  // namespace q35

@@ -158,9 +158,10 @@ def test_mmq_tensor_core_bit_exact(L, O, name, tokens):
     int8 (sub-)block dots on the tensor core, scales, mins and the f32 fold in
     block order on the CUDA cores -- bit-exact with the reference scalar tier
     like the decode GEMV"""
-    # 32-token tiles when row tiles are fewer than SMs, 64-token tiles for
-    # the 19000-row matrix (and at 16 tokens)
-    for rows, cols in [(300, 1024), (129, 2048), (1000, 768), (128, 256), (19000, 256)]:
+    # token tiles of 64 / 32 / 16 by how many row tiles there are (Q8_0 /
+    # IQ4_NL: 16 for the short matrices, 32 for 100 row tiles at 37 / 64
+    # tokens, 64 for 149 row tiles; K-quants: 32 or 64)
+    for rows, cols in [(300, 1024), (129, 2048), (1000, 768), (128, 256), (12800, 256), (19000, 256)]:
         got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + 7 * tokens)
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
     assert_no_kernel_error(L)
