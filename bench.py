@@ -276,9 +276,11 @@ def time_tp_decode(cfg_name, batch, ctx, steps, warmup, seed, dist, world, rank)
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("q35_timed")
     e0.record(st)
     run(steps)
     e1.record(st)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), dist)
     eng.close()  # its graphs hold NCCL work: released before the process group

@@ -219,16 +219,16 @@ namespace q35 {
 // the chunk's K rows are copied to shared memory with cp.async (every copy
 // in flight at once), then a lane per position computes the gqa heads'
 // serial dots from there.
-// Kernel 2 (softmax + P.V): CTA (q head, sequence, 64-dim chunk); every CTA
-// of a head recomputes the (cheap) softmax, then thread j walks t in order
-// for its dim over V tiles double-buffered in shared memory by cp.async.
-// Parallelism comes from dims, not positions, so no split re-associates a
-// sum.
+// Kernel 2 (softmax): CTA (q head, sequence), probabilities in place.
+// Kernel 3 (P.V): CTA (kv head, sequence, 64-dim chunk), the group's q heads
+// together so V streams once per kv head; thread (head, dim) walks t in
+// order over a 4-deep cp.async ring of V tiles.
+// Parallelism comes from heads and dims, not positions, so no split
+// re-associates a sum.
 // ---------------------------------------------------------------------------
 constexpr int ATTX_CHUNK = 32;             // positions per score CTA
 constexpr int ATTX_KLD = ATT_HD + 4;       // shared K row stride (floats): 1040 B, an odd multiple of 16
 constexpr int ATTX_DIMS = 64;
-constexpr int ATTX_VT = 128;               // positions per V tile
 
 
 struct AttnXArgs {
@@ -300,68 +300,105 @@ __global__ void __launch_bounds__(ATTX_CHUNK) k_attx_scores(const __grid_constan
         a.scores[((long long)seq * a.heads + kvh * G + g) * a.max_len + p0 + lane] = __fmul_rn(s[g], a.scale);
 }
 
-// dynamic shared memory: 2 V tiles [ATTX_VT][ATTX_DIMS] then the len probabilities
-__global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ AttnXArgs a) {
+// Softmax of one (sequence, head) row of scores, in place: the max (any
+// order gives the same value), exp(s - max), the sum in position order (one
+// thread, from shared memory), then p = e / sum -- the CPU's operations
+// (src/elementwise.zig:349-372).  Dynamic shared memory: len floats.
+constexpr int ATTX_SMT = 256;
+__global__ void __launch_bounds__(ATTX_SMT) k_attx_softmax(const __grid_constant__ AttnXArgs a) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ __align__(16) float s_dyn[];
-    float *s_v = s_dyn;                                  // [2][ATTX_VT][ATTX_DIMS]
-    float *s_p = s_dyn + 2 * ATTX_VT * ATTX_DIMS;        // [len]
-    __shared__ float s_red[2];
-    const int h = blockIdx.x, seq = blockIdx.y, dc = blockIdx.z, j = threadIdx.x;
+    extern __shared__ __align__(16) float s_e[];
+    __shared__ float s_red[ATTX_SMT / 32], s_sum;
+    const int h = blockIdx.x, seq = blockIdx.y, j = threadIdx.x;
     const int len = attx_len(a, seq);
-    const int gqa = a.heads / a.kv_heads, kvh = h / gqa;
-    const long long slot = a.slots ? a.slots[seq] : seq;
-    const float *vb = a.vc + slot * a.kv_slot + kvh * ATT_HD + dc * ATTX_DIMS;
-    const int ntile = (len + ATTX_VT - 1) / ATTX_VT;
-    // V tile k -> buffer k & 1: rows of 64 floats (16 x 16 B pieces)
-    auto load_tile = [&](int k) {
-        const int t0 = k * ATTX_VT, nt = min(ATTX_VT, len - t0);
-        float *dst = s_v + (size_t)(k & 1) * ATTX_VT * ATTX_DIMS;
-        for (int idx = j; idx < nt * (ATTX_DIMS / 4); idx += ATTX_DIMS) {
-            const int r = idx / (ATTX_DIMS / 4), c = idx - r * (ATTX_DIMS / 4);
-            cp_async16(dst + r * ATTX_DIMS + c * 4, vb + (long long)(t0 + r) * a.kv_dim + c * 4);
-        }
-        cp_async_commit();
-    };
-    if (ntile > 0) load_tile(0);  // in flight during the softmax
-
-    const float *sc = a.scores + ((long long)seq * a.heads + h) * a.max_len;
+    float *sc = a.scores + ((long long)seq * a.heads + h) * a.max_len;
     float m = -3.40282347e38f;
-    for (int t = j; t < len; t += ATTX_DIMS) {
+    for (int t = j; t < len; t += ATTX_SMT) {
         const float v = sc[t];
-        s_p[t] = v;
+        s_e[t] = v;
         m = fmaxf(m, v);
     }
     m = warp_max(m);
     if ((j & 31) == 0) s_red[j >> 5] = m;
     __syncthreads();
-    m = fmaxf(s_red[0], s_red[1]);
-    for (int t = j; t < len; t += ATTX_DIMS) s_p[t] = exp_f(__fsub_rn(s_p[t], m));
+    m = s_red[0];
+#pragma unroll
+    for (int w = 1; w < ATTX_SMT / 32; w++) m = fmaxf(m, s_red[w]);
+    for (int t = j; t < len; t += ATTX_SMT) s_e[t] = exp_f(__fsub_rn(s_e[t], m));
     __syncthreads();
     if (j == 0) {
+        // serial sum; the loads of the next 32 run ahead of the add chain
         float sum = 0.0f;
-        for (int t = 0; t < len; t++) sum = __fadd_rn(sum, s_p[t]);
-        s_red[0] = sum;
+        int t = 0;
+        for (; t + 32 <= len; t += 32) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = s_e[t + i];
+#pragma unroll
+            for (int i = 0; i < 32; i++) sum = __fadd_rn(sum, v[i]);
+        }
+        for (; t < len; t++) sum = __fadd_rn(sum, s_e[t]);
+        s_sum = sum;
     }
     __syncthreads();
-    const float sum = s_red[0];
-    for (int t = j; t < len; t += ATTX_DIMS) s_p[t] = __fdiv_rn(s_p[t], sum);
+    const float sum = s_sum;
+    for (int t = j; t < len; t += ATTX_SMT) sc[t] = __fdiv_rn(s_e[t], sum);
+}
 
+// P.V: CTA per (kv head, sequence, 64-dim chunk) with G x 64 threads, thread
+// = (q head g of the group, dim j); the V tiles (64 positions x 64 dims) and
+// the G probability rows stream through a 4-deep cp.async ring shared by the
+// group's q heads, so V is read once per kv head.  acc += p[t] * v[t] in
+// position order, then the gate (sigmoid) and, for a Q8_0 consumer, the
+// quantized output block.
+constexpr int ATTX_PT = 64;   // positions per tile
+constexpr int ATTX_NST = 4;   // tiles in flight
+inline size_t attx_pv_smem(int G) { return (size_t)ATTX_NST * ATTX_PT * (ATTX_DIMS + G) * 4; }
+
+__global__ void __launch_bounds__(8 * ATTX_DIMS) k_attx_pv(const __grid_constant__ AttnXArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float s_dyn[];
+    const int G = a.heads / a.kv_heads;
+    float *s_v = s_dyn;                                    // [NST][PT][DIMS]
+    float *s_p = s_dyn + ATTX_NST * ATTX_PT * ATTX_DIMS;   // [NST][G][PT]
+    const int kvh = blockIdx.x, seq = blockIdx.y, dc = blockIdx.z;
+    const int tid = threadIdx.x, nthr = G * ATTX_DIMS, g = tid / ATTX_DIMS, j = tid - g * ATTX_DIMS;
+    const int h = kvh * G + g;
+    const int len = attx_len(a, seq);
+    const long long slot = a.slots ? a.slots[seq] : seq;
+    const float *vb = a.vc + slot * a.kv_slot + kvh * ATT_HD + dc * ATTX_DIMS;
+    const float *pb = a.scores + ((long long)seq * a.heads + (long long)kvh * G) * a.max_len;
+    const int ntile = (len + ATTX_PT - 1) / ATTX_PT;
+    auto load_tile = [&](int k) {
+        if (k < ntile) {
+            const int t0 = k * ATTX_PT, nt = min(ATTX_PT, len - t0);
+            float *dv = s_v + (k % ATTX_NST) * ATTX_PT * ATTX_DIMS;
+            float *dp = s_p + (k % ATTX_NST) * G * ATTX_PT;
+            for (int idx = tid; idx < nt * (ATTX_DIMS / 4); idx += nthr) {
+                const int r = idx / (ATTX_DIMS / 4), c = idx - r * (ATTX_DIMS / 4);
+                cp_async16(dv + r * ATTX_DIMS + c * 4, vb + (long long)(t0 + r) * a.kv_dim + c * 4);
+            }
+            for (int idx = tid; idx < G * nt; idx += nthr) {
+                const int gg = idx / nt, r = idx - gg * nt;
+                cp_async4(dp + gg * ATTX_PT + r, pb + (long long)gg * a.max_len + t0 + r);
+            }
+        }
+        cp_async_commit();  // one group per tile index, empty past the end
+    };
+#pragma unroll
+    for (int k = 0; k < ATTX_NST - 1; k++) load_tile(k);
     float acc = 0.0f;
     for (int k = 0; k < ntile; k++) {
-        if (k + 1 < ntile) {
-            load_tile(k + 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();  // tile k (and, first time round, every s_p) visible to all
-        const float *v = s_v + (size_t)(k & 1) * ATTX_VT * ATTX_DIMS + j;
-        const int t0 = k * ATTX_VT, nt = min(ATTX_VT, len - t0);
+        cp_async_wait<ATTX_NST - 2>();  // this thread's copies of tile k landed
+        __syncthreads();                // everyone's; and tile k-1's buffer is no longer read
+        load_tile(k + ATTX_NST - 1);
+        const float *v = s_v + (k % ATTX_NST) * ATTX_PT * ATTX_DIMS + j;
+        const float *p = s_p + (k % ATTX_NST) * G * ATTX_PT + g * ATTX_PT;
+        const int nt = min(ATTX_PT, len - k * ATTX_PT);
 #pragma unroll 8
-        for (int r = 0; r < nt; r++) acc = __fadd_rn(acc, __fmul_rn(s_p[t0 + r], v[r * ATTX_DIMS]));
-        __syncthreads();  // done with buffer k & 1 before tile k + 2 lands in it
+        for (int r = 0; r < nt; r++) acc = __fadd_rn(acc, __fmul_rn(p[r], v[r * ATTX_DIMS]));
     }
     const int dim = dc * ATTX_DIMS + j;
     const float gt = a.gate[(long long)seq * a.q_tok + (long long)h * ATT_HD + dim];
@@ -373,16 +410,17 @@ __global__ void __launch_bounds__(ATTX_DIMS) k_attx_pv(const __grid_constant__ A
     }
 }
 
-inline size_t attx_pv_smem(int max_len) { return (size_t)(2 * ATTX_VT * ATTX_DIMS + max_len) * 4; }
-
-// raise k_attx_pv's dynamic shared-memory ceiling to cover contexts up to
-// max_len (a high-water mark; the engine calls this before any capture)
+// dynamic shared-memory ceilings: the softmax stages max_len floats, the
+// P.V ring needs attx_pv_smem(8) (a high-water mark; the engine calls this
+// before any capture)
 inline int attx_prepare(int max_len) {
-    static size_t configured = 48 * 1024;
-    const size_t smem = attx_pv_smem(max_len);
+    static size_t configured = 0;
+    const size_t smem = std::max((size_t)max_len * 4, attx_pv_smem(8));
     if (smem <= configured) return 0;
-    if (smem > 227 * 1024 - 256) return (int)cudaErrorInvalidValue;
-    const int rc = (int)cudaFuncSetAttribute(k_attx_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if ((size_t)max_len * 4 > 227 * 1024 - 1024) return (int)cudaErrorInvalidValue;
+    int rc = (int)cudaFuncSetAttribute(k_attx_softmax, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)std::max((size_t)max_len * 4, (size_t)48 * 1024));
+    if (!rc) rc = (int)cudaFuncSetAttribute(k_attx_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attx_pv_smem(8));
     if (rc) return rc;
     configured = smem;
     return 0;
@@ -405,11 +443,11 @@ inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t s
     default: return (int)cudaErrorInvalidValue;
     }
     if (rc) return rc;
-    const size_t smem = attx_pv_smem(max_len);
-    if (smem > 227 * 1024 - 256) return (int)cudaErrorInvalidValue;
     Q35_TRY_RC(attx_prepare(max_len));
-    return launch_k(k_attx_pv, dim3((unsigned)a.heads, (unsigned)nseq, ATT_HD / ATTX_DIMS), dim3(ATTX_DIMS), smem, st,
-                    a);
+    rc = launch_k(k_attx_softmax, dim3((unsigned)a.heads, (unsigned)nseq), dim3(ATTX_SMT), (size_t)max_len * 4, st, a);
+    if (rc) return rc;
+    return launch_k(k_attx_pv, dim3((unsigned)a.kv_heads, (unsigned)nseq, ATT_HD / ATTX_DIMS), dim3(G * ATTX_DIMS),
+                    attx_pv_smem(G), st, a);
 }
 
 }  // namespace q35

@@ -10,6 +10,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <utility>
 
 #define Q35_DEV __device__ __forceinline__

@@ -19,7 +19,6 @@
 namespace q35 {
 
 constexpr int MMQ_M = 128;          // weight rows per tile (TMEM lanes)
-constexpr int MMQ_N = 64;           // tokens per tile of the K-quant kernel (MMA N)
 constexpr int MMQ_MIN_TOK = 16;     // below this the decode GEMV is used
 constexpr int MMQ_KB = 8;           // 32-element blocks per chunk (256 columns)
 constexpr int MMQ_NS = 2;           // raw-chunk ring stages
@@ -47,7 +46,7 @@ Q35_DEV uint64_t umma_desc(const void *smem_ptr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
-// instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = MMQ_N
+// instruction descriptor: s8 x s8 -> s32, K-major A and B, M = 128, N = TN
 template <int TN>
 __host__ __device__ constexpr uint32_t mmq_idesc() {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(MMQ_M >> 4) << 24);
@@ -526,25 +525,14 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
 // 8 sub-blocks with 6-bit scales sc_j and mins m_j (kernels256.c:474-498,
 // 605-629):  isum = sum_j sc_j * dot_j,  summs = sum_j m_j * bsum_j,
 // sumf += (dy*d)*isum - (dy*dmin)*summs.  One MMA per sub-block (K = 32) into
-// its own 64-column TMEM region (8 regions = 512 columns); the epilogue forms
-// isum / summs in exact integer arithmetic, then the f32 fold.  Chunk = one
-// block (256 columns); the Q8_K activation rows (292 B, only 4-byte aligned)
-// are read by the converter threads directly.
+// its own TN-column TMEM region; the fold forms isum / summs in exact integer
+// arithmetic (any order), then the f32 step in the reference's order.
+// Chunk = one 256-element block.  Same warp roles and hand-offs as k_mmq;
+// the converters also copy the Q8_K activation rows (292 B, 4-byte aligned)
+// straight from global memory, their loads issued before the weight wait.
+// A round is 4 sub-blocks at TN = 64 (two rounds per block, TMEM halves of
+// 256 columns), all 8 otherwise.
 // ---------------------------------------------------------------------------
-constexpr int MMQK_THREADS = 192;
-constexpr int MMQK_TMEM_COLS = 8 * MMQ_N;                    // 512
-constexpr int MMQK_W_STAGE = MMQ_M * 176;                    // raw weight block rows (Q5_K size)
-constexpr int MMQK_OFF_A = 0;                                // 8 sub-blocks x (128 x 32 B)
-constexpr int MMQK_OFF_B = MMQK_OFF_A + 8 * MMQ_M * 32;      // 8 sub-blocks x (64 x 32 B)
-constexpr int MMQK_OFF_SC = MMQK_OFF_B + 8 * MMQ_N * 32;     // int [8][128] scales
-constexpr int MMQK_OFF_MN = MMQK_OFF_SC + 8 * MMQ_M * 4;     // int [8][128] mins
-constexpr int MMQK_OFF_D = MMQK_OFF_MN + 8 * MMQ_M * 4;      // f32 [128] d, [128] dmin
-constexpr int MMQK_OFF_DY = MMQK_OFF_D + 2 * MMQ_M * 4;      // f32 [2][64] activation scales (by block parity)
-constexpr int MMQK_OFF_BS = MMQK_OFF_DY + 2 * MMQ_N * 4;     // int [2][8][64] sub-block sums
-constexpr int MMQK_OFF_RAW = MMQK_OFF_BS + 2 * 8 * MMQ_N * 4;
-constexpr int MMQK_OFF_BAR = MMQK_OFF_RAW + MMQ_NS * MMQK_W_STAGE;
-constexpr int MMQK_SMEM = MMQK_OFF_BAR + 128 + 1024;
-
 struct MmqkArgs {
     CUtensorMap wmap[GV_MAX_SEG];   // weights: [rows][row_bytes/8] u64, box 128 rows x one block
     MmqSeg seg[GV_MAX_SEG];
@@ -556,22 +544,47 @@ struct MmqkArgs {
 };
 
 template <int TN>
-__global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
+struct MmqkPlan {
+    static constexpr int RB = TN == 64 ? 4 : 8;     // sub-blocks per round
+    static constexpr int ROUNDS = 8 / RB;
+    static constexpr int HALF = RB * TN;             // TMEM columns per half
+    static constexpr int TMEM_COLS = 2 * HALF;
+    static constexpr int NB = TN == 64 ? 2 : 3;      // operand / scale buffers
+    static constexpr int NS = 3;                     // raw weight stages
+    static constexpr int W_STAGE = MMQ_M * 176;      // one block of 128 rows (Q5_K size)
+    static constexpr int A_BUF = 8 * MMQ_M * 32;
+    static constexpr int B_BUF = 8 * TN * 32;
+    // per buffer: A | B | sc[128][8] u8 | mn[128][8] u8 | d[128] dmin[128] f32 | dy[TN] f32 | bs[TN][8] i32
+    static constexpr int OB_A = 0, OB_B = A_BUF, OB_SC = OB_B + B_BUF, OB_MN = OB_SC + MMQ_M * 8;
+    static constexpr int OB_D = OB_MN + MMQ_M * 8, OB_DY = OB_D + 2 * MMQ_M * 4, OB_BS = OB_DY + TN * 4;
+    static constexpr int BUF = (OB_BS + TN * 32 + 1023) / 1024 * 1024;
+    static constexpr int OFF_RAW = NB * BUF;
+    static constexpr int OFF_BAR = OFF_RAW + NS * W_STAGE;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+    static_assert(8 * (2 * NS + 3 * NB + 4) + 4 <= 256, "barrier area");
+    static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
+template <int TN>
+__global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
+    using P = MmqkPlan<TN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = sm + MMQK_OFF_A, *sB = sm + MMQK_OFF_B;
-    int *sSC = reinterpret_cast<int *>(sm + MMQK_OFF_SC), *sMN = reinterpret_cast<int *>(sm + MMQK_OFF_MN);
-    float *sD = reinterpret_cast<float *>(sm + MMQK_OFF_D), *sDY = reinterpret_cast<float *>(sm + MMQK_OFF_DY);
-    int *sBS = reinterpret_cast<int *>(sm + MMQK_OFF_BS);
-    uint8_t *raw = sm + MMQK_OFF_RAW;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + MMQK_OFF_BAR);
-    uint64_t *empty = full + MMQ_NS;
-    uint64_t *mma_bar = empty + MMQ_NS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 1);
-    __shared__ int s_fail;
+    uint8_t *raw = sm + P::OFF_RAW;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + P::OFF_BAR);  // [NS]
+    uint64_t *empty = full + P::NS;                                  // [NS]
+    uint64_t *ready = empty + P::NS;                                 // [NB]
+    uint64_t *opfree = ready + P::NB;                                // [NB]
+    uint64_t *sfree = opfree + P::NB;                                // [NB]
+    uint64_t *tfull = sfree + P::NB;                                 // [2]
+    uint64_t *tfree = tfull + 2;                                     // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + 2);
+    __shared__ volatile int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int issued = 0, ncommit = 0;
+    uint64_t *last_commit = nullptr;
+    uint32_t last_parity = 0;
     const long long tile = blockIdx.x;
     const int t0 = blockIdx.y * TN;
     int sgi = 0;
@@ -580,22 +593,28 @@ __global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constan
         if (i < a.nseg && tile >= a.seg[i].tile_begin) sgi = i;
     const MmqSeg &sg = a.seg[sgi];
     const long long r0 = (tile - sg.tile_begin) * MMQ_M;
-    const bool q5 = sg.ttype == TT_Q5_K;
-    const uint32_t idesc = mmq_idesc<TN>();
 
     pdl_trigger();
     if (threadIdx.x == 0) {
-        for (int s = 0; s < MMQ_NS; s++) {
+        for (int s = 0; s < P::NS; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 4);
         }
-        mbar_init(mma_bar, 1);
+        for (int p = 0; p < P::NB; p++) {
+            mbar_init(&ready[p], 4);
+            mbar_init(&opfree[p], 1);
+            mbar_init(&sfree[p], 8);
+        }
+        for (int h = 0; h < 2; h++) {
+            mbar_init(&tfull[h], 1);
+            mbar_init(&tfree[h], 8);
+        }
         s_fail = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(MMQK_TMEM_COLS)
+                     "r"(P::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -606,74 +625,129 @@ __global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constan
     pdl_wait();
 
     if (warp == 0) {
+        // ---------------- producer ----------------
         if (lane == 0) {
             const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes);
-            for (int c = 0; c < a.nblk; c++, issued++) {
-                const int s = c % MMQ_NS;
-                if (c >= MMQ_NS && !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 131)) {
+            for (int c = 0; c < a.nblk; c++) {
+                const int s = c % P::NS;
+                if (c >= P::NS &&
+                    (s_fail || !mbar_wait(&empty[s], (uint32_t)(((c / P::NS) - 1) & 1), 131))) {
                     s_fail = 1;
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], wbytes);
-                tma_load_2d(raw + s * MMQK_W_STAGE, &a.wmap[sgi], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
+                tma_load_2d(raw + s * P::W_STAGE, &a.wmap[sgi], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
+                issued++;
             }
         }
     } else if (warp == 1) {
-        for (int c = 0; c < a.nblk; c++) {
-            named_bar_sync(1, 160);  // operands of block c converted, TMEM of block c-1 read
+        // ---------------- MMA issuer ----------------
+        int g = 0;
+        bool ok = true;
+        const uint32_t idesc = mmq_idesc<TN>();
+        for (int c = 0; c < a.nblk && ok; c++) {
+            const int p = c % P::NB;
+            const uint32_t use = (uint32_t)(c / P::NB);
+            if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 136);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
             tc_fence_after();
-            if (lane == 0 && !s_fail) {
-                for (int j = 0; j < 8; j++) {
-                    const uint64_t ad = umma_desc(sA + j * MMQ_M * 32, 128, 256);
-                    const uint64_t bd = umma_desc(sB + j * MMQ_N * 32, 128, 256);
-                    umma_i8(tmem + (uint32_t)(j * MMQ_N), ad, bd, idesc, 0u);
+            const uint8_t *buf = sm + p * P::BUF;
+            for (int r = 0; r < P::ROUNDS; r++, g++) {
+                const int h = g & 1;
+                if (lane == 0 && g >= 2) ok = !s_fail && mbar_wait(&tfree[h], (uint32_t)(((g >> 1) - 1) & 1), 137);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    for (int kb = 0; kb < P::RB; kb++) {
+                        const int j = r * P::RB + kb;
+                        const uint64_t ad = umma_desc(buf + P::OB_A + j * MMQ_M * 32, 128, 256);
+                        const uint64_t bd = umma_desc(buf + P::OB_B + j * TN * 32, 128, 256);
+                        umma_i8(tmem + (uint32_t)(h * P::HALF + kb * TN), ad, bd, idesc, 0u);
+                    }
+                    umma_commit(&tfull[h]);
+                    last_commit = &tfull[h];
+                    last_parity = (uint32_t)((g >> 1) & 1);
+                    ncommit++;
                 }
-                umma_commit(mma_bar);
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) {
+                umma_commit(&opfree[p]);
+                last_commit = &opfree[p];
+                last_parity = use & 1u;
                 ncommit++;
             }
             __syncwarp();
         }
-    } else {
-        const int q = warp & 3;
-        const int row = q * 32 + lane;
+        if (!ok) s_fail = 1;
+        if (ok && lane == 0 && ncommit > 0 && !mbar_wait(last_commit, last_parity, 138)) s_fail = 1;
+        __syncwarp();
+    } else if (warp < 6) {
+        // ---------------- converters ----------------
+        // weights: thread ct = row ct; activations: thread ct = token ct % TN,
+        // sub-blocks [SPT*(ct/TN), SPT*(ct/TN) + SPT)
         const int ct = threadIdx.x - 64;
-        float acc[TN];
+        const bool q5 = sg.ttype == TT_Q5_K;
+        constexpr int SPT = TN / 16;
+        const int tk = ct % TN, hq = ct / TN;
+        const bool live = t0 + tk < a.ntok;
+        // activation words of block c + 1 are loaded (into registers) while
+        // block c is converted: a global round trip per block would
+        // otherwise sit on the converters' critical path
+        // sw: the f32 d bits, then the 16 int16 bsums as 8 words
+        uint32_t xw[SPT * 8], nxw[SPT * 8], xsw[9], nxsw[9];
+        auto fetch = [&](int c, uint32_t (&w)[SPT * 8], uint32_t (&sw)[9]) {
+            const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)c * 292;
+            const bool on = live && c < a.nblk;
 #pragma unroll
-        for (int t = 0; t < TN; t++) acc[t] = 0.0f;
-        for (int c = 0; c < a.nblk; c++) {
-            const int s = c % MMQ_NS;
-            // activations of block c (global -> operand layout), independent of the weight TMA
-            {
-                // thread: token tk, sub-blocks [SPT*h, SPT*h + SPT)
-                constexpr int SPT = TN / 16;
-                const int tk = ct % TN, h = ct / TN;
-                const bool live = t0 + tk < a.ntok;
-                const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)c * 292;
-                uint32_t w[SPT * 8];
+            for (int i = 0; i < SPT * 8; i++)
+                w[i] = on ? reinterpret_cast<const uint32_t *>(src + 4 + 32 * SPT * hq)[i] : 0u;
 #pragma unroll
-                for (int i = 0; i < SPT * 8; i++)
-                    w[i] = live ? reinterpret_cast<const uint32_t *>(src + 4 + 32 * SPT * h)[i] : 0u;
+            for (int i = 0; i < 9; i++) sw[i] = 0u;
+            if (hq == 0 && on) {
+                sw[0] = *reinterpret_cast<const uint32_t *>(src);
 #pragma unroll
-                for (int jj = 0; jj < SPT; jj++) {
-                    uint8_t *dst = sB + (SPT * h + jj) * MMQ_N * 32;
-                    *reinterpret_cast<uint4 *>(dst + umma_off(tk, 0)) =
-                        make_uint4(w[8 * jj], w[8 * jj + 1], w[8 * jj + 2], w[8 * jj + 3]);
-                    *reinterpret_cast<uint4 *>(dst + umma_off(tk, 1)) =
-                        make_uint4(w[8 * jj + 4], w[8 * jj + 5], w[8 * jj + 6], w[8 * jj + 7]);
-                }
-                // per-token values alternate between two buffers (see k_mmq)
-                if (h == 0) {
-                    sDY[(c & 1) * MMQ_N + tk] = live ? *reinterpret_cast<const float *>(src) : 0.0f;
-                    const int16_t *bs = reinterpret_cast<const int16_t *>(src + 260);
-#pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        sBS[((c & 1) * 8 + j) * MMQ_N + tk] = live ? (int)bs[2 * j] + (int)bs[2 * j + 1] : 0;
-                }
+                for (int i = 0; i < 8; i++) sw[1 + i] = reinterpret_cast<const uint32_t *>(src + 260)[i];
             }
-            if (!s_fail && !mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 132)) s_fail = 1;
-            if (!s_fail) {
-                // weights: each thread converts the row it folds later
-                const uint8_t *rp = raw + s * MMQK_W_STAGE + row * sg.chunk_bytes;
+        };
+        fetch(0, xw, xsw);
+        for (int c = 0; c < a.nblk; c++) {
+            const int s = c % P::NS, p = c % P::NB;
+            const uint32_t use = (uint32_t)(c / P::NB);
+            fetch(c + 1, nxw, nxsw);
+            bool ok = !s_fail && mbar_wait(&full[s], (uint32_t)((c / P::NS) & 1), 132);
+            if (ok && use > 0)
+                ok = mbar_wait(&opfree[p], (use - 1) & 1u, 139) && mbar_wait(&sfree[p], (use - 1) & 1u, 140);
+            if (!__all_sync(0xffffffffu, ok)) {
+                s_fail = 1;
+                break;
+            }
+            uint8_t *buf = sm + p * P::BUF;
+            // activations into the B operands and per-token values
+#pragma unroll
+            for (int jj = 0; jj < SPT; jj++) {
+                uint8_t *dst = buf + P::OB_B + (SPT * hq + jj) * TN * 32;
+                *reinterpret_cast<uint4 *>(dst + umma_off(tk, 0)) =
+                    make_uint4(xw[8 * jj], xw[8 * jj + 1], xw[8 * jj + 2], xw[8 * jj + 3]);
+                *reinterpret_cast<uint4 *>(dst + umma_off(tk, 1)) =
+                    make_uint4(xw[8 * jj + 4], xw[8 * jj + 5], xw[8 * jj + 6], xw[8 * jj + 7]);
+            }
+            if (hq == 0) {
+                reinterpret_cast<uint32_t *>(buf + P::OB_DY)[tk] = xsw[0];
+                int xbs[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    xbs[j] = (int)(int16_t)(xsw[1 + j] & 0xFFFFu) + (int)(int16_t)(xsw[1 + j] >> 16);
+                int4 *bsd = reinterpret_cast<int4 *>(buf + P::OB_BS + tk * 32);
+                bsd[0] = make_int4(xbs[0], xbs[1], xbs[2], xbs[3]);
+                bsd[1] = make_int4(xbs[4], xbs[5], xbs[6], xbs[7]);
+            }
+            // weights: row ct of the raw block
+            {
+                const uint8_t *rp = raw + s * P::W_STAGE + ct * sg.chunk_bytes;
                 uint32_t W[44];
                 const uint4 *v4 = reinterpret_cast<const uint4 *>(rp);
 #pragma unroll
@@ -694,14 +768,16 @@ __global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constan
                         W[4 * i + 3] = v.w;
                     }
                 }
-                sD[row] = f16_lo(W[0]);
-                sD[MMQ_M + row] = f16_hi(W[0]);
+                float *dd = reinterpret_cast<float *>(buf + P::OB_D);
+                dd[ct] = f16_lo(W[0]);
+                dd[MMQ_M + ct] = f16_hi(W[0]);
+                uint32_t scw[2] = {0u, 0u}, mnw[2] = {0u, 0u};
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     int sc, mn;
                     kq_scale_min_w(j, W + 1, sc, mn);
-                    sSC[j * MMQ_M + row] = sc;
-                    sMN[j * MMQ_M + row] = mn;
+                    scw[j >> 2] |= (uint32_t)sc << (8 * (j & 3));
+                    mnw[j >> 2] |= (uint32_t)mn << (8 * (j & 3));
                     const int cq = j >> 1;
                     uint32_t o[8];
 #pragma unroll
@@ -711,63 +787,100 @@ __global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constan
                         if (q5) v |= ((W[4 + i] >> j) & 0x01010101u) << 4;
                         o[i] = v;
                     }
-                    uint8_t *dst = sA + j * MMQ_M * 32;
-                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 0)) = make_uint4(o[0], o[1], o[2], o[3]);
-                    *reinterpret_cast<uint4 *>(dst + umma_off(row, 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                    uint8_t *dst = buf + P::OB_A + j * MMQ_M * 32;
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(o[4], o[5], o[6], o[7]);
                 }
+                *reinterpret_cast<uint2 *>(buf + P::OB_SC + ct * 8) = make_uint2(scw[0], scw[1]);
+                *reinterpret_cast<uint2 *>(buf + P::OB_MN + ct * 8) = make_uint2(mnw[0], mnw[1]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[s]);
+                mbar_arrive(&ready[p]);
+            }
+#pragma unroll
+            for (int i = 0; i < SPT * 8; i++) xw[i] = nxw[i];
+#pragma unroll
+            for (int i = 0; i < 9; i++) xsw[i] = nxsw[i];
+        }
+    } else {
+        // ---------------- fold (thread = row = TMEM lane, half the tokens) ----------------
+        constexpr int TH = TN / 2;
+        const int q = warp & 3;
+        const int fh = (warp - 6) >> 2;
+        const int row = q * 32 + lane;
+        float acc[TH];
+#pragma unroll
+        for (int t = 0; t < TH; t++) acc[t] = 0.0f;
+        int g = 0;
+        for (int c = 0; c < a.nblk; c++) {
+            const int p = c % P::NB;
+            if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(c / P::NB) & 1u, 133))) {
+                s_fail = 1;
+                break;
+            }
+            const uint8_t *buf = sm + p * P::BUF;
+            const uint2 scw = *reinterpret_cast<const uint2 *>(buf + P::OB_SC + row * 8);
+            int is[TH];
+#pragma unroll
+            for (int t = 0; t < TH; t++) is[t] = 0;
+            for (int r = 0; r < P::ROUNDS; r++, g++) {
+                const int h = g & 1;
+                if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&tfull[h], (uint32_t)((g >> 1) & 1), 134))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * P::HALF + fh * TH);
+                uint32_t dA[TH], dB[TH];
+                tmem_ldn<TH>(tbase, dA);
+                tmem_ld_wait();
+#pragma unroll
+                for (int kb = 0; kb < P::RB; kb++) {
+                    uint32_t(&d)[TH] = (kb & 1) ? dB : dA;
+                    if (kb + 1 < P::RB) tmem_ldn<TH>(tbase + (uint32_t)((kb + 1) * TN), (kb & 1) ? dA : dB);
+                    const int j = r * P::RB + kb;
+                    const int sc = (int)(((j < 4 ? scw.x : scw.y) >> (8 * (j & 3))) & 0xFFu);
+#pragma unroll
+                    for (int i = 0; i < TH; i++) is[i] += sc * (int)d[i];
+                    tmem_ld_wait();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tfree[h]);
+            }
+            if (__any_sync(0xffffffffu, s_fail != 0)) break;
+            // d = dy*d_w; dmin = dy*dmin_w; sumf += d*isum - dmin*summs
+            const uint2 mnw = *reinterpret_cast<const uint2 *>(buf + P::OB_MN + row * 8);
+            const float *dd = reinterpret_cast<const float *>(buf + P::OB_D);
+            const float dw = dd[row], dmw = dd[MMQ_M + row];
+            const float *dy = reinterpret_cast<const float *>(buf + P::OB_DY) + fh * TH;
+            const int4 *bs = reinterpret_cast<const int4 *>(buf + P::OB_BS) + fh * TH * 2;
+            int mn[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) mn[j] = (int)(((j < 4 ? mnw.x : mnw.y) >> (8 * (j & 3))) & 0xFFu);
+#pragma unroll
+            for (int i = 0; i < TH; i++) {
+                const int4 b0 = bs[2 * i], b1 = bs[2 * i + 1];
+                const int ms = mn[0] * b0.x + mn[1] * b0.y + mn[2] * b0.z + mn[3] * b0.w + mn[4] * b1.x +
+                               mn[5] * b1.y + mn[6] * b1.z + mn[7] * b1.w;
+                const float d = __fmul_rn(dy[i], dw), dm = __fmul_rn(dy[i], dmw);
+                acc[i] = __fadd_rn(acc[i], __fsub_rn(__fmul_rn(d, __int2float_rn(is[i])),
+                                                     __fmul_rn(dm, __int2float_rn(ms))));
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            fence_proxy_async_smem();
-            tc_fence_before();
-            named_bar_sync(1, 160);
-            if (!s_fail && !mbar_wait(mma_bar, (uint32_t)(c & 1), 133)) s_fail = 1;
-            tc_fence_after();
-            if (!s_fail) {
-                const float dw = sD[row], dmw = sD[MMQ_M + row];
-                int sc[8], mn[8];
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    sc[j] = sSC[j * MMQ_M + row];
-                    mn[j] = sMN[j * MMQ_M + row];
-                }
-#pragma unroll
-                for (int half = 0; half < TN / 32; half++) {
-                    int is[32];
-#pragma unroll
-                    for (int i = 0; i < 32; i++) is[i] = 0;
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        uint32_t d[32];
-                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * MMQ_N + half * 32), d);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; i++) is[i] += sc[j] * (int)d[i];
-                    }
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const int t = half * 32 + i;
-                        int ms = 0;
-#pragma unroll
-                        for (int j = 0; j < 8; j++) ms += mn[j] * sBS[((c & 1) * 8 + j) * MMQ_N + t];
-                        // d = dy*d_w; dmin = dy*dmin_w; sumf += d*isum - dmin*sumi
-                        const float dy = sDY[(c & 1) * MMQ_N + t];
-                        const float d = __fmul_rn(dy, dw), dm = __fmul_rn(dy, dmw);
-                        acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d, __int2float_rn(is[i])),
-                                                             __fmul_rn(dm, __int2float_rn(ms))));
-                    }
-                }
-            }
+            if (lane == 0) mbar_arrive(&sfree[p]);
         }
-        tc_fence_before();
-        const long long r = r0 + row;
-        if (!s_fail && r < sg.rows) {
-            const int nt = min(TN, a.ntok - t0);
+        const long long rr = r0 + row;
+        if (!s_fail && rr < sg.rows) {
+            const int nt = min(TN, a.ntok - t0) - fh * TH;
 #pragma unroll
-            for (int t = 0; t < TN; t++) {
-                if (t < nt) {
-                    float *o = sg.out + (long long)(t0 + t) * sg.out_ld + r;
-                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[t]) : acc[t];
+            for (int i = 0; i < TH; i++) {
+                if (i < nt) {
+                    float *o = sg.out + (long long)(t0 + fh * TH + i) * sg.out_ld + rr;
+                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, acc[i]) : acc[i];
                 }
             }
         }
@@ -775,15 +888,15 @@ __global__ void __launch_bounds__(MMQK_THREADS, 1) k_mmq_kq(const __grid_constan
     __syncthreads();
     if (s_fail) {
         if (warp == 0 && lane == 0)
-            for (int c = issued > MMQ_NS ? issued - MMQ_NS : 0; c < issued; c++)
-                if (!mbar_wait(&full[c % MMQ_NS], (uint32_t)((c / MMQ_NS) & 1), 134)) break;
-        if (warp == 1 && lane == 0 && ncommit > 0) mbar_wait(mma_bar, (uint32_t)((ncommit - 1) & 1), 135);
+            for (int c = issued > P::NS ? issued - P::NS : 0; c < issued; c++)
+                if (!mbar_wait(&full[c % P::NS], (uint32_t)((c / P::NS) & 1), 135)) break;
+        if (warp == 1 && lane == 0 && ncommit > 0) mbar_wait(last_commit, last_parity, 135);
         if (threadIdx.x == 0) set_error(130);
     }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(MMQK_TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TMEM_COLS)
                      : "memory");
     }
 }
@@ -811,28 +924,24 @@ inline int mmq_prepare() {
         cudaFuncSetAttribute(k_mmq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<64>::SMEM),
         cudaFuncSetAttribute(k_mmq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<32>::SMEM),
         cudaFuncSetAttribute(k_mmq<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<16>::SMEM),
-        cudaFuncSetAttribute(k_mmq_kq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM),
-        cudaFuncSetAttribute(k_mmq_kq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MMQK_SMEM)};
+        cudaFuncSetAttribute(k_mmq_kq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<64>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<32>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<16>::SMEM)};
     for (cudaError_t e : es)
         if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;
 }
 
-// token tile of the K-quant kernel: 64, or 32 when 64-token tiles would
-// leave SMs idle (short matrices: fewer row tiles than SMs)
-inline int mmq_token_tile(long long row_tiles, int ntok) {
-    const long long ctas64 = row_tiles * ((ntok + 63) / 64);
-    return ctas64 < gemv_sm_count() && ntok > 16 ? 32 : 64;
-}
-
-// token tile of k_mmq: the widest of 64 / 32 / 16 that still gives every SM
+// token tile of k_mmq / k_mmq_kq: the widest of 64 / 32 / 16 that still gives every SM
 // a tile (the fold work per tile scales with the tile's tokens, so narrower
-// tiles spread a short matrix over more SMs); 16 when none does
+// tiles spread a short matrix over more SMs) and is not wider than the
+// tokens rounded up to 16; 16 when none qualifies
 inline int mmq_q32_token_tile(long long row_tiles, int ntok) {
     const long long sms = gemv_sm_count();
+    const int ntok16 = (ntok + 15) / 16 * 16;
     for (int tn : {64, 32})
-        if (row_tiles * ((ntok + tn - 1) / tn) >= sms) return tn;
+        if (tn <= ntok16 && row_tiles * ((ntok + tn - 1) / tn) >= sms) return tn;
     return 16;
 }
 
@@ -870,11 +979,11 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
     a.ntok = ntok;
     a.nblk = cols / 256;
     Q35_TRY_RC(mmq_prepare());
-    if (mmq_token_tile(tiles, ntok) == 32)
-        return launch_k(k_mmq_kq<32>, dim3((unsigned)tiles, (unsigned)((ntok + 31) / 32)), dim3(MMQK_THREADS),
-                        (size_t)MMQK_SMEM, st, a);
-    return launch_k(k_mmq_kq<64>, dim3((unsigned)tiles, (unsigned)((ntok + 63) / 64)), dim3(MMQK_THREADS),
-                    (size_t)MMQK_SMEM, st, a);
+    const int tn = mmq_q32_token_tile(tiles, ntok);
+    const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn));
+    if (tn == 16) return launch_k(k_mmq_kq<16>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<16>::SMEM, st, a);
+    if (tn == 32) return launch_k(k_mmq_kq<32>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<32>::SMEM, st, a);
+    return launch_k(k_mmq_kq<64>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<64>::SMEM, st, a);
 }
 
 // Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL (Q8_0
