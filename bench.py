@@ -440,6 +440,202 @@ def run_reference_arm(args, rank):
     del keep, torch
 
 
+# ---------------------------------------------------------------------------
+# isolated kernel sweeps (BASELINE configs 2 and 3): `--sweep gemv|gdn|all`
+# ---------------------------------------------------------------------------
+SWEEP_TYPES = ("Q8_0", "IQ4_NL", "Q4_K", "Q5_K", "Q6_K")
+SWEEP_SHAPES = ((1024, 6144), (1024, 3584), (3584, 1024), (2048, 1024), (1024, 248320))  # [in, out]
+SWEEP_TOKENS = (1, 8, 64, 512)
+ROTATE_BYTES = 3 * 126 * 2**20  # distinct weight bytes cycled through: 3x L2
+
+
+def _timed_loop(torch, launch, n_rot, target_ms=40.0):
+    """average device time of one launch: `reps` launches cycling through
+    n_rot weight copies are captured in one CUDA graph (so host-side launch
+    cost does not gap the stream), the graph is replayed, and CUDA events on
+    the replay stream time 3 replays.  launch(i, stream) issues launch i."""
+    st = torch.cuda.current_stream()
+    for i in range(3):
+        launch(i % n_rot, st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(3):
+        launch(i % n_rot, st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    est = max(e0.elapsed_time(e1) / 3, 1e-3)
+    reps = int(min(400, max(8, target_ms / est)))
+    reps = max(reps, n_rot) if n_rot <= 400 else reps
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cs = torch.cuda.current_stream()
+        for i in range(reps):
+            launch(i % n_rot, cs)
+    g.replay()
+    g.replay()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(3):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (3 * reps)
+    del g
+    return ms, reps
+
+
+def sweep_gemv(L, hbm):
+    """quantized matvec / MMQ over BASELINE config 2: seeded N(0,1) f32
+    weights [in, out] encoded on the device (q35b_quantize_weight), f32
+    N(0,1) activations quantized by the activation quantizer of the weight's
+    family, timed through q35_launch_mul_mat_vec.  Weight copies are rotated
+    so that at least 3x L2 of distinct weight bytes pass between reuses."""
+    import numpy as np
+    import torch
+    from qwen35_b200.lib import GEOM, TT
+    st = torch.cuda.current_stream()
+    s = ctypes.c_void_p(st.cuda_stream)
+    g = torch.Generator(device="cuda")
+    for cols, rows in SWEEP_SHAPES:
+        for tname in SWEEP_TYPES:
+            tt = TT[tname]
+            e, b = GEOM[tt]
+            row_bytes = cols // e * b
+            mbytes = rows * row_bytes
+            pitch = (mbytes + 255) // 256 * 256
+            n_rot = max(2, -(-ROTATE_BYTES // mbytes))
+            g.manual_seed(1000 + rows + cols + tt)
+            wf = torch.randn(rows * cols, device="cuda", generator=g)
+            wq = torch.empty(n_rot * pitch, dtype=torch.uint8, device="cuda")
+            assert L.q35b_quantize_weight(tt, wf.data_ptr(), wq.data_ptr(), rows * cols // e, s) == 0
+            del wf
+            for i in range(1, n_rot):
+                wq[i * pitch:i * pitch + mbytes].copy_(wq[:mbytes])
+            fam = 32 if e == 32 else 256
+            abytes = cols // fam * (34 if fam == 32 else 292)
+            for ntok in SWEEP_TOKENS:
+                x = torch.randn(ntok * cols, device="cuda", generator=g)
+                xq = torch.empty(ntok * abytes, dtype=torch.uint8, device="cuda")
+                quant = L.q35_launch_quantize_q8_0 if fam == 32 else L.q35_launch_quantize_q8_K
+                assert quant(x.data_ptr(), xq.data_ptr(), ntok * cols // fam, s) == 0
+                out = torch.empty(ntok * rows, device="cuda")
+                base = wq.data_ptr()
+
+                def launch(i, ls):
+                    rc = L.q35_launch_mul_mat_vec(base + i * pitch, xq.data_ptr(), out.data_ptr(), rows, cols,
+                                                  ntok, tt, ctypes.c_void_p(ls.cuda_stream))
+                    assert rc == 0, rc
+
+                ms, reps = _timed_loop(torch, launch, n_rot)
+                algo = mbytes + ntok * cols * 4 + ntok * rows * 4
+                ops = 2.0 * rows * cols * ntok
+                if ntok >= 16 and tname != "Q6_K":
+                    path = "k_mmq" if tname in ("Q8_0", "IQ4_NL") else "k_mmq_kq"
+                elif tname != "Q6_K":
+                    path = "k_gemv_lpr"
+                else:
+                    path = "k_gemv"
+                line = {"sweep": "gemv", "type": tname, "in": cols, "out": rows, "tokens": ntok,
+                        "kernel": path, "us": ms * 1e3, "weight_bytes": mbytes, "algo_bytes": algo,
+                        "gbs": algo / (ms * 1e-3) / 1e9, "frac_hbm": algo / (ms * 1e-3) / 1e9 / hbm,
+                        "int8_tops": ops / (ms * 1e-3) / 1e12, "rotated_copies": n_rot, "reps": reps}
+                print(json.dumps(line), flush=True)
+                del x, xq, out
+            del wq
+            torch.cuda.empty_cache()
+
+
+def sweep_gdn(L, hbm):
+    """gated delta-net in isolation: 16 heads, dk = dv =
+    128, f32 state, q/k L2-normalised, beta = sigmoid(N(0,1)), gamma =
+    exp(-softplus(N(0,1))), causal conv k=4 over 6144 channels.  Decode step
+    at batch 1/16/64 (conv step + delta-rule step, each sequence its own
+    state); prefill of one sequence of 512/2048/8192 tokens, exact per-token
+    kernel and the WY chunked form; a ragged batch of 32 sequences with
+    lengths uniform in 64..4096 (one WY launch per sequence)."""
+    import numpy as np
+    import torch
+    st = torch.cuda.current_stream()
+    s = ctypes.c_void_p(st.cuda_stream)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    H, D, CH = 16, 128, 6144
+    F = torch.nn.functional
+
+    def qk(n):
+        return F.normalize(torch.randn(n, D, device="cuda", generator=g), dim=1).contiguous()
+
+    for B in (1, 16, 64):
+        nh = H * B
+        # rotate states so >= 3x L2 of distinct state passes between reuses
+        sbytes = nh * D * D * 4
+        n_rot = max(2, -(-ROTATE_BYTES // sbytes))
+        state = torch.randn(n_rot, nh * D * D, device="cuda", generator=g) * 0.01
+        k, q, v = qk(nh), qk(nh), torch.randn(nh, D, device="cuda", generator=g)
+        q.mul_(1.0 / np.sqrt(D))
+        gamma = torch.exp(-F.softplus(torch.randn(nh, device="cuda", generator=g)))
+        beta = torch.sigmoid(torch.randn(nh, device="cuda", generator=g))
+        km, delta, out = (torch.empty(nh, D, device="cuda") for _ in range(3))
+        conv = torch.randn(n_rot, B * CH * 3, device="cuda", generator=g)
+        wconv = torch.randn(B * CH * 4, device="cuda", generator=g)
+        y = torch.randn(B * CH, device="cuda", generator=g)
+
+        def launch(i, ls):
+            s = ctypes.c_void_p(ls.cuda_stream)
+            assert L.q35_launch_conv_step(conv[i].data_ptr(), y.data_ptr(), wconv.data_ptr(), B * CH, s) == 0
+            assert L.q35_launch_gdn_step_rows(state[i].data_ptr(), D * D, k.data_ptr(), D, v.data_ptr(), D,
+                                              q.data_ptr(), D, km.data_ptr(), delta.data_ptr(), out.data_ptr(),
+                                              gamma.data_ptr(), beta.data_ptr(), nh, nh, D, D, s) == 0
+
+        ms, reps = _timed_loop(torch, launch, n_rot)
+        algo = 2 * sbytes + B * CH * (3 * 2 + 4 + 2) * 4 + nh * D * 4 * 6
+        print(json.dumps({"sweep": "gdn", "mode": "decode", "batch": B, "heads": nh, "us": ms * 1e3,
+                          "algo_bytes": algo, "gbs": algo / (ms * 1e-3) / 1e9,
+                          "frac_hbm": algo / (ms * 1e-3) / 1e9 / hbm, "launches": 2, "rotated_copies": n_rot,
+                          "reps": reps}), flush=True)
+        del state, conv
+        torch.cuda.empty_cache()
+
+    def prefill(rows, wy, state):
+        k, q, v = qk(rows * H).view(rows, H * D), qk(rows * H).view(rows, H * D), \
+            torch.randn(rows, H * D, device="cuda", generator=g)
+        q.mul_(1.0 / np.sqrt(D))
+        gamma = torch.exp(-F.softplus(torch.randn(rows, H, device="cuda", generator=g)))
+        beta = torch.sigmoid(torch.randn(rows, H, device="cuda", generator=g))
+        km, delta, out = (torch.empty(rows, H * D, device="cuda") for _ in range(3))
+        fn = L.q35_launch_gdn_step_wy if wy else L.q35_launch_gdn_step_rows_chunk
+        keep = (k, q, v, gamma, beta, km, delta, out)
+
+        def launch(_i, ls):
+            assert fn(state.data_ptr(), D * D, k.data_ptr(), H * D, v.data_ptr(), H * D, q.data_ptr(), H * D,
+                      km.data_ptr(), H * D, delta.data_ptr(), H * D, out.data_ptr(), H * D, gamma.data_ptr(), H,
+                      beta.data_ptr(), H, H, H, D, D, rows, ctypes.c_void_p(ls.cuda_stream)) == 0
+        return launch, keep
+
+    state = torch.zeros(H * D * D, device="cuda")
+    for rows in (512, 2048, 8192):
+        for wy in (False, True):
+            launch, keep = prefill(rows, wy, state)
+            ms, reps = _timed_loop(torch, launch, 1, target_ms=100.0)
+            print(json.dumps({"sweep": "gdn", "mode": "prefill", "form": "WY (32-token blocks)" if wy else
+                              "exact per-token", "seq_len": rows, "us": ms * 1e3,
+                              "tokens_per_s": rows / (ms * 1e-3), "reps": reps}), flush=True)
+            del keep
+    # ragged: 32 sequences, lengths U[64, 4096], each its own state
+    lens = np.random.default_rng(3).integers(64, 4097, 32)
+    states = torch.zeros(32, H * D * D, device="cuda")
+    runs = [prefill(int(n), True, states[i]) for i, n in enumerate(lens)]
+
+    def ragged(_i, ls):
+        for launch, _k in runs:
+            launch(0, ls)
+
+    ms, reps = _timed_loop(torch, ragged, 1, target_ms=200.0)
+    print(json.dumps({"sweep": "gdn", "mode": "ragged prefill", "form": "WY (32-token blocks)", "sequences": 32,
+                      "tokens": int(lens.sum()), "us": ms * 1e3, "tokens_per_s": float(lens.sum()) / (ms * 1e-3),
+                      "launches": 32, "reps": reps}), flush=True)
+
+
 METRIC = "decode tokens/s at batch 1/64 (0.8B Q8_0, 4B IQ4_NL); GEMV HBM GB/s vs peak"
 CONFIG_08B = {"workload": "0.8B-Q8_0 greedy decode, batch 1, 128-token prompt (BASELINE config 1)",
               "model": "qwen3.5-0.8b-q8_0 (24 layers LLLFx6, hidden 1024, ffn 3584, vocab 248320)",
@@ -457,6 +653,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--no-variants", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", choices=["gemv", "gdn", "all"], default=None,
+                    help="isolated kernel sweeps (BASELINE configs 2 / 3) instead of the decode bench")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -487,6 +685,15 @@ def main():
     if dist:
         dist.barrier()
     pk, pk_kind = peaks()
+    if args.sweep:
+        from qwen35_b200 import lib as qlib
+        L = qlib.load()
+        hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        if args.sweep in ("gemv", "all"):
+            sweep_gemv(L, hbm)
+        if args.sweep in ("gdn", "all"):
+            sweep_gdn(L, hbm)
+        return
     extra = 2 * (args.warmup + args.steps) + 8
 
     # ---------------- headline: 0.8B Q8_0, batch 1 ----------------

@@ -450,4 +450,286 @@ inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t s
                     attx_pv_smem(G), st, a);
 }
 
+
+// ---------------------------------------------------------------------------
+// Fused decode attention for short contexts: prelude + scores + softmax +
+// P.V in ONE launch.  A cluster of ATTF_CS CTAs owns one (kv head, sequence);
+// the CTAs exchange through distributed shared memory:
+//   A. prelude: CTA g < G normalises / rotates q head g (RMSNorm with the
+//      serial sum, RoPE of dims 0..63); CTA kp = G % ATTF_CS does the kv
+//      head's k (norm, RoPE) and appends k and v to the cache at pos
+//      (engine.zig:1975-2010, the CPU operations of k_attn_prelude);
+//   B. scores: positions in 32-position chunks, chunk c on CTA c % ATTF_CS;
+//      thread (g, t) forms q_g . k_t over the 256 dims in order, times the
+//      scale (elementwise.zig:349-356);
+//   C. softmax: every CTA gathers the whole score rows of its G heads and
+//      takes max, exp(s - max), the serial sum in position order and the
+//      division (elementwise.zig:357-366);
+//   D. P.V: CTA r owns dims 32r .. 32r+31 of the G heads: acc += p_t * v_t
+//      in position order (elementwise.zig:367-372), then the sigmoid gate
+//      and, for a Q8_0 consumer, the quantized block (one warp = one block).
+// Same operations in the same order as the separate kernels, so the results
+// are identical; what goes away is three launches and the score round trips.
+// ---------------------------------------------------------------------------
+constexpr int ATTF_CS = 8;        // CTAs per cluster (dims 32 x 8 = 256)
+constexpr int ATTF_THREADS = 256;
+constexpr int ATTF_MAX_LEN = 1024;
+constexpr int ATTF_VT = 64;       // V rows per staged tile
+constexpr int ATTF_VST = 3;       // V tiles in flight
+
+struct AttfArgs {
+    const float *qg;      // [n][heads][q_h | gate_h] (2 * q_dim per token)
+    const float *kb, *vb; // [n][kv_dim]: this step's k and v projections
+    const float *qw, *kw; // q / k RMSNorm weights (256)
+    float eps, base, scale;
+    const int *pos, *slots;
+    float *kc, *vc;       // KV pools of this layer: [slot][max_seq][kv_dim]
+    long long kv_slot;
+    int heads, kv_heads;
+    float *out;           // gated attention output, [n][q_dim]
+    int fam;              // 32: also quantize the output into xq
+    uint8_t *xq;
+    long long xq_ld;
+};
+
+inline size_t attf_smem(int G) {
+    // q rows | own head (k or q) | v row | K chunk | own scores | all scores | V ring
+    return (size_t)(G * ATT_HD + 2 * ATT_HD + ATT_HD + ATTX_CHUNK * ATTX_KLD + 2 * G * ATTF_MAX_LEN +
+                    ATTF_VST * ATTF_VT * 32) * 4;
+}
+
+Q35_DEV float *attf_remote(float *p, int rank) {
+    uint32_t a = smem_u32(p), r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return reinterpret_cast<float *>((uintptr_t)r);  // a shared::cluster address, read with attf_ld
+}
+Q35_DEV float attf_ld(const float *p) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"((uint32_t)(uintptr_t)p) : "memory");
+    return v;
+}
+Q35_DEV void attf_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+Q35_DEV int attf_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return (int)r;
+}
+
+// RMSNorm (serial sum of squares) then RoPE on dims 0..63 of one 256-float
+// head vector in shared memory, by the whole CTA (as k_attn_prelude)
+Q35_DEV void attf_norm_rope(float *y, const float *wn, float eps, int p, float base, float *s_ss) {
+    const int j = threadIdx.x;
+    const float x = y[j];
+    __syncthreads();
+    if (j == 0) *s_ss = serial_sumsq(y, ATT_HD);
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(*s_ss, (float)ATT_HD), eps)));
+    y[j] = __fmul_rn(__fmul_rn(x, scale), wn[j]);
+    __syncthreads();
+    if (j < 32) {
+        float c, s;
+        rope_cs(p, base, j, c, s);
+        const float a = y[j], b = y[j + 32];
+        y[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        y[j + 32] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_constant__ AttfArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float s_f[];
+    __shared__ float s_ss, s_red[ATTF_THREADS / 32];
+    const int G = a.heads / a.kv_heads;
+    const int r = attf_rank(), kvh = blockIdx.y, seq = blockIdx.z, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    float *s_q = s_f;                              // [G][256]  all q rows (gathered)
+    float *s_own = s_q + G * ATT_HD;               // [2][256]  this CTA's q row / k row
+    float *s_vrow = s_own + 2 * ATT_HD;            // [256]     this step's v row
+    float *s_k = s_vrow + ATT_HD;                  // [32][ATTX_KLD]
+    float *s_sc = s_k + ATTX_CHUNK * ATTX_KLD;     // [G][MAX_LEN] own scores
+    float *s_p = s_sc + G * ATTF_MAX_LEN;          // [G][MAX_LEN] gathered rows -> probabilities
+    float *s_v = s_p + G * ATTF_MAX_LEN;           // [VST][VT][32]
+    const int p = a.pos[seq], len = p + 1;
+    const long long slot = a.slots[seq];
+    const int q_dim = a.heads * ATT_HD, kv_dim = a.kv_heads * ATT_HD;
+    const int kp = G % ATTF_CS;  // the CTA doing the k head
+    float *kdst = a.kc + slot * a.kv_slot + (long long)p * kv_dim + kvh * ATT_HD;
+    float *vdst = a.vc + slot * a.kv_slot + (long long)p * kv_dim + kvh * ATT_HD;
+
+    // ---- A: prelude ----
+    if (r < G) {
+        const int h = kvh * G + r;
+        s_own[tid] = a.qg[(long long)seq * 2 * q_dim + (long long)h * 2 * ATT_HD + tid];
+        attf_norm_rope(s_own, a.qw, a.eps, p, a.base, &s_ss);
+    }
+    if (r == kp) {
+        float *yk = s_own + ATT_HD;
+        yk[tid] = a.kb[(long long)seq * kv_dim + kvh * ATT_HD + tid];
+        const float v = a.vb[(long long)seq * kv_dim + kvh * ATT_HD + tid];
+        s_vrow[tid] = v;
+        attf_norm_rope(yk, a.kw, a.eps, p, a.base, &s_ss);
+        kdst[tid] = yk[tid];
+        vdst[tid] = v;
+        __threadfence();  // the appended rows are read by the cluster's CTAs after the barrier
+    }
+    attf_cluster_sync();
+
+    // ---- B: scores of this CTA's position chunks ----
+    for (int i = tid; i < G * ATT_HD; i += ATTF_THREADS) {
+        const int g = i / ATT_HD, d = i - g * ATT_HD;
+        s_q[i] = attf_ld(attf_remote(s_own + d, g));
+    }
+    const float *kbase = a.kc + slot * a.kv_slot + kvh * ATT_HD;
+    for (int c = r; c * ATTX_CHUNK < len; c += ATTF_CS) {
+        const int p0 = c * ATTX_CHUNK, np = min(ATTX_CHUNK, len - p0);
+        __syncthreads();  // s_k free (previous chunk done), s_q complete
+        for (int idx = tid; idx < np * (ATT_HD / 4); idx += ATTF_THREADS) {
+            const int rr = idx / (ATT_HD / 4), cc = idx - rr * (ATT_HD / 4);
+            cp_async16(&s_k[rr * ATTX_KLD + cc * 4], kbase + (long long)(p0 + rr) * kv_dim + cc * 4);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        for (int w = warp; w < G; w += ATTF_THREADS / 32) {
+            if (lane < np) {
+                const float4 *kr = reinterpret_cast<const float4 *>(s_k + lane * ATTX_KLD);
+                const float4 *qr = reinterpret_cast<const float4 *>(s_q + w * ATT_HD);
+                float s = 0.0f;
+#pragma unroll 8
+                for (int d4 = 0; d4 < ATT_HD / 4; d4++) {
+                    const float4 kv = kr[d4], qv = qr[d4];
+                    s = __fadd_rn(s, __fmul_rn(qv.x, kv.x));
+                    s = __fadd_rn(s, __fmul_rn(qv.y, kv.y));
+                    s = __fadd_rn(s, __fmul_rn(qv.z, kv.z));
+                    s = __fadd_rn(s, __fmul_rn(qv.w, kv.w));
+                }
+                s_sc[w * ATTF_MAX_LEN + p0 + lane] = __fmul_rn(s, a.scale);
+            }
+        }
+    }
+    attf_cluster_sync();
+
+    // ---- C: whole score rows, softmax ----
+    for (int i = tid; i < G * len; i += ATTF_THREADS) {
+        const int g = i / len, t = i - g * len;
+        const int owner = (t / ATTX_CHUNK) % ATTF_CS;
+        s_p[g * ATTF_MAX_LEN + t] = attf_ld(attf_remote(s_sc + g * ATTF_MAX_LEN + t, owner));
+    }
+    attf_cluster_sync();  // no remote reads after this point: CTAs may finish independently
+    for (int g = 0; g < G; g++) {
+        float *row = s_p + g * ATTF_MAX_LEN;
+        float m = -3.40282347e38f;
+        for (int t = tid; t < len; t += ATTF_THREADS) m = fmaxf(m, row[t]);
+        m = warp_max(m);
+        if (lane == 0) s_red[warp] = m;
+        __syncthreads();
+        m = s_red[0];
+#pragma unroll
+        for (int w = 1; w < ATTF_THREADS / 32; w++) m = fmaxf(m, s_red[w]);
+        for (int t = tid; t < len; t += ATTF_THREADS) row[t] = exp_f(__fsub_rn(row[t], m));
+        __syncthreads();
+    }
+    if (tid < G) {  // one thread per head: the serial sum, loads running ahead of the adds
+        const float *row = s_p + tid * ATTF_MAX_LEN;
+        float sum = 0.0f;
+        int t = 0;
+        for (; t + 32 <= len; t += 32) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = row[t + i];
+#pragma unroll
+            for (int i = 0; i < 32; i++) sum = __fadd_rn(sum, v[i]);
+        }
+        for (; t < len; t++) sum = __fadd_rn(sum, row[t]);
+        s_red[tid] = sum;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * len; i += ATTF_THREADS) {
+        const int g = i / len, t = i - g * len;
+        s_p[g * ATTF_MAX_LEN + t] = __fdiv_rn(s_p[g * ATTF_MAX_LEN + t], s_red[g]);
+    }
+
+    // ---- D: P.V for dims 32r .. 32r+31 ----
+    const float *vbase = a.vc + slot * a.kv_slot + kvh * ATT_HD + r * 32;
+    const int ntile = (len + ATTF_VT - 1) / ATTF_VT;
+    auto load_tile = [&](int k) {
+        if (k < ntile) {
+            const int t0 = k * ATTF_VT, nt = min(ATTF_VT, len - t0);
+            float *dv = s_v + (k % ATTF_VST) * ATTF_VT * 32;
+            for (int idx = tid; idx < nt * 8; idx += ATTF_THREADS) {
+                const int rr = idx >> 3, cc = idx & 7;
+                cp_async16(dv + rr * 32 + cc * 4, vbase + (long long)(t0 + rr) * kv_dim + cc * 4);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int k = 0; k < ATTF_VST - 1; k++) load_tile(k);
+    const int g = warp, dl = lane;  // thread = (head g of the group, dim 32r + dl)
+    float acc = 0.0f;
+    for (int k = 0; k < ntile; k++) {
+        cp_async_wait<ATTF_VST - 2>();
+        __syncthreads();  // tile k landed everywhere; tile k-1's buffer is free (and s_p is final)
+        load_tile(k + ATTF_VST - 1);
+        if (g < G) {
+            const float *v = s_v + (k % ATTF_VST) * ATTF_VT * 32 + dl;
+            const float *pr = s_p + g * ATTF_MAX_LEN + k * ATTF_VT;
+            const int nt = min(ATTF_VT, len - k * ATTF_VT);
+#pragma unroll 8
+            for (int t = 0; t < nt; t++) acc = __fadd_rn(acc, __fmul_rn(pr[t], v[t * 32]));
+        }
+    }
+    cp_async_wait<0>();
+    if (g < G) {
+        const int h = kvh * G + g, dim = r * 32 + dl;
+        const float gt = a.qg[(long long)seq * 2 * q_dim + (long long)h * 2 * ATT_HD + ATT_HD + dim];
+        const float o = __fmul_rn(acc, sigmoid_f(gt));
+        a.out[(long long)seq * q_dim + (long long)h * ATT_HD + dim] = o;
+        if (a.fam == 32) quant_q8_0_warp(o, a.xq + (long long)seq * a.xq_ld + (long long)(h * 8 + r) * 34, lane);
+    }
+}
+
+inline int attf_prepare() {
+    static int done = 0;
+    if (done) return 0;
+    const int rc = (int)cudaFuncSetAttribute(k_attn_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)attf_smem(8));
+    if (!rc) done = 1;
+    return rc;
+}
+
+// Returns -1 (nothing launched) when the fused kernel does not apply: heads
+// of 256 only, G <= 8, contexts up to ATTF_MAX_LEN positions, batches that
+// fit in one wave of clusters.
+inline int attf_launch(const AttfArgs &a, int nseq, int max_len, cudaStream_t st) {
+    if (nseq <= 0) return 0;
+    if (a.kv_heads <= 0 || a.heads % a.kv_heads) return -1;
+    const int G = a.heads / a.kv_heads;
+    if (G > 8 || max_len > ATTF_MAX_LEN) return -1;
+    // one wave (two clusters' CTAs per SM): beyond that the split kernels,
+    // which parallelise over positions without a cluster, are faster
+    if ((long long)nseq * a.kv_heads * ATTF_CS > 2LL * gemv_sm_count()) return -1;
+    Q35_TRY_RC(attf_prepare());
+    launch_count()++;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ATTF_CS, (unsigned)a.kv_heads, (unsigned)nseq);
+    cfg.blockDim = dim3(ATTF_THREADS);
+    cfg.dynamicSmemBytes = attf_smem(G);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ATTF_CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return (int)cudaLaunchKernelEx(&cfg, k_attn_fused, a);
+}
+
 }  // namespace q35

@@ -194,6 +194,17 @@ Q35_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
         : "memory");
 }
 
+// shared -> global bulk copy (16-byte aligned, size % 16 == 0) in a bulk
+// group; bulk_s2g_wait_read() returns once the source shared memory has been
+// read (the global writes complete on their own before the grid does)
+Q35_DEV void bulk_s2g(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+Q35_DEV void bulk_s2g_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 Q35_DEV void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -269,36 +280,157 @@ Q35_DEV float block_sum(float v, float *red) {
 // Sum of squares in the CPU's serial order: ((x0*x0 + x1*x1) + x2*x2) + ...
 // (src/elementwise.zig:45-46).  One thread, one dependent add per element;
 // `x` should be in shared memory (4-float reads keep the chain fed).
-Q35_DEV float serial_sumsq(const float *x, int n) {
-    float s = 0.0f;
+// The chain step for NC chains at once: add the 16 products p[] to every
+// chain c[0..NC) in order, while forming the 16 products of b[] into q[]
+#define Q35_SUMSQ_STEP(p, b, q)                                         \
+    _Pragma("unroll") for (int k = 0; k < 4; k++) {                     \
+        _Pragma("unroll") for (int h = 0; h < NC; h++) c[h] = __fadd_rn(c[h], p[4 * k]);     \
+        q[4 * k] = __fmul_rn(b[k].x, b[k].x);                           \
+        _Pragma("unroll") for (int h = 0; h < NC; h++) c[h] = __fadd_rn(c[h], p[4 * k + 1]); \
+        q[4 * k + 1] = __fmul_rn(b[k].y, b[k].y);                       \
+        _Pragma("unroll") for (int h = 0; h < NC; h++) c[h] = __fadd_rn(c[h], p[4 * k + 2]); \
+        q[4 * k + 2] = __fmul_rn(b[k].z, b[k].z);                       \
+        _Pragma("unroll") for (int h = 0; h < NC; h++) c[h] = __fadd_rn(c[h], p[4 * k + 3]); \
+        q[4 * k + 3] = __fmul_rn(b[k].w, b[k].w);                       \
+    }
+
+// NC serial chains c[h] <- ((c[h] + x0*x0) + x1*x1) + ... over x[0..n)
+// (the CPU's order, src/elementwise.zig:45-46), x in shared memory.  With
+// x 16-byte aligned the first multiple of 32 elements runs software-
+// pipelined in 16-element chunks, two per iteration (registers alternate,
+// nothing is copied): while the adds of chunk c run, the products of chunk
+// c+1 are formed and chunk c+2 is loaded, so the dependent adds are the
+// critical path (one add latency per element).  Same operations, same order.
+template <int NC>
+Q35_DEV void sumsq_chains(float (&c)[NC], const float *x, int n) {
     int i = 0;
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && n >= 32) {
-        // 32-element chunks: the next chunk's loads and all of this chunk's
-        // products are issued before the dependent adds, so the chain runs at
-        // one add latency per element
         const float4 *v = reinterpret_cast<const float4 *>(x);
-        float4 cur[8];
+        const int nc = (n / 32) * 2;  // even number of 16-element chunks
+        float p[16], q[16];
+        float4 b[4], cc[4];
 #pragma unroll
-        for (int k = 0; k < 8; k++) cur[k] = v[k];
-        for (; i + 32 <= n; i += 32) {
-            float p[32];
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                p[4 * k] = __fmul_rn(cur[k].x, cur[k].x);
-                p[4 * k + 1] = __fmul_rn(cur[k].y, cur[k].y);
-                p[4 * k + 2] = __fmul_rn(cur[k].z, cur[k].z);
-                p[4 * k + 3] = __fmul_rn(cur[k].w, cur[k].w);
-            }
-            if (i + 64 <= n) {
-#pragma unroll
-                for (int k = 0; k < 8; k++) cur[k] = v[(i + 32) / 4 + k];
-            }
-#pragma unroll
-            for (int k = 0; k < 32; k++) s = __fadd_rn(s, p[k]);
+        for (int k = 0; k < 4; k++) {
+            const float4 a = v[k];
+            p[4 * k] = __fmul_rn(a.x, a.x);
+            p[4 * k + 1] = __fmul_rn(a.y, a.y);
+            p[4 * k + 2] = __fmul_rn(a.z, a.z);
+            p[4 * k + 3] = __fmul_rn(a.w, a.w);
         }
+#pragma unroll
+        for (int k = 0; k < 4; k++) b[k] = v[4 + k];
+        for (int ci = 0; ci < nc; ci += 2) {
+            // p = products of chunk ci, b = values of chunk ci+1
+            const int n2 = ci + 2 < nc ? ci + 2 : 0;  // past the end: re-read chunk 0, unused
+#pragma unroll
+            for (int k = 0; k < 4; k++) cc[k] = v[4 * n2 + k];
+            Q35_SUMSQ_STEP(p, b, q)
+            const int n3 = ci + 3 < nc ? ci + 3 : 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) b[k] = v[4 * n3 + k];
+            Q35_SUMSQ_STEP(q, cc, p)
+        }
+        i = nc * 16;
     }
-    for (; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
-    return s;
+    for (; i < n; i++) {
+        const float sq = __fmul_rn(x[i], x[i]);
+#pragma unroll
+        for (int h = 0; h < NC; h++) c[h] = __fadd_rn(c[h], sq);
+    }
+}
+#undef Q35_SUMSQ_STEP
+
+// Sum of squares in the CPU's serial order, one thread
+Q35_DEV float serial_sumsq(const float *x, int n) {
+    float c[1] = {0.0f};
+    sumsq_chains<1>(c, x, n);
+    return c[0];
+}
+
+// The serial sum continued from `s` over x[0..n) (one thread)
+Q35_DEV float serial_sumsq_from(float s, const float *x, int n) {
+    float c[1] = {s};
+    sumsq_chains<1>(c, x, n);
+    return c[0];
+}
+
+// ---------------------------------------------------------------------------
+// The serial sum of squares by a whole CTA, bit-identical to serial_sumsq
+// but with the latency of n / nwarps dependent adds instead of n.
+//
+// The f32 chain s_{i+1} = fl(s_i + fl(x_i * x_i)) stays within a few ulps of
+// the exact prefix sum (all terms are >= 0; each add rounds by at most half
+// an ulp of the running value).  So the row is cut into one segment per
+// warp; a double-precision sum of the products (any order: it is only an
+// estimate) gives the prefix at each segment's start, and warp w runs the
+// chain over its segment from the 64 f32 values within 32 ulps of that
+// estimate at once (32 lanes x 2 independent chains: the same instruction
+// stream, so no more latency than one chain).  Then one thread stitches the
+// segments in order: the candidate whose start is bit-equal to the true
+// value reached so far holds the true value at the segment's end.  If the
+// true value lies outside the window (possible for adversarial rows, e.g. a
+// huge first element absorbing small ones), that segment is recomputed
+// serially.  Either way the result is the serial chain's, bit for bit.
+//
+// x: n floats in shared memory, 16-byte aligned; called by every thread of
+// the CTA (it synchronises); returns the sum in every thread.
+// ---------------------------------------------------------------------------
+constexpr int SPEC_MAX_WARPS = 8;
+constexpr int SPEC_NC = 2;                // chains per lane
+constexpr int SPEC_CAND = 32 * SPEC_NC;   // candidates per segment
+
+Q35_DEV float cta_spec_sumsq(const float *x, int n) {
+    __shared__ float s_res[SPEC_MAX_WARPS][SPEC_CAND];
+    __shared__ double s_dsum[SPEC_MAX_WARPS];
+    __shared__ uint32_t s_est[SPEC_MAX_WARPS];
+    __shared__ float s_tot;
+    const int nw = min((int)(blockDim.x >> 5), SPEC_MAX_WARPS);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int L = ((n + nw - 1) / nw + 31) & ~31;  // segment length, a multiple of 32
+    const bool act = warp < nw;
+    const int b0 = act ? min(n, warp * L) : n, b1 = act ? min(n, b0 + L) : n;
+    // 1. the estimate: double sums of the products per segment
+    double d = 0.0;
+    for (int i = b0 + lane; i < b1; i += 32) d += (double)__fmul_rn(x[i], x[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (act && lane == 0) s_dsum[warp] = d;
+    __syncthreads();
+    if (act) {
+        double pre = 0.0;
+        for (int w = 0; w < warp; w++) pre += s_dsum[w];
+        const uint32_t eb = __float_as_uint((float)pre);  // >= +0
+        // 2. candidate chains: candidate j = lane + 32 h starts eb + j - 32
+        //    ulps (clamped at +0); warp 0 starts at exactly 0 (eb = 0, j = 32)
+        float c[SPEC_NC];
+#pragma unroll
+        for (int h = 0; h < SPEC_NC; h++) {
+            const int bb = (int)eb + lane + 32 * h - SPEC_CAND / 2;
+            c[h] = __uint_as_float(bb < 0 ? 0u : (uint32_t)bb);
+        }
+        sumsq_chains<SPEC_NC>(c, x + b0, b1 - b0);
+#pragma unroll
+        for (int h = 0; h < SPEC_NC; h++) s_res[warp][lane + 32 * h] = c[h];
+        if (lane == 0) s_est[warp] = eb;
+    }
+    __syncthreads();
+    // 3. stitch the segments in order
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < nw; w++) {
+            const int w0 = min(n, w * L), w1 = min(n, w0 + L);
+            if (w0 >= w1) break;
+            const int sb = (int)__float_as_uint(s);
+            const int j = sb - (int)s_est[w] + SPEC_CAND / 2;
+            if (j >= 0 && j < SPEC_CAND)
+                s = s_res[w][j];  // that candidate started at exactly s (sb >= 0, so no clamping)
+            else
+                s = serial_sumsq_from(s, x + w0, w1 - w0);
+        }
+        s_tot = s;
+    }
+    __syncthreads();
+    return s_tot;
 }
 
 // The same serial sum for a row in global memory, by a whole CTA: the row is

@@ -362,7 +362,7 @@ inline int eng_len_bucket(int max_len, int max_seq) {
     return b < max_seq ? b : max_seq;
 }
 
-inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream_t st) {
+inline int eng_layer_full(q35b_engine *e, int li, int n, int nrun, int max_len, cudaStream_t st) {
     const q35b_config &c = e->c;
     const LayerW &W = e->L[li];
     const int heads = c.n_heads, kvh = c.n_kv_heads, hd = c.head_dim;
@@ -376,10 +376,44 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
     float *kp = e->kpool + fi * (long long)e->n_slots * e->kv_slot;
     float *vp = e->vpool + fi * (long long)e->n_slots * e->kv_slot;
     const int *slots = e->d_in + e->max_batch, *pos = e->d_in + 2 * e->max_batch;
+    const int fo = family_of(W.o);
+    if (nrun == n && hd == ATT_HD) {
+        // decode (every token a sequence of its own): prelude, scores,
+        // softmax and P.V in one clustered launch at short contexts
+        AttfArgs f{};
+        f.qg = e->qkv;
+        f.kb = e->kb;
+        f.vb = e->vb;
+        f.qw = W.q_norm;
+        f.kw = W.k_norm;
+        f.eps = c.rms_eps;
+        f.base = c.rope_freq_base;
+        f.scale = 1.0f / sqrtf((float)hd);
+        f.pos = pos;
+        f.slots = slots;
+        f.kc = kp;
+        f.vc = vp;
+        f.kv_slot = e->kv_slot;
+        f.heads = heads;
+        f.kv_heads = kvh;
+        f.out = e->gout;
+        f.fam = fo;
+        f.xq = e->xq;
+        f.xq_ld = e->xq_ld;
+        const int rc = attf_launch(f, n, max_len, st);
+        if (rc == 0) {
+            if (fo != 32) {
+                Q35_TRY(launch_k(k_quant_rows, dim3((q_dim / 256 + 7) / 8, n), dim3(256), 0, st,
+                                 (const float *)e->gout, (long long)q_dim, q_dim, fo, e->xq, e->xq_ld));
+            }
+            Q35_TRY(eng_gemv(e, n, {eng_rowpar_seg(e, W.o)}, e->xq, q_dim, st));
+            return eng_rowpar_finish(e, n, st);
+        }
+        if (rc != -1) return rc;
+    }
     Q35_TRY(launch_k(k_attn_prelude, dim3(heads + kvh, n), dim3(256), 0, st, (const float *)e->qkv,
                      (const float *)e->kb, (const float *)e->vb, e->q, e->gate, W.q_norm, W.k_norm, heads, kvh,
                      c.rms_eps, c.rope_freq_base, pos, slots, kp, vp, e->kv_slot));
-    const int fo = family_of(W.o);
     AttnXArgs a{};
     a.q = e->q;
     a.gate = e->gate;
@@ -412,11 +446,39 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int max_len, cudaStream
 inline int eng_mlp(q35b_engine *e, int li, int n, cudaStream_t st) {
     const q35b_config &c = e->c;
     const LayerW &W = e->L[li];
+    const int fd = family_of(W.ffn_down);
+    {
+        // decode: rmsnorm -> gate / up GEMV whose epilogue forms
+        // silu(gate) * up once per row -- as Q8_0 blocks the down projection
+        // reads directly, or as f32 rows it quantizes (Q8_K family)
+        const LprPrologue pro{LPR_PRO_NORM, e->x, nullptr, W.post_norm, (long long)c.hidden, c.rms_eps};
+        const LprPair pr{fd == 32 ? e->xq : nullptr, e->xq_ld, fd == 32 ? nullptr : e->mh, (long long)c.n_ff};
+        const GemvSegDesc gu[2] = {{W.ffn_gate.w, nullptr, W.ffn_gate.rows, W.ffn_gate.tt, c.n_ff, GV_STORE},
+                                   {W.ffn_up.w, nullptr, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}};
+        const int rc = gemv_lpr_launch(gu, 2, nullptr, c.hidden, n, st, e->xq_ld, &pro, &pr);
+        if (rc == 0) {
+            const GemvSegDesc down = eng_rowpar_seg(e, W.ffn_down);
+            if (fd == 32) {
+                Q35_TRY(eng_gemv(e, n, {down}, e->xq, c.n_ff, st));
+            } else {
+                const LprPrologue rows{LPR_PRO_ROWS, e->mh, nullptr, nullptr, (long long)c.n_ff, 0.0f};
+                const int r2 = gemv_lpr_launch(&down, 1, nullptr, c.n_ff, n, st, e->xq_ld, &rows);
+                if (r2 == -1) {
+                    Q35_TRY(launch_k(k_quant_rows, dim3((c.n_ff / 256 + 7) / 8, n), dim3(256), 0, st,
+                                     (const float *)e->mh, (long long)c.n_ff, c.n_ff, fd, e->xq, e->xq_ld));
+                    Q35_TRY(eng_gemv(e, n, {down}, e->xq, c.n_ff, st));
+                } else if (r2) {
+                    return r2;
+                }
+            }
+            return eng_rowpar_finish(e, n, st);
+        }
+        if (rc != -1) return rc;
+    }
     Q35_TRY(eng_norm_gemv(e, n, W.post_norm,
                           {{W.ffn_gate.w, e->mh, W.ffn_gate.rows, W.ffn_gate.tt, c.n_ff, GV_STORE},
                            {W.ffn_up.w, e->mh1, W.ffn_up.rows, W.ffn_up.tt, c.n_ff, GV_STORE}},
                           st));
-    const int fd = family_of(W.ffn_down);
     const GemvSegDesc down = eng_rowpar_seg(e, W.ffn_down);
     const LprPrologue pro{LPR_PRO_SWIGLU, e->mh, e->mh1, nullptr, (long long)c.n_ff, 0.0f};
     const int rc = gemv_lpr_launch(&down, 1, nullptr, c.n_ff, n, st, e->xq_ld, &pro);
@@ -456,13 +518,21 @@ inline int eng_step_body(q35b_engine *e, int n, int nrun, int max_len, cudaStrea
     const q35b_config &c = e->c;
     const long long l0 = launch_count();
     const int *tok = e->d_in;
-    Q35_TRY(launch_k(k_embed_rows, dim3((c.hidden + 255) / 256, n), dim3(256), 0, st, e->token_embd.tt,
-                     e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x, c.hidden));
+    // The step's first kernel is an ordinary launch: it starts only after
+    // everything earlier on the stream (the previous step included) is done,
+    // so the kernels of this step may read per-layer state the previous step
+    // wrote (GDN state, conv history) before their own dependency wait.
+    pdl_enabled() = false;
+    const int rc_embed = launch_k(k_embed_rows, dim3((c.hidden + 255) / 256, n), dim3(256), 0, st, e->token_embd.tt,
+                                  e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x,
+                                  c.hidden);
+    pdl_enabled() = true;
+    Q35_TRY(rc_embed);
     Q35_TRY(launch_k(k_pos_to_len, dim3((n + 127) / 128), dim3(128), 0, st, (const int *)(e->d_in + 2 * e->max_batch),
                      e->d_len, n));
     for (int li = 0; li < c.n_layers; li++) {
         if (is_full_layer(c, li))
-            Q35_TRY(eng_layer_full(e, li, n, max_len, st));
+            Q35_TRY(eng_layer_full(e, li, n, nrun, max_len, st));
         else
             Q35_TRY(eng_layer_gdn(e, li, n, nrun, st));
         Q35_TRY(eng_mlp(e, li, n, st));

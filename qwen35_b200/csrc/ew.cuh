@@ -70,7 +70,9 @@ __global__ void __launch_bounds__(NT) k_rmsnorm(float *out, const float *x, cons
     const float *xr = x + (long long)blockIdx.x * n;
     float *orow = out + (long long)blockIdx.x * n;
     extern __shared__ __align__(16) float xs[];  // n floats
-    const float ss = cta_serial_sumsq(xr, n, xs);
+    for (int i = threadIdx.x; i < n; i += NT) xs[i] = xr[i];
+    __syncthreads();
+    const float ss = cta_spec_sumsq(xs, n);  // the serial order's result, segments in parallel
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
     for (int i = threadIdx.x; i < n; i += NT) orow[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
 }

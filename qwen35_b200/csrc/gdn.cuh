@@ -141,7 +141,12 @@ struct GdnCoreArgs {
 
 __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ GdnCoreArgs a) {
     pdl_trigger();
-    pdl_wait();
+    // Before the dependency wait: everything this kernel reads that the
+    // step's earlier kernels do not write -- the batch descriptor (uploaded
+    // before the step), the state block and conv history (written by this
+    // layer's previous step, which finished before the step's first,
+    // ordinarily launched kernel began), conv taps and norm weights.  The
+    // projections (qkv, z, alpha / beta) are read after the wait.
     __shared__ __align__(16) float sq[GDN_KD], sk[GDN_KD], so[GDN_KD];
     __shared__ float s_scal[4];
     const int h = blockIdx.x, r = blockIdx.y, j = threadIdx.x;
@@ -186,6 +191,7 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     }
     const float nwj = a.ssm_norm[j];
     const float ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
+    pdl_wait();
     __shared__ int s_ok;
     if (j == 0) s_ok = mbar_wait(&s_bar, 0u, 140) ? 1 : 0;
     __syncthreads();  // thread 0 saw the copy land (or gave up); all threads learn which
@@ -304,8 +310,13 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
         }
         __syncthreads();  // s_scal / sq / sk / so reused by the next token
     }
+    // the state block goes back the way it came: into shared memory (row i,
+    // column j: conflict-free), then one bulk copy to global memory
 #pragma unroll
-    for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
+    for (int i = 0; i < GDN_KD; i++) s_state[i * GDN_KD + j] = col[i];
+    fence_proxy_async();
+    __syncthreads();
+    if (j == 0) bulk_s2g(S, s_state, (uint32_t)(kd * kd * 4));
     // the history after the run, for the position after it; the owner of a
     // k head's q / k channels writes those
     auto store = [&](int c) {
@@ -319,6 +330,7 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
         store(1);
     }
     store(2);
+    if (j == 0) bulk_s2g_wait_read();  // shared memory stays live until the copy has read it
 }
 
 // ---------------------------------------------------------------------------

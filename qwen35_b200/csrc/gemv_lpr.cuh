@@ -32,8 +32,11 @@ constexpr int LPR_MAX_CW = 8;    // warps per CTA
 constexpr int LPR_MAX_NS = 16;   // ring stages per warp
 constexpr int LPR_MAX_NT = 8;    // tokens per pass
 // dynamic shared memory ceiling: the 227 KB opt-in limit less room for the
-// kernel's static shared variables
-constexpr size_t LPR_SMEM_MAX = 226 * 1024;
+// kernel's static shared variables (the CTA-wide serial sum's ~4.3 KB)
+constexpr size_t LPR_SMEM_MAX = 222 * 1024;
+// per-CTA reserve when several CTAs share an SM's 228 KB: static shared
+// variables plus the 1 KB the system keeps per CTA
+constexpr size_t LPR_CTA_RESERVE = 6 * 1024;
 
 struct LprSeg {
     const uint8_t *w;
@@ -70,9 +73,22 @@ struct LprArgs {
     long long px_ld;
     float eps;
     int x_off;              // byte offset of the staged f32 rows (norm)
+    // pair mode (the MLP's gate / up projections): seg[0] = gate, seg[1] =
+    // up, same rows; tile 2t is gate tile t and tile 2t+1 up tile t, taken
+    // by row groups 2p and 2p+1 of one CTA.  The epilogue forms
+    // h = silu(gate) * up per row (engine.zig:2027-2036) and writes it as
+    // Q8_0 blocks into `hq` (32 rows = one block of the down projection's
+    // input; hq_ld bytes between tokens) or, when hq is null, as f32 rows
+    // into `hf` (hf_ld floats between tokens).
+    int pair;
+    int p_off;              // byte offset of the pair exchange buffers
+    uint8_t *hq;
+    long long hq_ld;
+    float *hf;
+    long long hf_ld;
 };
 
-enum { LPR_PRO_NONE = 0, LPR_PRO_NORM = 1, LPR_PRO_SWIGLU = 2 };
+enum { LPR_PRO_NONE = 0, LPR_PRO_NORM = 1, LPR_PRO_SWIGLU = 2, LPR_PRO_ROWS = 3 };
 
 // The activation quantizers (quant_q8_0_warp / quant_q8_K_warp), writing the
 // GEMV's shared layout directly: int8 plane, f32 scale per block (for Q8_0
@@ -152,6 +168,24 @@ Q35_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
             "r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// The same load with an L2 eviction-priority hint.  Decode weights are
+// streamed once per step and come back only after the whole model (0.8 to 15
+// GB) has passed through the 126 MB L2, so they are marked evict-first: the
+// data that IS reused from step to step (GDN state at small batch, KV rows,
+// activations, kernel code) keeps its lines.
+Q35_DEV uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+Q35_DEV void tma_load_2d_hint(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 
@@ -412,11 +446,16 @@ Q35_DEV void lpr_q6_k(const uint8_t *rp, const ActView &A, int ntok, int gb0, in
 }
 
 Q35_DEV int lpr_find_seg(const LprArgs &a, long long tile) {
+    if (a.pair) return (int)(tile & 1);
     int s = 0;
 #pragma unroll
     for (int i = 1; i < GV_MAX_SEG; i++)
         if (i < a.nseg && tile >= a.seg[i].tile_begin) s = i;
     return s;
+}
+// first row of `tile` within its matrix
+Q35_DEV long long lpr_tile_row0(const LprArgs &a, const LprSeg &sg, long long tile) {
+    return a.pair ? (tile >> 1) * 32 : (tile - sg.tile_begin) * 32;
 }
 
 template <int NT, class Sink>
@@ -456,6 +495,7 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     const long long my_tiles = t0 < a.total_tiles ? (a.total_tiles - 1 - t0) / tstride + 1 : 0;
     const int c_lo = kq * a.nchunk / kw, c_hi = (kq + 1) * a.nchunk / kw, nck = c_hi - c_lo;
     const long long nst = my_tiles * nck;  // stages this warp consumes
+    const uint64_t wpol = l2_policy_evict_first();
 
     // stage i of this warp -> (matrix, first row, chunk); lane `lane` copies its row
     auto issue = [&](long long i) {
@@ -463,12 +503,13 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
         const int c = c_lo + (int)(i % nck);
         const int si = lpr_find_seg(a, tile);
         const LprSeg &sg = a.seg[si];
-        const long long r0 = (tile - sg.tile_begin) * 32;
+        const long long r0 = lpr_tile_row0(a, sg, tile);
         const int slot = (int)(i % a.ns);
         if (lane == 0) {
             // the box is always 32 full rows (rows past the end are zero-filled)
             mbar_arrive_expect_tx(&bar[slot], (uint32_t)(32 * sg.chunk_bytes));
-            tma_load_2d(ring + (size_t)slot * 32 * a.rs, &a.tmap[si], c * (sg.chunk_bytes / 8), (int)r0, &bar[slot]);
+            tma_load_2d_hint(ring + (size_t)slot * 32 * a.rs, &a.tmap[si], c * (sg.chunk_bytes / 8), (int)r0,
+                             &bar[slot], wpol);
         }
     };
     long long issued = nst < a.ns ? nst : a.ns;
@@ -499,9 +540,20 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
                 xd[idx] = reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j];
             }
             __syncthreads();
-            if ((int)threadIdx.x < a.ntok) {
+            if (a.ntok == 1 && cw >= 2) {
+                // one row: the whole CTA runs the chain (segments in parallel)
+                const float ss = cta_spec_sumsq(xs, a.cols);
+                if (threadIdx.x == 0)
+                    s_scale[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
+            } else if ((int)threadIdx.x < a.ntok) {
                 const float ss = serial_sumsq(xs + (size_t)threadIdx.x * a.cols, a.cols);
                 s_scale[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
+            }
+        } else if (a.prologue == LPR_PRO_ROWS) {
+            // f32 rows as they are (a producer already applied the activation)
+            for (int idx = threadIdx.x; idx < a.ntok * c4; idx += blockDim.x) {
+                const int t = idx / c4, j = idx - t * c4;
+                xd[idx] = reinterpret_cast<const float4 *>(a.px + (long long)t * a.px_ld)[j];
             }
         } else {
             // silu(gate) * up (engine.zig:2027-2036)
@@ -587,7 +639,7 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     for (long long ti = 0; ti < my_tiles; ti++) {
         const long long tile = t0 + ti * tstride;
         const LprSeg &sg = a.seg[lpr_find_seg(a, tile)];
-        const long long r0 = (tile - sg.tile_begin) * 32;
+        const long long r0 = lpr_tile_row0(a, sg, tile);
         const int nv = (int)min(32LL, sg.rows - r0);
         float acc[NT];
 #pragma unroll
@@ -616,7 +668,7 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
             if (!failed && issued < nst && issued == i + a.ns) issue(issued++);
         }
         if (kw > 1) {
-            named_bar_sync(1, kw * 32);  // the group's terms for this tile are stored (kw > 1: one group)
+            named_bar_sync(1 + rg, kw * 32);  // the group's terms for this tile are stored
             if (kq == 0 && !failed && lane < nv) {
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
@@ -629,9 +681,35 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
                     }
                 }
             }
-            named_bar_sync(1, kw * 32);  // folded before the next tile's terms land
+            named_bar_sync(1 + rg, kw * 32);  // folded before the next tile's terms land
         }
-        if (kq == 0 && !failed && lane < nv) {
+        if (a.pair) {
+            // gate / up epilogue: the up group hands its sums to the gate
+            // group of the same pair through shared memory
+            if (kq == 0) {
+                const int pr = rg >> 1;
+                float *xb = reinterpret_cast<float *>(smem + a.p_off) + (size_t)pr * NT * 32;
+                if (rg & 1) {
+#pragma unroll
+                    for (int t = 0; t < NT; t++) xb[t * 32 + lane] = (!failed && lane < nv) ? acc[t] : 0.0f;
+                }
+                named_bar_sync(8 + pr, 64);
+                if (!(rg & 1)) {
+                    const long long blk = tile >> 1;  // = r0 / 32
+#pragma unroll
+                    for (int t = 0; t < NT; t++) {
+                        if (t < a.ntok) {
+                            const float h = (!failed && lane < nv) ? __fmul_rn(silu_f(acc[t]), xb[t * 32 + lane]) : 0.0f;
+                            if (a.hq)
+                                quant_q8_0_warp(h, a.hq + (long long)t * a.hq_ld + blk * 34, lane);
+                            else if (lane < nv)
+                                a.hf[(long long)t * a.hf_ld + r0 + lane] = h;
+                        }
+                    }
+                }
+                named_bar_sync(8 + pr, 64);  // the buffer is read before the next tile's sums land
+            }
+        } else if (kq == 0 && !failed && lane < nv) {
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t < a.ntok) {
@@ -672,12 +750,20 @@ inline bool lpr_type_ok(int tt) {
 
 // f32 rows the launch quantizes itself (see LprArgs::prologue)
 struct LprPrologue {
-    int kind;              // LPR_PRO_NORM or LPR_PRO_SWIGLU
+    int kind;              // LPR_PRO_NORM, LPR_PRO_SWIGLU or LPR_PRO_ROWS
     const float *x, *u, *w;
     long long ld;          // floats between tokens of x (and u)
     float eps;
 };
 constexpr size_t LPR_PRO_STAGE_MAX = 64 * 1024;  // f32 rows a fused prologue stages in shared memory
+
+// pair mode destination (see LprArgs::pair): Q8_0 blocks, or f32 rows
+struct LprPair {
+    uint8_t *hq;
+    long long hq_ld;
+    float *hf;
+    long long hf_ld;
+};
 
 // Try the lane-per-row kernel.  Returns -1 (nothing launched) when the
 // matrices or the shape are not eligible, else the launch status.
@@ -720,10 +806,18 @@ inline bool lpr_encode(CUtensorMap *m, const void *w, int row_bytes, long long r
 inline int lpr_tmpl_nt(int nt) { return nt == 1 ? 1 : (nt == 2 ? 2 : (nt <= 4 ? 4 : 8)); }
 
 inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
-                           long long xq_ld, const LprPrologue *pro = nullptr) {
+                           long long xq_ld, const LprPrologue *pro = nullptr, const LprPair *pair = nullptr) {
     if (nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || ntok <= 0 || cols % 256 != 0) return -1;
+    if (pair) {
+        // gate / up of one MLP: same rows and type, activation built in the
+        // kernel (the epilogue's Q8_0 output may be the buffer a caller would
+        // otherwise pass as xq)
+        if (nseg != 2 || !pro || segs[0].rows != segs[1].rows || segs[0].ttype != segs[1].ttype) return -1;
+        if (pair->hq ? (pair->hq_ld <= 0) : (!pair->hf || pair->hf_ld < segs[0].rows)) return -1;
+        if (pair->hq && segs[0].rows % 32) return -1;
+    }
     if (pro) {
-        if (pro->kind != LPR_PRO_NORM && pro->kind != LPR_PRO_SWIGLU) return -1;
+        if (pro->kind != LPR_PRO_NORM && pro->kind != LPR_PRO_SWIGLU && pro->kind != LPR_PRO_ROWS) return -1;
         if (ntok >= 16) return -1;  // many tokens: the tensor-core path, after a separate prologue kernel
         if ((reinterpret_cast<uintptr_t>(pro->x) & 15u) || (pro->ld & 3)) return -1;
     }
@@ -760,15 +854,15 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     if (T >= (long long)nsm * LPR_TALL_OCC * 4) {
         ctas = (T + 3) / 4;
     } else {
-        rw = 1;
+        rw = pair ? 2 : 1;  // pair mode: a CTA takes a gate tile and the matching up tile
         const long long want = (long long)nsm * LPR_WARPS_PER_SM / T;
-        while (kw * 2 <= want && kw * 2 <= LPR_MAX_CW && kw * 2 <= nchunk) kw *= 2;
-        ctas = T;
+        while (kw * 2 <= want && rw * kw * 2 <= LPR_MAX_CW && kw * 2 <= nchunk) kw *= 2;
+        ctas = (T + rw - 1) / rw;
         occ = (int)((ctas + nsm - 1) / nsm);
     }
     occ = occ < 1 ? 1 : (occ > 8 ? 8 : occ);
     const int cw = rw * kw;
-    size_t budget = occ == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / occ - 2048;
+    size_t budget = occ == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / occ - LPR_CTA_RESERVE;
     // prologue staging: the f32 rows (+ the norm weight) of one pass
     auto xbytes = [&](int nt) -> size_t {
         if (!pro) return 0;
@@ -776,9 +870,10 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         return (b + 127) & ~size_t(127);
     };
     auto tbytes = [&](int nt) { return kw > 1 ? (size_t)rw * lpr_tmpl_nt(nt) * 32 * tst * 4 : 0; };
-    auto base_of = [&](int nt) {  // barriers | activation | staged rows | terms
+    auto pbytes = [&](int nt) { return pair ? (size_t)(rw / 2) * lpr_tmpl_nt(nt) * 32 * 4 : 0; };
+    auto base_of = [&](int nt) {  // barriers | activation | staged rows | terms | pair buffers
         return (size_t)(LPR_MAX_CW * LPR_MAX_NS * 8) + (((size_t)nt * act_stride + 127) & ~size_t(127)) + xbytes(nt) +
-               ((tbytes(nt) + 127) & ~size_t(127));
+               ((tbytes(nt) + 127) & ~size_t(127)) + ((pbytes(nt) + 127) & ~size_t(127));
     };
     // tokens per pass: at most LPR_MAX_NT, with room for a 2-stage ring
     // tokens per pass: as many as the kernel takes (each pass streams the
@@ -786,7 +881,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     int group = ntok < LPR_MAX_NT ? lpr_tmpl_nt(ntok) : LPR_MAX_NT;
     if (pro && xbytes(group) > LPR_PRO_STAGE_MAX) return -1;  // a fused prologue stages a whole pass
     auto need = [&](int g, int nsmin) { return base_of(g) + (size_t)cw * nsmin * 32 * rs; };
-    auto budget_of = [](int o) { return o == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / o - 2048; };
+    auto budget_of = [](int o) { return o == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / o - LPR_CTA_RESERVE; };
     while (occ > 1 && need(group, 2) > budget) budget = budget_of(--occ);
     while (group > 1 && need(group, 1) > budget) group >>= 1;
     if (need(group, 1) > budget) return -1;
@@ -809,7 +904,15 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         a.act_off = LPR_MAX_CW * LPR_MAX_NS * 8;
         a.x_off = (int)(a.act_off + (((size_t)nt * act_stride + 127) & ~size_t(127)));
         a.t_off = (int)(a.x_off + xbytes(nt));
+        a.p_off = (int)(a.t_off + ((tbytes(nt) + 127) & ~size_t(127)));
         a.ring_off = (int)base_of(nt);
+        if (pair) {
+            a.pair = 1;
+            a.hq = pair->hq ? pair->hq + (size_t)t0 * pair->hq_ld : nullptr;
+            a.hq_ld = pair->hq_ld;
+            a.hf = pair->hf ? pair->hf + (size_t)t0 * pair->hf_ld : nullptr;
+            a.hf_ld = pair->hf_ld;
+        }
         if (pro) {
             a.prologue = pro->kind;
             a.px = pro->x + (size_t)t0 * pro->ld;
@@ -827,7 +930,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
             s.ttype = segs[i].ttype;
             s.row_bytes = cols / g.elems * g.bytes;
             s.chunk_bytes = chunk_cols / g.elems * g.bytes;
-            s.out = segs[i].out + (size_t)t0 * segs[i].out_ld;
+            s.out = segs[i].out ? segs[i].out + (size_t)t0 * segs[i].out_ld : nullptr;
             s.out_ld = segs[i].out_ld;
             s.mode = segs[i].mode;
             s.tile_begin = tiles;

@@ -432,6 +432,35 @@ def test_norms_and_activations(L, O):
     assert np.abs(host(dsm) - rsm).max() <= 1e-6
 
 
+def test_rmsnorm_segmented_sum_edge_rows(L, O):
+    """The CTA-wide sum of squares runs one chain segment per warp from
+    candidate start values around a double-precision estimate and stitches
+    them; rows whose f32 chain drifts far from the exact prefix (small
+    squares absorbed by a huge first one), all-zero rows, growing and tiny
+    magnitudes must still give the serial order's bits (the stitch falls
+    back to a serial pass over a segment whose window misses)."""
+    rng = np.random.default_rng(21)
+    n = 1024
+    rows = []
+    r = np.full(n, 1e14, np.float32)
+    r[0] = 1e18
+    rows.append(r)                                                   # absorbed: window misses
+    rows.append(np.zeros(n, np.float32))                             # stays at +0
+    rows.append((np.geomspace(1e-3, 1e3, n) * rng.choice([-1, 1], n)).astype(np.float32))
+    rows.append((rng.standard_normal(n) * 1e-20).astype(np.float32))  # subnormal squares
+    r = rng.standard_normal(n).astype(np.float32)
+    r[::7] *= 3e4
+    rows.append(r)
+    for cols in (1024, 1000, 2560, 37):
+        x = np.stack([np.resize(rr, cols) for rr in rows]).astype(np.float32)
+        w = rng.standard_normal(cols).astype(np.float32)
+        ref = np.zeros_like(x)
+        O.q35o_rmsnorm_rows(fp(ref), fp(x), fp(w), x.shape[0], cols, 1e-6)
+        out = torch.zeros_like(dev(x))
+        ok(L.q35_launch_rmsnorm(out.data_ptr(), dev(x).data_ptr(), dev(w).data_ptr(), x.shape[0], cols, 1e-6, S))
+        assert np.array_equal(host(out).view(np.uint32), ref.view(np.uint32)), cols
+
+
 def test_rope_and_argmax(L, O):
     rng = np.random.default_rng(10)
     heads, hd = 8, 256
