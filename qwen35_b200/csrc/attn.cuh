@@ -518,8 +518,9 @@ Q35_DEV int attf_rank() {
 }
 
 // RMSNorm (serial sum of squares) then RoPE on dims 0..63 of one 256-float
-// head vector in shared memory, by the whole CTA (as k_attn_prelude)
-Q35_DEV void attf_norm_rope(float *y, const float *wn, float eps, int p, float base, float *s_ss) {
+// head vector in shared memory, by the whole CTA (as k_attn_prelude); the
+// rotation's cos / sin (threads 0..31) are computed by the caller
+Q35_DEV void attf_norm_rope(float *y, const float *wn, float eps, float rc, float rs, float *s_ss) {
     const int j = threadIdx.x;
     const float x = y[j];
     __syncthreads();
@@ -529,18 +530,15 @@ Q35_DEV void attf_norm_rope(float *y, const float *wn, float eps, int p, float b
     y[j] = __fmul_rn(__fmul_rn(x, scale), wn[j]);
     __syncthreads();
     if (j < 32) {
-        float c, s;
-        rope_cs(p, base, j, c, s);
         const float a = y[j], b = y[j + 32];
-        y[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        y[j + 32] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+        y[j] = __fsub_rn(__fmul_rn(a, rc), __fmul_rn(b, rs));
+        y[j + 32] = __fadd_rn(__fmul_rn(a, rs), __fmul_rn(b, rc));
     }
     __syncthreads();
 }
 
 __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_constant__ AttfArgs a) {
     pdl_trigger();
-    pdl_wait();
     extern __shared__ __align__(16) float s_f[];
     __shared__ float s_ss, s_red[ATTF_THREADS / 32];
     const int G = a.heads / a.kv_heads;
@@ -553,8 +551,14 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
     float *s_sc = s_k + ATTX_CHUNK * ATTX_KLD;     // [G][MAX_LEN] own scores
     float *s_p = s_sc + G * ATTF_MAX_LEN;          // [G][MAX_LEN] gathered rows -> probabilities
     float *s_v = s_p + G * ATTF_MAX_LEN;           // [VST][VT][32]
+    // Before the dependency wait: the batch descriptor (uploaded before the
+    // step) and the rotation for this position (pow / cos / sin, the slow
+    // part of the prelude)
     const int p = a.pos[seq], len = p + 1;
     const long long slot = a.slots[seq];
+    float rc = 1.0f, rs = 0.0f;
+    if (tid < 32) rope_cs(p, a.base, tid, rc, rs);
+    pdl_wait();
     const int q_dim = a.heads * ATT_HD, kv_dim = a.kv_heads * ATT_HD;
     const int kp = G % ATTF_CS;  // the CTA doing the k head
     float *kdst = a.kc + slot * a.kv_slot + (long long)p * kv_dim + kvh * ATT_HD;
@@ -564,17 +568,18 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
     if (r < G) {
         const int h = kvh * G + r;
         s_own[tid] = a.qg[(long long)seq * 2 * q_dim + (long long)h * 2 * ATT_HD + tid];
-        attf_norm_rope(s_own, a.qw, a.eps, p, a.base, &s_ss);
+        attf_norm_rope(s_own, a.qw, a.eps, rc, rs, &s_ss);
     }
     if (r == kp) {
         float *yk = s_own + ATT_HD;
         yk[tid] = a.kb[(long long)seq * kv_dim + kvh * ATT_HD + tid];
         const float v = a.vb[(long long)seq * kv_dim + kvh * ATT_HD + tid];
         s_vrow[tid] = v;
-        attf_norm_rope(yk, a.kw, a.eps, p, a.base, &s_ss);
+        attf_norm_rope(yk, a.kw, a.eps, rc, rs, &s_ss);
+        // the cache rows for later steps; this kernel reads position p's k and
+        // v from this CTA's shared memory instead
         kdst[tid] = yk[tid];
         vdst[tid] = v;
-        __threadfence();  // the appended rows are read by the cluster's CTAs after the barrier
     }
     attf_cluster_sync();
 
@@ -586,31 +591,37 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
     const float *kbase = a.kc + slot * a.kv_slot + kvh * ATT_HD;
     for (int c = r; c * ATTX_CHUNK < len; c += ATTF_CS) {
         const int p0 = c * ATTX_CHUNK, np = min(ATTX_CHUNK, len - p0);
+        const int ncache = min(np, p - p0);  // rows from the cache; row p (if in the chunk) from the k CTA
         __syncthreads();  // s_k free (previous chunk done), s_q complete
-        for (int idx = tid; idx < np * (ATT_HD / 4); idx += ATTF_THREADS) {
+        for (int idx = tid; idx < ncache * (ATT_HD / 4); idx += ATTF_THREADS) {
             const int rr = idx / (ATT_HD / 4), cc = idx - rr * (ATT_HD / 4);
             cp_async16(&s_k[rr * ATTX_KLD + cc * 4], kbase + (long long)(p0 + rr) * kv_dim + cc * 4);
         }
         cp_async_commit();
+        if (ncache < np) s_k[(p - p0) * ATTX_KLD + tid] = attf_ld(attf_remote(s_own + ATT_HD + tid, kp));
         cp_async_wait<0>();
         __syncthreads();
         for (int w = warp; w < G; w += ATTF_THREADS / 32) {
             if (lane < np) {
                 const float4 *kr = reinterpret_cast<const float4 *>(s_k + lane * ATTX_KLD);
                 const float4 *qr = reinterpret_cast<const float4 *>(s_q + w * ATT_HD);
-                float s = 0.0f;
+                float sacc = 0.0f;
 #pragma unroll 8
                 for (int d4 = 0; d4 < ATT_HD / 4; d4++) {
                     const float4 kv = kr[d4], qv = qr[d4];
-                    s = __fadd_rn(s, __fmul_rn(qv.x, kv.x));
-                    s = __fadd_rn(s, __fmul_rn(qv.y, kv.y));
-                    s = __fadd_rn(s, __fmul_rn(qv.z, kv.z));
-                    s = __fadd_rn(s, __fmul_rn(qv.w, kv.w));
+                    sacc = __fadd_rn(sacc, __fmul_rn(qv.x, kv.x));
+                    sacc = __fadd_rn(sacc, __fmul_rn(qv.y, kv.y));
+                    sacc = __fadd_rn(sacc, __fmul_rn(qv.z, kv.z));
+                    sacc = __fadd_rn(sacc, __fmul_rn(qv.w, kv.w));
                 }
-                s_sc[w * ATTF_MAX_LEN + p0 + lane] = __fmul_rn(s, a.scale);
+                s_sc[w * ATTF_MAX_LEN + p0 + lane] = __fmul_rn(sacc, a.scale);
             }
         }
     }
+    // position p's v row, this CTA's 32 dims (before the barrier below, the
+    // last point at which the k CTA's shared memory may be read)
+    float *s_vp = s_vrow;  // reused: [32]
+    const float vp_own = tid < 32 ? attf_ld(attf_remote(s_vrow + r * 32 + tid, kp)) : 0.0f;
     attf_cluster_sync();
 
     // ---- C: whole score rows, softmax ----
@@ -620,21 +631,24 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
         s_p[g * ATTF_MAX_LEN + t] = attf_ld(attf_remote(s_sc + g * ATTF_MAX_LEN + t, owner));
     }
     attf_cluster_sync();  // no remote reads after this point: CTAs may finish independently
-    for (int g = 0; g < G; g++) {
-        float *row = s_p + g * ATTF_MAX_LEN;
+    if (tid < 32) s_vp[tid] = vp_own;
+    // all heads at once: warp w serves head w % G (positions strided over the
+    // head's warps); max in any order, then exp(s - max)
+    const int hg = warp % G, hq = warp / G, hn = (ATTF_THREADS / 32 - hg + G - 1) / G;
+    {
+        float *row = s_p + hg * ATTF_MAX_LEN;
         float m = -3.40282347e38f;
-        for (int t = tid; t < len; t += ATTF_THREADS) m = fmaxf(m, row[t]);
+        for (int t = hq * 32 + lane; t < len; t += hn * 32) m = fmaxf(m, row[t]);
         m = warp_max(m);
         if (lane == 0) s_red[warp] = m;
         __syncthreads();
-        m = s_red[0];
-#pragma unroll
-        for (int w = 1; w < ATTF_THREADS / 32; w++) m = fmaxf(m, s_red[w]);
-        for (int t = tid; t < len; t += ATTF_THREADS) row[t] = exp_f(__fsub_rn(row[t], m));
-        __syncthreads();
+        m = s_red[hg];
+        for (int w = hg + G; w < ATTF_THREADS / 32; w += G) m = fmaxf(m, s_red[w]);
+        for (int t = hq * 32 + lane; t < len; t += hn * 32) row[t] = exp_f(__fsub_rn(row[t], m));
     }
-    if (tid < G) {  // one thread per head: the serial sum, loads running ahead of the adds
-        const float *row = s_p + tid * ATTF_MAX_LEN;
+    __syncthreads();
+    if (lane == 0 && warp < G) {  // one thread per head: the serial sum, loads running ahead of the adds
+        const float *row = s_p + warp * ATTF_MAX_LEN;
         float sum = 0.0f;
         int t = 0;
         for (; t + 32 <= len; t += 32) {
@@ -645,7 +659,7 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
             for (int i = 0; i < 32; i++) sum = __fadd_rn(sum, v[i]);
         }
         for (; t < len; t++) sum = __fadd_rn(sum, row[t]);
-        s_red[tid] = sum;
+        s_red[warp] = sum;
     }
     __syncthreads();
     for (int i = tid; i < G * len; i += ATTF_THREADS) {
@@ -658,7 +672,7 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
     const int ntile = (len + ATTF_VT - 1) / ATTF_VT;
     auto load_tile = [&](int k) {
         if (k < ntile) {
-            const int t0 = k * ATTF_VT, nt = min(ATTF_VT, len - t0);
+            const int t0 = k * ATTF_VT, nt = min(ATTF_VT, p - t0);  // row p comes from s_vp
             float *dv = s_v + (k % ATTF_VST) * ATTF_VT * 32;
             for (int idx = tid; idx < nt * 8; idx += ATTF_THREADS) {
                 const int rr = idx >> 3, cc = idx & 7;
@@ -673,14 +687,16 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
     float acc = 0.0f;
     for (int k = 0; k < ntile; k++) {
         cp_async_wait<ATTF_VST - 2>();
-        __syncthreads();  // tile k landed everywhere; tile k-1's buffer is free (and s_p is final)
+        __syncthreads();  // tile k landed everywhere; tile k-1's buffer is free (and s_p, s_vp are final)
         load_tile(k + ATTF_VST - 1);
         if (g < G) {
             const float *v = s_v + (k % ATTF_VST) * ATTF_VT * 32 + dl;
             const float *pr = s_p + g * ATTF_MAX_LEN + k * ATTF_VT;
-            const int nt = min(ATTF_VT, len - k * ATTF_VT);
+            const int t0 = k * ATTF_VT, nt = min(ATTF_VT, len - t0);
+            const int nc = min(nt, p - t0);  // cached rows of this tile
 #pragma unroll 8
-            for (int t = 0; t < nt; t++) acc = __fadd_rn(acc, __fmul_rn(pr[t], v[t * 32]));
+            for (int t = 0; t < nc; t++) acc = __fadd_rn(acc, __fmul_rn(pr[t], v[t * 32]));
+            if (nc < nt) acc = __fadd_rn(acc, __fmul_rn(pr[nc], s_vp[dl]));  // position p, the last
         }
     }
     cp_async_wait<0>();

@@ -224,6 +224,9 @@ struct q35b_engine {
     ncclComm_t comm = nullptr;
     float *part = nullptr;                     // row-parallel partial sums [n][hidden]
     int *am_pair = nullptr, *am_all = nullptr; // (max, index) per run: local / every rank
+    float *am_v = nullptr;                     // split argmax partials [max_batch][AM_SPLIT]
+    int *am_i = nullptr;
+    unsigned *am_cnt = nullptr;                // per row arrival counters (kept at zero between uses)
     uint8_t *xq = nullptr;
     long long xq_ld = 0;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -560,8 +563,8 @@ inline int eng_step_body(q35b_engine *e, int n, int nrun, int max_len, cudaStrea
         rc = launch_k(k_argmax_combine, dim3((unsigned)((nrun + 127) / 128)), dim3(128), 0, st,
                       (const int *)e->am_all, nrun, e->tp_n, e->d_next);
     } else {
-        rc = launch_k(k_argmax, dim3(nrun), dim3(1024), 0, st, (const float *)e->logits, (long long)c.vocab,
-                      c.vocab, e->d_next);
+        rc = launch_k(k_argmax_split, dim3(AM_SPLIT, nrun), dim3(256), 0, st, (const float *)e->logits,
+                      (long long)c.vocab, c.vocab, e->d_next, e->am_v, e->am_i, e->am_cnt);
     }
     e->launches = launch_count() - l0;
     return rc;

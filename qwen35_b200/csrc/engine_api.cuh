@@ -192,6 +192,9 @@ int q35b_engine_finalize(q35b_engine *e) {
         ALLOC(am_pair, 4 * 2 * B);
         ALLOC(am_all, 4 * 2 * B * e->tp_n);
     }
+    ALLOC(am_v, 4 * B * AM_SPLIT);
+    ALLOC(am_i, 4 * B * AM_SPLIT);
+    ALLOC(am_cnt, 4 * B);
     ALLOC(xh, 4 * B * h);
     ALLOC(d_len, 4 * B);
     ALLOC(d_next, 4 * B);
@@ -221,6 +224,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY((int)cudaMemset(e->kpool, 0, 4 * nfull * S * e->kv_slot));
     Q35_TRY((int)cudaMemset(e->vpool, 0, 4 * nfull * S * e->kv_slot));
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 4 * B));
+    Q35_TRY((int)cudaMemset(e->am_cnt, 0, 4 * B));
     // load-time repack: Q6_K projections to 224-byte blocks (16-byte rows for
     // the TMA-streamed GEMV); the caller's buffers stay untouched
     auto repack = [&](Lin &l) -> int {

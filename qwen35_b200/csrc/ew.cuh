@@ -215,6 +215,73 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *x, long long row_s
     }
 }
 
+// The same first-index-of-max over AM_SPLIT CTAs per row: each CTA takes a
+// contiguous slice (float4 loads), writes its (max, index) partial, and the
+// CTA that arrives last on the row's counter combines the partials with the
+// same rule (larger value, then lower index) and resets the counter for the
+// next use.  Partials and counters are engine-owned device memory; counters
+// start at zero.
+constexpr int AM_SPLIT = 32;
+__global__ void __launch_bounds__(256) k_argmax_split(const float *x, long long row_stride, int n, int *out,
+                                                      float *pv, int *pi, unsigned *cnt) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    __shared__ int s_last;
+    const int row = blockIdx.y, part = blockIdx.x, tid = threadIdx.x;
+    const float *xr = x + (long long)row * row_stride;
+    const int per = ((n + AM_SPLIT - 1) / AM_SPLIT + 3) & ~3;
+    const int i0 = min(n, part * per), i1 = min(n, i0 + per);
+    float bv = -INFINITY;
+    int bi = n;
+    const bool vec = (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
+    for (int i = i0 + 4 * tid; i < i1; i += 4 * 256) {
+        if (vec && i + 4 <= i1) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + i);
+            if (v.x > bv) { bv = v.x; bi = i; }
+            if (v.y > bv) { bv = v.y; bi = i + 1; }
+            if (v.z > bv) { bv = v.z; bi = i + 2; }
+            if (v.w > bv) { bv = v.w; bi = i + 3; }
+        } else {
+            for (int k = i; k < min(i + 4, i1); k++)
+                if (xr[k] > bv) { bv = xr[k]; bi = k; }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((tid & 31) == 0) { sv[tid >> 5] = bv; si[tid >> 5] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < 8; w++)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        pv[row * AM_SPLIT + part] = bv;
+        pi[row * AM_SPLIT + part] = bi;
+        __threadfence();
+        s_last = atomicAdd(&cnt[row], 1u) == AM_SPLIT - 1;
+    }
+    __syncthreads();
+    if (s_last && tid < 32) {
+        __threadfence();
+        float v = __ldcg(&pv[row * AM_SPLIT + tid]);
+        int ix = __ldcg(&pi[row * AM_SPLIT + tid]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+            if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+        }
+        if (tid == 0) {
+            out[row] = ix >= n ? 0 : ix;
+            cnt[row] = 0u;
+        }
+    }
+}
+
 // f32 weights x f32 activation: out[t*rows + r] = W[r] . x[t] (warp per row)
 __global__ void k_matvec_f32(const float *w, const float *x, float *out, int rows, int cols) {
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.y;
