@@ -498,13 +498,22 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     const uint64_t wpol = l2_policy_evict_first();
 
     // stage i of this warp -> (matrix, first row, chunk); lane `lane` copies its row
-    auto issue = [&](long long i) {
-        const long long tile = t0 + (i / nck) * tstride;
-        const int c = c_lo + (int)(i % nck);
+    // The producer walks the stages in order with running counters (tile
+    // index, chunk, ring slot): no 64-bit division on the issue path.
+    long long p_tile = t0;
+    int p_c = 0, p_slot = 0;
+    auto issue = [&]() {
+        const long long tile = p_tile;
+        const int c = c_lo + p_c;
+        const int slot = p_slot;
+        if (++p_c == nck) {
+            p_c = 0;
+            p_tile += tstride;
+        }
+        if (++p_slot == a.ns) p_slot = 0;
         const int si = lpr_find_seg(a, tile);
         const LprSeg &sg = a.seg[si];
         const long long r0 = lpr_tile_row0(a, sg, tile);
-        const int slot = (int)(i % a.ns);
         if (lane == 0) {
             // the box is always 32 full rows (rows past the end are zero-filled)
             mbar_arrive_expect_tx(&bar[slot], (uint32_t)(32 * sg.chunk_bytes));
@@ -513,7 +522,7 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
         }
     };
     long long issued = nst < a.ns ? nst : a.ns;
-    for (long long i = 0; i < issued; i++) issue(i);
+    for (long long i = 0; i < issued; i++) issue();
     // the norm weight is constant: staged before the dependency wait
     if (a.prologue == LPR_PRO_NORM) {
         float4 *wd = reinterpret_cast<float4 *>(smem + a.x_off) + (size_t)a.ntok * (a.cols / 4);
@@ -636,6 +645,8 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
     bool failed = false;
     long long waited = 0;
     long long i = 0;
+    int slot = 0;        // ring slot of stage i, and the parity of its fill
+    uint32_t par = 0;
     for (long long ti = 0; ti < my_tiles; ti++) {
         const long long tile = t0 + ti * tstride;
         const LprSeg &sg = a.seg[lpr_find_seg(a, tile)];
@@ -645,9 +656,8 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = 0.0f;
         for (int c = c_lo; c < c_hi; c++, i++) {
-            const int slot = (int)(i % a.ns);
             if (!failed) {
-                if (mbar_wait(&bar[slot], (uint32_t)((i / a.ns) & 1), 111))
+                if (mbar_wait(&bar[slot], par, 111))
                     waited = i + 1;
                 else
                     failed = true;  // keep walking the loop: the named barriers below need every warp
@@ -665,7 +675,14 @@ __global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_const
             // every lane is done reading this slot before the bulk engine refills it
             __syncwarp();
             fence_proxy_async_smem();
-            if (!failed && issued < nst && issued == i + a.ns) issue(issued++);
+            if (!failed && issued < nst && issued == i + a.ns) {
+                issue();  // stage i + ns, into the slot just consumed
+                issued++;
+            }
+            if (++slot == a.ns) {
+                slot = 0;
+                par ^= 1u;
+            }
         }
         if (kw > 1) {
             named_bar_sync(1 + rg, kw * 32);  // the group's terms for this tile are stored
