@@ -36,7 +36,7 @@ constexpr int LPR_MAX_NT = 8;    // tokens per pass
 constexpr size_t LPR_SMEM_MAX = 222 * 1024;
 // per-CTA reserve when several CTAs share an SM's 228 KB: static shared
 // variables plus the 1 KB the system keeps per CTA
-constexpr size_t LPR_CTA_RESERVE = 6 * 1024;
+constexpr size_t LPR_CTA_RESERVE = 5 * 1024;
 
 struct LprSeg {
     const uint8_t *w;
@@ -817,7 +817,10 @@ inline bool lpr_encode(CUtensorMap *m, const void *w, int row_bytes, long long r
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 #ifndef LPR_WARPS_PER_SM
-#define LPR_WARPS_PER_SM 8      // warps per SM aimed at for short matrices (columns split)
+// warps per SM aimed at for short matrices (columns split): the register-
+// limited capacity (65536 registers / (32 lanes x ~128 registers)), so the
+// whole split still runs in one wave
+#define LPR_WARPS_PER_SM 16
 #endif
 
 inline int lpr_tmpl_nt(int nt) { return nt == 1 ? 1 : (nt == 2 ? 2 : (nt <= 4 ? 4 : 8)); }
@@ -878,7 +881,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         occ = (int)((ctas + nsm - 1) / nsm);
     }
     occ = occ < 1 ? 1 : (occ > 8 ? 8 : occ);
-    const int cw = rw * kw;
+    int cw = rw * kw;
     size_t budget = occ == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / occ - LPR_CTA_RESERVE;
     // prologue staging: the f32 rows (+ the norm weight) of one pass
     auto xbytes = [&](int nt) -> size_t {
@@ -899,7 +902,20 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     if (pro && xbytes(group) > LPR_PRO_STAGE_MAX) return -1;  // a fused prologue stages a whole pass
     auto need = [&](int g, int nsmin) { return base_of(g) + (size_t)cw * nsmin * 32 * rs; };
     auto budget_of = [](int o) { return o == 1 ? LPR_SMEM_MAX : (size_t)(228 * 1024) / o - LPR_CTA_RESERVE; };
-    while (occ > 1 && need(group, 2) > budget) budget = budget_of(--occ);
+    // CTAs per SM come down only when the minimum ring no longer fits.  Short
+    // matrices need one stage per warp: keeping every warp tile in the first
+    // wave matters more at decode (weights prefetched before the dependency
+    // wait, compute latency-bound) than a deeper ring.  A tall matrix streams
+    // many chunks per warp and keeps at least two stages in flight.
+    const bool tall = kw == 1 && rw == 4;
+    const int nsmin = tall ? 2 : 1;
+    // a short matrix first narrows its column split (fewer warps, smaller
+    // rings) until the CTAs of one wave fit, then gives up CTAs per SM
+    while (!tall && kw > 1 && need(group, 1) > budget) {
+        kw >>= 1;
+        cw = rw * kw;
+    }
+    while (occ > 1 && need(group, nsmin) > budget) budget = budget_of(--occ);
     while (group > 1 && need(group, 1) > budget) group >>= 1;
     if (need(group, 1) > budget) return -1;
     const long long grid = ctas < (long long)nsm * occ ? ctas : (long long)nsm * occ;
