@@ -55,7 +55,9 @@ __global__ void __launch_bounds__(256) k_rmsnorm_quant(const float *x, const flo
     if (active && !active[t]) return;
     const float *xr = x + (long long)t * cols;
     extern __shared__ __align__(16) float xs[];  // cols floats
-    const float ss = cta_serial_sumsq(xr, cols, xs);
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = xr[i];
+    __syncthreads();
+    const float ss = cta_spec_sumsq(xs, cols);  // the serial order's sum, segments in parallel
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     quantize_row_cta([&](int i) { return __fmul_rn(__fmul_rn(xs[i], scale), w[i]); }, cols, fam,
                      xq + (long long)t * xq_ld);
