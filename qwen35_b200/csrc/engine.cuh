@@ -214,6 +214,7 @@ struct q35b_engine {
     long long conv_slot = 0, state_slot = 0, kv_slot = 0;
     // per-step buffers
     int *d_in = nullptr;  // tokens | slots | pos | run_end (4 * max_batch)
+    int *h_io = nullptr;  // pinned host staging: tokens | slots | pos (as d_in), then next (max_batch)
     int *d_len = nullptr, *d_next = nullptr;
     float *x = nullptr, *qkv = nullptr, *z = nullptr, *ab = nullptr, *gam = nullptr, *gout = nullptr;
     float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;

@@ -53,6 +53,7 @@ int q35b_engine_destroy(q35b_engine *e) {
     e->graphs.clear();
     if (e->comm) nccl_api().comm_destroy(e->comm);
     for (void *p : e->allocs) cudaFree(p);
+    if (e->h_io) cudaFreeHost(e->h_io);
     delete e;
     return 0;
 }
@@ -224,6 +225,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY((int)cudaMemset(e->kpool, 0, 4 * nfull * S * e->kv_slot));
     Q35_TRY((int)cudaMemset(e->vpool, 0, 4 * nfull * S * e->kv_slot));
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 4 * B));
+    Q35_TRY((int)cudaHostAlloc((void **)&e->h_io, 4 * 4 * B, cudaHostAllocDefault));
     Q35_TRY((int)cudaMemset(e->am_cnt, 0, 4 * B));
     // load-time repack: Q6_K projections to 224-byte blocks (16-byte rows for
     // the TMA-streamed GEMV); the caller's buffers stay untouched
@@ -359,12 +361,21 @@ int q35b_engine_step_host(q35b_engine *e, int n, const int *tokens, const int *s
             return (int)cudaErrorInvalidValue;
         max_len = std::max(max_len, pos[i] + 1);
     }
-    Q35_TRY((int)cudaMemcpyAsync(e->d_in, tokens, b, cudaMemcpyHostToDevice, st));
-    Q35_TRY((int)cudaMemcpyAsync(e->d_in + e->max_batch, slots, b, cudaMemcpyHostToDevice, st));
-    Q35_TRY((int)cudaMemcpyAsync(e->d_in + 2 * e->max_batch, pos, b, cudaMemcpyHostToDevice, st));
+    // the inputs go through pinned staging laid out like d_in: one
+    // asynchronous copy in, one out (pageable copies would each be staged
+    // and synchronous); the staging is reused only after this call's sync
+    const long long B = e->max_batch;
+    int *hi = e->h_io, *hn = e->h_io + 3 * B;
+    std::memcpy(hi, tokens, b);
+    std::memcpy(hi + B, slots, b);
+    std::memcpy(hi + 2 * B, pos, b);
+    const size_t span = (size_t)(2 * B + n) * 4;  // tokens .. pos[n-1]
+    Q35_TRY((int)cudaMemcpyAsync(e->d_in, hi, span, cudaMemcpyHostToDevice, st));
     Q35_TRY(engine_run(e, n, max_len, 1, st));
-    Q35_TRY((int)cudaMemcpyAsync(next, e->d_next, b, cudaMemcpyDeviceToHost, st));
-    return (int)cudaStreamSynchronize(st);
+    Q35_TRY((int)cudaMemcpyAsync(hn, e->d_next, b, cudaMemcpyDeviceToHost, st));
+    Q35_TRY((int)cudaStreamSynchronize(st));
+    std::memcpy(next, hn, b);
+    return 0;
 }
 
 int q35b_engine_device_inputs(q35b_engine *e, int **d_tokens, int **d_slots, int **d_pos, int **d_next) {
