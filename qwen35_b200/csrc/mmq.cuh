@@ -933,12 +933,17 @@ inline int mmq_prepare() {
     return 0;
 }
 
-// token tile of k_mmq / k_mmq_kq: the widest of 64 / 32 / 16 that still gives every SM
-// a tile (the fold work per tile scales with the tile's tokens, so narrower
-// tiles spread a short matrix over more SMs) and is not wider than the
-// tokens rounded up to 16; 16 when none qualifies
+// token tile of k_mmq / k_mmq_kq: the widest of 64 / 32 / 16 that still gives
+// half the SMs a tile (the fold work per tile scales with the tile's tokens,
+// so narrower tiles spread a short matrix over more SMs, but every token tile
+// streams the weights again; measured on B200, half the SMs beat all of them
+// and a quarter at batch 32 / 64) and is not wider than the tokens rounded up
+// to 16; 16 when none qualifies
+#ifndef Q35_MMQ_TILE_SM_DIV
+#define Q35_MMQ_TILE_SM_DIV 2
+#endif
 inline int mmq_q32_token_tile(long long row_tiles, int ntok) {
-    const long long sms = gemv_sm_count();
+    const long long sms = gemv_sm_count() / Q35_MMQ_TILE_SM_DIV;
     const int ntok16 = (ntok + 15) / 16 * 16;
     for (int tn : {64, 32})
         if (tn <= ntok16 && row_tiles * ((ntok + tn - 1) / tn) >= sms) return tn;
