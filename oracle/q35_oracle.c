@@ -717,27 +717,27 @@ void q35o_l2norm_qk_scale(float *x, int nk, int kd, int k_offset, float qscale)
     q35o_scale_vec(x, nk * kd, qscale);
 }
 
-float q35o_silu(float x) { return x / (1.0f + expf(-x)); }
-float q35o_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+float q35o_silu(float x) { return x / (1.0f + Q35O_EXPF(-x)); }
+float q35o_sigmoid(float x) { return 1.0f / (1.0f + Q35O_EXPF(-x)); }
 /* elementwise.zig:89-91 (threshold 20) */
-float q35o_softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+float q35o_softplus(float x) { return x > 20.0f ? x : Q35O_LOG1PF(Q35O_EXPF(x)); }
 
 void q35o_silu_vec(float *x, int n)
 {
-    for (int i = 0; i < n; i++) x[i] = x[i] / (1.0f + expf(-x[i]));
+    for (int i = 0; i < n; i++) x[i] = x[i] / (1.0f + Q35O_EXPF(-x[i]));
 }
 
 void q35o_mul_silu(float *out, const float *gate, int n)
 {
     for (int i = 0; i < n; i++) {
         const float g = gate[i];
-        out[i] = out[i] * (g / (1.0f + expf(-g)));
+        out[i] = out[i] * (g / (1.0f + Q35O_EXPF(-g)));
     }
 }
 
 void q35o_mul_sigmoid(float *out, const float *gate, int n)
 {
-    for (int i = 0; i < n; i++) out[i] = out[i] * (1.0f / (1.0f + expf(-gate[i])));
+    for (int i = 0; i < n; i++) out[i] = out[i] * (1.0f / (1.0f + Q35O_EXPF(-gate[i])));
 }
 
 /* elementwise.zig:27 bufSwiglu: g = silu(g) * u */
@@ -753,7 +753,7 @@ void q35o_softmax(float *x, int n)
     for (int i = 0; i < n; i++) mx = x[i] > mx ? x[i] : mx;
     float sum = 0.0f;
     for (int i = 0; i < n; i++) {
-        x[i] = expf(x[i] - mx);
+        x[i] = Q35O_EXPF(x[i] - mx);
         sum += x[i];
     }
     for (int i = 0; i < n; i++) x[i] /= sum;
@@ -812,7 +812,7 @@ void q35o_gdn_gamma(const float *a_raw, float *b_raw, const float *ssm_a,
     for (int h = 0; h < nv; h++) {
         b_raw[h] = q35o_sigmoid(b_raw[h]);
         const float g = ssm_a[h] * q35o_softplus(a_raw[h] + dt_bias[h]);
-        gamma[h] = expf(g);
+        gamma[h] = Q35O_EXPF(g);
     }
 }
 

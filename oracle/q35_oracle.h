@@ -35,8 +35,24 @@
 #ifndef Q35_ORACLE_H
 #define Q35_ORACLE_H
 
+#include <math.h>
 #include <stdint.h>
 #include <stddef.h>
+
+/* exp and log1p.  By default the C library's f32 functions, which the
+ * reference's CPU engine calls.  Built with -DQ35O_CR_EXP: correctly rounded
+ * (evaluated in double, rounded once), the device kernels' arithmetic.  The
+ * two differ in a last ulp now and then, and one such difference can flip an
+ * int8 activation rounding downstream, after which a long decode drifts by a
+ * few percent in both directions alike; the correctly rounded build is the
+ * oracle for comparisons that must stay exact over many positions. */
+#ifdef Q35O_CR_EXP
+#define Q35O_EXPF(x) ((float)exp((double)(x)))
+#define Q35O_LOG1PF(x) ((float)log1p((double)(x)))
+#else
+#define Q35O_EXPF(x) expf(x)
+#define Q35O_LOG1PF(x) log1pf(x)
+#endif
 
 #ifdef __cplusplus
 extern "C" {

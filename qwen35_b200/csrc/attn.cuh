@@ -490,6 +490,7 @@ struct AttfArgs {
     int fam;              // 32: also quantize the output into xq
     uint8_t *xq;
     long long xq_ld;
+    const float2 *rope;   // (cos, sin) per (position, pair), or null: evaluated here
 };
 
 inline size_t attf_smem(int G) {
@@ -557,7 +558,7 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attn_fused(const __grid_consta
     const int p = a.pos[seq], len = p + 1;
     const long long slot = a.slots[seq];
     float rc = 1.0f, rs = 0.0f;
-    if (tid < 32) rope_cs(p, a.base, tid, rc, rs);
+    if (tid < 32) rope_lookup(a.rope, p, a.base, tid, rc, rs);
     pdl_wait();
     const int q_dim = a.heads * ATT_HD, kv_dim = a.kv_heads * ATT_HD;
     const int kp = G % ATTF_CS;  // the CTA doing the k head

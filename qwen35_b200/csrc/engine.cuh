@@ -118,7 +118,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float *x, long long x_
 __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const float *kb, const float *vb, float *q,
                                                       float *gate, const float *qw, const float *kw, int heads,
                                                       int kv_heads, float eps, float base, const int *pos,
-                                                      const int *slots, float *kpool, float *vpool, long long kv_slot) {
+                                                      const int *slots, float *kpool, float *vpool, long long kv_slot,
+                                                      const float2 *rope) {
     pdl_trigger();
     pdl_wait();
     __shared__ float y[256];
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const flo
     const int p = pos[t];
     if (j < 32) {
         float c, s;
-        rope_cs(p, base, j, c, s);
+        rope_lookup(rope, p, base, j, c, s);
         const float a = y[j], b = y[j + 32];
         y[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
         y[j + 32] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
@@ -214,7 +215,8 @@ struct q35b_engine {
     long long conv_slot = 0, state_slot = 0, kv_slot = 0;
     // per-step buffers
     int *d_in = nullptr;  // tokens | slots | pos | run_end (4 * max_batch)
-    int *h_io = nullptr;  // pinned host staging: tokens | slots | pos (as d_in), then next (max_batch)
+    int *h_io = nullptr;
+    float2 *rope_tab = nullptr;  // RoPE (cos, sin) per (position, pair): [max_seq][32]  // pinned host staging: tokens | slots | pos (as d_in), then next (max_batch)
     int *d_len = nullptr, *d_next = nullptr;
     float *x = nullptr, *qkv = nullptr, *z = nullptr, *ab = nullptr, *gam = nullptr, *gout = nullptr;
     float *q = nullptr, *gate = nullptr, *kb = nullptr, *vb = nullptr, *mh = nullptr, *mh1 = nullptr;
@@ -406,6 +408,7 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int nrun, int max_len, 
         f.fam = fo;
         f.xq = e->xq;
         f.xq_ld = e->xq_ld;
+        f.rope = e->rope_tab;
         const int rc = attf_launch(f, n, max_len, st);
         if (rc == 0) {
             if (fo != 32) {
@@ -419,7 +422,7 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int nrun, int max_len, 
     }
     Q35_TRY(launch_k(k_attn_prelude, dim3(heads + kvh, n), dim3(256), 0, st, (const float *)e->qkv,
                      (const float *)e->kb, (const float *)e->vb, e->q, e->gate, W.q_norm, W.k_norm, heads, kvh,
-                     c.rms_eps, c.rope_freq_base, pos, slots, kp, vp, e->kv_slot));
+                     c.rms_eps, c.rope_freq_base, pos, slots, kp, vp, e->kv_slot, (const float2 *)e->rope_tab));
     AttnXArgs a{};
     a.q = e->q;
     a.gate = e->gate;

@@ -1,6 +1,7 @@
 // engine_api.cuh -- q35b_engine_* / q35b_serve: the batched engine's C ABI.
 #pragma once
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <deque>
@@ -217,6 +218,20 @@ int q35b_engine_finalize(q35b_engine *e) {
     long long maxcols = std::max(std::max(h, (long long)c.n_ff), std::max(vdim, q_dim));
     e->xq_ld = ((maxcols / 32 * 34 + maxcols / 256 * 292) + 15) & ~15LL;
     ALLOC(xq, e->xq_ld * B + 64);
+    ALLOC(rope_tab, (size_t)e->max_seq * 32 * sizeof(float2));
+    {
+        // RoPE rotations per (position, pair j): theta = pos * base^(-2j/64)
+        // and its cos / sin in f32 through the C library, the expression and
+        // functions of the reference's CPU engine (elementwise.zig:306-318),
+        // so the device rotates with the CPU's exact values
+        std::vector<float2> rt((size_t)e->max_seq * 32);
+        for (int p = 0; p < e->max_seq; p++)
+            for (int j = 0; j < 32; j++) {
+                const float th = (float)p * powf(c.rope_freq_base, -(float)(2 * j) / 64.0f);
+                rt[(size_t)p * 32 + j] = make_float2(cosf(th), sinf(th));
+            }
+        Q35_TRY((int)cudaMemcpy(e->rope_tab, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
 #undef ALLOC
     Q35_TRY((int)cudaMemset(e->conv_pool, 0, 4 * ngdn * S * e->conv_slot));
     Q35_TRY((int)cudaMemset(e->state_pool, 0, 4 * ngdn * S * e->state_slot));

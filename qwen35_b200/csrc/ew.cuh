@@ -160,6 +160,19 @@ Q35_DEV void rope_cs(int pos, float base, int j, float &c, float &s) {
     c = (float)cos((double)th);
     s = (float)sin((double)th);
 }
+// The rotation of pair j at `pos` from the engine's table when there is one
+// (values computed on the host with the C library's f32 powf / cosf / sinf,
+// the functions the reference's CPU engine calls, so they are the CPU's
+// bits), else evaluated here in double precision (within an ulp of them)
+Q35_DEV void rope_lookup(const float2 *tab, int pos, float base, int j, float &c, float &s) {
+    if (tab) {
+        const float2 v = tab[(long long)pos * 32 + j];
+        c = v.x;
+        s = v.y;
+    } else {
+        rope_cs(pos, base, j, c, s);
+    }
+}
 Q35_DEV void rope_apply(float *hp, int j, float c, float s) {
     const float a = hp[j], b = hp[j + 32];
     hp[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));

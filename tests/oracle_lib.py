@@ -84,10 +84,20 @@ def _declare(lib):
 
 
 _LIB = None
+_LIB_CR = None
 
 
-def load_oracle():
-    global _LIB
+def load_oracle(cr_exp=False):
+    """The oracle library; cr_exp: the build with correctly rounded exp /
+    log1p (the device's arithmetic) instead of the C library's expf / log1pf"""
+    global _LIB, _LIB_CR
+    if cr_exp:
+        if _LIB_CR is None:
+            so = os.path.join(ORACLE_DIR, "_build", "liboracle_crexp.so")
+            if not os.path.exists(so):
+                subprocess.run(["make", "-C", ORACLE_DIR], check=True, capture_output=True)
+            _LIB_CR = _declare(ctypes.CDLL(so))
+        return _LIB_CR
     if _LIB is None:
         if not os.path.exists(ORACLE_SO):
             subprocess.run(["make", "-C", ORACLE_DIR], check=True, capture_output=True)
@@ -160,10 +170,10 @@ def matvec_q(lib, tt, wq, xq, rows, cols, tokens):
     return out
 
 
-def oracle_model(synth, threads=1, max_seq=512):
+def oracle_model(synth, threads=1, max_seq=512, cr_exp=False):
     """CPU oracle engine over the exact packed bytes of a SyntheticModel
     (copied device -> host).  Returns (lib, handle, keepalive)."""
-    lib = load_oracle()
+    lib = load_oracle(cr_exp)
     c = synth.cfg
     cfg = Config(c.n_layers, c.full_attention_interval, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.n_ff,
                  c.vocab, c.rms_eps, c.rope_freq_base, c.gdn_n_heads, c.gdn_num_k_heads, c.gdn_head_dim,
