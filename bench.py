@@ -231,6 +231,46 @@ def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False):
     return ms
 
 
+SERVE_SEQS, SERVE_PROMPT, SERVE_GEN = 64, (64, 512), 32
+
+
+def time_serve(cfg_name, seed, dist, world, rank):
+    """BASELINE config 4 in a bounded sample: continuous batching of
+    SERVE_SEQS sequences (seeded prompt lengths uniform in SERVE_PROMPT,
+    SERVE_GEN greedy tokens each; the config itself has prompts of 64..2048
+    and 256 tokens) through q35b_serve, the sequences sharded over the ranks
+    (every rank serves its share of the fixed set: strong scaling).  Returns
+    (ms, prompt tokens, generated tokens) of this rank."""
+    import numpy as np
+    import torch
+
+    from qwen35_b200 import model as q35
+    cfg = q35.CONFIGS[cfg_name]
+    rng = np.random.default_rng(seed + 41)
+    lens = rng.integers(SERVE_PROMPT[0], SERVE_PROMPT[1] + 1, SERVE_SEQS)
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab, n)] for n in lens]
+    mine = list(range(rank, SERVE_SEQS, world))
+    synth = q35.SyntheticModel(cfg, seed=seed)
+    nslot = len(mine)
+    eng = q35.Engine(synth, n_slots=nslot, max_seq=SERVE_PROMPT[1] + SERVE_GEN + 8, max_batch=256)
+    eng.serve([prompts[mine[0]][:40]], [4], max_batch=nslot)  # warm-up (graphs, attributes)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    out, steps = eng.serve([prompts[i] for i in mine], [SERVE_GEN] * nslot, max_batch=nslot, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    assert all(len(o) == SERVE_GEN for o in out)
+    eng.close()
+    del synth
+    torch.cuda.empty_cache()
+    return ms, int(sum(lens[i] for i in mine)), nslot * SERVE_GEN
+
+
 def time_tp_decode(cfg_name, batch, ctx, steps, warmup, seed, dist, world, rank):
     """batch-`batch` greedy decode at `ctx` context, tensor-parallel over all
     `world` ranks (one engine per rank on its shard, NCCL all-reduce of the
@@ -736,6 +776,14 @@ def main():
                          "context_fill": "synthetic (zero KV / GDN state, positions at 4096)",
                          "steps": ksteps, "ms_per_step": tms / ksteps, "value": 32 * ksteps / (tms * 1e-3),
                          "unit": "tokens/s", "scaling": "strong", "weight_bytes_per_rank": wb})
+        sms, sp, sg = time_serve("4b", args.seed, dist, world, rank)
+        sms = max_over_ranks(sms, dist)
+        variants.append({"model": "qwen3.5-4b-mixed", "workload": "continuous batching (BASELINE config 4, bounded "
+                         "sample): %d sequences, prompts uniform in %d..%d tokens, %d greedy tokens each, sharded "
+                         "by sequence over the ranks" % (SERVE_SEQS, SERVE_PROMPT[0], SERVE_PROMPT[1], SERVE_GEN),
+                         "ms": sms, "value": SERVE_SEQS * SERVE_GEN / (sms * 1e-3), "unit": "generated tokens/s",
+                         "total_tokens_per_s": (sp * world + sg * world) / (sms * 1e-3) if world == 1 else None,
+                         "scaling": "strong"})
         for cfg_name, ntok, chunk in (("0.8b", 512, 256), ("4b", 512, 256)):
             for wy in (False, True):
                 pms = time_prefill(cfg_name, ntok, chunk, args.seed + rank, dist, wy)
