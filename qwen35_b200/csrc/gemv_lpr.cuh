@@ -28,7 +28,10 @@
 
 namespace q35 {
 
-constexpr int LPR_MAX_CW = 8;    // warps per CTA
+constexpr int LPR_MAX_CW = 16;   // warps per CTA (passes of 1-2 tokens; wider passes: 8)
+// warps per CTA a pass of NT tokens may use: the NT = 4 / 8 kernels need
+// more than the 128 registers a 512-thread block leaves each thread
+constexpr int lpr_cw_max(int nt) { return nt <= 2 ? LPR_MAX_CW : LPR_MAX_CW / 2; }
 constexpr int LPR_MAX_NS = 16;   // ring stages per warp
 constexpr int LPR_MAX_NT = 8;    // tokens per pass
 // dynamic shared memory ceiling: the 227 KB opt-in limit less room for the
@@ -475,7 +478,7 @@ Q35_DEV void lpr_chunk(int tt, const uint8_t *rp, const ActView &A, int ntok, in
 // block terms, and after a named barrier warp 0 of the group folds each row's
 // terms in block order (the same rounding sequence).
 template <int NT>
-__global__ void __launch_bounds__(LPR_MAX_CW * 32) k_gemv_lpr(const __grid_constant__ LprArgs a) {
+__global__ void __launch_bounds__(lpr_cw_max(NT) * 32) k_gemv_lpr(const __grid_constant__ LprArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int cw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kw = a.kw, rg = warp / kw, kq = warp - rg * kw, rw = cw / kw;
@@ -875,8 +878,17 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         ctas = (T + 3) / 4;
     } else {
         rw = pair ? 2 : 1;  // pair mode: a CTA takes a gate tile and the matching up tile
-        const long long want = (long long)nsm * LPR_WARPS_PER_SM / T;
-        while (kw * 2 <= want && rw * kw * 2 <= LPR_MAX_CW && kw * 2 <= nchunk) kw *= 2;
+        // the widest column split (any count of warps, at most one chunk
+        // range per warp) whose CTAs still fit in one wave at the register-
+        // limited LPR_WARPS_PER_SM warps per SM
+        const long long tiles_ctas = (T + rw - 1) / rw;
+        const int nt_pass = ntok < LPR_MAX_NT ? ntok : LPR_MAX_NT;
+        const int warps_sm = nt_pass <= 2 ? LPR_WARPS_PER_SM : LPR_WARPS_PER_SM * 3 / 4;  // wider: ~169 registers
+        for (int k = 2; rw * k <= lpr_cw_max(nt_pass) && k <= nchunk; k++) {
+            const int per_sm = warps_sm / (rw * k);
+            if (per_sm < 1 || tiles_ctas > (long long)nsm * per_sm) break;
+            kw = k;
+        }
         ctas = (T + rw - 1) / rw;
         occ = (int)((ctas + nsm - 1) / nsm);
     }
