@@ -61,6 +61,23 @@ class ClockSampler:
                  "-lms", "25"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi takes longer to start than a short timed region lasts:
+        # begin timing only once it is writing samples
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
+        self.skip = 0
+        try:
+            with open(self.path) as f:
+                self.skip = sum(1 for _ in f)  # samples from before the timed region
+        except OSError:
+            pass
 
     def stop(self):
         if self.proc is None:
@@ -72,7 +89,9 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in open(self.path):
+        lines = open(self.path).readlines()
+        lines = lines[getattr(self, "skip", 0):] or lines[-1:]
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
