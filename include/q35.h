@@ -229,7 +229,12 @@ int q35b_quantize_weight(int ttype, const float *d_src, void *d_dst, long long n
 
 /* Matvec over up to 4 matrices sharing one quantized activation, with an
  * optional residual add (mode 1: out += W x).  out_ld = floats between
- * tokens.  All matrices must share the activation family of `ttype[0]`. */
+ * tokens.  All matrices must share the activation family of `ttype[0]`.
+ * Besides the GGML codes, ttype may be Q35B_TT_Q6_K_PADDED: Q6_K blocks
+ * padded from 210 to 224 bytes (zeros after byte 210), the layout the engine
+ * repacks Q6_K weights to at load so that rows are 16-byte multiples for TMA
+ * (the tensor-core path for 16 tokens and more requires it for Q6_K). */
+#define Q35B_TT_Q6_K_PADDED 0x100E
 int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
                            float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq,
                            int cols, int tokens, void *stream);

@@ -532,6 +532,17 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
 // straight from global memory, their loads issued before the weight wait.
 // A round is 4 sub-blocks at TN = 64 (two rounds per block, TMEM halves of
 // 256 columns), all 8 otherwise.
+//
+// Q6_K (224-byte padded blocks, kernels256.c:720-738): 16 groups of 16
+// elements with signed 8-bit scales s_g, isum = sum_g s_g * dot16_g, sumf +=
+// (d*dy)*isum.  The converters fold the scale into the weight, w = s_g * q
+// (q = 6-bit value - 32, so -4064 <= w <= 4096), and split it into two int8
+// digits, w = 64*hi + lo with hi = w >> 6 in [-64, 64] and lo = w & 63; the
+// MMAs of all sub-blocks of a block accumulate the hi digits into one TMEM
+// region H and the lo digits into L, so isum = 64*H + L exactly (|isum| <
+// 2^27) and the fold reads two values per block and token.  A chunk is half
+// a block (4 sub-blocks x 2 digits = the 8 operand tiles of one buffer); the
+// raw stage holds the whole block and is released after its second half.
 // ---------------------------------------------------------------------------
 struct MmqkArgs {
     CUtensorMap wmap[GV_MAX_SEG];   // weights: [rows][row_bytes/8] u64, box 128 rows x one block
@@ -551,7 +562,7 @@ struct MmqkPlan {
     static constexpr int TMEM_COLS = 2 * HALF;
     static constexpr int NB = TN == 64 ? 2 : 3;      // operand / scale buffers
     static constexpr int NS = 3;                     // raw weight stages
-    static constexpr int W_STAGE = MMQ_M * 176;      // one block of 128 rows (Q5_K size)
+    static constexpr int W_STAGE = MMQ_M * 224;      // one block of 128 rows (padded Q6_K size)
     static constexpr int A_BUF = 8 * MMQ_M * 32;
     static constexpr int B_BUF = 8 * TN * 32;
     // per buffer: A | B | sc[128][8] u8 | mn[128][8] u8 | d[128] dmin[128] f32 | dy[TN] f32 | bs[TN][8] i32
@@ -593,6 +604,8 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         if (i < a.nseg && tile >= a.seg[i].tile_begin) sgi = i;
     const MmqSeg &sg = a.seg[sgi];
     const long long r0 = (tile - sg.tile_begin) * MMQ_M;
+    const bool q6 = sg.ttype == TT_Q6_K_P;
+    const int nch = q6 ? 2 * a.nblk : a.nblk;  // chunks: blocks, or half blocks for Q6_K
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -645,7 +658,41 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         int g = 0;
         bool ok = true;
         const uint32_t idesc = mmq_idesc<TN>();
-        for (int c = 0; c < a.nblk && ok; c++) {
+        if (q6) {
+            // chunk c = half c & 1 of block c >> 1; block b into TMEM half b & 1
+            for (int c = 0; c < 2 * a.nblk && ok; c++) {
+                const int p = c % P::NB, b = c >> 1, hb = c & 1, h = b & 1;
+                const uint32_t use = (uint32_t)(c / P::NB);
+                if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 136);
+                if (lane == 0 && ok && hb == 0 && b >= 2)
+                    ok = !s_fail && mbar_wait(&tfree[h], (uint32_t)(((b >> 1) - 1) & 1), 137);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint8_t *buf = sm + p * P::BUF;
+                    for (int kb = 0; kb < 4; kb++) {
+                        const uint64_t bd = umma_desc(buf + P::OB_B + kb * TN * 32, 128, 256);
+                        for (int dg = 0; dg < 2; dg++) {
+                            const uint64_t ad = umma_desc(buf + P::OB_A + (2 * kb + dg) * MMQ_M * 32, 128, 256);
+                            umma_i8(tmem + (uint32_t)(h * P::HALF + dg * TN), ad, bd, idesc, (hb | kb) ? 1u : 0u);
+                        }
+                    }
+                    umma_commit(&opfree[p]);
+                    last_commit = &opfree[p];
+                    last_parity = use & 1u;
+                    ncommit++;
+                    if (hb) {
+                        umma_commit(&tfull[h]);
+                        last_commit = &tfull[h];
+                        last_parity = (uint32_t)((b >> 1) & 1);
+                        ncommit++;
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        for (int c = 0; c < a.nblk && ok && !q6; c++) {
             const int p = c % P::NB;
             const uint32_t use = (uint32_t)(c / P::NB);
             if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 136);
@@ -699,26 +746,32 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         // otherwise sit on the converters' critical path
         // sw: the f32 d bits, then the 16 int16 bsums as 8 words
         uint32_t xw[SPT * 8], nxw[SPT * 8], xsw[9], nxsw[9];
+        // (Q6_K: chunk c is elements 128*(c & 1).. of block c >> 1, and only
+        // the threads with SPT * hq < 4 have sub-blocks in it)
+        const bool xact = !q6 || SPT * hq < 4;
         auto fetch = [&](int c, uint32_t (&w)[SPT * 8], uint32_t (&sw)[9]) {
-            const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)c * 292;
-            const bool on = live && c < a.nblk;
+            const int cb = q6 ? c >> 1 : c;
+            const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)cb * 292;
+            const bool on = live && c < nch && xact;
+            const int xo = 4 + (q6 ? 128 * (c & 1) : 0) + 32 * SPT * hq;
 #pragma unroll
             for (int i = 0; i < SPT * 8; i++)
-                w[i] = on ? reinterpret_cast<const uint32_t *>(src + 4 + 32 * SPT * hq)[i] : 0u;
+                w[i] = on ? reinterpret_cast<const uint32_t *>(src + xo)[i] : 0u;
 #pragma unroll
             for (int i = 0; i < 9; i++) sw[i] = 0u;
-            if (hq == 0 && on) {
+            if (hq == 0 && live && c < nch) {
                 sw[0] = *reinterpret_cast<const uint32_t *>(src);
 #pragma unroll
                 for (int i = 0; i < 8; i++) sw[1 + i] = reinterpret_cast<const uint32_t *>(src + 260)[i];
             }
         };
         fetch(0, xw, xsw);
-        for (int c = 0; c < a.nblk; c++) {
-            const int s = c % P::NS, p = c % P::NB;
+        for (int c = 0; c < nch; c++) {
+            const int cb = q6 ? c >> 1 : c;  // block of this chunk = its raw stage
+            const int s = cb % P::NS, p = c % P::NB;
             const uint32_t use = (uint32_t)(c / P::NB);
             fetch(c + 1, nxw, nxsw);
-            bool ok = !s_fail && mbar_wait(&full[s], (uint32_t)((c / P::NS) & 1), 132);
+            bool ok = !s_fail && mbar_wait(&full[s], (uint32_t)((cb / P::NS) & 1), 132);
             if (ok && use > 0)
                 ok = mbar_wait(&opfree[p], (use - 1) & 1u, 139) && mbar_wait(&sfree[p], (use - 1) & 1u, 140);
             if (!__all_sync(0xffffffffu, ok)) {
@@ -729,12 +782,70 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
             // activations into the B operands and per-token values
 #pragma unroll
             for (int jj = 0; jj < SPT; jj++) {
+                if (!xact) break;
                 uint8_t *dst = buf + P::OB_B + (SPT * hq + jj) * TN * 32;
                 *reinterpret_cast<uint4 *>(dst + umma_off(tk, 0)) =
                     make_uint4(xw[8 * jj], xw[8 * jj + 1], xw[8 * jj + 2], xw[8 * jj + 3]);
                 *reinterpret_cast<uint4 *>(dst + umma_off(tk, 1)) =
                     make_uint4(xw[8 * jj + 4], xw[8 * jj + 5], xw[8 * jj + 6], xw[8 * jj + 7]);
             }
+            if (q6) {
+                if (hq == 0) reinterpret_cast<uint32_t *>(buf + P::OB_DY)[tk] = xsw[0];
+                // weights: row ct, half c & 1 of the raw block -> hi / lo digit tiles
+                const uint8_t *rp = raw + s * P::W_STAGE + ct * sg.chunk_bytes;
+                const int hb = c & 1;
+                uint32_t QL[16], QH[8];
+                const uint4 *v4 = reinterpret_cast<const uint4 *>(rp + 64 * hb);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const uint4 v = v4[i];
+                    QL[4 * i] = v.x;
+                    QL[4 * i + 1] = v.y;
+                    QL[4 * i + 2] = v.z;
+                    QL[4 * i + 3] = v.w;
+                }
+                const uint4 *h4 = reinterpret_cast<const uint4 *>(rp + 128 + 32 * hb);
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const uint4 v = h4[i];
+                    QH[4 * i] = v.x;
+                    QH[4 * i + 1] = v.y;
+                    QH[4 * i + 2] = v.z;
+                    QH[4 * i + 3] = v.w;
+                }
+                const uint2 scw = *reinterpret_cast<const uint2 *>(rp + 192 + 8 * hb);  // scales[8*hb .. +7]
+                reinterpret_cast<float *>(buf + P::OB_D)[ct] = f16_lo(*reinterpret_cast<const uint32_t *>(rp + 208));
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    // sub-block k of the half: element l = ql[64*hb + 32*(k & 1) + l]
+                    // (low nibble for k < 2, high for k >= 2) | qh bits 2k, 2k+1
+                    const int sa = (int)(int8_t)(((2 * k < 4 ? scw.x : scw.y) >> (8 * ((2 * k) & 3))) & 0xFFu);
+                    const int sb = (int)(int8_t)(((2 * k + 1 < 4 ? scw.x : scw.y) >> (8 * ((2 * k + 1) & 3))) & 0xFFu);
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const uint32_t ql = QL[8 * (k & 1) + i];
+                        const uint32_t v = ((k < 2 ? ql : ql >> 4) & 0x0F0F0F0Fu) |
+                                           (((QH[i] >> (2 * k)) & 0x03030303u) << 4);
+                        const int sc = i < 4 ? sa : sb;  // elements 0..15 | 16..31
+                        uint32_t hw = 0u, lw = 0u;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int w = ((int)((v >> (8 * e)) & 0xFFu) - 32) * sc;
+                            hw |= (uint32_t)((w >> 6) & 0xFF) << (8 * e);
+                            lw |= (uint32_t)(w & 63) << (8 * e);
+                        }
+                        hi[i] = hw;
+                        lo[i] = lw;
+                    }
+                    uint8_t *dh = buf + P::OB_A + (2 * k) * MMQ_M * 32;
+                    uint8_t *dl = dh + MMQ_M * 32;
+                    *reinterpret_cast<uint4 *>(dh + umma_off(ct, 0)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4 *>(dh + umma_off(ct, 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    *reinterpret_cast<uint4 *>(dl + umma_off(ct, 0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4 *>(dl + umma_off(ct, 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                }
+            } else {
             if (hq == 0) {
                 reinterpret_cast<uint32_t *>(buf + P::OB_DY)[tk] = xsw[0];
                 int xbs[8];
@@ -794,10 +905,11 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
                 *reinterpret_cast<uint2 *>(buf + P::OB_SC + ct * 8) = make_uint2(scw[0], scw[1]);
                 *reinterpret_cast<uint2 *>(buf + P::OB_MN + ct * 8) = make_uint2(mnw[0], mnw[1]);
             }
+            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&empty[s]);
+                if (!q6 || (c & 1)) mbar_arrive(&empty[s]);  // Q6_K: the stage after the block's second half
                 mbar_arrive(&ready[p]);
             }
 #pragma unroll
@@ -815,7 +927,40 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
 #pragma unroll
         for (int t = 0; t < TH; t++) acc[t] = 0.0f;
         int g = 0;
-        for (int c = 0; c < a.nblk; c++) {
+        for (int c = 0; c < nch && q6; c++) {
+            // Q6_K: after the second half of block b, isum = 64*H + L
+            const int p = c % P::NB, b = c >> 1, h = b & 1;
+            if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(c / P::NB) & 1u, 133))) {
+                s_fail = 1;
+                break;
+            }
+            if (c & 1) {
+                if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&tfull[h], (uint32_t)((b >> 1) & 1), 134))) {
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * P::HALF + fh * TH);
+                uint32_t dH[TH], dL[TH];
+                tmem_ldn<TH>(tbase, dH);
+                tmem_ldn<TH>(tbase + (uint32_t)TN, dL);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tfree[h]);
+                const uint8_t *buf = sm + p * P::BUF;
+                const float dw = reinterpret_cast<const float *>(buf + P::OB_D)[row];
+                const float *dy = reinterpret_cast<const float *>(buf + P::OB_DY) + fh * TH;
+#pragma unroll
+                for (int i = 0; i < TH; i++) {
+                    const int is = 64 * (int)dH[i] + (int)dL[i];
+                    acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, dy[i]), __int2float_rn(is)));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sfree[p]);
+        }
+        for (int c = 0; c < a.nblk && !q6; c++) {
             const int p = c % P::NB;
             if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(c / P::NB) & 1u, 133))) {
                 s_fail = 1;
@@ -950,7 +1095,8 @@ inline int mmq_q32_token_tile(long long row_tiles, int ntok) {
     return 16;
 }
 
-// K-quant (Q4_K / Q5_K) weights x Q8_K activations; -1 when not eligible
+// K-quant (Q4_K / Q5_K / Q6_K in 224-byte blocks) weights x Q8_K activations;
+// -1 when not eligible
 inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
                          long long xq_ld) {
     const long long act_row = (long long)(cols / 256) * 292;
@@ -960,7 +1106,7 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
     long long tiles = 0;
     for (int i = 0; i < nseg; i++) {
         const int tt = segs[i].ttype;
-        if (tt != TT_Q4_K && tt != TT_Q5_K) return -1;
+        if (tt != TT_Q4_K && tt != TT_Q5_K && tt != TT_Q6_K_P) return -1;
         const Geom g = geom_of(tt);
         const int rb = cols / 256 * g.bytes;
         if (rb % 16 || (reinterpret_cast<uintptr_t>(segs[i].w) & 15u)) return -1;
@@ -970,7 +1116,7 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
         s.out_ld = segs[i].out_ld;
         s.ttype = tt;
         s.row_bytes = rb;
-        s.chunk_bytes = g.bytes;  // 144 / 176
+        s.chunk_bytes = g.bytes;  // 144 / 176 / 224
         s.mode = segs[i].mode;
         s.tile_begin = tiles;
         tiles += (s.rows + MMQ_M - 1) / MMQ_M;
@@ -992,8 +1138,8 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
 }
 
 // Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL (Q8_0
-// activation at a 16-byte multiple stride) or Q4_K / Q5_K (Q8_K activation)
-// weights with 16-byte-aligned rows.  Returns -1 (nothing launched) when not
+// activation at a 16-byte multiple stride) or Q4_K / Q5_K / padded Q6_K (Q8_K
+// activation) weights with 16-byte-aligned rows.  Returns -1 (nothing launched) when not
 // eligible.
 inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
                       long long xq_ld) {

@@ -167,6 +167,64 @@ def test_mmq_tensor_core_bit_exact(L, O, name, tokens):
     assert_no_kernel_error(L)
 
 
+Q6_K_PADDED = 0x1000 + 14  # Q6_K in 224-byte blocks (210 bytes + 14 of padding): 16-byte rows
+
+
+def _pad_q6k(wq, rows, cols):
+    nb = cols // 256
+    out = np.zeros((rows, nb, 224), dtype=np.uint8)
+    out[:, :, :210] = wq.reshape(rows, nb, 210)
+    return out.reshape(rows, nb * 224)
+
+
+@pytest.mark.parametrize("tokens", [16, 37, 64, 100])
+def test_mmq_q6_k_bit_exact(L, O, tokens):
+    """>= 16 tokens of Q6_K (224-byte blocks, the engine's load-time layout)
+    go to the tcgen05 MMQ: scales folded into the weights, split into two
+    int8 digits, isum = 64*H + L from two TMEM accumulators per block, the f32
+    step (d*dy)*isum in block order -- bit-exact with the scalar tier"""
+    tt = TT["Q6_K"]
+    for rows, cols in [(300, 1024), (129, 2560), (128, 256), (12800, 256), (19000, 512)]:
+        rng = np.random.default_rng(rows + 7 * tokens)
+        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((tokens, cols)).astype(np.float32)
+        wq = quantize_weight(O, tt, w)
+        xq = quantize_act(O, tt, x)
+        ref = matvec_q(O, tt, wq, xq, rows, cols, tokens)
+        out = torch.full((tokens, rows), float("nan"), dtype=torch.float32, device="cuda")
+        wp = dev(_pad_q6k(wq, rows, cols))
+        ok(L.q35b_mul_mat_vec_multi(1, (ctypes.c_void_p * 1)(wp.data_ptr()), (ctypes.c_int * 1)(Q6_K_PADDED),
+                                    (ctypes.c_longlong * 1)(rows), (ctypes.c_void_p * 1)(out.data_ptr()),
+                                    (ctypes.c_longlong * 1)(rows), (ctypes.c_int * 1)(0), dev(xq).data_ptr(),
+                                    cols, tokens, S))
+        got = host(out)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (rows, cols, tokens)
+    assert_no_kernel_error(L)
+
+
+def test_mmq_q6_k_mixed_segments_residual(L, O):
+    """Q4_K and padded Q6_K matrices in one MMQ launch, the Q6_K one in
+    residual mode"""
+    rng = np.random.default_rng(21)
+    cols, tokens = 512, 40
+    x = rng.standard_normal((tokens, cols)).astype(np.float32)
+    xq = quantize_act(O, TT["Q4_K"], x)
+    wk = quantize_weight(O, TT["Q4_K"], (rng.standard_normal((200, cols)) * 0.02).astype(np.float32))
+    w6 = quantize_weight(O, TT["Q6_K"], (rng.standard_normal((150, cols)) * 0.02).astype(np.float32))
+    base = rng.standard_normal((tokens, 150)).astype(np.float32)
+    ref_k = matvec_q(O, TT["Q4_K"], wk, xq, 200, cols, tokens)
+    ref_6 = (base + matvec_q(O, TT["Q6_K"], w6, xq, 150, cols, tokens)).astype(np.float32)
+    ok_, o6 = torch.zeros((tokens, 200), dtype=torch.float32, device="cuda"), dev(base)
+    ws = [dev(wk), dev(_pad_q6k(w6, 150, cols))]
+    ok(L.q35b_mul_mat_vec_multi(2, (ctypes.c_void_p * 2)(*[w.data_ptr() for w in ws]),
+                                (ctypes.c_int * 2)(TT["Q4_K"], Q6_K_PADDED), (ctypes.c_longlong * 2)(200, 150),
+                                (ctypes.c_void_p * 2)(ok_.data_ptr(), o6.data_ptr()), (ctypes.c_longlong * 2)(200, 150),
+                                (ctypes.c_int * 2)(0, 1), dev(xq).data_ptr(), cols, tokens, S))
+    assert np.array_equal(host(ok_).view(np.uint32), ref_k.view(np.uint32))
+    assert np.array_equal(host(o6).view(np.uint32), ref_6.view(np.uint32))
+    assert_no_kernel_error(L)
+
+
 def test_mmq_multi_and_residual(L, O):
     """the MMQ over mixed IQ4_NL / Q8_0 matrices in one launch, residual mode"""
     rng = np.random.default_rng(14)
