@@ -702,6 +702,88 @@ CONFIG_08B = {"workload": "0.8B-Q8_0 greedy decode, batch 1, 128-token prompt (B
               "l2": "weights 0.80 GB per step > 126 MB L2: no flush needed"}
 
 
+# the batched-decode matrices of the 4B and 27B configs on the tensor-core
+# MMQ, as the engine lays them out (Q6_K repacked to 224-byte blocks):
+# (type, in, out)
+MMQ_SWEEP = (("Q4_K", 5120, 17408), ("Q4_K", 17408, 5120), ("Q6_K_P", 5120, 248320),
+             ("Q5_K", 9216, 2560), ("Q6_K_P", 2560, 248320))
+MMQ_SWEEP_TOKENS = (16, 32, 64)
+
+
+def sweep_mmq(L, hbm, only=None):
+    """k_mmq_kq over MMQ_SWEEP at batch 16 / 32 / 64 through
+    q35b_mul_mat_vec_multi (the engine's entry), weights rotated past 3x L2.
+    only: "TYPE:INxOUT:TOKENS" runs that one case."""
+    import torch
+    from qwen35_b200.lib import GEOM, TT
+    st = torch.cuda.current_stream()
+    s = ctypes.c_void_p(st.cuda_stream)
+    g = torch.Generator(device="cuda")
+    for tname, cols, rows in MMQ_SWEEP:
+        padded = tname == "Q6_K_P"
+        tt = TT["Q6_K"] if padded else TT[tname]
+        code = 0x1000 + tt if padded else tt
+        e, b = GEOM[tt]
+        nblk = rows * cols // e
+        bb = 224 if padded else b
+        mbytes = nblk * bb
+        cases = [t for t in MMQ_SWEEP_TOKENS if only is None or only == f"{tname}:{cols}x{rows}:{t}"]
+        if not cases:
+            continue
+        pitch = (mbytes + 255) // 256 * 256
+        n_rot = max(2, -(-ROTATE_BYTES // mbytes))
+        g.manual_seed(2000 + rows + cols + tt)
+        wf = torch.randn(rows * cols, device="cuda", generator=g)
+        raw = torch.empty(nblk * b, dtype=torch.uint8, device="cuda")
+        assert L.q35b_quantize_weight(tt, wf.data_ptr(), raw.data_ptr(), nblk, s) == 0
+        del wf
+        wq = torch.zeros(n_rot * pitch, dtype=torch.uint8, device="cuda")
+        first = wq[:mbytes].view(nblk, bb)
+        first[:, :b].copy_(raw.view(nblk, b))
+        del raw
+        for i in range(1, n_rot):
+            wq[i * pitch:i * pitch + mbytes].copy_(wq[:mbytes])
+        for ntok in cases:
+            x = torch.randn(ntok * cols, device="cuda", generator=g)
+            xq = torch.empty(ntok * (cols // 256) * 292, dtype=torch.uint8, device="cuda")
+            assert L.q35_launch_quantize_q8_K(x.data_ptr(), xq.data_ptr(), ntok * cols // 256, s) == 0
+            out = torch.empty(ntok * rows, device="cuda")
+            base = wq.data_ptr()
+            T, R, LD, M = (ctypes.c_int * 1)(code), (ctypes.c_longlong * 1)(rows), \
+                (ctypes.c_longlong * 1)(rows), (ctypes.c_int * 1)(0)
+            O = (ctypes.c_void_p * 1)(out.data_ptr())
+
+            def launch(i, ls):
+                W = (ctypes.c_void_p * 1)(base + i * pitch)
+                rc = L.q35b_mul_mat_vec_multi(1, W, T, R, O, LD, M, xq.data_ptr(), cols, ntok,
+                                              ctypes.c_void_p(ls.cuda_stream))
+                assert rc == 0, rc
+
+            # split-K through q35b_mul_mat_vec_multi_ws (the engine passes its
+            # own workspace the same way); used only where the rule allows
+            work = torch.empty((cols // 256) * ntok * rows, dtype=torch.float32, device="cuda")
+
+            def launch_ws(i, ls):
+                W = (ctypes.c_void_p * 1)(base + i * pitch)
+                rc = L.q35b_mul_mat_vec_multi_ws(1, W, T, R, O, LD, M, xq.data_ptr(), cols, ntok,
+                                                 work.data_ptr(), work.numel() * 4, ctypes.c_void_p(ls.cuda_stream))
+                assert rc == 0, rc
+
+            for split, fn in ((False, launch), (True, launch_ws)):
+                ms, reps = _timed_loop(torch, fn, n_rot)
+                algo = mbytes + ntok * (cols // 256) * 292 + ntok * rows * 4
+                line = {"sweep": "mmq", "type": tname, "in": cols, "out": rows, "tokens": ntok,
+                        "kernel": "k_mmq_kq" + (" + k_mmq_term_sum (workspace given)" if split else ""),
+                        "us": ms * 1e3, "weight_bytes": mbytes, "algo_bytes": algo,
+                        "gbs": algo / (ms * 1e-3) / 1e9, "frac_hbm": algo / (ms * 1e-3) / 1e9 / hbm,
+                        "int8_tops": 2.0 * rows * cols * ntok / (ms * 1e-3) / 1e12, "rotated_copies": n_rot,
+                        "reps": reps}
+                print(json.dumps(line), flush=True)
+            del x, xq, out, work
+        del wq, first
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -712,8 +794,10 @@ def main():
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--no-variants", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--sweep", choices=["gemv", "gdn", "all"], default=None,
-                    help="isolated kernel sweeps (BASELINE configs 2 / 3) instead of the decode bench")
+    ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "all"], default=None,
+                    help="isolated kernel sweeps (BASELINE configs 2 / 3; mmq: the 4B / 27B batched-decode "
+                         "matrices) instead of the decode bench")
+    ap.add_argument("--sweep-case", default=None, help="--sweep mmq: one case, TYPE:INxOUT:TOKENS")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -752,6 +836,8 @@ def main():
             sweep_gemv(L, hbm)
         if args.sweep in ("gdn", "all"):
             sweep_gdn(L, hbm)
+        if args.sweep in ("mmq", "all"):
+            sweep_mmq(L, hbm, args.sweep_case)
         return
     extra = 2 * (args.warmup + args.steps) + 8
 

@@ -235,9 +235,22 @@ int q35b_quantize_weight(int ttype, const float *d_src, void *d_dst, long long n
  * repacks Q6_K weights to at load so that rows are 16-byte multiples for TMA
  * (the tensor-core path for 16 tokens and more requires it for Q6_K). */
 #define Q35B_TT_Q6_K_PADDED 0x100E
+
 int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
                            float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq,
                            int cols, int tokens, void *stream);
+
+/* q35b_mul_mat_vec_multi with a caller-provided device workspace (no
+ * reference counterpart).  With one matrix of a 256-element family (Q4_K,
+ * Q5_K, padded Q6_K) at 16 tokens or more whose row tiles (128 rows each)
+ * leave more than half the SMs idle, the tensor-core path splits K over CTAs
+ * when work_bytes >= (cols / 256) * tokens * rows * 4: each block's f32 term
+ * goes to d_work and a second kernel adds them in block order, so results
+ * are identical to the unsplit call.  d_work must not be in use by another
+ * call in flight; work_bytes = 0 behaves as q35b_mul_mat_vec_multi. */
+int q35b_mul_mat_vec_multi_ws(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
+                              float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq,
+                              int cols, int tokens, float *d_work, long long work_bytes, void *stream);
 
 /* Decode attention that allocates nothing (no counterpart in the reference):
  * q35_launch_attn_decode's arguments and result, computed split-KV with the

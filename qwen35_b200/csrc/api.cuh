@@ -519,4 +519,15 @@ int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, c
     return gemv_launch(s, nmat, d_xq, cols, tokens, S(stream));
 }
 
+int q35b_mul_mat_vec_multi_ws(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
+                              float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq,
+                              int cols, int tokens, float *d_work, long long work_bytes, void *stream) {
+    if (nmat < 1 || nmat > GV_MAX_SEG || work_bytes < 0 || (work_bytes > 0 && !d_work) ||
+        (reinterpret_cast<uintptr_t>(d_work) & 3u))
+        return (int)cudaErrorInvalidValue;
+    GemvSegDesc s[GV_MAX_SEG];
+    for (int i = 0; i < nmat; i++) s[i] = GemvSegDesc{d_w[i], d_out[i], rows[i], ttype[i], out_ld[i], mode ? mode[i] : 0};
+    return gemv_launch(s, nmat, d_xq, cols, tokens, S(stream), 0, d_work, (size_t)work_bytes);
+}
+
 }  // extern "C"

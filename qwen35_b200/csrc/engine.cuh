@@ -230,6 +230,8 @@ struct q35b_engine {
     float *part = nullptr;                     // row-parallel partial sums [n][hidden]
     int *am_pair = nullptr, *am_all = nullptr; // (max, index) per run: local / every rank
     float *am_v = nullptr;                     // split argmax partials [max_batch][AM_SPLIT]
+    float *mmq_terms = nullptr;                // split-K terms of the K-quant MMQ (row-parallel projections)
+    size_t mmq_terms_bytes = 0;
     int *am_i = nullptr;
     unsigned *am_cnt = nullptr;                // per row arrival counters (kept at zero between uses)
     uint8_t *xq = nullptr;
@@ -261,7 +263,7 @@ inline bool is_full_layer(const q35b_config &c, int li) {
 // one GEMV launch over up to 4 matrices of the same family sharing `xq`
 inline int eng_gemv(q35b_engine *e, int n, std::initializer_list<GemvSegDesc> segs, const uint8_t *xq, int cols,
                     cudaStream_t st) {
-    return gemv_launch(segs.begin(), (int)segs.size(), xq, cols, n, st, e->xq_ld);
+    return gemv_launch(segs.begin(), (int)segs.size(), xq, cols, n, st, e->xq_ld, e->mmq_terms, e->mmq_terms_bytes);
 }
 
 inline int family_of(const Lin &l) { return geom_of(l.tt).family; }

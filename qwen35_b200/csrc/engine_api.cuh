@@ -197,6 +197,20 @@ int q35b_engine_finalize(q35b_engine *e) {
     ALLOC(am_v, 4 * B * AM_SPLIT);
     ALLOC(am_i, 4 * B * AM_SPLIT);
     ALLOC(am_cnt, 4 * B);
+    {
+        // split-K terms of the K-quant MMQ: the row-parallel projections have
+        // few row tiles (hidden / 128), so at batch >= 16 their K is split
+        // over CTAs; nblk x batch x rows floats for the largest of them
+        size_t tb = 0;
+        for (const LayerW &W : e->L)
+            for (const Lin *l : {&W.o, &W.ssm_out, &W.ffn_down})
+                if (l->w && geom_of(l->tt).family == 256)
+                    tb = std::max(tb, (size_t)(l->cols / 256) * (size_t)B * (size_t)l->rows * 4);
+        if (tb) {
+            ALLOC(mmq_terms, tb);
+            e->mmq_terms_bytes = tb;
+        }
+    }
     ALLOC(xh, 4 * B * h);
     ALLOC(d_len, 4 * B);
     ALLOC(d_next, 4 * B);

@@ -1013,11 +1013,13 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
 // the matrices allow it, else the block-splitting kernel.  Validation
 // (types, families, alignment) is the latter's.
 inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
-                      long long xq_ld);
+                      long long xq_ld, float *terms, size_t terms_bytes);
 
+// terms / terms_bytes: optional scratch that lets the K-quant MMQ split K
+// over CTAs when one matrix has too few row tiles to fill the GPU
 inline int gemv_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
-                       long long xq_ld = 0) {
-    int rc = mmq_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
+                       long long xq_ld = 0, float *terms = nullptr, size_t terms_bytes = 0) {
+    int rc = mmq_launch(segs, nseg, xq, cols, ntok, st, xq_ld, terms, terms_bytes);
     if (rc != -1) return rc;
     rc = gemv_lpr_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
     if (rc != -1) return rc;

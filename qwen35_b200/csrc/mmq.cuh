@@ -552,6 +552,10 @@ struct MmqkArgs {
     const uint8_t *xq;              // Q8_K activation rows
     long long xq_ld;
     int ntok, nblk;                 // tokens, 256-element blocks per row
+    // split-K (one segment): CTA z takes blocks [nblk*z/Z, nblk*(z+1)/Z) and
+    // writes each block's f32 term to terms[(block*ntok + token)*rows + row]
+    // for k_mmq_term_sum to add in block order; null: fold and write here
+    float *terms;
 };
 
 template <int TN>
@@ -605,7 +609,9 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
     const MmqSeg &sg = a.seg[sgi];
     const long long r0 = (tile - sg.tile_begin) * MMQ_M;
     const bool q6 = sg.ttype == TT_Q6_K_P;
-    const int nch = q6 ? 2 * a.nblk : a.nblk;  // chunks: blocks, or half blocks for Q6_K
+    const int kb0 = (int)((long long)a.nblk * blockIdx.z / gridDim.z);
+    const int nb = (int)((long long)a.nblk * (blockIdx.z + 1) / gridDim.z) - kb0;  // blocks of this CTA
+    const int nch = q6 ? 2 * nb : nb;  // chunks: blocks, or half blocks for Q6_K
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -641,7 +647,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         // ---------------- producer ----------------
         if (lane == 0) {
             const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes);
-            for (int c = 0; c < a.nblk; c++) {
+            for (int c = 0; c < nb; c++) {
                 const int s = c % P::NS;
                 if (c >= P::NS &&
                     (s_fail || !mbar_wait(&empty[s], (uint32_t)(((c / P::NS) - 1) & 1), 131))) {
@@ -649,7 +655,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], wbytes);
-                tma_load_2d(raw + s * P::W_STAGE, &a.wmap[sgi], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
+                tma_load_2d(raw + s * P::W_STAGE, &a.wmap[sgi], (kb0 + c) * (sg.chunk_bytes / 8), (int)r0, &full[s]);
                 issued++;
             }
         }
@@ -660,7 +666,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         const uint32_t idesc = mmq_idesc<TN>();
         if (q6) {
             // chunk c = half c & 1 of block c >> 1; block b into TMEM half b & 1
-            for (int c = 0; c < 2 * a.nblk && ok; c++) {
+            for (int c = 0; c < 2 * nb && ok; c++) {
                 const int p = c % P::NB, b = c >> 1, hb = c & 1, h = b & 1;
                 const uint32_t use = (uint32_t)(c / P::NB);
                 if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 136);
@@ -692,7 +698,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
                 __syncwarp();
             }
         }
-        for (int c = 0; c < a.nblk && ok && !q6; c++) {
+        for (int c = 0; c < nb && ok && !q6; c++) {
             const int p = c % P::NB;
             const uint32_t use = (uint32_t)(c / P::NB);
             if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 136);
@@ -750,7 +756,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         // the threads with SPT * hq < 4 have sub-blocks in it)
         const bool xact = !q6 || SPT * hq < 4;
         auto fetch = [&](int c, uint32_t (&w)[SPT * 8], uint32_t (&sw)[9]) {
-            const int cb = q6 ? c >> 1 : c;
+            const int cb = kb0 + (q6 ? c >> 1 : c);
             const uint8_t *src = a.xq + (long long)(t0 + tk) * a.xq_ld + (long long)cb * 292;
             const bool on = live && c < nch && xact;
             const int xo = 4 + (q6 ? 128 * (c & 1) : 0) + 32 * SPT * hq;
@@ -951,16 +957,21 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
                 const uint8_t *buf = sm + p * P::BUF;
                 const float dw = reinterpret_cast<const float *>(buf + P::OB_D)[row];
                 const float *dy = reinterpret_cast<const float *>(buf + P::OB_DY) + fh * TH;
+                const long long tb = (long long)(kb0 + b) * a.ntok + t0 + fh * TH;
 #pragma unroll
                 for (int i = 0; i < TH; i++) {
                     const int is = 64 * (int)dH[i] + (int)dL[i];
-                    acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, dy[i]), __int2float_rn(is)));
+                    const float term = __fmul_rn(__fmul_rn(dw, dy[i]), __int2float_rn(is));
+                    if (!a.terms)
+                        acc[i] = __fadd_rn(acc[i], term);
+                    else if (r0 + row < sg.rows && t0 + fh * TH + i < a.ntok)
+                        a.terms[(tb + i) * sg.rows + r0 + row] = term;
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sfree[p]);
         }
-        for (int c = 0; c < a.nblk && !q6; c++) {
+        for (int c = 0; c < nb && !q6; c++) {
             const int p = c % P::NB;
             if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(c / P::NB) & 1u, 133))) {
                 s_fail = 1;
@@ -1006,20 +1017,24 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
             int mn[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) mn[j] = (int)(((j < 4 ? mnw.x : mnw.y) >> (8 * (j & 3))) & 0xFFu);
+            const long long tb = (long long)(kb0 + c) * a.ntok + t0 + fh * TH;
 #pragma unroll
             for (int i = 0; i < TH; i++) {
                 const int4 b0 = bs[2 * i], b1 = bs[2 * i + 1];
                 const int ms = mn[0] * b0.x + mn[1] * b0.y + mn[2] * b0.z + mn[3] * b0.w + mn[4] * b1.x +
                                mn[5] * b1.y + mn[6] * b1.z + mn[7] * b1.w;
                 const float d = __fmul_rn(dy[i], dw), dm = __fmul_rn(dy[i], dmw);
-                acc[i] = __fadd_rn(acc[i], __fsub_rn(__fmul_rn(d, __int2float_rn(is[i])),
-                                                     __fmul_rn(dm, __int2float_rn(ms))));
+                const float term = __fsub_rn(__fmul_rn(d, __int2float_rn(is[i])), __fmul_rn(dm, __int2float_rn(ms)));
+                if (!a.terms)
+                    acc[i] = __fadd_rn(acc[i], term);
+                else if (r0 + row < sg.rows && t0 + fh * TH + i < a.ntok)
+                    a.terms[(tb + i) * sg.rows + r0 + row] = term;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sfree[p]);
         }
         const long long rr = r0 + row;
-        if (!s_fail && rr < sg.rows) {
+        if (!s_fail && rr < sg.rows && !a.terms) {
             const int nt = min(TN, a.ntok - t0) - fh * TH;
 #pragma unroll
             for (int i = 0; i < TH; i++) {
@@ -1044,6 +1059,24 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P::TMEM_COLS)
                      : "memory");
     }
+}
+
+// split-K epilogue: y[t][r] = sum over blocks b, in block order from 0.0f,
+// of terms[b][t][r] (the fold of k_mmq_kq, operation for operation), then
+// written or added to the output like the unsplit kernel
+__global__ void k_mmq_term_sum(const float *__restrict__ terms, int nblk, int ntok, long long rows, float *out,
+                               long long out_ld, int mode) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)ntok * rows) return;
+    const long long t = i / rows, r = i - t * rows;
+    const long long stride = (long long)ntok * rows;
+    const float *p = terms + i;
+    float acc = 0.0f;
+    for (int b = 0; b < nblk; b++) acc = __fadd_rn(acc, p[b * stride]);
+    float *o = out + t * out_ld + r;
+    *o = mode == GV_ADD ? __fadd_rn(*o, acc) : acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -1095,10 +1128,26 @@ inline int mmq_q32_token_tile(long long row_tiles, int ntok) {
     return 16;
 }
 
+// split-K factor for one segment of `tiles` row tiles: when the widest
+// token tile leaves more than half the SMs idle, K is split over CTAs (at
+// least 2 blocks each, at most 16 splits, one wave) if the caller's term
+// buffer holds nblk x ntok x rows floats; 1 = no split
+inline int mmq_kq_split(long long tiles, long long rows, int ntok, int nblk, size_t terms_bytes, int &tn) {
+    const long long sms = gemv_sm_count();
+    const int wide = ntok > 32 ? 64 : ntok > 16 ? 32 : 16;
+    const long long ctas = tiles * ((ntok + wide - 1) / wide);
+    if (2 * ctas > sms || (size_t)nblk * ntok * rows * sizeof(float) > terms_bytes) return 1;
+    const long long ks = std::min<long long>(std::min<long long>(sms / ctas, nblk / 2), 16);
+    if (ks < 2) return 1;
+    tn = wide;
+    return (int)ks;
+}
+
 // K-quant (Q4_K / Q5_K / Q6_K in 224-byte blocks) weights x Q8_K activations;
-// -1 when not eligible
+// -1 when not eligible.  terms / terms_bytes: the caller's scratch for split-K
+// (null: never split)
 inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
-                         long long xq_ld) {
+                         long long xq_ld, float *terms = nullptr, size_t terms_bytes = 0) {
     const long long act_row = (long long)(cols / 256) * 292;
     const long long ld = xq_ld > 0 ? xq_ld : act_row;
     if ((reinterpret_cast<uintptr_t>(xq) & 3u) || (ld & 3)) return -1;
@@ -1130,11 +1179,21 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
     a.ntok = ntok;
     a.nblk = cols / 256;
     Q35_TRY_RC(mmq_prepare());
-    const int tn = mmq_q32_token_tile(tiles, ntok);
-    const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn));
-    if (tn == 16) return launch_k(k_mmq_kq<16>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<16>::SMEM, st, a);
-    if (tn == 32) return launch_k(k_mmq_kq<32>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<32>::SMEM, st, a);
-    return launch_k(k_mmq_kq<64>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<64>::SMEM, st, a);
+    int tn = mmq_q32_token_tile(tiles, ntok);
+    const int ks = (terms && nseg == 1) ? mmq_kq_split(tiles, a.seg[0].rows, ntok, a.nblk, terms_bytes, tn) : 1;
+    a.terms = ks > 1 ? terms : nullptr;
+    const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn), (unsigned)ks);
+    int rc;
+    if (tn == 16)
+        rc = launch_k(k_mmq_kq<16>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<16>::SMEM, st, a);
+    else if (tn == 32)
+        rc = launch_k(k_mmq_kq<32>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<32>::SMEM, st, a);
+    else
+        rc = launch_k(k_mmq_kq<64>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<64>::SMEM, st, a);
+    if (rc || ks == 1) return rc;
+    const long long n = (long long)ntok * a.seg[0].rows;
+    return launch_k(k_mmq_term_sum, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const float *)terms,
+                    a.nblk, ntok, a.seg[0].rows, a.seg[0].out, a.seg[0].out_ld, a.seg[0].mode);
 }
 
 // Tensor-core path for >= MMQ_MIN_TOK tokens of Q8_0 / IQ4_NL (Q8_0
@@ -1142,9 +1201,10 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
 // activation) weights with 16-byte-aligned rows.  Returns -1 (nothing launched) when not
 // eligible.
 inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int cols, int ntok, cudaStream_t st,
-                      long long xq_ld) {
+                      long long xq_ld, float *terms, size_t terms_bytes) {
     if (ntok < MMQ_MIN_TOK || nseg < 1 || nseg > GV_MAX_SEG || cols <= 0 || cols % 256 != 0) return -1;
-    if (geom_of(segs[0].ttype).family == 256) return mmq_kq_launch(segs, nseg, xq, cols, ntok, st, xq_ld);
+    if (geom_of(segs[0].ttype).family == 256)
+        return mmq_kq_launch(segs, nseg, xq, cols, ntok, st, xq_ld, terms, terms_bytes);
     const long long act_row = (long long)(cols / 32) * 34;
     const long long ld = xq_ld > 0 ? xq_ld : act_row;
     if ((reinterpret_cast<uintptr_t>(xq) & 15u) || (ld & 15)) return -1;

@@ -202,6 +202,39 @@ def test_mmq_q6_k_bit_exact(L, O, tokens):
     assert_no_kernel_error(L)
 
 
+@pytest.mark.parametrize("name", ["Q4_K", "Q5_K", "Q6_K"])
+@pytest.mark.parametrize("tokens", [16, 40, 64])
+def test_mmq_split_k_bit_exact(L, O, name, tokens):
+    """q35b_mul_mat_vec_multi_ws: a matrix with few row tiles splits K over
+    CTAs, each block's f32 term goes to the workspace and a second kernel adds
+    them in block order -- bit-exact with the scalar tier, write and residual
+    mode, and a workspace reused across calls"""
+    tt = TT[name]
+    code = Q6_K_PADDED if name == "Q6_K" else tt
+    for rows, cols, mode in [(300, 4096, 0), (128, 2048, 1), (640, 9216, 1)]:
+        rng = np.random.default_rng(rows + cols + tokens)
+        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((tokens, cols)).astype(np.float32)
+        wq = quantize_weight(O, tt, w)
+        xq = quantize_act(O, tt, x)
+        ref = matvec_q(O, tt, wq, xq, rows, cols, tokens)
+        base = rng.standard_normal((tokens, rows)).astype(np.float32)
+        if mode:
+            ref = (base + ref).astype(np.float32)
+        wd = dev(_pad_q6k(wq, rows, cols) if name == "Q6_K" else wq)
+        work = torch.full(((cols // 256) * tokens * rows,), float("nan"), dtype=torch.float32, device="cuda")
+        for _ in range(2):
+            out = dev(base) if mode else torch.full((tokens, rows), float("nan"), dtype=torch.float32, device="cuda")
+            ok(L.q35b_mul_mat_vec_multi_ws(1, (ctypes.c_void_p * 1)(wd.data_ptr()), (ctypes.c_int * 1)(code),
+                                           (ctypes.c_longlong * 1)(rows), (ctypes.c_void_p * 1)(out.data_ptr()),
+                                           (ctypes.c_longlong * 1)(rows), (ctypes.c_int * 1)(mode),
+                                           dev(xq).data_ptr(), cols, tokens, work.data_ptr(), work.numel() * 4, S))
+            got = host(out)
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens, mode)
+        assert not torch.isnan(work).all().item()  # the split ran and wrote its terms
+    assert_no_kernel_error(L)
+
+
 def test_mmq_q6_k_mixed_segments_residual(L, O):
     """Q4_K and padded Q6_K matrices in one MMQ launch, the Q6_K one in
     residual mode"""
