@@ -558,7 +558,9 @@ struct MmqkArgs {
     float *terms;
 };
 
-template <int TN>
+// Q6: raw stages sized for padded Q6_K (224 bytes per row and block); the
+// Q4_K / Q5_K instances keep 176-byte stages and the larger L1 that leaves
+template <int TN, bool Q6>
 struct MmqkPlan {
     static constexpr int RB = TN == 64 ? 4 : 8;     // sub-blocks per round
     static constexpr int ROUNDS = 8 / RB;
@@ -566,7 +568,7 @@ struct MmqkPlan {
     static constexpr int TMEM_COLS = 2 * HALF;
     static constexpr int NB = TN == 64 ? 2 : 3;      // operand / scale buffers
     static constexpr int NS = 3;                     // raw weight stages
-    static constexpr int W_STAGE = MMQ_M * 224;      // one block of 128 rows (padded Q6_K size)
+    static constexpr int W_STAGE = MMQ_M * (Q6 ? 224 : 176);  // one block of 128 rows
     static constexpr int A_BUF = 8 * MMQ_M * 32;
     static constexpr int B_BUF = 8 * TN * 32;
     // per buffer: A | B | sc[128][8] u8 | mn[128][8] u8 | d[128] dmin[128] f32 | dy[TN] f32 | bs[TN][8] i32
@@ -580,9 +582,9 @@ struct MmqkPlan {
     static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-template <int TN>
+template <int TN, bool Q6>
 __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
-    using P = MmqkPlan<TN>;
+    using P = MmqkPlan<TN, Q6>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *raw = sm + P::OFF_RAW;
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
         if (i < a.nseg && tile >= a.seg[i].tile_begin) sgi = i;
     const MmqSeg &sg = a.seg[sgi];
     const long long r0 = (tile - sg.tile_begin) * MMQ_M;
-    const bool q6 = sg.ttype == TT_Q6_K_P;
+    const bool q6 = Q6 && sg.ttype == TT_Q6_K_P;
     const int kb0 = (int)((long long)a.nblk * blockIdx.z / gridDim.z);
     const int nb = (int)((long long)a.nblk * (blockIdx.z + 1) / gridDim.z) - kb0;  // blocks of this CTA
     const int nch = q6 ? 2 * nb : nb;  // chunks: blocks, or half blocks for Q6_K
@@ -1102,9 +1104,12 @@ inline int mmq_prepare() {
         cudaFuncSetAttribute(k_mmq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<64>::SMEM),
         cudaFuncSetAttribute(k_mmq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<32>::SMEM),
         cudaFuncSetAttribute(k_mmq<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqPlan<16>::SMEM),
-        cudaFuncSetAttribute(k_mmq_kq<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<64>::SMEM),
-        cudaFuncSetAttribute(k_mmq_kq<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<32>::SMEM),
-        cudaFuncSetAttribute(k_mmq_kq<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<16>::SMEM)};
+        cudaFuncSetAttribute(k_mmq_kq<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<64, false>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<32, false>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<16, false>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<64, true>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<32, true>::SMEM),
+        cudaFuncSetAttribute(k_mmq_kq<16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmqkPlan<16, true>::SMEM)};
     for (cudaError_t e : es)
         if (e != cudaSuccess) return (int)e;
     done = 1;
@@ -1183,13 +1188,24 @@ inline int mmq_kq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int 
     const int ks = (terms && nseg == 1) ? mmq_kq_split(tiles, a.seg[0].rows, ntok, a.nblk, terms_bytes, tn) : 1;
     a.terms = ks > 1 ? terms : nullptr;
     const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn), (unsigned)ks);
+    bool q6 = false;
+    for (int i = 0; i < nseg; i++) q6 = q6 || segs[i].ttype == TT_Q6_K_P;
     int rc;
-    if (tn == 16)
-        rc = launch_k(k_mmq_kq<16>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<16>::SMEM, st, a);
-    else if (tn == 32)
-        rc = launch_k(k_mmq_kq<32>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<32>::SMEM, st, a);
-    else
-        rc = launch_k(k_mmq_kq<64>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<64>::SMEM, st, a);
+    if (q6) {
+        if (tn == 16)
+            rc = launch_k(k_mmq_kq<16, true>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<16, true>::SMEM, st, a);
+        else if (tn == 32)
+            rc = launch_k(k_mmq_kq<32, true>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<32, true>::SMEM, st, a);
+        else
+            rc = launch_k(k_mmq_kq<64, true>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<64, true>::SMEM, st, a);
+    } else {
+        if (tn == 16)
+            rc = launch_k(k_mmq_kq<16, false>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<16, false>::SMEM, st, a);
+        else if (tn == 32)
+            rc = launch_k(k_mmq_kq<32, false>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<32, false>::SMEM, st, a);
+        else
+            rc = launch_k(k_mmq_kq<64, false>, grid, dim3(MMQ_THREADS), (size_t)MmqkPlan<64, false>::SMEM, st, a);
+    }
     if (rc || ks == 1) return rc;
     const long long n = (long long)ntok * a.seg[0].rows;
     return launch_k(k_mmq_term_sum, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const float *)terms,
