@@ -27,7 +27,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-PUBLISHED_08B_Q8_0_B1 = 121.84  # reference CUDA backend, RTX 4090 D
+PUBLISHED_08B_Q8_0_B1 = 121.84  # reference CUDA backend, RTX 4090 D (docs/cuda-bench-0.8b.md:17)
 
 
 def peaks():
@@ -129,14 +129,14 @@ def make_prompts(rng, n, length, vocab):
 class Run:
     """one model + engine on this rank, prefilled and ready to decode"""
 
-    def __init__(self, cfg_name, batch, prompt_len, extra_steps, seed):
+    def __init__(self, cfg_name, batch, prompt_len, extra_steps, seed, gen="torch"):
         import numpy as np
         import torch
 
         from qwen35_b200 import model as q35
         self.torch = torch
         self.cfg = q35.CONFIGS[cfg_name]
-        self.synth = q35.SyntheticModel(self.cfg, seed=seed)
+        self.synth = q35.SyntheticModel(self.cfg, seed=seed, gen=gen)
         self.batch = batch
         self.max_seq = prompt_len + extra_steps + 8
         self.eng = q35.Engine(self.synth, n_slots=batch, max_seq=self.max_seq, max_batch=batch)
@@ -375,7 +375,7 @@ def gemv_roofline(run, reps=20):
         assert L.q35_launch_mul_mat_vec(w.data_ptr(), xq.data_ptr(), out.data_ptr(), rows, cols, 1, tt, s) == 0
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-    # NVTX range for the ncu capture of this kernel (profiles/gemv_lpr_lmhead_0p8b_q8_0.md)
+    # NVTX range that an ncu capture of this kernel selects
     torch.cuda.nvtx.range_push("q35_roofline")
     for a, c in ev:
         a.record(run.stream)
@@ -407,96 +407,164 @@ def measured_traffic(kernel):
     return float(e["dram_bytes_per_launch"]) if e else None
 
 
-def cpu_baseline(run, seconds_target=15.0):
-    """the reference's x86 kernels (oracle/_ref, compiled from the reference
-    sources) under the restated engine loop, on this host's cores"""
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
+def host_weights(lib, cfg_name, seed):
+    """The headline model's weights built on the host, with no GPU and no
+    libq35b: the oracle's restatement of q35b_synth_fill (same keys, same
+    f32 bits) and of the reference's Q8_0 weight quantizer
+    (src/quant_dequant.zig:1404-1425; the device encoder gives the same bytes),
+    f32 vectors from the same host generator.  Returns (cfg, {name: (ttype,
+    rows, cols, array)}, checksum), the checksum as SyntheticModel.checksum."""
     import numpy as np
 
+    from qwen35_b200 import configs  # shapes and the host generator only: no torch, no libq35b
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_lib as ol
-    ref = os.path.exists(ol.REF_SO)
-    lib = ol._declare(ctypes.CDLL(ol.REF_SO)) if ref else ol.load_oracle()
-    ol._LIB_SAVE = ol._LIB
-    ol._LIB = lib
-    cores = os.cpu_count() or 1
-    try:
-        lib_m = _cpu_model(lib, run.synth, cores, 64)
-        m, keep = lib_m
-        prompt = run.prompts[0][:4]
-        for i, t in enumerate(prompt):
-            lib.q35o_forward(m, t, i)
-        # calibrate: one step, then size the sample to ~seconds_target
-        out = (ctypes.c_int * 64)()
-        dt1 = lib.q35o_time_decode(m, prompt[-1], len(prompt), 1, out)
-        n = int(max(2, min(48, seconds_target / max(dt1, 1e-3))))
-        dt = lib.q35o_time_decode(m, int(out[0]), len(prompt) + 1, n, out)
-        lib.q35o_model_destroy(m)
-        del keep
-        return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "reference" if ref else "port",
-                "sample": f"{run.cfg.name}, batch 1, {len(prompt)}-token prompt, {n} timed decode tokens "
-                          f"({'reference x86 C kernels' if ref else 'C restatement'} + restated engine loop, "
-                          f"{cores} threads)"}
-    finally:
-        ol._LIB = ol._LIB_SAVE
+    cfg = configs.CONFIGS[cfg_name]
+    plan = configs.tensor_plan(cfg)
+    scratch = np.empty(max(r * c for (_, _, _, r, c, init) in plan if init == "w"), np.float32)
+    tensors, acc = {}, 0
+    for i, (name, role, tt, rows, cols, init) in enumerate(plan):
+        key, n = configs.synth_key(seed, i), rows * cols
+        if init == "w":
+            lib.q35o_synth_fill(key, n, configs.synth_k(0.02), ol.fp(scratch))
+            e, b = ol.GEOM[tt]
+            out = np.empty(n // e * b, np.uint8)
+            lib.q35o_quantize_weight(tt, n, ol.fp(scratch), ol.bp(out))
+        else:
+            out = configs.synth_vector(key, n, init)
+        tensors[name] = (tt, rows, cols, out)
+        raw = out.view(np.uint8).reshape(-1)
+        pad = (-raw.size) % 8
+        if pad:
+            raw = np.concatenate([raw, np.zeros(pad, np.uint8)])
+        acc = (acc + int(raw.view("<u8").sum(dtype=np.uint64))) & (2**64 - 1)
+    return cfg, tensors, acc
 
 
-def _cpu_model(lib, synth, threads, max_seq):
+def _cpu_model(lib, cfg, tensors, threads, max_seq):
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_lib as ol
-    c = synth.cfg
-    cfg = ol.Config(c.n_layers, c.full_attention_interval, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.n_ff,
-                    c.vocab, c.rms_eps, c.rope_freq_base, c.gdn_n_heads, c.gdn_num_k_heads, c.gdn_head_dim,
-                    c.conv_kernel)
-    m = lib.q35o_model_create(ctypes.byref(cfg), max_seq, threads)
-    keep = []
-    for name in synth.tensors:
-        tt, rows, cols, arr = synth.host(name)
-        arr = np.ascontiguousarray(arr)
-        keep.append(arr)
+    c = cfg
+    ccfg = ol.Config(c.n_layers, c.full_attention_interval, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.n_ff,
+                     c.vocab, c.rms_eps, c.rope_freq_base, c.gdn_n_heads, c.gdn_num_k_heads, c.gdn_head_dim,
+                     c.conv_kernel)
+    m = lib.q35o_model_create(ctypes.byref(ccfg), max_seq, threads)
+    for name, (tt, rows, cols, arr) in tensors.items():
+        assert arr.flags["C_CONTIGUOUS"], name
         assert lib.q35o_model_set_tensor(m, name.encode(), tt, arr.ctypes.data, rows, cols) == 0
     assert lib.q35o_model_check(m) == 0
-    return m, keep
+    return m
+
+
+def cpu_model_name():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class CpuDecode:
+    """The reference's CPU path for the headline workload: the reference's own
+    x86 C kernels (oracle/_ref/libq35ref.so, compiled from the reference
+    sources; the C restatement when the reference tree was absent at build
+    time) under the restated engine loop and row-parallel pool
+    (src/pool.zig:468-533), over the same weights and the same 128-token
+    prompt as the GPU arm, prefilled with all host threads."""
+
+    def __init__(self, seed, prompt_len, max_steps):
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import numpy as np
+
+        import oracle_lib as ol
+        self.ref = os.path.exists(ol.REF_SO)
+        self.lib = ol._declare(ctypes.CDLL(ol.REF_SO)) if self.ref else ol.load_oracle()
+        self.cores = os.cpu_count() or 1
+        self.cfg, self.tensors, self.checksum = host_weights(self.lib, "0.8b", seed)
+        self.m = _cpu_model(self.lib, self.cfg, self.tensors, self.cores, prompt_len + max_steps + 8)
+        prompt = make_prompts(np.random.default_rng(seed + 17), 1, prompt_len, self.cfg.vocab)[0]
+        logits = None
+        for i, t in enumerate(prompt):
+            logits = self.lib.q35o_forward(self.m, t, i)
+        self.tok = int(np.argmax(np.ctypeslib.as_array(logits, shape=(self.cfg.vocab,))))
+        self.pos = prompt_len
+        self.prompt_len = prompt_len
+        self.buf = (ctypes.c_int * (max_steps + 1))()
+
+    def decode(self, n, threads=None):
+        """n greedy decode steps; seconds (wall, CPU)"""
+        if n <= 0:
+            return 0.0
+        if threads is not None:
+            self.lib.q35o_model_set_threads(self.m, threads)
+        dt = self.lib.q35o_time_decode(self.m, self.tok, self.pos, n, self.buf)
+        self.tok = int(self.buf[n - 1])
+        self.pos += n
+        return dt
+
+    def kind(self):
+        return "reference" if self.ref else "port"
+
+    def what(self):
+        return ("reference x86 C kernels compiled from the reference sources" if self.ref
+                else "C restatement") + ", restated engine loop"
+
+    def close(self):
+        self.lib.q35o_model_destroy(self.m)
+
+
+def cpu_baseline(args, seconds_target=10.0, seconds_1t=4.0):
+    """bounded sample of the headline workload on this host's cores: all
+    threads, then one thread (decode steps sized to about seconds_target /
+    seconds_1t of CPU time)"""
+    cd = CpuDecode(args.seed, args.prompt, 64 + 48)
+    try:
+        dt1 = cd.decode(1, cd.cores)
+        n = int(max(2, min(64, seconds_target / max(dt1, 1e-3))))
+        dt = cd.decode(n)
+        t1 = cd.decode(1, 1)
+        n1 = int(max(2, min(48, seconds_1t / max(t1, 1e-3))))
+        dt_1 = cd.decode(n1)
+        return {"value": n / dt, "unit": "tokens/s", "cores": cd.cores, "kind": cd.kind(),
+                "value_1_thread": n1 / dt_1, "cpu": cpu_model_name(), "weights_checksum": "%016x" % cd.checksum,
+                "sample": f"0.8B Q8_0 batch 1, the GPU arm's {args.prompt}-token prompt and weights, {n} timed "
+                          f"decode tokens on {cd.cores} threads, then {n1} on 1 thread ({cd.what()})"}
+    finally:
+        cd.close()
 
 
 def run_reference_arm(args, rank):
     """`--impl reference`: the reference's CPU implementation of the path on
-    this box's host cores, same metric and config; rank 0 only."""
+    this box's host cores, on the headline workload (same weights, same
+    128-token prompt, same decode positions as the GPU arm); rank 0 only.
+    Loads no GPU code: the weights are built on the host (host_weights)."""
     if rank != 0:
         return
-    import torch
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    import oracle_lib as ol
-    from qwen35_b200 import model as q35
-    synth = q35.SyntheticModel(q35.CONFIGS["0.8b"], seed=args.seed)
-    ref = os.path.exists(ol.REF_SO)
-    lib = ol._declare(ctypes.CDLL(ol.REF_SO)) if ref else ol.load_oracle()
-    cores = os.cpu_count() or 1
-    m, keep = _cpu_model(lib, synth, cores, 4 + args.warmup + args.steps + 8)
-    import numpy as np
-    rng = np.random.default_rng(args.seed + 17)
-    prompt = [int(t) for t in rng.integers(0, synth.cfg.vocab, 4)]
-    for i, t in enumerate(prompt):
-        lib.q35o_forward(m, t, i)
-    out = (ctypes.c_int * (args.warmup + args.steps + 1))()
-    lib.q35o_time_decode(m, prompt[-1], len(prompt), args.warmup, out)
-    tok = int(out[args.warmup - 1]) if args.warmup > 0 else prompt[-1]
-    dt = lib.q35o_time_decode(m, tok, len(prompt) + args.warmup, args.steps, out)
+    cd = CpuDecode(args.seed, args.prompt, args.warmup + args.steps + 48)
+    cd.decode(args.warmup)
+    dt = cd.decode(args.steps)
     v = args.steps / dt
+    t1 = cd.decode(1, 1)
+    n1 = int(max(2, min(24, 4.0 / max(t1, 1e-3))))
+    v1 = n1 / cd.decode(n1)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32", "data": "synthetic",
         "config": CONFIG_08B,
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference" if ref else "port",
-                         "sample": f"0.8B Q8_0 batch 1, 4-token prompt, {args.steps} timed decode tokens per run "
-                                   f"({'reference x86 C kernels compiled from the reference sources' if ref else 'C restatement'}"
-                                   f", restated engine loop, {cores} threads)"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cd.cores, "kind": cd.kind(),
+                         "value_1_thread": v1, "cpu": cpu_model_name(), "weights_checksum": "%016x" % cd.checksum,
+                         "sample": f"0.8B Q8_0 batch 1, {args.prompt}-token prompt, decode positions "
+                                   f"{args.prompt}..{args.prompt + args.warmup + args.steps - 1} ({args.warmup} "
+                                   f"warm-up + {args.steps} timed on {cd.cores} threads; then {n1} steps on 1 "
+                                   f"thread for value_1_thread), {cd.what()}"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-    lib.q35o_model_destroy(m)
-    del keep, torch
+    cd.close()
 
 
 # ---------------------------------------------------------------------------
@@ -804,6 +872,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # a CPU run: no process group, no CUDA context, no libq35b
+        run_reference_arm(args, rank)
+        return
     import torch
     dist = None
     if world > 1:
@@ -815,12 +887,6 @@ def main():
         dist = tdist
     else:
         torch.cuda.set_device(0)
-
-    if args.impl == "reference":
-        run_reference_arm(args, rank)
-        if dist:
-            dist.destroy_process_group()
-        return
 
     from qwen35_b200.build import build
     if rank == 0:
@@ -842,7 +908,7 @@ def main():
     extra = 2 * (args.warmup + args.steps) + 8
 
     # ---------------- headline: 0.8B Q8_0, batch 1 ----------------
-    run = Run("0.8b", 1, args.prompt, extra, seed=args.seed + rank)
+    run = Run("0.8b", 1, args.prompt, extra, seed=args.seed + rank, gen="synth")
     clocks = ClockSampler(nvsmi_id(local))
     clocks.start()
     ms = time_decode(run, args.steps, args.warmup, dist)
@@ -850,13 +916,14 @@ def main():
     ms = max_over_ranks(ms, dist)
     e2e_ms = max_over_ranks(time_e2e(run, args.steps, args.warmup, dist), dist)
     launches = run.launches_per_step() * args.steps
+    wsum = run.synth.checksum()
     roof = gemv_roofline(run) if rank == 0 else None
     value = world * run.batch * args.steps / (ms * 1e-3)
     e2e_val = world * run.batch * args.steps / (e2e_ms * 1e-3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(run)
+        cpu = cpu_baseline(args)
     run.close()
     del run
     torch.cuda.empty_cache()
@@ -915,6 +982,7 @@ def main():
                          "peak_source": f"{pk_kind} (MEASURED_PEAKS.json hbm_gbs)" if pk_kind == "measured"
                          else "fallback 6.65 TB/s"},
             "cpu_baseline": cpu,
+            "weights_checksum": "%016x" % wsum,
             "variants": variants,
         }
         print(json.dumps(line), flush=True)

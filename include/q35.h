@@ -227,6 +227,16 @@ int q35b_selftest_wait(int limit_ms, void *stream);
  * IQ4_NL / Q4_K / Q5_K / Q6_K are this library's deterministic encoders. */
 int q35b_quantize_weight(int ttype, const float *d_src, void *d_dst, long long nblocks, void *stream);
 
+/* Seeded synthetic values (no counterpart in the reference; its benchmarks
+ * load real checkpoints): d_dst[i] = (h0 + h1 + h2 + h3 - 131070) * k for
+ * i < n, where h0..h3 are the four 16-bit fields of splitmix64's finalizer
+ * applied to key * 0x9E3779B97F4A7C15 + i * 0xD1B54A32D192ED03, and the
+ * product is one f32 multiply.  With k = sigma / 37837.23 the values are
+ * approximately N(0, sigma^2).  A C restatement of the same integer steps
+ * gives the same bits on the host, which lets a CPU run decode the same
+ * weights without touching the GPU. */
+int q35b_synth_fill(unsigned long long key, long long n, float k, float *d_dst, void *stream);
+
 /* Matvec over up to 4 matrices sharing one quantized activation, with an
  * optional residual add (mode 1: out += W x).  out_ld = floats between
  * tokens.  All matrices must share the activation family of `ttype[0]`.

@@ -899,3 +899,23 @@ int q35o_argmax(const float *x, int n)
         if (x[i] > bv) { bv = x[i]; best = i; }
     return best;
 }
+
+/* ====================================================================== */
+/* seeded synthetic values (the library's q35b_synth_fill, restated):      */
+/* splitmix64 finalizer over key*0x9E37.. + i*0xD1B5.., the four 16-bit    */
+/* fields summed (Irwin-Hall n = 4) and centred, one f32 multiply by k.    */
+/* Not part of the reference: it builds benchmark weights on the host.     */
+/* ====================================================================== */
+void q35o_synth_fill(uint64_t key, long long n, float k, float *dst)
+{
+    for (long long i = 0; i < n; i++) {
+        uint64_t z = key * 0x9E3779B97F4A7C15ull + (uint64_t)i * 0xD1B54A32D192ED03ull;
+        z ^= z >> 30;
+        z *= 0xBF58476D1CE4E5B9ull;
+        z ^= z >> 27;
+        z *= 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        const int sum = (int)(z & 0xffff) + (int)((z >> 16) & 0xffff) + (int)((z >> 32) & 0xffff) + (int)(z >> 48);
+        dst[i] = (float)(sum - 131070) * k;
+    }
+}

@@ -92,6 +92,8 @@ void q35o_quantize_weight_q8_0(int n, const float *x, uint8_t *out);
  * qwen35_b200/csrc/wquant.cu).  Any valid encoding is acceptable because
  * parity is defined from the packed bytes onward. */
 void q35o_quantize_weight(int ttype, int n, const float *x, uint8_t *out);
+/* seeded synthetic values, bit-identical to the library's q35b_synth_fill */
+void q35o_synth_fill(uint64_t key, long long n, float k, float *dst);
 
 /* ---- dequantization -------------------------------------------------- */
 void q35o_dequant_row(int ttype, const uint8_t *row, float *out, int cols);
@@ -155,6 +157,8 @@ typedef struct q35o_model q35o_model;
 
 /* `threads` <= 1 runs serially (the parity configuration) */
 q35o_model *q35o_model_create(const q35o_config *cfg, int max_seq, int threads);
+/* replace the row-parallel pool with one of `threads` threads (<= 1: serial) */
+void q35o_model_set_threads(q35o_model *m, int threads);
 void q35o_model_destroy(q35o_model *m);
 /* Register a tensor by its GGUF name.  The pointer is borrowed (caller keeps
  * it alive).  1-D f32 tensors pass ttype 0 and cols = length.  Returns 0 or

@@ -276,6 +276,12 @@ q35o_model *q35o_model_create(const q35o_config *cfg, int max_seq, int threads)
     return m;
 }
 
+void q35o_model_set_threads(q35o_model *m, int threads)
+{
+    pool_destroy(m->pool);
+    m->pool = pool_create(threads);
+}
+
 void q35o_model_destroy(q35o_model *m)
 {
     if (!m) return;

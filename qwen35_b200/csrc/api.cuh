@@ -510,6 +510,14 @@ int q35b_quantize_weight(int ttype, const float *d_src, void *d_dst, long long n
     return (int)cudaGetLastError();
 }
 
+int q35b_synth_fill(unsigned long long key, long long n, float k, float *d_dst, void *stream) {
+    if (n < 0 || (n > 0 && !d_dst)) return (int)cudaErrorInvalidValue;
+    if (n == 0) return 0;
+    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+    k_synth_fill<<<(unsigned)blocks, 256, 0, S(stream)>>>(key, n, k, d_dst);
+    return (int)cudaGetLastError();
+}
+
 int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
                            float *const *d_out, const long long *out_ld, const int *mode, const void *d_xq, int cols,
                            int tokens, void *stream) {

@@ -200,12 +200,14 @@ int q35b_engine_finalize(q35b_engine *e) {
     {
         // split-K terms of the K-quant MMQ: the row-parallel projections have
         // few row tiles (hidden / 128), so at batch >= 16 their K is split
-        // over CTAs; nblk x batch x rows floats for the largest of them
+        // over CTAs (up to MMQ_SPLIT_MAX_TOK tokens); nblk x tokens x rows
+        // floats for the largest of them
+        const size_t Bs = (size_t)std::min<long long>(B, MMQ_SPLIT_MAX_TOK);
         size_t tb = 0;
         for (const LayerW &W : e->L)
             for (const Lin *l : {&W.o, &W.ssm_out, &W.ffn_down})
                 if (l->w && geom_of(l->tt).family == 256)
-                    tb = std::max(tb, (size_t)(l->cols / 256) * (size_t)B * (size_t)l->rows * 4);
+                    tb = std::max(tb, (size_t)(l->cols / 256) * Bs * (size_t)l->rows * 4);
         if (tb) {
             ALLOC(mmq_terms, tb);
             e->mmq_terms_bytes = tb;

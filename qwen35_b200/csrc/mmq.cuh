@@ -1065,11 +1065,15 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant
 
 // split-K epilogue: y[t][r] = sum over blocks b, in block order from 0.0f,
 // of terms[b][t][r] (the fold of k_mmq_kq, operation for operation), then
-// written or added to the output like the unsplit kernel
+// written or added to the output like the unsplit kernel.  When a kernel has
+// recorded an error (k_mmq_kq gives up a bounded wait with code 130 and
+// leaves some term slots unwritten), nothing is written: the output keeps
+// its previous contents, as after a failed unsplit launch.
 __global__ void k_mmq_term_sum(const float *__restrict__ terms, int nblk, int ntok, long long rows, float *out,
                                long long out_ld, int mode) {
     pdl_trigger();
     pdl_wait();
+    if (*(volatile int *)&g_q35_error != 0) return;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)ntok * rows) return;
     const long long t = i / rows, r = i - t * rows;
@@ -1136,8 +1140,15 @@ inline int mmq_q32_token_tile(long long row_tiles, int ntok) {
 // split-K factor for one segment of `tiles` row tiles: when the widest
 // token tile leaves more than half the SMs idle, K is split over CTAs (at
 // least 2 blocks each, at most 16 splits, one wave) if the caller's term
-// buffer holds nblk x ntok x rows floats; 1 = no split
+// buffer holds nblk x ntok x rows floats; 1 = no split.  Only up to
+// MMQ_SPLIT_MAX_TOK tokens: the terms are written and read back once
+// (8 bytes per block, token and row against 144-224 weight bytes per block
+// and row), so past 32 tokens their traffic outweighs the weights' and the
+// split stops paying (measured on B200: 27B ffn_down 101 -> 52 us at 16
+// tokens, 101 -> 83 at 32, none at 64)
+constexpr int MMQ_SPLIT_MAX_TOK = 32;
 inline int mmq_kq_split(long long tiles, long long rows, int ntok, int nblk, size_t terms_bytes, int &tn) {
+    if (ntok > MMQ_SPLIT_MAX_TOK) return 1;
     const long long sms = gemv_sm_count();
     const int wide = ntok > 32 ? 64 : ntok > 16 ? 32 : 16;
     const long long ctas = tiles * ((ntok + wide - 1) / wide);

@@ -4,8 +4,10 @@
 // Who needs it: a host that sizes its weights and KV slots to fill HBM at
 // start-up has no room left for a per-call partials buffer, and a decode loop
 // that is latency-bound cannot afford cudaMalloc / cudaFree (both may
-// synchronize the device).  q35_launch_attn_decode_split2 expects the caller
-// to pass such a buffer; this entry point needs none.
+// synchronize the device).  The reference's split-KV entry points take a
+// caller-allocated partials buffer; this backend's q35_launch_attn_decode_split2
+// ignores that buffer and runs a single split.  This entry point is the
+// split-KV path that needs no buffer from the caller.
 //
 // The scratch is one file-scope array per device, NA_MAX_HEADS query heads x
 // NA_MAX_SPLITS splits of (256 partial sums + max + sum) floats, 4.2 MB.

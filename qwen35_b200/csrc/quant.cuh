@@ -324,4 +324,30 @@ __global__ void k_quantize_weight(int tt, const float *__restrict__ x, uint8_t *
     }
 }
 
+// Seeded synthetic values for benchmark / test weights, identical on the CPU
+// (the same integer steps in C or numpy): element i of stream `key` hashes
+// the counter (splitmix64's finalizer, Steele, Lea & Flood 2014) and sums
+// the four 16-bit fields of the hash (Irwin-Hall with n = 4: mean 131070,
+// standard deviation 37837.23), so the centred sum is an exact integer and
+// its one rounded product with k (scale / 37837.23, formed by the caller)
+// gives the same f32 bits on any IEEE machine.
+Q35_DEV uint64_t synth_hash(uint64_t key, uint64_t i) {
+    uint64_t z = key * 0x9E3779B97F4A7C15ull + i * 0xD1B54A32D192ED03ull;
+    z ^= z >> 30;
+    z *= 0xBF58476D1CE4E5B9ull;
+    z ^= z >> 27;
+    z *= 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return z;
+}
+
+__global__ void k_synth_fill(uint64_t key, long long n, float k, float *__restrict__ y) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint64_t z = synth_hash(key, (uint64_t)i);
+        const int s = (int)(z & 0xffff) + (int)((z >> 16) & 0xffff) + (int)((z >> 32) & 0xffff) + (int)(z >> 48);
+        y[i] = __fmul_rn((float)(s - 131070), k);
+    }
+}
+
 }  // namespace q35

@@ -1,130 +1,19 @@
-"""Qwen3.5 hybrid model configs, seeded synthetic weights and the batched
-engine, on top of libq35b's C ABI.
+"""Seeded synthetic weights and the batched engine, on top of libq35b's C
+ABI (configs and the tensor plan: `configs.py`).
 
-Tensor names and shapes follow the GGUF layout the reference engine loads
-(src/engine.zig:826-993): linear weights are [rows = out, cols = in],
-`blk.N.ssm_conv1d.weight` is [conv_dim, 4] f32, norms are pre-folded (1 + w).
 Weights are generated on the device from a seeded generator and packed by
 the library's device encoders (`q35b_quantize_weight`): Q8_0 is the
 reference's own weight quantizer, IQ4_NL / K-quants are deterministic
 encoders of this library (the reference has none).
 """
 import ctypes
-import dataclasses
 
+import numpy as np
 import torch
 
 from . import lib as _lib
+from .configs import CONFIGS, ModelConfig, synth_k, synth_key, synth_vector, tensor_plan  # noqa: F401
 from .lib import GEOM, TT, check
-
-
-@dataclasses.dataclass(frozen=True)
-class ModelConfig:
-    name: str
-    n_layers: int
-    hidden: int
-    n_ff: int
-    vocab: int
-    n_heads: int
-    n_kv_heads: int
-    gdn_n_heads: int
-    gdn_num_k_heads: int
-    head_dim: int = 256
-    gdn_head_dim: int = 128
-    full_attention_interval: int = 4
-    rms_eps: float = 1e-6
-    rope_freq_base: float = 1e7
-    conv_kernel: int = 4
-    # weight type per role
-    quant: tuple = ()
-
-    def qtype(self, role):
-        d = dict(self.quant)
-        return TT[d.get(role, d.get("bulk", "Q8_0"))]
-
-    def is_full(self, li):
-        f = self.full_attention_interval
-        return f > 0 and li % f == f - 1
-
-    @property
-    def conv_dim(self):
-        return 2 * self.gdn_num_k_heads * self.gdn_head_dim + self.gdn_n_heads * self.gdn_head_dim
-
-    def c_config(self):
-        return _lib.Config(self.n_layers, self.full_attention_interval, self.hidden, self.n_heads, self.n_kv_heads,
-                           self.head_dim, self.n_ff, self.vocab, self.rms_eps, self.rope_freq_base,
-                           self.gdn_n_heads, self.gdn_num_k_heads, self.gdn_head_dim, self.conv_kernel)
-
-
-# 0.8B (all Q8_0), 4B (mixed), 27B (Q4_K, Q6_K output)
-CONFIGS = {
-    "0.8b": ModelConfig("qwen3.5-0.8b-q8_0", 24, 1024, 3584, 248320, 8, 2, 16, 16,
-                        quant=(("bulk", "Q8_0"),)),
-    "4b": ModelConfig("qwen3.5-4b-mixed", 32, 2560, 9216, 248320, 16, 4, 32, 16,
-                      quant=(("bulk", "IQ4_NL"), ("ffn_down", "Q5_K"), ("ssm_alpha", "Q8_0"),
-                             ("ssm_beta", "Q8_0"), ("output", "Q6_K"))),
-    "27b": ModelConfig("qwen3.5-27b-q4_k", 64, 5120, 17408, 248320, 24, 4, 48, 16,
-                       quant=(("bulk", "Q4_K"), ("output", "Q6_K"))),
-    # small shapes for parity tests (same head sizes, fewer/narrower layers)
-    "tiny": ModelConfig("tiny-q8_0", 4, 256, 512, 2048, 2, 1, 2, 2, quant=(("bulk", "Q8_0"),)),
-    "tiny-mixed": ModelConfig("tiny-mixed", 8, 512, 1024, 4096, 4, 1, 4, 2,
-                              quant=(("bulk", "IQ4_NL"), ("ffn_down", "Q5_K"), ("ssm_alpha", "Q8_0"),
-                                     ("ssm_beta", "Q8_0"), ("output", "Q6_K"), ("attn_output", "Q4_K"))),
-    # tensor-parallel parity cases: every head count splits two ways
-    "tiny-tp": ModelConfig("tiny-tp-q8_0", 4, 256, 1024, 2048, 4, 2, 4, 2, quant=(("bulk", "Q8_0"),)),
-    "tiny-tp-mixed": ModelConfig("tiny-tp-mixed", 4, 512, 1024, 4096, 4, 2, 8, 4,
-                                 quant=(("bulk", "IQ4_NL"), ("ffn_down", "Q5_K"), ("ssm_alpha", "Q8_0"),
-                                        ("ssm_beta", "Q8_0"), ("output", "Q6_K"), ("attn_output", "Q4_K"))),
-    # the 27B TP-8 shapes in small: one kv head replicated on both ranks, an
-    # odd count of ffn blocks (3 -> 2 + 1), Q4_K bulk with a Q6_K lm_head
-    # (GDN value heads in pairs: ssm_out columns in whole 256-blocks)
-    "tiny-tp-rep": ModelConfig("tiny-tp-rep", 4, 512, 768, 4096, 4, 1, 8, 4,
-                               quant=(("bulk", "Q4_K"), ("output", "Q6_K"))),
-}
-
-
-def tensor_plan(cfg):
-    """[(name, role, ttype, rows, cols, init)] in GGUF naming.  init is one of
-    'w' (N(0, 0.02)), 'norm' (1 + N(0, 0.02)), 'conv', 'ssm_a', 'dt'."""
-    h, nv, kd = cfg.hidden, cfg.gdn_n_heads, cfg.gdn_head_dim
-    q_dim, kv_dim = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
-    P = []
-
-    def lin(name, role, rows, cols):
-        P.append((name, role, cfg.qtype(role), rows, cols, "w"))
-
-    def vec(name, n, init):
-        P.append((name, init, TT["F32"], 1, n, init))
-
-    lin("token_embd.weight", "token_embd", cfg.vocab, h)
-    if "output" in dict(cfg.quant):
-        lin("output.weight", "output", cfg.vocab, h)
-    vec("output_norm.weight", h, "norm")
-    for li in range(cfg.n_layers):
-        b = f"blk.{li}."
-        vec(b + "attn_norm.weight", h, "norm")
-        vec(b + "post_attention_norm.weight", h, "norm")
-        if cfg.is_full(li):
-            lin(b + "attn_q.weight", "attn_q", 2 * q_dim, h)
-            lin(b + "attn_k.weight", "attn_k", kv_dim, h)
-            lin(b + "attn_v.weight", "attn_v", kv_dim, h)
-            lin(b + "attn_output.weight", "attn_output", h, q_dim)
-            vec(b + "attn_q_norm.weight", cfg.head_dim, "norm")
-            vec(b + "attn_k_norm.weight", cfg.head_dim, "norm")
-        else:
-            lin(b + "attn_qkv.weight", "attn_qkv", cfg.conv_dim, h)
-            lin(b + "attn_gate.weight", "attn_gate", nv * kd, h)
-            lin(b + "ssm_alpha.weight", "ssm_alpha", nv, h)
-            lin(b + "ssm_beta.weight", "ssm_beta", nv, h)
-            lin(b + "ssm_out.weight", "ssm_out", h, nv * kd)
-            vec(b + "ssm_conv1d.weight", cfg.conv_dim * 4, "conv")
-            vec(b + "ssm_dt.bias", nv, "dt")
-            vec(b + "ssm_a", nv, "ssm_a")
-            vec(b + "ssm_norm.weight", kd, "norm")
-        lin(b + "ffn_gate.weight", "ffn_gate", cfg.n_ff, h)
-        lin(b + "ffn_up.weight", "ffn_up", cfg.n_ff, h)
-        lin(b + "ffn_down.weight", "ffn_down", h, cfg.n_ff)
-    return P
 
 
 def packed_bytes(tt, rows, cols):
@@ -140,13 +29,22 @@ def _stream(stream=None):
 
 
 class SyntheticModel:
-    """Seeded synthetic weights, generated and packed on the GPU."""
+    """Seeded synthetic weights, generated and packed on the GPU.
 
-    def __init__(self, cfg, seed=0, device="cuda"):
+    gen="torch": torch's device generator (the test models).  gen="synth":
+    the library's q35b_synth_fill for the linear weights and the host
+    generator of `configs.synth_vector` for the f32 vectors; a CPU process
+    rebuilds exactly these values from `configs` alone (the benchmark's
+    reference arm decodes the same bytes)."""
+
+    def __init__(self, cfg, seed=0, device="cuda", gen="torch"):
         self.cfg = cfg
         self.device = torch.device(device)
         self.tensors = {}  # name -> (ttype, rows, cols, uint8/float32 device tensor)
         L = _lib.load()
+        if gen == "synth":
+            self._init_synth(L, seed)
+            return
         gen = torch.Generator(device=self.device)
         for i, (name, role, tt, rows, cols, init) in enumerate(tensor_plan(cfg)):
             gen.manual_seed(seed * 1000003 + i)
@@ -169,6 +67,34 @@ class SyntheticModel:
                 raise ValueError(init)
             self.tensors[name] = (tt, rows, cols, out)
         torch.cuda.synchronize(self.device)
+
+    def _init_synth(self, L, seed):
+        for i, (name, role, tt, rows, cols, init) in enumerate(tensor_plan(self.cfg)):
+            n = rows * cols
+            key = synth_key(seed, i)
+            if init == "w":
+                f = torch.empty(n, dtype=torch.float32, device=self.device)
+                check(L.q35b_synth_fill(key, n, synth_k(0.02), f.data_ptr(), _stream()), name)
+                e, b = GEOM[tt]
+                out = torch.empty(n // e * b, dtype=torch.uint8, device=self.device)
+                check(L.q35b_quantize_weight(tt, f.data_ptr(), out.data_ptr(), n // e, _stream()), name)
+                del f
+            else:
+                out = torch.from_numpy(synth_vector(key, n, init)).to(self.device)
+            self.tensors[name] = (tt, rows, cols, out)
+        torch.cuda.synchronize(self.device)
+
+    def checksum(self):
+        """sum of the packed bytes as little-endian 64-bit words, mod 2^64,
+        over every tensor in plan order (padded to 8 bytes with zeros)"""
+        acc = 0
+        for name in self.tensors:
+            t = self.tensors[name][3].reshape(-1).view(torch.uint8)
+            pad = (-t.numel()) % 8
+            if pad:
+                t = torch.cat([t, torch.zeros(pad, dtype=torch.uint8, device=t.device)])
+            acc = (acc + int(t.view(torch.int64).sum().item())) & (2**64 - 1)
+        return acc
 
     def weight_bytes(self):
         return sum(t.numel() * t.element_size() for (_, _, _, t) in self.tensors.values())

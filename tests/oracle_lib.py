@@ -40,6 +40,7 @@ def _declare(lib):
         "q35o_quantize_q8_K": (V, [I, f32p, u8p]),
         "q35o_quantize_act": (V, [I, I, f32p, u8p]),
         "q35o_quantize_weight": (V, [I, I, f32p, u8p]),
+        "q35o_synth_fill": (V, [ctypes.c_uint64, ctypes.c_longlong, F, f32p]),
         "q35o_dequant_row": (V, [I, u8p, f32p, I]),
         "q35o_vec_dot": (F, [I, I, u8p, u8p]),
         "q35o_block_isum": (ctypes.c_int32, [I, u8p, u8p]),
@@ -67,6 +68,7 @@ def _declare(lib):
         "q35o_argmax": (I, [f32p, I]),
         "q35o_model_create": (ctypes.c_void_p, [ctypes.POINTER(Config), I, I]),
         "q35o_model_destroy": (V, [ctypes.c_void_p]),
+        "q35o_model_set_threads": (V, [ctypes.c_void_p, I]),
         "q35o_model_set_tensor": (I, [ctypes.c_void_p, ctypes.c_char_p, I, ctypes.c_void_p, I, I]),
         "q35o_model_check": (I, [ctypes.c_void_p]),
         "q35o_model_reset": (V, [ctypes.c_void_p]),

@@ -92,6 +92,58 @@ def test_engine_0p8b_32_greedy_tokens(q35):
     assert tg == tc
 
 
+def test_engine_4b_mixed_32_greedy_tokens(q35):
+    """BASELINE parity bar on the 4B-class mixed-precision config at its full
+    shape (IQ4_NL bulk, Q5_K ffn_down, Q8_0 ssm_alpha / beta, Q6_K lm_head
+    248320 x 2560, 32 GDN value heads over 16 k heads, 16 q / 4 kv attention
+    heads): 32 identical greedy tokens, per-layer outputs within 1e-3
+    relative L2"""
+    tg, tc, wl, wlay = _run_parity(q35, "4b", prompt_len=8, n_gen=32, seed=7)
+    assert wl < 1e-3 and wlay < 1e-3, (wl, wlay)
+    assert tg == tc
+
+
+def test_engine_context_past_4096(q35):
+    """A 4100-token prompt prefilled through q35b_engine_prefill (runs of up
+    to 256 tokens: tensor-core projections, the exact chunked GDN
+    recurrence, causal attention over the run), then 12 decode steps to
+    position 4111 (max_seq 4128, past the reference's 4096 default):
+    every decode step's logits bit for bit against the oracle stepping the
+    same 4112 tokens one at a time (the build with correctly rounded exp /
+    log1p, the device's arithmetic), and the same greedy tokens"""
+    import ctypes
+    cfg = q35.CONFIGS["tiny-mixed"]
+    synth = q35.SyntheticModel(cfg, seed=9)
+    n_prompt, n_gen, max_seq = 4100, 12, 4128
+    eng = q35.Engine(synth, n_slots=1, max_seq=max_seq, max_batch=256)
+    O, m, keep = oracle_model(synth, threads=min(16, os.cpu_count() or 1), max_seq=max_seq, cr_exp=True)
+    prompt = [int(t) for t in np.random.default_rng(9).integers(0, cfg.vocab, n_prompt)]
+    eng.reset_slot(0)
+    tok_g = eng.prefill(0, prompt)
+    lc = None
+    for pos, t in enumerate(prompt):
+        lc = O.q35o_forward(m, t, pos)
+    tok_c = int(np.argmax(np.ctypeslib.as_array(lc, shape=(cfg.vocab,))))
+    assert tok_g == tok_c
+    d_tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d_slot = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d_pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d_next = torch.zeros(1, dtype=torch.int32, device="cuda")
+    logits = torch.zeros((1, cfg.vocab), dtype=torch.float32, device="cuda")
+    for pos in range(n_prompt, n_prompt + n_gen):
+        d_tok.fill_(tok_g)
+        d_pos.fill_(pos)
+        eng.step(d_tok, d_slot, d_pos, d_next, logits, use_graph=True)
+        lg = logits[0].cpu().numpy()
+        lc = oracle_forward(O, m, tok_c, pos, cfg.vocab)
+        assert np.array_equal(lg.view(np.uint32), lc.view(np.uint32)), pos
+        tok_g, tok_c = int(d_next.item()), int(np.argmax(lc))
+        assert tok_g == tok_c
+    O.q35o_model_destroy(m)
+    eng.close()
+    del ctypes
+
+
 def test_engine_long_context_decode(q35):
     """Decode one token at a time to 600 positions: the fused decode attention
     takes 8 x 32 positions per pass of its cluster (so positions past 256 take

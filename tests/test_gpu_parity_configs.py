@@ -1,0 +1,198 @@
+"""Parity at the benchmark's own sizes, on the GPU, against the CPU oracle.
+
+* the quantized matvec over BASELINE config 2 -- every hot type on the
+  1024 x 6144 and 1024 x 248320 matrices at 1, 8, 64 and 512 tokens, through
+  the drop-in launcher (and the engine's padded Q6_K layout): the GPU computes
+  every row, the oracle a sample of rows (both ends, every 128-row tile edge
+  it lands on, random rows), compared bit for bit;
+* the chunked GDN prefill at config 3's lengths (2048 and 8192 tokens, and a
+  ragged 4099) against the oracle's per-token recurrence: the exact chunk
+  kernel bit for bit, the WY form within 1e-4 relative L2;
+* q / gate deinterleave, and the seeded synthetic generator that lets a CPU
+  process rebuild the benchmark's weights.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle_lib import GEOM, TT, bp, fp, load_oracle, matvec_q, quantize_act
+
+pytestmark = pytest.mark.gpu
+
+S = None
+
+
+@pytest.fixture(scope="module")
+def L():
+    from qwen35_b200 import lib
+    return lib.load()
+
+
+@pytest.fixture(scope="module")
+def O():
+    return load_oracle()
+
+
+def ok(rc):
+    assert rc == 0, f"cuda error {rc}"
+
+
+def no_kernel_error(L):
+    code = ctypes.c_int(-1)
+    ok(L.q35b_get_error(ctypes.byref(code)))
+    assert code.value == 0
+
+
+def test_synth_fill_matches_host(L, O):
+    """q35b_synth_fill == the oracle's C restatement == the numpy statement,
+    bit for bit (the benchmark's CPU arm rebuilds the GPU arm's weights)"""
+    from qwen35_b200 import configs
+    for key, sigma, n in ((0, 0.02, 1 << 20), (2**64 - 7, 0.5, 100003), (123456789, 1.0, 4097)):
+        k = configs.synth_k(sigma)
+        d = torch.empty(n, dtype=torch.float32, device="cuda")
+        ok(L.q35b_synth_fill(key, n, k, d.data_ptr(), S))
+        got = d.cpu().numpy()
+        ref = np.empty(n, np.float32)
+        O.q35o_synth_fill(key, n, k, fp(ref))
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        assert np.array_equal(configs.synth_normal_np(key, n, sigma).view(np.uint32), ref.view(np.uint32))
+    assert abs(float(got.std()) - 1.0) < 0.05
+
+
+CONFIG2_TYPES = ["Q8_0", "IQ4_NL", "Q4_K", "Q5_K", "Q6_K"]
+CONFIG2_SHAPES = [(1024, 6144), (1024, 248320)]  # [in, out]
+Q6_K_PADDED = 0x1000 + 14
+
+
+def _device_weights(L, tt, rows, cols, key):
+    """config-2 weights: N(0, 1) f32 from q35b_synth_fill, packed by the
+    device encoder (bit-identical with the oracle's, test_weight_encoder_bit_exact)"""
+    from qwen35_b200 import configs
+    e, b = GEOM[tt]
+    n = rows * cols
+    f = torch.empty(n, dtype=torch.float32, device="cuda")
+    ok(L.q35b_synth_fill(key, n, configs.synth_k(1.0), f.data_ptr(), S))
+    wq = torch.empty(n // e * b, dtype=torch.uint8, device="cuda")
+    ok(L.q35b_quantize_weight(tt, f.data_ptr(), wq.data_ptr(), n // e, S))
+    del f
+    return wq.view(rows, cols // e * b)
+
+
+def _sample_rows(rows, rng):
+    idx = set(range(min(rows, 96))) | set(range(max(0, rows - 96), rows))
+    for t in range(128, rows, 128 * max(1, rows // (128 * 24))):  # tile edges
+        idx |= {t - 1, t}
+    idx |= set(int(i) for i in rng.choice(rows, min(rows, 600), replace=False))
+    return np.array(sorted(idx), dtype=np.int64)
+
+
+@pytest.mark.parametrize("tokens", [1, 8, 64, 512])
+@pytest.mark.parametrize("shape", CONFIG2_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+@pytest.mark.parametrize("name", CONFIG2_TYPES)
+def test_matvec_config2_grid(L, O, name, shape, tokens):
+    """q35_launch_mul_mat_vec on BASELINE config 2 (lane-per-row GEMV below 16
+    tokens, the tcgen05 MMQ from 16; raw 210-byte Q6_K rows on the generic
+    kernel, and the engine's 224-byte Q6_K layout on the MMQ), bit-exact with
+    the scalar tier on sampled rows"""
+    cols, rows = shape
+    tt = TT[name]
+    wq = _device_weights(L, tt, rows, cols, key=tt * 1000003 + rows + 7 * cols)
+    rng = np.random.default_rng(rows + tokens)
+    x = rng.standard_normal((tokens, cols)).astype(np.float32)
+    xq = quantize_act(O, tt, x)
+    dxq = torch.from_numpy(xq).cuda()
+    idx = _sample_rows(rows, rng)
+    ref = matvec_q(O, tt, np.ascontiguousarray(wq[torch.from_numpy(idx).cuda()].cpu().numpy()), xq, len(idx), cols,
+                   tokens)
+    out = torch.full((tokens, rows), float("nan"), dtype=torch.float32, device="cuda")
+    ok(L.q35_launch_mul_mat_vec(wq.data_ptr(), dxq.data_ptr(), out.data_ptr(), rows, cols, tokens, tt, S))
+    got = out.cpu().numpy()[:, idx]
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
+    assert not torch.isnan(out).any().item()
+    if name == "Q6_K" and tokens >= 16:
+        nb = cols // 256
+        wp = torch.zeros((rows, nb, 224), dtype=torch.uint8, device="cuda")
+        wp[:, :, :210] = wq.view(rows, nb, 210)
+        out.fill_(float("nan"))
+        ok(L.q35b_mul_mat_vec_multi(1, (ctypes.c_void_p * 1)(wp.data_ptr()), (ctypes.c_int * 1)(Q6_K_PADDED),
+                                    (ctypes.c_longlong * 1)(rows), (ctypes.c_void_p * 1)(out.data_ptr()),
+                                    (ctypes.c_longlong * 1)(rows), (ctypes.c_int * 1)(0), dxq.data_ptr(), cols,
+                                    tokens, S))
+        got = out.cpu().numpy()[:, idx]
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), ("Q6_K padded", rows, cols, tokens)
+    no_kernel_error(L)
+
+
+def _gdn_inputs(rng, heads, nk, kd, rows):
+    """config-3 statistics: q / k l2-normalised (q also x 1/sqrt(kd)),
+    v ~ N(0,1), beta = sigmoid(N(0,1)), gamma = exp(-softplus(N(0,1)))"""
+    def l2n(x):
+        return x / np.sqrt((x.astype(np.float64) ** 2).sum(-1, keepdims=True) + 1e-6)
+    k = l2n(rng.standard_normal((rows, nk, kd))).astype(np.float32)
+    q = (l2n(rng.standard_normal((rows, nk, kd))) / np.sqrt(kd)).astype(np.float32)
+    v = rng.standard_normal((rows, heads, kd)).astype(np.float32)
+    bet = (1 / (1 + np.exp(-rng.standard_normal((rows, heads))))).astype(np.float32)
+    gam = np.exp(-np.log1p(np.exp(rng.standard_normal((rows, heads))))).astype(np.float32)
+    state = (rng.standard_normal((heads, kd, kd)) * 0.1).astype(np.float32)
+    return k, q, v, bet, gam, state
+
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.parametrize("rows,heads,nk", [(2048, 16, 16), (4099, 4, 2), (8192, 2, 1)])
+def test_gdn_prefill_vs_oracle_per_token(L, O, rows, heads, nk):
+    """BASELINE config 3 prefill lengths: the oracle steps the recurrence one
+    token at a time (src/backend_cpu.zig:1036-1056); the exact chunk kernel
+    (q35_launch_gdn_step_rows_chunk) matches it bit for bit, the WY form
+    (q35_launch_gdn_step_wy) within 1e-4 relative L2 in out, km, delta and
+    the final state"""
+    kd = 128
+    rng = np.random.default_rng(rows + heads)
+    k, q, v, bet, gam, state = _gdn_inputs(rng, heads, nk, kd, rows)
+    rs = state.copy()
+    rout, rkm, rdl = (np.zeros((rows, heads * kd), np.float32) for _ in range(3))
+    for t in range(rows):
+        O.q35o_gdn_step_rows(fp(rs), fp(k[t]), fp(v[t]), fp(q[t]), fp(rkm[t]), fp(rdl[t]), fp(rout[t]),
+                             fp(gam[t]), fp(bet[t]), heads, nk, kd, kd)
+    dk, dq, dv, db, dg = (torch.from_numpy(a).cuda() for a in (k, q, v, bet, gam))
+    for fn, exact in ((L.q35_launch_gdn_step_rows_chunk, True), (L.q35_launch_gdn_step_wy, False)):
+        ds = torch.from_numpy(state).cuda()
+        dkm, ddl, dout = (torch.zeros((rows, heads * kd), device="cuda") for _ in range(3))
+        ok(fn(ds.data_ptr(), kd * kd, dk.data_ptr(), nk * kd, dv.data_ptr(), heads * kd, dq.data_ptr(), nk * kd,
+              dkm.data_ptr(), heads * kd, ddl.data_ptr(), heads * kd, dout.data_ptr(), heads * kd,
+              dg.data_ptr(), heads, db.data_ptr(), heads, heads, nk, kd, kd, rows, S))
+        got = [t.cpu().numpy() for t in (dout, dkm, ddl, ds)]
+        for nm, a, b in zip(("out", "km", "delta", "state"), got, (rout, rkm, rdl, rs)):
+            if exact:
+                assert np.array_equal(a.reshape(-1).view(np.uint32), b.reshape(-1).view(np.uint32)), nm
+            else:
+                assert np.isfinite(a).all(), nm
+                assert _rel(a, b) < 1e-4, (nm, _rel(a, b))
+    no_kernel_error(L)
+
+
+@pytest.mark.parametrize("tokens", [1, 5])
+def test_deinterleave_qg(L, O, tokens):
+    """attn_q rows [h][q_h | gate_h] -> q and gate (elementwise.zig:428-433),
+    single and strided over tokens"""
+    heads, hd = 8, 256
+    rng = np.random.default_rng(tokens)
+    src = rng.standard_normal((tokens, 2 * heads * hd)).astype(np.float32)
+    rq = np.zeros((tokens, heads * hd), np.float32)
+    rg = np.zeros_like(rq)
+    for t in range(tokens):
+        O.q35o_deinterleave_qg(fp(rq[t]), fp(rg[t]), fp(src[t]), heads, hd)
+    ds = torch.from_numpy(src).cuda()
+    dq = torch.full((tokens, heads * hd), float("nan"), device="cuda")
+    dg = torch.full_like(dq, float("nan"))
+    if tokens == 1:
+        ok(L.q35_launch_deinterleave_qg(dq.data_ptr(), dg.data_ptr(), ds.data_ptr(), heads, hd, S))
+    else:
+        ok(L.q35_launch_deinterleave_qg_strided(dq.data_ptr(), dg.data_ptr(), ds.data_ptr(), heads, hd, tokens, S))
+    assert np.array_equal(dq.cpu().numpy(), rq)
+    assert np.array_equal(dg.cpu().numpy(), rg)

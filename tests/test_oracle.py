@@ -306,3 +306,19 @@ def test_against_reference_kernels_scalar_tier():
 def test_against_reference_kernels_default_tier():
     """The default (AVX2/VNNI) tier reorders the Q8_0 f32 fold; within 1e-5."""
     assert _run_ref("default") == 0
+
+
+def test_synth_generator_c_equals_numpy(L):
+    """the oracle's q35o_synth_fill (the CPU side of q35b_synth_fill) and the
+    numpy statement in qwen35_b200.configs give the same bits, and the values
+    have the intended spread"""
+    from qwen35_b200 import configs
+    for key, sigma, n in ((0, 0.02, 65536), (2**64 - 1, 1.0, 4099), (977, 0.5, 31)):
+        a = np.empty(n, np.float32)
+        L.q35o_synth_fill(key, n, configs.synth_k(sigma), fp(a))
+        b = configs.synth_normal_np(key, n, sigma)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    a = configs.synth_normal_np(5, 1 << 18, 1.0)
+    assert abs(float(a.mean())) < 0.01 and abs(float(a.std()) - 1.0) < 0.01
+    v = configs.synth_vector(3, 1000, "ssm_a")
+    assert (v < 0).all() and v.min() >= -np.e and v.max() <= -1 / np.e
