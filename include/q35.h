@@ -182,16 +182,26 @@ int q35_launch_attn_decode_split2(const float *d_q, const float *d_gate, const f
                                   const float *d_vcache, float *d_att, float *d_gout, float *d_part, int slot,
                                   int heads, int gqa, int hd, int kv_dim, float scale, int split, void *stream);
 
-/* device sampler (reference sample.cu:559-664, control block of 16 int32).
- * Sampling is outside this backend's hot path: q35_launch_sample implements
- * the greedy branch (ctl[6] = first index of the max logit).  A non-zero
- * temperature in ctl[1] still writes the argmax and records error 201 for
- * q35b_get_error.  _init allocates the two regions, as in the reference. */
+/* device sampler (reference sample.cu:559-664, control block of 16 int32:
+ * [1] temperature bits, [2] top_k, [3] top_p bits, [4..5] PRNG state in,
+ * [6] token out, [7..8] PRNG state out, [9] threshold bits out, [10] flags).
+ * The selection rules are src/sampler.zig's (greedy at temperature <= 0, the
+ * k-th largest value as the top-k threshold with ties kept, top-p as a raised
+ * threshold, one xorshift64* draw walked in index order).  n <= 262144.
+ * _init allocates the two regions, as in the reference; the kernel keeps its
+ * working state on chip, so the scratch region is not written. */
 int q35_sample_scratch_ints(void);
 int q35_sample_ctl_ints(void);
 int q35_launch_sample_init(void **d_ctl, void **d_scratch);
 void q35_launch_sample_deinit(void **d_ctl, void **d_scratch);
 int q35_launch_sample(const float *d_logits, int n, int *d_ctl, void *d_scratch, void *stream);
+/* The sampler over `rows` logits rows (ld floats apart) in one launch; row r
+ * uses the control block d_ctl + r * ctl_ld (ctl_ld >= 16).  advance = 1 also
+ * writes the advanced PRNG state over the input state ([4..5]), so the next
+ * call continues the stream; d_tokens (optional) receives the tokens.  No
+ * counterpart in the reference, whose engine samples one row. */
+int q35b_sample_rows(const float *d_logits, long long ld, int n, int rows, int *d_ctl, long long ctl_ld, int advance,
+                     int *d_tokens, void *stream);
 
 /* codebook upload (api.h:433-442).  The IQ4_NL codebook is compiled into
  * the kernels, so init is a no-op that reports success. */
@@ -351,6 +361,16 @@ int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slo
  * the recurrence's sums: it agrees with the per-token form to rounding, not
  * bitwise. */
 int q35b_engine_set_prefill_wy(q35b_engine *e, int on);
+
+/* Sampling in the engine's step (replaces the greedy argmax when on): every
+ * run's next token is drawn with the parameters of its slot, whose PRNG state
+ * advances on the device, so the step stays one CUDA graph.  set_sampler sets
+ * a slot's parameters and restarts its stream at `seed` (0: the reference's
+ * fixed default); temperature <= 0 keeps that slot greedy.  Not with tensor
+ * parallelism (the logits are split over the ranks). */
+int q35b_engine_set_sampling(q35b_engine *e, int on);
+int q35b_engine_set_sampler(q35b_engine *e, int slot, float temperature, int top_k, float top_p,
+                            unsigned long long seed);
 
 /* Prompt prefill of one slot: ntok tokens from position pos0 as runs of up
  * to max_batch tokens (src/engine.zig:2078-2177, forwardChunk); *next = greedy token after

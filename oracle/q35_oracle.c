@@ -919,3 +919,90 @@ void q35o_synth_fill(uint64_t key, long long n, float k, float *dst)
         dst[i] = (float)(sum - 131070) * k;
     }
 }
+
+/* ====================================================================== */
+/* sampler (src/sampler.zig:60-190, Sampler.nextU64 / nextF32 / sample)    */
+/* ====================================================================== */
+static uint64_t o_xs64(uint64_t *s)
+{
+    uint64_t x = *s;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *s = x;
+    return x * 0x2545F4914F6CDD1DULL;
+}
+
+static int o_cmp_desc(const void *a, const void *b)
+{
+    const float x = *(const float *)a, y = *(const float *)b;
+    return (x < y) - (x > y);
+}
+
+/* the k-th largest value (0-based rank), sampler.zig:196-255: any exact
+ * selection gives the same value; a descending sort here */
+float q35o_kth_largest(float *a, int n, int rank)
+{
+    qsort(a, (size_t)n, sizeof(float), o_cmp_desc);
+    return a[rank];
+}
+
+int q35o_sample(const float *logits, int n, float temperature, int top_k, float top_p, uint64_t *state,
+                float *scratch)
+{
+    if (!(temperature > 0)) { /* :71-80 greedy, ties to the lowest index */
+        int best = 0;
+        float bv = -3.402823466e38f;
+        for (int i = 0; i < n; i++)
+            if (logits[i] > bv) {
+                bv = logits[i];
+                best = i;
+            }
+        return best;
+    }
+    const float t = temperature;
+    float maxv = logits[0];
+    for (int i = 1; i < n; i++)
+        if (logits[i] > maxv) maxv = logits[i];
+    float thresh = -3.402823466e38f;
+    if (top_k > 0 && top_k < n) { /* :93-99 */
+        memcpy(scratch, logits, (size_t)n * sizeof(float));
+        thresh = q35o_kth_largest(scratch, n, top_k - 1);
+    }
+    if (top_p > 0 && top_p < 1) { /* :125-165 */
+        double total = 0;
+        for (int i = 0; i < n; i++)
+            if (logits[i] >= thresh) total += (double)Q35O_EXPF((logits[i] - maxv) / t);
+        if (total > 0) {
+            const double target = total * (double)top_p;
+            int ns = 0;
+            for (int i = 0; i < n; i++)
+                if (!(logits[i] < thresh)) scratch[ns++] = logits[i];
+            qsort(scratch, (size_t)ns, sizeof(float), o_cmp_desc);
+            double acc = 0;
+            float cut = thresh;
+            for (int i = 0; i < ns; i++) {
+                acc += (double)Q35O_EXPF((scratch[i] - maxv) / t);
+                if (acc >= target) {
+                    cut = scratch[i];
+                    break;
+                }
+            }
+            if (cut > thresh) thresh = cut;
+        }
+    }
+    double sum = 0; /* :167-172 */
+    for (int i = 0; i < n; i++)
+        if (logits[i] >= thresh) sum += (double)Q35O_EXPF((logits[i] - maxv) / t);
+    if (*state == 0) *state = 0x9E3779B97F4A7C15ULL;
+    const double coin = (double)((float)(o_xs64(state) >> 40) / 16777216.0f);
+    double acc = 0;
+    for (int i = 0; i < n; i++) { /* :174-184 */
+        if (logits[i] < thresh) continue;
+        acc += (double)Q35O_EXPF((logits[i] - maxv) / t);
+        if (coin < acc / sum) return i;
+    }
+    for (int i = n; i > 0; i--) /* :185-189 */
+        if (logits[i - 1] >= thresh) return i - 1;
+    return 0;
+}

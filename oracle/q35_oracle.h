@@ -144,6 +144,12 @@ void q35o_attn_decode(const float *q, const float *gate, const float *kcache,
                       const float *vcache, float *att, float *gout, int slot,
                       int heads, int gqa, int hd, int kv_dim, float scale);
 int q35o_argmax(const float *x, int n);
+/* Sampler.sample (src/sampler.zig:67-190): greedy at temperature <= 0,
+ * else top-k / top-p thresholds and one xorshift64* draw from *state (0
+ * selects the fixed default); scratch holds n floats */
+int q35o_sample(const float *logits, int n, float temperature, int top_k, float top_p, uint64_t *state,
+                float *scratch);
+float q35o_kth_largest(float *a, int n, int rank);
 
 /* ---- engine (src/engine.zig forwardLogits / generate) --------------- */
 typedef struct q35o_config {

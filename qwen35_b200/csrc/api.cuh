@@ -425,19 +425,20 @@ void *q35_func_attn_pv_split_dyn(void) { return (void *)k_attn_merge; }
 void *q35_func_attn_softmax_dyn(void) { return (void *)k_attn_merge; }
 void *q35_func_attn_reduce(void) { return (void *)k_attn_merge; }
 
-// ---- device sampler (src/kernels/cuda/sample.cu:559-664): greedy only ----
+// ---- device sampler (src/kernels/cuda/sample.cu:559-664; rules of
+// src/sampler.zig): temperature, top-k, top-p, one xorshift64* draw ----
 int q35_sample_scratch_ints(void) { return 16; }
-int q35_sample_ctl_ints(void) { return 16; }
+int q35_sample_ctl_ints(void) { return SC_INTS; }
 int q35_launch_sample_init(void **d_ctl, void **d_scratch) {
     if (!d_ctl || !d_scratch) return (int)cudaErrorInvalidValue;
     if (!*d_ctl) {
-        if (cudaMalloc(d_ctl, 16 * sizeof(int)) != cudaSuccess) {
+        if (cudaMalloc(d_ctl, SC_INTS * sizeof(int)) != cudaSuccess) {
             *d_ctl = nullptr;
             return (int)cudaGetLastError();
         }
-        cudaMemset(*d_ctl, 0, 16 * sizeof(int));
+        cudaMemset(*d_ctl, 0, SC_INTS * sizeof(int));
     }
-    if (!*d_scratch) {
+    if (!*d_scratch) {  // the kernel keeps its working state on chip; the region is the contract's
         if (cudaMalloc(d_scratch, 16 * sizeof(int)) != cudaSuccess) {
             cudaFree(*d_ctl);
             *d_ctl = nullptr;
@@ -452,8 +453,14 @@ void q35_launch_sample_deinit(void **d_ctl, void **d_scratch) {
 }
 int q35_launch_sample(const float *d_logits, int n, int *d_ctl, void *d_scratch, void *stream) {
     if (!d_logits || !d_ctl || !d_scratch || n <= 0) return (int)cudaErrorInvalidValue;
-    k_sample_greedy<<<1, 1024, 0, S(stream)>>>(d_logits, n, d_ctl);
-    return (int)cudaGetLastError();
+    const SmpArgs a{d_logits, n, n, 1, d_ctl, SC_INTS, nullptr, nullptr, nullptr, 0};
+    return sample_launch(a, S(stream));
+}
+int q35b_sample_rows(const float *d_logits, long long ld, int n, int rows, int *d_ctl, long long ctl_ld, int advance,
+                     int *d_tokens, void *stream) {
+    if (rows < 0) return (int)cudaErrorInvalidValue;
+    const SmpArgs a{d_logits, ld, n, rows, d_ctl, ctl_ld, nullptr, nullptr, d_tokens, advance ? 1 : 0};
+    return sample_launch(a, S(stream));
 }
 
 // ---- codebooks (api.h:433-442): compiled into the kernels ----

@@ -223,6 +223,8 @@ struct q35b_engine {
     float *logits = nullptr, *scores = nullptr, *probe_buf = nullptr;
     float *xh = nullptr;  // last row of each run, gathered for the model head
     bool gdn_wy = false;  // prefill runs through the chunked (WY) GDN form
+    bool sampling = false;  // next tokens drawn by the device sampler (per-slot parameters) instead of argmax
+    int *samp = nullptr;    // per-slot sampler control blocks [n_slots][SC_INTS]
     // tensor parallelism (1 rank: off)
     int tp_n = 1, tp_rank = 0;
     long long vocab_local = 0, vocab_off = 0;  // this rank's lm_head rows
@@ -563,7 +565,12 @@ inline int eng_step_body(q35b_engine *e, int n, int nrun, int max_len, cudaStrea
         Q35_TRY(eng_norm_gemv(e, n, e->output_norm, {{H.w, e->logits, H.rows, H.tt, vl, GV_STORE}}, st));
     }
     int rc;
-    if (e->tp_n > 1) {
+    if (e->sampling) {
+        if (e->tp_n > 1) return (int)cudaErrorNotSupported;
+        const SmpArgs sa{e->logits, (long long)c.vocab, c.vocab, nrun, e->samp, SC_INTS, e->d_in + e->max_batch,
+                         nrun < n ? (const int *)(e->d_in + 3 * e->max_batch) : nullptr, e->d_next, 1};
+        rc = sample_launch(sa, st);
+    } else if (e->tp_n > 1) {
         Q35_TRY(launch_k(k_argmax_pair, dim3(nrun), dim3(1024), 0, st, (const float *)e->logits, vl, (int)vl,
                          (int)e->vocab_off, e->am_pair));
         if (nccl_api().all_gather(e->am_pair, e->am_all, (size_t)2 * nrun, ncclInt32, e->comm, st) != ncclSuccess)

@@ -65,6 +65,32 @@ int q35b_engine_set_prefill_wy(q35b_engine *e, int on) {
     return 0;
 }
 
+int q35b_engine_set_sampling(q35b_engine *e, int on) {
+    if (!e) return (int)cudaErrorInvalidValue;
+    if (on && e->tp_n > 1) return (int)cudaErrorNotSupported;
+    if (on && e->c.vocab > SMP_MAX_N) return (int)cudaErrorInvalidValue;
+    if (e->sampling != (on != 0)) {
+        for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+        e->graphs.clear();
+    }
+    e->sampling = on != 0;
+    return 0;
+}
+
+int q35b_engine_set_sampler(q35b_engine *e, int slot, float temperature, int top_k, float top_p,
+                            unsigned long long seed) {
+    if (!e || !e->finalized || slot < 0 || slot >= e->n_slots || top_k < 0) return (int)cudaErrorInvalidValue;
+    if (seed == 0) seed = 0x9E3779B97F4A7C15ULL;  // src/sampler.zig:47
+    int blk[SC_INTS] = {};
+    blk[SC_VOCAB] = e->c.vocab;
+    memcpy(&blk[SC_TEMP], &temperature, 4);
+    blk[SC_TOPK] = top_k;
+    memcpy(&blk[SC_TOPP], &top_p, 4);
+    blk[SC_RNG_LO] = (int)(uint32_t)(seed & 0xFFFFFFFFu);
+    blk[SC_RNG_HI] = (int)(uint32_t)(seed >> 32);
+    return (int)cudaMemcpy(e->samp + (long long)slot * SC_INTS, blk, sizeof(blk), cudaMemcpyHostToDevice);
+}
+
 int q35b_tp_unique_id(void *out, int bytes) {
     const NcclApi &api = nccl_api();
     if (!api.ok) return (int)cudaErrorSharedObjectInitFailed;
@@ -214,6 +240,7 @@ int q35b_engine_finalize(q35b_engine *e) {
         }
     }
     ALLOC(xh, 4 * B * h);
+    ALLOC(samp, 4 * SC_INTS * S);  // zeroed below: every slot greedy until set_sampler
     ALLOC(d_len, 4 * B);
     ALLOC(d_next, 4 * B);
     ALLOC(x, 4 * B * h);
@@ -258,6 +285,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY((int)cudaMemset(e->d_in, 0, 4 * 4 * B));
     Q35_TRY((int)cudaHostAlloc((void **)&e->h_io, 4 * 4 * B, cudaHostAllocDefault));
     Q35_TRY((int)cudaMemset(e->am_cnt, 0, 4 * B));
+    Q35_TRY((int)cudaMemset(e->samp, 0, 4 * SC_INTS * S));
     // load-time repack: Q6_K projections to 224-byte blocks (16-byte rows for
     // the TMA-streamed GEMV); the caller's buffers stay untouched
     auto repack = [&](Lin &l) -> int {

@@ -335,32 +335,4 @@ __global__ void k_matvec_w16(const uint16_t *w, const float *x, float *out, int 
     if (lane == 0) out[(long long)t * rows + r] = sum;
 }
 
-// greedy branch of the reference's device sampler contract: ctl[6] <- argmax
-__global__ void __launch_bounds__(1024) k_sample_greedy(const float *x, int n, int *ctl) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    float bv = -INFINITY;
-    int bi = n;
-    for (int i = threadIdx.x; i < n; i += 1024) {
-        const float v = x[i];
-        if (v > bv) { bv = v; bi = i; }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < 32; w++)
-            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
-        ctl[6] = bi >= n ? 0 : bi;
-        // a non-zero temperature asks for a stochastic draw, which this build
-        // does not implement: record it rather than pretend
-        if (ctl[1] != 0) set_error(201);
-    }
-}
-
 }  // namespace q35

@@ -14,6 +14,7 @@
 #include "ew.cuh"
 #include "gdn.cuh"
 #include "attn.cuh"
+#include "sample.cuh"
 #include "api.cuh"
 #include "engine_api.cuh"
 #include "noalloc.cuh"

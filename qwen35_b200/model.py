@@ -184,6 +184,14 @@ class Engine:
                                       d_logits.data_ptr() if d_logits is not None else None,
                                       1 if use_graph else 0, _stream(stream)), "step")
 
+    def set_sampling(self, on):
+        """device sampler (per-slot parameters) instead of the greedy argmax"""
+        check(self.L.q35b_engine_set_sampling(self.h, 1 if on else 0), "set_sampling")
+
+    def set_sampler(self, slot, temperature=0.0, top_k=0, top_p=0.0, seed=0):
+        check(self.L.q35b_engine_set_sampler(self.h, slot, float(temperature), int(top_k), float(top_p),
+                                             int(seed)), "set_sampler")
+
     def set_probe(self, on):
         check(self.L.q35b_engine_set_probe(self.h, 1 if on else 0), "set_probe")
 

@@ -66,6 +66,8 @@ def _declare(lib):
         "q35o_deinterleave_qg": (V, [f32p, f32p, f32p, I, I]),
         "q35o_attn_decode": (V, [f32p, f32p, f32p, f32p, f32p, f32p, I, I, I, I, I, F]),
         "q35o_argmax": (I, [f32p, I]),
+        "q35o_sample": (I, [f32p, I, F, I, F, ctypes.POINTER(ctypes.c_uint64), f32p]),
+        "q35o_kth_largest": (F, [f32p, I, I]),
         "q35o_model_create": (ctypes.c_void_p, [ctypes.POINTER(Config), I, I]),
         "q35o_model_destroy": (V, [ctypes.c_void_p]),
         "q35o_model_set_threads": (V, [ctypes.c_void_p, I]),
@@ -200,3 +202,18 @@ def oracle_forward(lib, m, token, pos, vocab):
 def oracle_layer_out(lib, m, li, hidden):
     p = lib.q35o_layer_out(m, li)
     return np.ctypeslib.as_array(p, shape=(hidden,)).copy()
+
+
+class OracleSampler:
+    """Sampler.sample (src/sampler.zig) through the oracle: the PRNG state
+    lives here, as in the reference's Sampler struct"""
+
+    def __init__(self, lib, temperature=0.0, top_k=0, top_p=0.0, seed=0):
+        self.lib, self.t, self.k, self.p = lib, float(temperature), int(top_k), float(top_p)
+        self.state = ctypes.c_uint64(seed if seed else 0x9E3779B97F4A7C15)
+
+    def sample(self, logits):
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        scratch = np.empty(max(1, x.size), np.float32)
+        return int(self.lib.q35o_sample(fp(x), x.size, self.t, self.k, self.p, ctypes.byref(self.state),
+                                        fp(scratch)))
