@@ -250,16 +250,15 @@ def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False):
     return ms
 
 
-SERVE_SEQS, SERVE_PROMPT, SERVE_GEN = 64, (64, 512), 32
+SERVE_SEQS, SERVE_PROMPT, SERVE_GEN = 64, (64, 2048), 256
 
 
 def time_serve(cfg_name, seed, dist, world, rank):
-    """BASELINE config 4 in a bounded sample: continuous batching of
-    SERVE_SEQS sequences (seeded prompt lengths uniform in SERVE_PROMPT,
-    SERVE_GEN greedy tokens each; the config itself has prompts of 64..2048
-    and 256 tokens) through q35b_serve, the sequences sharded over the ranks
-    (every rank serves its share of the fixed set: strong scaling).  Returns
-    (ms, prompt tokens, generated tokens) of this rank."""
+    """continuous batching of SERVE_SEQS sequences (seeded
+    prompt lengths uniform in SERVE_PROMPT, SERVE_GEN greedy tokens each)
+    through q35b_serve, the sequences sharded over the ranks (every rank
+    serves its share of the fixed set: strong scaling).  Returns (ms of this
+    rank, prompt tokens and generated tokens of the whole set)."""
     import numpy as np
     import torch
 
@@ -287,7 +286,7 @@ def time_serve(cfg_name, seed, dist, world, rank):
     eng.close()
     del synth
     torch.cuda.empty_cache()
-    return ms, int(sum(lens[i] for i in mine)), nslot * SERVE_GEN
+    return ms, int(sum(lens)), SERVE_SEQS * SERVE_GEN
 
 
 def time_tp_decode(cfg_name, batch, ctx, steps, warmup, seed, dist, world, rank):
@@ -950,11 +949,12 @@ def main():
                          "unit": "tokens/s", "scaling": "strong", "weight_bytes_per_rank": wb})
         sms, sp, sg = time_serve("4b", args.seed, dist, world, rank)
         sms = max_over_ranks(sms, dist)
-        variants.append({"model": "qwen3.5-4b-mixed", "workload": "continuous batching (BASELINE config 4, bounded "
-                         "sample): %d sequences, prompts uniform in %d..%d tokens, %d greedy tokens each, sharded "
-                         "by sequence over the ranks" % (SERVE_SEQS, SERVE_PROMPT[0], SERVE_PROMPT[1], SERVE_GEN),
+        variants.append({"model": "qwen3.5-4b-mixed", "workload": "continuous batching (BASELINE config 4): %d "
+                         "sequences, prompts uniform in %d..%d tokens, %d greedy tokens each, sharded by sequence "
+                         "over the ranks" % (SERVE_SEQS, SERVE_PROMPT[0], SERVE_PROMPT[1], SERVE_GEN),
                          "ms": sms, "value": SERVE_SEQS * SERVE_GEN / (sms * 1e-3), "unit": "generated tokens/s",
-                         "total_tokens_per_s": (sp * world + sg * world) / (sms * 1e-3) if world == 1 else None,
+                         "prompt_tokens": sp, "generated_tokens": sg,
+                         "total_tokens_per_s": (sp + sg) / (sms * 1e-3),
                          "scaling": "strong"})
         for cfg_name, ntok, chunk in (("0.8b", 512, 256), ("4b", 512, 256)):
             for wy in (False, True):

@@ -195,6 +195,19 @@ int q35_sample_ctl_ints(void);
 int q35_launch_sample_init(void **d_ctl, void **d_scratch);
 void q35_launch_sample_deinit(void **d_ctl, void **d_scratch);
 int q35_launch_sample(const float *d_logits, int n, int *d_ctl, void *d_scratch, void *stream);
+/* Prefill-shaped causal attention over a chunk of one sequence: row r
+ * (q, gate, out: rows x heads x hd floats) attends to cache positions
+ * [0, slot0 + r] in the CPU's operation order (serial dots, max, exp, serial
+ * sum, divide, serial P.V, sigmoid gate; src/elementwise.zig:349-372), i.e.
+ * bit for bit the rows of a token-by-token decode, with each K / V tile
+ * loaded once per 8 rows.  d_scores: caller workspace of rows x heads x
+ * scores_ld floats (scores_ld >= slot0 + rows).  hd = 256; heads / gqa kv
+ * heads; q, K and V 16-byte aligned.  No counterpart in the reference, whose
+ * q35_launch_attn_chunk runs the rows one by one (attn.cu:107-189). */
+int q35b_attn_prefill(const float *d_q, const float *d_gate, const float *d_kcache, const float *d_vcache,
+                      float *d_gout, float *d_scores, long long scores_ld, int slot0, int rows, int heads, int gqa,
+                      int hd, int kv_dim, float scale, void *stream);
+
 /* The sampler over `rows` logits rows (ld floats apart) in one launch; row r
  * uses the control block d_ctl + r * ctl_ld (ctl_ld >= 16).  advance = 1 also
  * writes the advanced PRNG state over the input state ([4..5]), so the next

@@ -113,6 +113,9 @@ int q35o_block_geom(int ttype, int *elems, int *bytes)
     switch (ttype) {
     case Q35O_TT_Q8_0: e = 32; b = 34; break;
     case Q35O_TT_Q4_0: e = 32; b = 18; break;
+    case Q35O_TT_Q4_1: e = 32; b = 20; break;
+    case Q35O_TT_Q5_0: e = 32; b = 22; break;
+    case Q35O_TT_Q5_1: e = 32; b = 24; break;
     case Q35O_TT_IQ4_NL: e = 32; b = 18; break;
     case Q35O_TT_Q4_K: e = 256; b = 144; break;
     case Q35O_TT_Q5_K: e = 256; b = 176; break;
@@ -283,6 +286,59 @@ static void wq_iq4_nl_block(const float *x, uint8_t *y)
     for (int j = 0; j < 16; j++) y[2 + j] = (uint8_t)(idx[j] | (idx[j + 16] << 4));
 }
 
+/* Q4_0 / Q5_0 (symmetric, 2^(bits-1) levels either side) and Q4_1 / Q5_1
+ * (affine over [min, max]) encoders of this project, one 32-element block:
+ * d from the value of largest magnitude (or the range) rounded to f16, the
+ * elements quantized against the rounded scale.  GGUF layout: element j < 16
+ * in the low nibble of qs[j], element j + 16 in the high nibble; Q5 keeps bit
+ * 4 of element j in bit j of qh. */
+static void wq_legacy_block(int tt, const float *x, uint8_t *y)
+{
+    const int affine = tt == Q35O_TT_Q4_1 || tt == Q35O_TT_Q5_1;
+    const int five = tt == Q35O_TT_Q5_0 || tt == Q35O_TT_Q5_1;
+    const int qmax = five ? 31 : 15;
+    uint8_t q[32];
+    if (affine) {
+        float mn = x[0], mx = x[0];
+        for (int i = 1; i < 32; i++) {
+            if (x[i] < mn) mn = x[i];
+            if (x[i] > mx) mx = x[i];
+        }
+        const uint16_t dh = q35o_f32_to_f16((mx - mn) / (float)qmax), mh = q35o_f32_to_f16(mn);
+        const float dr = q35o_f16_to_f32(dh), mr = q35o_f16_to_f32(mh);
+        const float id = dr != 0.0f ? 1.0f / dr : 0.0f;
+        for (int i = 0; i < 32; i++) {
+            int v = (int)((x[i] - mr) * id + 0.5f);
+            q[i] = (uint8_t)(v < 0 ? 0 : (v > qmax ? qmax : v));
+        }
+        y[0] = (uint8_t)(dh & 0xFF); y[1] = (uint8_t)(dh >> 8);
+        y[2] = (uint8_t)(mh & 0xFF); y[3] = (uint8_t)(mh >> 8);
+    } else {
+        float amax = 0.0f, vmax = 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const float a = fabsf(x[i]);
+            if (a > amax) { amax = a; vmax = x[i]; }
+        }
+        const float half = five ? 16.0f : 8.0f;
+        const uint16_t dh = q35o_f32_to_f16(vmax / -half);
+        const float dr = q35o_f16_to_f32(dh);
+        const float id = dr != 0.0f ? 1.0f / dr : 0.0f;
+        for (int i = 0; i < 32; i++) {
+            int v = (int)(x[i] * id + (half + 0.5f));
+            q[i] = (uint8_t)(v < 0 ? 0 : (v > qmax ? qmax : v));
+        }
+        y[0] = (uint8_t)(dh & 0xFF); y[1] = (uint8_t)(dh >> 8);
+    }
+    const int qs_off = affine ? (five ? 8 : 4) : (five ? 6 : 2);
+    if (five) {
+        uint32_t qh = 0;
+        for (int j = 0; j < 32; j++) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
+        uint8_t *h = y + (affine ? 4 : 2);
+        h[0] = (uint8_t)qh; h[1] = (uint8_t)(qh >> 8); h[2] = (uint8_t)(qh >> 16); h[3] = (uint8_t)(qh >> 24);
+    }
+    for (int j = 0; j < 16; j++) y[qs_off + j] = (uint8_t)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
+}
+
 /* Q4_K / Q5_K, one 256-element super-block.  Each 32-element sub-block gets
  * an affine range [mn, mx] with mn <= 0; its scale (mx-mn)/L and offset -mn
  * are quantized to 6 bits against f16 super-scales, and the elements are
@@ -408,6 +464,15 @@ void q35o_quantize_weight(int ttype, int n, const float *x, uint8_t *out)
 {
     switch (ttype) {
     case Q35O_TT_Q8_0: q35o_quantize_weight_q8_0(n, x, out); break;
+    case Q35O_TT_Q4_0:
+    case Q35O_TT_Q4_1:
+    case Q35O_TT_Q5_0:
+    case Q35O_TT_Q5_1: {
+        int e, b;
+        q35o_block_geom(ttype, &e, &b);
+        for (int i = 0; i < n / 32; i++) wq_legacy_block(ttype, x + i * 32, out + (size_t)i * b);
+        break;
+    }
     case Q35O_TT_IQ4_NL:
         for (int b = 0; b < n / 32; b++) wq_iq4_nl_block(x + b * 32, out + b * 18);
         break;
@@ -454,6 +519,27 @@ static void dequant_block(int ttype, const uint8_t *x, float *out)
         for (int j = 0; j < 16; j++) {
             out[j] = ((float)(x[2 + j] & 0x0F) - 8.0f) * d;
             out[j + 16] = ((float)(x[2 + j] >> 4) - 8.0f) * d;
+        }
+        break;
+    }
+    case Q35O_TT_Q4_1: { /* quant_dequant.zig:92-103 */
+        const float d = f16at(x), m = f16at(x + 2);
+        for (int j = 0; j < 16; j++) {
+            out[j] = (float)(x[4 + j] & 0x0F) * d + m;
+            out[j + 16] = (float)(x[4 + j] >> 4) * d + m;
+        }
+        break;
+    }
+    case Q35O_TT_Q5_0:
+    case Q35O_TT_Q5_1: { /* GGUF layout: low nibbles 0..15, high 16..31, bit 4 from qh */
+        const int aff = ttype == Q35O_TT_Q5_1;
+        const float d = f16at(x), m = aff ? f16at(x + 2) : 0.0f;
+        const uint32_t qh = (uint32_t)x[aff ? 4 : 2] | ((uint32_t)x[aff ? 5 : 3] << 8) |
+                            ((uint32_t)x[aff ? 6 : 4] << 16) | ((uint32_t)x[aff ? 7 : 5] << 24);
+        const uint8_t *qs = x + (aff ? 8 : 6);
+        for (int j = 0; j < 32; j++) {
+            const int q = (j < 16 ? (qs[j] & 0x0F) : (qs[j - 16] >> 4)) | (int)(((qh >> j) & 1u) << 4);
+            out[j] = aff ? (float)q * d + m : ((float)q - 16.0f) * d;
         }
         break;
     }
@@ -542,12 +628,36 @@ static int32_t isum32(int ttype, const uint8_t *xb, const uint8_t *yb)
             s += (int32_t)kIq4nl[xb[2 + j] & 0x0F] * (int32_t)(int8_t)yb[2 + j];
             s += (int32_t)kIq4nl[xb[2 + j] >> 4] * (int32_t)(int8_t)yb[2 + 16 + j];
         }
-    } else if (ttype == Q35O_TT_Q4_0) {
+    } else if (ttype == Q35O_TT_Q4_0) { /* kernels32.c:297-316 */
         for (int j = 0; j < 16; j++) {
             s += ((int32_t)(xb[2 + j] & 0x0F) - 8) * (int32_t)(int8_t)yb[2 + j];
             s += ((int32_t)(xb[2 + j] >> 4) - 8) * (int32_t)(int8_t)yb[2 + 16 + j];
         }
+    } else if (ttype == Q35O_TT_Q4_1) { /* kernels32.c:318-340 */
+        for (int j = 0; j < 16; j++) {
+            s += (int32_t)(xb[4 + j] & 0x0F) * (int32_t)(int8_t)yb[2 + j];
+            s += (int32_t)(xb[4 + j] >> 4) * (int32_t)(int8_t)yb[2 + 16 + j];
+        }
+    } else if (ttype == Q35O_TT_Q5_0 || ttype == Q35O_TT_Q5_1) {
+        /* kernels32.c:546-566, 628-652 arithmetic; the GGUF nibble layout
+         * (the reference's AVX2 unpack, kernels32.c:485-509) */
+        const int aff = ttype == Q35O_TT_Q5_1;
+        const uint8_t *h = xb + (aff ? 4 : 2), *qs = xb + (aff ? 8 : 6);
+        const uint32_t qh = (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+        for (int j = 0; j < 32; j++) {
+            const int32_t q = (j < 16 ? (qs[j] & 0x0F) : (qs[j - 16] >> 4)) | (int32_t)(((qh >> j) & 1u) << 4);
+            s += (aff ? q : q - 16) * (int32_t)(int8_t)yb[2 + j];
+        }
     }
+    return s;
+}
+
+/* sum of the 32 activation values of a Q8_0 block (the min term of Q4_1 /
+ * Q5_1, kernels32.c:336, 646) */
+static int32_t sumy32(const uint8_t *yb)
+{
+    int32_t s = 0;
+    for (int j = 0; j < 32; j++) s += (int32_t)(int8_t)yb[2 + j];
     return s;
 }
 
@@ -631,11 +741,15 @@ float q35o_vec_dot(int ttype, int n, const uint8_t *w, const uint8_t *xq)
     if (q35o_act_block_elems(ttype) == 32) {
         int e, b;
         q35o_block_geom(ttype, &e, &b);
+        const int aff = ttype == Q35O_TT_Q4_1 || ttype == Q35O_TT_Q5_1;
         for (int ib = 0; ib < n / 32; ib++) {
             const uint8_t *xb = w + (size_t)ib * b, *yb = xq + (size_t)ib * 34;
             const float dx = f16at(xb), dy = f16at(yb);
             const int32_t s = isum32(ttype, xb, yb);
-            sumf += dx * dy * (float)s;
+            if (aff) /* kernels32.c:338, 648: sumf += dx*dy*sumi + mx*dy*sumy */
+                sumf += dx * dy * (float)s + f16at(xb + 2) * dy * (float)sumy32(yb);
+            else
+                sumf += dx * dy * (float)s;
         }
         return sumf;
     }

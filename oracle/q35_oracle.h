@@ -61,6 +61,9 @@ extern "C" {
 /* GGUF TensorType ids (src/gguf.zig:87-122). */
 #define Q35O_TT_F32 0
 #define Q35O_TT_Q4_0 2
+#define Q35O_TT_Q4_1 3
+#define Q35O_TT_Q5_0 6
+#define Q35O_TT_Q5_1 7
 #define Q35O_TT_Q8_0 8
 #define Q35O_TT_Q4_K 12
 #define Q35O_TT_Q5_K 13

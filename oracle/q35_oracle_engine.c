@@ -29,6 +29,10 @@
  * kernels256.c public dispatch) */
 float q8_0_q8_0(int n, const void *vx, const void *vy);
 float iq4_nl_q8_0(int n, const void *vx, const void *vy);
+float q4_0_q8_0(int n, const void *vx, const void *vy);
+float q4_1_q8_0(int n, const void *vx, const void *vy);
+float q5_0_q8_0(int n, const void *vx, const void *vy);
+float q5_1_q8_0(int n, const void *vx, const void *vy);
 float q4_k_q8_k(int n, const void *vx, const void *vy);
 float q5_k_q8_k(int n, const void *vx, const void *vy);
 float q6_k_q8_k(int n, const void *vx, const void *vy);
@@ -40,6 +44,10 @@ static float row_dot(int tt, int n, const uint8_t *w, const uint8_t *xq)
     switch (tt) {
     case Q35O_TT_Q8_0: return q8_0_q8_0(n, w, xq);
     case Q35O_TT_IQ4_NL: return iq4_nl_q8_0(n, w, xq);
+    case Q35O_TT_Q4_0: return q4_0_q8_0(n, w, xq);
+    case Q35O_TT_Q4_1: return q4_1_q8_0(n, w, xq);
+    case Q35O_TT_Q5_0: return q5_0_q8_0(n, w, xq);
+    case Q35O_TT_Q5_1: return q5_1_q8_0(n, w, xq);
     case Q35O_TT_Q4_K: return q4_k_q8_k(n, w, xq);
     case Q35O_TT_Q5_K: return q5_k_q8_k(n, w, xq);
     case Q35O_TT_Q6_K: return q6_k_q8_k(n, w, xq);

@@ -78,6 +78,10 @@ CONFIGS = {
     # the 27B TP-8 shapes in small: one kv head replicated on both ranks, an
     # odd count of ffn blocks (3 -> 2 + 1), Q4_K bulk with a Q6_K lm_head
     # (GDN value heads in pairs: ssm_out columns in whole 256-blocks)
+    # the legacy 32-element families (Q4_0 / Q4_1 / Q5_0 / Q5_1) in one model
+    "tiny-legacy": ModelConfig("tiny-legacy", 8, 512, 1024, 4096, 4, 1, 4, 2,
+                               quant=(("bulk", "Q4_0"), ("attn_qkv", "Q5_0"), ("ffn_down", "Q5_1"),
+                                      ("ffn_up", "Q4_1"), ("attn_output", "Q5_1"), ("output", "Q4_1"))),
     # the 27B layer shapes (hidden 5120, ffn 17408, 24 q / 4 kv heads, 48 GDN
     # value heads over 16 k heads, Q4_K with a Q6_K lm_head) in 4 layers
     # (3 GDN + 1 attention) and a 32768-entry vocab: TP parity against the

@@ -416,6 +416,39 @@ int q35_launch_attn_chunk(const float *d_q, const float *d_gate, const float *d_
     return 0;
 }
 int q35_attn_chunk_max_rows(int) { return 1 << 20; }
+
+// Prefill-shaped causal attention over a chunk, in the CPU's operation
+// order (the token-tiled kernels of attn.cuh); d_scores: the caller's
+// workspace of rows x heads x scores_ld floats, scores_ld >= slot0 + rows
+int q35b_attn_prefill(const float *d_q, const float *d_gate, const float *d_kcache, const float *d_vcache,
+                      float *d_gout, float *d_scores, long long scores_ld, int slot0, int rows, int heads, int gqa,
+                      int hd, int kv_dim, float scale, void *stream) {
+    if (rows <= 0 || heads <= 0) return 0;
+    if (hd != ATT_HD || gqa <= 0 || heads % gqa || slot0 < 0 || !d_scores || scores_ld < (long long)slot0 + rows ||
+        kv_dim < (heads / gqa) * hd || (kv_dim & 3) || (reinterpret_cast<uintptr_t>(d_kcache) & 15u) ||
+        (reinterpret_cast<uintptr_t>(d_vcache) & 15u) || (reinterpret_cast<uintptr_t>(d_q) & 15u))
+        return (int)cudaErrorInvalidValue;
+    AttnXArgs a{};
+    a.q = d_q;
+    a.gate = d_gate;
+    a.q_tok = (long long)heads * hd;
+    a.kc = d_kcache;
+    a.vc = d_vcache;
+    a.kv_slot = 0;
+    a.kv_dim = kv_dim;
+    a.len_imm = slot0 + 1;
+    a.len_step = 1;
+    a.scores = d_scores;
+    a.max_len = (int)scores_ld;
+    a.out = d_gout;
+    a.out_tok = (long long)heads * hd;
+    a.heads = heads;
+    a.kv_heads = heads / gqa;
+    a.scale = scale;
+    a.fam = 0;
+    const int rc = attp_launch(a, rows, slot0 + rows, S(stream));
+    return rc == -1 ? (int)cudaErrorInvalidValue : rc;
+}
 void *q35_func_attn_decode(void) { return (void *)k_attn_split<4>; }
 void *q35_func_attn_decode_dyn(void) { return (void *)k_attn_split<4>; }
 void *q35_func_attn_decode_coal(void) { return (void *)k_attn_split<4>; }

@@ -240,6 +240,7 @@ struct AttnXArgs {
     const int *slots, *lens;
     const int *last_pos;
     int len_imm;
+    int len_step;        // no lens / last_pos: token t attends to len_imm + len_step * t positions
     float *scores;       // [n][heads][max_len]
     int max_len;
     float *out;          // gated attention output
@@ -252,7 +253,7 @@ struct AttnXArgs {
 };
 
 Q35_DEV int attx_len(const AttnXArgs &a, int seq) {
-    return a.lens ? a.lens[seq] : (a.last_pos ? a.last_pos[0] + 1 : a.len_imm);
+    return a.lens ? a.lens[seq] : (a.last_pos ? a.last_pos[0] + 1 : a.len_imm + a.len_step * seq);
 }
 
 template <int G>
@@ -450,6 +451,186 @@ inline int attx_launch(const AttnXArgs &a, int nseq, int max_len, cudaStream_t s
                     attx_pv_smem(G), st, a);
 }
 
+
+// ---------------------------------------------------------------------------
+// Prefill-shaped causal attention: the same three steps for a run of
+// consecutive positions of ONE sequence (a prompt chunk), with the run's
+// tokens tiled ATTP_QT at a time so that each K chunk and each V tile is
+// loaded once per tile instead of once per token.  Token i of the run attends
+// to lens[i] positions.  Every per-element operation and its order is the
+// token-by-token kernels' (serial dots over dims, serial softmax sum, serial
+// P.V over positions), so the results are identical bit for bit.
+//   k_attp_scores: CTA (kv head, token tile, 32-position chunk), thread
+//     (token of the tile, position of the chunk), the group's G dots;
+//   k_attx_softmax: unchanged (a row per (head, token));
+//   k_attp_pv: CTA (kv head, token tile, 64-dim chunk), thread (token, dim)
+//     with the G heads' sums, V and probability tiles through a cp.async ring.
+// ---------------------------------------------------------------------------
+constexpr int ATTP_QT = 8;    // tokens per tile
+constexpr int ATTP_NST = 3;   // P.V tiles in flight
+
+inline size_t attp_scores_smem(int G) { return (size_t)(ATTX_CHUNK * ATTX_KLD + ATTP_QT * G * ATT_HD) * 4; }
+inline size_t attp_pv_smem(int G) { return (size_t)ATTP_NST * ATTX_PT * (ATTX_DIMS + ATTP_QT * G) * 4; }
+
+Q35_DEV int attp_len(const AttnXArgs &a, int t) { return attx_len(a, t); }
+
+template <int G>
+__global__ void __launch_bounds__(ATTX_CHUNK * ATTP_QT) k_attp_scores(const __grid_constant__ AttnXArgs a, int ntok) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float s_ps[];
+    float *s_k = s_ps;                                // [CHUNK][KLD]
+    float *s_q = s_ps + ATTX_CHUNK * ATTX_KLD;        // [QT][G][HD]
+    const int kvh = blockIdx.x, t0 = blockIdx.y * ATTP_QT, p0 = blockIdx.z * ATTX_CHUNK;
+    const int tid = threadIdx.x, ti = tid / ATTX_CHUNK, lane = tid - ti * ATTX_CHUNK;
+    const int nt = min(ATTP_QT, ntok - t0);
+    const int len_max = attp_len(a, t0 + nt - 1);  // positions ascend along the run
+    if (p0 >= len_max) return;
+    const int np = min(ATTX_CHUNK, len_max - p0);
+    const long long slot = a.slots ? a.slots[t0] : 0;
+    const float *kb = a.kc + slot * a.kv_slot + (long long)p0 * a.kv_dim + kvh * ATT_HD;
+    for (int idx = tid; idx < np * (ATT_HD / 4); idx += blockDim.x) {
+        const int r = idx / (ATT_HD / 4), c = idx - r * (ATT_HD / 4);
+        cp_async16(&s_k[r * ATTX_KLD + c * 4], kb + (long long)r * a.kv_dim + c * 4);
+    }
+    cp_async_commit();
+    for (int idx = tid; idx < nt * G * (ATT_HD / 4); idx += blockDim.x) {
+        const int i = idx / (G * ATT_HD / 4), rem = idx - i * (G * ATT_HD / 4);
+        const int g = rem / (ATT_HD / 4), c = rem - g * (ATT_HD / 4);
+        reinterpret_cast<float4 *>(s_q + (i * G + g) * ATT_HD)[c] =
+            reinterpret_cast<const float4 *>(a.q + (long long)(t0 + i) * a.q_tok + (long long)(kvh * G + g) * ATT_HD)[c];
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (ti >= nt || p0 + lane >= attp_len(a, t0 + ti)) return;
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) sc[g] = 0.0f;
+    const float4 *kr = reinterpret_cast<const float4 *>(s_k + lane * ATTX_KLD);
+    const float *qt = s_q + ti * G * ATT_HD;
+#pragma unroll 4
+    for (int c = 0; c < ATT_HD / 4; c++) {
+        const float4 kv = kr[c];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float4 qv = reinterpret_cast<const float4 *>(qt + g * ATT_HD)[c];
+            sc[g] = __fadd_rn(sc[g], __fmul_rn(qv.x, kv.x));
+            sc[g] = __fadd_rn(sc[g], __fmul_rn(qv.y, kv.y));
+            sc[g] = __fadd_rn(sc[g], __fmul_rn(qv.z, kv.z));
+            sc[g] = __fadd_rn(sc[g], __fmul_rn(qv.w, kv.w));
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        a.scores[((long long)(t0 + ti) * a.heads + kvh * G + g) * a.max_len + p0 + lane] = __fmul_rn(sc[g], a.scale);
+}
+
+template <int G>
+__global__ void __launch_bounds__(ATTP_QT * ATTX_DIMS) k_attp_pv(const __grid_constant__ AttnXArgs a, int ntok) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float s_pv[];
+    constexpr int PW = ATTP_QT * G;                              // probability rows per tile
+    float *s_v = s_pv;                                           // [NST][PT][DIMS]
+    float *s_p = s_pv + ATTP_NST * ATTX_PT * ATTX_DIMS;          // [NST][QT*G][PT]
+    const int kvh = blockIdx.x, t0 = blockIdx.y * ATTP_QT, dc = blockIdx.z;
+    const int tid = threadIdx.x, ti = tid / ATTX_DIMS, j = tid - ti * ATTX_DIMS;
+    const int nt = min(ATTP_QT, ntok - t0);
+    const int len_max = attp_len(a, t0 + nt - 1);
+    const int my_len = ti < nt ? attp_len(a, t0 + ti) : 0;
+    const long long slot = a.slots ? a.slots[t0] : 0;
+    const float *vb = a.vc + slot * a.kv_slot + kvh * ATT_HD + dc * ATTX_DIMS;
+    const int ntile = (len_max + ATTX_PT - 1) / ATTX_PT;
+    auto load_tile = [&](int k) {
+        if (k < ntile) {
+            const int q0 = k * ATTX_PT, np = min(ATTX_PT, len_max - q0);
+            float *dv = s_v + (k % ATTP_NST) * ATTX_PT * ATTX_DIMS;
+            float *dp = s_p + (k % ATTP_NST) * PW * ATTX_PT;
+            for (int idx = tid; idx < np * (ATTX_DIMS / 4); idx += blockDim.x) {
+                const int r = idx / (ATTX_DIMS / 4), c = idx - r * (ATTX_DIMS / 4);
+                cp_async16(dv + r * ATTX_DIMS + c * 4, vb + (long long)(q0 + r) * a.kv_dim + c * 4);
+            }
+            // probability rows: only positions a token attends to were written
+            for (int idx = tid; idx < nt * G * np; idx += blockDim.x) {
+                const int row = idx / np, r = idx - row * np;
+                const int i = row / G, g = row - i * G;
+                if (q0 + r < attp_len(a, t0 + i))
+                    cp_async4(dp + row * ATTX_PT + r,
+                              a.scores + ((long long)(t0 + i) * a.heads + kvh * G + g) * a.max_len + q0 + r);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int k = 0; k < ATTP_NST - 1; k++) load_tile(k);
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) acc[g] = 0.0f;
+    for (int k = 0; k < ntile; k++) {
+        cp_async_wait<ATTP_NST - 2>();
+        __syncthreads();
+        load_tile(k + ATTP_NST - 1);
+        const float *v = s_v + (k % ATTP_NST) * ATTX_PT * ATTX_DIMS + j;
+        const float *p = s_p + (k % ATTP_NST) * PW * ATTX_PT + ti * G * ATTX_PT;
+        const int nr = max(0, min(ATTX_PT, my_len - k * ATTX_PT));
+        for (int r = 0; r < nr; r++) {
+            const float vv = v[r * ATTX_DIMS];
+#pragma unroll
+            for (int g = 0; g < G; g++) acc[g] = __fadd_rn(acc[g], __fmul_rn(p[g * ATTX_PT + r], vv));
+        }
+    }
+    if (ti >= nt) return;
+    const long long tok = t0 + ti;
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const int h = kvh * G + g, dim = dc * ATTX_DIMS + j;
+        const float gt = a.gate[tok * a.q_tok + (long long)h * ATT_HD + dim];
+        const float o = __fmul_rn(acc[g], sigmoid_f(gt));
+        a.out[tok * a.out_tok + (long long)h * ATT_HD + dim] = o;
+        if (a.fam == 32) {
+            const int blk = (h * ATT_HD + dc * ATTX_DIMS) / 32 + (j >> 5);
+            quant_q8_0_warp(o, a.xq + tok * a.xq_ld + (long long)blk * 34, j & 31);
+        }
+    }
+}
+
+template <int G>
+inline int attp_launch_g(const AttnXArgs &a, int ntok, int max_len, cudaStream_t st) {
+    static bool ready = false;
+    if (!ready) {
+        int rc = (int)cudaFuncSetAttribute(k_attp_scores<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)attp_scores_smem(G));
+        if (!rc) rc = (int)cudaFuncSetAttribute(k_attp_pv<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)attp_pv_smem(G));
+        if (rc) return rc;
+        ready = true;
+    }
+    const unsigned tiles = (unsigned)((ntok + ATTP_QT - 1) / ATTP_QT);
+    Q35_TRY_RC(launch_k(k_attp_scores<G>, dim3((unsigned)a.kv_heads, tiles, (unsigned)((max_len + ATTX_CHUNK - 1) / ATTX_CHUNK)),
+                        dim3(ATTX_CHUNK * ATTP_QT), attp_scores_smem(G), st, a, ntok));
+    Q35_TRY_RC(attx_prepare(max_len));
+    Q35_TRY_RC(launch_k(k_attx_softmax, dim3((unsigned)a.heads, (unsigned)ntok), dim3(ATTX_SMT), (size_t)max_len * 4, st,
+                        a));
+    return launch_k(k_attp_pv<G>, dim3((unsigned)a.kv_heads, tiles, ATT_HD / ATTX_DIMS), dim3(ATTP_QT * ATTX_DIMS),
+                    attp_pv_smem(G), st, a, ntok);
+}
+
+// a run of ntok tokens of one sequence (a.slots[0..ntok) all the same slot,
+// or none: slot 0; lengths ascending: a.lens, or len_imm + len_step * t);
+// max_len bounds the lengths.  -1: this group size is not served
+inline int attp_launch(const AttnXArgs &a, int ntok, int max_len, cudaStream_t st) {
+    if (ntok <= 0) return 0;
+    if (a.kv_heads <= 0 || a.heads % a.kv_heads) return (int)cudaErrorInvalidValue;
+    if (max_len <= 0 || max_len > a.max_len) return (int)cudaErrorInvalidValue;
+    switch (a.heads / a.kv_heads) {
+    case 1: return attp_launch_g<1>(a, ntok, max_len, st);
+    case 2: return attp_launch_g<2>(a, ntok, max_len, st);
+    case 4: return attp_launch_g<4>(a, ntok, max_len, st);
+    case 6: return attp_launch_g<6>(a, ntok, max_len, st);
+    case 8: return attp_launch_g<8>(a, ntok, max_len, st);
+    default: return -1;
+    }
+}
 
 // ---------------------------------------------------------------------------
 // Fused decode attention for short contexts: prelude + scores + softmax +

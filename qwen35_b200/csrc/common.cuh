@@ -19,7 +19,7 @@ namespace q35 {
 
 // GGUF TensorType ids (the values of api.h / src/gguf.zig:87-122).
 enum : int {
-    TT_F32 = 0, TT_F16 = 1, TT_Q4_0 = 2, TT_Q8_0 = 8, TT_Q4_K = 12, TT_Q5_K = 13,
+    TT_F32 = 0, TT_F16 = 1, TT_Q4_0 = 2, TT_Q4_1 = 3, TT_Q5_0 = 6, TT_Q5_1 = 7, TT_Q8_0 = 8, TT_Q4_K = 12, TT_Q5_K = 13,
     TT_Q6_K = 14, TT_Q8_K = 15, TT_IQ4_NL = 20, TT_BF16 = 30,
     // engine-internal: Q6_K blocks padded from 210 to 224 bytes (same field
     // offsets, 14 zero bytes after d), so that rows are 16-byte multiples for
@@ -27,12 +27,29 @@ enum : int {
     TT_Q6_K_P = 0x1000 + 14,
 };
 
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 (32-element blocks, Q8_0 activation): offsets of
+// the fields in a block, GGUF layout (qs: element j < 16 in the low nibble of
+// byte j, element j + 16 in the high nibble; qh: bit 4 of element j in bit j)
+__host__ __device__ constexpr bool legacy_type(int tt) {
+    return tt == TT_Q4_0 || tt == TT_Q4_1 || tt == TT_Q5_0 || tt == TT_Q5_1;
+}
+__host__ __device__ constexpr bool legacy_affine(int tt) { return tt == TT_Q4_1 || tt == TT_Q5_1; }  // d and min
+__host__ __device__ constexpr bool legacy_five(int tt) { return tt == TT_Q5_0 || tt == TT_Q5_1; }    // qh plane
+__host__ __device__ constexpr int legacy_qh_off(int tt) { return legacy_affine(tt) ? 4 : 2; }
+__host__ __device__ constexpr int legacy_qs_off(int tt) {
+    return (legacy_affine(tt) ? 4 : 2) + (legacy_five(tt) ? 4 : 0);
+}
+
 // Native block geometry of the weight types this library serves.
 struct Geom { int elems, bytes, family; };  // family: 32 = Q8_0 act, 256 = Q8_K act
 __host__ __device__ inline Geom geom_of(int tt) {
     switch (tt) {
     case TT_Q8_0: return {32, 34, 32};
     case TT_IQ4_NL: return {32, 18, 32};
+    case TT_Q4_0: return {32, 18, 32};
+    case TT_Q4_1: return {32, 20, 32};
+    case TT_Q5_0: return {32, 22, 32};
+    case TT_Q5_1: return {32, 24, 32};
     case TT_Q4_K: return {256, 144, 256};
     case TT_Q5_K: return {256, 176, 256};
     case TT_Q6_K: return {256, 210, 256};

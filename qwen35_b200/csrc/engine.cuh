@@ -447,7 +447,12 @@ inline int eng_layer_full(q35b_engine *e, int li, int n, int nrun, int max_len, 
     a.fam = fo;
     a.xq = e->xq;
     a.xq_ld = e->xq_ld;
-    Q35_TRY(attx_launch(a, n, max_len, st));
+    // one run of several tokens (a prompt chunk of one sequence): the
+    // prefill-shaped kernels; otherwise (decode tokens, or several runs in one
+    // forward) a row per token
+    int arc = nrun == 1 && n > 1 ? attp_launch(a, n, max_len, st) : -1;
+    if (arc == -1) arc = attx_launch(a, n, max_len, st);
+    Q35_TRY(arc);
     if (fo != 32) {
         Q35_TRY(launch_k(k_quant_rows, dim3((q_dim / 256 + 7) / 8, n), dim3(256), 0, st, (const float *)e->gout,
                          (long long)q_dim, q_dim, fo, e->xq, e->xq_ld));

@@ -128,6 +128,63 @@ Q35_DEV void part_iq4_nl(const uint8_t *wb, const ActView &A, int ntok, int b, i
     }
 }
 
+// spread the 4 bits of x (bits 0..3) to bit 4 of bytes 0..3
+Q35_DEV uint32_t bits4_to_b4(uint32_t x) {
+    return ((x & 1u) | ((x & 2u) << 7) | ((x & 4u) << 14) | ((x & 8u) << 21)) << 4;
+}
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 block (GGUF layout): the 32 quantized values as
+// signed bytes -- lo[i] = elements 4i..4i+3, hi[i] = elements 16+4i.. --
+// centred (q - 8 / q - 16) for the symmetric types, raw q for the affine ones
+// (kernels32.c:297-340, 546-652)
+Q35_DEV void legacy_bytes(int tt, uint32_t qh, const uint32_t (&q)[4], uint32_t (&lo)[4], uint32_t (&hi)[4]) {
+    const bool five = legacy_five(tt), affine = legacy_affine(tt);
+    const uint32_t bias = five ? 0x10101010u : 0x08080808u;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        lo[i] = q[i] & 0x0F0F0F0Fu;
+        hi[i] = (q[i] >> 4) & 0x0F0F0F0Fu;
+        if (five) {
+            lo[i] |= bits4_to_b4((qh >> (4 * i)) & 0xFu);
+            hi[i] |= bits4_to_b4((qh >> (16 + 4 * i)) & 0xFu);
+        }
+        if (!affine) {
+            lo[i] = __vsub4(lo[i], bias);
+            hi[i] = __vsub4(hi[i], bias);
+        }
+    }
+}
+
+// is: sum of q * y; ms (affine types): sum of the 32 activation values
+template <int NT>
+Q35_DEV void part_legacy(int tt, const uint8_t *wb, const ActView &A, int ntok, int b, int (&is)[NT],
+                         int (&ms)[NT]) {
+    uint32_t q[4], lo[4], hi[4], h[1] = {0u};
+    lds_words_a2<4>(wb + legacy_qs_off(tt), q);
+    if (legacy_five(tt)) lds_words_a2<1>(wb + legacy_qh_off(tt), h);
+    legacy_bytes(tt, h[0], q, lo, hi);
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        if (t < ntok) {
+            const uint4 y0 = A.q16(t, b * 32), y1 = A.q16(t, b * 32 + 16);
+            int s = dot4x4(lo[0], lo[1], lo[2], lo[3], y0, 0);
+            is[t] = dot4x4(hi[0], hi[1], hi[2], hi[3], y1, s);
+            if (legacy_affine(tt)) {
+                constexpr uint32_t one = 0x01010101u;
+                ms[t] = dot4x4(one, one, one, one, y1, dot4x4(one, one, one, one, y0, 0));
+            }
+        }
+    }
+}
+
+// f32 term of one legacy block (kernels32.c:313, 338): dx*dy*sumi, plus
+// mx*dy*sumy for the affine types, added as one term
+Q35_DEV float legacy_term(int tt, const uint8_t *wb, float dy, int is, int ms) {
+    const float t0 = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb)), dy), __int2float_rn(is));
+    if (!legacy_affine(tt)) return t0;
+    return __fadd_rn(t0, __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb + 2)), dy), __int2float_rn(ms)));
+}
+
 // Q4_K / Q5_K: part c covers elements [64c, 64c+64) = sub-blocks 2c, 2c+1
 template <int NT, bool Q5>
 Q35_DEV void part_q45_k(const uint8_t *wb, const ActView &A, int ntok, int b, int c, int (&is)[NT],
@@ -229,8 +286,10 @@ Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, 
             if (LPB == 1) {
                 if (tt == TT_Q8_0)
                     part_q8_0<NT>(wb, A, ntok, b, is);
-                else
+                else if (tt == TT_IQ4_NL)
                     part_iq4_nl<NT>(wb, A, ntok, b, is);
+                else
+                    part_legacy<NT>(tt, wb, A, ntok, b, is, ms);
             } else {
                 if (tt == TT_Q4_K)
                     part_q45_k<NT, false>(wb, A, ntok, b, p, is, ms);
@@ -257,6 +316,8 @@ Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, 
                     if (tt == TT_Q8_0 || tt == TT_IQ4_NL) {
                         // sumf += dx * dy * (float)sumi
                         term = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb)), A.dsc(t, b)), __int2float_rn(is[t]));
+                    } else if (legacy_type(tt)) {
+                        term = legacy_term(tt, wb, A.dsc(t, b), is[t], ms[t]);
                     } else if (tt == TT_Q6_K || tt == TT_Q6_K_P) {
                         // sumf += d_w * dy * (float)isum
                         term = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb + 208)), A.dsc(t, b)), __int2float_rn(is[t]));
@@ -423,7 +484,7 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
         const uintptr_t start = reinterpret_cast<uintptr_t>(sg.w) + (uintptr_t)r0 * sg.row_bytes;
         const uint8_t *buf = stages + (size_t)s * stage_ld + (start & 15);
         const int nb = a.cols / geom_of(sg.ttype).elems;
-        const bool lpb1 = sg.ttype == TT_Q8_0 || sg.ttype == TT_IQ4_NL;
+        const bool lpb1 = geom_of(sg.ttype).elems == 32;
         for (int rg = warp * R; rg < nr; rg += GV_WARPS * R) {
             const int nv = min(R, nr - rg);
             if (lpb1)

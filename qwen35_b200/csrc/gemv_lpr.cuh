@@ -323,6 +323,67 @@ Q35_DEV void lpr_iq4_nl(const uint8_t *rp, const ActView &A, int ntok, int gb0, 
     }
 }
 
+// u32 at an even byte offset o of a register copy of 16-byte-aligned words
+template <int N>
+Q35_DEV uint32_t w32_at(const uint32_t (&W)[N], int o) {
+    return (o & 3) == 0 ? W[o >> 2] : __funnelshift_r(W[o >> 2], W[(o >> 2) + 1], 16);
+}
+template <int N>
+Q35_DEV float f16_at_w(const uint32_t (&W)[N], int o) {
+    return (o & 3) == 0 ? f16_lo(W[o >> 2]) : f16_hi(W[o >> 2]);
+}
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 (18 / 20 / 22 / 24-byte blocks): 8 blocks of a
+// 256-column chunk (144 / 160 / 176 / 192 bytes, 16-byte multiples) in
+// registers; per block the signed bytes of legacy_bytes, dot products with
+// the Q8_0 activation, the f32 term of kernels32.c (legacy_term's steps)
+template <int NT, int TT, class Sink>
+Q35_DEV void lpr_legacy(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
+    constexpr int B = TT == TT_Q4_0 ? 18 : TT == TT_Q4_1 ? 20 : TT == TT_Q5_0 ? 22 : 24;
+    constexpr int NW = 2 * B;  // words of 8 blocks
+    constexpr int QS = legacy_qs_off(TT), QH = legacy_qh_off(TT);
+    constexpr bool AFF = legacy_affine(TT), FIVE = legacy_five(TT);
+    for (int g = 0; g < nblk; g += 8) {
+        uint32_t W[NW + 1];
+        const uint4 *s = reinterpret_cast<const uint4 *>(rp + g * B);
+#pragma unroll
+        for (int i = 0; i < NW / 4; i++) {
+            const uint4 v = s[i];
+            W[4 * i] = v.x;
+            W[4 * i + 1] = v.y;
+            W[4 * i + 2] = v.z;
+            W[4 * i + 3] = v.w;
+        }
+        W[NW] = 0u;  // read by the funnel shift of the last block's last word, never used
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int o = B * k;
+            const float dx = f16_at_w(W, o);
+            const float mx = AFF ? f16_at_w(W, o + 2) : 0.0f;
+            uint32_t q[4], lo[4], hi[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) q[i] = w32_at(W, o + QS + 4 * i);
+            legacy_bytes(TT, FIVE ? w32_at(W, o + QH) : 0u, q, lo, hi);
+            const int b = gb0 + g + k;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t < ntok) {
+                    const uint4 y0 = A.q16(t, b * 32), y1 = A.q16(t, b * 32 + 16);
+                    const int si = dot4x4(hi[0], hi[1], hi[2], hi[3], y1, dot4x4(lo[0], lo[1], lo[2], lo[3], y0, 0));
+                    const float dy = A.dsc(t, b);
+                    float term = __fmul_rn(__fmul_rn(dx, dy), __int2float_rn(si));
+                    if (AFF) {
+                        constexpr uint32_t one = 0x01010101u;
+                        const int sy = dot4x4(one, one, one, one, y1, dot4x4(one, one, one, one, y0, 0));
+                        term = __fadd_rn(term, __fmul_rn(__fmul_rn(mx, dy), __int2float_rn(sy)));
+                    }
+                    sk.put(t, b, term);
+                }
+            }
+        }
+    }
+}
+
 // Q4_K (144 B: d|dmin, 12 scale bytes, 128 qs) and Q5_K (176 B: d|dmin,
 // scales, 32 qh, 128 qs); both 16-byte multiples, so every block of the
 // chunk starts 16-byte aligned.
@@ -466,6 +527,10 @@ Q35_DEV void lpr_chunk(int tt, const uint8_t *rp, const ActView &A, int ntok, in
     switch (tt) {
     case TT_Q8_0: lpr_q8_0<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_IQ4_NL: lpr_iq4_nl<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_Q4_0: lpr_legacy<NT, TT_Q4_0>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_Q4_1: lpr_legacy<NT, TT_Q4_1>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_Q5_0: lpr_legacy<NT, TT_Q5_0>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_Q5_1: lpr_legacy<NT, TT_Q5_1>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_Q4_K: lpr_q45_k<NT, false>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
     case TT_Q6_K_P: lpr_q6_k<NT>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
     default: lpr_q45_k<NT, true>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
@@ -765,7 +830,7 @@ inline int gemv_lpr_prepare() {
 }
 
 inline bool lpr_type_ok(int tt) {
-    return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K || tt == TT_Q6_K_P;
+    return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K || tt == TT_Q6_K_P || legacy_type(tt);
 }
 
 // f32 rows the launch quantizes itself (see LprArgs::prologue)

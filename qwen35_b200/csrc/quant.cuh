@@ -111,6 +111,24 @@ Q35_DEV float dequant_elem(int tt, const uint8_t *row, int i) {
         const int nib = j < 16 ? (x[2 + j] & 0xF) : (x[2 + j - 16] >> 4);
         return __fmul_rn(f16_to_f32(ld_u16(x)), (float)c_iq4nl[nib]);
     }
+    case TT_Q4_0:
+    case TT_Q4_1:
+    case TT_Q5_0:
+    case TT_Q5_1: {
+        // quant_dequant.zig:78-103 (Q4_0: (q - 8) * d; Q4_1: q * d + m); Q5
+        // likewise with 5-bit q, centred at 16 for Q5_0
+        const uint8_t *x = row + (i / 32) * geom_of(tt).bytes;
+        const int j = i & 31;
+        const uint8_t *qs = x + legacy_qs_off(tt);
+        int q = j < 16 ? (qs[j] & 0xF) : (qs[j - 16] >> 4);
+        if (legacy_five(tt)) {
+            const uint8_t *h = x + legacy_qh_off(tt);
+            q |= ((h[j >> 3] >> (j & 7)) & 1) << 4;
+        }
+        const float d = f16_to_f32(ld_u16(x));
+        if (legacy_affine(tt)) return __fadd_rn(__fmul_rn((float)q, d), f16_to_f32(ld_u16(x + 2)));
+        return __fmul_rn(__fsub_rn((float)q, legacy_five(tt) ? 16.0f : 8.0f), d);
+    }
     case TT_Q4_K:
     case TT_Q5_K: {
         const bool q5 = tt == TT_Q5_K;
@@ -207,6 +225,55 @@ Q35_DEV void wq_iq4_nl(const float *x, uint8_t *y) {
         idx[i] = (uint8_t)best;
     }
     for (int j = 0; j < 16; j++) y[2 + j] = (uint8_t)(idx[j] | (idx[j + 16] << 4));
+}
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 encoders of this project (the oracle's
+// wq_legacy_block, operation for operation): d from the value of largest
+// magnitude (Q4_0 / Q5_0) or the range (Q4_1 / Q5_1), rounded to f16, the
+// elements quantized against the rounded scale, GGUF nibble / qh layout
+Q35_DEV void wq_legacy(int tt, const float *x, uint8_t *y) {
+    const bool affine = legacy_affine(tt), five = legacy_five(tt);
+    const int qmax = five ? 31 : 15;
+    uint8_t q[32];
+    if (affine) {
+        float mn = x[0], mx = x[0];
+        for (int i = 1; i < 32; i++) {
+            if (x[i] < mn) mn = x[i];
+            if (x[i] > mx) mx = x[i];
+        }
+        const uint16_t dh = f16_ieee(__fdiv_rn(__fsub_rn(mx, mn), (float)qmax)), mh = f16_ieee(mn);
+        const float dr = f16_to_f32(dh), mr = f16_to_f32(mh);
+        const float id = dr != 0.0f ? __fdiv_rn(1.0f, dr) : 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const int v = (int)__fadd_rn(__fmul_rn(__fsub_rn(x[i], mr), id), 0.5f);
+            q[i] = (uint8_t)(v < 0 ? 0 : (v > qmax ? qmax : v));
+        }
+        y[0] = (uint8_t)(dh & 0xFF); y[1] = (uint8_t)(dh >> 8);
+        y[2] = (uint8_t)(mh & 0xFF); y[3] = (uint8_t)(mh >> 8);
+    } else {
+        float amax = 0.0f, vmax = 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const float a = fabsf(x[i]);
+            if (a > amax) { amax = a; vmax = x[i]; }
+        }
+        const float half = five ? 16.0f : 8.0f;
+        const uint16_t dh = f16_ieee(__fdiv_rn(vmax, -half));
+        const float dr = f16_to_f32(dh);
+        const float id = dr != 0.0f ? __fdiv_rn(1.0f, dr) : 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const int v = (int)__fadd_rn(__fmul_rn(x[i], id), __fadd_rn(half, 0.5f));
+            q[i] = (uint8_t)(v < 0 ? 0 : (v > qmax ? qmax : v));
+        }
+        y[0] = (uint8_t)(dh & 0xFF); y[1] = (uint8_t)(dh >> 8);
+    }
+    if (five) {
+        uint32_t qh = 0;
+        for (int j = 0; j < 32; j++) qh |= (uint32_t)((q[j] >> 4) & 1) << j;
+        uint8_t *h = y + legacy_qh_off(tt);
+        h[0] = (uint8_t)qh; h[1] = (uint8_t)(qh >> 8); h[2] = (uint8_t)(qh >> 16); h[3] = (uint8_t)(qh >> 24);
+    }
+    uint8_t *qs = y + legacy_qs_off(tt);
+    for (int j = 0; j < 16; j++) qs[j] = (uint8_t)((q[j] & 0x0F) | ((q[j + 16] & 0x0F) << 4));
 }
 
 Q35_DEV void wq_kq(const float *x, uint8_t *y, bool q5) {
@@ -317,6 +384,10 @@ __global__ void k_quantize_weight(int tt, const float *__restrict__ x, uint8_t *
     switch (tt) {
     case TT_Q8_0: wq_q8_0(xb, yb); break;
     case TT_IQ4_NL: wq_iq4_nl(xb, yb); break;
+    case TT_Q4_0:
+    case TT_Q4_1:
+    case TT_Q5_0:
+    case TT_Q5_1: wq_legacy(tt, xb, yb); break;
     case TT_Q4_K: wq_kq(xb, yb, false); break;
     case TT_Q5_K: wq_kq(xb, yb, true); break;
     case TT_Q6_K: wq_q6_k(xb, yb); break;

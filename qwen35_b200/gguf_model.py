@@ -24,7 +24,8 @@ import torch
 from .model import TT, ModelConfig, tensor_plan
 
 ARCH = "qwen35"
-LINEAR_TYPES = {TT["Q8_0"], TT["IQ4_NL"], TT["Q4_K"], TT["Q5_K"], TT["Q6_K"]}
+LINEAR_TYPES = {TT["Q8_0"], TT["IQ4_NL"], TT["Q4_K"], TT["Q5_K"], TT["Q6_K"], TT["Q4_0"], TT["Q4_1"], TT["Q5_0"],
+                TT["Q5_1"]}
 F16, BF16 = 1, 30
 
 
@@ -113,7 +114,7 @@ class GGUFModel:
                 self.tensors[t.name] = (tt, rows, cols, dev)
             else:
                 raise ValueError(f"{t.name}: GGUF tensor type {tt} is not supported by this backend "
-                                 "(linear layers: Q8_0, IQ4_NL, Q4_K, Q5_K, Q6_K)")
+                                 "(linear layers: Q8_0, IQ4_NL, Q4_K, Q5_K, Q6_K, Q4_0, Q4_1, Q5_0, Q5_1)")
         missing = sorted(set(plan) - set(self.tensors) - {"output.weight"})
         if missing:
             raise ValueError(f"GGUF file lacks {len(missing)} decoder tensors, e.g. {missing[:3]}")

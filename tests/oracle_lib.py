@@ -15,8 +15,10 @@ ORACLE_DIR = os.path.join(ROOT, "oracle")
 ORACLE_SO = os.path.join(ORACLE_DIR, "_build", "liboracle.so")
 REF_SO = os.path.join(ORACLE_DIR, "_ref", "libq35ref.so")
 
-TT = {"F32": 0, "Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q8_K": 15, "IQ4_NL": 20}
-GEOM = {8: (32, 34), 2: (32, 18), 20: (32, 18), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
+TT = {"F32": 0, "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
+      "Q8_K": 15, "IQ4_NL": 20}
+GEOM = {8: (32, 34), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18), 12: (256, 144),
+        13: (256, 176), 14: (256, 210)}
 
 f32p = ctypes.POINTER(ctypes.c_float)
 u8p = ctypes.POINTER(ctypes.c_uint8)

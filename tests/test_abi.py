@@ -70,7 +70,9 @@ def test_loads_and_binds_without_gpu(built):
     e, b = ctypes.c_int(), ctypes.c_int()
     assert L.q35_quant_geom(8, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (32, 34)
     assert L.q35_quant_geom(14, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (256, 210)
-    assert L.q35_quant_geom(3, ctypes.byref(e), ctypes.byref(b)) == 0
+    assert L.q35_quant_geom(3, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (32, 20)  # Q4_1
+    assert L.q35_quant_geom(7, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (32, 24)  # Q5_1
+    assert L.q35_quant_geom(16, ctypes.byref(e), ctypes.byref(b)) == 0  # IQ2_XXS: not served
     assert L.q35_quant_act_block_elems(20) == 32 and L.q35_quant_act_block_elems(13) == 256
     assert L.q35_quant_act_block_elems(99) == 0
     assert L.q35_mmq_dp4a_wants(12) == 0
@@ -91,7 +93,7 @@ def test_bad_shapes_rejected(built):
     L = q35lib.load()
     inv = 1  # cudaErrorInvalidValue
     assert L.q35_launch_mul_mat_vec(None, None, None, 4, 100, 1, 8, None) == inv   # cols % 32
-    assert L.q35_launch_mul_mat_vec(None, None, None, 4, 256, 1, 3, None) == inv   # unknown type
+    assert L.q35_launch_mul_mat_vec(None, None, None, 4, 256, 1, 16, None) == inv  # unknown type (IQ2_XXS)
     assert L.q35_launch_gdn_step_rows(None, 0, None, 0, None, 0, None, 0, None, None, None, None, None,
                                       4, 2, 64, 64, None) == inv                     # kd != 128
     assert L.q35_launch_dequantize_row(8, None, None, 33, None) == inv

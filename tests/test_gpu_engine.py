@@ -76,7 +76,7 @@ def _run_parity(q35, cfg_name, prompt_len, n_gen, seed=1, threads=None, cr_exp=F
     return toks_gpu, toks_cpu, worst_logit, worst_layer
 
 
-@pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed"])
+@pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed", "tiny-legacy"])
 def test_engine_matches_oracle(q35, cfg_name):
     tg, tc, wl, wlay = _run_parity(q35, cfg_name, prompt_len=7, n_gen=12)
     assert wl < 1e-3 and wlay < 1e-3, (wl, wlay)

@@ -296,7 +296,7 @@ def test_gemv_golden_rows(L, O):
     """the reference's udtest rows (96 x 256) through the device GEMV"""
     gold = os.path.join(ROOT, "tests", "golden", "udtest")
     ax = np.fromfile(os.path.join(gold, "A_x.f32"), dtype=np.float32)
-    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144)]:
+    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144), ("Q4_0", 144)]:
         tt = TT[name]
         rows = np.fromfile(os.path.join(gold, f"{name}.bin"), dtype=np.uint8).reshape(-1, rb)
         exp = np.fromfile(os.path.join(gold, f"{name}_expected.f32"), dtype=np.float32)
@@ -635,4 +635,44 @@ def test_bounded_wait_ends_with_an_error_not_a_hang(L):
     # the context is still usable: a GEMV runs and is exact
     got, ref = _gemv_case(L, load_oracle(), "Q8_0", 64, 512, 1, seed=3)
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    assert_no_kernel_error(L)
+
+
+LEGACY = ["Q4_0", "Q4_1", "Q5_0", "Q5_1"]
+
+
+@pytest.mark.parametrize("name", LEGACY)
+def test_legacy_encoder_and_dequant_bit_exact(L, O, name):
+    """Q4_0 / Q4_1 / Q5_0 / Q5_1: the device weight encoder gives the oracle's
+    bytes, and the device dequantizer its values (GGUF nibble layout)"""
+    tt = TT[name]
+    rng = np.random.default_rng(31)
+    w = (rng.standard_normal((16, 1024)) * 0.05).astype(np.float32)
+    w[0, :64] = 0.0
+    w[1, :32] = 3.0
+    ref = quantize_weight(O, tt, w)
+    e, b = GEOM[tt]
+    out = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+    ok(L.q35b_quantize_weight(tt, dev(w).data_ptr(), out.data_ptr(), w.size // e, S))
+    assert np.array_equal(host(out).reshape(ref.shape), ref)
+    deq = dequant(O, tt, ref, 1024)
+    wd = dev(ref)
+    for r in range(16):
+        o = torch.zeros(1024, dtype=torch.float32, device="cuda")
+        ok(L.q35_launch_dequantize_row(tt, wd[r].data_ptr(), o.data_ptr(), 1024, S))
+        assert np.array_equal(host(o).view(np.uint32), deq[r].view(np.uint32))
+    # the encoding is close to the input (a round trip of the format)
+    assert np.abs(deq - w).max() <= np.abs(w).max() * (0.15 if name.startswith("Q4") else 0.08)
+
+
+@pytest.mark.parametrize("name", LEGACY)
+@pytest.mark.parametrize("tokens", [1, 3, 8, 16, 37])
+def test_legacy_gemv_bit_exact(L, O, name, tokens):
+    """Q4_0 / Q4_1 / Q5_0 / Q5_1 through q35_launch_mul_mat_vec: the
+    lane-per-row kernel (cols % 256 == 0, passes of up to 8 tokens; the MMQ
+    declines these types) and the block-splitting kernel (cols % 256 != 0,
+    unaligned base) against the reference scalar tier's fold, bit for bit"""
+    for rows, cols in [(300, 1024), (64, 3584), (129, 2048), (10000, 512), (77, 2080)]:
+        got, ref = _gemv_case(L, O, name, rows, cols, tokens, seed=rows + 3 * tokens)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (name, rows, cols, tokens)
     assert_no_kernel_error(L)

@@ -59,7 +59,7 @@ def test_golden_rowdot_matches_dequant(L):
     here on the quantized activation the matvec path consumes: the only
     difference left is the f32 block fold, so the bar is 1e-5 relative."""
     ax = np.fromfile(os.path.join(GOLD, "A_x.f32"), dtype=np.float32)
-    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144)]:
+    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144), ("Q4_0", 144)]:
         tt = TT[name]
         rows = np.fromfile(os.path.join(GOLD, f"{name}.bin"), dtype=np.uint8).reshape(-1, rb)
         xq = quantize_act(L, tt, ax)
@@ -255,7 +255,18 @@ import ctypes, sys, numpy as np
 sys.path.insert(0, sys.argv[1])
 from oracle_lib import load_oracle, load_ref, quantize_weight, TT, fp, bp, row_bytes, act_row_bytes
 O = load_oracle(); R = ctypes.CDLL(sys.argv[2])
-for nm in ("q8_0_q8_0","iq4_nl_q8_0","q4_k_q8_k","q5_k_q8_k","q6_k_q8_k"):
+def interleave_q5(w, tt):
+    # GGUF Q5_0 / Q5_1 blocks -> the nibble order the reference's scalar
+    # kernels read (element j in nibble j & 1 of qs[j / 2])
+    b = 22 if tt == "Q5_0" else 24
+    off = 6 if tt == "Q5_0" else 8
+    w = w.reshape(-1, b).copy()
+    qs = w[:, off:off + 16]
+    q = np.concatenate([qs & 0x0F, qs >> 4], axis=1)  # element order 0..31
+    w[:, off:off + 16] = (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
+    return w.reshape(-1)
+for nm in ("q8_0_q8_0","iq4_nl_q8_0","q4_k_q8_k","q5_k_q8_k","q6_k_q8_k","q4_0_q8_0","q4_1_q8_0","q5_0_q8_0",
+           "q5_1_q8_0"):
     getattr(R, nm).restype = ctypes.c_float
     getattr(R, nm).argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
 R.quantize_q8_0.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
@@ -271,10 +282,13 @@ for trial in range(40):
     ak = np.zeros(cols // 256 * 292, np.uint8); bk = np.zeros_like(ak)
     R.quantize_q8_K(cols, x.ctypes.data, ak.ctypes.data); O.q35o_quantize_q8_K(cols, fp(x), bp(bk))
     bad += (not np.array_equal(a0, b0)) + (not np.array_equal(ak, bk))
-    for nm, tt in (("q8_0_q8_0","Q8_0"),("iq4_nl_q8_0","IQ4_NL"),("q4_k_q8_k","Q4_K"),("q5_k_q8_k","Q5_K"),("q6_k_q8_k","Q6_K")):
+    for nm, tt in (("q8_0_q8_0","Q8_0"),("iq4_nl_q8_0","IQ4_NL"),("q4_k_q8_k","Q4_K"),("q5_k_q8_k","Q5_K"),
+                   ("q6_k_q8_k","Q6_K"),("q4_0_q8_0","Q4_0"),("q4_1_q8_0","Q4_1"),("q5_0_q8_0","Q5_0"),
+                   ("q5_1_q8_0","Q5_1")):
         w = quantize_weight(O, TT[tt], rng.standard_normal((1, cols)).astype(np.float32) * 0.02)[0]
-        xq = a0 if tt in ("Q8_0","IQ4_NL") else ak
-        r = np.float32(getattr(R, nm)(cols, w.ctypes.data, xq.ctypes.data))
+        xq = a0 if tt in ("Q8_0","IQ4_NL","Q4_0","Q4_1","Q5_0","Q5_1") else ak
+        wr = interleave_q5(w, tt) if (tt in ("Q5_0","Q5_1") and sys.argv[3] == "exact") else w
+        r = np.float32(getattr(R, nm)(cols, wr.ctypes.data, xq.ctypes.data))
         o = np.float32(O.q35o_vec_dot(TT[tt], cols, bp(w), bp(xq)))
         if sys.argv[3] == "exact":
             bad += int(r.view(np.uint32) != o.view(np.uint32))
@@ -298,13 +312,21 @@ def _run_ref(mode):
 
 @pytest.mark.skipif(not os.path.exists(REF_SO), reason="reference kernels not built (no reference tree)")
 def test_against_reference_kernels_scalar_tier():
-    """Oracle == reference x86 kernels' scalar tier, bit for bit."""
+    """Oracle == reference x86 kernels' scalar tier, bit for bit, for the
+    five hot types and Q4_0 / Q4_1 / Q5_0 / Q5_1.  The reference's scalar
+    Q5_0 / Q5_1 kernels read element j from nibble j & 1 of qs[j / 2]
+    (kernels32.c:557, 640), unlike its AVX2 kernels and the GGUF format (low
+    nibbles are elements 0..15): they are fed the same weights in that order,
+    so the arithmetic is pinned bit for bit and the layout by the default
+    tier below."""
     assert _run_ref("exact") == 0
 
 
 @pytest.mark.skipif(not os.path.exists(REF_SO), reason="reference kernels not built (no reference tree)")
 def test_against_reference_kernels_default_tier():
-    """The default (AVX2/VNNI) tier reorders the Q8_0 f32 fold; within 1e-5."""
+    """The default (AVX2/VNNI) tier reorders the f32 folds (FMA lanes); within
+    1e-5.  Q5_0 / Q5_1 here run the reference's AVX2 unpack, the GGUF nibble
+    layout, on the oracle's weights as they are."""
     assert _run_ref("default") == 0
 
 
