@@ -610,12 +610,13 @@ def _timed_loop(torch, launch, n_rot, target_ms=40.0):
     return ms, reps
 
 
-def sweep_gemv(L, hbm):
+def sweep_gemv(L, hbm, only=None):
     """quantized matvec / MMQ over BASELINE config 2: seeded N(0,1) f32
     weights [in, out] encoded on the device (q35b_quantize_weight), f32
     N(0,1) activations quantized by the activation quantizer of the weight's
     family, timed through q35_launch_mul_mat_vec.  Weight copies are rotated
-    so that at least 3x L2 of distinct weight bytes pass between reuses."""
+    so that at least 3x L2 of distinct weight bytes pass between reuses.
+    only: "TYPE:INxOUT:TOKENS" runs that one case."""
     import numpy as np
     import torch
     from qwen35_b200.lib import GEOM, TT
@@ -624,6 +625,9 @@ def sweep_gemv(L, hbm):
     g = torch.Generator(device="cuda")
     for cols, rows in SWEEP_SHAPES:
         for tname in SWEEP_TYPES:
+            cases = [t for t in SWEEP_TOKENS if only is None or only == f"{tname}:{cols}x{rows}:{t}"]
+            if not cases:
+                continue
             tt = TT[tname]
             e, b = GEOM[tt]
             row_bytes = cols // e * b
@@ -639,7 +643,7 @@ def sweep_gemv(L, hbm):
                 wq[i * pitch:i * pitch + mbytes].copy_(wq[:mbytes])
             fam = 32 if e == 32 else 256
             abytes = cols // fam * (34 if fam == 32 else 292)
-            for ntok in SWEEP_TOKENS:
+            for ntok in cases:
                 x = torch.randn(ntok * cols, device="cuda", generator=g)
                 xq = torch.empty(ntok * abytes, dtype=torch.uint8, device="cuda")
                 quant = L.q35_launch_quantize_q8_0 if fam == 32 else L.q35_launch_quantize_q8_K
@@ -864,7 +868,7 @@ def main():
     ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "all"], default=None,
                     help="isolated kernel sweeps (BASELINE configs 2 / 3; mmq: the 4B / 27B batched-decode "
                          "matrices) instead of the decode bench")
-    ap.add_argument("--sweep-case", default=None, help="--sweep mmq: one case, TYPE:INxOUT:TOKENS")
+    ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -898,7 +902,7 @@ def main():
         L = qlib.load()
         hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
         if args.sweep in ("gemv", "all"):
-            sweep_gemv(L, hbm)
+            sweep_gemv(L, hbm, args.sweep_case)
         if args.sweep in ("gdn", "all"):
             sweep_gdn(L, hbm)
         if args.sweep in ("mmq", "all"):
