@@ -294,7 +294,7 @@ int q35_launch_gdn_step_wy(float *d_state, int state_stride, const float *d_k, i
     a.gamma = d_gamma; a.g_tok = gamma_stride;
     a.beta = d_beta; a.b_tok = beta_stride;
     a.heads = heads; a.nk = nk; a.rows = rows;
-    return gdn_wy_rows_launch(a, S(stream));
+    return gdn_wy_cols_launch(a, S(stream));
 }
 int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
                              int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,

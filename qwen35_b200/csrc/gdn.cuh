@@ -683,6 +683,174 @@ inline int gdn_wy_rows_launch(const GdnArgs &a, cudaStream_t st) {
     return (int)cudaGetLastError();
 }
 
+// The API's WY prefill with each head's state columns split over WY_NCB CTAs
+// (WY_CB columns each).  The delta rule updates every value column on its
+// own (km_j, delta_j and column j of S involve only column j), so the split
+// needs no exchange; each CTA recomputes the chunk's shared quantities
+// (cumulative decay, A, M: wy_chunk's code, so the same values) and runs the
+// per-column steps for its columns with the threads spread over (token,
+// column) and (state row, column) pairs, every dot and chain in wy_chunk's
+// order.  The results equal k_gdn_wy_rows' bit for bit; a 16-head sequence
+// runs on 16 x WY_NCB SMs instead of 16.
+constexpr int WY_CB = 16;                      // state columns per CTA
+constexpr int WY_NCB = GDN_KD / WY_CB;         // CTAs per head
+constexpr int WY_CLD = WY_CB + 1;              // pitch of the per-column tiles (floats)
+constexpr size_t WY_COLS_SMEM = (size_t)2 * WY_C * WY_LD * 4             // Qs, Ks
+                                + (size_t)4 * WY_C * WY_CLD * 4         // Vc, Uc, Wc, Dc
+                                + (size_t)WY_C * WY_CLD * 4             // Ec: eE[t] * delta
+                                + (size_t)GDN_KD * WY_CLD * 4           // state columns
+                                + (size_t)2 * WY_C * (WY_C + 1) * 4     // Am, Mm
+                                + (size_t)6 * WY_C * 4;                 // Lc, eL, eE, bet, lg
+
+__global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ GdnArgs a) {
+    extern __shared__ __align__(128) float smc[];
+    float *Qs = smc, *Ks = Qs + WY_C * WY_LD;
+    float *Vc = Ks + WY_C * WY_LD, *Uc = Vc + WY_C * WY_CLD, *Wc = Uc + WY_C * WY_CLD, *Dc = Wc + WY_C * WY_CLD;
+    float *Ec = Dc + WY_C * WY_CLD, *Sc = Ec + WY_C * WY_CLD;
+    float *Am = Sc + GDN_KD * WY_CLD, *Mm = Am + WY_C * (WY_C + 1);
+    float *Lc = Mm + WY_C * (WY_C + 1), *eL = Lc + WY_C, *eE = eL + WY_C, *bet = eE + WY_C, *lg = bet + WY_C;
+    const int h = blockIdx.x / WY_NCB, cb = blockIdx.x - h * WY_NCB, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int kh = h % a.nk, c0 = cb * WY_CB;
+    const int jj = tid & (WY_CB - 1), tg = tid / WY_CB;  // (token group, column) of the pair loops
+    constexpr int NTG = GDN_KD / WY_CB;                    // token groups
+    float *S = a.state + h * a.state_head;
+    for (int idx = tid; idx < GDN_KD * WY_CB; idx += GDN_KD) {
+        const int i = idx / WY_CB, c = idx - i * WY_CB;
+        Sc[i * WY_CLD + c] = S[(long long)i * GDN_KD + c0 + c];
+    }
+    for (int t0 = 0; t0 < a.rows; t0 += WY_C) {
+        const int nc = min(WY_C, a.rows - t0);
+        for (int t = 0; t < nc; t++) {
+            const long long tok = t0 + t;
+            Qs[t * WY_LD + tid] = a.q[tok * a.q_tok + kh * a.q_head + tid];
+            Ks[t * WY_LD + tid] = a.k[tok * a.k_tok + kh * a.k_head + tid];
+        }
+        for (int idx = tid; idx < nc * WY_CB; idx += GDN_KD) {
+            const int t = idx / WY_CB, c = idx - t * WY_CB;
+            Vc[t * WY_CLD + c] = a.v[(t0 + t) * a.v_tok + h * a.v_head + c0 + c];
+        }
+        if (tid < nc) {
+            const long long tok = t0 + tid;
+            lg[tid] = fmaxf(logf(a.gamma ? a.gamma[tok * a.g_tok + h] : a.gamma_imm), WY_LOG_MIN);
+            bet[tid] = a.beta ? a.beta[tok * a.b_tok + h] : a.beta_imm;
+        }
+        __syncthreads();
+        if (tid == GDN_KD - 1) {  // wy_cumulate
+            float L = 0.0f;
+            for (int t = 0; t < nc; t++) {
+                L = __fadd_rn(L, lg[t]);
+                Lc[t] = L;
+            }
+        }
+        __syncthreads();
+        if (tid < nc) {
+            eL[tid] = expf(Lc[tid]);
+            eE[tid] = expf(Lc[nc - 1] - Lc[tid]);
+        }
+        // U = S0^T k_t, W = S0^T q_t for (token, column) pairs; wy_chunk's
+        // four partial sums per dot
+        for (int t = tg; t < nc; t += NTG) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(Ks + t * WY_LD);
+            const float4 *q4 = reinterpret_cast<const float4 *>(Qs + t * WY_LD);
+            const float *sc = Sc + jj;
+            float u0 = 0.0f, u1 = 0.0f, u2 = 0.0f, u3 = 0.0f, w0 = 0.0f, w1 = 0.0f, w2 = 0.0f, w3 = 0.0f;
+#pragma unroll 8
+            for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+                const float4 kv = k4[i4], qv = q4[i4];
+                const float s0 = sc[(4 * i4) * WY_CLD], s1 = sc[(4 * i4 + 1) * WY_CLD];
+                const float s2 = sc[(4 * i4 + 2) * WY_CLD], s3 = sc[(4 * i4 + 3) * WY_CLD];
+                u0 = __fmaf_rn(s0, kv.x, u0);
+                u1 = __fmaf_rn(s1, kv.y, u1);
+                u2 = __fmaf_rn(s2, kv.z, u2);
+                u3 = __fmaf_rn(s3, kv.w, u3);
+                w0 = __fmaf_rn(s0, qv.x, w0);
+                w1 = __fmaf_rn(s1, qv.y, w1);
+                w2 = __fmaf_rn(s2, qv.z, w2);
+                w3 = __fmaf_rn(s3, qv.w, w3);
+            }
+            Uc[t * WY_CLD + jj] = (u0 + u1) + (u2 + u3);
+            Wc[t * WY_CLD + jj] = (w0 + w1) + (w2 + w3);
+        }
+        // A and M: wy_chunk's mapping (lane = s, warp w takes t = w, w + 4, ...)
+        {
+            const int sidx = lane;
+            const float4 *ks4 = reinterpret_cast<const float4 *>(Ks + sidx * WY_LD);
+            for (int t = warp; t < nc; t += 4) {
+                const float4 *kt4 = reinterpret_cast<const float4 *>(Ks + t * WY_LD);
+                const float4 *qt4 = reinterpret_cast<const float4 *>(Qs + t * WY_LD);
+                float kk = 0.0f, qk = 0.0f;
+                if (sidx <= t) {
+                    float k0 = 0.0f, k1 = 0.0f, k2 = 0.0f, k3 = 0.0f, q0 = 0.0f, q1 = 0.0f, q2 = 0.0f, q3 = 0.0f;
+#pragma unroll 8
+                    for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
+                        const float4 x = ks4[i4], y = kt4[i4], z = qt4[i4];
+                        k0 = __fmaf_rn(y.x, x.x, k0);
+                        k1 = __fmaf_rn(y.y, x.y, k1);
+                        k2 = __fmaf_rn(y.z, x.z, k2);
+                        k3 = __fmaf_rn(y.w, x.w, k3);
+                        q0 = __fmaf_rn(z.x, x.x, q0);
+                        q1 = __fmaf_rn(z.y, x.y, q1);
+                        q2 = __fmaf_rn(z.z, x.z, q2);
+                        q3 = __fmaf_rn(z.w, x.w, q3);
+                    }
+                    kk = (k0 + k1) + (k2 + k3);
+                    qk = (q0 + q1) + (q2 + q3);
+                }
+                const float dec = sidx <= t ? expf(Lc[t] - Lc[sidx]) : 0.0f;
+                Am[t * (WY_C + 1) + sidx] = sidx < t ? dec * kk : 0.0f;
+                Mm[t * (WY_C + 1) + sidx] = sidx <= t ? dec * qk : 0.0f;
+            }
+        }
+        __syncthreads();
+        // forward substitution for km / delta, one thread per column
+        if (tid < WY_CB) {
+            float dl[WY_C];
+#pragma unroll
+            for (int t = 0; t < WY_C; t++) {
+                dl[t] = 0.0f;
+                if (t < nc) {
+                    float km = eL[t] * Uc[t * WY_CLD + tid];
+#pragma unroll
+                    for (int s2 = 0; s2 < t; s2++) km = __fmaf_rn(Am[t * (WY_C + 1) + s2], dl[s2], km);
+                    dl[t] = bet[t] * (Vc[t * WY_CLD + tid] - km);
+                    Dc[t * WY_CLD + tid] = dl[t];
+                    Ec[t * WY_CLD + tid] = eE[t] * dl[t];
+                    const long long tok = t0 + t;
+                    if (a.km) a.km[tok * a.km_tok + h * a.km_head + c0 + tid] = km;
+                    if (a.delta) a.delta[tok * a.delta_tok + h * a.delta_head + c0 + tid] = dl[t];
+                }
+            }
+        }
+        __syncthreads();
+        // outputs for (token, column) pairs
+        for (int t = tg; t < nc; t += NTG) {
+            float o = eL[t] * Wc[t * WY_CLD + jj];
+            for (int s2 = 0; s2 <= t; s2++) o = __fmaf_rn(Mm[t * (WY_C + 1) + s2], Dc[s2 * WY_CLD + jj], o);
+            a.out[(t0 + t) * a.out_tok + h * a.out_head + c0 + jj] = o;
+        }
+        // state for (row, column) pairs: exp(L_end) S0 + sum_t decay(end, t) k_t delta_t
+        const float gend = eL[nc - 1];
+        for (int i = tg; i < GDN_KD; i += NTG) {
+            float x = gend * Sc[i * WY_CLD + jj];
+            for (int t = 0; t < nc; t++) x = __fmaf_rn(Ks[t * WY_LD + i], Ec[t * WY_CLD + jj], x);
+            Sc[i * WY_CLD + jj] = x;
+        }
+        __syncthreads();  // chunk buffers and the state columns are reused
+    }
+    for (int idx = tid; idx < GDN_KD * WY_CB; idx += GDN_KD) {
+        const int i = idx / WY_CB, c = idx - i * WY_CB;
+        S[(long long)i * GDN_KD + c0 + c] = Sc[i * WY_CLD + c];
+    }
+}
+
+inline int gdn_wy_cols_launch(const GdnArgs &a, cudaStream_t st) {
+    if (a.heads <= 0 || a.rows <= 0) return 0;
+    if (a.nk <= 0) return (int)cudaErrorInvalidValue;
+    k_gdn_wy_cols<<<(unsigned)(a.heads * WY_NCB), GDN_KD, WY_COLS_SMEM, st>>>(a);
+    return (int)cudaGetLastError();
+}
+
 // k_gdn_core stages the 64 KB state block in dynamic shared memory
 inline int gdn_prepare() {
     static int done = 0;
@@ -691,6 +859,8 @@ inline int gdn_prepare() {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gdn_wy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_SMEM);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_gdn_wy_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_ROWS_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gdn_wy_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_COLS_SMEM);
     if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;

@@ -855,6 +855,9 @@ struct LprPair {
 #ifndef LPR_TALL_OCC
 #define LPR_TALL_OCC 3          // CTAs per SM for tall matrices (4 row groups each)
 #endif
+#ifndef LPR_TALL_OCC_SMALL
+#define LPR_TALL_OCC_SMALL 4    // the same for 144-byte row chunks at 1-2 tokens
+#endif
 constexpr int LPR_CHUNK_COLS = 256;  // columns per streamed chunk (row chunks are odd multiples of 16 B)
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
@@ -941,6 +944,11 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     long long ctas;
     if (T >= (long long)nsm * LPR_TALL_OCC * 4) {
         ctas = (T + 3) / 4;
+        // 144-byte chunks (IQ4_NL, Q4_0, Q4_K): the decode is instruction-
+        // bound (the integer ALU pipe, not DRAM, is the busiest unit), so a
+        // fourth CTA per SM (the registers allow it; the ring still gets two
+        // stages) adds warps to issue from
+        if (rs <= 144 && ntok <= 2) occ = LPR_TALL_OCC_SMALL;
     } else {
         rw = pair ? 2 : 1;  // pair mode: a CTA takes a gate tile and the matching up tile
         // the widest column split (any count of warps, at most one chunk
