@@ -661,6 +661,8 @@ def sweep_gemv(L, hbm, only=None):
                 ops = 2.0 * rows * cols * ntok
                 if ntok >= 16 and tname != "Q6_K":
                     path = "k_mmq" if tname in ("Q8_0", "IQ4_NL") else "k_mmq_kq"
+                elif ntok >= 16:
+                    path = "k_repack_q6k + k_mmq_kq"  # raw 210-byte rows, repacked per call
                 elif tname != "Q6_K":
                     path = "k_gemv_lpr"
                 else:

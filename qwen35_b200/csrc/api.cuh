@@ -82,11 +82,58 @@ int q35_launch_dequantize(int ttype, const void *d_src, float *d_dst, int nblock
 }
 
 // ---- matvec (api.h:110-124) ----
+// Raw 210-byte Q6_K rows at MMQ_MIN_TOK tokens or more go to the tensor-core
+// MMQ after a repack to the 224-byte layout, in a per-device buffer kept
+// between calls.  The buffer grows only outside stream capture (cudaMalloc
+// there would break a capture); a captured call that finds it too small runs
+// the block-splitting kernel on the raw rows instead.  Calls on one device
+// share the buffer, so they must be ordered (one stream, or events), as the
+// single-threaded host of the reference orders them.
+struct Q6Repack {
+    void *p = nullptr;
+    size_t bytes = 0;
+};
+inline Q6Repack &q6_repack_buf(int dev) {
+    static Q6Repack bufs[64];
+    return bufs[dev & 63];
+}
+inline int q6k_raw_mmq(const void *d_w, const void *d_xq, float *d_out, int rows, int cols, int tokens,
+                       cudaStream_t st) {
+    if (tokens < MMQ_MIN_TOK || cols % 256 || (reinterpret_cast<uintptr_t>(d_w) & 1u)) return -1;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    Q6Repack &b = q6_repack_buf(dev);
+    const long long nblk = (long long)rows * (cols / 256);
+    const size_t need = (size_t)nblk * 224;
+    if (b.bytes < need) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusActive;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return -1;
+        void *p = nullptr;
+        if (cudaMalloc(&p, need) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        if (b.p) cudaFree(b.p);
+        b.p = p;
+        b.bytes = need;
+    }
+    k_repack_q6k<<<(unsigned)((nblk * 112 + 255) / 256), 256, 0, st>>>(static_cast<const uint8_t *>(d_w),
+                                                                      static_cast<uint8_t *>(b.p), nblk);
+    const int rc = (int)cudaGetLastError();
+    if (rc) return rc;
+    GemvSegDesc s{b.p, d_out, rows, TT_Q6_K_P, rows, GV_STORE};
+    return mmq_launch(&s, 1, d_xq, cols, tokens, st, 0, nullptr, 0);
+}
+
 int q35_launch_mul_mat_vec(const void *d_w, const void *d_xq, float *d_out, int rows, int cols, int tokens, int ttype,
                            void *stream) {
     if (rows <= 0 || cols <= 0 || tokens <= 0) return 0;
     const Geom g = geom_of(ttype);
     if (!g.elems || cols % g.elems) return (int)cudaErrorInvalidValue;
+    if (ttype == TT_Q6_K) {
+        const int rc = q6k_raw_mmq(d_w, d_xq, d_out, rows, cols, tokens, S(stream));
+        if (rc != -1) return rc;
+    }
     GemvSegDesc s{d_w, d_out, rows, ttype, rows, GV_STORE};
     return gemv_launch(&s, 1, d_xq, cols, tokens, S(stream));
 }
@@ -294,7 +341,10 @@ int q35_launch_gdn_step_wy(float *d_state, int state_stride, const float *d_k, i
     a.gamma = d_gamma; a.g_tok = gamma_stride;
     a.beta = d_beta; a.b_tok = beta_stride;
     a.heads = heads; a.nk = nk; a.rows = rows;
-    return gdn_wy_cols_launch(a, S(stream));
+    // the column-split kernel stages q / k rows with 16-byte async copies
+    const bool al16 = !(reinterpret_cast<uintptr_t>(d_q) & 15u) && !(reinterpret_cast<uintptr_t>(d_k) & 15u) &&
+                      !(q_stride & 3) && !(k_stride & 3);
+    return al16 ? gdn_wy_cols_launch(a, S(stream)) : gdn_wy_rows_launch(a, S(stream));
 }
 int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
                              int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,

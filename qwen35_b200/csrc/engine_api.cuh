@@ -155,14 +155,6 @@ int q35b_engine_set_tensor(q35b_engine *e, const char *name, int tt, const void 
 }
 
 // Q6_K (210 B) -> padded Q6_K (224 B): 105 halfwords of a block, then zeros
-__global__ void k_repack_q6k(const uint8_t *src, uint8_t *dst, long long nblk) {
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i >= nblk * 112) return;
-    const long long b = i / 112;
-    const int hw = (int)(i - b * 112);
-    const uint16_t v = hw < 105 ? reinterpret_cast<const uint16_t *>(src + b * 210)[hw] : (uint16_t)0;
-    reinterpret_cast<uint16_t *>(dst + b * 224)[hw] = v;
-}
 
 int q35b_engine_finalize(q35b_engine *e) {
     if (!e || e->finalized) return (int)cudaErrorInvalidValue;

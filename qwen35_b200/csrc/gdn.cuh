@@ -695,51 +695,73 @@ inline int gdn_wy_rows_launch(const GdnArgs &a, cudaStream_t st) {
 constexpr int WY_CB = 16;                      // state columns per CTA
 constexpr int WY_NCB = GDN_KD / WY_CB;         // CTAs per head
 constexpr int WY_CLD = WY_CB + 1;              // pitch of the per-column tiles (floats)
-constexpr size_t WY_COLS_SMEM = (size_t)2 * WY_C * WY_LD * 4             // Qs, Ks
-                                + (size_t)4 * WY_C * WY_CLD * 4         // Vc, Uc, Wc, Dc
+constexpr size_t WY_COLS_SMEM = (size_t)2 * 2 * WY_C * WY_LD * 4         // Qs, Ks (two buffers)
+                                + (size_t)2 * WY_C * WY_CLD * 4         // Vc (two buffers)
+                                + (size_t)3 * WY_C * WY_CLD * 4         // Uc, Wc, Dc
                                 + (size_t)WY_C * WY_CLD * 4             // Ec: eE[t] * delta
                                 + (size_t)GDN_KD * WY_CLD * 4           // state columns
                                 + (size_t)2 * WY_C * (WY_C + 1) * 4     // Am, Mm
-                                + (size_t)6 * WY_C * 4;                 // Lc, eL, eE, bet, lg
+                                + (size_t)4 * WY_C * 4                  // Lc, eL, eE, bet
+                                + (size_t)2 * 2 * WY_C * 4;             // gamma, beta (two buffers)
 
 __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ GdnArgs a) {
     extern __shared__ __align__(128) float smc[];
-    float *Qs = smc, *Ks = Qs + WY_C * WY_LD;
-    float *Vc = Ks + WY_C * WY_LD, *Uc = Vc + WY_C * WY_CLD, *Wc = Uc + WY_C * WY_CLD, *Dc = Wc + WY_C * WY_CLD;
+    float *Qb = smc, *Kb = Qb + 2 * WY_C * WY_LD;     // [2][C][LD]
+    float *Vb = Kb + 2 * WY_C * WY_LD;                // [2][C][CLD]
+    float *Uc = Vb + 2 * WY_C * WY_CLD, *Wc = Uc + WY_C * WY_CLD, *Dc = Wc + WY_C * WY_CLD;
     float *Ec = Dc + WY_C * WY_CLD, *Sc = Ec + WY_C * WY_CLD;
     float *Am = Sc + GDN_KD * WY_CLD, *Mm = Am + WY_C * (WY_C + 1);
-    float *Lc = Mm + WY_C * (WY_C + 1), *eL = Lc + WY_C, *eE = eL + WY_C, *bet = eE + WY_C, *lg = bet + WY_C;
+    float *Lc = Mm + WY_C * (WY_C + 1), *eL = Lc + WY_C, *eE = eL + WY_C, *bet = eE + WY_C;
+    float *Gb = bet + WY_C, *Bb = Gb + 2 * WY_C;      // [2][C] gamma, beta
     const int h = blockIdx.x / WY_NCB, cb = blockIdx.x - h * WY_NCB, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int kh = h % a.nk, c0 = cb * WY_CB;
     const int jj = tid & (WY_CB - 1), tg = tid / WY_CB;  // (token group, column) of the pair loops
     constexpr int NTG = GDN_KD / WY_CB;                    // token groups
     float *S = a.state + h * a.state_head;
+    // the chunk starting at token t0 into buffer b: every copy in flight at once
+    auto stage = [&](int t0, int b) {
+        const int nc = min(WY_C, a.rows - t0);
+        if (nc > 0) {
+            float *qd = Qb + b * WY_C * WY_LD, *kd = Kb + b * WY_C * WY_LD, *vd = Vb + b * WY_C * WY_CLD;
+            for (int idx = tid; idx < nc * (GDN_KD / 4); idx += GDN_KD) {
+                const int t = idx / (GDN_KD / 4), c = idx - t * (GDN_KD / 4);
+                const long long tok = t0 + t;
+                cp_async16(qd + t * WY_LD + 4 * c, a.q + tok * a.q_tok + kh * a.q_head + 4 * c);
+                cp_async16(kd + t * WY_LD + 4 * c, a.k + tok * a.k_tok + kh * a.k_head + 4 * c);
+            }
+            for (int idx = tid; idx < nc * WY_CB; idx += GDN_KD) {
+                const int t = idx / WY_CB, c = idx - t * WY_CB;
+                cp_async4(vd + t * WY_CLD + c, a.v + (t0 + t) * a.v_tok + h * a.v_head + c0 + c);
+            }
+            if (tid < nc) {
+                const long long tok = t0 + tid;
+                if (a.gamma) cp_async4(Gb + b * WY_C + tid, a.gamma + tok * a.g_tok + h);
+                if (a.beta) cp_async4(Bb + b * WY_C + tid, a.beta + tok * a.b_tok + h);
+            }
+        }
+        cp_async_commit();  // one group per chunk, empty past the end
+    };
     for (int idx = tid; idx < GDN_KD * WY_CB; idx += GDN_KD) {
         const int i = idx / WY_CB, c = idx - i * WY_CB;
         Sc[i * WY_CLD + c] = S[(long long)i * GDN_KD + c0 + c];
     }
-    for (int t0 = 0; t0 < a.rows; t0 += WY_C) {
+    stage(0, 0);
+    for (int t0 = 0, buf = 0; t0 < a.rows; t0 += WY_C, buf ^= 1) {
         const int nc = min(WY_C, a.rows - t0);
-        for (int t = 0; t < nc; t++) {
-            const long long tok = t0 + t;
-            Qs[t * WY_LD + tid] = a.q[tok * a.q_tok + kh * a.q_head + tid];
-            Ks[t * WY_LD + tid] = a.k[tok * a.k_tok + kh * a.k_head + tid];
-        }
-        for (int idx = tid; idx < nc * WY_CB; idx += GDN_KD) {
-            const int t = idx / WY_CB, c = idx - t * WY_CB;
-            Vc[t * WY_CLD + c] = a.v[(t0 + t) * a.v_tok + h * a.v_head + c0 + c];
-        }
-        if (tid < nc) {
-            const long long tok = t0 + tid;
-            lg[tid] = fmaxf(logf(a.gamma ? a.gamma[tok * a.g_tok + h] : a.gamma_imm), WY_LOG_MIN);
-            bet[tid] = a.beta ? a.beta[tok * a.b_tok + h] : a.beta_imm;
+        stage(t0 + WY_C, buf ^ 1);  // the next chunk, into the buffer the previous one left
+        cp_async_wait<1>();         // this thread's copies of this chunk landed
+        __syncthreads();            // everyone's
+        const float *Qs = Qb + buf * WY_C * WY_LD, *Ks = Kb + buf * WY_C * WY_LD, *Vc = Vb + buf * WY_C * WY_CLD;
+        if (tid < nc) {  // floored log decays (in Lc), then their running sum (wy_cumulate)
+            Lc[tid] = fmaxf(logf(a.gamma ? Gb[buf * WY_C + tid] : a.gamma_imm), WY_LOG_MIN);
+            bet[tid] = a.beta ? Bb[buf * WY_C + tid] : a.beta_imm;
         }
         __syncthreads();
-        if (tid == GDN_KD - 1) {  // wy_cumulate
+        if (tid == GDN_KD - 1) {
             float L = 0.0f;
             for (int t = 0; t < nc; t++) {
-                L = __fadd_rn(L, lg[t]);
+                L = __fadd_rn(L, Lc[t]);
                 Lc[t] = L;
             }
         }
@@ -829,15 +851,28 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ 
             for (int s2 = 0; s2 <= t; s2++) o = __fmaf_rn(Mm[t * (WY_C + 1) + s2], Dc[s2 * WY_CLD + jj], o);
             a.out[(t0 + t) * a.out_tok + h * a.out_head + c0 + jj] = o;
         }
-        // state for (row, column) pairs: exp(L_end) S0 + sum_t decay(end, t) k_t delta_t
+        // state for (row, column) pairs: exp(L_end) S0 + sum_t decay(end, t) k_t delta_t,
+        // four rows at a time so four chains are in flight
         const float gend = eL[nc - 1];
-        for (int i = tg; i < GDN_KD; i += NTG) {
-            float x = gend * Sc[i * WY_CLD + jj];
-            for (int t = 0; t < nc; t++) x = __fmaf_rn(Ks[t * WY_LD + i], Ec[t * WY_CLD + jj], x);
-            Sc[i * WY_CLD + jj] = x;
+        for (int i = tg; i < GDN_KD; i += 4 * NTG) {
+            float x0 = gend * Sc[i * WY_CLD + jj], x1 = gend * Sc[(i + NTG) * WY_CLD + jj];
+            float x2 = gend * Sc[(i + 2 * NTG) * WY_CLD + jj], x3 = gend * Sc[(i + 3 * NTG) * WY_CLD + jj];
+            for (int t = 0; t < nc; t++) {
+                const float e = Ec[t * WY_CLD + jj];
+                const float *kr = Ks + t * WY_LD + i;
+                x0 = __fmaf_rn(kr[0], e, x0);
+                x1 = __fmaf_rn(kr[NTG], e, x1);
+                x2 = __fmaf_rn(kr[2 * NTG], e, x2);
+                x3 = __fmaf_rn(kr[3 * NTG], e, x3);
+            }
+            Sc[i * WY_CLD + jj] = x0;
+            Sc[(i + NTG) * WY_CLD + jj] = x1;
+            Sc[(i + 2 * NTG) * WY_CLD + jj] = x2;
+            Sc[(i + 3 * NTG) * WY_CLD + jj] = x3;
         }
         __syncthreads();  // chunk buffers and the state columns are reused
     }
+    cp_async_wait<0>();
     for (int idx = tid; idx < GDN_KD * WY_CB; idx += GDN_KD) {
         const int i = idx / WY_CB, c = idx - i * WY_CB;
         S[(long long)i * GDN_KD + c0 + c] = Sc[i * WY_CLD + c];

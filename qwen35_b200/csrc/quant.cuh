@@ -421,4 +421,16 @@ __global__ void k_synth_fill(uint64_t key, long long n, float k, float *__restri
     }
 }
 
+// Q6_K blocks from the GGUF 210-byte layout to the 224-byte one (14 zero
+// bytes after d), whose rows are 16-byte multiples for the TMA / MMQ paths;
+// one thread per 16-bit word
+__global__ void k_repack_q6k(const uint8_t *src, uint8_t *dst, long long nblk) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= nblk * 112) return;
+    const long long b = i / 112;
+    const int hw = (int)(i - b * 112);
+    const uint16_t v = hw < 105 ? reinterpret_cast<const uint16_t *>(src + b * 210)[hw] : (uint16_t)0;
+    reinterpret_cast<uint16_t *>(dst + b * 224)[hw] = v;
+}
+
 }  // namespace q35

@@ -234,3 +234,30 @@ def test_attn_prefill_vs_oracle_rows(L, heads, kvh, slot0, rows):
     assert np.array_equal(got.view(np.uint32), ref_cr.view(np.uint32))
     assert np.abs(got - ref).max() <= 1e-5 * max(1.0, float(np.abs(ref).max()))
     no_kernel_error(L)
+
+
+@pytest.mark.parametrize("rows,heads,nk", [(525, 4, 2), (100, 16, 16)])
+def test_wy_column_split_equals_per_head(L, rows, heads, nk):
+    """q35_launch_gdn_step_wy runs the column-split kernel when the q / k rows
+    are 16-byte aligned and the per-head kernel otherwise (row strides of 129
+    floats here): the two give the same out, km, delta and state, bit for bit"""
+    kd = 128
+    rng = np.random.default_rng(rows + 3 * heads)
+    k, q, v, bet, gam, state = _gdn_inputs(rng, heads, nk, kd, rows)
+    res = []
+    for pad in (0, 1):
+        ld = nk * kd + pad
+        kp = np.zeros((rows, ld), np.float32)
+        qp = np.zeros((rows, ld), np.float32)
+        kp[:, :nk * kd] = k.reshape(rows, -1)
+        qp[:, :nk * kd] = q.reshape(rows, -1)
+        dk, dq, dv, db, dg = (torch.from_numpy(a).cuda() for a in (kp, qp, v, bet, gam))
+        ds = torch.from_numpy(state).cuda()
+        dkm, ddl, dout = (torch.zeros((rows, heads * kd), device="cuda") for _ in range(3))
+        ok(L.q35_launch_gdn_step_wy(ds.data_ptr(), kd * kd, dk.data_ptr(), ld, dv.data_ptr(), heads * kd,
+                                    dq.data_ptr(), ld, dkm.data_ptr(), heads * kd, ddl.data_ptr(), heads * kd,
+                                    dout.data_ptr(), heads * kd, dg.data_ptr(), heads, db.data_ptr(), heads, heads,
+                                    nk, kd, kd, rows, S))
+        res.append([t.cpu().numpy() for t in (dout, dkm, ddl, ds)])
+    for nm, a, b in zip(("out", "km", "delta", "state"), res[0], res[1]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), nm
