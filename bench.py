@@ -677,14 +677,19 @@ def sweep_gemv(L, hbm, only=None):
             torch.cuda.empty_cache()
 
 
-def sweep_gdn(L, hbm):
+WY_FORM = ("WY, 32-token chunks: Gram matrices on tcgen05 kind::tf32 (3xTF32, k_wy_gram), "
+           "column-split recurrence (k_gdn_wy_cols)")
+
+
+def sweep_gdn(L, hbm, only=None):
     """gated delta-net in isolation: 16 heads, dk = dv =
     128, f32 state, q/k L2-normalised, beta = sigmoid(N(0,1)), gamma =
     exp(-softplus(N(0,1))), causal conv k=4 over 6144 channels.  Decode step
     at batch 1/16/64 (conv step + delta-rule step, each sequence its own
     state); prefill of one sequence of 512/2048/8192 tokens, exact per-token
     kernel and the WY chunked form; a ragged batch of 32 sequences with
-    lengths uniform in 64..4096 (one WY launch per sequence)."""
+    lengths uniform in 64..4096 (one WY launch per sequence).  `only` = a
+    prefill length: that WY prefill alone (a small case to profile)."""
     import numpy as np
     import torch
     st = torch.cuda.current_stream()
@@ -697,7 +702,7 @@ def sweep_gdn(L, hbm):
     def qk(n):
         return F.normalize(torch.randn(n, D, device="cuda", generator=g), dim=1).contiguous()
 
-    for B in (1, 16, 64):
+    for B in (1, 16, 64) if only is None else ():
         nh = H * B
         # rotate states so >= 3x L2 of distinct state passes between reuses
         sbytes = nh * D * D * 4
@@ -745,14 +750,16 @@ def sweep_gdn(L, hbm):
         return launch, keep
 
     state = torch.zeros(H * D * D, device="cuda")
-    for rows in (512, 2048, 8192):
-        for wy in (False, True):
+    for rows in (512, 2048, 8192) if only is None else (int(only),):
+        for wy in (False, True) if only is None else (True,):
             launch, keep = prefill(rows, wy, state)
             ms, reps = _timed_loop(torch, launch, 1, target_ms=100.0)
-            print(json.dumps({"sweep": "gdn", "mode": "prefill", "form": "WY (32-token blocks)" if wy else
+            print(json.dumps({"sweep": "gdn", "mode": "prefill", "form": WY_FORM if wy else
                               "exact per-token", "seq_len": rows, "us": ms * 1e3,
                               "tokens_per_s": rows / (ms * 1e-3), "reps": reps}), flush=True)
             del keep
+    if only is not None:
+        return
     # ragged: 32 sequences, lengths U[64, 4096], each its own state
     lens = np.random.default_rng(3).integers(64, 4097, 32)
     states = torch.zeros(32, H * D * D, device="cuda")
@@ -763,7 +770,7 @@ def sweep_gdn(L, hbm):
             launch(0, ls)
 
     ms, reps = _timed_loop(torch, ragged, 1, target_ms=200.0)
-    print(json.dumps({"sweep": "gdn", "mode": "ragged prefill", "form": "WY (32-token blocks)", "sequences": 32,
+    print(json.dumps({"sweep": "gdn", "mode": "ragged prefill", "form": WY_FORM, "sequences": 32,
                       "tokens": int(lens.sum()), "us": ms * 1e3, "tokens_per_s": float(lens.sum()) / (ms * 1e-3),
                       "launches": 32, "reps": reps}), flush=True)
 
@@ -870,7 +877,7 @@ def main():
     ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "all"], default=None,
                     help="isolated kernel sweeps (BASELINE configs 2 / 3; mmq: the 4B / 27B batched-decode "
                          "matrices) instead of the decode bench")
-    ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS")
+    ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS; --sweep gdn: one WY prefill length")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -906,7 +913,7 @@ def main():
         if args.sweep in ("gemv", "all"):
             sweep_gemv(L, hbm, args.sweep_case)
         if args.sweep in ("gdn", "all"):
-            sweep_gdn(L, hbm)
+            sweep_gdn(L, hbm, args.sweep_case)
         if args.sweep in ("mmq", "all"):
             sweep_mmq(L, hbm, args.sweep_case)
         return

@@ -128,8 +128,11 @@ int q35_launch_rope64_setenv(int *d_dyn, int pos, float base, void *stream);
 
 /* gated delta net (api.h:256-335): bit-exact with the CPU gdnFused.
  * q35_launch_gdn_step_wy (api.h:290-308) takes the chunk form's arguments and
- * solves the same recurrence in the WY form, 32 tokens per block: equal to
- * the per-token kernels to f32 rounding, not bitwise. */
+ * solves the same recurrence in the WY form, 32 tokens per block, with each
+ * block's K K^T and Q K^T on the tensor cores (tf32 x3 split) when the q / k
+ * rows are 16-byte aligned: within 1e-4 relative L2 of the per-token kernels,
+ * not bitwise.  Calls on one device share the buffer of those products, so
+ * order them (one stream, or events). */
 int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
                              int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,
                              const float *d_gamma, const float *d_beta, int heads, int nk, int kd, int vd,

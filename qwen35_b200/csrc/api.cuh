@@ -344,7 +344,12 @@ int q35_launch_gdn_step_wy(float *d_state, int state_stride, const float *d_k, i
     // the column-split kernel stages q / k rows with 16-byte async copies
     const bool al16 = !(reinterpret_cast<uintptr_t>(d_q) & 15u) && !(reinterpret_cast<uintptr_t>(d_k) & 15u) &&
                       !(q_stride & 3) && !(k_stride & 3);
-    return al16 ? gdn_wy_cols_launch(a, S(stream)) : gdn_wy_rows_launch(a, S(stream));
+    if (!al16) return gdn_wy_rows_launch(a, S(stream));
+    // the Gram matrices of each 64-token chunk on the tensor cores, then the
+    // column-split recurrence; without room for them (inside a capture) the
+    // CUDA-core column split
+    const int rc = wy_tc_launch(a, S(stream));
+    return rc != -1 ? rc : gdn_wy_cols_launch(a, S(stream));
 }
 int q35_launch_gdn_step_rows(float *d_state, int state_stride, const float *d_k, int k_stride, const float *d_v,
                              int v_stride, const float *d_q, int q_stride, float *d_km, float *d_delta, float *d_out,

@@ -683,68 +683,96 @@ inline int gdn_wy_rows_launch(const GdnArgs &a, cudaStream_t st) {
     return (int)cudaGetLastError();
 }
 
-// The API's WY prefill with each head's state columns split over WY_NCB CTAs
-// (WY_CB columns each).  The delta rule updates every value column on its
-// own (km_j, delta_j and column j of S involve only column j), so the split
-// needs no exchange; each CTA recomputes the chunk's shared quantities
-// (cumulative decay, A, M: wy_chunk's code, so the same values) and runs the
-// per-column steps for its columns with the threads spread over (token,
-// column) and (state row, column) pairs, every dot and chain in wy_chunk's
-// order.  The results equal k_gdn_wy_rows' bit for bit; a 16-head sequence
-// runs on 16 x WY_NCB SMs instead of 16.
-constexpr int WY_CB = 16;                      // state columns per CTA
-constexpr int WY_NCB = GDN_KD / WY_CB;         // CTAs per head
-constexpr int WY_CLD = WY_CB + 1;              // pitch of the per-column tiles (floats)
-constexpr size_t WY_COLS_SMEM = (size_t)2 * 2 * WY_C * WY_LD * 4         // Qs, Ks (two buffers)
-                                + (size_t)2 * WY_C * WY_CLD * 4         // Vc (two buffers)
-                                + (size_t)3 * WY_C * WY_CLD * 4         // Uc, Wc, Dc
-                                + (size_t)WY_C * WY_CLD * 4             // Ec: eE[t] * delta
-                                + (size_t)GDN_KD * WY_CLD * 4           // state columns
-                                + (size_t)2 * WY_C * (WY_C + 1) * 4     // Am, Mm
-                                + (size_t)4 * WY_C * 4                  // Lc, eL, eE, bet
-                                + (size_t)2 * 2 * WY_C * 4;             // gamma, beta (two buffers)
+// The API's WY prefill with each head's state columns split over
+// GDN_KD / CB CTAs (CB columns each).  The delta rule updates every value
+// column on its own (km_j, delta_j and column j of S involve only column j),
+// so the split needs no exchange; each CTA recomputes the chunk's shared
+// quantities (cumulative decay, A, M) and runs the per-column steps for its
+// columns with the threads spread over (token, column) and (state row,
+// column) pairs.  A and M come from the tensor-core pass's Gram matrices (G,
+// staged with the chunk) or, with G null, from wy_chunk's own dots; with G
+// null every dot and chain runs in wy_chunk's order and the results equal
+// k_gdn_wy_rows' bit for bit.  Two 256-thread CTAs fit on an SM, so a 16-head sequence
+// runs on 256 CTAs of 8 columns, a 32-head one on 256 CTAs of 16.
+constexpr int WY_AP = WY_C + 4;                // pitch of A^T (floats)
+constexpr int WY_GC = 2 * WY_C * WY_C;         // floats of G per (chunk, k head): K K^T, then Q K^T
+constexpr int WY_SP = GDN_KD + 4;              // pitch of the state columns (floats)
+template <int CB>
+constexpr size_t wy_cols_smem() {
+    return (size_t)2 * 2 * WY_C * WY_LD * 4          // Qs, Ks (two buffers)
+           + (size_t)2 * WY_GC * 4                   // G (two buffers)
+           + (size_t)2 * WY_C * (CB + 1) * 4         // Vc (two buffers)
+           + (size_t)3 * WY_C * (CB + 1) * 4         // Uc (then km), Wc, Dc
+           + (size_t)WY_C * (CB + 1) * 4             // Ec: eE[t] * delta
+           + (size_t)CB * WY_SP * 4                  // state columns, column-major
+           + (size_t)WY_C * WY_AP * 4                // At: A transposed
+           + (size_t)WY_C * (WY_C + 1) * 4           // Mm
+           + (size_t)4 * WY_C * 4                    // Lc, eL, eE, bet
+           + (size_t)2 * 2 * WY_C * 4;               // gamma, beta (two buffers)
+}
 
-__global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ GdnArgs a) {
+// G: null, or the tensor-core pass's Gram matrices per (chunk, k head)
+// ([2][WY_C][WY_C]: K K^T, then Q K^T; wy_tc.cuh), used for A and M
+constexpr int WY_NT = 256;  // threads per CTA of the column-split kernel
+template <int CB>
+__global__ void __launch_bounds__(WY_NT, 2) k_gdn_wy_cols(const __grid_constant__ GdnArgs a, const float *__restrict__ G) {
+    constexpr int NT = WY_NT, NW = NT / 32;
+    constexpr int CLD = CB + 1;       // pitch of the per-column tiles (floats)
+    constexpr int NCB = GDN_KD / CB;  // CTAs per head
+    constexpr int NTG = NT / CB;      // token groups of the (token, column) loops
+    constexpr int TPT = WY_C / NTG;   // tokens per thread in them
+    constexpr int P = NT / CB;        // lanes per column in the forward substitution
+    constexpr int NSLOT = WY_C / P;   // tokens each of those lanes owns
+    constexpr int RPT = GDN_KD / NTG; // state rows per thread
+    constexpr int RG = RPT % 8 == 0 ? 8 : 4;  // state rows per pass
+    static_assert(P <= 32 && 32 % P == 0 && NSLOT >= 1 && RPT % 4 == 0 && (TPT == 1 || TPT % 2 == 0),
+                  "column split");
     extern __shared__ __align__(128) float smc[];
     float *Qb = smc, *Kb = Qb + 2 * WY_C * WY_LD;     // [2][C][LD]
-    float *Vb = Kb + 2 * WY_C * WY_LD;                // [2][C][CLD]
-    float *Uc = Vb + 2 * WY_C * WY_CLD, *Wc = Uc + WY_C * WY_CLD, *Dc = Wc + WY_C * WY_CLD;
-    float *Ec = Dc + WY_C * WY_CLD, *Sc = Ec + WY_C * WY_CLD;
-    float *Am = Sc + GDN_KD * WY_CLD, *Mm = Am + WY_C * (WY_C + 1);
+    float *Gs = Kb + 2 * WY_C * WY_LD;                // [2][2][C][C]
+    float *Vb = Gs + 2 * WY_GC;                       // [2][C][CLD]
+    float *Uc = Vb + 2 * WY_C * CLD, *Wc = Uc + WY_C * CLD, *Dc = Wc + WY_C * CLD;
+    float *Ec = Dc + WY_C * CLD, *St = Ec + WY_C * CLD;  // St[column][row]
+    float *At = St + CB * WY_SP, *Mm = At + WY_C * WY_AP;
+    static_assert((2 * 2 * WY_C * WY_LD + 2 * WY_GC + 6 * WY_C * CLD) % 4 == 0, "St 16-byte aligned");
     float *Lc = Mm + WY_C * (WY_C + 1), *eL = Lc + WY_C, *eE = eL + WY_C, *bet = eE + WY_C;
     float *Gb = bet + WY_C, *Bb = Gb + 2 * WY_C;      // [2][C] gamma, beta
-    const int h = blockIdx.x / WY_NCB, cb = blockIdx.x - h * WY_NCB, tid = threadIdx.x;
+    const int h = blockIdx.x / NCB, cb = blockIdx.x - h * NCB, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int kh = h % a.nk, c0 = cb * WY_CB;
-    const int jj = tid & (WY_CB - 1), tg = tid / WY_CB;  // (token group, column) of the pair loops
-    constexpr int NTG = GDN_KD / WY_CB;                    // token groups
+    const int kh = h % a.nk, c0 = cb * CB;
+    const int jj = tid & (CB - 1), tg = tid / CB;     // (token group, column) of the pair loops
     float *S = a.state + h * a.state_head;
     // the chunk starting at token t0 into buffer b: every copy in flight at once
     auto stage = [&](int t0, int b) {
         const int nc = min(WY_C, a.rows - t0);
         if (nc > 0) {
-            float *qd = Qb + b * WY_C * WY_LD, *kd = Kb + b * WY_C * WY_LD, *vd = Vb + b * WY_C * WY_CLD;
-            for (int idx = tid; idx < nc * (GDN_KD / 4); idx += GDN_KD) {
+            float *qd = Qb + b * WY_C * WY_LD, *kd = Kb + b * WY_C * WY_LD, *vd = Vb + b * WY_C * CLD;
+            for (int idx = tid; idx < nc * (GDN_KD / 4); idx += NT) {
                 const int t = idx / (GDN_KD / 4), c = idx - t * (GDN_KD / 4);
                 const long long tok = t0 + t;
                 cp_async16(qd + t * WY_LD + 4 * c, a.q + tok * a.q_tok + kh * a.q_head + 4 * c);
                 cp_async16(kd + t * WY_LD + 4 * c, a.k + tok * a.k_tok + kh * a.k_head + 4 * c);
             }
-            for (int idx = tid; idx < nc * WY_CB; idx += GDN_KD) {
-                const int t = idx / WY_CB, c = idx - t * WY_CB;
-                cp_async4(vd + t * WY_CLD + c, a.v + (t0 + t) * a.v_tok + h * a.v_head + c0 + c);
+            for (int idx = tid; idx < nc * CB; idx += NT) {
+                const int t = idx / CB, c = idx - t * CB;
+                cp_async4(vd + t * CLD + c, a.v + (t0 + t) * a.v_tok + h * a.v_head + c0 + c);
             }
             if (tid < nc) {
                 const long long tok = t0 + tid;
                 if (a.gamma) cp_async4(Gb + b * WY_C + tid, a.gamma + tok * a.g_tok + h);
                 if (a.beta) cp_async4(Bb + b * WY_C + tid, a.beta + tok * a.b_tok + h);
             }
+            if (G) {
+                const float *gsrc = G + ((long long)(t0 / WY_C) * a.nk + kh) * WY_GC;
+                for (int idx = tid; idx < WY_GC / 4; idx += NT)
+                    cp_async16(Gs + b * WY_GC + 4 * idx, gsrc + 4 * idx);
+            }
         }
         cp_async_commit();  // one group per chunk, empty past the end
     };
-    for (int idx = tid; idx < GDN_KD * WY_CB; idx += GDN_KD) {
-        const int i = idx / WY_CB, c = idx - i * WY_CB;
-        Sc[i * WY_CLD + c] = S[(long long)i * GDN_KD + c0 + c];
+    for (int idx = tid; idx < GDN_KD * CB; idx += NT) {
+        const int i = idx / CB, c = idx - i * CB;
+        St[c * WY_SP + i] = S[(long long)i * GDN_KD + c0 + c];
     }
     stage(0, 0);
     for (int t0 = 0, buf = 0; t0 < a.rows; t0 += WY_C, buf ^= 1) {
@@ -752,36 +780,50 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ 
         stage(t0 + WY_C, buf ^ 1);  // the next chunk, into the buffer the previous one left
         cp_async_wait<1>();         // this thread's copies of this chunk landed
         __syncthreads();            // everyone's
-        const float *Qs = Qb + buf * WY_C * WY_LD, *Ks = Kb + buf * WY_C * WY_LD, *Vc = Vb + buf * WY_C * WY_CLD;
-        if (tid < nc) {  // floored log decays (in Lc), then their running sum (wy_cumulate)
-            Lc[tid] = fmaxf(logf(a.gamma ? Gb[buf * WY_C + tid] : a.gamma_imm), WY_LOG_MIN);
-            bet[tid] = a.beta ? Bb[buf * WY_C + tid] : a.beta_imm;
-        }
-        __syncthreads();
-        if (tid == GDN_KD - 1) {
-            float L = 0.0f;
-            for (int t = 0; t < nc; t++) {
-                L = __fadd_rn(L, Lc[t]);
-                Lc[t] = L;
+        const float *Qs = Qb + buf * WY_C * WY_LD, *Ks = Kb + buf * WY_C * WY_LD, *Vc = Vb + buf * WY_C * CLD;
+        // the last warp: floored log decays (in Lc), their running sum
+        // (wy_cumulate, one lane, in token order) and its exponentials; the
+        // other warps start on U / W, which needs none of them
+        if (warp == NW - 1) {
+            if (lane < nc) {
+                Lc[lane] = fmaxf(logf(a.gamma ? Gb[buf * WY_C + lane] : a.gamma_imm), WY_LOG_MIN);
+                bet[lane] = a.beta ? Bb[buf * WY_C + lane] : a.beta_imm;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                float lv[WY_C];
+#pragma unroll
+                for (int t = 0; t < WY_C; t++) lv[t] = Lc[t];
+                float L = 0.0f;
+#pragma unroll
+                for (int t = 0; t < WY_C; t++)
+                    if (t < nc) {
+                        L = __fadd_rn(L, lv[t]);
+                        Lc[t] = L;
+                    }
+            }
+            __syncwarp();
+            if (lane < nc) {
+                eL[lane] = expf(Lc[lane]);
+                eE[lane] = expf(Lc[nc - 1] - Lc[lane]);
             }
         }
-        __syncthreads();
-        if (tid < nc) {
-            eL[tid] = expf(Lc[tid]);
-            eE[tid] = expf(Lc[nc - 1] - Lc[tid]);
-        }
-        // U = S0^T k_t, W = S0^T q_t for (token, column) pairs; wy_chunk's
-        // four partial sums per dot
-        for (int t = tg; t < nc; t += NTG) {
+        // U = S0^T k_t, W = S0^T q_t for (token, column) pairs, two tokens
+        // (t, t + NTG) at a time where a thread has several, so each state
+        // load serves both; wy_chunk's four partial sums per dot
+        auto uw = [&](int t, int t2, bool two) {
             const float4 *k4 = reinterpret_cast<const float4 *>(Ks + t * WY_LD);
             const float4 *q4 = reinterpret_cast<const float4 *>(Qs + t * WY_LD);
-            const float *sc = Sc + jj;
+            const float4 *k4b = reinterpret_cast<const float4 *>(Ks + t2 * WY_LD);
+            const float4 *q4b = reinterpret_cast<const float4 *>(Qs + t2 * WY_LD);
+            const float4 *st4 = reinterpret_cast<const float4 *>(St + jj * WY_SP);
             float u0 = 0.0f, u1 = 0.0f, u2 = 0.0f, u3 = 0.0f, w0 = 0.0f, w1 = 0.0f, w2 = 0.0f, w3 = 0.0f;
-#pragma unroll 8
+            float x0 = 0.0f, x1 = 0.0f, x2 = 0.0f, x3 = 0.0f, y0 = 0.0f, y1 = 0.0f, y2 = 0.0f, y3 = 0.0f;
+#pragma unroll 4
             for (int i4 = 0; i4 < GDN_KD / 4; i4++) {
                 const float4 kv = k4[i4], qv = q4[i4];
-                const float s0 = sc[(4 * i4) * WY_CLD], s1 = sc[(4 * i4 + 1) * WY_CLD];
-                const float s2 = sc[(4 * i4 + 2) * WY_CLD], s3 = sc[(4 * i4 + 3) * WY_CLD];
+                const float4 sv = st4[i4];
+                const float s0 = sv.x, s1 = sv.y, s2 = sv.z, s3 = sv.w;
                 u0 = __fmaf_rn(s0, kv.x, u0);
                 u1 = __fmaf_rn(s1, kv.y, u1);
                 u2 = __fmaf_rn(s2, kv.z, u2);
@@ -790,15 +832,60 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ 
                 w1 = __fmaf_rn(s1, qv.y, w1);
                 w2 = __fmaf_rn(s2, qv.z, w2);
                 w3 = __fmaf_rn(s3, qv.w, w3);
+                if (two) {
+                    const float4 kb = k4b[i4], qb = q4b[i4];
+                    x0 = __fmaf_rn(s0, kb.x, x0);
+                    x1 = __fmaf_rn(s1, kb.y, x1);
+                    x2 = __fmaf_rn(s2, kb.z, x2);
+                    x3 = __fmaf_rn(s3, kb.w, x3);
+                    y0 = __fmaf_rn(s0, qb.x, y0);
+                    y1 = __fmaf_rn(s1, qb.y, y1);
+                    y2 = __fmaf_rn(s2, qb.z, y2);
+                    y3 = __fmaf_rn(s3, qb.w, y3);
+                }
             }
-            Uc[t * WY_CLD + jj] = (u0 + u1) + (u2 + u3);
-            Wc[t * WY_CLD + jj] = (w0 + w1) + (w2 + w3);
+            Uc[t * CLD + jj] = (u0 + u1) + (u2 + u3);
+            Wc[t * CLD + jj] = (w0 + w1) + (w2 + w3);
+            if (two && t2 < nc) {
+                Uc[t2 * CLD + jj] = (x0 + x1) + (x2 + x3);
+                Wc[t2 * CLD + jj] = (y0 + y1) + (y2 + y3);
+            }
+        };
+        if constexpr (TPT == 1) {
+            if (tg < nc) uw(tg, tg, false);
+        } else {
+            // t2 < WY_C: in the buffer (stale past nc, not stored)
+            for (int t = tg; t < nc; t += 2 * NTG) uw(t, t + NTG, true);
         }
-        // A and M: wy_chunk's mapping (lane = s, warp w takes t = w, w + 4, ...)
-        {
+        __syncthreads();
+        // A and M: the Gram matrices with this head's decays, or wy_chunk's
+        // own computation (lane = s, warp w takes t = w, w + NW, ...)
+        if (G) {
+            const float *gk = Gs + buf * WY_GC, *gq = gk + WY_C * WY_C;
+            // every load first (shared stores would otherwise pin them)
+            constexpr int NE = WY_C * WY_C / NT;
+            float lt[NE], ls[NE], vk[NE], vq[NE];
+#pragma unroll
+            for (int k = 0; k < NE; k++) {
+                const int idx = tid + k * NT, t = idx / WY_C, s2 = idx - t * WY_C;
+                lt[k] = Lc[t];
+                ls[k] = Lc[s2];
+                vk[k] = gk[idx];
+                vq[k] = gq[idx];
+            }
+#pragma unroll
+            for (int k = 0; k < NE; k++) {
+                const int idx = tid + k * NT, t = idx / WY_C, s2 = idx - t * WY_C;
+                if (t < nc) {
+                    const float dec = s2 <= t ? expf(lt[k] - ls[k]) : 0.0f;
+                    At[s2 * WY_AP + t] = s2 < t ? dec * vk[k] : 0.0f;
+                    Mm[t * (WY_C + 1) + s2] = s2 <= t ? dec * vq[k] : 0.0f;
+                }
+            }
+        } else {
             const int sidx = lane;
             const float4 *ks4 = reinterpret_cast<const float4 *>(Ks + sidx * WY_LD);
-            for (int t = warp; t < nc; t += 4) {
+            for (int t = warp; t < nc; t += NW) {
                 const float4 *kt4 = reinterpret_cast<const float4 *>(Ks + t * WY_LD);
                 const float4 *qt4 = reinterpret_cast<const float4 *>(Qs + t * WY_LD);
                 float kk = 0.0f, qk = 0.0f;
@@ -820,69 +907,119 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_cols(const __grid_constant__ 
                     qk = (q0 + q1) + (q2 + q3);
                 }
                 const float dec = sidx <= t ? expf(Lc[t] - Lc[sidx]) : 0.0f;
-                Am[t * (WY_C + 1) + sidx] = sidx < t ? dec * kk : 0.0f;
+                At[sidx * WY_AP + t] = sidx < t ? dec * kk : 0.0f;
                 Mm[t * (WY_C + 1) + sidx] = sidx <= t ? dec * qk : 0.0f;
             }
         }
         __syncthreads();
-        // forward substitution for km / delta, one thread per column
-        if (tid < WY_CB) {
-            float dl[WY_C];
+        // forward substitution for km / delta: P lanes per column, lane r
+        // owning tokens r, r + P, ...; right looking, so once delta_s is
+        // known (from its owner, by shuffle) it enters every later km_t at
+        // once; each km_t still sums eL_t U_t, then A_t0 delta_0,
+        // A_t1 delta_1, ... in wy_chunk's order.  The loop holds everything
+        // in registers (no shared stores between the loads of A); km and
+        // delta of the owned tokens go to Uc and Dc after it.
+        {
+            const int c = tid / P, r = tid % P;
+            float kmv[NSLOT], vv[NSLOT], bb[NSLOT], dv[NSLOT];
 #pragma unroll
-            for (int t = 0; t < WY_C; t++) {
-                dl[t] = 0.0f;
-                if (t < nc) {
-                    float km = eL[t] * Uc[t * WY_CLD + tid];
+            for (int j = 0; j < NSLOT; j++) {
+                const int t = r + j * P;
+                kmv[j] = eL[t] * Uc[t * CLD + c];
+                vv[j] = Vc[t * CLD + c];
+                bb[j] = bet[t];
+                dv[j] = 0.0f;
+            }
 #pragma unroll
-                    for (int s2 = 0; s2 < t; s2++) km = __fmaf_rn(Am[t * (WY_C + 1) + s2], dl[s2], km);
-                    dl[t] = bet[t] * (Vc[t * WY_CLD + tid] - km);
-                    Dc[t * WY_CLD + tid] = dl[t];
-                    Ec[t * WY_CLD + tid] = eE[t] * dl[t];
-                    const long long tok = t0 + t;
-                    if (a.km) a.km[tok * a.km_tok + h * a.km_head + c0 + tid] = km;
-                    if (a.delta) a.delta[tok * a.delta_tok + h * a.delta_head + c0 + tid] = dl[t];
-                }
+            for (int s2 = 0; s2 < WY_C; s2++) {
+                constexpr int PM = P - 1;
+                const int js = s2 / P;
+                const float mine = bb[js] * (vv[js] - kmv[js]);
+                const float d = __shfl_sync(0xffffffffu, mine, (lane & ~PM) | (s2 & PM));
+                if (r == (s2 & PM)) dv[js] = d;
+#pragma unroll
+                for (int j = js; j < NSLOT; j++)
+                    if (r + j * P > s2) kmv[j] = __fmaf_rn(At[s2 * WY_AP + r + j * P], d, kmv[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < NSLOT; j++) {
+                const int t = r + j * P;
+                Dc[t * CLD + c] = dv[j];
+                Ec[t * CLD + c] = eE[t] * dv[j];
+                Uc[t * CLD + c] = kmv[j];
             }
         }
         __syncthreads();
-        // outputs for (token, column) pairs
-        for (int t = tg; t < nc; t += NTG) {
-            float o = eL[t] * Wc[t * WY_CLD + jj];
-            for (int s2 = 0; s2 <= t; s2++) o = __fmaf_rn(Mm[t * (WY_C + 1) + s2], Dc[s2 * WY_CLD + jj], o);
-            a.out[(t0 + t) * a.out_tok + h * a.out_head + c0 + jj] = o;
+        // outputs for (token, column) pairs; where a thread has several
+        // tokens, t and its mirror in the group's span go together so every
+        // thread's chains have equal length; km and delta leave with them
+        auto emit = [&](int t) {
+            if (t < nc) {
+                float o = eL[t] * Wc[t * CLD + jj];
+                for (int s2 = 0; s2 <= t; s2++) o = __fmaf_rn(Mm[t * (WY_C + 1) + s2], Dc[s2 * CLD + jj], o);
+                const long long tok = t0 + t;
+                a.out[tok * a.out_tok + h * a.out_head + c0 + jj] = o;
+                if (a.km) a.km[tok * a.km_tok + h * a.km_head + c0 + jj] = Uc[t * CLD + jj];
+                if (a.delta) a.delta[tok * a.delta_tok + h * a.delta_head + c0 + jj] = Dc[t * CLD + jj];
+            }
+        };
+        if constexpr (TPT == 1) {
+            emit(tg);
+        } else {
+            for (int base = 0; base < WY_C; base += 2 * NTG) {
+                emit(base + tg);
+                emit(base + 2 * NTG - 1 - tg);
+            }
         }
         // state for (row, column) pairs: exp(L_end) S0 + sum_t decay(end, t) k_t delta_t,
-        // four rows at a time so four chains are in flight
+        // RG consecutive rows per pass so RG chains are in flight and the
+        // k rows load as 16-byte vectors
         const float gend = eL[nc - 1];
-        for (int i = tg; i < GDN_KD; i += 4 * NTG) {
-            float x0 = gend * Sc[i * WY_CLD + jj], x1 = gend * Sc[(i + NTG) * WY_CLD + jj];
-            float x2 = gend * Sc[(i + 2 * NTG) * WY_CLD + jj], x3 = gend * Sc[(i + 3 * NTG) * WY_CLD + jj];
-            for (int t = 0; t < nc; t++) {
-                const float e = Ec[t * WY_CLD + jj];
-                const float *kr = Ks + t * WY_LD + i;
-                x0 = __fmaf_rn(kr[0], e, x0);
-                x1 = __fmaf_rn(kr[NTG], e, x1);
-                x2 = __fmaf_rn(kr[2 * NTG], e, x2);
-                x3 = __fmaf_rn(kr[3 * NTG], e, x3);
+#pragma unroll 1
+        for (int i0 = tg * RPT; i0 < tg * RPT + RPT; i0 += RG) {
+            float x[RG];
+#pragma unroll
+            for (int m4 = 0; m4 < RG; m4 += 4) {
+                const float4 sv = *reinterpret_cast<const float4 *>(St + jj * WY_SP + i0 + m4);
+                x[m4] = gend * sv.x;
+                x[m4 + 1] = gend * sv.y;
+                x[m4 + 2] = gend * sv.z;
+                x[m4 + 3] = gend * sv.w;
             }
-            Sc[i * WY_CLD + jj] = x0;
-            Sc[(i + NTG) * WY_CLD + jj] = x1;
-            Sc[(i + 2 * NTG) * WY_CLD + jj] = x2;
-            Sc[(i + 3 * NTG) * WY_CLD + jj] = x3;
+            for (int t = 0; t < nc; t++) {
+                const float e = Ec[t * CLD + jj];
+#pragma unroll
+                for (int m4 = 0; m4 < RG; m4 += 4) {
+                    const float4 kv = *reinterpret_cast<const float4 *>(Ks + t * WY_LD + i0 + m4);
+                    x[m4] = __fmaf_rn(kv.x, e, x[m4]);
+                    x[m4 + 1] = __fmaf_rn(kv.y, e, x[m4 + 1]);
+                    x[m4 + 2] = __fmaf_rn(kv.z, e, x[m4 + 2]);
+                    x[m4 + 3] = __fmaf_rn(kv.w, e, x[m4 + 3]);
+                }
+            }
+#pragma unroll
+            for (int m4 = 0; m4 < RG; m4 += 4)
+                *reinterpret_cast<float4 *>(St + jj * WY_SP + i0 + m4) = make_float4(x[m4], x[m4 + 1], x[m4 + 2], x[m4 + 3]);
         }
         __syncthreads();  // chunk buffers and the state columns are reused
     }
     cp_async_wait<0>();
-    for (int idx = tid; idx < GDN_KD * WY_CB; idx += GDN_KD) {
-        const int i = idx / WY_CB, c = idx - i * WY_CB;
-        S[(long long)i * GDN_KD + c0 + c] = Sc[i * WY_CLD + c];
+    for (int idx = tid; idx < GDN_KD * CB; idx += NT) {
+        const int i = idx / CB, c = idx - i * CB;
+        S[(long long)i * GDN_KD + c0 + c] = St[c * WY_SP + i];
     }
 }
 
-inline int gdn_wy_cols_launch(const GdnArgs &a, cudaStream_t st) {
+// 8 columns per CTA while the heads' CTAs stay within two per SM, else 16
+inline int gdn_wy_cols_launch(const GdnArgs &a, cudaStream_t st, const float *G = nullptr) {
     if (a.heads <= 0 || a.rows <= 0) return 0;
     if (a.nk <= 0) return (int)cudaErrorInvalidValue;
-    k_gdn_wy_cols<<<(unsigned)(a.heads * WY_NCB), GDN_KD, WY_COLS_SMEM, st>>>(a);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (a.heads * (GDN_KD / 8) <= 2 * sms)
+        k_gdn_wy_cols<8><<<(unsigned)(a.heads * (GDN_KD / 8)), WY_NT, wy_cols_smem<8>(), st>>>(a, G);
+    else
+        k_gdn_wy_cols<16><<<(unsigned)(a.heads * (GDN_KD / 16)), WY_NT, wy_cols_smem<16>(), st>>>(a, G);
     return (int)cudaGetLastError();
 }
 
@@ -895,7 +1032,10 @@ inline int gdn_prepare() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_gdn_wy_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_ROWS_SMEM);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gdn_wy_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_COLS_SMEM);
+        e = cudaFuncSetAttribute(k_gdn_wy_cols<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wy_cols_smem<8>());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gdn_wy_cols<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)wy_cols_smem<16>());
     if (e != cudaSuccess) return (int)e;
     done = 1;
     return 0;

@@ -13,6 +13,7 @@
 #include "mmq.cuh"
 #include "ew.cuh"
 #include "gdn.cuh"
+#include "wy_tc.cuh"
 #include "attn.cuh"
 #include "sample.cuh"
 #include "api.cuh"

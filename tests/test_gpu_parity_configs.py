@@ -237,10 +237,13 @@ def test_attn_prefill_vs_oracle_rows(L, heads, kvh, slot0, rows):
 
 
 @pytest.mark.parametrize("rows,heads,nk", [(525, 4, 2), (100, 16, 16)])
-def test_wy_column_split_equals_per_head(L, rows, heads, nk):
-    """q35_launch_gdn_step_wy runs the column-split kernel when the q / k rows
-    are 16-byte aligned and the per-head kernel otherwise (row strides of 129
-    floats here): the two give the same out, km, delta and state, bit for bit"""
+def test_wy_tensor_core_path_vs_per_head(L, rows, heads, nk):
+    """q35_launch_gdn_step_wy runs the tensor-core path (Gram matrices of
+    32-token chunks, two chunks per 128-row tcgen05 kind::tf32 tile with a
+    3xTF32 split, feeding the column-split recurrence) when the q / k rows
+    are 16-byte aligned, and the per-head CUDA-core kernel otherwise (row
+    strides of 129 floats here): two re-associations of one recurrence,
+    within 1e-5 of each other"""
     kd = 128
     rng = np.random.default_rng(rows + 3 * heads)
     k, q, v, bet, gam, state = _gdn_inputs(rng, heads, nk, kd, rows)
@@ -260,4 +263,57 @@ def test_wy_column_split_equals_per_head(L, rows, heads, nk):
                                     nk, kd, kd, rows, S))
         res.append([t.cpu().numpy() for t in (dout, dkm, ddl, ds)])
     for nm, a, b in zip(("out", "km", "delta", "state"), res[0], res[1]):
+        assert np.isfinite(a).all(), nm
+        assert _rel(a, b) < 1e-5, (nm, _rel(a, b))
+
+
+def test_wy_captured_column_split_equals_per_head(L):
+    """inside a stream capture the Gram buffer of the tensor-core pass cannot
+    grow, so a sequence needing more than any earlier call runs the
+    column-split kernel with its own A / M dots (no G), which follows the
+    per-head kernel (the unaligned path) bit for bit; the graph's replay is
+    compared with the per-head result and with the tensor-core path's"""
+    kd, heads, nk, rows = 128, 16, 16, 4099
+    rng = np.random.default_rng(4099)
+    k, q, v, bet, gam, state = _gdn_inputs(rng, heads, nk, kd, rows)
+    dv, db, dg = (torch.from_numpy(a).cuda() for a in (v, bet, gam))
+
+    def call(ld, stream, rows_):
+        kp = np.zeros((rows_, ld), np.float32)
+        qp = np.zeros((rows_, ld), np.float32)
+        kp[:, :nk * kd] = k[:rows_].reshape(rows_, -1)
+        qp[:, :nk * kd] = q[:rows_].reshape(rows_, -1)
+        dk, dq = torch.from_numpy(kp).cuda(), torch.from_numpy(qp).cuda()
+        ds = torch.from_numpy(state).cuda()
+        dkm, ddl, dout = (torch.zeros((rows_, heads * kd), device="cuda") for _ in range(3))
+        torch.cuda.synchronize()
+
+        def run():
+            ok(L.q35_launch_gdn_step_wy(ds.data_ptr(), kd * kd, dk.data_ptr(), ld, dv.data_ptr(), heads * kd,
+                                        dq.data_ptr(), ld, dkm.data_ptr(), heads * kd, ddl.data_ptr(), heads * kd,
+                                        dout.data_ptr(), heads * kd, dg.data_ptr(), heads, db.data_ptr(), heads,
+                                        heads, nk, kd, kd, rows_, stream))
+        return run, (dout, dkm, ddl, ds), (dk, dq)
+
+    run, _, _ = call(nk * kd, S, 64)  # a small aligned call: every launch attribute set
+    run()
+    torch.cuda.synchronize()
+    run, per_head, _keep1 = call(nk * kd + 1, S, rows)
+    run()
+    gs = torch.cuda.Stream()
+    with torch.cuda.stream(gs):
+        run, captured, _keep2 = call(nk * kd, ctypes.c_void_p(gs.cuda_stream), rows)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
+            run()
+    graph.replay()
+    torch.cuda.synchronize()
+    run, tensor_core, _keep3 = call(nk * kd, S, rows)
+    run()
+    torch.cuda.synchronize()
+    for nm, a, b, c in zip(("out", "km", "delta", "state"), captured, per_head, tensor_core):
+        a, b, c = (t.cpu().numpy() for t in (a, b, c))
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), nm
+        assert _rel(c, b) < 1e-5, (nm, _rel(c, b))
+    del graph
+    no_kernel_error(L)
