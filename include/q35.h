@@ -48,6 +48,8 @@ extern "C" {
 #define Q35_TT_Q6_K 14
 #define Q35_TT_Q8_K 15
 #define Q35_TT_IQ4_NL 20
+#define Q35_TT_IQ4_XS 23
+#define Q35_TT_BF16 30
 
 /* device capability probe (api.h:35-37) */
 int q35_gpu_cc(void);
@@ -70,15 +72,19 @@ int q35_launch_dequantize_row(int ttype, const void *d_src_row, float *d_dst, in
 
 /* matvec (api.h:110-124): out[t*rows + r] = W[r] . xq[t], bit-exact with the
  * reference scalar CPU tier (per-block integer dot, f32 fold in block order).
- * Types: Q8_0, IQ4_NL, Q4_K, Q5_K, Q6_K; others -> cudaErrorInvalidValue. */
+ * Types: Q8_0, IQ4_NL, Q4_0, Q4_1, Q5_0, Q5_1 (Q8_0 activation) and Q4_K,
+ * Q5_K, Q6_K, IQ4_XS (Q8_K activation; IQ4_XS folds one term per 32-element
+ * sub-block, iq_kernels.c:967-1000); others -> cudaErrorInvalidValue. */
 int q35_launch_mul_mat_vec(const void *d_w, const void *d_xq, float *d_out, int rows, int cols, int tokens,
                            int ttype, void *stream);
 int q35_launch_mul_mat_vec_q8_0(const void *d_w, const void *d_xq, float *d_out, int rows, int cols,
                                 int tokens, void *stream);
+/* f32 weights x f32 activation (reference mmvq.cu:994) and f16 / bf16
+ * weights x f32 activation (mmvq.cu:1011): the reference's CUDA order, one
+ * chain per (row, token) acc = fmaf(w[c], x[c], acc) over c = 0..cols-1, the
+ * 2-byte weights widened exactly (mmvq.cu:339-367, dotq.cuh:202-218). */
 int q35_launch_mul_mat_vec_f32(const float *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens,
                                void *stream);
-/* f16 / bf16 weights x f32 activation (reference mmvq.cu:1011): per-32 block
- * serial sums folded in block order, as rowDotF16 / rowDotBF16. */
 int q35_launch_mul_mat_vec_w16(const void *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens,
                                int ttype, void *stream);
 /* prefill tile path (mmq.cu:2232-2245 in the reference): returns -1

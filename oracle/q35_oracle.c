@@ -120,6 +120,7 @@ int q35o_block_geom(int ttype, int *elems, int *bytes)
     case Q35O_TT_Q4_K: e = 256; b = 144; break;
     case Q35O_TT_Q5_K: e = 256; b = 176; break;
     case Q35O_TT_Q6_K: e = 256; b = 210; break;
+    case Q35O_TT_IQ4_XS: e = 256; b = 136; break;
     case Q35O_TT_Q8_K: e = 256; b = 292; break;
     default: return 0;
     }
@@ -551,6 +552,20 @@ static void dequant_block(int ttype, const uint8_t *x, float *out)
         }
         break;
     }
+    case Q35O_TT_IQ4_XS: { /* quant_dequant.zig:323-345: dl = d * (ls - 32) per 32 */
+        const float d = f16at(x);
+        const int sh = x[2] | (x[3] << 8);
+        for (int ib = 0; ib < 8; ib++) {
+            const int ls = ((x[4 + ib / 2] >> (4 * (ib % 2))) & 0x0F) | (((sh >> (2 * ib)) & 3) << 4);
+            const float dl = d * (float)(ls - 32);
+            const uint8_t *qs = x + 8 + 16 * ib;
+            for (int j = 0; j < 16; j++) {
+                out[32 * ib + j] = dl * (float)kIq4nl[qs[j] & 0x0F];
+                out[32 * ib + 16 + j] = dl * (float)kIq4nl[qs[j] >> 4];
+            }
+        }
+        break;
+    }
     case Q35O_TT_Q4_K:
     case Q35O_TT_Q5_K: { /* quant_dequant.zig:54-76, 188-220 */
         const int q5 = ttype == Q35O_TT_Q5_K;
@@ -755,6 +770,28 @@ float q35o_vec_dot(int ttype, int n, const uint8_t *w, const uint8_t *xq)
     }
     int e, b;
     q35o_block_geom(ttype, &e, &b);
+    if (ttype == Q35O_TT_IQ4_XS) {
+        /* iq_kernels.c:967-1000 (scalar tier): d4d8 = d * dy; per 32-element
+         * sub-block d1 = d4d8 * (ls - 32), sumf += d1 * (sumi1 + sumi2) */
+        for (int i = 0; i < n / 256; i++) {
+            const uint8_t *x = w + (size_t)i * b, *y = xq + (size_t)i * 292;
+            const float d4d8 = f16at(x) * f32at(y);
+            const int sh = x[2] | (x[3] << 8);
+            const int8_t *q8 = (const int8_t *)(y + 4);
+            for (int ib = 0; ib < 8; ib++) {
+                const int ls = ((x[4 + ib / 2] >> (4 * (ib % 2))) & 0x0F) | (((sh >> (2 * ib)) & 3) << 4);
+                const float d1 = d4d8 * (float)(ls - 32);
+                const uint8_t *qs = x + 8 + 16 * ib;
+                int32_t s1 = 0, s2 = 0;
+                for (int j = 0; j < 16; j++) {
+                    s1 += (int32_t)q8[32 * ib + j] * (int32_t)kIq4nl[qs[j] & 0x0F];
+                    s2 += (int32_t)q8[32 * ib + 16 + j] * (int32_t)kIq4nl[qs[j] >> 4];
+                }
+                sumf += d1 * (float)(s1 + s2);
+            }
+        }
+        return sumf;
+    }
     for (int i = 0; i < n / 256; i++) {
         const uint8_t *x = w + (size_t)i * b, *y = xq + (size_t)i * 292;
         int32_t isum, msum;
@@ -769,6 +806,36 @@ float q35o_vec_dot(int ttype, int n, const uint8_t *w, const uint8_t *xq)
         }
     }
     return sumf;
+}
+
+void q35o_matvec_f32(const float *w, const float *x, float *out, int rows, int cols, int tokens)
+{
+    for (int t = 0; t < tokens; t++)
+        for (int r = 0; r < rows; r++) {
+            float acc = 0.0f;
+            for (int c = 0; c < cols; c++) acc = fmaf(w[(size_t)r * cols + c], x[(size_t)t * cols + c], acc);
+            out[(size_t)t * rows + r] = acc;
+        }
+}
+
+void q35o_matvec_w16(int ttype, const uint16_t *w, const float *x, float *out, int rows, int cols, int tokens)
+{
+    for (int t = 0; t < tokens; t++)
+        for (int r = 0; r < rows; r++) {
+            float acc = 0.0f;
+            for (int c = 0; c < cols; c++) {
+                const uint16_t h = w[(size_t)r * cols + c];
+                float wv;
+                if (ttype == 30) {
+                    const uint32_t bits = (uint32_t)h << 16;
+                    memcpy(&wv, &bits, 4);
+                } else {
+                    wv = q35o_f16_to_f32(h);
+                }
+                acc = fmaf(wv, x[(size_t)t * cols + c], acc);
+            }
+            out[(size_t)t * rows + r] = acc;
+        }
 }
 
 void q35o_matvec_q(int ttype, const uint8_t *w, const uint8_t *xq, float *out,

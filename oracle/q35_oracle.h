@@ -70,6 +70,7 @@ extern "C" {
 #define Q35O_TT_Q6_K 14
 #define Q35O_TT_Q8_K 15
 #define Q35O_TT_IQ4_NL 20
+#define Q35O_TT_IQ4_XS 23
 
 /* ---- formats -------------------------------------------------------- */
 float q35o_f16_to_f32(uint16_t h);
@@ -107,6 +108,11 @@ float q35o_vec_dot(int ttype, int n, const uint8_t *w, const uint8_t *xq);
 int32_t q35o_block_isum(int ttype, const uint8_t *wblk, const uint8_t *xblk);
 
 /* out[t*rows + r] = W[r] . xq[t]; xq already quantized for the family */
+/* unquantized weights x f32 activation, the reference CUDA order
+ * (mmvq.cu:339-367, dotq.cuh:202-218): acc = fmaf(w[c], x[c], acc) per row;
+ * w16: ttype 1 (f16) or 30 (bf16), widened exactly */
+void q35o_matvec_f32(const float *w, const float *x, float *out, int rows, int cols, int tokens);
+void q35o_matvec_w16(int ttype, const uint16_t *w, const float *x, float *out, int rows, int cols, int tokens);
 void q35o_matvec_q(int ttype, const uint8_t *w, const uint8_t *xq, float *out,
                    int rows, int cols, int tokens);
 /* quantize x (tokens x cols f32) then matvec */

@@ -36,6 +36,7 @@ float q5_1_q8_0(int n, const void *vx, const void *vy);
 float q4_k_q8_k(int n, const void *vx, const void *vy);
 float q5_k_q8_k(int n, const void *vx, const void *vy);
 float q6_k_q8_k(int n, const void *vx, const void *vy);
+float iq4_xs_q8_k(int n, const void *vx, const void *vy);  /* iq_kernels.c:1004 */
 void quantize_q8_0(int n, const float *x, uint8_t *out);
 void quantize_q8_K(int n, const float *x, uint8_t *out);
 
@@ -51,6 +52,7 @@ static float row_dot(int tt, int n, const uint8_t *w, const uint8_t *xq)
     case Q35O_TT_Q4_K: return q4_k_q8_k(n, w, xq);
     case Q35O_TT_Q5_K: return q5_k_q8_k(n, w, xq);
     case Q35O_TT_Q6_K: return q6_k_q8_k(n, w, xq);
+    case Q35O_TT_IQ4_XS: return iq4_xs_q8_k(n, w, xq);
     default: return q35o_vec_dot(tt, n, w, xq);
     }
 }

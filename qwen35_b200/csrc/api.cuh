@@ -144,15 +144,19 @@ int q35_launch_mul_mat_vec_q8_0(const void *d_w, const void *d_xq, float *d_out,
 int q35_launch_mul_mat_vec_f32(const float *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens,
                                void *stream) {
     if (rows <= 0 || cols <= 0 || tokens <= 0) return 0;
-    k_matvec_f32<<<dim3((unsigned)((rows + 7) / 8), (unsigned)tokens), 256, 0, S(stream)>>>(d_w, d_x, d_out, rows, cols);
+    k_matvec_seq<MV_F32><<<dim3((unsigned)((rows + 127) / 128), (unsigned)tokens), 128, 0, S(stream)>>>(
+        d_w, d_x, d_out, rows, cols);
     return (int)cudaGetLastError();
 }
 int q35_launch_mul_mat_vec_w16(const void *d_w, const float *d_x, float *d_out, int rows, int cols, int tokens, int ttype,
                                void *stream) {
     if (rows <= 0 || cols <= 0 || tokens <= 0) return 0;
-    if ((ttype != TT_F16 && ttype != TT_BF16) || cols % 32) return (int)cudaErrorInvalidValue;
-    k_matvec_w16<<<dim3((unsigned)((rows + 7) / 8), (unsigned)tokens), 256, 0, S(stream)>>>(
-        (const uint16_t *)d_w, d_x, d_out, rows, cols, ttype == TT_BF16);
+    if (ttype != TT_F16 && ttype != TT_BF16) return (int)cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((rows + 127) / 128), (unsigned)tokens);
+    if (ttype == TT_BF16)
+        k_matvec_seq<MV_BF16><<<grid, 128, 0, S(stream)>>>(d_w, d_x, d_out, rows, cols);
+    else
+        k_matvec_seq<MV_F16><<<grid, 128, 0, S(stream)>>>(d_w, d_x, d_out, rows, cols);
     return (int)cudaGetLastError();
 }
 int q35_launch_mul_mat_vec_tile(const void *, const void *, float *, int, int, int, int, void *) { return -1; }

@@ -20,7 +20,7 @@ namespace q35 {
 // GGUF TensorType ids (the values of api.h / src/gguf.zig:87-122).
 enum : int {
     TT_F32 = 0, TT_F16 = 1, TT_Q4_0 = 2, TT_Q4_1 = 3, TT_Q5_0 = 6, TT_Q5_1 = 7, TT_Q8_0 = 8, TT_Q4_K = 12, TT_Q5_K = 13,
-    TT_Q6_K = 14, TT_Q8_K = 15, TT_IQ4_NL = 20, TT_BF16 = 30,
+    TT_Q6_K = 14, TT_Q8_K = 15, TT_IQ4_NL = 20, TT_IQ4_XS = 23, TT_BF16 = 30,
     // engine-internal: Q6_K blocks padded from 210 to 224 bytes (same field
     // offsets, 14 zero bytes after d), so that rows are 16-byte multiples for
     // TMA; not a GGUF type id
@@ -54,8 +54,23 @@ __host__ __device__ inline Geom geom_of(int tt) {
     case TT_Q5_K: return {256, 176, 256};
     case TT_Q6_K: return {256, 210, 256};
     case TT_Q6_K_P: return {256, 224, 256};
+    case TT_IQ4_XS: return {256, 136, 256};
     default: return {0, 0, 0};
     }
+}
+
+// Elements per f32 term of the ordered fold: one term per native block,
+// except IQ4_XS, whose 256-element block contributes one term per 32-element
+// sub-block (iq_kernels.c:967-1000: sumf += d1 * (sumi1 + sumi2) per sub-block)
+__host__ __device__ inline int term_elems(int tt) { return tt == TT_IQ4_XS ? 32 : geom_of(tt).elems; }
+
+// IQ4_XS block (256 elements, 136 bytes): d (f16) @0, scales_h (u16) @2,
+// scales_l[4] @4, qs[128] @8; sub-block ib (32 elements) takes qs[16 ib ..
+// 16 ib + 15] (element j in the low nibble, j + 16 in the high nibble, as
+// IQ4_NL) and the 6-bit scale below, applied as ls - 32
+// (iq_kernels.c:96-103, 978-979)
+__host__ __device__ inline int iq4xs_ls(int scales_l_byte, int scales_h, int ib) {
+    return ((scales_l_byte >> (4 * (ib & 1))) & 0xF) | (((scales_h >> (2 * ib)) & 3) << 4);
 }
 
 // ---------------------------------------------------------------------------

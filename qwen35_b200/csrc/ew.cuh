@@ -295,44 +295,51 @@ __global__ void __launch_bounds__(256) k_argmax_split(const float *x, long long 
     }
 }
 
-// f32 weights x f32 activation: out[t*rows + r] = W[r] . x[t] (warp per row)
-__global__ void k_matvec_f32(const float *w, const float *x, float *out, int rows, int cols) {
-    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.y;
-    if (r >= rows) return;
-    const float *wr = w + (long long)r * cols, *xr = x + (long long)t * cols;
-    float s = 0.0f;
-    for (int c = lane; c < cols; c += 32) s = __fadd_rn(s, __fmul_rn(wr[c], xr[c]));
-    s = warp_sum(s);
-    if (lane == 0) out[(long long)t * rows + r] = s;
-}
-
-// f16 / bf16 weights (2 B per element, no block metadata) x f32 activation:
-// per 32-element block a serial f32 sum, blocks folded in order
-// (src/quant_dequant.zig:1352-1384 rowDotF16 / rowDotBF16).  Warp per row,
-// lane per block, lane 0 folds the block sums in block order.
-__global__ void k_matvec_w16(const uint16_t *w, const float *x, float *out, int rows, int cols, int bf16) {
-    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.y;
-    if (r >= rows) return;
-    const uint16_t *wr = w + (long long)r * cols;
+// Unquantized weights (f32, f16, bf16) x f32 activation, in the order of the
+// reference's CUDA kernels (mmvq.cu:339-367, dotq.cuh:202-218): one f32 chain
+// per (row, token), acc = fmaf(w[c], x[c], acc) for c = 0, 1, ..., cols - 1,
+// the weights widened exactly (bf16: bits << 16; f16: the half's value).  A
+// warp owns 32 rows: each 32-column chunk arrives as 32 coalesced row reads
+// (lane = column) while the previous chunk, transposed through shared
+// memory, feeds lane r's chain for row r; the activation chunk is one
+// coalesced read broadcast by shuffles.
+enum { MV_F32 = 0, MV_F16 = 1, MV_BF16 = 2 };
+template <int KIND>
+__global__ void __launch_bounds__(128) k_matvec_seq(const void *__restrict__ w, const float *__restrict__ x,
+                                                    float *__restrict__ out, int rows, int cols) {
+    __shared__ float tw[4][32][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = blockIdx.y;
+    const long long r0 = ((long long)blockIdx.x * 4 + warp) * 32;
+    if (r0 >= rows) return;
+    const int nr = (int)min(32LL, (long long)rows - r0);
     const float *xr = x + (long long)t * cols;
-    const int nb = cols / 32;
-    float sum = 0.0f;
-    for (int b0 = 0; b0 < nb; b0 += 32) {
-        const int b = b0 + lane;
-        float acc = 0.0f;
-        if (b < nb)
-            for (int k = 0; k < 32; k++) {
-                const uint16_t h = wr[b * 32 + k];
-                const float wv = bf16 ? __uint_as_float((uint32_t)h << 16) : __half2float(__ushort_as_half(h));
-                acc = __fadd_rn(acc, __fmul_rn(wv, xr[b * 32 + k]));
-            }
-        const int n = min(32, nb - b0);
-        for (int j = 0; j < n; j++) {
-            const float v = __shfl_sync(0xffffffffu, acc, j);
-            sum = __fadd_rn(sum, v);
-        }
+    float(*T)[33] = tw[warp];
+    auto ld = [&](int rr, int c) -> float {
+        if (rr >= nr || c >= cols) return 0.0f;
+        const long long off = (r0 + rr) * cols + c;
+        if (KIND == MV_F32) return static_cast<const float *>(w)[off];
+        const uint16_t h = static_cast<const uint16_t *>(w)[off];
+        return KIND == MV_BF16 ? __uint_as_float((uint32_t)h << 16) : __half2float(__ushort_as_half(h));
+    };
+    float cur[32], nxt[32];
+#pragma unroll
+    for (int rr = 0; rr < 32; rr++) cur[rr] = ld(rr, lane);
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < cols; c0 += 32) {
+        const bool more = c0 + 32 < cols;
+#pragma unroll
+        for (int rr = 0; rr < 32; rr++) nxt[rr] = more ? ld(rr, c0 + 32 + lane) : 0.0f;
+#pragma unroll
+        for (int rr = 0; rr < 32; rr++) T[rr][lane] = cur[rr];
+        const float xv = c0 + lane < cols ? xr[c0 + lane] : 0.0f;
+        __syncwarp();
+        const int nc = min(32, cols - c0);
+        for (int c = 0; c < nc; c++) acc = __fmaf_rn(T[lane][c], __shfl_sync(0xffffffffu, xv, c), acc);
+        __syncwarp();
+#pragma unroll
+        for (int rr = 0; rr < 32; rr++) cur[rr] = nxt[rr];
     }
-    if (lane == 0) out[(long long)t * rows + r] = sum;
+    if (lane < nr) out[(long long)t * rows + r0 + lane] = acc;
 }
 
 }  // namespace q35

@@ -72,6 +72,7 @@ __host__ __device__ inline int gemv_act_stride(int cols, int family) {
 struct ActView {
     const uint8_t *base;
     int stride, cols;
+    int il = 0;  // Q8_0 blocks staged in the IQ4_NL interleaved order (gemv_lpr.cuh)
     Q35_DEV const int8_t *qs(int t) const { return reinterpret_cast<const int8_t *>(base + t * stride); }
     Q35_DEV float dsc(int t, int b) const {
         return reinterpret_cast<const float *>(base + t * stride + cols)[b];
@@ -126,6 +127,35 @@ Q35_DEV void part_iq4_nl(const uint8_t *wb, const ActView &A, int ntok, int b, i
             is[t] = dot4x4(hi[0], hi[1], hi[2], hi[3], y1, s);
         }
     }
+}
+
+// IQ4_XS sub-block b (32 elements) of the 256-element block at wb: the
+// IQ4_NL lookup on its 16 bytes of nibbles, Q8_K activation elements 32b..
+template <int NT>
+Q35_DEV void part_iq4_xs(const uint8_t *wb, const ActView &A, int ntok, int b, int (&is)[NT]) {
+    uint32_t q[4], lo[4], hi[4];
+    lds_words_a2<4>(wb + 8 + 16 * (b & 7), q);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        lo[i] = iq4_lookup4(q[i] & 0x0F0F0F0Fu);
+        hi[i] = iq4_lookup4((q[i] >> 4) & 0x0F0F0F0Fu);
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        if (t < ntok) {
+            const uint4 y0 = A.q16(t, b * 32), y1 = A.q16(t, b * 32 + 16);
+            int s = dot4x4(lo[0], lo[1], lo[2], lo[3], y0, 0);
+            is[t] = dot4x4(hi[0], hi[1], hi[2], hi[3], y1, s);
+        }
+    }
+}
+
+// f32 term of IQ4_XS sub-block ib (iq_kernels.c:975-990):
+// d4d8 = d * dy, d1 = d4d8 * (ls - 32), sumf += d1 * (float)isum
+Q35_DEV float iq4xs_term(const uint8_t *wb, int ib, float dy, int is) {
+    const float d4d8 = __fmul_rn(f16_to_f32(ld_u16(wb)), dy);
+    const int ls = iq4xs_ls(wb[4 + (ib >> 1)], ld_u16(wb + 2), ib);
+    return __fmul_rn(__fmul_rn(d4d8, __int2float_rn(ls - 32)), __int2float_rn(is));
 }
 
 // spread the 4 bits of x (bits 0..3) to bit 4 of bytes 0..3
@@ -278,7 +308,8 @@ Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, 
     for (int cb = 0; cb < nb; cb += BPP) {
         const int b = cb + j;
         const bool act = row_ok && b < nb;
-        const uint8_t *wb = rowp + (size_t)(act ? b : 0) * bsz;
+        // IQ4_XS: b counts 32-element sub-blocks, wb is their 256-element block
+        const uint8_t *wb = rowp + (size_t)(act ? (tt == TT_IQ4_XS ? b >> 3 : b) : 0) * bsz;
         int is[NT], ms[NT];
 #pragma unroll
         for (int t = 0; t < NT; t++) is[t] = 0, ms[t] = 0;
@@ -288,6 +319,8 @@ Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, 
                     part_q8_0<NT>(wb, A, ntok, b, is);
                 else if (tt == TT_IQ4_NL)
                     part_iq4_nl<NT>(wb, A, ntok, b, is);
+                else if (tt == TT_IQ4_XS)
+                    part_iq4_xs<NT>(wb, A, ntok, b, is);
                 else
                     part_legacy<NT>(tt, wb, A, ntok, b, is, ms);
             } else {
@@ -318,6 +351,8 @@ Q35_DEV void gemv_rows(int tt, const uint8_t *rowp0, int row_bytes, int nvalid, 
                         term = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb)), A.dsc(t, b)), __int2float_rn(is[t]));
                     } else if (legacy_type(tt)) {
                         term = legacy_term(tt, wb, A.dsc(t, b), is[t], ms[t]);
+                    } else if (tt == TT_IQ4_XS) {
+                        term = iq4xs_term(wb, b & 7, A.dsc(t, b >> 3), is[t]);
                     } else if (tt == TT_Q6_K || tt == TT_Q6_K_P) {
                         // sumf += d_w * dy * (float)isum
                         term = __fmul_rn(__fmul_rn(f16_to_f32(ld_u16(wb + 208)), A.dsc(t, b)), __int2float_rn(is[t]));
@@ -483,8 +518,8 @@ __global__ void __launch_bounds__(GV_THREADS) k_gemv(const __grid_constant__ Gem
         const int nr = (int)min((long long)sg.rows_per_tile, sg.rows - r0);
         const uintptr_t start = reinterpret_cast<uintptr_t>(sg.w) + (uintptr_t)r0 * sg.row_bytes;
         const uint8_t *buf = stages + (size_t)s * stage_ld + (start & 15);
-        const int nb = a.cols / geom_of(sg.ttype).elems;
-        const bool lpb1 = geom_of(sg.ttype).elems == 32;
+        const int nb = a.cols / term_elems(sg.ttype);  // f32 terms per row
+        const bool lpb1 = term_elems(sg.ttype) == 32;
         for (int rg = warp * R; rg < nr; rg += GV_WARPS * R) {
             const int nv = min(R, nr - rg);
             if (lpb1)

@@ -76,6 +76,7 @@ struct LprArgs {
     long long px_ld;
     float eps;
     int x_off;              // byte offset of the staged f32 rows (norm)
+    int il;                 // every matrix IQ4_NL / every one IQ4_XS: the activation is staged interleaved
     // pair mode (the MLP's gate / up projections): seg[0] = gate, seg[1] =
     // up, same rows; tile 2t is gate tile t and tile 2t+1 up tile t, taken
     // by row groups 2p and 2p+1 of one CTA.  The epilogue forms
@@ -199,16 +200,39 @@ Q35_DEV float f16_hi(uint32_t w) { return f16_to_f32((uint16_t)(w >> 16)); }
 // four low nibbles (elements j..j+3), hi = of the four high nibbles
 // (elements j+16..j+19).  Byte permutes over the codebook split in halves;
 // bit 3 of each index then picks the half.
-Q35_DEV void iq4_word(uint32_t q, uint32_t &lo, uint32_t &hi) {
-    const uint32_t s = q & 0x77777777u;
+// iq4_word_il: the values in nibble order, v0 = [lo b0, hi b0, lo b1, hi b1]
+// and v1 = [lo b2, hi b2, lo b3, hi b3] (elements j, j+16, j+1, j+17 and
+// j+2, j+18, j+3, j+19), which an activation staged in the same interleaved
+// order (lpr_interleave_act) dots without re-ordering.
+Q35_DEV void iq4_word_il(uint32_t q, uint32_t &v0, uint32_t &v1) {
+    const uint32_t s = q & 0x77777777u, s1 = s >> 16;
     const uint32_t l0 = __byte_perm(kIq4T0, kIq4T1, s), h0 = __byte_perm(kIq4T2, kIq4T3, s);
-    const uint32_t l1 = __byte_perm(kIq4T0, kIq4T1, s >> 16), h1 = __byte_perm(kIq4T2, kIq4T3, s >> 16);
-    // nibble n of q -> value n: choose the upper table half where bit 3 is set
-    const uint32_t v0 = __byte_perm(l0, h0, 0x3210u | ((q >> 1) & 0x4444u));
-    const uint32_t v1 = __byte_perm(l1, h1, 0x3210u | ((q >> 17) & 0x4444u));
-    // v0 = [lo b0, hi b0, lo b1, hi b1], v1 = [lo b2, hi b2, lo b3, hi b3]
+    const uint32_t l1 = __byte_perm(kIq4T0, kIq4T1, s1), h1 = __byte_perm(kIq4T2, kIq4T3, s1);
+    // nibble n of q -> value n: choose the upper table half where bit 3 is
+    // set; one mask serves both halves (a permute reads 16 selector bits)
+    const uint32_t m = ((q >> 1) & 0x44444444u) | 0x32103210u;
+    v0 = __byte_perm(l0, h0, m);
+    v1 = __byte_perm(l1, h1, m >> 16);
+}
+Q35_DEV void iq4_word(uint32_t q, uint32_t &lo, uint32_t &hi) {
+    uint32_t v0, v1;
+    iq4_word_il(q, v0, v1);
     lo = __byte_perm(v0, v1, 0x6420u);
     hi = __byte_perm(v0, v1, 0x7531u);
+}
+
+// One 32-element Q8_0 activation block (8 words) re-ordered in place so
+// word 2i + h holds elements 4i+2h, 16+4i+2h, 4i+2h+1, 17+4i+2h: the order
+// iq4_word_il leaves the weights in.  Integer dots are exact in any order.
+Q35_DEV void lpr_interleave_act(uint32_t *w) {
+    uint32_t x[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) x[i] = w[i];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        w[2 * i] = __byte_perm(x[i], x[i + 4], 0x5140u);
+        w[2 * i + 1] = __byte_perm(x[i], x[i + 4], 0x7362u);
+    }
 }
 
 // byte k of the 12 K-quant scale bytes held in words S[0..2]
@@ -280,7 +304,8 @@ Q35_DEV void lpr_q8_0(const uint8_t *rp, const ActView &A, int ntok, int gb0, in
     }
 }
 
-template <int NT, class Sink>
+// IL: the activation is staged interleaved (lpr_interleave_act)
+template <int NT, bool IL, class Sink>
 Q35_DEV void lpr_iq4_nl(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
     for (int g = 0; g < nblk; g += 8) {  // 8 blocks = 144 bytes = 9 x 16
         uint32_t W[36];
@@ -307,16 +332,85 @@ Q35_DEV void lpr_iq4_nl(const uint8_t *rp, const ActView &A, int ntok, int gb0, 
 #pragma unroll
                 for (int i = 0; i < 4; i++) q[i] = W[w0 + 1 + i];
             }
-            uint32_t lo[4], hi[4];
+            uint32_t lo[4], hi[4];  // IL: v0 / v1 of each word
 #pragma unroll
-            for (int i = 0; i < 4; i++) iq4_word(q[i], lo[i], hi[i]);
+            for (int i = 0; i < 4; i++) {
+                if (IL)
+                    iq4_word_il(q[i], lo[i], hi[i]);
+                else
+                    iq4_word(q[i], lo[i], hi[i]);
+            }
             const int b = gb0 + g + k;
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t < ntok) {
-                    const int s0 = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, b * 32), 0);
-                    const int si = s0 + dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, b * 32 + 16), 0);
+                    int si;
+                    if (IL) {
+                        const int s0 = dot4x4(lo[0], hi[0], lo[1], hi[1], A.q16(t, b * 32), 0);
+                        si = s0 + dot4x4(lo[2], hi[2], lo[3], hi[3], A.q16(t, b * 32 + 16), 0);
+                    } else {
+                        const int s0 = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, b * 32), 0);
+                        si = s0 + dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, b * 32 + 16), 0);
+                    }
                     sk.put(t, b, __fmul_rn(__fmul_rn(dx, A.dsc(t, b)), __int2float_rn(si)));
+                }
+            }
+        }
+    }
+}
+
+// IQ4_XS: two 136-byte blocks per 272-byte step (chunks of 512 columns).
+// Eight f32 terms per block, one per 32-element sub-block, in sub-block
+// order: d4d8 = d * dy, term = (d4d8 * (ls - 32)) * isum
+// (iq_kernels.c:967-1000).  IL: the Q8_K plane is staged interleaved.
+template <int NT, bool IL, class Sink>
+Q35_DEV void lpr_iq4_xs(const uint8_t *rp, const ActView &A, int ntok, int gb0, int nblk, Sink &sk) {
+    for (int g = 0; g < nblk; g += 2) {
+        uint32_t W[68];
+        const uint4 *s = reinterpret_cast<const uint4 *>(rp + g * 136);
+#pragma unroll
+        for (int i = 0; i < 17; i++) {
+            const uint4 v = s[i];
+            W[4 * i] = v.x;
+            W[4 * i + 1] = v.y;
+            W[4 * i + 2] = v.z;
+            W[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int w0 = 34 * k;  // 136 bytes = 34 words: both blocks word-aligned
+            const int b = gb0 + g + k;
+            const float d = f16_lo(W[w0]);
+            const int sh = (int)(W[w0] >> 16);
+            const uint32_t sl = W[w0 + 1];
+            float d4d8[NT];
+#pragma unroll
+            for (int t = 0; t < NT; t++) d4d8[t] = t < ntok ? __fmul_rn(d, A.dsc(t, b)) : 0.0f;
+#pragma unroll
+            for (int ib = 0; ib < 8; ib++) {
+                uint32_t lo[4], hi[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    if (IL)
+                        iq4_word_il(W[w0 + 2 + 4 * ib + i], lo[i], hi[i]);
+                    else
+                        iq4_word(W[w0 + 2 + 4 * ib + i], lo[i], hi[i]);
+                }
+                const float dls = __int2float_rn(iq4xs_ls((int)((sl >> (8 * (ib >> 1))) & 0xFFu), sh, ib) - 32);
+                const int e0 = b * 256 + ib * 32;
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    if (t < ntok) {
+                        int si;
+                        if (IL) {
+                            const int s0 = dot4x4(lo[0], hi[0], lo[1], hi[1], A.q16(t, e0), 0);
+                            si = s0 + dot4x4(lo[2], hi[2], lo[3], hi[3], A.q16(t, e0 + 16), 0);
+                        } else {
+                            const int s0 = dot4x4(lo[0], lo[1], lo[2], lo[3], A.q16(t, e0), 0);
+                            si = s0 + dot4x4(hi[0], hi[1], hi[2], hi[3], A.q16(t, e0 + 16), 0);
+                        }
+                        sk.put(t, b * 8 + ib, __fmul_rn(__fmul_rn(d4d8[t], dls), __int2float_rn(si)));
+                    }
                 }
             }
         }
@@ -526,12 +620,23 @@ template <int NT, class Sink>
 Q35_DEV void lpr_chunk(int tt, const uint8_t *rp, const ActView &A, int ntok, int c, int chunk_cols, Sink &sk) {
     switch (tt) {
     case TT_Q8_0: lpr_q8_0<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
-    case TT_IQ4_NL: lpr_iq4_nl<NT>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
+    case TT_IQ4_NL:
+        if (A.il)
+            lpr_iq4_nl<NT, true>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk);
+        else
+            lpr_iq4_nl<NT, false>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk);
+        break;
     case TT_Q4_0: lpr_legacy<NT, TT_Q4_0>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_Q4_1: lpr_legacy<NT, TT_Q4_1>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_Q5_0: lpr_legacy<NT, TT_Q5_0>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_Q5_1: lpr_legacy<NT, TT_Q5_1>(rp, A, ntok, c * (chunk_cols / 32), chunk_cols / 32, sk); break;
     case TT_Q4_K: lpr_q45_k<NT, false>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
+    case TT_IQ4_XS:
+        if (A.il)
+            lpr_iq4_xs<NT, true>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk);
+        else
+            lpr_iq4_xs<NT, false>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk);
+        break;
     case TT_Q6_K_P: lpr_q6_k<NT>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
     default: lpr_q45_k<NT, true>(rp, A, ntok, c * (chunk_cols / 256), chunk_cols / 256, sk); break;
     }
@@ -707,9 +812,17 @@ __global__ void __launch_bounds__(lpr_cw_max(NT) * 32) k_gemv_lpr(const __grid_c
         }
     }
     __syncthreads();
+    if (a.il) {
+        const int nb = a.cols / 32;
+        for (int idx = threadIdx.x; idx < a.ntok * nb; idx += blockDim.x) {
+            const int t = idx / nb, b = idx - t * nb;
+            lpr_interleave_act(reinterpret_cast<uint32_t *>(act + (size_t)t * a.act_stride + b * 32));
+        }
+        __syncthreads();
+    }
 
-    const ActView A{act, a.act_stride, a.cols};
-    const int nb = a.cols / geom_of(a.seg[0].ttype).elems;  // blocks per row
+    const ActView A{act, a.act_stride, a.cols, a.il};
+    const int nb = a.cols / term_elems(a.seg[0].ttype);  // f32 terms per row
     bool failed = false;
     long long waited = 0;
     long long i = 0;
@@ -830,7 +943,8 @@ inline int gemv_lpr_prepare() {
 }
 
 inline bool lpr_type_ok(int tt) {
-    return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K || tt == TT_Q6_K_P || legacy_type(tt);
+    return tt == TT_Q8_0 || tt == TT_IQ4_NL || tt == TT_Q4_K || tt == TT_Q5_K || tt == TT_Q6_K_P || tt == TT_IQ4_XS ||
+           legacy_type(tt);
 }
 
 // f32 rows the launch quantizes itself (see LprArgs::prologue)
@@ -913,7 +1027,15 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
         if ((reinterpret_cast<uintptr_t>(pro->x) & 15u) || (pro->ld & 3)) return -1;
     }
     const int fam = geom_of(segs[0].ttype).family;
-    const int chunk_cols = LPR_CHUNK_COLS;
+    // IQ4_XS blocks are 136 bytes: two per chunk keep the chunk a 16-byte
+    // multiple (the TMA box rule); its eight terms per block need every
+    // matrix of the launch to be IQ4_XS
+    bool xs = false;
+    for (int i = 0; i < nseg; i++) xs = xs || segs[i].ttype == TT_IQ4_XS;
+    for (int i = 0; i < nseg && xs; i++)
+        if (segs[i].ttype != TT_IQ4_XS) return -1;
+    const int chunk_cols = xs ? 2 * LPR_CHUNK_COLS : LPR_CHUNK_COLS;
+    if (cols % chunk_cols) return -1;
     int rs = 0;
     long long T = 0;
     for (int i = 0; i < nseg; i++) {
@@ -933,7 +1055,7 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     Q35_TRY_RC(gemv_lpr_prepare());
     const int nsm = gemv_sm_count();
     const int nchunk = cols / chunk_cols;
-    const int nb = cols / (fam == 32 ? 32 : 256);
+    const int nb = cols / term_elems(segs[0].ttype);  // f32 terms per row
     const int tst = nb % 2 == 0 ? nb + 1 : nb;
     const int act_stride = gemv_act_stride(cols, fam);
 
@@ -1040,6 +1162,10 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
             a.eps = pro->eps;
         }
         long long tiles = 0;
+        // every matrix IQ4_NL (Q8_0 plane) or every one IQ4_XS (Q8_K plane)
+        a.il = 1;
+        for (int i = 0; i < nseg; i++)
+            if (segs[i].ttype != segs[0].ttype || (segs[i].ttype != TT_IQ4_NL && segs[i].ttype != TT_IQ4_XS)) a.il = 0;
         for (int i = 0; i < nseg; i++) {
             const Geom g = geom_of(segs[i].ttype);
             LprSeg &s = a.seg[i];

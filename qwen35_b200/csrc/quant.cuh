@@ -111,6 +111,16 @@ Q35_DEV float dequant_elem(int tt, const uint8_t *row, int i) {
         const int nib = j < 16 ? (x[2 + j] & 0xF) : (x[2 + j - 16] >> 4);
         return __fmul_rn(f16_to_f32(ld_u16(x)), (float)c_iq4nl[nib]);
     }
+    case TT_IQ4_XS: {
+        // quant_dequant.zig:323-345: dl = d * (ls - 32) per 32-element sub-block
+        const uint8_t *x = row + (i / 256) * 136;
+        const int k = i & 255, ib = k >> 5, j = k & 31;
+        const int ls = iq4xs_ls(x[4 + (ib >> 1)], ld_u16(x + 2), ib);
+        const float dl = __fmul_rn(f16_to_f32(ld_u16(x)), (float)(ls - 32));
+        const uint8_t *qs = x + 8 + 16 * ib;
+        const int nib = j < 16 ? (qs[j] & 0xF) : (qs[j - 16] >> 4);
+        return __fmul_rn(dl, (float)c_iq4nl[nib]);
+    }
     case TT_Q4_0:
     case TT_Q4_1:
     case TT_Q5_0:

@@ -13,9 +13,9 @@ HEADER = os.path.join(ROOT, "include", "q35.h")
 LIB_PATH = os.path.join(PKG, "lib", "libq35b.so")
 
 TT = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
-      "Q8_K": 15, "IQ4_NL": 20}
+      "Q8_K": 15, "IQ4_NL": 20, "IQ4_XS": 23}
 GEOM = {8: (32, 34), 20: (32, 18), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 12: (256, 144),
-        13: (256, 176), 14: (256, 210)}
+        13: (256, 176), 14: (256, 210), 23: (256, 136)}
 
 
 class Config(ctypes.Structure):

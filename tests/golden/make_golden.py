@@ -13,7 +13,7 @@ import os
 import shutil
 import sys
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "IQ4_NL", "Q4_0"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "IQ4_NL", "Q4_0", "Q4_1", "IQ4_XS", "F16"]
 
 
 def main():

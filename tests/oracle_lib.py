@@ -16,9 +16,9 @@ ORACLE_SO = os.path.join(ORACLE_DIR, "_build", "liboracle.so")
 REF_SO = os.path.join(ORACLE_DIR, "_ref", "libq35ref.so")
 
 TT = {"F32": 0, "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
-      "Q8_K": 15, "IQ4_NL": 20}
+      "Q8_K": 15, "IQ4_NL": 20, "IQ4_XS": 23}
 GEOM = {8: (32, 34), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18), 12: (256, 144),
-        13: (256, 176), 14: (256, 210)}
+        13: (256, 176), 14: (256, 210), 23: (256, 136)}
 
 f32p = ctypes.POINTER(ctypes.c_float)
 u8p = ctypes.POINTER(ctypes.c_uint8)
@@ -47,6 +47,8 @@ def _declare(lib):
         "q35o_vec_dot": (F, [I, I, u8p, u8p]),
         "q35o_block_isum": (ctypes.c_int32, [I, u8p, u8p]),
         "q35o_matvec_q": (V, [I, u8p, u8p, f32p, I, I, I]),
+        "q35o_matvec_f32": (V, [f32p, f32p, f32p, I, I, I]),
+        "q35o_matvec_w16": (V, [I, ctypes.c_void_p, f32p, f32p, I, I, I]),
         "q35o_matvec": (V, [I, u8p, f32p, f32p, I, I, I]),
         "q35o_rmsnorm": (V, [f32p, f32p, f32p, I, F]),
         "q35o_rmsnorm_rows": (V, [f32p, f32p, f32p, I, I, F]),

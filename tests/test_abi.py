@@ -72,6 +72,7 @@ def test_loads_and_binds_without_gpu(built):
     assert L.q35_quant_geom(14, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (256, 210)
     assert L.q35_quant_geom(3, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (32, 20)  # Q4_1
     assert L.q35_quant_geom(7, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (32, 24)  # Q5_1
+    assert L.q35_quant_geom(23, ctypes.byref(e), ctypes.byref(b)) == 1 and (e.value, b.value) == (256, 136)  # IQ4_XS
     assert L.q35_quant_geom(16, ctypes.byref(e), ctypes.byref(b)) == 0  # IQ2_XXS: not served
     assert L.q35_quant_act_block_elems(20) == 32 and L.q35_quant_act_block_elems(13) == 256
     assert L.q35_quant_act_block_elems(99) == 0

@@ -27,7 +27,7 @@ def L():
 
 
 @pytest.mark.parametrize("name,rb", [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210),
-                                     ("IQ4_NL", 144), ("Q4_0", 144)])
+                                     ("IQ4_NL", 144), ("Q4_0", 144), ("Q4_1", 160), ("IQ4_XS", 136)])
 def test_golden_dequant(L, name, rb):
     ax = np.fromfile(os.path.join(GOLD, "A_x.f32"), dtype=np.float32)
     rows = np.fromfile(os.path.join(GOLD, f"{name}.bin"), dtype=np.uint8).reshape(-1, rb)
@@ -59,7 +59,8 @@ def test_golden_rowdot_matches_dequant(L):
     here on the quantized activation the matvec path consumes: the only
     difference left is the f32 block fold, so the bar is 1e-5 relative."""
     ax = np.fromfile(os.path.join(GOLD, "A_x.f32"), dtype=np.float32)
-    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144), ("Q4_0", 144)]:
+    for name, rb in [("Q4_K", 144), ("Q5_K", 176), ("Q6_K", 210), ("IQ4_NL", 144), ("Q4_0", 144), ("Q4_1", 160),
+                     ("IQ4_XS", 136)]:
         tt = TT[name]
         rows = np.fromfile(os.path.join(GOLD, f"{name}.bin"), dtype=np.uint8).reshape(-1, rb)
         xq = quantize_act(L, tt, ax)
@@ -255,6 +256,7 @@ import ctypes, sys, numpy as np
 sys.path.insert(0, sys.argv[1])
 from oracle_lib import load_oracle, load_ref, quantize_weight, TT, fp, bp, row_bytes, act_row_bytes
 O = load_oracle(); R = ctypes.CDLL(sys.argv[2])
+rng = np.random.default_rng(11)
 def interleave_q5(w, tt):
     # GGUF Q5_0 / Q5_1 blocks -> the nibble order the reference's scalar
     # kernels read (element j in nibble j & 1 of qs[j / 2])
@@ -265,13 +267,17 @@ def interleave_q5(w, tt):
     q = np.concatenate([qs & 0x0F, qs >> 4], axis=1)  # element order 0..31
     w[:, off:off + 16] = (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
     return w.reshape(-1)
+def iq4xs_row(cols):
+    # any nibbles / scale bits are valid IQ4_XS; d a finite f16
+    w = rng.integers(0, 256, size=(cols // 256, 136), dtype=np.uint8)
+    w[:, 0:2] = (rng.uniform(0.5, 2.0, cols // 256) * 1e-3).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    return w.reshape(-1)
 for nm in ("q8_0_q8_0","iq4_nl_q8_0","q4_k_q8_k","q5_k_q8_k","q6_k_q8_k","q4_0_q8_0","q4_1_q8_0","q5_0_q8_0",
-           "q5_1_q8_0"):
+           "q5_1_q8_0","iq4_xs_q8_k"):
     getattr(R, nm).restype = ctypes.c_float
     getattr(R, nm).argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
 R.quantize_q8_0.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
 R.quantize_q8_K.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
-rng = np.random.default_rng(11)
 cols = 1024
 bad = 0
 for trial in range(40):
@@ -284,8 +290,9 @@ for trial in range(40):
     bad += (not np.array_equal(a0, b0)) + (not np.array_equal(ak, bk))
     for nm, tt in (("q8_0_q8_0","Q8_0"),("iq4_nl_q8_0","IQ4_NL"),("q4_k_q8_k","Q4_K"),("q5_k_q8_k","Q5_K"),
                    ("q6_k_q8_k","Q6_K"),("q4_0_q8_0","Q4_0"),("q4_1_q8_0","Q4_1"),("q5_0_q8_0","Q5_0"),
-                   ("q5_1_q8_0","Q5_1")):
-        w = quantize_weight(O, TT[tt], rng.standard_normal((1, cols)).astype(np.float32) * 0.02)[0]
+                   ("q5_1_q8_0","Q5_1"),("iq4_xs_q8_k","IQ4_XS")):
+        w = (iq4xs_row(cols) if tt == "IQ4_XS" else
+             quantize_weight(O, TT[tt], rng.standard_normal((1, cols)).astype(np.float32) * 0.02)[0])
         xq = a0 if tt in ("Q8_0","IQ4_NL","Q4_0","Q4_1","Q5_0","Q5_1") else ak
         wr = interleave_q5(w, tt) if (tt in ("Q5_0","Q5_1") and sys.argv[3] == "exact") else w
         r = np.float32(getattr(R, nm)(cols, wr.ctypes.data, xq.ctypes.data))
@@ -302,8 +309,10 @@ def _run_ref(mode):
     env = dict(os.environ)
     if mode == "exact":
         env["QWEN35_FORCE_SCALAR"] = "all"
+        env["QWEN35_IQ_FORCE_SCALAR"] = "1"  # the IQ kernels' own scalar switch (iq_kernels.c:1008)
     else:
         env.pop("QWEN35_FORCE_SCALAR", None)
+        env.pop("QWEN35_IQ_FORCE_SCALAR", None)
     r = subprocess.run([sys.executable, "-c", REF_PROBE, os.path.join(ROOT, "tests"), REF_SO, mode],
                        env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr
@@ -313,7 +322,7 @@ def _run_ref(mode):
 @pytest.mark.skipif(not os.path.exists(REF_SO), reason="reference kernels not built (no reference tree)")
 def test_against_reference_kernels_scalar_tier():
     """Oracle == reference x86 kernels' scalar tier, bit for bit, for the
-    five hot types and Q4_0 / Q4_1 / Q5_0 / Q5_1.  The reference's scalar
+    five hot types, Q4_0 / Q4_1 / Q5_0 / Q5_1 and IQ4_XS.  The reference's scalar
     Q5_0 / Q5_1 kernels read element j from nibble j & 1 of qs[j / 2]
     (kernels32.c:557, 640), unlike its AVX2 kernels and the GGUF format (low
     nibbles are elements 0..15): they are fed the same weights in that order,
@@ -344,3 +353,24 @@ def test_synth_generator_c_equals_numpy(L):
     assert abs(float(a.mean())) < 0.01 and abs(float(a.std()) - 1.0) < 0.01
     v = configs.synth_vector(3, 1000, "ssm_a")
     assert (v < 0).all() and v.min() >= -np.e and v.max() <= -1 / np.e
+
+
+def test_golden_f16_rows_w16_order(L):
+    """the reference's F16 known-answer rows (testdata/udtest/F16, 96 x 256)
+    through the oracle's restatement of the reference CUDA w16 kernel
+    (mmvq.cu:339-351: one fmaf chain per row).  The reference's own golden
+    check leaves F16 out (quant_dequant.zig:1185-1200) and its expected values
+    differ from an exact f64 dot by up to 1.7e-3 relative, so they serve as a
+    sanity band here (2e-3 relative); the order itself is pinned bit for bit
+    against the f32 chain below and against the GPU (tests/test_gpu_formats.py)"""
+    ax = np.fromfile(os.path.join(GOLD, "A_x.f32"), dtype=np.float32)
+    w = np.fromfile(os.path.join(GOLD, "F16.bin"), dtype=np.uint16).reshape(96, 256)
+    exp = np.fromfile(os.path.join(GOLD, "F16_expected.f32"), dtype=np.float32)
+    out = np.zeros(96, np.float32)
+    L.q35o_matvec_w16(1, w.ctypes.data, fp(ax), fp(out), 96, 256, 1)
+    assert (np.abs(out - exp) / np.maximum(1.0, np.abs(exp))).max() < 2e-3
+    # bf16 / f32: the same chain over exactly widened values
+    wf = w.astype(np.uint16).view(np.float16).astype(np.float32)
+    out32 = np.zeros(96, np.float32)
+    L.q35o_matvec_f32(fp(np.ascontiguousarray(wf)), fp(ax), fp(out32), 96, 256, 1)
+    assert np.array_equal(out32.view(np.uint32), out.view(np.uint32))
