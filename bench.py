@@ -296,8 +296,11 @@ def time_tp_decode(cfg_name, batch, ctx, steps, warmup, seed, dist, world, rank)
     context is synthetic: every slot steps from position `ctx` over the
     engine's zeroed KV pools and a zero GDN state, which reads and writes the
     same bytes per step as after a real prefill (values do not change the
-    work) without prefilling batch x ctx prompt tokens.  Returns (ms for
-    `steps` steps, max over ranks; this rank's weight bytes)."""
+    work) without prefilling batch x ctx prompt tokens.  With several ranks
+    the steps are timed twice on one engine: the row-parallel all-reduce
+    through NCCL, then through the peer all-reduce kernel.  Returns (ms for
+    `steps` steps with the peer all-reduce -- NCCL's at one rank -- max over
+    ranks; the NCCL form's ms or None; this rank's weight bytes)."""
     import numpy as np
     import torch
 
@@ -328,23 +331,34 @@ def time_tp_decode(cfg_name, batch, ctx, steps, warmup, seed, dist, world, rank)
             rc = eng.L.q35b_engine_advance(eng.h, batch, s)
             assert rc == 0, rc
 
-    run(warmup)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.nvtx.range_push("q35_timed")
-    e0.record(st)
-    run(steps)
-    e1.record(st)
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), dist)
+    def timed():
+        # every timed run starts at the same context (a second run on the
+        # engine would otherwise step past max_seq)
+        q35.device_view(eng.d_pos, batch, i32).fill_(ctx)
+        run(warmup)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("q35_timed")
+        e0.record(st)
+        run(steps)
+        e1.record(st)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1), dist)
+
+    ms, ms_nccl = timed(), None
+    if world > 1:
+        ms_nccl = ms
+        tp.connect_peers(dist, eng)
+        ms = timed()
+        dist.barrier()  # no rank unmaps or frees while another may still read it
     eng.close()  # its graphs hold NCCL work: released before the process group
     del m
     torch.cuda.empty_cache()
-    return ms, wbytes
+    return ms, ms_nccl, wbytes
 
 
 def max_over_ranks(v, dist):
@@ -955,11 +969,16 @@ def main():
         # 27B tensor-parallel over every rank of this run (strong scaling: the
         # batch of 32 sequences at 4096 context is fixed)
         ksteps = min(args.steps, 16)
-        tms, wb = time_tp_decode("27b", 32, 4096, ksteps, args.warmup, args.seed, dist, world, rank)
-        variants.append({"model": "qwen3.5-27b-q4_k", "tp": world, "batch": 32, "context": 4096,
-                         "context_fill": "synthetic (zero KV / GDN state, positions at 4096)",
-                         "steps": ksteps, "ms_per_step": tms / ksteps, "value": 32 * ksteps / (tms * 1e-3),
-                         "unit": "tokens/s", "scaling": "strong", "weight_bytes_per_rank": wb})
+        tms, tms_nccl, wb = time_tp_decode("27b", 32, 4096, ksteps, args.warmup, args.seed, dist, world, rank)
+        tpv = {"model": "qwen3.5-27b-q4_k", "tp": world, "batch": 32, "context": 4096,
+               "context_fill": "synthetic (zero KV / GDN state, positions at 4096)",
+               "steps": ksteps, "ms_per_step": tms / ksteps, "value": 32 * ksteps / (tms * 1e-3),
+               "unit": "tokens/s", "scaling": "strong", "weight_bytes_per_rank": wb}
+        if tms_nccl is not None:
+            tpv["allreduce"] = "peer (k_tp_allreduce_add: NVLink peer loads / stores, residual add fused)"
+            tpv["nccl_ms_per_step"] = tms_nccl / ksteps
+            tpv["nccl_value"] = 32 * ksteps / (tms_nccl * 1e-3)
+        variants.append(tpv)
         sms, sp, sg = time_serve("4b", args.seed, dist, world, rank)
         sms = max_over_ranks(sms, dist)
         variants.append({"model": "qwen3.5-4b-mixed", "workload": "continuous batching (BASELINE config 4): %d "

@@ -367,6 +367,24 @@ long long q35b_engine_launches_per_step(q35b_engine *e);
 int q35b_tp_unique_id(void *out, int bytes);
 int q35b_engine_set_tp(q35b_engine *e, int nranks, int rank, long long vocab_local, long long vocab_offset,
                        const void *unique_id);
+/* The peer all-reduce: the row-parallel all-reduce and the residual add as
+ * one kernel over NVLink peer memory (up to 8 ranks, hidden a multiple of
+ * 4 x nranks).  After finalize, q35b_engine_ipc_handles writes this rank's
+ * 192 bytes of CUDA IPC handles (partial sums, residual, flag words); the
+ * ranks exchange them (rank p's at offset 192 p) and each passes the whole
+ * set to q35b_engine_set_peers, which maps the other ranks' buffers and
+ * switches the engine to the peer form; q35b_engine_set_allreduce(e, 0 / 1)
+ * then selects NCCL or the peer form (every rank the same, between steps).
+ * Rank q sums the partials of hidden columns [q h/N, (q+1) h/N) in rank
+ * order, so all ranks hold the same residual bits; every wait is bounded (2 s)
+ * and records error 150 / 151 (q35b_get_error) instead of hanging. */
+int q35b_engine_ipc_handles(q35b_engine *e, void *out, int bytes);
+int q35b_engine_set_peers(q35b_engine *e, const void *all, int bytes);
+int q35b_engine_set_allreduce(q35b_engine *e, int peer);
+/* one GPU: runs the peer all-reduce kernel as rank 0 of two whose rank 1
+ * never runs, with waits bounded at limit_ns (<= 2 s); returns the stream's
+ * status, and q35b_get_error then reports 150 */
+int q35b_tp_selftest_timeout(unsigned long long limit_ns, void *stream);
 
 /* One forward over n tokens packed as nrun runs: run r is tokens
  * [run_end[r-1], run_end[r]) (run_end[-1] = 0), all of one slot at

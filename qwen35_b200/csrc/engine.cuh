@@ -165,11 +165,27 @@ __global__ void __launch_bounds__(256) k_attn_prelude(const float *qg, const flo
     }
 }
 
-__global__ void k_pos_to_len(const int *pos, int *len, int n) {
+// lengths from positions; positions outside [0, max_seq) and slots outside
+// [0, n_slots) are clamped in place (error 161 / 162 recorded), so the step's
+// KV, state and RoPE indexing stays inside the pools whatever the inputs
+__global__ void k_pos_to_len(int *pos, int *slots, int *len, int n, int max_seq, int n_slots) {
     pdl_trigger();
     pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) len[i] = pos[i] + 1;
+    if (i < n) {
+        int p = pos[i];
+        if (p < 0 || p >= max_seq) {
+            set_error(161);
+            p = p < 0 ? 0 : max_seq - 1;
+            pos[i] = p;
+        }
+        const int s = slots[i];
+        if (s < 0 || s >= n_slots) {
+            set_error(162);
+            slots[i] = 0;
+        }
+        len[i] = p + 1;
+    }
 }
 
 __global__ void k_copy_rows(float *dst, const float *src, long long n) {
@@ -230,6 +246,16 @@ struct q35b_engine {
     long long vocab_local = 0, vocab_off = 0;  // this rank's lm_head rows
     ncclComm_t comm = nullptr;
     float *part = nullptr;                     // row-parallel partial sums [n][hidden]
+    // the peer all-reduce (k_tp_allreduce_add): its own partial-sum buffer
+    // (never handed to NCCL, whose graph-captured collectives may register
+    // `part` with the driver), flag words and epoch state, every rank's
+    // buffers as mapped here, the mappings opened, and the mode
+    float *ppart = nullptr;
+    int *ar_flags = nullptr, *ar_state = nullptr;
+    q35::TpPeers peers{};
+    bool peers_open = false, ar_peer = false;
+    std::vector<void *> ipc_open;
+    unsigned long long ar_limit_ns = 5000000000ull;
     int *am_pair = nullptr, *am_all = nullptr; // (max, index) per run: local / every rank
     float *am_v = nullptr;                     // split argmax partials [max_batch][AM_SPLIT]
     float *mmq_terms = nullptr;                // split-K terms of the K-quant MMQ (row-parallel projections)
@@ -297,11 +323,15 @@ inline int eng_norm_gemv(q35b_engine *e, int n, const float *w, std::initializer
 // residual stream.  Under tensor parallelism they write partial sums, which
 // are all-reduced over the ranks and then added.
 inline GemvSegDesc eng_rowpar_seg(q35b_engine *e, const Lin &w) {
-    if (e->tp_n > 1) return {w.w, e->part, w.rows, w.tt, (long long)e->c.hidden, GV_STORE};
+    if (e->tp_n > 1) return {w.w, e->ar_peer ? e->ppart : e->part, w.rows, w.tt, (long long)e->c.hidden, GV_STORE};
     return {w.w, e->x, w.rows, w.tt, (long long)e->c.hidden, GV_ADD};
 }
 inline int eng_rowpar_finish(q35b_engine *e, int n, cudaStream_t st) {
     if (e->tp_n <= 1) return 0;
+    if (e->ar_peer) {
+        const TpArArgs a{e->peers, e->ar_state, e->tp_rank, e->tp_n, e->c.hidden, n, e->ar_limit_ns};
+        return tp_ar_launch(a, st);
+    }
     const long long cnt = (long long)n * e->c.hidden;
     const NcclApi &api = nccl_api();
     if (api.all_reduce(e->part, e->part, (size_t)cnt, ncclFloat32, ncclSum, e->comm, st) != ncclSuccess)
@@ -543,11 +573,11 @@ inline int eng_step_body(q35b_engine *e, int n, int nrun, int max_len, cudaStrea
     pdl_enabled() = false;
     const int rc_embed = launch_k(k_embed_rows, dim3((c.hidden + 255) / 256, n), dim3(256), 0, st, e->token_embd.tt,
                                   e->token_embd.w, (size_t)weight_row_bytes(e->token_embd.tt, c.hidden), tok, e->x,
-                                  c.hidden);
+                                  c.hidden, (long long)e->token_embd.rows);
     pdl_enabled() = true;
     Q35_TRY(rc_embed);
-    Q35_TRY(launch_k(k_pos_to_len, dim3((n + 127) / 128), dim3(128), 0, st, (const int *)(e->d_in + 2 * e->max_batch),
-                     e->d_len, n));
+    Q35_TRY(launch_k(k_pos_to_len, dim3((n + 127) / 128), dim3(128), 0, st, e->d_in + 2 * e->max_batch,
+                     e->d_in + e->max_batch, e->d_len, n, e->max_seq, e->n_slots));
     for (int li = 0; li < c.n_layers; li++) {
         if (is_full_layer(c, li))
             Q35_TRY(eng_layer_full(e, li, n, nrun, max_len, st));

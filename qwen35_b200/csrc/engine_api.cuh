@@ -52,6 +52,8 @@ int q35b_engine_destroy(q35b_engine *e) {
     // graphs holding collectives go before the communicator
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
+    for (void *p : e->ipc_open) cudaIpcCloseMemHandle(p);
+    e->ipc_open.clear();
     if (e->comm) nccl_api().comm_destroy(e->comm);
     for (void *p : e->allocs) cudaFree(p);
     if (e->h_io) cudaFreeHost(e->h_io);
@@ -118,6 +120,98 @@ int q35b_engine_set_tp(q35b_engine *e, int nranks, int rank, long long vocab_loc
     e->vocab_local = vocab_local;
     e->vocab_off = vocab_offset;
     return 0;
+}
+
+// ---- peer all-reduce (tp.cuh k_tp_allreduce_add) ----
+constexpr int TP_HANDLES = 3;  // partial sums, residual, flag words
+
+int q35b_engine_ipc_handles(q35b_engine *e, void *out, int bytes) {
+    if (!e || !e->finalized || e->tp_n < 2 || !out || bytes < TP_HANDLES * (int)sizeof(cudaIpcMemHandle_t))
+        return (int)cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h[TP_HANDLES];
+    const void *ptrs[TP_HANDLES] = {e->ppart, e->x, e->ar_flags};
+    for (int i = 0; i < TP_HANDLES; i++) {
+        const cudaError_t r = cudaIpcGetMemHandle(&h[i], const_cast<void *>(ptrs[i]));
+        if (r != cudaSuccess) return (int)r;
+    }
+    memcpy(out, h, sizeof(h));
+    return 0;
+}
+
+static void drop_graphs(q35b_engine *e) {
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+}
+
+int q35b_engine_set_peers(q35b_engine *e, const void *all, int bytes) {
+    const int hb = TP_HANDLES * (int)sizeof(cudaIpcMemHandle_t);
+    if (!e || !e->finalized || e->tp_n < 2 || e->tp_n > TP_MAX || !all || bytes < e->tp_n * hb || e->peers_open)
+        return (int)cudaErrorInvalidValue;
+    if (e->c.hidden % (4 * e->tp_n)) return (int)cudaErrorInvalidValue;  // owned slices of whole float4s
+    TpPeers pe{};
+    std::vector<void *> opened;
+    for (int p = 0; p < e->tp_n; p++) {
+        void *ptr[TP_HANDLES] = {e->ppart, e->x, e->ar_flags};
+        if (p != e->tp_rank) {
+            for (int i = 0; i < TP_HANDLES; i++) {
+                cudaIpcMemHandle_t h;
+                memcpy(&h, static_cast<const uint8_t *>(all) + (size_t)p * hb + (size_t)i * sizeof(h), sizeof(h));
+                const cudaError_t r = cudaIpcOpenMemHandle(&ptr[i], h, cudaIpcMemLazyEnablePeerAccess);
+                if (r != cudaSuccess) {
+                    for (void *q : opened) cudaIpcCloseMemHandle(q);
+                    return (int)r;
+                }
+                opened.push_back(ptr[i]);
+            }
+        }
+        pe.part[p] = static_cast<float *>(ptr[0]);
+        pe.x[p] = static_cast<float *>(ptr[1]);
+        pe.flags[p] = static_cast<int *>(ptr[2]);
+    }
+    e->peers = pe;
+    e->ipc_open = opened;
+    e->peers_open = true;
+    e->ar_peer = true;
+    drop_graphs(e);  // steps captured before hold the NCCL form
+    return 0;
+}
+
+int q35b_engine_set_allreduce(q35b_engine *e, int peer) {
+    if (!e || (peer && !e->peers_open)) return (int)cudaErrorInvalidValue;
+    if (e->ar_peer != (peer != 0)) drop_graphs(e);
+    e->ar_peer = peer != 0;
+    return 0;
+}
+
+// the bounded waits of k_tp_allreduce_add on one GPU: a two-rank exchange
+// whose second rank never runs (its flags are local words nothing sets);
+// the kernel gives up after limit_ns per wait and records error 150
+int q35b_tp_selftest_timeout(unsigned long long limit_ns, void *stream) {
+    if (limit_ns == 0 || limit_ns > 2000000000ull) return (int)cudaErrorInvalidValue;
+    void *buf = nullptr;
+    const size_t fl = 4 * TP_FLAG_WORDS;
+    cudaError_t r = cudaMalloc(&buf, 4 * 4 * 8 + 2 * fl + 8);
+    if (r != cudaSuccess) return (int)r;
+    r = cudaMemset(buf, 0, 4 * 4 * 8 + 2 * fl + 8);
+    float *f = static_cast<float *>(buf);
+    int *fl0 = reinterpret_cast<int *>(f + 32), *fl1 = fl0 + TP_FLAG_WORDS, *state = fl1 + TP_FLAG_WORDS;
+    TpArArgs a{};
+    a.pe.part[0] = f;
+    a.pe.part[1] = f + 8;
+    a.pe.x[0] = f + 16;
+    a.pe.x[1] = f + 24;
+    a.pe.flags[0] = fl0;
+    a.pe.flags[1] = fl1;
+    a.state = state;
+    a.rank = 0;
+    a.nranks = 2;
+    a.hidden = 8;
+    a.n = 1;
+    a.limit_ns = limit_ns;
+    if (r == cudaSuccess) r = (cudaError_t)tp_ar_launch(a, S(stream));
+    if (r == cudaSuccess) r = cudaStreamSynchronize(S(stream));
+    cudaFree(buf);
+    return (int)r;
 }
 
 int q35b_engine_set_tensor(q35b_engine *e, const char *name, int tt, const void *d, long long rows, long long cols) {
@@ -211,6 +305,11 @@ int q35b_engine_finalize(q35b_engine *e) {
         ALLOC(part, 4 * B * h);
         ALLOC(am_pair, 4 * 2 * B);
         ALLOC(am_all, 4 * 2 * B * e->tp_n);
+        ALLOC(ppart, 4 * B * h);
+        ALLOC(ar_flags, 4 * TP_FLAG_WORDS);
+        ALLOC(ar_state, 4 * 2);
+        Q35_TRY((int)cudaMemset(e->ar_flags, 0, 4 * TP_FLAG_WORDS));
+        Q35_TRY((int)cudaMemset(e->ar_state, 0, 4 * 2));
     }
     ALLOC(am_v, 4 * B * AM_SPLIT);
     ALLOC(am_i, 4 * B * AM_SPLIT);

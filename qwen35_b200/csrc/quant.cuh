@@ -175,12 +175,18 @@ __global__ void k_dequant_row(int tt, const uint8_t *__restrict__ row, float *__
 }
 
 // rows gathered by token id: out[t*cols + i] = dequant(W[tokens[t]])[i]
+// token ids outside [0, vocab) read row 0 and record error 160
 __global__ void k_embed_rows(int tt, const uint8_t *__restrict__ w, size_t row_bytes,
-                             const int *__restrict__ tokens, float *__restrict__ out, int cols) {
+                             const int *__restrict__ tokens, float *__restrict__ out, int cols, long long vocab) {
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.y;
-    const uint8_t *row = w + (size_t)tokens[t] * row_bytes;
+    long long tok = tokens[t];
+    if (tok < 0 || tok >= vocab) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) set_error(160);
+        tok = 0;
+    }
+    const uint8_t *row = w + (size_t)tok * row_bytes;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x)
         out[(size_t)t * cols + i] = dequant_elem(tt, row, i);
 }

@@ -165,6 +165,22 @@ class Engine:
                                          (ctypes.c_int * nrun)(*run_end), nx, _stream(stream)), "forward")
         return list(nx)
 
+    def ipc_handles(self):
+        """this rank's CUDA IPC handles for the peer all-reduce (bytes)"""
+        buf = ctypes.create_string_buffer(192)
+        check(self.L.q35b_engine_ipc_handles(self.h, ctypes.cast(buf, ctypes.c_void_p), 192), "ipc_handles")
+        return buf.raw
+
+    def set_peers(self, handles):
+        """map every rank's buffers (handles: the ranks' ipc_handles() in
+        rank order) and switch to the peer all-reduce"""
+        raw = b"".join(handles)
+        buf = ctypes.create_string_buffer(raw, len(raw))
+        check(self.L.q35b_engine_set_peers(self.h, ctypes.cast(buf, ctypes.c_void_p), len(raw)), "set_peers")
+
+    def set_allreduce(self, peer):
+        check(self.L.q35b_engine_set_allreduce(self.h, 1 if peer else 0), "set_allreduce")
+
     def set_prefill_wy(self, on):
         check(self.L.q35b_engine_set_prefill_wy(self.h, 1 if on else 0), "set_prefill_wy")
 

@@ -233,3 +233,15 @@ def shared_nccl_id(dist, device):
         buf.copy_(torch.frombuffer(bytearray(raw.raw), dtype=torch.uint8))
     dist.broadcast(buf, 0)
     return buf.cpu().numpy().tobytes()
+
+
+def connect_peers(dist, eng):
+    """exchange the engines' IPC handles over the process group `dist` and
+    map every rank's buffers, switching `eng` to the peer all-reduce (every
+    rank calls this, after its engine is built)"""
+    mine = eng.ipc_handles()
+    allh = [None] * dist.get_world_size()
+    dist.all_gather_object(allh, mine)
+    eng.set_peers(allh)
+    dist.barrier()
+

@@ -1,6 +1,7 @@
-"""Tensor-parallel decode on 2 GPUs (NCCL): two ranks, each running the
-engine on its shard, against one GPU running the whole model and against the
-CPU oracle stepping the whole model.
+"""Tensor-parallel decode on 2 GPUs: two ranks, each running the engine on
+its shard, against one GPU running the whole model and against the CPU oracle
+stepping the whole model; the row-parallel all-reduce both through NCCL and
+through the peer all-reduce kernel (identical bits at two ranks).
 
 Row-parallel partial sums are added in a different order than the single
 GPU's one serial fold, so the comparison is by tolerance: the residual
@@ -88,9 +89,16 @@ def _worker(rank, world, port, out_dir, cfg_name, n_steps):
     eng.set_probe(True)
     prompt = [int(v) for v in np.random.default_rng(21).integers(0, cfg.vocab, 6)]
     toks, probes = _run(eng, cfg, prompt, cfg.n_layers, n_steps)
-    eng.close()  # its graphs hold NCCL work: released before the process group
     np.save(os.path.join(out_dir, f"probe{rank}.npy"), probes)
     np.save(os.path.join(out_dir, f"toks{rank}.npy"), np.array(toks))
+    # the same steps with the peer all-reduce (one kernel over NVLink peer
+    # memory instead of the NCCL call and the residual add)
+    tp.connect_peers(dist, eng)
+    ptoks, pprobes = _run(eng, cfg, prompt, cfg.n_layers, n_steps)
+    np.save(os.path.join(out_dir, f"pprobe{rank}.npy"), pprobes)
+    np.save(os.path.join(out_dir, f"ptoks{rank}.npy"), np.array(ptoks))
+    dist.barrier()  # no rank unmaps or frees while another may still read it
+    eng.close()  # its graphs hold NCCL work: released before the process group
     if rank == 0:
         ref = q35.Engine(full, n_slots=2, max_seq=64, max_batch=4)
         ref.set_probe(True)
@@ -127,6 +135,13 @@ def test_tp2_matches_single_gpu_and_oracle(cfg_name, n_steps, bound):
         # the ranks hold one residual stream, bit for bit
         assert np.array_equal(p0.view(np.uint32), p1.view(np.uint32))
         assert np.array_equal(t0, t1)
+        # the peer all-reduce: at two ranks its rank-order sum p0 + p1 and the
+        # residual add are NCCL's sum and k_add_rows bit for bit
+        q0, q1 = (np.load(os.path.join(d, f)) for f in ("pprobe0.npy", "pprobe1.npy"))
+        u0, u1 = (np.load(os.path.join(d, f)) for f in ("ptoks0.npy", "ptoks1.npy"))
+        assert np.array_equal(q0.view(np.uint32), q1.view(np.uint32))
+        assert np.array_equal(q0.view(np.uint32), p0.view(np.uint32))
+        assert np.array_equal(u0, t0) and np.array_equal(u1, t1)
         # the single GPU is the oracle's (bit-exact engine); TP follows both
         # within the per-layer bar, with the same greedy tokens
         w_ref, w_or = _worst(p0, pr), _worst(p0, po)
@@ -135,3 +150,21 @@ def test_tp2_matches_single_gpu_and_oracle(cfg_name, n_steps, bound):
         assert w_or < bound, w_or
         assert np.array_equal(t0, tr)
         assert np.array_equal(t0, to)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_peer_allreduce_waits_are_bounded():
+    """the peer all-reduce's waits end: run as rank 0 of two whose rank 1
+    never runs (its flags are words nothing sets), the kernel gives up after
+    1 ms per wait and records error 150; the context stays usable"""
+    import ctypes
+    from qwen35_b200 import lib
+    L = lib.load()
+    code = ctypes.c_int(-1)
+    assert L.q35b_get_error(ctypes.byref(code)) == 0
+    assert L.q35b_tp_selftest_timeout(1_000_000, None) == 0
+    assert L.q35b_get_error(ctypes.byref(code)) == 0
+    assert code.value == 150
+    x = torch.ones(1024, device="cuda")
+    assert float((x * 2).sum()) == 2048.0
+
