@@ -37,6 +37,7 @@ struct MmqArgs {
     int nseg;
     long long total_tiles;          // row tiles over all matrices
     int ntok, nchunk;
+    int ntt;                        // token tiles (k_mmq walks row tiles x token tiles)
 };
 
 // ---- tcgen05 / descriptor helpers -----------------------------------------
@@ -209,7 +210,9 @@ Q35_DEV uint64_t f2_exact_i2f(uint32_t d0, uint32_t d1) {
 }
 
 // ---------------------------------------------------------------------------
-// k_mmq: warp-specialised pipeline, one 128-row x TN-token tile per CTA
+// k_mmq: warp-specialised pipeline over 128-row x TN-token tiles; one
+// persistent CTA per SM walks its tiles (w = blockIdx.x, + gridDim.x, ...)
+// with every ring, buffer and TMEM half counting chunks across tiles
 //   warp 0      TMA producer: raw weight + activation chunks, 2-stage ring
 //   warp 1      TMEM owner; one lane issues the MMAs of a round (RB blocks)
 //               into one of two TMEM halves and commits
@@ -272,11 +275,11 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
     int issued = 0, ncommit = 0;
     uint64_t *last_commit = nullptr;
     uint32_t last_parity = 0;
-    const long long tile = blockIdx.x;
-    const int t0 = blockIdx.y * TN;
-    const int si = mmq_find_seg(a, tile);
-    const MmqSeg &sg = a.seg[si];
-    const long long r0 = (tile - sg.tile_begin) * MMQ_M;
+    // persistent: this CTA walks work items w = blockIdx.x, + gridDim.x, ...
+    // (w = row tile * ntt + token tile); every role counts chunks `it`
+    // across its items, so the rings, buffers and TMEM halves run on from
+    // one tile into the next
+    const long long nwork = a.total_tiles * a.ntt;
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -312,111 +315,128 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes), xbytes = (uint32_t)(TN * 272);
-            for (int c = 0; c < a.nchunk; c++) {
-                const int s = c % MMQ_NS;
-                if (c >= MMQ_NS && (s_fail || !mbar_wait(&empty[s], (uint32_t)(((c / MMQ_NS) - 1) & 1), 121))) {
-                    s_fail = 1;
-                    break;
+            const uint32_t xbytes = (uint32_t)(TN * 272);
+            int it = 0;
+            for (long long w = blockIdx.x; w < nwork && !s_fail; w += gridDim.x) {
+                const long long tile = w / a.ntt;
+                const int t0 = (int)(w - tile * a.ntt) * TN;
+                const int si = mmq_find_seg(a, tile);
+                const MmqSeg &sg = a.seg[si];
+                const long long r0 = (tile - sg.tile_begin) * MMQ_M;
+                const uint32_t wbytes = (uint32_t)(MMQ_M * sg.chunk_bytes);
+                for (int c = 0; c < a.nchunk; c++, it++) {
+                    const int s = it % MMQ_NS;
+                    if (it >= MMQ_NS && (s_fail || !mbar_wait(&empty[s], (uint32_t)(((it / MMQ_NS) - 1) & 1), 121))) {
+                        s_fail = 1;
+                        break;
+                    }
+                    uint8_t *wst = raw + s * (P::W_STAGE + P::X_STAGE);
+                    mbar_arrive_expect_tx(&full[s], wbytes + xbytes);
+                    tma_load_2d(wst, &a.wmap[si], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
+                    tma_load_2d(wst + P::W_STAGE, &a.xmap, c * 34, t0, &full[s]);
+                    issued++;
                 }
-                uint8_t *wst = raw + s * (P::W_STAGE + P::X_STAGE);
-                mbar_arrive_expect_tx(&full[s], wbytes + xbytes);
-                tma_load_2d(wst, &a.wmap[si], c * (sg.chunk_bytes / 8), (int)r0, &full[s]);
-                tma_load_2d(wst + P::W_STAGE, &a.xmap, c * 34, t0, &full[s]);
-                issued++;
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         // lane 0 waits and issues; its verdict is shuffled to the warp so
         // the warp stays converged
-        int g = 0;
+        int g = 0, it = 0;
         bool ok = true;
-        for (int c = 0; c < a.nchunk && ok; c++) {
-            const int p = c % P::NB;
-            const uint32_t use = (uint32_t)(c / P::NB);  // this buffer's use count
-            if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 126);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            tc_fence_after();
-            const uint8_t *sA = sm + P::OFF_A + p * P::A_BUF, *sB = sm + P::OFF_B + p * P::B_BUF;
-            for (int r = 0; r < P::ROUNDS; r++, g++) {
-                const int h = g & 1;
-                if (lane == 0 && g >= 2) ok = !s_fail && mbar_wait(&tfree[h], (uint32_t)(((g >> 1) - 1) & 1), 127);
+        for (long long w = blockIdx.x; w < nwork && ok; w += gridDim.x) {
+            for (int c = 0; c < a.nchunk && ok; c++, it++) {
+                const int p = it % P::NB;
+                const uint32_t use = (uint32_t)(it / P::NB);  // this buffer's use count
+                if (lane == 0) ok = !s_fail && mbar_wait(&ready[p], use & 1u, 126);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    for (int kb = 0; kb < P::RB; kb++) {
-                        const int b = r * P::RB + kb;
-                        const uint64_t ad = umma_desc(sA + b * MMQ_M * 32, 128, 256);
-                        const uint64_t bd = umma_desc(sB + b * TN * 32, 128, 256);
-                        umma_i8(tmem + (uint32_t)(h * P::HALF + kb * TN), ad, bd, mmq_idesc<TN>(), 0u);
+                const uint8_t *sA = sm + P::OFF_A + p * P::A_BUF, *sB = sm + P::OFF_B + p * P::B_BUF;
+                for (int r = 0; r < P::ROUNDS; r++, g++) {
+                    const int h = g & 1;
+                    if (lane == 0 && g >= 2) ok = !s_fail && mbar_wait(&tfree[h], (uint32_t)(((g >> 1) - 1) & 1), 127);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        for (int kb = 0; kb < P::RB; kb++) {
+                            const int b = r * P::RB + kb;
+                            const uint64_t ad = umma_desc(sA + b * MMQ_M * 32, 128, 256);
+                            const uint64_t bd = umma_desc(sB + b * TN * 32, 128, 256);
+                            umma_i8(tmem + (uint32_t)(h * P::HALF + kb * TN), ad, bd, mmq_idesc<TN>(), 0u);
+                        }
+                        umma_commit(&tfull[h]);
+                        last_commit = &tfull[h];
+                        last_parity = (uint32_t)((g >> 1) & 1);
+                        ncommit++;
                     }
-                    umma_commit(&tfull[h]);
-                    last_commit = &tfull[h];
-                    last_parity = (uint32_t)((g >> 1) & 1);
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (lane == 0) {
+                    umma_commit(&opfree[p]);
+                    last_commit = &opfree[p];
+                    last_parity = use & 1u;
                     ncommit++;
                 }
                 __syncwarp();
             }
-            if (!ok) break;
-            if (lane == 0) {
-                umma_commit(&opfree[p]);
-                last_commit = &opfree[p];
-                last_parity = use & 1u;
-                ncommit++;
-            }
-            __syncwarp();
         }
         if (!ok) s_fail = 1;
-        // the last commit covers every MMA of the tile: wait for its arrival
+        // the last commit covers every MMA issued here: wait for its arrival
         // before the barriers' memory can go away
         if (ok && lane == 0 && ncommit > 0 && !mbar_wait(last_commit, last_parity, 130)) s_fail = 1;
         __syncwarp();
     } else if (warp < 6) {
         // ---------------- converters (thread = weight row; < TN: also a token row) ----------------
         const int ct = threadIdx.x - 64;
-        for (int c = 0; c < a.nchunk; c++) {
-            const int s = c % MMQ_NS, p = c % P::NB;
-            const uint32_t use = (uint32_t)(c / P::NB);
-            // every lane waits (acquire); the warp votes so it breaks as one
-            bool ok = !s_fail && mbar_wait(&full[s], (uint32_t)((c / MMQ_NS) & 1), 122);
-            if (ok && use > 0)
-                ok = mbar_wait(&opfree[p], (use - 1) & 1u, 128) && mbar_wait(&sfree[p], (use - 1) & 1u, 129);
-            if (!__all_sync(0xffffffffu, ok)) {
-                s_fail = 1;
-                break;
-            }
-            const uint8_t *wst = raw + s * (P::W_STAGE + P::X_STAGE);
-            uint8_t *sA = sm + P::OFF_A + p * P::A_BUF, *sB = sm + P::OFF_B + p * P::B_BUF;
-            float *sDW = reinterpret_cast<float *>(sm + P::OFF_DW) + p * MMQ_KB * MMQ_M;
-            float *sDX = reinterpret_cast<float *>(sm + P::OFF_DX) + p * MMQ_KB * TN;
-            auto putw = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
-                uint8_t *dst = sA + b * MMQ_M * 32;
-                *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                sDW[b * MMQ_M + ct] = f16_to_f32(d);
-            };
-            if (sg.ttype == TT_Q8_0)
-                unpack_q8_0_chunk(wst + ct * sg.chunk_bytes, putw);
-            else
-                unpack_iq4_nl_chunk(wst + ct * sg.chunk_bytes, putw);
-            if (ct < TN) {
-                auto putx = [&](int b, uint16_t d, const uint32_t (&w)[8]) {
-                    uint8_t *dst = sB + b * TN * 32;
-                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                    sDX[b * TN + ct] = f16_to_f32(d);
+        int it = 0;
+        bool ok = true;
+        for (long long w = blockIdx.x; w < nwork && ok; w += gridDim.x) {
+            const MmqSeg &sg = a.seg[mmq_find_seg(a, w / a.ntt)];
+            for (int c = 0; c < a.nchunk; c++, it++) {
+                const int s = it % MMQ_NS, p = it % P::NB;
+                const uint32_t use = (uint32_t)(it / P::NB);
+                // every lane waits (acquire); the warp votes so it breaks as one
+                ok = !s_fail && mbar_wait(&full[s], (uint32_t)((it / MMQ_NS) & 1), 122);
+                if (ok && use > 0)
+                    ok = mbar_wait(&opfree[p], (use - 1) & 1u, 128) && mbar_wait(&sfree[p], (use - 1) & 1u, 129);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    s_fail = 1;
+                    ok = false;
+                    break;
+                }
+                const uint8_t *wst = raw + s * (P::W_STAGE + P::X_STAGE);
+                uint8_t *sA = sm + P::OFF_A + p * P::A_BUF, *sB = sm + P::OFF_B + p * P::B_BUF;
+                float *sDW = reinterpret_cast<float *>(sm + P::OFF_DW) + p * MMQ_KB * MMQ_M;
+                float *sDX = reinterpret_cast<float *>(sm + P::OFF_DX) + p * MMQ_KB * TN;
+                auto putw = [&](int b, uint16_t d, const uint32_t (&wv)[8]) {
+                    uint8_t *dst = sA + b * MMQ_M * 32;
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                    *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+                    sDW[b * MMQ_M + ct] = f16_to_f32(d);
                 };
-                unpack_q8_0_chunk(wst + P::W_STAGE + ct * 272, putx);
-            }
-            // operands visible to the tensor core's (async) proxy
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&empty[s]);
-                mbar_arrive(&ready[p]);
+                if (sg.ttype == TT_Q8_0)
+                    unpack_q8_0_chunk(wst + ct * sg.chunk_bytes, putw);
+                else
+                    unpack_iq4_nl_chunk(wst + ct * sg.chunk_bytes, putw);
+                if (ct < TN) {
+                    auto putx = [&](int b, uint16_t d, const uint32_t (&wv)[8]) {
+                        uint8_t *dst = sB + b * TN * 32;
+                        *reinterpret_cast<uint4 *>(dst + umma_off(ct, 0)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                        *reinterpret_cast<uint4 *>(dst + umma_off(ct, 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+                        sDX[b * TN + ct] = f16_to_f32(d);
+                    };
+                    unpack_q8_0_chunk(wst + P::W_STAGE + ct * 272, putx);
+                }
+                // operands visible to the tensor core's (async) proxy
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&empty[s]);
+                    mbar_arrive(&ready[p]);
+                }
             }
         }
     } else {
@@ -425,79 +445,85 @@ __global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ 
         const int q = warp & 3;               // TMEM lane quarter this warp may access
         const int fh = (warp - 6) >> 2;       // its token half
         const int row = q * 32 + lane;
-        uint64_t acc[TH / 2];
-#pragma unroll
-        for (int t = 0; t < TH / 2; t++) acc[t] = 0ull;
         const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-        int g = 0;
-        for (int c = 0; c < a.nchunk; c++) {
-            const int p = c % P::NB;
-            if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(c / P::NB) & 1u, 123))) {
-                s_fail = 1;
-                break;
-            }
-            const float *sDW = reinterpret_cast<const float *>(sm + P::OFF_DW) + p * MMQ_KB * MMQ_M;
-            const float *sDX = reinterpret_cast<const float *>(sm + P::OFF_DX) + p * MMQ_KB * TN + fh * TH;
-            for (int r = 0; r < P::ROUNDS; r++, g++) {
-                const int h = g & 1;
-                if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&tfull[h], (uint32_t)((g >> 1) & 1), 124))) {
+        int g = 0, it = 0;
+        for (long long w = blockIdx.x; w < nwork && !s_fail; w += gridDim.x) {
+            const long long tile = w / a.ntt;
+            const int t0 = (int)(w - tile * a.ntt) * TN;
+            const MmqSeg &sg = a.seg[mmq_find_seg(a, tile)];
+            const long long r0 = (tile - sg.tile_begin) * MMQ_M;
+            uint64_t acc[TH / 2];
+#pragma unroll
+            for (int t = 0; t < TH / 2; t++) acc[t] = 0ull;
+            for (int c = 0; c < a.nchunk; c++, it++) {
+                const int p = it % P::NB;
+                if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&ready[p], (uint32_t)(it / P::NB) & 1u, 123))) {
                     s_fail = 1;
                     break;
                 }
-                tc_fence_after();
-                // one block's TH columns per load, the next block's load in
-                // flight while the current one is folded
-                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * P::HALF + fh * TH);
-                uint32_t dA[TH], dB[TH];
-                tmem_ldn<TH>(tbase, dA);
-                tmem_ld_wait();
-#pragma unroll
-                for (int kb = 0; kb < P::RB; kb++) {
-                    uint32_t(&d)[TH] = (kb & 1) ? dB : dA;
-                    if (kb + 1 < P::RB) tmem_ldn<TH>(tbase + (uint32_t)((kb + 1) * TN), (kb & 1) ? dA : dB);
-                    const int b = r * P::RB + kb;
-                    const float dw = sDW[b * MMQ_M + row];
-                    const uint64_t dw2 = f2_pack(dw, dw);
-                    const uint64_t *dx2 = reinterpret_cast<const uint64_t *>(sDX + b * TN);
-#pragma unroll
-                    for (int i = 0; i < TH; i += 2) {
-                        // sumf += dw * dx * (float)sumi for a pair of tokens: the
-                        // products on packed f32x2, the sum in scalar adds (a
-                        // packed multiply feeding a packed add may be contracted
-                        // into one fused multiply-add, which rounds once)
-                        const uint64_t f = f2_sub(f2_pack(__int_as_float(0x4B400000 + (int)d[i]),
-                                                          __int_as_float(0x4B400000 + (int)d[i + 1])),
-                                                  magic);
-                        float a0, a1, p0, p1;
-                        f2_unpack(acc[i / 2], a0, a1);
-                        f2_unpack(f2_mul(f2_mul(dw2, dx2[i / 2]), f), p0, p1);
-                        acc[i / 2] = f2_pack(__fadd_rn(a0, p0), __fadd_rn(a1, p1));
+                const float *sDW = reinterpret_cast<const float *>(sm + P::OFF_DW) + p * MMQ_KB * MMQ_M;
+                const float *sDX = reinterpret_cast<const float *>(sm + P::OFF_DX) + p * MMQ_KB * TN + fh * TH;
+                for (int r = 0; r < P::ROUNDS; r++, g++) {
+                    const int h = g & 1;
+                    if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&tfull[h], (uint32_t)((g >> 1) & 1), 124))) {
+                        s_fail = 1;
+                        break;
                     }
+                    tc_fence_after();
+                    // one block's TH columns per load, the next block's load in
+                    // flight while the current one is folded
+                    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * P::HALF + fh * TH);
+                    uint32_t dA[TH], dB[TH];
+                    tmem_ldn<TH>(tbase, dA);
                     tmem_ld_wait();
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tfree[h]);
-            }
-            if (__any_sync(0xffffffffu, s_fail != 0)) break;
-            if (lane == 0) mbar_arrive(&sfree[p]);
-        }
-        // outputs: row `row` of this tile, tokens t0 + fh*TH .. + TH - 1
-        const long long rr = r0 + row;
-        if (!s_fail && rr < sg.rows) {
-            const int nt = min(TN, a.ntok - t0) - fh * TH;
 #pragma unroll
-            for (int i = 0; i < TH; i += 2) {
-                float v0, v1;
-                f2_unpack(acc[i / 2], v0, v1);
-                const long long tk = t0 + fh * TH + i;
-                if (i < nt) {
-                    float *o = sg.out + tk * sg.out_ld + rr;
-                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, v0) : v0;
+                    for (int kb = 0; kb < P::RB; kb++) {
+                        uint32_t(&d)[TH] = (kb & 1) ? dB : dA;
+                        if (kb + 1 < P::RB) tmem_ldn<TH>(tbase + (uint32_t)((kb + 1) * TN), (kb & 1) ? dA : dB);
+                        const int b = r * P::RB + kb;
+                        const float dw = sDW[b * MMQ_M + row];
+                        const uint64_t dw2 = f2_pack(dw, dw);
+                        const uint64_t *dx2 = reinterpret_cast<const uint64_t *>(sDX + b * TN);
+#pragma unroll
+                        for (int i = 0; i < TH; i += 2) {
+                            // sumf += dw * dx * (float)sumi for a pair of tokens: the
+                            // products on packed f32x2, the sum in scalar adds (a
+                            // packed multiply feeding a packed add may be contracted
+                            // into one fused multiply-add, which rounds once)
+                            const uint64_t f = f2_sub(f2_pack(__int_as_float(0x4B400000 + (int)d[i]),
+                                                              __int_as_float(0x4B400000 + (int)d[i + 1])),
+                                                      magic);
+                            float a0, a1, p0, p1;
+                            f2_unpack(acc[i / 2], a0, a1);
+                            f2_unpack(f2_mul(f2_mul(dw2, dx2[i / 2]), f), p0, p1);
+                            acc[i / 2] = f2_pack(__fadd_rn(a0, p0), __fadd_rn(a1, p1));
+                        }
+                        tmem_ld_wait();
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tfree[h]);
                 }
-                if (i + 1 < nt) {
-                    float *o = sg.out + (tk + 1) * sg.out_ld + rr;
-                    *o = sg.mode == GV_ADD ? __fadd_rn(*o, v1) : v1;
+                if (__any_sync(0xffffffffu, s_fail != 0)) break;
+                if (lane == 0) mbar_arrive(&sfree[p]);
+            }
+            // outputs: row `row` of this tile, tokens t0 + fh*TH .. + TH - 1
+            const long long rr = r0 + row;
+            if (!s_fail && rr < sg.rows) {
+                const int nt = min(TN, a.ntok - t0) - fh * TH;
+#pragma unroll
+                for (int i = 0; i < TH; i += 2) {
+                    float v0, v1;
+                    f2_unpack(acc[i / 2], v0, v1);
+                    const long long tk = t0 + fh * TH + i;
+                    if (i < nt) {
+                        float *o = sg.out + tk * sg.out_ld + rr;
+                        *o = sg.mode == GV_ADD ? __fadd_rn(*o, v0) : v0;
+                    }
+                    if (i + 1 < nt) {
+                        float *o = sg.out + (tk + 1) * sg.out_ld + rr;
+                        *o = sg.mode == GV_ADD ? __fadd_rn(*o, v1) : v1;
+                    }
                 }
             }
         }
@@ -1262,8 +1288,12 @@ inline int mmq_launch(const GemvSegDesc *segs, int nseg, const void *xq, int col
     a.total_tiles = tiles;
     a.ntok = ntok;
     a.nchunk = cols / 256;
+    a.ntt = (ntok + tn - 1) / tn;
     Q35_TRY_RC(mmq_prepare());
-    const dim3 grid((unsigned)tiles, (unsigned)((ntok + tn - 1) / tn));
+    // persistent: one CTA per SM (shared memory and TMEM allow one) walks
+    // the tiles, so one tile's fold overlaps the next tile's loads
+    const long long nwork = tiles * a.ntt;
+    const dim3 grid((unsigned)std::min<long long>(nwork, gemv_sm_count()));
     if (tn == 16) return launch_k(k_mmq<16>, grid, dim3(MMQ_THREADS), (size_t)MmqPlan<16>::SMEM, st, a);
     if (tn == 32) return launch_k(k_mmq<32>, grid, dim3(MMQ_THREADS), (size_t)MmqPlan<32>::SMEM, st, a);
     return launch_k(k_mmq<64>, grid, dim3(MMQ_THREADS), (size_t)MmqPlan<64>::SMEM, st, a);
