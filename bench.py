@@ -673,9 +673,10 @@ def sweep_gemv(L, hbm, only=None):
                 ms, reps = _timed_loop(torch, launch, n_rot)
                 algo = mbytes + ntok * cols * 4 + ntok * rows * 4
                 ops = 2.0 * rows * cols * ntok
-                if ntok >= 16 and tname != "Q6_K":
+                # the library's routing: tensor-core MMQ from 8 tokens (MMQ_MIN_TOK)
+                if ntok >= 8 and tname != "Q6_K":
                     path = "k_mmq" if tname in ("Q8_0", "IQ4_NL") else "k_mmq_kq"
-                elif ntok >= 16:
+                elif ntok >= 8:
                     path = "k_repack_q6k + k_mmq_kq"  # raw 210-byte rows, repacked per call
                 elif tname != "Q6_K":
                     path = "k_gemv_lpr"

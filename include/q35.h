@@ -275,7 +275,7 @@ int q35b_synth_fill(unsigned long long key, long long n, float k, float *d_dst, 
  * Besides the GGML codes, ttype may be Q35B_TT_Q6_K_PADDED: Q6_K blocks
  * padded from 210 to 224 bytes (zeros after byte 210), the layout the engine
  * repacks Q6_K weights to at load so that rows are 16-byte multiples for TMA
- * (the tensor-core path for 16 tokens and more requires it for Q6_K). */
+ * (the tensor-core path for 8 tokens and more requires it for Q6_K). */
 #define Q35B_TT_Q6_K_PADDED 0x100E
 
 int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, const long long *rows,
@@ -284,7 +284,7 @@ int q35b_mul_mat_vec_multi(int nmat, const void *const *d_w, const int *ttype, c
 
 /* q35b_mul_mat_vec_multi with a caller-provided device workspace (no
  * reference counterpart).  With one matrix of a 256-element family (Q4_K,
- * Q5_K, padded Q6_K) at 16 tokens or more whose row tiles (128 rows each)
+ * Q5_K, padded Q6_K) at 8 tokens or more whose row tiles (128 rows each)
  * leave more than half the SMs idle, the tensor-core path splits K over CTAs
  * when work_bytes >= (cols / 256) * tokens * rows * 4: each block's f32 term
  * goes to d_work and a second kernel adds them in block order, so results

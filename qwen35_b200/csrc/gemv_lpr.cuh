@@ -1023,7 +1023,8 @@ inline int gemv_lpr_launch(const GemvSegDesc *segs, int nseg, const void *xq, in
     }
     if (pro) {
         if (pro->kind != LPR_PRO_NORM && pro->kind != LPR_PRO_SWIGLU && pro->kind != LPR_PRO_ROWS) return -1;
-        if (ntok >= 16) return -1;  // many tokens: the tensor-core path, after a separate prologue kernel
+        // 8 tokens or more: the tensor-core path (MMQ_MIN_TOK), after a separate prologue kernel
+        if (ntok >= 8) return -1;
         if ((reinterpret_cast<uintptr_t>(pro->x) & 15u) || (pro->ld & 3)) return -1;
     }
     const int fam = geom_of(segs[0].ttype).family;

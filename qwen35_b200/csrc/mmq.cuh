@@ -19,7 +19,10 @@
 namespace q35 {
 
 constexpr int MMQ_M = 128;          // weight rows per tile (TMEM lanes)
-constexpr int MMQ_MIN_TOK = 16;     // below this the decode GEMV is used
+// below this the decode GEMV is used; from 8 tokens a 16-token tile (rows
+// past the tokens zero-filled by TMA, never stored) already beats the
+// lane-per-row GEMV's 8-token passes (lm_head 1024 x 248320 Q8_0: 75 vs 131 us)
+constexpr int MMQ_MIN_TOK = 8;
 constexpr int MMQ_KB = 8;           // 32-element blocks per chunk (256 columns)
 constexpr int MMQ_NS = 2;           // raw-chunk ring stages
 
