@@ -637,9 +637,14 @@ def sweep_gemv(L, hbm, only=None):
     st = torch.cuda.current_stream()
     s = ctypes.c_void_p(st.cuda_stream)
     g = torch.Generator(device="cuda")
-    for cols, rows in SWEEP_SHAPES:
-        for tname in SWEEP_TYPES:
-            cases = [t for t in SWEEP_TOKENS if only is None or only == f"{tname}:{cols}x{rows}:{t}"]
+    shapes, types, tokens = SWEEP_SHAPES, SWEEP_TYPES, SWEEP_TOKENS
+    if only is not None:  # one case, any shape and token count
+        o_t, o_shape, o_tok = only.split(":")
+        o_in, o_out = (int(v) for v in o_shape.split("x"))
+        shapes, types, tokens = [(o_in, o_out)], [o_t], [int(o_tok)]
+    for cols, rows in shapes:
+        for tname in types:
+            cases = [t for t in tokens if only is None or only == f"{tname}:{cols}x{rows}:{t}"]
             if not cases:
                 continue
             tt = TT[tname]
