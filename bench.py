@@ -253,7 +253,7 @@ def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False):
 SERVE_SEQS, SERVE_PROMPT, SERVE_GEN = 64, (64, 2048), 256
 
 
-def time_serve(cfg_name, seed, dist, world, rank):
+def time_serve(cfg_name, seed, dist, world, rank, wy=False):
     """continuous batching of SERVE_SEQS sequences (seeded
     prompt lengths uniform in SERVE_PROMPT, SERVE_GEN greedy tokens each)
     through q35b_serve, the sequences sharded over the ranks (every rank
@@ -271,6 +271,7 @@ def time_serve(cfg_name, seed, dist, world, rank):
     synth = q35.SyntheticModel(cfg, seed=seed)
     nslot = len(mine)
     eng = q35.Engine(synth, n_slots=nslot, max_seq=SERVE_PROMPT[1] + SERVE_GEN + 8, max_batch=256)
+    eng.set_prefill_wy(wy)
     eng.serve([prompts[mine[0]][:40]], [4], max_batch=nslot)  # warm-up (graphs, attributes)
     torch.cuda.synchronize()
     if dist:
@@ -985,15 +986,17 @@ def main():
             tpv["nccl_ms_per_step"] = tms_nccl / ksteps
             tpv["nccl_value"] = 32 * ksteps / (tms_nccl * 1e-3)
         variants.append(tpv)
-        sms, sp, sg = time_serve("4b", args.seed, dist, world, rank)
-        sms = max_over_ranks(sms, dist)
-        variants.append({"model": "qwen3.5-4b-mixed", "workload": "continuous batching (BASELINE config 4): %d "
-                         "sequences, prompts uniform in %d..%d tokens, %d greedy tokens each, sharded by sequence "
-                         "over the ranks" % (SERVE_SEQS, SERVE_PROMPT[0], SERVE_PROMPT[1], SERVE_GEN),
-                         "ms": sms, "value": SERVE_SEQS * SERVE_GEN / (sms * 1e-3), "unit": "generated tokens/s",
-                         "prompt_tokens": sp, "generated_tokens": sg,
-                         "total_tokens_per_s": (sp + sg) / (sms * 1e-3),
-                         "scaling": "strong"})
+        for wy in (False, True):
+            sms, sp, sg = time_serve("4b", args.seed, dist, world, rank, wy)
+            sms = max_over_ranks(sms, dist)
+            variants.append({"model": "qwen3.5-4b-mixed", "workload": "continuous batching (BASELINE config 4): %d "
+                             "sequences, prompts uniform in %d..%d tokens, %d greedy tokens each, sharded by "
+                             "sequence over the ranks" % (SERVE_SEQS, SERVE_PROMPT[0], SERVE_PROMPT[1], SERVE_GEN),
+                             "gdn": "chunked WY for prompt runs >= 16 tokens" if wy else "per-token (exact)",
+                             "ms": sms, "value": SERVE_SEQS * SERVE_GEN / (sms * 1e-3), "unit": "generated tokens/s",
+                             "prompt_tokens": sp, "generated_tokens": sg,
+                             "total_tokens_per_s": (sp + sg) / (sms * 1e-3),
+                             "scaling": "strong"})
         for cfg_name, ntok, chunk in (("0.8b", 512, 256), ("4b", 512, 256)):
             for wy in (False, True):
                 pms = time_prefill(cfg_name, ntok, chunk, args.seed + rank, dist, wy)

@@ -396,10 +396,12 @@ int q35b_tp_selftest_timeout(unsigned long long limit_ns, void *stream);
 int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int nrun,
                         const int *run_end, int *next, void *stream);
 
-/* Prefill runs (longer than one token) through the chunked WY form of the
- * GDN recurrence (on) or token by token (off, the default).  WY re-associates
- * the recurrence's sums: it agrees with the per-token form to rounding, not
- * bitwise. */
+/* Runs of 16 tokens or more in a forward with runs longer than one token
+ * (prefill, prompt chunks of q35b_serve) through the chunked WY form of the
+ * GDN recurrence on the tensor-core Gram pass (on), or every run token by
+ * token (off, the default); shorter runs stay per token either way.  WY
+ * re-associates the recurrence's sums: it agrees with the per-token form to
+ * rounding, not bitwise.  The first WY forward allocates its scratch. */
 int q35b_engine_set_prefill_wy(q35b_engine *e, int on);
 
 /* Sampling in the engine's step (replaces the greedy argmax when on): every

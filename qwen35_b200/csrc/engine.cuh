@@ -239,6 +239,13 @@ struct q35b_engine {
     float *logits = nullptr, *scores = nullptr, *probe_buf = nullptr;
     float *xh = nullptr;  // last row of each run, gathered for the model head
     bool gdn_wy = false;  // prefill runs through the chunked (WY) GDN form
+    // WY scratch (allocated at the first WY forward): conv'd / normalised
+    // q | k | v, log decays | betas, the recurrence output, Gram blocks
+    float *wy_q = nullptr, *wy_k = nullptr, *wy_v = nullptr, *wy_lg = nullptr, *wy_beta = nullptr, *wy_o = nullptr;
+    float *wy_g = nullptr;
+    size_t wy_g_bytes = 0;
+    // the current forward's runs as the host passed them (prefill forwards)
+    std::vector<int> h_run_end, h_run_slot;
     bool sampling = false;  // next tokens drawn by the device sampler (per-slot parameters) instead of argmax
     int *samp = nullptr;    // per-slot sampler control blocks [n_slots][SC_INTS]
     // tensor parallelism (1 rank: off)
@@ -381,10 +388,52 @@ inline int eng_layer_gdn(q35b_engine *e, int li, int n, int nrun, cudaStream_t s
     g.xq_ld = e->xq_ld;
     g.gout = e->gout;
     g.gout_ld = vdim;
-    if (g.run_end && e->gdn_wy)
-        Q35_TRY(launch_k(k_gdn_wy, dim3(nv, nrun), dim3(GDN_KD), WY_SMEM, st, g));
-    else
+    if (g.run_end && e->gdn_wy) {
+        // WY form for runs of WY_MIN_RUN tokens or more: per-token prologue,
+        // the chunked recurrence per run on its slot's state, per-token
+        // epilogue; shorter runs (decode tokens in a mixed forward, prompt
+        // tails) stay with k_gdn_core, which skips the others
+        g.wy_min = WY_MIN_RUN;
+        bool any_short = false, any_long = false;
+        for (int r = 0; r < nrun; r++) {
+            const int len = e->h_run_end[r] - (r ? e->h_run_end[r - 1] : 0);
+            (len >= WY_MIN_RUN ? any_long : any_short) = true;
+        }
+        if (any_short)
+            Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), (size_t)GDN_KD * GDN_KD * 4, st, g));
+        if (any_long) {
+            WyPrepOut o{e->wy_q, e->wy_k, e->wy_v, e->wy_lg, e->wy_beta, nrun};
+            Q35_TRY(launch_k(k_gdn_wy_prep, dim3(n, nv), dim3(GDN_KD), 0, st, g, o));
+            for (int r = 0; r < nrun; r++) {
+                const int i0 = r ? e->h_run_end[r - 1] : 0, i1 = e->h_run_end[r];
+                if (i1 - i0 < WY_MIN_RUN) continue;
+                GdnArgs w{};
+                w.state = g.state + (long long)e->h_run_slot[r] * e->state_slot;
+                w.state_head = (long long)kd * kd;
+                w.q = e->wy_q + (long long)i0 * kq;
+                w.k = e->wy_k + (long long)i0 * kq;
+                w.v = e->wy_v + (long long)i0 * vdim;
+                w.q_tok = w.k_tok = kq;
+                w.v_tok = vdim;
+                w.q_head = w.k_head = w.v_head = kd;
+                w.out = e->wy_o + (long long)i0 * vdim;
+                w.out_tok = vdim;
+                w.out_head = kd;
+                w.gamma = e->wy_lg + (long long)i0 * nv;
+                w.g_tok = nv;
+                w.gamma_log = 1;
+                w.beta = e->wy_beta + (long long)i0 * nv;
+                w.b_tok = nv;
+                w.heads = nv;
+                w.nk = nk;
+                w.rows = i1 - i0;
+                Q35_TRY(wy_tc_launch(w, st, e->wy_g, e->wy_g_bytes));
+            }
+            Q35_TRY(launch_k(k_gdn_wy_post, dim3(n, nv), dim3(GDN_KD), 0, st, g, (const float *)e->wy_o, nrun));
+        }
+    } else {
         Q35_TRY(launch_k(k_gdn_core, dim3(nv, nrun), dim3(GDN_KD), (size_t)GDN_KD * GDN_KD * 4, st, g));
+    }
     if (g.run_end)
         Q35_TRY(launch_k(k_gdn_hist_settle, dim3((unsigned)((conv_dim * 3 + 255) / 256), (unsigned)nrun), dim3(256), 0,
                          st, g.hist, g.hist_slot, conv_dim, g.slots, g.pos, g.run_end));

@@ -557,6 +557,28 @@ int q35b_engine_advance(q35b_engine *e, int n, void *stream) {
     return (int)cudaGetLastError();
 }
 
+// the WY prefill's scratch for max_batch tokens, at its first use (an
+// ordinary forward, never inside stream capture)
+static int eng_wy_scratch(q35b_engine *e) {
+    if (e->wy_q) return 0;
+    const q35b_config &c = e->c;
+    const size_t B = (size_t)e->max_batch, kq = (size_t)c.gdn_num_k_heads * GDN_KD,
+                 vd = (size_t)c.gdn_n_heads * GDN_KD;
+    float **dst[6] = {&e->wy_q, &e->wy_k, &e->wy_v, &e->wy_o, &e->wy_lg, &e->wy_beta};
+    const size_t len[6] = {B * kq, B * kq, B * vd, B * vd, B * c.gdn_n_heads, B * c.gdn_n_heads};
+    for (int i = 0; i < 6; i++) {
+        void *p = nullptr;
+        Q35_TRY(eng_alloc(e, &p, 4 * len[i]));
+        *dst[i] = static_cast<float *>(p);
+    }
+    void *p = nullptr;
+    const size_t gb = wy_gram_bytes(e->max_batch, c.gdn_num_k_heads);
+    Q35_TRY(eng_alloc(e, &p, gb));
+    e->wy_g = static_cast<float *>(p);
+    e->wy_g_bytes = gb;
+    return 0;
+}
+
 // One forward over n tokens in nrun runs (host arrays); see include/q35.h.
 int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int nrun,
                         const int *run_end, int *next, void *stream) {
@@ -590,6 +612,12 @@ int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slo
         // launch cost spread over the run's tokens
         Q35_TRY((int)cudaMemcpyAsync(e->d_in + 3 * e->max_batch, run_end, (size_t)nrun * 4, cudaMemcpyHostToDevice,
                                      st));
+        if (e->gdn_wy) {
+            Q35_TRY(eng_wy_scratch(e));
+            e->h_run_end.assign(run_end, run_end + nrun);
+            e->h_run_slot.resize(nrun);
+            for (int r = 0; r < nrun; r++) e->h_run_slot[r] = slots[r ? run_end[r - 1] : 0];
+        }
         Q35_TRY(eng_step_body(e, n, nrun, eng_len_bucket(max_len, e->max_seq), st));
     }
     Q35_TRY((int)cudaMemcpyAsync(next, e->d_next, (size_t)nrun * 4, cudaMemcpyDeviceToHost, st));

@@ -48,6 +48,7 @@ struct GdnArgs {
     float gamma_imm, beta_imm;
     int heads, nk, rows;             // rows: tokens stepped in order per sequence
     const int *active;               // optional per-sequence flag: 0 = skip
+    int gamma_log;                   // WY kernels: gamma holds floored log decays (not decays)
 };
 
 __global__ void __launch_bounds__(GDN_KD) k_gdn_step(const __grid_constant__ GdnArgs a) {
@@ -137,6 +138,7 @@ struct GdnCoreArgs {
     long long xq_ld;
     float *gout;          // f32 gated output when fam != 32
     long long gout_ld;
+    int wy_min;           // > 0: runs of at least wy_min tokens take the WY form (k_gdn_core skips them)
 };
 
 __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ GdnCoreArgs a) {
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
     // the run: consecutive positions of one sequence, stepped in order
     const int i0 = a.run_end ? (r == 0 ? 0 : a.run_end[r - 1]) : r;
     const int i1 = a.run_end ? a.run_end[r] : r + 1;
+    if (a.wy_min > 0 && i1 - i0 >= a.wy_min) return;  // a WY run
     const long long slot = a.slots[i0];
     const int p0 = a.pos[i0];
     // history: read the buffer of the run's first position's parity, write
@@ -504,130 +507,139 @@ struct WyNoSink {
     __device__ void operator()(int, float, float) const {}
 };
 
-// The engine's GDN layer core over prefill runs in the WY form: the same
-// conv / gates / l2 norms / gated RMSNorm as k_gdn_core around wy_chunk.
-__global__ void __launch_bounds__(GDN_KD) k_gdn_wy(const __grid_constant__ GdnCoreArgs a) {
+// The engine's GDN layer core over prefill runs in the WY form, as three
+// steps around the operator's chunked recurrence (wy_tc_launch: the tensor-
+// core Gram pass and the column-split kernel, one launch pair per run):
+//   k_gdn_wy_prep  CTA per (token, head): causal conv k=4 + silu, the q / k
+//                  l2 norms (serial sums), the floored log decay and beta --
+//                  every per-token operation of k_gdn_core in its order, run
+//                  for all tokens at once (a token's conv window is its
+//                  run's previous three inputs, or the slot's history)
+//   recurrence     per run, on the slot's state (q35::wy_tc_launch)
+//   k_gdn_wy_post  CTA per (token, head): gated RMSNorm (serial sum) x
+//                  silu(z), quantized for ssm_out as k_gdn_core does
+// The conv history after a run is written by the CTAs of the run's last
+// token into the other parity buffer, as k_gdn_core's (k_gdn_hist_settle
+// follows either).
+// shortest run the engine steps in the WY form: a shorter one costs
+// k_gdn_core less than the per-run launches of the chunked recurrence
+constexpr int WY_MIN_RUN = 16;
+
+// the run holding token b: the first r with run_end[r] > b
+__device__ __forceinline__ int run_of(const int *run_end, int nrun, int b) {
+    int lo = 0, hi = nrun - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (run_end[mid] > b)
+            hi = mid;
+        else
+            lo = mid + 1;
+    }
+    return lo;
+}
+
+struct WyPrepOut {
+    float *q, *k;     // [n][nk * kd]: l2-normalised (q also scaled)
+    float *v;         // [n][nv * kd]: conv + silu
+    float *lg, *beta; // [n][nv]: floored log decay, beta
+    int nrun;
+};
+
+__global__ void __launch_bounds__(GDN_KD) k_gdn_wy_prep(const __grid_constant__ GdnCoreArgs a,
+                                                        const __grid_constant__ WyPrepOut o) {
     pdl_trigger();
-    pdl_wait();
-    extern __shared__ __align__(128) float smw[];
-    float *s_state = smw;  // [kd][kd] (bulk copy)
-    const WyBufs m = wy_bufs(s_state + GDN_KD * GDN_KD);
-    float *lg = m.bet + WY_C;  // [C] log g_t
-    float *scq = lg + WY_C, *sck = scq + WY_C, *sco = sck + WY_C;
-    __shared__ __align__(8) uint64_t s_bar;
-    __shared__ int s_ok;
-    __shared__ float s_h[3][3][GDN_KD], s_w[3][4][GDN_KD];
-    const int h = blockIdx.x, r = blockIdx.y, j = threadIdx.x, warp = j >> 5, lane = j & 31;
-    const int kd = GDN_KD, kq = a.nk * kd, conv_dim = 2 * kq + a.nv * kd;
-    const int kh = h % a.nk;
-    const int i0 = a.run_end ? (r == 0 ? 0 : a.run_end[r - 1]) : r;
-    const int i1 = a.run_end ? a.run_end[r] : r + 1;
+    __shared__ float sq[GDN_KD], sk[GDN_KD];
+    __shared__ float s_sc[2];
+    const int b = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+    const int kd = GDN_KD, kq = a.nk * kd, vdim = a.nv * kd, conv_dim = 2 * kq + vdim;
+    const int lo = run_of(a.run_end, o.nrun, b);
+    const int i0 = lo == 0 ? 0 : a.run_end[lo - 1], i1 = a.run_end[lo];
+    if (i1 - i0 < a.wy_min) return;  // a short run: k_gdn_core's
     const long long slot = a.slots[i0];
-    const int p0 = a.pos[i0];
+    const int p0 = a.pos[i0], u = b - i0;
     const float *hin = a.hist + slot * a.hist_slot + (long long)(p0 & 1) * conv_dim * 3;
     float *hout = a.hist + slot * a.hist_slot + (long long)((p0 & 1) ^ 1) * conv_dim * 3;
-    float *S = a.state + slot * a.state_slot + (long long)h * kd * kd;
-    if (j == 0) {
-        mbar_init(&s_bar, 1);
-        fence_mbar_init();
-        mbar_arrive_expect_tx(&s_bar, (uint32_t)(kd * kd * 4));
-        bulk_g2s(s_state, S, (uint32_t)(kd * kd * 4), &s_bar);
-    }
-    const int chq = kh * kd + j, chk = kq + kh * kd + j, chv = 2 * kq + h * kd + j;
+    const bool qk = h < a.nk;  // this CTA also owns k head h's q / k channels
+    const int chq = h * kd + j, chk = kq + h * kd + j, chv = 2 * kq + h * kd + j;
+    // history and taps (not written by this step's kernels) before the wait
+    float hv[3][3], wv[3][4];
     const int chs[3] = {chq, chk, chv};
 #pragma unroll
     for (int c = 0; c < 3; c++) {
+        if (c < 2 && !qk) continue;
 #pragma unroll
-        for (int i = 0; i < 3; i++) s_h[c][i][j] = hin[(long long)chs[c] * 3 + i];
+        for (int i = 0; i < 3; i++) hv[c][i] = hin[(long long)chs[c] * 3 + i];
 #pragma unroll
-        for (int i = 0; i < 4; i++) s_w[c][i][j] = a.conv_w[(long long)chs[c] * 4 + i];
+        for (int i = 0; i < 4; i++) wv[c][i] = a.conv_w[(long long)chs[c] * 4 + i];
     }
-    const float nwj = a.ssm_norm[j];
     const float ssm_a = a.ssm_a[h], dtb = a.dt_bias[h];
-    if (j == 0) s_ok = mbar_wait(&s_bar, 0u, 142) ? 1 : 0;
+    pdl_wait();
+    // input at run offset m of channel c: the projection, or the history
+    // before the run's first token
+    auto input = [&](int c, int m) {
+        return m >= 0 ? a.qkv[(long long)(i0 + m) * a.qkv_ld + chs[c]] : hv[c][3 + m];
+    };
+    // k_gdn_core's conv: w0*x[u-3] + w1*x[u-2] + w2*x[u-1] + w3*x[u], left to right
+    auto conv = [&](int c) {
+        const float x0 = input(c, u - 3), x1 = input(c, u - 2), x2 = input(c, u - 1), x3 = input(c, u);
+        if (b == i1 - 1) {  // the history after the run
+            float *ho = hout + (long long)chs[c] * 3;
+            ho[0] = x1;
+            ho[1] = x2;
+            ho[2] = x3;
+        }
+        const float s = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(x0, wv[c][0]), __fmul_rn(x1, wv[c][1])),
+                                            __fmul_rn(x2, wv[c][2])),
+                                  __fmul_rn(x3, wv[c][3]));
+        return silu_f(s);
+    };
+    o.v[(long long)b * vdim + h * kd + j] = conv(2);
+    if (j == 64) {
+        const float *ar = a.ab + (long long)b * a.ab_ld;
+        o.lg[(long long)b * a.nv + h] = fmaxf(__fmul_rn(ssm_a, softplus_f(__fadd_rn(ar[h], dtb))), WY_LOG_MIN);
+        o.beta[(long long)b * a.nv + h] = sigmoid_f(ar[a.nv + h]);
+    }
+    if (qk) {  // uniform over the CTA
+        const float yq = conv(0), yk = conv(1);
+        sq[j] = yq;
+        sk[j] = yk;
+        __syncthreads();
+        if (j == 0) s_sc[0] = serial_sumsq(sq, kd);
+        if (j == 32) s_sc[1] = serial_sumsq(sk, kd);
+        __syncthreads();
+        const float iq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_sc[0], 1e-6f)));
+        const float ik = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_sc[1], 1e-6f)));
+        o.q[(long long)b * kq + h * kd + j] = __fmul_rn(__fmul_rn(yq, iq), a.qscale);
+        o.k[(long long)b * kq + h * kd + j] = __fmul_rn(yk, ik);
+    }
+}
+
+// gated RMSNorm of the recurrence output y ([n][nv * kd]) x silu(z),
+// quantized per token (or f32 when ssm_out takes another family)
+__global__ void __launch_bounds__(GDN_KD) k_gdn_wy_post(const __grid_constant__ GdnCoreArgs a, const float *y,
+                                                        int nrun) {
+    pdl_trigger();
+    __shared__ float so[GDN_KD];
+    __shared__ float s_sc;
+    const int b = blockIdx.x, h = blockIdx.y, j = threadIdx.x, warp = j >> 5, lane = j & 31;
+    {
+        const int r = run_of(a.run_end, nrun, b);
+        if (a.run_end[r] - (r ? a.run_end[r - 1] : 0) < a.wy_min) return;  // a short run: k_gdn_core's
+    }
+    const int kd = GDN_KD, vdim = a.nv * kd;
+    const float nwj = a.ssm_norm[j];
+    pdl_wait();
+    const float ov = y[(long long)b * vdim + h * kd + j];
+    so[j] = ov;
     __syncthreads();
-    if (!s_ok) {
-        if (j == 0) mbar_wait(&s_bar, 0u, 143);
-        return;
-    }
-    float col[GDN_KD];
-#pragma unroll
-    for (int i = 0; i < GDN_KD; i++) col[i] = s_state[i * GDN_KD + j];
-    auto conv = [&](int c, float cur) {
-        const float sm = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(s_h[c][0][j], s_w[c][0][j]),
-                                                       __fmul_rn(s_h[c][1][j], s_w[c][1][j])),
-                                             __fmul_rn(s_h[c][2][j], s_w[c][2][j])),
-                                   __fmul_rn(cur, s_w[c][3][j]));
-        s_h[c][0][j] = s_h[c][1][j];
-        s_h[c][1][j] = s_h[c][2][j];
-        s_h[c][2][j] = cur;
-        return silu_f(sm);
-    };
-    for (int t0 = i0; t0 < i1; t0 += WY_C) {
-        const int nc = min(WY_C, i1 - t0);
-        // 1. q, k, v of every token: the raw inputs first (independent loads),
-        //    then the conv in token order (history advanced in order), gates
-#pragma unroll 4
-        for (int t = 0; t < nc; t++) {
-            const float *raw = a.qkv + (long long)(t0 + t) * a.qkv_ld;
-            m.Qs[t * WY_LD + j] = raw[chq];
-            m.Ks[t * WY_LD + j] = raw[chk];
-            m.Vs[t * WY_LD + j] = raw[chv];
-        }
-        for (int t = 0; t < nc; t++) {
-            m.Qs[t * WY_LD + j] = conv(0, m.Qs[t * WY_LD + j]);
-            m.Ks[t * WY_LD + j] = conv(1, m.Ks[t * WY_LD + j]);
-            m.Vs[t * WY_LD + j] = conv(2, m.Vs[t * WY_LD + j]);
-        }
-        if (j < nc) {
-            const float *ar = a.ab + (long long)(t0 + j) * a.ab_ld;
-            // log of k_gdn_core's gamma, floored
-            lg[j] = fmaxf(__fmul_rn(ssm_a, softplus_f(__fadd_rn(ar[h], dtb))), WY_LOG_MIN);
-            m.bet[j] = sigmoid_f(ar[a.nv + h]);
-        }
-        __syncthreads();
-        // 2. l2norm scales (serial sums, as k_gdn_core), cumulative log decay
-        if (j < nc) scq[j] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(serial_sumsq(m.Qs + j * WY_LD, kd), 1e-6f)));
-        if (j >= 64 && j < 64 + nc)
-            sck[j - 64] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(serial_sumsq(m.Ks + (j - 64) * WY_LD, kd), 1e-6f)));
-        wy_cumulate(m, lg, nc, j);
-        __syncthreads();
-        for (int t = 0; t < nc; t++) {
-            m.Qs[t * WY_LD + j] = __fmul_rn(__fmul_rn(m.Qs[t * WY_LD + j], scq[t]), a.qscale);
-            m.Ks[t * WY_LD + j] = __fmul_rn(m.Ks[t * WY_LD + j], sck[t]);
-        }
-        __syncthreads();
-        // 3. the recurrence over the chunk
-        wy_chunk(col, m, nc, j, WyNoSink{});
-        __syncthreads();
-        // 4. gated RMSNorm (serial sums, as k_gdn_core) x silu(z), quantized per token
-        if (j < nc)
-            sco[j] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(serial_sumsq(m.Us + j * WY_LD, kd), (float)kd), a.eps)));
-        __syncthreads();
-        for (int t = 0; t < nc; t++) {
-            const long long b = t0 + t;
-            float y = __fmul_rn(__fmul_rn(m.Us[t * WY_LD + j], sco[t]), nwj);
-            y = __fmul_rn(y, silu_f(a.z[b * a.z_ld + (long long)h * kd + j]));
-            if (a.fam == 32)
-                quant_q8_0_warp(y, a.xq + b * a.xq_ld + (long long)(h * (kd / 32) + warp) * 34, lane);
-            else
-                a.gout[b * a.gout_ld + (long long)h * kd + j] = y;
-        }
-        __syncthreads();  // chunk buffers reused
-    }
-#pragma unroll
-    for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
-    auto store = [&](int c) {
-        float *ho = hout + (long long)chs[c] * 3;
-        ho[0] = s_h[c][0][j];
-        ho[1] = s_h[c][1][j];
-        ho[2] = s_h[c][2][j];
-    };
-    if (h < a.nk) {
-        store(0);
-        store(1);
-    }
-    store(2);
+    if (j == 0) s_sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(serial_sumsq(so, kd), (float)kd), a.eps)));
+    __syncthreads();
+    float r = __fmul_rn(__fmul_rn(ov, s_sc), nwj);
+    r = __fmul_rn(r, silu_f(a.z[(long long)b * a.z_ld + (long long)h * kd + j]));
+    if (a.fam == 32)
+        quant_q8_0_warp(r, a.xq + (long long)b * a.xq_ld + (long long)(h * (kd / 32) + warp) * 34, lane);
+    else
+        a.gout[(long long)b * a.gout_ld + (long long)h * kd + j] = r;
 }
 
 // The operator form (q35_launch_gdn_step_wy, api.h:290-308): q / k already
@@ -655,7 +667,8 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_rows(const __grid_constant__ 
         }
         if (j < nc) {
             const long long tok = t0 + j;
-            lg[j] = fmaxf(logf(a.gamma ? a.gamma[tok * a.g_tok + h] : a.gamma_imm), WY_LOG_MIN);
+            lg[j] = a.gamma_log ? a.gamma[tok * a.g_tok + h]
+                                : fmaxf(logf(a.gamma ? a.gamma[tok * a.g_tok + h] : a.gamma_imm), WY_LOG_MIN);
             m.bet[j] = a.beta ? a.beta[tok * a.b_tok + h] : a.beta_imm;
         }
         __syncthreads();
@@ -786,7 +799,8 @@ __global__ void __launch_bounds__(WY_NT, 2) k_gdn_wy_cols(const __grid_constant_
         // other warps start on U / W, which needs none of them
         if (warp == NW - 1) {
             if (lane < nc) {
-                Lc[lane] = fmaxf(logf(a.gamma ? Gb[buf * WY_C + lane] : a.gamma_imm), WY_LOG_MIN);
+                Lc[lane] = a.gamma_log ? Gb[buf * WY_C + lane]
+                                       : fmaxf(logf(a.gamma ? Gb[buf * WY_C + lane] : a.gamma_imm), WY_LOG_MIN);
                 bet[lane] = a.beta ? Bb[buf * WY_C + lane] : a.beta_imm;
             }
             __syncwarp();
@@ -1028,7 +1042,6 @@ inline int gdn_prepare() {
     static int done = 0;
     if (done) return 0;
     cudaError_t e = cudaFuncSetAttribute(k_gdn_core, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_KD * GDN_KD * 4);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gdn_wy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_SMEM);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_gdn_wy_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WY_ROWS_SMEM);
     if (e == cudaSuccess)

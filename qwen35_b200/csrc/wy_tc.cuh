@@ -166,7 +166,14 @@ inline WyGramBuf &wy_gram_buf(int dev) {
     return bufs[dev & 63];
 }
 
-inline int wy_tc_launch(const GdnArgs &a, cudaStream_t st) {
+// bytes of Gram blocks a run of `rows` tokens needs
+inline size_t wy_gram_bytes(int rows, int nk) {
+    return (size_t)2 * ((rows + WYT_C - 1) / WYT_C) * nk * WYT_G * sizeof(float);
+}
+
+// gbuf / gbytes: the caller's Gram scratch (the engine's own), or null for a
+// per-device buffer grown outside stream capture
+inline int wy_tc_launch(const GdnArgs &a, cudaStream_t st, float *gbuf = nullptr, size_t gbytes = 0) {
     if (a.heads <= 0 || a.rows <= 0) return 0;
     if (a.nk <= 0 || a.q_head != GDN_KD || a.k_head != GDN_KD) return -1;
     static int ready = 0;
@@ -175,11 +182,19 @@ inline int wy_tc_launch(const GdnArgs &a, cudaStream_t st) {
         if (e != cudaSuccess) return (int)e;
         ready = 1;
     }
+    const int npair = (a.rows + WYT_C - 1) / WYT_C;
+    const size_t need = wy_gram_bytes(a.rows, a.nk);
+    if (gbuf) {
+        if (gbytes < need) return (int)cudaErrorInvalidValue;
+        WyGramArgs g{a.q, a.k, a.q_tok, a.k_tok, a.q_head, a.k_head, a.rows, a.nk, gbuf};
+        k_wy_gram<<<dim3((unsigned)npair, (unsigned)a.nk), 128, WYT_GRAM_SMEM, st>>>(g);
+        const int rc = (int)cudaGetLastError();
+        if (rc) return rc;
+        return gdn_wy_cols_launch(a, st, gbuf);
+    }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return -1;
     WyGramBuf &b = wy_gram_buf(dev);
-    const int npair = (a.rows + WYT_C - 1) / WYT_C;
-    const size_t need = (size_t)2 * npair * a.nk * WYT_G * sizeof(float);
     if (b.bytes < need) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusActive;
         if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return -1;

@@ -249,10 +249,12 @@ def test_prefill_chunks_equal_token_steps(q35, cfg_name):
     eng.close()
 
 
-@pytest.mark.parametrize("cfg_name", ["tiny", "tiny-mixed"])
-def test_wy_prefill_matches_per_token(q35, cfg_name):
+@pytest.mark.parametrize("cfg_name,max_batch", [("tiny", 80), ("tiny-mixed", 80), ("tiny-mixed", 32)])
+def test_wy_prefill_matches_per_token(q35, cfg_name, max_batch):
     """the engine's chunked WY GDN form over a 70-token prompt run (3 chunks
-    of <= 32) against the exact per-token recurrence: the same greedy tokens.
+    of <= 32; with max_batch 32, three forwards of 32 / 32 / 6 tokens, each
+    starting from the state and conv history the previous one left) against
+    the exact per-token recurrence: the same greedy tokens.
     Layer outputs are compared loosely: the GDN output is quantized (Q8_0 /
     Q8_K) before ssm_out, so the WY form's f32-rounding differences (bounded
     at 1e-4 per op by test_gdn_wy_matches_per_token) either vanish or flip a
@@ -265,12 +267,13 @@ def test_wy_prefill_matches_per_token(q35, cfg_name):
     prompt = [int(t) for t in rng.integers(0, cfg.vocab, 70)]
     res = []
     for wy in (False, True):
-        eng = q35.Engine(synth, n_slots=1, max_seq=96, max_batch=80)
+        eng = q35.Engine(synth, n_slots=1, max_seq=96, max_batch=max_batch)
         eng.set_prefill_wy(wy)
         eng.set_probe(True)
         eng.reset_slot(0)
         nxt = eng.prefill(0, prompt)
-        layers = [eng.layer_out(li, len(prompt)).cpu().numpy() for li in range(cfg.n_layers)]
+        nlast = len(prompt) - (len(prompt) - 1) // max_batch * max_batch  # tokens of the last forward
+        layers = [eng.layer_out(li, nlast).cpu().numpy() for li in range(cfg.n_layers)]
         toks = [nxt]
         for pos in range(len(prompt), len(prompt) + 5):
             toks.append(eng.step_host([toks[-1]], [0], [pos])[0])
@@ -281,6 +284,66 @@ def test_wy_prefill_matches_per_token(q35, cfg_name):
     assert rels[0] < 2e-3, rels
     assert max(rels) < 0.1, rels
     assert tw == te
+
+
+def test_wy_forward_mixes_runs(q35):
+    """WY form over one forward of three runs in three slots: a decode token,
+    a 40-token prompt (two chunks) and a 3-token prompt (shorter than the
+    conv window).  Runs shorter than WY_MIN_RUN (16) stay on the per-token
+    kernel.  (1) The prompt runs equal the same prompts prefilled alone in
+    the WY form bit for bit -- their rows of every layer, their next tokens
+    and the decode step after them (state and conv history the runs left):
+    runs are independent.  (2) Against the per-token form on the same
+    forward: the short runs' rows are identical at every layer; over all
+    rows the first layer is within 2e-3 and every layer within 0.1 (the
+    loose bound of test_wy_prefill_matches_per_token); the next tokens are
+    the same."""
+    cfg = q35.CONFIGS["tiny-mixed"]
+    synth = q35.SyntheticModel(cfg, seed=17)
+    rng = np.random.default_rng(17)
+    pa = [int(t) for t in rng.integers(0, cfg.vocab, 6)]
+    pb = [int(t) for t in rng.integers(0, cfg.vocab, 40)]
+    pc = [int(t) for t in rng.integers(0, cfg.vocab, 3)]
+    toks = None
+    res = []
+    for wy in (False, True):
+        eng = q35.Engine(synth, n_slots=3, max_seq=64, max_batch=48)
+        for s in range(3):
+            eng.reset_slot(s)
+        na = eng.prefill(0, pa)
+        eng.set_prefill_wy(wy)
+        eng.set_probe(True)
+        toks = [na] + pb + pc
+        slots = [0] + [1] * len(pb) + [2] * len(pc)
+        pos = [len(pa)] + list(range(len(pb))) + list(range(len(pc)))
+        nxt = eng.forward(toks, slots, pos, [1, 1 + len(pb), len(toks)])
+        layers = [eng.layer_out(li, len(toks)).cpu().numpy() for li in range(cfg.n_layers)]
+        after = eng.step_host(nxt[1:], [1, 2], [len(pb), len(pc)])
+        res.append((nxt, layers, after))
+        eng.close()
+    (ne, le, _), (nw, lw, aw) = res
+    rels = [np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b) for a, b in zip(lw, le)]
+    assert rels[0] < 2e-3, rels
+    assert max(rels) < 0.1, rels
+    assert nw == ne
+    short = [0] + list(range(1 + len(pb), len(toks)))  # the decode token and the 3-token run
+    for li in range(cfg.n_layers):
+        assert np.array_equal(lw[li][short], le[li][short]), li
+    # the prompts alone, WY form
+    eng = q35.Engine(synth, n_slots=3, max_seq=64, max_batch=48)
+    eng.set_prefill_wy(True)
+    eng.set_probe(True)
+    alone_next, alone_after = [], []
+    for slot, prompt, r0 in ((1, pb, 1), (2, pc, 1 + len(pb))):
+        eng.reset_slot(slot)
+        alone_next.append(eng.prefill(slot, prompt))
+        for li in range(cfg.n_layers):
+            got = eng.layer_out(li, len(prompt)).cpu().numpy()
+            assert np.array_equal(got, lw[li][r0:r0 + len(prompt)]), (slot, li)
+    alone_after = eng.step_host(alone_next, [1, 2], [len(pb), len(pc)])
+    eng.close()
+    assert alone_next == nw[1:]
+    assert alone_after == aw
 
 
 def test_forward_mixes_prefill_and_decode_runs(q35):
