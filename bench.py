@@ -219,7 +219,7 @@ def time_e2e(run, steps, warmup, dist):
     return ms
 
 
-def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False):
+def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False, nvtx=False):
     """one prompt of ntok seeded tokens through q35b_engine_prefill (runs of
     `chunk` tokens: tensor-core projections, chunked GDN recurrence, causal
     attention), CUDA events on the stream the engine runs on"""
@@ -239,10 +239,14 @@ def time_prefill(cfg_name, ntok, chunk, seed, dist, wy=False):
         dist.barrier()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if nvtx:
+        torch.cuda.nvtx.range_push("q35_timed")
     e0.record(st)
     eng.prefill(0, prompt, stream=st)
     e1.record(st)
     torch.cuda.synchronize()
+    if nvtx:
+        torch.cuda.nvtx.range_pop()
     ms = max_over_ranks(e0.elapsed_time(e1), dist)
     eng.close()
     del synth
@@ -895,10 +899,11 @@ def main():
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--no-variants", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "all"], default=None,
+    ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "prefill", "all"], default=None,
                     help="isolated kernel sweeps (BASELINE configs 2 / 3; mmq: the 4B / 27B batched-decode "
                          "matrices) instead of the decode bench")
-    ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS; --sweep gdn: one WY prefill length")
+    ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS; --sweep gdn: one WY "
+                    "prefill length; --sweep prefill: MODEL:TOKENS:CHUNK[:exact]")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -937,6 +942,15 @@ def main():
             sweep_gdn(L, hbm, args.sweep_case)
         if args.sweep in ("mmq", "all"):
             sweep_mmq(L, hbm, args.sweep_case)
+        if args.sweep == "prefill":
+            # one engine prefill (the prefill variants' timing, inside the NVTX
+            # range q35_timed for a launch list)
+            f = (args.sweep_case or "4b:512:256").split(":")
+            wy = not (len(f) > 3 and f[3] == "exact")
+            pms = time_prefill(f[0], int(f[1]), int(f[2]), args.seed, None, wy, nvtx=True)
+            print(json.dumps({"sweep": "prefill", "model": f[0], "prefill_tokens": int(f[1]), "chunk": int(f[2]),
+                              "gdn": "chunked WY" if wy else "per-token (exact)", "ms": pms,
+                              "value": int(f[1]) / (pms * 1e-3), "unit": "prefill tokens/s"}))
         return
     extra = 2 * (args.warmup + args.steps) + 8
 
