@@ -899,11 +899,11 @@ def main():
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--no-variants", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "prefill", "all"], default=None,
+    ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "prefill", "decode", "all"], default=None,
                     help="isolated kernel sweeps (BASELINE configs 2 / 3; mmq: the 4B / 27B batched-decode "
                          "matrices) instead of the decode bench")
     ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS; --sweep gdn: one WY "
-                    "prefill length; --sweep prefill: MODEL:TOKENS:CHUNK[:exact]")
+                    "prefill length; --sweep prefill: MODEL:TOKENS:CHUNK[:exact]; --sweep decode: MODEL:BATCH")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -942,6 +942,16 @@ def main():
             sweep_gdn(L, hbm, args.sweep_case)
         if args.sweep in ("mmq", "all"):
             sweep_mmq(L, hbm, args.sweep_case)
+        if args.sweep == "decode":
+            # one model's batched decode steps alone (the variants' timing,
+            # inside the NVTX range q35_timed for a launch list)
+            f = (args.sweep_case or "4b:64").split(":")
+            r = Run(f[0], int(f[1]), args.prompt, 2 * (args.warmup + args.steps) + 8, seed=args.seed)
+            vms = time_decode(r, args.steps, args.warmup, None)
+            print(json.dumps({"sweep": "decode", "model": r.cfg.name, "batch": r.batch, "steps": args.steps,
+                              "ms_per_step": vms / args.steps,
+                              "value": r.batch * args.steps / (vms * 1e-3), "unit": "tokens/s"}))
+            r.close()
         if args.sweep == "prefill":
             # one engine prefill (the prefill variants' timing, inside the NVTX
             # range q35_timed for a launch list)
