@@ -401,7 +401,8 @@ int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slo
  * GDN recurrence on the tensor-core Gram pass (on), or every run token by
  * token (off, the default); shorter runs stay per token either way.  WY
  * re-associates the recurrence's sums: it agrees with the per-token form to
- * rounding, not bitwise.  The first WY forward allocates its scratch. */
+ * rounding, not bitwise.  Switching it on for a finalized engine (or
+ * finalizing with it on) allocates its scratch; forwards allocate nothing. */
 int q35b_engine_set_prefill_wy(q35b_engine *e, int on);
 
 /* Sampling in the engine's step (replaces the greedy argmax when on): every

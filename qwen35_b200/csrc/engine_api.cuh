@@ -25,6 +25,29 @@ bool lin_ok(const Lin &l, long long rows, long long cols) { return l.w && l.rows
 
 long long graph_key(int n, int len_bucket) { return (long long)n * (1LL << 32) + len_bucket; }
 
+// the WY prefill's scratch for max_batch tokens: allocated when the WY form
+// is switched on for a finalized engine, or at finalize, so that no forward
+// allocates (a forward may run inside the caller's stream capture)
+int eng_wy_scratch(q35b_engine *e) {
+    if (e->wy_g) return 0;  // the last of them: all allocated
+    const q35b_config &c = e->c;
+    const size_t B = (size_t)e->max_batch, kq = (size_t)c.gdn_num_k_heads * GDN_KD,
+                 vd = (size_t)c.gdn_n_heads * GDN_KD;
+    float **dst[6] = {&e->wy_q, &e->wy_k, &e->wy_v, &e->wy_o, &e->wy_lg, &e->wy_beta};
+    const size_t len[6] = {B * kq, B * kq, B * vd, B * vd, B * c.gdn_n_heads, B * c.gdn_n_heads};
+    for (int i = 0; i < 6; i++) {
+        void *p = nullptr;
+        Q35_TRY(eng_alloc(e, &p, 4 * len[i]));
+        *dst[i] = static_cast<float *>(p);
+    }
+    void *p = nullptr;
+    const size_t gb = wy_gram_bytes(e->max_batch, c.gdn_num_k_heads);
+    Q35_TRY(eng_alloc(e, &p, gb));
+    e->wy_g = static_cast<float *>(p);
+    e->wy_g_bytes = gb;
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -64,6 +87,7 @@ int q35b_engine_destroy(q35b_engine *e) {
 int q35b_engine_set_prefill_wy(q35b_engine *e, int on) {
     if (!e) return (int)cudaErrorInvalidValue;
     e->gdn_wy = on != 0;
+    if (e->gdn_wy && e->finalized) return eng_wy_scratch(e);
     return 0;
 }
 
@@ -400,6 +424,7 @@ int q35b_engine_finalize(q35b_engine *e) {
     Q35_TRY(gemv_lpr_prepare());
     Q35_TRY(gdn_prepare());
     Q35_TRY(attx_prepare(e->max_seq));
+    if (e->gdn_wy) Q35_TRY(eng_wy_scratch(e));
     Q35_TRY((int)cudaDeviceSynchronize());
     e->finalized = true;
     return 0;
@@ -557,28 +582,6 @@ int q35b_engine_advance(q35b_engine *e, int n, void *stream) {
     return (int)cudaGetLastError();
 }
 
-// the WY prefill's scratch for max_batch tokens, at its first use (an
-// ordinary forward, never inside stream capture)
-static int eng_wy_scratch(q35b_engine *e) {
-    if (e->wy_q) return 0;
-    const q35b_config &c = e->c;
-    const size_t B = (size_t)e->max_batch, kq = (size_t)c.gdn_num_k_heads * GDN_KD,
-                 vd = (size_t)c.gdn_n_heads * GDN_KD;
-    float **dst[6] = {&e->wy_q, &e->wy_k, &e->wy_v, &e->wy_o, &e->wy_lg, &e->wy_beta};
-    const size_t len[6] = {B * kq, B * kq, B * vd, B * vd, B * c.gdn_n_heads, B * c.gdn_n_heads};
-    for (int i = 0; i < 6; i++) {
-        void *p = nullptr;
-        Q35_TRY(eng_alloc(e, &p, 4 * len[i]));
-        *dst[i] = static_cast<float *>(p);
-    }
-    void *p = nullptr;
-    const size_t gb = wy_gram_bytes(e->max_batch, c.gdn_num_k_heads);
-    Q35_TRY(eng_alloc(e, &p, gb));
-    e->wy_g = static_cast<float *>(p);
-    e->wy_g_bytes = gb;
-    return 0;
-}
-
 // One forward over n tokens in nrun runs (host arrays); see include/q35.h.
 int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slots, const int *pos, int nrun,
                         const int *run_end, int *next, void *stream) {
@@ -613,7 +616,7 @@ int q35b_engine_forward(q35b_engine *e, int n, const int *tokens, const int *slo
         Q35_TRY((int)cudaMemcpyAsync(e->d_in + 3 * e->max_batch, run_end, (size_t)nrun * 4, cudaMemcpyHostToDevice,
                                      st));
         if (e->gdn_wy) {
-            Q35_TRY(eng_wy_scratch(e));
+            if (!e->wy_g) return (int)cudaErrorInvalidValue;  // allocated when switched on
             e->h_run_end.assign(run_end, run_end + nrun);
             e->h_run_slot.resize(nrun);
             for (int r = 0; r < nrun; r++) e->h_run_slot[r] = slots[r ? run_end[r - 1] : 0];
