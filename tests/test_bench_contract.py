@@ -43,3 +43,21 @@ def test_reference_arm_line_and_libraries():
     assert not any(n.startswith("libcudart") or n.startswith("libcuda.") for n in names), names
     if cb["kind"] == "reference":
         assert any(n.startswith("libq35ref") for n in names), names
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """launched as the driver launches N > 1 (torchrun, two ranks on this
+    host): rank 0 alone runs and prints its line, the other rank exits 0
+    without work; no process group is needed for it"""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                          "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--impl", "reference",
+                          "--gpus", "2", "--steps", "1", "--warmup", "3"],
+                         cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [json.loads(l) for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    assert lines[0]["impl"] == "reference" and lines[0]["n_gpus"] == 2 and lines[0]["value"] > 0
