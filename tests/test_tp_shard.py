@@ -103,3 +103,53 @@ def test_local_config_and_rejects():
         tp.local_config(cfg, 16)  # 24 q heads do not split 16 ways
     with pytest.raises(ValueError):
         tp.local_config(CONFIGS["tiny-tp-mixed"], 3)
+
+
+class _FakeEngine:
+    """stands in for model.Engine in the handle exchange: this rank's IPC
+    handle bytes, and the list set_peers receives"""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.peers = None
+
+    def ipc_handles(self):
+        return bytes([self.rank + 1]) * 192
+
+    def set_peers(self, handles):
+        self.peers = list(handles)
+
+
+def _peers_worker(rank, world, port, out_dir):
+    import datetime
+    import os
+
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    try:
+        eng = _FakeEngine(rank)
+        tp.connect_peers(dist, eng)
+        with open(os.path.join(out_dir, f"r{rank}"), "wb") as f:
+            f.write(b"".join(eng.peers))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_connect_peers_exchanges_handles_in_rank_order():
+    """tp.connect_peers over a world-size-3 gloo group: every rank's engine
+    receives all ranks' handles, in rank order (the order the peer
+    all-reduce indexes its peer table by)"""
+    import os
+    import socket
+    import tempfile
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_peers_worker, args=(3, port, d), nprocs=3, start_method="spawn")
+        expect = b"".join(bytes([r + 1]) * 192 for r in range(3))
+        for r in range(3):
+            assert open(os.path.join(d, f"r{r}"), "rb").read() == expect
