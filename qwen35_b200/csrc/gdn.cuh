@@ -348,15 +348,16 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_core(const __grid_constant__ Gdn
 // km_t = g_t S_{t-1}^T k_t, o_t = S_t^T q_t  exactly; the sums are
 // re-associated (f32, fused multiply-adds), so this form agrees with the
 // per-token kernels to f32 rounding, not bitwise.
-// CTA per (value head, run), thread j owns state column j (128 registers);
+// k_gdn_wy_rows: CTA per value head, thread j owns state column j (128 registers);
 // the chunk's q / k / v rows sit in shared memory with a 132-float pitch
 // (an odd multiple of 16 bytes: float4 row reads by 8 lanes of different
 // rows hit 8 distinct bank quads).
 // ---------------------------------------------------------------------------
 constexpr int WY_C = 32;
 constexpr int WY_LD = GDN_KD + 4;
-constexpr size_t WY_SMEM = (size_t)GDN_KD * GDN_KD * 4 + (size_t)5 * WY_C * WY_LD * 4 +
-                           (size_t)2 * WY_C * (WY_C + 1) * 4 + (size_t)8 * WY_C * 4;
+// chunk buffers of wy_bufs (Qs..Ws, Am, Mm, the per-token vectors) and log g
+constexpr size_t WY_ROWS_SMEM =
+    (size_t)5 * WY_C * WY_LD * 4 + (size_t)2 * WY_C * (WY_C + 1) * 4 + (size_t)8 * WY_C * 4;
 constexpr float WY_LOG_MIN = -88.0f;  // log decay floor: exp() of it is ~0, sums stay finite
 
 struct WyBufs {
@@ -687,7 +688,6 @@ __global__ void __launch_bounds__(GDN_KD) k_gdn_wy_rows(const __grid_constant__ 
     for (int i = 0; i < GDN_KD; i++) S[(long long)i * GDN_KD + j] = col[i];
 }
 
-constexpr size_t WY_ROWS_SMEM = WY_SMEM - (size_t)GDN_KD * GDN_KD * 4;
 
 inline int gdn_wy_rows_launch(const GdnArgs &a, cudaStream_t st) {
     if (a.heads <= 0 || a.rows <= 0) return 0;
