@@ -233,6 +233,13 @@ Q35_DEV uint64_t f2_exact_i2f(uint32_t d0, uint32_t d1) {
 //   sfree [buffer]          fold -> converters (scales read)
 // ---------------------------------------------------------------------------
 constexpr int MMQ_THREADS = 448;  // 14 warps
+// registers per thread of the MMQ kernels: all that one 448-thread CTA per
+// SM can hold (14 warps x 32 x 144 = 64,512 of 65,536).  Left to the
+// launch bound alone, ptxas stops at 128 and spills the fold's state at
+// 64-token tiles; at 144 the K-quant kernels spill nothing and k_mmq<64>
+// 12 bytes.
+constexpr int MMQ_MAXNREG = 144;
+static_assert(MMQ_THREADS * MMQ_MAXNREG <= 65536, "one CTA's registers");
 
 template <int TN>
 struct MmqPlan {
@@ -259,7 +266,7 @@ struct MmqPlan {
 };
 
 template <int TN>
-__global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq(const __grid_constant__ MmqArgs a) {
+__global__ void __maxnreg__(MMQ_MAXNREG) k_mmq(const __grid_constant__ MmqArgs a) {
     using P = MmqPlan<TN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -612,7 +619,7 @@ struct MmqkPlan {
 };
 
 template <int TN, bool Q6>
-__global__ void __launch_bounds__(MMQ_THREADS, 1) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
+__global__ void __maxnreg__(MMQ_MAXNREG) k_mmq_kq(const __grid_constant__ MmqkArgs a) {
     using P = MmqkPlan<TN, Q6>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
