@@ -901,7 +901,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", choices=["gemv", "gdn", "mmq", "prefill", "decode", "all"], default=None,
                     help="isolated kernel sweeps (BASELINE configs 2 / 3; mmq: the 4B / 27B batched-decode "
-                         "matrices) instead of the decode bench")
+                         "matrices) or one engine workload alone (prefill, decode; inside the NVTX range "
+                         "q35_timed) instead of the decode bench")
     ap.add_argument("--sweep-case", default=None, help="--sweep gemv|mmq: one case, TYPE:INxOUT:TOKENS; --sweep gdn: one WY "
                     "prefill length; --sweep prefill: MODEL:TOKENS:CHUNK[:exact]; --sweep decode: MODEL:BATCH")
     args = ap.parse_args()
